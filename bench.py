@@ -1,0 +1,349 @@
+"""Benchmark: RWKV-7 2.9B grouped-U8 (SG8 g128) greedy decode tok/s on B200.
+
+One JSON line on rank 0.  A *step* is one decode token at batch 1 (the whole
+packed RWKV-7 token step: embedding, 32 layers of time mix + channel mix,
+head, greedy argmax).  Inputs are resident in HBM before timing; the weights
+streamed per token (~3 GB) are far larger than the 126 MB L2, so no flush is
+needed between steps.
+
+Multi-GPU (torchrun): decode does not shard at batch 1 — every rank runs an
+independent replica (its own model copy and session), ``scaling: "weak"``;
+``value`` = tokens decoded by all ranks / max-over-ranks device time.
+
+``--impl reference`` times the reference's own C kernels (built from its
+sources into ``oracle/_ref``) driving the packed RWKV-7 forward on the host
+cores, on the same workload and metric (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "ssd-rwkv-engine_b200"))
+sys.path.insert(0, str(REPO))
+os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+SEED = 2026
+PROMPT = 8
+
+
+def _env_int(k: str, d: int) -> int:
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def _peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", ",".join(map(str, self.gpus))],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxes.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sms)) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def bytes_per_token(pack, shape) -> int:
+    """Algorithmic HBM bytes of one decode token: every packed matrix read once
+    (embedding: one row; layer 0's unused v1/v2 excluded), skeleton vectors,
+    and the recurrent state read + written."""
+    C, L, H = shape.n_embd, shape.n_layer, shape.n_head
+    tot = 0
+    for n, e in pack.items():
+        if n in ("blocks.0.att.v1", "blocks.0.att.v2", "blocks.0.att.v0"):
+            continue
+        p = e.payload
+        nb = int(p.numel() * p.element_size()) if isinstance(p, torch.Tensor) else (
+            len(p) if isinstance(p, (bytes, bytearray)) else int(np.asarray(p).nbytes))
+        if n == "emb.weight":
+            g = 128
+            nb = C + (C // g) * 8
+        tot += nb
+    state = L * (2 * C + H * 64 * 64) * 4
+    return tot + 2 * state
+
+
+def run_reference(args, shape, rank: int) -> dict:
+    """The reference's C kernels (oracle/_ref) driving the packed forward on the host."""
+    from oracle import kernels as ok
+    from oracle.forward import OracleRWKV7
+    from rwkv_b200 import synth
+
+    if not ok.ref_available():
+        return {"impl": "reference", "unavailable": "reference C kernels (oracle/_ref) not built"}
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    pack = synth.pack_to_host(synth.make_pack_streaming(shape, SEED, dev, policy=args.policy))
+    if dev == "cuda":
+        torch.cuda.empty_cache()
+    model = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size,
+                        impl="reference")
+    state = model.zero_state()
+    prompt = synth.seeded_prompt(PROMPT, shape.vocab, SEED)
+    for t in prompt[:2]:
+        logits = model.forward_token(t, state)
+    tok = int(np.argmax(logits))
+    for _ in range(args.warmup):
+        logits = model.forward_token(tok, state)
+        tok = int(np.argmax(logits))
+    t0 = time.perf_counter()
+    n = 0
+    for _ in range(args.steps):
+        logits = model.forward_token(tok, state)
+        tok = int(np.argmax(logits))
+        n += 1
+        if time.perf_counter() - t0 > args.ref_budget_s:
+            break
+    dt = time.perf_counter() - t0
+    v = n / dt
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"metric": f"RWKV-7 {args.config} {args.policy.upper()} decode tok/s (bs1)", "value": v,
+            "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 * dt / n,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"rwkv7-{args.config} {args.policy} bs1 greedy decode", "batch": 1},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                             "sample": f"{n} decode tokens (time budget {args.ref_budget_s}s) after "
+                                       f"{args.warmup} warm-up tokens: reference lut2_gather.c GEMVs "
+                                       f"(oracle/_ref, -O3 -mavx2 -mfma -fopenmp) + NumPy fp32 glue"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_baseline(pack_dev, shape, args) -> dict:
+    from oracle import kernels as ok
+    from oracle.forward import OracleRWKV7
+    from rwkv_b200 import synth
+
+    impl = "reference" if ok.ref_available() else "oracle"
+    pack = synth.pack_to_host(pack_dev)
+    model = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size, impl=impl)
+    st = model.zero_state()
+    logits = model.forward_token(1, st)
+    tok = int(np.argmax(logits))
+    t0 = time.perf_counter()
+    n = 0
+    while n < 64:
+        logits = model.forward_token(tok, st)
+        tok = int(np.argmax(logits))
+        n += 1
+        if time.perf_counter() - t0 > args.cpu_budget_s:
+            break
+    dt = time.perf_counter() - t0
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": "reference" if impl == "reference" else "port",
+            "sample": f"{n} decode tokens of the same {args.config} {args.policy} model "
+                      f"({dt:.1f}s) through the packed forward with "
+                      + ("the reference's lut2_gather.c GEMVs" if impl == "reference" else "the oracle C GEMVs")}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=64)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="2.9b", choices=["tiny", "0.1b", "2.9b", "7.2b"])
+    ap.add_argument("--policy", default="sg8", choices=["sg8", "lut2"])
+    ap.add_argument("--prefetch", type=int, default=None)
+    ap.add_argument("--e2e-steps", type=int, default=256)
+    ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    ap.add_argument("--ref-budget-s", type=float, default=60.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = _env_int("WORLD_SIZE", 1)
+    rank = _env_int("RANK", 0)
+    local = _env_int("LOCAL_RANK", 0)
+    from rwkv_b200 import synth
+
+    shape = synth.PRESETS[args.config]
+
+    if args.impl == "reference":
+        if rank == 0:
+            if torch.cuda.is_available():
+                torch.cuda.set_device(local)
+            print(json.dumps(run_reference(args, shape, rank)), flush=True)
+        return
+
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from rwkv_b200.engine import B200Engine
+
+    pack = synth.make_pack_streaming(shape, SEED + rank, dev, policy=args.policy)
+    bpt = bytes_per_token(pack, shape)
+    eng = B200Engine(pack, device=local, prefetch_distance=args.prefetch)
+    cpu_pack = pack if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    del pack
+    torch.cuda.empty_cache()
+
+    stream = torch.cuda.current_stream(dev)
+    prompt = synth.seeded_prompt(PROMPT, shape.vocab, SEED + rank)
+    eng.forward(prompt)
+    first = int(torch.argmax(eng.logits).item())
+    out = torch.empty(max(args.steps, args.warmup) + 8, dtype=torch.int32, device=dev)
+    eng.decode_greedy_async(first, args.warmup, out)
+    torch.cuda.synchronize(dev)
+    nxt = int(out[args.warmup - 1].item())
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    clocks = ClockSampler(list(range(world)) if rank == 0 else [])
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.3)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    eng.decode_greedy_async(nxt, args.steps, out)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1)
+    clk = clocks.stop() if rank == 0 else {}
+    if world > 1:
+        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+        dist.barrier()
+    total_tokens = args.steps * world
+    value = total_tokens / (ms / 1e3)
+    ms_step = ms / args.steps
+
+    # end to end through the host API: every step copies its input token
+    # host->device and its argmax device->host (pinned), synchronising per token
+    e2e_steps = min(args.e2e_steps, args.steps)
+    tok_h = torch.empty(1, dtype=torch.int32, pin_memory=True)
+    tok_h[0] = nxt
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        eng.forward([int(tok_h[0])])
+        am = torch.argmax(eng.logits).to(torch.int32)
+        tok_h.copy_(am.reshape(1), non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_val = e2e_steps * world / (e2e_ms / 1e3)
+
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        achieved = bpt / (ms_step / 1e3) / 1e9
+        traffic = None
+        tf = REPO / "profiles" / f"decode_{args.config}_{args.policy}_traffic.json"
+        if tf.is_file():
+            try:
+                traffic = json.loads(tf.read_text()).get("dram_bytes_per_step")
+            except Exception:
+                traffic = None
+        res = {
+            "metric": f"RWKV-7 {args.config} U8 decode tok/s (bs1)" if args.policy == "sg8"
+            else f"RWKV-7 {args.config} LUT2 decode tok/s (bs1)",
+            "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (u8/2-bit weights)", "data": "synthetic (seeded random RWKV-7 weights, reference codecs)",
+            "config": {"workload": f"rwkv7-{args.config} {args.policy} bs1 greedy decode, {PROMPT}-token prompt",
+                       "model": f"rwkv7-{args.config}", "global_batch": world, "batch_per_gpu": 1,
+                       "n_layer": shape.n_layer, "d_model": shape.n_embd, "ffn": shape.ffn, "vocab": shape.vocab,
+                       "codec": "SG8 g128" if args.policy == "sg8" else "TR2x04 g64 (+SG8 g128 adapters/emb)",
+                       "parallelism": f"replicas x{world}",
+                       "l2": "weights per token (%.2f GB) >> 126 MB L2; no flush needed" % (bpt / 1e9)},
+            "gpu_launches": eng.launches_per_step * args.steps + 1,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "what": "whole token step (one CUDA-graph launch): algorithmic bytes/token "
+                                 f"{bpt} / device time per token; peak {peak_kind}"},
+            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "steps": e2e_steps, "how": "B200Engine.forward(host token) + argmax D2H per token"},
+            "clocks": clk,
+        }
+        if cpu_pack is not None:
+            eng.close()
+            res["cpu_baseline"] = cpu_baseline(cpu_pack, shape, args)
+        print(json.dumps(res), flush=True)
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

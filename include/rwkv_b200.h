@@ -1,0 +1,202 @@
+/*
+ * rwkv_b200.h — C ABI of the B200 (sm_100a) RWKV-7 packed-weight decode library.
+ *
+ * Drop-in boundary for the reference engine's native hot path.  The reference
+ * binds one portable C file through ctypes (rwkv_ssd/native/lut2_gather.c,
+ * loader rwkv_ssd/native/lut2_gather_loader.py:165-367); every entry point
+ * below names the reference export or Python function it replaces.
+ *
+ * Conventions
+ *  - Every pointer to weights, activations or outputs is a DEVICE pointer,
+ *    except the `header` argument of rwkvb_packed_init (host bytes) and the
+ *    host-side arrays of descriptors/pointers noted per function.
+ *  - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *    Calls are asynchronous on that stream; outputs are ready when it is.
+ *  - Every call returns an int status (RWKVB_OK = 0).  Invalid arguments or a
+ *    malformed blob return RWKVB_EARG and launch nothing (the reference zero-
+ *    fills or returns early in the same cases, lut2_gather.c:515-523, and its
+ *    Python decoders raise ValueError, pack_codec.py:129-137).
+ *  - Packed weights are the reference's own wire blobs, byte for byte,
+ *    uploaded to device memory unchanged:
+ *      SG8\x01 : u32 group | f32[groups][2] (min,max) | u8[numel]      (pack_codec.py:13-68)
+ *      TR2\x03..\x07 : u32 group | records[groups] | 2-bit codes       (trinity_codec.py:52-58)
+ *    The fast GEMV paths need the code payload 16-byte aligned; other
+ *    placements use the general (slower) path with identical results.
+ *  - All arithmetic is fp32.  Dequantised weights are bit-identical to the
+ *    reference decoders; GEMV results differ from the reference C only by
+ *    reduction order.
+ *  - No entry point falls back to the CPU.
+ */
+#ifndef RWKV_B200_H
+#define RWKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RWKVB_ABI_VERSION 1
+
+#define RWKVB_OK 0
+#define RWKVB_EARG 1        /* invalid arguments / malformed blob */
+#define RWKVB_EALLOC 2      /* device allocation failed */
+#define RWKVB_ECUDA 3       /* a CUDA runtime call failed */
+#define RWKVB_ETIMEOUT 4    /* a bounded device wait gave up */
+#define RWKVB_EUNSUPPORTED 5
+
+/* blob kinds: the 4th magic byte ("SG8\x01" is kind 1, "TR2\xNN" is kind NN) */
+#define RWKVB_KIND_SG8 1u
+#define RWKVB_KIND_LUT2_F32 3u     /* TR2\x03: fp32 centroids, 16-byte records */
+#define RWKVB_KIND_LUT2_F16 4u     /* TR2\x04: fp16 centroids, 8-byte records */
+#define RWKVB_KIND_LUT2_RES 5u     /* TR2\x05: fp16 centroids + 2 residuals, 16-byte records */
+#define RWKVB_KIND_LUT2_IN_F16 6u  /* TR2\x06: as \x04, tensor stored input-major */
+#define RWKVB_KIND_LUT2_IN_RES 7u  /* TR2\x07: as \x05, tensor stored input-major */
+
+/* One packed matrix of checkpoint shape [rows, cols] resident in device memory. */
+typedef struct rwkvb_packed {
+  const uint8_t* data; /* device pointer to the blob's first byte (the magic) */
+  uint64_t bytes;      /* blob length */
+  uint32_t kind;       /* RWKVB_KIND_* */
+  uint32_t group_size; /* elements per group */
+  int32_t rows;
+  int32_t cols;
+} rwkvb_packed;
+
+static inline uint32_t rwkvb_lut2_record_bytes(uint32_t kind) {
+  return (kind == RWKVB_KIND_LUT2_F16 || kind == RWKVB_KIND_LUT2_IN_F16) ? 8u : 16u;
+}
+
+/* Library ABI version (RWKVB_ABI_VERSION). */
+int rwkvb_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* rwkvb_status_string(int status);
+
+/* Parse and validate a blob header and fill `out`.
+ * `header` = host copy of at least the first 8 blob bytes.  Validation follows
+ * decode_scale_u8_grouped_to_tensor (pack_codec.py:126-137: magic, group > 0,
+ * exact length 8 + groups*8 + numel) and decode_trinity_lut2_to_tensor
+ * (trinity_codec.py:769-790: grouped kinds 3..7, group > 0, records + codes fit). */
+int rwkvb_packed_init(rwkvb_packed* out, const uint8_t* header, uint64_t blob_bytes,
+                      const uint8_t* device_blob, int32_t rows, int32_t cols);
+
+/* out[rows*cols] = decoded weights in checkpoint order, fp32, bit-exact.
+ * Replaces decode_scale_u8_grouped_to_tensor (pack_codec.py:126-144) and the
+ * grouped branch of decode_trinity_lut2_to_tensor (trinity_codec.py:769-885). */
+int rwkvb_dequant_f32(float* out, const rwkvb_packed* w, void* stream);
+
+/* y[rows] = W @ x[cols].  SG8 replaces scale_u8_grouped_gemv_f32_export
+ * (lut2_gather.c:491-496); LUT2 kinds replace trinity_grouped_lut2_gemv_f32_export
+ * (lut2_gather.c:328-333); the dispatch mirrors lut2_gemv (lut_gemm_fused.py:1095-1192). */
+int rwkvb_gemv_f32(float* y, const rwkvb_packed* w, const float* x, void* stream);
+
+/* y[cols] = x[rows] @ W for a row-major SG8 W (compact TMix adapters).
+ * Replaces scale_u8_grouped_transposed_gemv_f32_export (lut2_gather.c:939-944). */
+int rwkvb_transposed_gemv_f32(float* y, const rwkvb_packed* w, const float* x, void* stream);
+
+/* y_out[3][n] = (Wr @ xr, Wk @ xk, Wv @ xv) in one launch; `w3` and `x3` are HOST
+ * arrays of 3 descriptors / device pointers, all W of one shape [n, m].
+ * Replaces scale_u8_grouped_tmix_qkv_gemv_f32_export (lut2_gather.c:1436-1449)
+ * behind lut2_tmix_qkv_gemv_batched (lut_gemm_fused.py:1771-1817). */
+int rwkvb_tmix_qkv_gemv_f32(float* y_out, const rwkvb_packed* const* w3,
+                            const float* const* x3, void* stream);
+
+/* Fused RWKV-7 TMix adapters (all SG8):
+ *   w = W2 @ tanh(W1 @ xw); a = sigmoid(a0 + A2 @ (A1 @ xa));
+ *   g = G2 @ sigmoid(G1 @ xg); v = V2 @ (V1 @ xv)   (x @ W convention)
+ * `mats` = HOST array of 8 descriptors w1,w2,a1,a2,g1,g2,v1,v2 (the v pair is
+ * ignored when has_v == 0); `xs` = HOST array of 4 device pointers xw,xa,xg,xv.
+ * Replaces scale_u8_grouped_transposed_tmix_fused_f32_export (lut2_gather.c:1006-1103). */
+int rwkvb_tmix_adapters_f32(float* w_out, float* a_out, float* g_out, float* v_out,
+                            const rwkvb_packed* const* mats, const float* const* xs,
+                            const float* a0, int has_v, void* stream);
+
+/* y = Wv @ relu(Wk @ x)^2 (RWKV-7 channel mix).  The ffn-wide intermediate lives
+ * in a stream-ordered device allocation made by this call.
+ * Replaces scale_u8_grouped_cmix_gemv_f32_export (lut2_gather.c:505-610). */
+int rwkvb_cmix_gemv_f32(float* y, const rwkvb_packed* key, const rwkvb_packed* value,
+                        const float* x, void* stream);
+
+/* WKV7 recurrent state update for `batch` x `n_head` heads of size N = head_size (64):
+ *   d = decay(w);  S = S * diag(d) + (S @ -kk) (kk*a)^T + v k^T;  y = S @ r
+ * state [batch][n_head][N][N] fp32 (value index major), vectors [batch][n_head*N].
+ * decay_mode 0: d = exp(-0.606531 * sigmoid(w))   (rwkv7_linear.py:314, the model form)
+ * decay_mode 1: d = exp(-exp(w))                 (the kernel microbenchmark form)
+ * Replaces the state-update block of tmix_one_fused (rwkv7_linear.py:314-337). */
+int rwkvb_wkv7_f32(float* state, float* y, const float* r, const float* w, const float* k,
+                   const float* v, const float* kk, const float* a, int batch, int n_head,
+                   int head_size, int decay_mode, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Decode engine: the whole packed RWKV-7 token step on the device.
+ * Replaces, per token, forward_block_packed (packed_block_forward.py:76-166) for
+ * every layer, the embedding + ln0 (rwkv7_skeleton.py:74-81), ln_out + packed head
+ * (rwkv7_forward.py:791-809) and greedy argmax (sampling.py:161-163).
+ * ------------------------------------------------------------------------------ */
+
+/* Per-layer tensors.  Matrices are packed descriptors; vectors are fp32 [n_embd]
+ * device arrays (r_k flattened [n_head*head_size], already decoded). */
+typedef struct rwkvb_layer_desc {
+  rwkvb_packed att_r, att_k, att_v, att_o;
+  rwkvb_packed w1, w2, a1, a2, g1, g2, v1, v2; /* v1/v2 unused on layer 0 */
+  rwkvb_packed ffn_key, ffn_value;
+  const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
+  const float *x_r, *x_w, *x_k, *x_v, *x_a, *x_g;
+  const float *w0, *a0, *v0, *k_k, *k_a, *r_k;
+  const float *lnx_w, *lnx_b, *ffn_x_k;
+} rwkvb_layer_desc;
+
+typedef struct rwkvb_model_desc {
+  int32_t n_layer, n_embd, head_size, ffn, vocab;
+  rwkvb_packed emb;  /* [vocab, n_embd] */
+  rwkvb_packed head; /* [vocab, n_embd] */
+  const float *ln0_w, *ln0_b, *ln_out_w, *ln_out_b;
+  const rwkvb_layer_desc* layers; /* HOST array of n_layer descriptors */
+} rwkvb_model_desc;
+
+typedef struct rwkvb_engine rwkvb_engine;
+
+/* Creates an engine on the current device.  The engine copies the descriptors,
+ * owns the recurrent state, activations and scratch, and borrows the weights
+ * (they must stay resident while the engine lives).  flags: bit0 = disable
+ * CUDA-graph capture of the token step. */
+int rwkvb_engine_create(const rwkvb_model_desc* desc, uint32_t flags, rwkvb_engine** out);
+int rwkvb_engine_destroy(rwkvb_engine* e);
+
+/* Device pointers of the recurrent state, laid out as RecurrentState.rwkv7_state
+ * (state_cache.py:38-56, rwkv7_skeleton.py:121-131): per layer l
+ *   att_x + l*n_embd              x_prev of the time mix   [n_embd]
+ *   wkv   + l*n_head*N*N          WKV7 state               [n_head][N][N]
+ *   ffn_x + l*n_embd              x_prev of the channel mix [n_embd]
+ * `logits` = the last step's fp32 logits [vocab]. */
+int rwkvb_engine_buffers(rwkvb_engine* e, float** att_x, float** wkv, float** ffn_x,
+                         float** logits);
+
+/* Zero the recurrent state (rwkv7_skeleton.py:121-131). */
+int rwkvb_engine_reset(rwkvb_engine* e, void* stream);
+
+/* Run one token step per entry of `tokens` (HOST array), in order, updating the
+ * state; logits of the last step stay in the engine's logits buffer. */
+int rwkvb_engine_forward(rwkvb_engine* e, const int32_t* tokens, int32_t n_tokens, void* stream);
+
+/* Greedy decode: step 0 consumes `first_token`; step i>0 consumes step i-1's
+ * argmax, all on the device.  Writes the n argmax ids to out_tokens (HOST).
+ * Synchronises `stream` before returning. */
+int rwkvb_engine_decode_greedy(rwkvb_engine* e, int32_t first_token, int32_t n_tokens,
+                               int32_t* out_tokens, void* stream);
+
+/* Same as rwkvb_engine_decode_greedy but leaves the ids in device memory
+ * (`out_tokens_dev`, n_tokens int32) and does not synchronise. */
+int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first_token, int32_t n_tokens,
+                                     int32_t* out_tokens_dev, void* stream);
+
+/* Kernel launches per token step (for launch accounting). */
+int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RWKV_B200_H */

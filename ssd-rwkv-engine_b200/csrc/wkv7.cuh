@@ -1,0 +1,47 @@
+// WKV7 per-head recurrent state update (RWKV-7 time mix, rwkv7_linear.py:314-337).
+#pragma once
+
+#include "common.cuh"
+
+namespace rwkvb {
+
+// One head, N = 64, 256 threads.  S is the head's [64][64] fp32 state in global
+// memory (row i = value index, column j = key index), updated in place:
+//   sa[i] = sum_j S[i][j] * (-kk[j])
+//   S[i][j] = S[i][j] * d[j] + sa[i] * ka[j] + v[i] * k[j]
+//   y[i] = sum_j S[i][j] * r[j]
+// Vectors live in shared memory.  Thread t owns row t/4, columns (t%4)*16..+16:
+// the state is read and written exactly once, with 64-byte vector accesses.
+__device__ __forceinline__ void wkv7_head64(float* __restrict__ S, const float* r, const float* d,
+                                            const float* k, const float* v, const float* kk, const float* ka,
+                                            float* y) {
+  const int t = threadIdx.x;
+  const int i = t >> 2, q = (t & 3) << 4;
+  float4* row = reinterpret_cast<float4*>(S + i * 64 + q);
+  float s[16];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    float4 a = row[u];
+    s[4 * u] = a.x; s[4 * u + 1] = a.y; s[4 * u + 2] = a.z; s[4 * u + 3] = a.w;
+  }
+  float sa = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) sa = fmaf(s[j], -kk[q + j], sa);
+  sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+  sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+  const float vi = v[i];
+  float yy = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float nv = s[j] * d[q + j] + sa * ka[q + j] + vi * k[q + j];
+    s[j] = nv;
+    yy = fmaf(nv, r[q + j], yy);
+  }
+  yy += __shfl_xor_sync(0xffffffffu, yy, 1);
+  yy += __shfl_xor_sync(0xffffffffu, yy, 2);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) row[u] = make_float4(s[4 * u], s[4 * u + 1], s[4 * u + 2], s[4 * u + 3]);
+  if ((t & 3) == 0) y[i] = yy;
+}
+
+}  // namespace rwkvb

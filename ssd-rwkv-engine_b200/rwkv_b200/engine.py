@@ -1,0 +1,205 @@
+"""Host wrapper of the device decode engine (``rwkvb_engine_*`` in the C ABI).
+
+``B200Engine`` takes a packed RWKV-7 model — a mapping ``name -> entry`` with
+``codec`` (``"sg8"``, ``"lut2"`` or ``"none"``), ``payload`` (wire blob as
+bytes / uint8 tensor, or fp32 values) and checkpoint ``shape`` — uploads it to
+HBM once (``residency.WeightArena``) and drives the fused token step.
+
+It replaces, per token, the reference's embedding + ``ln0``
+(``rwkv7_skeleton.py:74-81``), ``forward_block_packed`` for every layer
+(``packed_block_forward.py:76-166``), ``ln_out`` + packed head
+(``rwkv7_forward.py:791-809``) and greedy argmax (``sampling.py:161-163``).
+The recurrent state keeps the reference ``RecurrentState.rwkv7_state`` layout
+(``state_cache.py:38-56``): per layer ``[x_prev_att (C), S (H, N, N), x_prev_ffn (C)]``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import numpy as np
+import torch
+
+from . import native
+from .residency import VectorArena, WeightArena
+from .synth import RWKV7Shape
+
+_MATS = ("att.receptance.weight", "att.key.weight", "att.value.weight", "att.output.weight",
+         "att.w1", "att.w2", "att.a1", "att.a2", "att.g1", "att.g2", "att.v1", "att.v2",
+         "ffn.key.weight", "ffn.value.weight")
+_DESC_FIELD = {"att.receptance.weight": "att_r", "att.key.weight": "att_k", "att.value.weight": "att_v",
+               "att.output.weight": "att_o", "att.w1": "w1", "att.w2": "w2", "att.a1": "a1", "att.a2": "a2",
+               "att.g1": "g1", "att.g2": "g2", "att.v1": "v1", "att.v2": "v2",
+               "ffn.key.weight": "ffn_key", "ffn.value.weight": "ffn_value"}
+_VEC_FIELD = {"ln1.weight": "ln1_w", "ln1.bias": "ln1_b", "ln2.weight": "ln2_w", "ln2.bias": "ln2_b",
+              "att.x_r": "x_r", "att.x_w": "x_w", "att.x_k": "x_k", "att.x_v": "x_v", "att.x_a": "x_a",
+              "att.x_g": "x_g", "att.w0": "w0", "att.a0": "a0", "att.v0": "v0", "att.k_k": "k_k",
+              "att.k_a": "k_a", "att.ln_x.weight": "lnx_w", "att.ln_x.bias": "lnx_b", "ffn.x_k": "ffn_x_k"}
+
+
+class _CudaArray:
+    """Expose a raw device pointer to torch via ``__cuda_array_interface__``."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def infer_shape(pack) -> RWKV7Shape:
+    """Model dimensions from checkpoint tensor shapes."""
+    L = 1 + max(int(m.group(1)) for n in pack if (m := re.match(r"blocks\.(\d+)\.", n)))
+    V, C = pack["emb.weight"].shape
+    H, N = pack["blocks.0.att.r_k"].shape
+    F = pack["blocks.0.ffn.key.weight"].shape[0]
+    rw = pack["blocks.0.att.w1"].shape[1]
+    ra = pack["blocks.0.att.a1"].shape[1]
+    rv = pack["blocks.1.att.v1"].shape[1] if L > 1 else pack["blocks.0.att.v1"].shape[1]
+    rg = pack["blocks.0.att.g1"].shape[1]
+    return RWKV7Shape(L, int(C), int(N), int(F), int(V), int(rw), int(ra), int(rv), int(rg))
+
+
+class B200Engine:
+    """A packed RWKV-7 model resident on one GPU, decoded by the fused engine."""
+
+    def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
+                 prefetch_distance: int | None = None):
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
+        self.lib = native.lib()
+        self.shape = infer_shape(pack)
+        s = self.shape
+        with torch.cuda.device(self.device):
+            mats, vecs = [], {}
+            for name, e in pack.items():
+                if e.codec in ("sg8", "lut2"):
+                    mats.append((name, e.payload, (int(e.shape[0]), int(e.shape[1])), e.codec))
+                else:
+                    vecs[name] = np.asarray(e.payload, dtype=np.float32).reshape(-1) \
+                        if not isinstance(e.payload, torch.Tensor) else e.payload
+            self.weights = WeightArena(mats, self.device)
+            self.vectors = VectorArena(vecs, self.device)
+            for i in range(s.n_layer):
+                nm = f"blocks.{i}.att.r_k"
+                if nm in self.weights:
+                    self.vectors.add_decoded(nm, self.weights[nm])
+            torch.cuda.synchronize(self.device)
+            self._layers = (native.LayerDesc * s.n_layer)()
+            for i in range(s.n_layer):
+                d = self._layers[i]
+                for suffix in _MATS:
+                    name = f"blocks.{i}.{suffix}"
+                    if name in self.weights:
+                        setattr(d, _DESC_FIELD[suffix], self.weights[name].desc)
+                for suffix, field in _VEC_FIELD.items():
+                    name = f"blocks.{i}.{suffix}"
+                    if name in self.vectors.offs or name in self.vectors.extra:
+                        setattr(d, field, self.vectors.ptr(name))
+                d.r_k = self.vectors.ptr(f"blocks.{i}.att.r_k")
+            md = native.ModelDesc()
+            md.n_layer, md.n_embd, md.head_size, md.ffn, md.vocab = s.n_layer, s.n_embd, s.head_size, s.ffn, s.vocab
+            md.emb = self.weights["emb.weight"].desc
+            md.head = self.weights["head.weight"].desc
+            md.ln0_w = self.vectors.ptr("blocks.0.ln0.weight")
+            md.ln0_b = self.vectors.ptr("blocks.0.ln0.bias")
+            md.ln_out_w = self.vectors.ptr("ln_out.weight")
+            md.ln_out_b = self.vectors.ptr("ln_out.bias")
+            md.layers = self._layers
+            flags = 0 if use_graph else native.FLAG_NO_GRAPH
+            if prefetch_distance is not None:
+                flags |= native.FLAG_EXPLICIT_PREFETCH | ((int(prefetch_distance) & 0xF) << 4)
+            h = ctypes.c_void_p()
+            native.check(self.lib.rwkvb_engine_create(ctypes.byref(md), flags, ctypes.byref(h)),
+                         "rwkvb_engine_create")
+            self._h = h
+            att, wkv, ffn, logits = (ctypes.c_void_p() for _ in range(4))
+            native.check(self.lib.rwkvb_engine_buffers(h, ctypes.byref(att), ctypes.byref(wkv), ctypes.byref(ffn),
+                                                       ctypes.byref(logits)), "rwkvb_engine_buffers")
+            L, C, H, N = s.n_layer, s.n_embd, s.n_head, s.head_size
+            dev = self.device
+            self.att_x = torch.as_tensor(_CudaArray(att.value, (L, C)), device=dev)
+            self.wkv = torch.as_tensor(_CudaArray(wkv.value, (L, H, N, N)), device=dev)
+            self.ffn_x = torch.as_tensor(_CudaArray(ffn.value, (L, C)), device=dev)
+            self.logits = torch.as_tensor(_CudaArray(logits.value, (s.vocab,)), device=dev)
+            n = ctypes.c_int32()
+            native.check(self.lib.rwkvb_engine_launches_per_step(h, ctypes.byref(n)), "launches_per_step")
+            self.launches_per_step = int(n.value)
+
+    # ------------------------------------------------------------ lifecycle
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            torch.cuda.synchronize(self.device)
+            self.lib.rwkvb_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _stream(self, stream=None) -> int:
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        return st.cuda_stream
+
+    # --------------------------------------------------------------- state
+    def reset(self, stream=None) -> None:
+        native.check(self.lib.rwkvb_engine_reset(self._h, self._stream(stream)), "rwkvb_engine_reset")
+
+    def get_state(self) -> list[torch.Tensor]:
+        """Clone of the state as ``RecurrentState.rwkv7_state`` (3 tensors per layer)."""
+        out = []
+        for i in range(self.shape.n_layer):
+            out += [self.att_x[i].clone(), self.wkv[i].clone(), self.ffn_x[i].clone()]
+        return out
+
+    def set_state(self, state: list[torch.Tensor]) -> None:
+        if len(state) != 3 * self.shape.n_layer:
+            raise ValueError(f"expected {3 * self.shape.n_layer} state tensors, got {len(state)}")
+        for i in range(self.shape.n_layer):
+            self.att_x[i].copy_(state[3 * i].reshape(-1).to(self.device, torch.float32))
+            self.wkv[i].copy_(state[3 * i + 1].reshape(self.wkv[i].shape).to(self.device, torch.float32))
+            self.ffn_x[i].copy_(state[3 * i + 2].reshape(-1).to(self.device, torch.float32))
+
+    # ------------------------------------------------------------- stepping
+    def forward(self, tokens, stream=None) -> torch.Tensor:
+        """Run one step per token; returns the device logits of the last step."""
+        toks = (ctypes.c_int32 * len(tokens))(*[int(t) for t in tokens])
+        native.check(self.lib.rwkvb_engine_forward(self._h, toks, len(tokens), self._stream(stream)),
+                     "rwkvb_engine_forward")
+        return self.logits
+
+    def decode_greedy(self, first_token: int, n: int, stream=None) -> list[int]:
+        out = (ctypes.c_int32 * max(n, 1))()
+        native.check(self.lib.rwkvb_engine_decode_greedy(self._h, int(first_token), int(n), out,
+                                                         self._stream(stream)), "rwkvb_engine_decode_greedy")
+        return [int(v) for v in out[:n]]
+
+    def decode_greedy_async(self, first_token: int, n: int, out: torch.Tensor, stream=None) -> None:
+        if out.dtype != torch.int32 or not out.is_cuda or out.numel() < n:
+            raise ValueError("out must be a CUDA int32 tensor with at least n elements")
+        native.check(self.lib.rwkvb_engine_decode_greedy_async(self._h, int(first_token), int(n), out.data_ptr(),
+                                                               self._stream(stream)),
+                     "rwkvb_engine_decode_greedy_async")
+
+    def greedy(self, prompt: list[int], n_new: int, keep_logits: bool = False):
+        """Prompt token by token, then ``n_new`` greedy ids (as the oracle's ``greedy``)."""
+        rows = []
+        if keep_logits:
+            for t in prompt:
+                self.forward([t])
+                rows.append(self.logits.clone())
+        else:
+            self.forward(prompt)
+        first = int(torch.argmax(self.logits).item())
+        ids = [first]
+        if keep_logits:
+            for i in range(1, n_new):
+                self.forward([ids[-1]])
+                rows.append(self.logits.clone())
+                ids.append(int(torch.argmax(self.logits).item()))
+            return ids, torch.stack(rows)
+        if n_new > 1:
+            ids += self.decode_greedy(first, n_new - 1)
+        return ids, None

@@ -292,3 +292,36 @@ def packed_nbytes(pack: dict[str, PackedTensor], names=None) -> int:
         tot += len(p) if isinstance(p, (bytes, bytearray)) else int(np.prod(getattr(p, "shape", (0,)))) * (
             1 if e.codec != "none" else 4)
     return tot
+
+
+def make_pack_streaming(s: RWKV7Shape, seed: int, device="cuda", *, policy: str = "sg8", sg8_group: int = 128,
+                        lut2_group: int = 64) -> dict[str, PackedTensor]:
+    """Draw and encode one tensor at a time on ``device`` (blobs stay uint8
+    tensors there), so multi-GB packs never hold the whole fp32 model."""
+    gen = torch.Generator(device=device)
+    gen.manual_seed(int(seed))
+    out: dict[str, PackedTensor] = {}
+    for name, shp, kind in tensor_specs(s):
+        t = _draw(kind, shp, gen, device)
+        codec = codec_for(name, shp, policy)
+        if codec == "sg8":
+            payload = encode_sg8(t, sg8_group)
+        elif codec == "lut2":
+            payload = encode_lut2(t, lut2_group)
+        else:
+            payload = t.reshape(-1).clone()
+        out[name] = PackedTensor(name, shp, codec, payload)
+        del t
+    return out
+
+
+def pack_to_host(pack: dict[str, PackedTensor]) -> dict[str, PackedTensor]:
+    """Host copy (bytes / fp32 numpy) of a device-resident pack."""
+    out = {}
+    for n, e in pack.items():
+        p = e.payload
+        if isinstance(p, torch.Tensor):
+            p = p.cpu().numpy()
+            p = p.tobytes() if e.codec != "none" else p.astype(np.float32)
+        out[n] = PackedTensor(n, e.shape, e.codec, p)
+    return out
