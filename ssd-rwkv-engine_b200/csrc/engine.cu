@@ -1,22 +1,26 @@
-// Fused RWKV-7 decode engine: one packed-model token step as a chain of
-// phase kernels captured in a CUDA graph.
+// Fused RWKV-7 decode engine: one packed-model token step as a chain of phase
+// kernels, launched with programmatic dependent launch (PDL) and captured in a
+// CUDA graph.
 //
 // Per layer (mirrors forward_block_packed, packed_block_forward.py:76-166):
-//   att_in  : ln1 + token-shift mixes (rwkv7_linear.py:165-171), r/k/v GEMVs
-//             and the first adapter projections (x @ W1, A1, G1, V1) as
-//             split-row partial sums
-//   wkv     : one CTA per head: adapter second projections for the head's
-//             channels, kk-normalize, k update, v-first mix, decay, WKV7
-//             state update, GroupNorm, bonus, gate (rwkv7_linear.py:301-349)
+//   att_in  : ln1 + token-shift mixes (rwkv7_linear.py:165-171); r/k/v GEMVs;
+//             first adapter projections (x @ W1, A1, G1, V1) as split-row
+//             partial sums
+//   wkv     : one CTA per head: second adapter projections for the head's
+//             channels, kk-normalize, k update, v-first mix, decay, WKV7 state
+//             update, GroupNorm, bonus, gate (rwkv7_linear.py:301-349)
 //   att_out : output GEMV + residual; x_prev(att) <- ln1(x)
 //   ffn_in  : ln2 + mix, key GEMV, relu^2 (rwkv7_linear.py:370-371, 409)
 //   ffn_out : value GEMV + residual; x_prev(ffn) <- ln2(x)
 // then head: ln_out + head GEMV + greedy argmax (first maximum).
 //
-// Weights are streamed once per token.  Every phase kernel first issues bulk
-// L2 prefetches of the weights of the phase `prefetch_distance` steps ahead
-// (split across its CTAs), so HBM keeps streaming while the dependent chain
-// of small kernels advances.
+// Data movement.  Weights never depend on the previous kernel, so every phase
+// kernel starts its weight transfers (1-D TMA bulk copies into a shared-memory
+// ring for the large SG8 projections, cp.async for the small adapter tiles)
+// BEFORE `griddepcontrol.wait`; it then releases its dependent
+// (`launch_dependents`) so the next phase can start its own transfers while
+// this one computes.  Everything mutable (activations, recurrent state) is
+// read and written only after the wait.
 #include <cstring>
 #include <new>
 #include <vector>
@@ -24,12 +28,17 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "internal.h"
+#include "stream.cuh"
 #include "wkv7.cuh"
 
 namespace rwkvb {
 
 constexpr int kThreads = 256;
+constexpr int kWkvThreads = 1024;
 constexpr int kMaxPf = 8;
+constexpr int kSlotBudget = 20 * 1024;
+constexpr int kSlots = 4;
+constexpr int kAdpRowsMax = 128;  // rows of a first-adapter matrix per CTA (upper bound)
 
 struct Prefetch {
   const uint8_t* ptr[kMaxPf];
@@ -40,8 +49,6 @@ struct Prefetch {
 
 struct LayerDev {
   PackedView r, k, v, o, w1, w2, a1, a2, g1, g2, v1, v2, fk, fv;
-  int mode_r, mode_k, mode_v, mode_o, mode_fk, mode_fv;
-  int lg_r, lg_k, lg_v, lg_o, lg_fk, lg_fv;
   const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
   const float *x_r, *x_w, *x_k, *x_v, *x_a, *x_g;
   const float *w0, *a0, *v0, *k_k, *k_a, *r_k, *lnx_w, *lnx_b, *ffn_x_k;
@@ -63,13 +70,13 @@ struct Bufs {
   int *tok;                    // token consumed by the next step
   int *hist;                   // argmax history ring
   int *step;                   // steps since the last history reset
-  int *err;                    // error flags (bit0: token out of range)
+  int *err;                    // error flags (kErrToken | kErrTimeout)
 };
 
 struct Dims {
   int L, C, H, F, V;
   int rw, ra, rg, rv, rtot;  // adapter ranks, total
-  int adp_splits, adp_rows;  // first-adapter row split
+  int adp_splits, adp_rows;  // first-adapter row chunks
   int hist_cap;
 };
 
@@ -98,12 +105,12 @@ __device__ __forceinline__ void issue_prefetch(const Prefetch& pf) {
   }
 }
 
-// LayerNorm of a global vector into shared memory (two-pass mean / variance).
+// LayerNorm (two-pass mean / variance, eps 1e-5) of x[0..C) into out (shared).
 __device__ __forceinline__ void layer_norm_to_smem(const float* x, const float* w, const float* b, int C,
                                                    float* out, float* red) {
   float s = 0.f;
   for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    float v = x[i];
+    float v = __ldcg(x + i);
     out[i] = v;
     s += v;
   }
@@ -119,6 +126,43 @@ __device__ __forceinline__ void layer_norm_to_smem(const float* x, const float* 
   __syncthreads();
 }
 
+// Shared-memory carve-up for ring phases: [ring slots][bars][partials][ln]
+struct RingLayout {
+  uint32_t slots_off, bars_off, part_off, ln_off, total;
+};
+
+__host__ inline RingLayout ring_layout(const RingPlan& P, int ln_floats) {
+  RingLayout L;
+  L.slots_off = 0;
+  L.bars_off = (uint32_t)P.nst * P.slot_bytes;
+  L.bars_off = (L.bars_off + 15) & ~15u;
+  L.part_off = L.bars_off + 8 * kSlots;
+  L.ln_off = L.part_off + (uint32_t)(2 * P.rs * P.nseg * 4);
+  L.ln_off = (L.ln_off + 15) & ~15u;
+  L.total = L.ln_off + (uint32_t)ln_floats * 4 + 16;
+  return L;
+}
+
+__device__ __forceinline__ RingSmem ring_smem(uint8_t* base, const RingLayout& L) {
+  RingSmem S;
+  S.slots = base + L.slots_off;
+  S.bars = reinterpret_cast<uint64_t*>(base + L.bars_off);
+  S.part = reinterpret_cast<float*>(base + L.part_off);
+  return S;
+}
+
+template <class XIn, class Epi>
+__device__ __forceinline__ bool ring_dispatch(int cpl, const PackedView& W, const RingPlan& P, const RingSmem& S,
+                                              XIn xin, Epi epi, int* err) {
+  switch (cpl) {
+    case 1: return ring_run<1>(W, P, S, xin, epi, err);
+    case 2: return ring_run<2>(W, P, S, xin, epi, err);
+    case 3: return ring_run<3>(W, P, S, xin, epi, err);
+    case 4: return ring_run<4>(W, P, S, xin, epi, err);
+    default: return ring_run<5>(W, P, S, xin, epi, err);
+  }
+}
+
 // ------------------------------------------------------------- embed
 struct EmbedArgs {
   PackedView emb;
@@ -131,18 +175,30 @@ struct EmbedArgs {
 __global__ void __launch_bounds__(kThreads) embed_kernel(EmbedArgs a) {
   __shared__ float red[32];
   extern __shared__ __align__(16) float sm[];
+  pdl_launch_dependents();
   issue_prefetch(a.pf);
+  pdl_wait();
   const int C = a.d.C;
-  int tok = *a.b.tok;
+  int tok = __ldcg(a.b.tok);
   if (tok < 0 || tok >= a.d.V) {
-    if (threadIdx.x == 0) atomicOr(a.b.err, 1);
+    if (threadIdx.x == 0) atomicOr(a.b.err, kErrToken);
     tok = 0;
   }
   float* row = sm;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) row[i] = packed_at(a.emb, tok, i);
-  __syncthreads();
-  layer_norm_to_smem(row, a.ln0_w, a.ln0_b, C, row, red);
-  for (int i = threadIdx.x; i < C; i += blockDim.x) a.b.xa[i] = row[i];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float v = packed_at(a.emb, tok, i);
+    row[i] = v;
+    s += v;
+  }
+  const float mean = block_sum(s, red) / (float)C;
+  float q = 0.f;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float dd = row[i] - mean;
+    q += dd * dd;
+  }
+  const float rstd = rsqrtf(block_sum(q, red) / (float)C + 1e-5f);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) a.b.xa[i] = (row[i] - mean) * rstd * a.ln0_w[i] + a.ln0_b[i];
 }
 
 // ------------------------------------------------------------ att_in
@@ -151,55 +207,100 @@ struct AttInArgs {
   Bufs b;
   Dims d;
   Prefetch pf;
-  int rkv_ctas, rkv_rpc;  // CTAs [0, rkv_ctas) do r/k/v rows; the rest adapters
+  RingPlan plan;      // row range resolved per CTA
+  RingLayout lay;
+  int cpl;
+  int ring;           // 1: ring path for r/k/v; 0: direct loads
+  int gm;             // CTAs per matrix (r, k, v)
+  int mode[3], lg[3]; // direct-path modes
   int layer;
 };
 
 __global__ void __launch_bounds__(kThreads, 2) att_in_kernel(AttInArgs a) {
   __shared__ float red[32];
-  extern __shared__ __align__(16) float sm[];
-  issue_prefetch(a.pf);
+  extern __shared__ __align__(16) uint8_t smb[];
   const int C = a.d.C;
-  float* ln = sm;                       // ln1(x)          [C]
-  float* sx = sm + C;                   // mixed input     [C]
-  float* sxc = sx + C;                  // chunk sums      [C/16]
-  layer_norm_to_smem(a.b.xa, a.l.ln1_w, a.l.ln1_b, C, ln, red);
-  const float* prev = a.b.att_x + (size_t)a.layer * C;
-  if (blockIdx.x == 0)
-    for (int i = threadIdx.x; i < C; i += blockDim.x) a.b.xln1[i] = ln[i];
-
-  if ((int)blockIdx.x < a.rkv_ctas) {
-    const int g0 = blockIdx.x * a.rkv_rpc;
-    const int g1 = min(3 * C, g0 + a.rkv_rpc);
-    for (int m = g0 / C; m <= (g1 - 1) / C && g0 < g1; ++m) {
-      const int r0 = max(g0, m * C) - m * C, r1 = min(g1, (m + 1) * C) - m * C;
-      const float* mix = m == 0 ? a.l.x_r : (m == 1 ? a.l.x_k : a.l.x_v);
-      const PackedView& W = m == 0 ? a.l.r : (m == 1 ? a.l.k : a.l.v);
-      const int mode = m == 0 ? a.l.mode_r : (m == 1 ? a.l.mode_k : a.l.mode_v);
-      const int lg = m == 0 ? a.l.lg_r : (m == 1 ? a.l.lg_k : a.l.lg_v);
-      if (mode == 1) {
-        stage_input(C, sx, sxc, [&](int i) { return ln[i] + (prev[i] - ln[i]) * mix[i]; });
+  const bool rkv = (int)blockIdx.x < 3 * a.gm;
+  if (rkv) {
+    const int m = blockIdx.x / a.gm, cb = blockIdx.x % a.gm;
+    const PackedView& W = m == 0 ? a.l.r : (m == 1 ? a.l.k : a.l.v);
+    const float* mix = m == 0 ? a.l.x_r : (m == 1 ? a.l.x_k : a.l.x_v);
+    float* out = a.b.rkv + (size_t)m * C;
+    RingPlan P = a.plan;
+    P.row0 = cb * a.plan.row1;  // plan.row1 holds rows per CTA
+    P.row1 = min(C, P.row0 + a.plan.row1);
+    RingSmem S = ring_smem(smb, a.lay);
+    float* ln = reinterpret_cast<float*>(smb + a.lay.ln_off);
+    if (a.ring && P.row0 < P.row1) ring_start(W, P, S);
+    pdl_launch_dependents();
+    issue_prefetch(a.pf);
+    pdl_wait();
+    layer_norm_to_smem(a.b.xa, a.l.ln1_w, a.l.ln1_b, C, ln, red);
+    if (blockIdx.x == 0)
+      for (int i = threadIdx.x; i < C; i += blockDim.x) a.b.xln1[i] = ln[i];
+    if (P.row0 >= P.row1) return;
+    const float* prev = a.b.att_x + (size_t)a.layer * C;
+    if (a.ring) {
+      ring_dispatch(a.cpl, W, P, S, [&](int i) { return ln[i] + (__ldcg(prev + i) - ln[i]) * __ldg(mix + i); },
+                    [&](int row, float v) { out[row] = v; }, a.b.err);
+    } else {
+      float* sx = ln + C;
+      float* sxc = sx + C;
+      if (a.mode[m] == 1) {
+        stage_input(C, sx, sxc, [&](int i) { return ln[i] + (__ldcg(prev + i) - ln[i]) * mix[i]; });
       } else {
-        for (int i = threadIdx.x; i < C; i += blockDim.x) sx[i] = ln[i] + (prev[i] - ln[i]) * mix[i];
+        for (int i = threadIdx.x; i < C; i += blockDim.x) sx[i] = ln[i] + (__ldcg(prev + i) - ln[i]) * mix[i];
         __syncthreads();
       }
-      float* out = a.b.rkv + (size_t)m * C;
-      packed_rows(W, mode, lg, sx, sxc, r0, r1, [&](int row, float v) { out[row] = v; });
-      __syncthreads();
+      packed_rows(W, a.mode[m], a.lg[m], sx, sxc, P.row0, P.row1, [&](int row, float v) { out[row] = v; });
     }
-  } else {
-    // first adapter projections: work item = (matrix, row chunk)
-    const int item = blockIdx.x - a.rkv_ctas;
-    const int nm = a.layer == 0 ? 3 : 4;
-    const int m = item / a.d.adp_splits, s = item % a.d.adp_splits;
-    if (m >= nm) return;
-    const float* mix = m == 0 ? a.l.x_w : (m == 1 ? a.l.x_a : (m == 2 ? a.l.x_g : a.l.x_v));
-    const PackedView& W = m == 0 ? a.l.w1 : (m == 1 ? a.l.a1 : (m == 2 ? a.l.g1 : a.l.v1));
-    const int off = m == 0 ? 0 : (m == 1 ? a.d.rw : (m == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
-    const int i0 = s * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows);
-    for (int i = threadIdx.x; i < C; i += blockDim.x) sx[i] = ln[i] + (prev[i] - ln[i]) * mix[i];
-    __syncthreads();
-    transposed_partial(W, sx, i0, i1, 0, W.cols, a.b.adp + (size_t)s * a.d.rtot + off);
+    return;
+  }
+  // first adapter projections: work item = (matrix, chunk of adp_rows rows)
+  const int item = blockIdx.x - 3 * a.gm;
+  const bool active = item < (a.layer == 0 ? 3 : 4) * a.d.adp_splits;
+  const int m = item / a.d.adp_splits, s = item % a.d.adp_splits;
+  const PackedView& W = m == 0 ? a.l.w1 : (m == 1 ? a.l.a1 : (m == 2 ? a.l.g1 : a.l.v1));
+  const float* mix = m == 0 ? a.l.x_w : (m == 1 ? a.l.x_a : (m == 2 ? a.l.x_g : a.l.x_v));
+  const int off = m == 0 ? 0 : (m == 1 ? a.d.rw : (m == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
+  const int R = W.cols;
+  const int i0 = s * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows);
+  float* ln = reinterpret_cast<float*>(smb);
+  uint8_t* tq = smb + (size_t)C * 4;                                   // codes [rows][R]
+  float2* tsc = reinterpret_cast<float2*>(tq + kAdpRowsMax * R + 16);  // scale pairs
+  const bool tiled = W.kind == RWKVB_KIND_SG8 && W.lg >= 0 && (R % 16) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(W.payload) & 15u) == 0);
+  uint32_t g0 = 0, ng = 0;
+  if (active && tiled && i0 < i1) {
+    // codes with cp.async (16B pieces), scale pairs with plain 8-byte loads
+    cp_async_block(tq, W.payload + (size_t)i0 * R, (uint32_t)((i1 - i0) * R));
+    cp_async_commit();
+    g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg);
+    ng = (uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) - g0 + 1);
+    for (uint32_t j = threadIdx.x; j < ng; j += blockDim.x)
+      tsc[j] = __ldg(reinterpret_cast<const float2*>(W.meta) + g0 + j);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+  if (!active) return;
+  layer_norm_to_smem(a.b.xa, a.l.ln1_w, a.l.ln1_b, C, ln, red);
+  const float* prev = a.b.att_x + (size_t)a.layer * C;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) ln[i] = ln[i] + (__ldcg(prev + i) - ln[i]) * mix[i];
+  if (tiled) cp_async_wait_all();
+  __syncthreads();
+  float* outp = a.b.adp + (size_t)s * a.d.rtot + off;
+  for (int j = threadIdx.x; j < R; j += blockDim.x) {
+    float acc = 0.f;
+    if (tiled) {
+      for (int i = i0; i < i1; ++i) {
+        const uint32_t e = (uint32_t)i * (uint32_t)R + (uint32_t)j;
+        const float2 sc = tsc[(e >> W.lg) - g0];
+        acc = fmaf(ln[i], sg8_dequant(tq[(i - i0) * R + j], sc.x, sc.y), acc);
+      }
+    } else {
+      for (int i = i0; i < i1; ++i) acc = fmaf(ln[i], packed_at(W, i, j), acc);
+    }
+    outp[j] = acc;
   }
 }
 
@@ -210,16 +311,19 @@ struct WkvArgs {
   Dims d;
   Prefetch pf;
   int layer;
+  int tiled;  // second-adapter tiles staged with cp.async (SG8, group >= 64)
 };
 
-__global__ void __launch_bounds__(1024) wkv_kernel(WkvArgs a) {
+__global__ void __launch_bounds__(kWkvThreads) wkv_kernel(WkvArgs a) {
   __shared__ float red[32];
-  extern __shared__ __align__(16) float sm[];
-  issue_prefetch(a.pf);
-  const int h = blockIdx.x, C = a.d.C;
+  extern __shared__ __align__(16) uint8_t smb[];
+  const int h = blockIdx.x, C = a.d.C, t = threadIdx.x;
   const int nm = a.layer == 0 ? 3 : 4;
-  float* mid = sm;                          // [rtot] first-projection results
-  float* vec = sm + ((a.d.rtot + 3) & ~3);  // 4 x 64: w, a, g, v_gate of this head
+  const int R[4] = {a.d.rw, a.d.ra, a.d.rg, a.d.rv};
+  const int off[4] = {0, a.d.rw, a.d.rw + a.d.ra, a.d.rw + a.d.ra + a.d.rg};
+  float* S = reinterpret_cast<float*>(smb);                          // [64][64] state
+  float* mid = S + 4096;                                            // [rtot]
+  float* vec = mid + ((a.d.rtot + 3) & ~3);                         // 4 x 64
   float* sr = vec + 256;
   float* sd = sr + 64;
   float* sk = sd + 64;
@@ -227,56 +331,74 @@ __global__ void __launch_bounds__(1024) wkv_kernel(WkvArgs a) {
   float* skk = sv + 64;
   float* ska = skk + 64;
   float* sy = ska + 64;
+  float2* tsc = reinterpret_cast<float2*>(sy + 64);                 // [rtot] scale pair per row
+  uint8_t* tq = reinterpret_cast<uint8_t*>(tsc + a.d.rtot);         // [rtot][64] codes
+  // constant weights first: this head's 64 columns of W2/A2/G2/V2
+  if (a.tiled) {
+    for (int m = 0; m < nm; ++m) {
+      const PackedView& W = m == 0 ? a.l.w2 : (m == 1 ? a.l.a2 : (m == 2 ? a.l.g2 : a.l.v2));
+      for (int u = t; u < R[m] * 4; u += blockDim.x) {
+        const int i = u >> 2, p = u & 3;
+        cp_async16(tq + (size_t)(off[m] + i) * 64 + p * 16, W.payload + (size_t)i * C + h * 64 + p * 16);
+      }
+      for (int i = t; i < R[m]; i += blockDim.x)
+        tsc[off[m] + i] = __ldg(reinterpret_cast<const float2*>(W.meta) + (((size_t)i * C + h * 64) >> W.lg));
+    }
+    cp_async_commit();
+  }
+  pdl_launch_dependents();
+  issue_prefetch(a.pf);
+  pdl_wait();
+  // this head's recurrent state
+  float* Sg = a.b.wkv + ((size_t)a.layer * a.d.H + h) * 4096;
+  for (int u = t; u < 1024; u += blockDim.x) cp_async16(S + u * 4, Sg + u * 4);
+  cp_async_commit();
   // reduce the first-projection partial sums (fixed order) and activate
   const int used = a.layer == 0 ? a.d.rw + a.d.ra + a.d.rg : a.d.rtot;
-  for (int j = threadIdx.x; j < used; j += blockDim.x) {
+  for (int j = t; j < used; j += blockDim.x) {
     float acc = 0.f;
-    for (int s = 0; s < a.d.adp_splits; ++s) acc += a.b.adp[(size_t)s * a.d.rtot + j];
+    for (int s = 0; s < a.d.adp_splits; ++s) acc += __ldcg(a.b.adp + (size_t)s * a.d.rtot + j);
     if (j < a.d.rw) acc = tanhf(acc);
     else if (j >= a.d.rw + a.d.ra && j < a.d.rw + a.d.ra + a.d.rg) acc = sigmoidf_(acc);
     mid[j] = acc;
   }
+  cp_async_wait_all();
   __syncthreads();
-  // second projections for this head's 64 channels:
-  // thread -> (matrix m, channel c, quarter q of the rank), reduced over q
+  // second projections for the head's 64 channels: thread -> (matrix, channel, quarter)
   {
-    const int t = threadIdx.x;
     const int q = t & 3, c = (t >> 2) & 63, m = t >> 8;
     float acc = 0.f;
     if (m < nm) {
-      const PackedView& W = m == 0 ? a.l.w2 : (m == 1 ? a.l.a2 : (m == 2 ? a.l.g2 : a.l.v2));
-      const int off = m == 0 ? 0 : (m == 1 ? a.d.rw : (m == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
-      const int ch = h * 64 + c;
-      for (int i = q; i < W.rows; i += 4) acc = fmaf(mid[off + i], packed_at(W, i, ch), acc);
+      if (a.tiled) {
+        for (int i = q; i < R[m]; i += 4) {
+          const float2 sc = tsc[off[m] + i];
+          acc = fmaf(mid[off[m] + i], sg8_dequant(tq[(size_t)(off[m] + i) * 64 + c], sc.x, sc.y), acc);
+        }
+      } else {
+        const PackedView& W = m == 0 ? a.l.w2 : (m == 1 ? a.l.a2 : (m == 2 ? a.l.g2 : a.l.v2));
+        for (int i = q; i < R[m]; i += 4) acc = fmaf(mid[off[m] + i], packed_at(W, i, h * 64 + c), acc);
+      }
     }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
     acc += __shfl_xor_sync(0xffffffffu, acc, 2);
     if (q == 0 && m < nm) vec[m * 64 + c] = acc;
   }
   __syncthreads();
-  // per-channel preparation (threads 0..63)
-  const int t = threadIdx.x;
   float kkv = 0.f;
-  if (t < 64) {
-    const int ch = h * 64 + t;
-    const float k = a.b.rkv[C + ch];
-    kkv = k * a.l.k_k[ch];
-  }
-  // ||kk|| over the head: threads 0..63 hold the values, others hold 0
+  if (t < 64) kkv = __ldcg(a.b.rkv + C + h * 64 + t) * a.l.k_k[h * 64 + t];
   const float nrm = sqrtf(block_sum(kkv * kkv, red));
   if (t < 64) {
     const int ch = h * 64 + t;
-    const float r = a.b.rkv[ch];
-    const float k = a.b.rkv[C + ch];
-    float v = a.b.rkv[2 * C + ch];
+    const float r = __ldcg(a.b.rkv + ch);
+    const float k = __ldcg(a.b.rkv + C + ch);
+    float v = __ldcg(a.b.rkv + 2 * C + ch);
     const float aa = sigmoidf_(a.l.a0[ch] + vec[64 + t]);
     const float kk = kkv / fmaxf(nrm, 1e-12f);
     const float kn = k * (1.0f + (aa - 1.0f) * a.l.k_a[ch]);
     if (a.layer == 0) {
       a.b.v_first[ch] = v;
     } else {
-      const float vf = a.b.v_first[ch];
-      v = v + (vf - v) * sigmoidf_(a.l.v0[ch] + vec[192 + t]);
+      v = v + (__ldcg(a.b.v_first + ch) - v) * sigmoidf_(a.l.v0[ch] + vec[192 + t]);
     }
     sr[t] = r;
     sd[t] = expf(-0.606531f * sigmoidf_(a.l.w0[ch] + vec[t]));
@@ -286,10 +408,12 @@ __global__ void __launch_bounds__(1024) wkv_kernel(WkvArgs a) {
     ska[t] = kk * aa;
   }
   __syncthreads();
-  if (t < 256) wkv7_head64(a.b.wkv + ((size_t)a.layer * a.d.H + h) * 4096, sr, sd, sk, sv, skk, ska, sy);
+  if (t < 256) wkv7_head64(S, sr, sd, sk, sv, skk, ska, sy);
   __syncthreads();
+  for (int u = t; u < 1024; u += blockDim.x)
+    reinterpret_cast<float4*>(Sg)[u] = reinterpret_cast<const float4*>(S)[u];
   // GroupNorm over the head (eps 64e-5), bonus, gate
-  float yv = t < 64 ? sy[t] : 0.f;
+  const float yv = t < 64 ? sy[t] : 0.f;
   const float mean = block_sum(yv, red) / 64.f;
   const float dv = t < 64 ? yv - mean : 0.f;
   const float var = block_sum(dv * dv, red) / 64.f;
@@ -303,99 +427,119 @@ __global__ void __launch_bounds__(1024) wkv_kernel(WkvArgs a) {
   }
 }
 
-// ------------------------------------------------------ generic GEMV phase
-// One packed GEMV over `rows` rows with the input staged from `src` (optionally
-// layer-normed and token-shift mixed) and a residual / activation epilogue.
-struct GemvPhaseArgs {
+// ------------------------------------------------------ GEMV phases
+// kinds: 0 att_out, 1 ffn_in, 2 ffn_out, 3 head
+struct PhaseArgs {
   PackedView w;
-  int mode, lg, rpc;
-  // input = ln ? mix(LN(src)) : src ; mix(z) = z + (prev - z) * mixv
-  const float* src;
-  const float *ln_w, *ln_b, *prev, *mixv;
-  float* ln_out;      // CTA 0 stores LN(src) here (may be null)
-  // epilogue: out[row] = resid ? resid[row] + v : (relu2 ? relu(v)^2 : v)
-  float* out;
-  const float* resid;
-  int relu2;
-  // state copy: state_dst[row] = state_src[row] for this CTA's rows
-  float* state_dst;
-  const float* state_src;
+  RingPlan plan;
+  RingLayout lay;
+  int cpl, ring, mode, lg;
+  int kind;
+  int layer;
+  const float *ln_w, *ln_b, *mixv;
   Prefetch pf;
-  // argmax (head)
-  int argmax;
   Bufs b;
   Dims d;
 };
 
-__global__ void __launch_bounds__(kThreads, 2) gemv_phase_kernel(GemvPhaseArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) phase_kernel(PhaseArgs a) {
   __shared__ float red[32];
   __shared__ float bv[kThreads / 32];
   __shared__ int bi[kThreads / 32];
-  extern __shared__ __align__(16) float sm[];
+  extern __shared__ __align__(16) uint8_t smb[];
+  const int K = a.w.cols, C = a.d.C;
+  RingPlan P = a.plan;
+  P.row0 = blockIdx.x * a.plan.row1;
+  P.row1 = min(a.w.rows, P.row0 + a.plan.row1);
+  RingSmem S = ring_smem(smb, a.lay);
+  float* ln = reinterpret_cast<float*>(smb + a.lay.ln_off);
+  if (a.ring && P.row0 < P.row1) ring_start(a.w, P, S);
+  pdl_launch_dependents();
   issue_prefetch(a.pf);
-  const int K = a.w.cols;
-  float* ln = sm;
-  float* sx = sm + K;
-  float* sxc = sx + K;
-  const float* in = a.src;
-  if (a.ln_w) {
-    layer_norm_to_smem(a.src, a.ln_w, a.ln_b, K, ln, red);
-    if (blockIdx.x == 0 && a.ln_out)
-      for (int i = threadIdx.x; i < K; i += blockDim.x) a.ln_out[i] = ln[i];
-    in = ln;
+  pdl_wait();
+  const Bufs& b = a.b;
+  const int kind = a.kind;
+  // input vector
+  const float* src = kind == 0 ? b.att_y : (kind == 1 ? b.xb : (kind == 2 ? b.h : b.xa));
+  if (kind == 1 || kind == 3) {
+    layer_norm_to_smem(src, a.ln_w, a.ln_b, K, ln, red);
+    if (kind == 1 && blockIdx.x == 0)
+      for (int i = threadIdx.x; i < K; i += blockDim.x) b.xln2[i] = ln[i];
   }
-  const float* prev = a.prev;
+  if (P.row0 >= P.row1) return;
+  // recurrent-state copies for this CTA's rows (their readers ran in earlier phases)
+  if (kind == 0)
+    for (int i = P.row0 + threadIdx.x; i < P.row1; i += blockDim.x) b.att_x[(size_t)a.layer * C + i] = __ldcg(b.xln1 + i);
+  if (kind == 2)
+    for (int i = P.row0 + threadIdx.x; i < P.row1; i += blockDim.x) b.ffn_x[(size_t)a.layer * C + i] = __ldcg(b.xln2 + i);
+  const float* prev = b.ffn_x + (size_t)a.layer * C;
   const float* mixv = a.mixv;
-  auto f = [&](int i) { float z = in[i]; return mixv ? z + (prev[i] - z) * mixv[i] : z; };
-  if (a.mode == 1) {
-    stage_input(K, sx, sxc, f);
-  } else {
-    for (int i = threadIdx.x; i < K; i += blockDim.x) sx[i] = f(i);
-    __syncthreads();
-  }
-  const int r0 = blockIdx.x * a.rpc, r1 = min(a.w.rows, r0 + a.rpc);
-  if (a.state_dst)
-    for (int i = r0 + threadIdx.x; i < r1; i += blockDim.x) a.state_dst[i] = a.state_src[i];
+  auto xin = [&](int i) -> float {
+    if (kind == 1) return ln[i] + (__ldcg(prev + i) - ln[i]) * __ldg(mixv + i);
+    if (kind == 3) return ln[i];
+    return __ldcg(src + i);
+  };
   float best = -INFINITY;
   int besti = 0x7fffffff;
-  float* out = a.out;
-  const float* resid = a.resid;
-  const int relu2 = a.relu2, am = a.argmax;
-  packed_rows(a.w, a.mode, a.lg, sx, sxc, r0, r1, [&](int row, float v) {
-    if (resid) v = resid[row] + v;
-    else if (relu2) v = v > 0.f ? v * v : 0.f;
-    out[row] = v;
-    if (am && (v > best || (v == best && row < besti))) { best = v; besti = row; }
-  });
-  if (!am) return;
-  // per-CTA argmax (lane 0 of each warp holds its rows' best), then the last CTA reduces
+  auto epi = [&](int row, float v) {
+    if (kind == 0) b.xb[row] = __ldcg(b.xa + row) + v;
+    else if (kind == 1) b.h[row] = v > 0.f ? v * v : 0.f;
+    else if (kind == 2) b.xa[row] = __ldcg(b.xb + row) + v;
+    else {
+      b.logits[row] = v;
+      if (v > best || (v == best && row < besti)) { best = v; besti = row; }
+    }
+  };
+  if (a.ring) {
+    ring_dispatch(a.cpl, a.w, P, S, xin, epi, b.err);
+  } else {
+    float* sx = ln + K;
+    float* sxc = sx + K;
+    if (a.mode == 1) {
+      stage_input(K, sx, sxc, xin);
+    } else {
+      for (int i = threadIdx.x; i < K; i += blockDim.x) sx[i] = xin(i);
+      __syncthreads();
+    }
+    packed_rows(a.w, a.mode, a.lg, sx, sxc, P.row0, P.row1, epi);
+  }
+  if (kind != 3) return;
+  // per-CTA argmax, then the last CTA to finish reduces and records the token
+  float wb = best;
+  int wi = besti;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, wb, o);
+    int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+    if (ov > wb || (ov == wb && oi < wi)) { wb = ov; wi = oi; }
+  }
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (lane == 0) { bv[wid] = best; bi[wid] = besti; }
+  if (lane == 0) { bv[wid] = wb; bi[wid] = wi; }
   __syncthreads();
   if (threadIdx.x == 0) {
     float cb = -INFINITY;
     int ci = 0x7fffffff;
     for (int w = 0; w < kThreads / 32; ++w)
       if (bv[w] > cb || (bv[w] == cb && bi[w] < ci)) { cb = bv[w]; ci = bi[w]; }
-    a.b.amax_v[blockIdx.x] = cb;
-    a.b.amax_i[blockIdx.x] = ci;
+    b.amax_v[blockIdx.x] = cb;
+    b.amax_i[blockIdx.x] = ci;
     __threadfence();
-    unsigned prevt = atomicAdd(a.b.ticket, 1u);
+    const unsigned prevt = atomicAdd(b.ticket, 1u);
     if (prevt == gridDim.x - 1) {
       __threadfence();
       float gb = -INFINITY;
       int gi = 0x7fffffff;
       for (unsigned c = 0; c < gridDim.x; ++c) {
-        float v = __ldcg(a.b.amax_v + c);
-        int i = __ldcg(a.b.amax_i + c);
+        const float v = __ldcg(b.amax_v + c);
+        const int i = __ldcg(b.amax_i + c);
         if (v > gb || (v == gb && i < gi)) { gb = v; gi = i; }
       }
-      if (gi == 0x7fffffff) gi = 0;  // all logits NaN: torch would return a NaN index; keep 0
-      *a.b.tok = gi;
-      int st = *a.b.step;
-      a.b.hist[st % a.d.hist_cap] = gi;
-      *a.b.step = st + 1;
-      *a.b.ticket = 0u;
+      if (gi == 0x7fffffff) gi = 0;  // every logit NaN
+      *b.tok = gi;
+      const int st = *b.step;
+      b.hist[st % a.d.hist_cap] = gi;
+      *b.step = st + 1;
+      *b.ticket = 0u;
     }
   }
 }
@@ -414,17 +558,15 @@ struct rwkvb_engine {
   int dev = 0;
   int sms = 148;
   uint32_t flags = 0;
-  int pf_dist = 1;
+  int pf_dist = 0;
+  bool pdl = true;
   Dims d{};
   std::vector<LayerDev> layers;
   PackedView emb{}, head{};
-  int head_mode = 0, head_lg = 0;
   const float *ln0_w = nullptr, *ln0_b = nullptr, *lnout_w = nullptr, *lnout_b = nullptr;
   Bufs b{};
   void* arena = nullptr;
-  size_t arena_bytes = 0;
   int head_grid = 0;
-  // phase schedule
   std::vector<Prefetch> phase_pf;  // weights of each phase, in step order
   cudaStream_t cap = nullptr;
   cudaGraph_t graph = nullptr;
@@ -438,12 +580,10 @@ LayerDev make_layer(const rwkvb_layer_desc& s) {
   LayerDev l;
   l.r = make_view(s.att_r); l.k = make_view(s.att_k); l.v = make_view(s.att_v); l.o = make_view(s.att_o);
   l.w1 = make_view(s.w1); l.w2 = make_view(s.w2); l.a1 = make_view(s.a1); l.a2 = make_view(s.a2);
-  l.g1 = make_view(s.g1); l.g2 = make_view(s.g2); l.v1 = make_view(s.v1); l.v2 = make_view(s.v2);
+  l.g1 = make_view(s.g1); l.g2 = make_view(s.g2);
+  l.v1 = s.v1.data ? make_view(s.v1) : make_view(s.w1);
+  l.v2 = s.v2.data ? make_view(s.v2) : make_view(s.w2);
   l.fk = make_view(s.ffn_key); l.fv = make_view(s.ffn_value);
-  l.mode_r = gemv_mode(l.r); l.mode_k = gemv_mode(l.k); l.mode_v = gemv_mode(l.v);
-  l.mode_o = gemv_mode(l.o); l.mode_fk = gemv_mode(l.fk); l.mode_fv = gemv_mode(l.fv);
-  l.lg_r = ilog2u(l.r.group); l.lg_k = ilog2u(l.k.group); l.lg_v = ilog2u(l.v.group);
-  l.lg_o = ilog2u(l.o.group); l.lg_fk = ilog2u(l.fk.group); l.lg_fv = ilog2u(l.fv.group);
   l.ln1_w = s.ln1_w; l.ln1_b = s.ln1_b; l.ln2_w = s.ln2_w; l.ln2_b = s.ln2_b;
   l.x_r = s.x_r; l.x_w = s.x_w; l.x_k = s.x_k; l.x_v = s.x_v; l.x_a = s.x_a; l.x_g = s.x_g;
   l.w0 = s.w0; l.a0 = s.a0; l.v0 = s.v0; l.k_k = s.k_k; l.k_a = s.k_a; l.r_k = s.r_k;
@@ -471,7 +611,6 @@ Prefetch pf_empty() {
   return p;
 }
 
-// Cap one phase's prefetch (the vocabulary head is larger than L2).
 void pf_cap(Prefetch& pf, uint64_t cap) {
   uint64_t tot = 0;
   for (int i = 0; i < pf.n; ++i) {
@@ -486,6 +625,46 @@ void pf_cap(Prefetch& pf, uint64_t cap) {
   pf.total = tot;
 }
 
+template <class Arg>
+cudaError_t launch(void (*k)(Arg), int grid, int block, size_t smem, cudaStream_t s, bool pdl, const Arg& arg) {
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k, arg);
+}
+
+// Phase plan for a packed GEMV over `ctas` CTAs: ring when the layout allows.
+void plan_phase(const PackedView& w, int ctas, int ln_floats, RingPlan* plan, RingLayout* lay, int* cpl,
+                int* ring, int* mode, int* lg, size_t* smem) {
+  memset(plan, 0, sizeof(*plan));
+  *mode = gemv_mode(w);
+  *lg = ilog2u(w.group);
+  *ring = ring_plan(w, ctas, kSlotBudget, kSlots, cpl, plan) ? 1 : 0;
+  if (!*ring) {
+    *cpl = 0;
+    plan->row1 = (w.rows + ctas - 1) / ctas;
+    plan->nst = kSlots;
+    plan->rs = 1;
+    plan->nseg = 1;
+    plan->slot_bytes = 0;
+    *lay = ring_layout(*plan, 0);
+    // direct path: ln [K] + x [K] + chunk sums [K/16]
+    const int K = w.cols;
+    *smem = lay->ln_off + (size_t)(ln_floats + 2 * K + K / 16 + 8) * 4;
+    return;
+  }
+  *lay = ring_layout(*plan, ln_floats);
+  *smem = lay->total;
+}
+
 int record_step(rwkvb_engine* e, cudaStream_t s) {
   const Dims& d = e->d;
   const int P = (int)e->phase_pf.size();
@@ -494,73 +673,81 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
     if (e->pf_dist <= 0) return pf_empty();
     return e->phase_pf[(p + e->pf_dist) % P];
   };
+  cudaError_t err = cudaSuccess;
+  auto chk = [&](cudaError_t x) { if (err == cudaSuccess && x != cudaSuccess) err = x; };
   e->launches = 0;
   {
     EmbedArgs a;
     a.emb = e->emb; a.ln0_w = e->ln0_w; a.ln0_b = e->ln0_b; a.b = e->b; a.d = d; a.pf = pf_for(phase++);
-    embed_kernel<<<1, kThreads, d.C * sizeof(float), s>>>(a);
+    chk(launch(embed_kernel, 1, kThreads, d.C * sizeof(float), s, e->pdl, a));
     ++e->launches;
   }
-  const int rows3 = 3 * d.C;
-  const int rkv_ctas_target = 2 * e->sms;
-  const int rkv_rpc = (rows3 + rkv_ctas_target - 1) / rkv_ctas_target;
-  const int rkv_ctas = (rows3 + rkv_rpc - 1) / rkv_rpc;
-  const size_t att_in_smem = (size_t)(2 * d.C + d.C / 16 + 4) * sizeof(float);
-  const size_t wkv_smem = (size_t)(((d.rtot + 3) & ~3) + 256 + 7 * 64) * sizeof(float);
+  const int gm = e->sms / 3 > 0 ? e->sms / 3 : 1;
   for (int li = 0; li < d.L; ++li) {
     const LayerDev& l = e->layers[li];
     {
       AttInArgs a;
-      a.l = l; a.b = e->b; a.d = d; a.pf = pf_for(phase++);
-      a.rkv_ctas = rkv_ctas; a.rkv_rpc = rkv_rpc; a.layer = li;
-      const int nm = li == 0 ? 3 : 4;
-      att_in_kernel<<<rkv_ctas + nm * d.adp_splits, kThreads, att_in_smem, s>>>(a);
+      memset(&a, 0, sizeof(a));
+      a.l = l; a.b = e->b; a.d = d; a.pf = pf_for(phase++); a.layer = li; a.gm = gm;
+      size_t smem = 0;
+      int mode = 0, lg = 0;
+      plan_phase(l.r, gm, d.C, &a.plan, &a.lay, &a.cpl, &a.ring, &mode, &lg, &smem);
+      const PackedView* mats[3] = {&l.r, &l.k, &l.v};
+      for (int m = 0; m < 3; ++m) { a.mode[m] = gemv_mode(*mats[m]); a.lg[m] = ilog2u(mats[m]->group); }
+      const int maxr = d.rw > d.ra ? (d.rw > d.rg ? d.rw : d.rg) : (d.ra > d.rg ? d.ra : d.rg);
+      const int maxr2 = maxr > d.rv ? maxr : d.rv;
+      const size_t adp_smem = (size_t)d.C * 4 + (size_t)kAdpRowsMax * maxr2 + 16 + 8 * ((size_t)kAdpRowsMax * maxr2 / 16 + 4);
+      if (adp_smem > smem) smem = adp_smem;
+      const int items = 4 * d.adp_splits;
+      chk(launch(att_in_kernel, 3 * gm + items, kThreads, smem, s, e->pdl, a));
     }
     {
       WkvArgs a;
       a.l = l; a.b = e->b; a.d = d; a.pf = pf_for(phase++); a.layer = li;
-      wkv_kernel<<<d.H, 1024, wkv_smem, s>>>(a);
+      const PackedView* w2s[4] = {&l.w2, &l.a2, &l.g2, &l.v2};
+      a.tiled = 1;
+      for (int m = 0; m < 4; ++m) {
+        const PackedView& w = *w2s[m];
+        if (!(w.kind == RWKVB_KIND_SG8 && w.lg >= 6 && (d.C % (int)w.group) == 0 &&
+              (reinterpret_cast<uintptr_t>(w.payload) & 15u) == 0))
+          a.tiled = 0;
+      }
+      const size_t smem = (size_t)(4096 + ((d.rtot + 3) & ~3) + 256 + 7 * 64) * 4 + (size_t)d.rtot * 8 +
+                          (size_t)d.rtot * 64 + 64;
+      chk(launch(wkv_kernel, d.H, kWkvThreads, smem, s, e->pdl, a));
     }
-    auto gemv_phase = [&](const PackedView& w, int mode, int lg, const float* src, const float* lnw,
-                          const float* lnb, const float* prev, const float* mixv, float* ln_out, float* out,
-                          const float* resid, int relu2, float* sdst, const float* ssrc, int argmax, int grid_target) {
-      GemvPhaseArgs a;
+    const PackedView* ws[3] = {&l.o, &l.fk, &l.fv};
+    for (int k = 0; k < 3; ++k) {
+      PhaseArgs a;
       memset(&a, 0, sizeof(a));
-      a.w = w; a.mode = mode; a.lg = lg;
-      a.rpc = (w.rows + grid_target - 1) / grid_target;
-      a.src = src; a.ln_w = lnw; a.ln_b = lnb; a.prev = prev; a.mixv = mixv; a.ln_out = ln_out;
-      a.out = out; a.resid = resid; a.relu2 = relu2; a.state_dst = sdst; a.state_src = ssrc;
-      a.pf = pf_for(phase++); a.argmax = argmax; a.b = e->b; a.d = d;
-      const int grid = (w.rows + a.rpc - 1) / a.rpc;
-      const size_t smem = (size_t)(2 * w.cols + w.cols / 16 + 4) * sizeof(float);
-      gemv_phase_kernel<<<grid, kThreads, smem, s>>>(a);
-      return grid;
-    };
-    const int gt = 2 * e->sms;
-    // att_out: x_b = x_a + Wo @ att_y ; att_x[l] <- ln1(x_a)
-    gemv_phase(l.o, l.mode_o, l.lg_o, e->b.att_y, nullptr, nullptr, nullptr, nullptr, nullptr, e->b.xb, e->b.xa, 0,
-               e->b.att_x + (size_t)li * d.C, e->b.xln1, 0, gt);
-    // ffn_in: h = relu(Wk @ mix(ln2(x_b), ffn_x[l]))^2 ; xln2 <- ln2(x_b)
-    gemv_phase(l.fk, l.mode_fk, l.lg_fk, e->b.xb, l.ln2_w, l.ln2_b, e->b.ffn_x + (size_t)li * d.C, l.ffn_x_k,
-               e->b.xln2, e->b.h, nullptr, 1, nullptr, nullptr, 0, gt);
-    // ffn_out: x_a = x_b + Wv @ h ; ffn_x[l] <- ln2(x_b)
-    gemv_phase(l.fv, l.mode_fv, l.lg_fv, e->b.h, nullptr, nullptr, nullptr, nullptr, nullptr, e->b.xa, e->b.xb, 0,
-               e->b.ffn_x + (size_t)li * d.C, e->b.xln2, 0, gt);
+      a.w = *ws[k];
+      a.kind = k;
+      a.layer = li;
+      a.ln_w = k == 1 ? l.ln2_w : nullptr;
+      a.ln_b = k == 1 ? l.ln2_b : nullptr;
+      a.mixv = k == 1 ? l.ffn_x_k : nullptr;
+      a.pf = pf_for(phase++);
+      a.b = e->b;
+      a.d = d;
+      size_t smem = 0;
+      plan_phase(a.w, e->sms, k == 1 ? d.C : 0, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
+      const int grid = (a.w.rows + a.plan.row1 - 1) / a.plan.row1;
+      chk(launch(phase_kernel, grid, kThreads, smem, s, e->pdl, a));
+    }
     e->launches += 5;
   }
   {
-    GemvPhaseArgs a;
+    PhaseArgs a;
     memset(&a, 0, sizeof(a));
-    a.w = e->head; a.mode = e->head_mode; a.lg = e->head_lg;
-    a.rpc = (e->head.rows + e->head_grid - 1) / e->head_grid;
-    a.src = e->b.xa; a.ln_w = e->lnout_w; a.ln_b = e->lnout_b;
-    a.out = e->b.logits; a.pf = pf_for(phase++); a.argmax = 1; a.b = e->b; a.d = d;
-    const int grid = (e->head.rows + a.rpc - 1) / a.rpc;
-    const size_t smem = (size_t)(2 * e->head.cols + e->head.cols / 16 + 4) * sizeof(float);
-    gemv_phase_kernel<<<grid, kThreads, smem, s>>>(a);
+    a.w = e->head; a.kind = 3; a.ln_w = e->lnout_w; a.ln_b = e->lnout_b;
+    a.pf = pf_for(phase++); a.b = e->b; a.d = d;
+    size_t smem = 0;
+    plan_phase(a.w, e->head_grid, d.C, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
+    const int grid = (a.w.rows + a.plan.row1 - 1) / a.plan.row1;
+    chk(launch(phase_kernel, grid, kThreads, smem, s, e->pdl, a));
     ++e->launches;
   }
-  return cuda_status(cudaGetLastError());
+  return cuda_status(err != cudaSuccess ? err : cudaGetLastError());
 }
 
 int ensure_graph(rwkvb_engine* e) {
@@ -595,12 +782,12 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   if (!m || !out || !m->layers) return RWKVB_EARG;
   *out = nullptr;
   const int L = m->n_layer, C = m->n_embd, N = m->head_size, F = m->ffn, V = m->vocab;
-  if (L <= 0 || C <= 0 || F <= 0 || V <= 0 || N != 64 || C % 64 != 0 || C % 16 != 0 || F % 16 != 0)
-    return RWKVB_EUNSUPPORTED;
+  if (L <= 0 || C <= 0 || F <= 0 || V <= 0 || N != 64 || C % 64 != 0 || F % 16 != 0) return RWKVB_EUNSUPPORTED;
   if (!desc_ok(m->emb, V, C) || !desc_ok(m->head, V, C)) return RWKVB_EARG;
   if (!m->ln0_w || !m->ln0_b || !m->ln_out_w || !m->ln_out_b) return RWKVB_EARG;
   const rwkvb_layer_desc& l0 = m->layers[0];
-  const int rw = l0.w1.cols, ra = l0.a1.cols, rg = l0.g1.cols, rv = l0.v1.cols;
+  const int rw = l0.w1.cols, ra = l0.a1.cols, rg = l0.g1.cols;
+  const int rv = L > 1 ? m->layers[1].v1.cols : (l0.v1.data ? l0.v1.cols : 0);
   for (int i = 0; i < L; ++i) {
     const rwkvb_layer_desc& s = m->layers[i];
     if (!desc_ok(s.att_r, C, C) || !desc_ok(s.att_k, C, C) || !desc_ok(s.att_v, C, C) || !desc_ok(s.att_o, C, C))
@@ -616,44 +803,40 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
       if (!p) return RWKVB_EARG;
     if (i > 0 && !s.v0) return RWKVB_EARG;
   }
-  if (rw + ra + rg + rv > 4096 || rw <= 0 || ra <= 0 || rg <= 0) return RWKVB_EUNSUPPORTED;
+  if (rw <= 0 || ra <= 0 || rg <= 0 || rw + ra + rg + rv > 2048) return RWKVB_EUNSUPPORTED;
 
   rwkvb_engine* e = new (std::nothrow) rwkvb_engine();
   if (!e) return RWKVB_EALLOC;
   cudaGetDevice(&e->dev);
   e->sms = device_sms();
   e->flags = flags;
-  e->pf_dist = (int)((flags >> 4) & 0xF);  // bits 4..7: prefetch distance (0 = off)
-  if (!(flags & 0x100u)) e->pf_dist = 1;    // bit 8 set: use the explicit distance
+  e->pf_dist = (flags & 0x100u) ? (int)((flags >> 4) & 0xF) : 0;  // bit 8: explicit L2 prefetch distance
+  e->pdl = !(flags & 0x2u);                                        // bit 1: disable PDL
   Dims& d = e->d;
   d.L = L; d.C = C; d.H = C / 64; d.F = F; d.V = V;
   d.rw = rw; d.ra = ra; d.rg = rg; d.rv = rv; d.rtot = rw + ra + rg + rv;
-  d.adp_rows = C >= 2048 ? 64 : 128;
+  d.adp_rows = C >= 2048 ? 128 : 64;
   d.adp_splits = (C + d.adp_rows - 1) / d.adp_rows;
   d.hist_cap = 1 << 16;
   for (int i = 0; i < L; ++i) e->layers.push_back(make_layer(m->layers[i]));
   e->emb = make_view(m->emb);
   e->head = make_view(m->head);
-  e->head_mode = gemv_mode(e->head);
-  e->head_lg = ilog2u(e->head.group);
   e->ln0_w = m->ln0_w; e->ln0_b = m->ln0_b; e->lnout_w = m->ln_out_w; e->lnout_b = m->ln_out_b;
-  e->head_grid = 2 * e->sms;
+  e->head_grid = e->sms;
 
-  // one arena for every engine-owned buffer
   const size_t H = d.H;
   size_t fl[] = {(size_t)L * C, (size_t)L * H * 4096, (size_t)L * C, (size_t)C, (size_t)C, (size_t)C, (size_t)C,
                  (size_t)3 * C, (size_t)d.adp_splits * d.rtot, (size_t)C, (size_t)F, (size_t)C, (size_t)V,
-                 (size_t)e->head_grid + 8};
-  size_t total = 0;
-  size_t offs[16];
+                 (size_t)e->sms * 4 + 8};
+  size_t total = 0, offs[16];
   for (int i = 0; i < 14; ++i) {
     offs[i] = total;
     total += ((fl[i] * 4 + 255) / 256) * 256;
   }
   const size_t ints_off = total;
-  total += ((size_t)(e->head_grid + 8) * 4 + 255) / 256 * 256;  // amax_i
+  total += ((size_t)(e->sms * 4 + 8) * 4 + 255) / 256 * 256;
   const size_t misc_off = total;
-  total += 256;                                                  // ticket, tok, step, err
+  total += 256;
   const size_t hist_off = total;
   total += (size_t)d.hist_cap * 4;
   if (cudaMalloc(&e->arena, total) != cudaSuccess) {
@@ -661,7 +844,6 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
     delete e;
     return RWKVB_EALLOC;
   }
-  e->arena_bytes = total;
   cudaMemset(e->arena, 0, total);
   char* base = (char*)e->arena;
   float** fb[] = {&e->b.att_x, &e->b.wkv, &e->b.ffn_x, &e->b.xa, &e->b.xb, &e->b.xln1, &e->b.xln2,
@@ -699,12 +881,10 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   }
 
   int st = RWKVB_OK;
-  const size_t big = (size_t)(2 * (F > C ? F : C) + (F > C ? F : C) / 16 + 4) * sizeof(float);
-  if (big > kMaxSmem) st = RWKVB_EUNSUPPORTED;
-  if (st == RWKVB_OK && big > 48 * 1024) st = allow_big_smem((const void*)gemv_phase_kernel);
-  if (st == RWKVB_OK) st = allow_big_smem((const void*)att_in_kernel);
-  if (st == RWKVB_OK) st = allow_big_smem((const void*)wkv_kernel);
-  if (st == RWKVB_OK) st = allow_big_smem((const void*)embed_kernel);
+  const void* kernels[] = {(const void*)phase_kernel, (const void*)att_in_kernel, (const void*)wkv_kernel,
+                           (const void*)embed_kernel};
+  for (const void* k : kernels)
+    if (st == RWKVB_OK) st = allow_big_smem(k);
   if (st == RWKVB_OK) st = cuda_status(cudaStreamCreateWithFlags(&e->cap, cudaStreamNonBlocking));
   if (st == RWKVB_OK) st = cuda_status(cudaDeviceSynchronize());
   if (st != RWKVB_OK) {
@@ -753,7 +933,7 @@ static int check_err_flag(rwkvb_engine* e, cudaStream_t s) {
   if (h) {
     cudaMemsetAsync(e->b.err, 0, sizeof(int), s);
     cudaStreamSynchronize(s);
-    return RWKVB_EARG;
+    return (h & kErrTimeout) ? RWKVB_ETIMEOUT : RWKVB_EARG;
   }
   return RWKVB_OK;
 }
@@ -787,10 +967,7 @@ extern "C" int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first, 
     if (st == RWKVB_OK)
       st = cuda_status(cudaMemcpyAsync(out_dev + done, e->b.hist, sizeof(int32_t) * chunk,
                                        cudaMemcpyDeviceToDevice, s));
-    if (st == RWKVB_OK && done + chunk < n) {
-      // restart the history ring; the next step still consumes the last argmax
-      st = cuda_status(cudaMemsetAsync(e->b.step, 0, sizeof(int), s));
-    }
+    if (st == RWKVB_OK && done + chunk < n) st = cuda_status(cudaMemsetAsync(e->b.step, 0, sizeof(int), s));
     done += chunk;
   }
   return st;
@@ -809,7 +986,7 @@ extern "C" int rwkvb_engine_decode_greedy(rwkvb_engine* e, int32_t first, int32_
   if (st == RWKVB_OK && n > 0)
     st = cuda_status(cudaMemcpyAsync(out_host, dev, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToHost, s));
   if (dev) cudaFreeAsync(dev, s);
-  int st2 = cuda_status(cudaStreamSynchronize(s));
+  const int st2 = cuda_status(cudaStreamSynchronize(s));
   if (st == RWKVB_OK) st = st2;
   if (st == RWKVB_OK) st = check_err_flag(e, s);
   return st;

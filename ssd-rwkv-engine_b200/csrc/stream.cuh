@@ -1,0 +1,247 @@
+// Asynchronous data movement for the decode engine: mbarriers, 1-D TMA bulk
+// copies into shared memory, cp.async 16-byte copies, programmatic dependent
+// launch, and the ring-streamed SG8 GEMV built on them.
+#pragma once
+
+#include "common.cuh"
+
+namespace rwkvb {
+
+// Error flags written by device code (engine err word).
+constexpr int kErrToken = 1;    // token id out of range
+constexpr int kErrTimeout = 4;  // a bounded wait gave up
+
+// ------------------------------------------------------------- PDL
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// -------------------------------------------------------- mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete, giving up after `limit`
+// polls (each poll may suspend the thread for a short hardware interval).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit = 1u << 22) {
+  for (uint32_t i = 0; i < limit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// 1-D bulk copy global -> shared (this CTA), completion counted on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---------------------------------------------------- cp.async (16B)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Copy `bytes` (multiple of 16, both pointers 16-byte aligned) with all threads.
+__device__ __forceinline__ void cp_async_block(void* dst, const void* src, uint32_t bytes) {
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  const uint8_t* s = static_cast<const uint8_t*>(src);
+  for (uint32_t o = threadIdx.x * 16u; o < bytes; o += blockDim.x * 16u) cp_async16(d + o, s + o);
+}
+
+// ======================================================= ring-streamed GEMV
+// One CTA computes rows [row0, row1) of an SG8 W [rows, K] (row-aligned
+// groups, gpr = K/group even, payload and metadata 16-byte aligned).
+// Its rows stream through `nst` shared-memory slots of `rs` rows each
+// (codes + scales as two bulk copies per slot).  Each warp owns one K segment
+// (kseg = K / nseg) and keeps the input values of its lane's 16-wide chunks
+// in registers (CPL chunks per lane); per row and segment a warp reduces
+//   sum_chunks d_g * sum(q * x) + min_g * sum(x)      (lut2_gather.c:344-381)
+// and the per-segment partials are summed in fixed order.
+struct RingPlan {
+  int row0, row1;  // this CTA's rows
+  int K, gpr, lg;  // row length, groups per row, log2(group)
+  int nseg, kseg;  // K segments
+  int rs;          // rows per slot
+  int nst;         // slots
+  uint32_t slot_bytes;
+};
+
+struct RingSmem {
+  uint8_t* slots;   // nst * slot_bytes
+  uint64_t* bars;   // nst mbarriers
+  float* part;      // 2 * rs * nseg partials
+};
+
+__device__ __forceinline__ void ring_issue(const PackedView& W, const RingPlan& P, const RingSmem& S, int stage) {
+  const int r = P.row0 + stage * P.rs;
+  const int nr = min(P.rs, P.row1 - r);
+  const int slot = stage % P.nst;
+  uint8_t* dst = S.slots + (size_t)slot * P.slot_bytes;
+  const uint32_t qb = (uint32_t)nr * (uint32_t)P.K;
+  const uint32_t sb = (uint32_t)nr * (uint32_t)P.gpr * 8u;
+  mbar_expect_tx(&S.bars[slot], qb + sb);
+  bulk_g2s(dst, W.payload + (size_t)r * P.K, qb, &S.bars[slot]);
+  bulk_g2s(dst + (size_t)P.rs * P.K, W.meta + (size_t)r * P.gpr * 8, sb, &S.bars[slot]);
+}
+
+// Prologue: barrier init + first slots in flight.  Call with all threads,
+// BEFORE pdl_wait() (weights never depend on the previous kernel).
+__device__ __forceinline__ void ring_start(const PackedView& W, const RingPlan& P, const RingSmem& S) {
+  const int nstage = (P.row1 - P.row0 + P.rs - 1) / P.rs;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P.nst; ++i) mbar_init(&S.bars[i], 1);
+    fence_mbar_init();
+    for (int t = 0; t < min(P.nst, nstage); ++t) ring_issue(W, P, S, t);
+  }
+  __syncthreads();
+}
+
+// Consume every stage.  xin(i) gives input element i of the row (called once
+// per element per lane, after pdl_wait).  epi(row, value) receives each row.
+// Returns false (and sets err) if a bounded wait gave up.
+template <int CPL, class XIn, class Epi>
+__device__ __forceinline__ bool ring_run(const PackedView& W, const RingPlan& P, const RingSmem& S, XIn xin,
+                                         Epi epi, int* err) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int seg = warp % P.nseg, wsub = warp / P.nseg, wper = nw / P.nseg;
+  const int nchunk = P.kseg >> 4;
+  const int gshift = P.lg - 4;
+  // input values of this lane's chunks, and their sums
+  float xr[CPL][16];
+  float xs[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const int c = lane + 32 * j;
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      float v = c < nchunk ? xin(seg * P.kseg + c * 16 + e) : 0.f;
+      xr[j][e] = v;
+      s += v;
+    }
+    xs[j] = s;
+  }
+  const int nstage = (P.row1 - P.row0 + P.rs - 1) / P.rs;
+  bool ok = true;
+  int t = 0;
+  for (; t < nstage; ++t) {
+    const int slot = t % P.nst;
+    // every thread polls (bounded); the CTA then agrees on the outcome
+    const bool got = mbar_wait_bounded(&S.bars[slot], (uint32_t)((t / P.nst) & 1));
+    if (!__syncthreads_and(got)) {
+      ok = false;
+      if (threadIdx.x == 0) atomicOr(err, kErrTimeout);
+      break;
+    }
+    const int r0 = P.row0 + t * P.rs;
+    const int nr = min(P.rs, P.row1 - r0);
+    const uint8_t* sq = S.slots + (size_t)slot * P.slot_bytes;
+    const float2* ss = reinterpret_cast<const float2*>(sq + (size_t)P.rs * P.K);
+    float* part = S.part + (t & 1) * P.rs * P.nseg;
+    for (int ri = wsub; ri < nr; ri += wper) {
+      const uint8_t* q = sq + (size_t)ri * P.K + seg * P.kseg;
+      const float2* sc = ss + ri * P.gpr + ((seg * P.kseg) >> P.lg);
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c < nchunk) {
+          const uint4 qq = *reinterpret_cast<const uint4*>(q + c * 16);
+          const float2 s = sc[c >> gshift];
+          float2 a = make_float2(0.f, 0.f);
+          a = dot4_u8(qq.x, make_float4(xr[j][0], xr[j][1], xr[j][2], xr[j][3]), a);
+          a = dot4_u8(qq.y, make_float4(xr[j][4], xr[j][5], xr[j][6], xr[j][7]), a);
+          a = dot4_u8(qq.z, make_float4(xr[j][8], xr[j][9], xr[j][10], xr[j][11]), a);
+          a = dot4_u8(qq.w, make_float4(xr[j][12], xr[j][13], xr[j][14], xr[j][15]), a);
+          const float d = (s.y - s.x) * kInv255;
+          acc = fmaf(d, a.x + a.y, fmaf(s.x, xs[j], acc));
+        }
+      }
+      acc = warp_sum(acc);
+      if (lane == 0) part[ri * P.nseg + seg] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && t + P.nst < nstage) ring_issue(W, P, S, t + P.nst);
+    if ((int)threadIdx.x < nr) {
+      float v = 0.f;
+      for (int s = 0; s < P.nseg; ++s) v += part[threadIdx.x * P.nseg + s];
+      epi(r0 + (int)threadIdx.x, v);
+    }
+  }
+  if (!ok) {
+    // let this CTA's outstanding copies land before it exits (bounded)
+    if (threadIdx.x == 0) {
+      const int issued = min(nstage, t + P.nst);
+      for (int u = t; u < issued; ++u) mbar_wait_bounded(&S.bars[u % P.nst], (uint32_t)((u / P.nst) & 1), 1u << 16);
+    }
+    __syncthreads();
+  }
+  return ok;
+}
+
+// Host-side planning for a CTA count `ctas` over W's rows.  Returns false when
+// W does not have the ring layout (callers then use the direct-load path).
+__host__ inline bool ring_plan(const PackedView& W, int ctas, int slot_budget, int nst, int* cpl_out,
+                               RingPlan* base) {
+  if (W.kind != RWKVB_KIND_SG8 || W.lg < 4 || (W.cols % W.group) != 0) return false;
+  const int K = W.cols, gpr = K / (int)W.group;
+  if (gpr % 2 != 0) return false;
+  if ((reinterpret_cast<uintptr_t>(W.payload) & 15u) || (reinterpret_cast<uintptr_t>(W.meta) & 15u)) return false;
+  int nseg = 1;
+  while (nseg <= 8) {
+    const int kseg = K / nseg;
+    const bool fits = (K % nseg == 0) && (kseg % (int)W.group == 0) && (kseg % 16 == 0);
+    const int cpl = (kseg / 16 + 31) / 32;
+    if (fits && cpl <= 5) break;
+    nseg *= 2;
+  }
+  if (nseg > 8) return false;
+  const int kseg = K / nseg;
+  const int row_bytes = K + gpr * 8;
+  const int wper = 8 / nseg;
+  int rs = wper;
+  while ((rs + wper) * row_bytes <= slot_budget) rs += wper;
+  const int rpc = (W.rows + ctas - 1) / ctas;
+  if (rs > rpc) rs = ((rpc + wper - 1) / wper) * wper;
+  if (rs > 256) rs = 256;
+  base->K = K;
+  base->gpr = gpr;
+  base->lg = W.lg;
+  base->nseg = nseg;
+  base->kseg = kseg;
+  base->rs = rs;
+  base->nst = nst;
+  base->slot_bytes = (uint32_t)(rs * row_bytes);
+  base->row0 = 0;
+  base->row1 = rpc;  // rows per CTA (row0/row1 resolved per CTA on the device)
+  *cpl_out = (kseg / 16 + 31) / 32;
+  return true;
+}
+
+}  // namespace rwkvb

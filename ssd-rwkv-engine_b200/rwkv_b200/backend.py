@@ -1,0 +1,416 @@
+"""``cuda_b200``: the drop-in pack backend of the reference engine's plugin API.
+
+Mirrors, method for method, the reference's ``PackBackend`` contract
+(``rwkv_ssd/backends/pack_backend.py:18-165``, ``base.py:11-67``) as the
+Albatross adapter implements it (``rwkv_ssd/backends/albatross.py:715-1015``):
+
+* ``load_pack(manifest, device)``   — remember the pack layout and target GPU
+* ``prepare_provider(provider, *, config)`` — copy every packed blob once from
+  the provider into HBM and build the fused decode engine
+* ``prefill_text`` / ``prefill_tokens`` -> ``RecurrentState``
+* ``decode_greedy(state, provider, max_tokens, metrics, *, temperature,
+  token_callback, cancel_event, deadline)`` -> token ids
+* ``generate`` / ``generate_greedy`` / ``generate_greedy_batch``
+* ``get_recurrent_state`` / ``set_recurrent_state`` / ``probe_logits``
+* ``capabilities()``
+
+``RecurrentState`` keeps the reference layout (``state_cache.py:38-56``):
+``rwkv7_state`` is the 3-tensors-per-layer list ``[x_prev_att, S, x_prev_ffn]``
+(device tensors here); the pending next-token logits ride in
+``external_state`` like the Albatross backend's ``pending_logits``.
+
+Providers: any object exposing the reference ``ManifestWeightProvider``'s
+``manifest`` + ``_read_packed_bytes(entry, timing)`` (raw pack bytes per
+``TensorEntry``), or this module's in-memory ``PackProvider``.
+"""
+
+from __future__ import annotations
+
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Any
+
+import numpy as np
+import torch
+
+from .synth import PackedTensor
+
+CUDA_B200_BACKENDS = frozenset({"cuda_b200", "b200"})
+SUPPORTED_CODECS = ("none", "scale_u8_grouped", "trinity_lut2")
+
+
+class BackendNotAvailableError(Exception):
+    """Mirror of ``rwkv_ssd.runtime.errors.BackendNotAvailableError``."""
+
+
+class CapabilityNotSupportedError(Exception):
+    """Mirror of ``rwkv_ssd.runtime.errors.CapabilityNotSupportedError``."""
+
+    def __init__(self, capability: str, backend: str, detail: str | None = None):
+        self.capability = capability
+        super().__init__(f"{backend} does not support {capability}" + (f": {detail}" if detail else ""))
+
+
+class GenerationCancelled(RuntimeError):
+    """Mirror of ``rwkv_ssd.runtime.generation_control.GenerationCancelled``."""
+
+
+@dataclass
+class RecurrentState:
+    """Field-compatible with the reference ``RecurrentState`` (state_cache.py:38-56)."""
+
+    last_token_id: int = 0
+    h: torch.Tensor | None = None
+    rwkv7_state: list[torch.Tensor] | None = None
+    external_state: object | None = None
+
+    def clone(self) -> "RecurrentState":
+        ext = self.external_state
+        if isinstance(ext, dict):
+            ext = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in ext.items()}
+        return RecurrentState(int(self.last_token_id), self.h.clone() if self.h is not None else None,
+                              [t.clone() for t in self.rwkv7_state] if self.rwkv7_state is not None else None, ext)
+
+
+class _Control:
+    """Token-boundary cancellation / deadline / callback (generation_control.py:19-35)."""
+
+    def __init__(self, token_callback=None, cancel_event=None, deadline=None):
+        self.cb, self.cancel, self.deadline = token_callback, cancel_event, deadline
+
+    def check(self) -> None:
+        if self.cancel is not None and self.cancel.is_set():
+            raise GenerationCancelled("generation cancelled")
+        if self.deadline is not None and time.monotonic() >= self.deadline:
+            raise GenerationCancelled("generation deadline exceeded")
+
+    def emit(self, tok: int) -> None:
+        self.check()
+        if self.cb is not None:
+            self.cb(int(tok))
+
+
+def _control(token_callback=None, cancel_event=None, deadline=None):
+    if token_callback is None and cancel_event is None and deadline is None:
+        return None
+    return _Control(token_callback, cancel_event, deadline)
+
+
+# ---------------------------------------------------------------- providers
+_DEQUANT_CODEC = {"scale_u8_grouped": "sg8", "trinity_lut2": "lut2", "none": "none"}
+_DTYPES = {"float32": np.float32, "float16": np.float16, "bfloat16": "bf16"}
+
+
+@dataclass
+class _Entry:
+    name: str
+    shape: list
+    dtype: str = "float32"
+    dequant: str = "none"
+    layer_id: int = -1
+
+
+class PackProvider:
+    """In-memory pack provider (name -> ``PackedTensor``) with the reference
+    provider's fused-blob protocol (``weight_provider.py:660-667``)."""
+
+    def __init__(self, pack: dict[str, PackedTensor]):
+        self.pack = pack
+        self._fused = {n: (e.payload, int(e.shape[0]), int(e.shape[1])) for n, e in pack.items()
+                       if e.codec in ("sg8", "lut2")}
+
+    def packed_tensors(self) -> dict[str, PackedTensor]:
+        return self.pack
+
+    def _use_fused_lut_matmul(self) -> bool:
+        return True
+
+    def get_fused_lut_blob(self, name: str):
+        return self._fused.get(name)
+
+
+def packed_tensors_from_provider(provider) -> dict[str, PackedTensor]:
+    """Raw packed tensors from a provider (in-memory or the reference's)."""
+    if hasattr(provider, "packed_tensors"):
+        return provider.packed_tensors()
+    manifest = getattr(provider, "manifest", None) or getattr(provider, "_manifest", None)
+    reader = getattr(provider, "_read_packed_bytes", None)
+    if manifest is None or not callable(reader):
+        raise TypeError("provider exposes neither packed_tensors() nor manifest + _read_packed_bytes()")
+    out: dict[str, PackedTensor] = {}
+    for entry in manifest.tensors:
+        raw = reader(entry, None)
+        dq = (entry.dequant or "none").strip().lower()
+        if dq not in _DEQUANT_CODEC:
+            raise CapabilityNotSupportedError("codec", "CudaB200Backend", f"{entry.name}: {dq}")
+        codec = _DEQUANT_CODEC[dq]
+        shape = tuple(int(d) for d in entry.shape)
+        if codec == "none":
+            dt = _DTYPES.get(str(entry.dtype), np.float32)
+            if dt == "bf16":
+                u16 = np.frombuffer(bytes(raw), dtype=np.uint16).astype(np.uint32) << 16
+                vals = u16.view(np.float32)
+            else:
+                vals = np.frombuffer(bytes(raw), dtype=dt).astype(np.float32)
+            out[entry.name] = PackedTensor(entry.name, shape, "none", vals.reshape(-1).copy())
+        else:
+            if codec == "lut2" and bytes(raw[:3]) != b"TR2":
+                raise CapabilityNotSupportedError("codec", "CudaB200Backend", f"{entry.name}: per-tensor LUT2")
+            if len(shape) != 2:
+                shape = (1, int(np.prod(shape)))
+            out[entry.name] = PackedTensor(entry.name, shape, codec, bytes(raw))
+    return out
+
+
+# ----------------------------------------------------------------- backend
+class CudaB200Backend:
+    """RWKV-7 packed decode on one B200 through the sm_100a library."""
+
+    supports_streaming: bool = True
+
+    def __init__(self, tokenizer: Any | None = None, *, use_graph: bool = True):
+        self.tokenizer = tokenizer
+        self.use_graph = use_graph
+        self._manifest = None
+        self._device = torch.device("cuda", 0)
+        self._engine = None
+        self._last_state: RecurrentState | None = None
+        self._lock = threading.Lock()
+
+    # -------------------------------------------------------- RecurrentBackend
+    def load(self, model_path: str, strategy: str, device: str) -> None:
+        self.capability_error("checkpoint_load", "cuda_b200 consumes runtime packs via load_pack()")
+
+    def load_pack(self, manifest, device: str) -> None:
+        self._manifest = manifest
+        dev = torch.device(device if device not in ("auto", "", None) else "cuda")
+        if dev.type != "cuda":
+            raise BackendNotAvailableError(f"cuda_b200 needs a CUDA device, got {device!r}")
+        self._device = torch.device("cuda", dev.index if dev.index is not None else torch.cuda.current_device())
+
+    def prepare_provider(self, provider, *, config: Any = None) -> None:
+        from .engine import B200Engine
+
+        if self._engine is not None:
+            return
+        if not torch.cuda.is_available():
+            raise BackendNotAvailableError("cuda_b200 needs a CUDA device")
+        pack = packed_tensors_from_provider(provider)
+        self._engine = B200Engine(pack, device=self._device, use_graph=self.use_graph)
+
+    @property
+    def num_layers(self) -> int:
+        if self._engine is not None:
+            return self._engine.shape.n_layer
+        if self._manifest is not None:
+            return 1 + max(int(e.name.split(".")[1]) for e in self._manifest.tensors if e.name.startswith("blocks."))
+        return 0
+
+    def decode_text(self, token_ids: list[int]) -> str:
+        if self.tokenizer is not None and hasattr(self.tokenizer, "decode"):
+            return self.tokenizer.decode(list(token_ids))
+        return " ".join(str(int(t)) for t in token_ids)
+
+    def capability_error(self, capability: str, detail: str | None = None) -> None:
+        raise CapabilityNotSupportedError(capability, type(self).__name__, detail)
+
+    def capabilities(self) -> dict[str, object]:
+        return {
+            "name": "cuda_b200",
+            "declared": {
+                "pack_streaming": True, "skeleton": False, "resident": True, "state_snapshot": True,
+                "batch": True, "prefix_cache": True, "tokenizer": self.tokenizer is not None,
+                "state_kind": "rwkv7", "supported_codecs": list(SUPPORTED_CODECS), "requires_ggml_bin": False,
+                "token_generation": True, "logits_probe": True, "state_transfer": True,
+                "followup_generation": True, "sampling": True, "incremental_streaming": True,
+                "cancellation": True, "deadlines": True, "process_workers": False,
+                "native_layer_streaming": False, "native_cached_layer_step": True,
+            },
+            "runtime": {"loaded": self._engine is not None, "device": str(self._device)},
+        }
+
+    def supports_capability(self, capability: str) -> bool:
+        return bool(self.capabilities()["declared"].get(capability, False))
+
+    # ---------------------------------------------------------------- state
+    def _engine_or_raise(self):
+        if self._engine is None:
+            raise RuntimeError("cuda_b200: call prepare_provider() before generating")
+        return self._engine
+
+    def _snapshot(self, last: int) -> RecurrentState:
+        eng = self._engine
+        return RecurrentState(last_token_id=int(last), rwkv7_state=eng.get_state(),
+                              external_state={"pending_logits": eng.logits.clone()})
+
+    def _restore(self, state: RecurrentState) -> None:
+        eng = self._engine
+        if state.rwkv7_state is None:
+            raise ValueError("cuda_b200 state has no rwkv7_state")
+        eng.set_state(state.rwkv7_state)
+        ext = state.external_state if isinstance(state.external_state, dict) else {}
+        pl = ext.get("pending_logits")
+        if pl is not None:
+            eng.logits.copy_(pl.to(eng.device, torch.float32))
+
+    def get_recurrent_state(self) -> RecurrentState | None:
+        return self._last_state.clone() if self._last_state is not None else None
+
+    def set_recurrent_state(self, state: RecurrentState) -> None:
+        if state.rwkv7_state is None or len(state.rwkv7_state) != 3 * self.num_layers:
+            raise ValueError("cuda_b200 state has an incompatible representation")
+        self._last_state = state.clone()
+
+    def probe_logits(self, state: RecurrentState | None = None):
+        cur = state or self._last_state
+        if cur is None or not isinstance(cur.external_state, dict):
+            return None
+        pl = cur.external_state.get("pending_logits")
+        return pl.detach().clone() if pl is not None else None
+
+    # ------------------------------------------------------------- prefill
+    def _encode(self, text: str) -> list[int]:
+        if self.tokenizer is None:
+            raise CapabilityNotSupportedError("tokenizer", "CudaB200Backend",
+                                              "construct with a tokenizer or call prefill_tokens()")
+        enc = self.tokenizer.encode(text)
+        return list(getattr(enc, "ids", enc))
+
+    def prefill_tokens(self, token_ids: list[int], initial_state: RecurrentState | None = None, *,
+                       metrics: Any = None, cancel_event=None, deadline=None) -> RecurrentState:
+        eng = self._engine_or_raise()
+        ctl = _control(cancel_event=cancel_event, deadline=deadline)
+        t0 = time.perf_counter()
+        with self._lock:
+            if initial_state is not None:
+                self._restore(initial_state)
+            else:
+                eng.reset()
+            ids = [int(t) for t in token_ids] or [0]
+            if ctl is None:
+                eng.forward(ids)
+            else:
+                for t in ids:
+                    ctl.check()
+                    eng.forward([t])
+            state = self._snapshot(ids[-1])
+        torch.cuda.synchronize(eng.device)
+        if metrics is not None and hasattr(metrics, "prefill_wall_s"):
+            metrics.prefill_wall_s = time.perf_counter() - t0
+        self._last_state = state
+        return state.clone()
+
+    def prefill_text(self, text: str, provider, metrics, initial_state: RecurrentState | None = None, *,
+                     cancel_event=None, deadline=None) -> RecurrentState:
+        self.prepare_provider(provider)
+        return self.prefill_tokens(self._encode(text), initial_state, metrics=metrics, cancel_event=cancel_event,
+                                   deadline=deadline)
+
+    # -------------------------------------------------------------- decode
+    def decode_greedy(self, state: RecurrentState, provider, max_tokens: int, metrics, *, temperature: float = 0.0,
+                      token_callback=None, cancel_event=None, deadline=None) -> list[int]:
+        self.prepare_provider(provider)
+        eng = self._engine_or_raise()
+        n = max(0, int(max_tokens))
+        ctl = _control(token_callback, cancel_event, deadline)
+        out: list[int] = []
+        with self._lock:
+            self._restore(state)
+            if isinstance(state.external_state, dict) and state.external_state.get("pending_logits") is None:
+                eng.forward([state.last_token_id])
+            t0 = time.perf_counter()
+            if n and ctl is None and float(temperature) <= 0.0:
+                # whole greedy loop on the device: step i consumes step i-1's argmax
+                first = int(torch.argmax(eng.logits).item())
+                out = [first] + (eng.decode_greedy(first, n - 1) if n > 1 else [])
+                eng.forward([out[-1]])  # advance past the last emitted token (as the reference does)
+                lat = (time.perf_counter() - t0) * 1e3 / n
+                self._record(metrics, [lat] * n)
+            else:
+                lats = []
+                for _ in range(n):
+                    if ctl is not None:
+                        ctl.check()
+                    s0 = time.perf_counter()
+                    tok = self._sample(eng.logits, float(temperature))
+                    out.append(tok)
+                    eng.forward([tok])
+                    if ctl is not None:
+                        ctl.emit(tok)
+                    lats.append((time.perf_counter() - s0) * 1e3)
+                self._record(metrics, lats)
+            self._last_state = self._snapshot(out[-1] if out else state.last_token_id)
+        return out
+
+    @staticmethod
+    def _sample(logits: torch.Tensor, temperature: float) -> int:
+        if temperature <= 0.0:
+            return int(torch.argmax(logits).item())
+        probs = torch.softmax(logits.float() / temperature, dim=-1)
+        probs = torch.nan_to_num(probs, nan=0.0, posinf=0.0, neginf=0.0)
+        if not bool(torch.isfinite(probs.sum())) or float(probs.sum()) <= 0.0:
+            return int(torch.argmax(logits).item())
+        return int(torch.multinomial(probs, 1).item())
+
+    @staticmethod
+    def _record(metrics, lats: list[float]) -> None:
+        if metrics is None:
+            return
+        tl = getattr(metrics, "token_latencies_ms", None)
+        if isinstance(tl, list):
+            tl.extend(lats)
+        if hasattr(metrics, "tokens_generated"):
+            metrics.tokens_generated = len(lats)
+        if hasattr(metrics, "ttft_s") and lats and getattr(metrics, "ttft_s", 0.0) <= 0.0:
+            metrics.ttft_s = lats[0] / 1e3
+
+    # ---------------------------------------------------------- generation
+    def generate(self, prompt: str, provider, max_tokens: int, metrics, *, temperature: float = 0.0,
+                 greedy: bool = True, token_callback=None, cancel_event=None, deadline=None) -> list[int]:
+        ctl = _control(token_callback, cancel_event, deadline)
+        if ctl is not None:
+            ctl.check()
+        state = self.prefill_text(prompt, provider, metrics, cancel_event=cancel_event, deadline=deadline)
+        if ctl is not None:
+            ctl.check()
+        return self.decode_greedy(state, provider, max_tokens, metrics, temperature=0.0 if greedy else temperature,
+                                  token_callback=token_callback, cancel_event=cancel_event, deadline=deadline)
+
+    def generate_tokens(self, *a, **kw) -> list[int]:
+        return self.generate(*a, **kw)
+
+    def generate_greedy(self, prompt: str, provider, max_tokens: int, metrics) -> list[int]:
+        return self.generate(prompt, provider, max_tokens, metrics)
+
+    def generate_greedy_batch(self, prompts: list[str], provider, max_tokens: int, metrics) -> list[list[int]]:
+        return [self.generate(p, provider, max_tokens, metrics) for p in prompts]
+
+    def close(self) -> None:
+        if self._engine is not None:
+            self._engine.close()
+            self._engine = None
+
+
+# ------------------------------------------------------------- factory
+def create_backend(name: str):
+    """Mirror of ``create_backend`` (``backends/factory.py:32-46``) for this backend's keys."""
+    key = name.lower().strip()
+    if key in CUDA_B200_BACKENDS:
+        return CudaB200Backend()
+    raise ValueError(f"Unknown backend {name!r}. Choose: cuda_b200 (B200 sm_100a packed decode).")
+
+
+def ensure_v0_backend(name: str) -> None:
+    """Availability gate like ``ensure_v0_backend`` (``backends/factory.py:60-78``)."""
+    key = name.lower().strip()
+    if key not in CUDA_B200_BACKENDS:
+        raise ValueError(f"Unknown backend {name!r}")
+    if not torch.cuda.is_available():
+        raise BackendNotAvailableError(f"Backend {name!r} requires a CUDA device (B200, sm_100a).")
+    major, minor = torch.cuda.get_device_capability()
+    if (major, minor) != (10, 0):
+        raise BackendNotAvailableError(f"Backend {name!r} is built for sm_100a; device is sm_{major}{minor}.")
+    from . import native
+
+    native.lib()

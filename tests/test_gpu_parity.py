@@ -58,7 +58,10 @@ def test_gemv_family_matches_reference_kernels():
         if c.startswith(("sg8_", "lut2_")):
             o, i = (int(v) for v in d["shape"])
             y = lg.lut2_gemv(d["blob"].tobytes(), torch.from_numpy(d["x"]), out_features=o, in_features=i)
-            np.testing.assert_allclose(_np(y), d["y"], **TOL, err_msg=c)
+            # the reference LUT2 kernel sums sequentially in fp32 (lut2_gather.c:300-324): its own
+            # rounding error reaches ~1e-4 relative on these rows
+            tol = TOL if c.startswith("sg8_") else dict(rtol=1e-4, atol=1e-4)
+            np.testing.assert_allclose(_np(y), d["y"], **tol, err_msg=c)
         elif c.startswith("tr_"):
             i, o = (int(v) for v in d["shape"])
             y = lg.grouped_u8_transposed_gemv(d["blob"].tobytes(), torch.from_numpy(d["x"]), out_features=o,
