@@ -105,41 +105,64 @@ __device__ __forceinline__ void issue_prefetch(const Prefetch& pf) {
   }
 }
 
-// LayerNorm (two-pass mean / variance, eps 1e-5) of x[0..C) into out (shared).
-__device__ __forceinline__ void layer_norm_to_smem(const float* x, const float* w, const float* b, int C,
-                                                   float* out, float* red) {
+// In-place LayerNorm of buf[0..C) (shared, already staged): two-pass mean /
+// variance, eps 1e-5 (F.layer_norm, packed_block_forward.py:94-98).
+__device__ __forceinline__ void layer_norm_inplace(float* buf, const float* w, const float* b, int C, float* red) {
   float s = 0.f;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    float v = __ldcg(x + i);
-    out[i] = v;
-    s += v;
-  }
+  for (int i = threadIdx.x; i < C; i += blockDim.x) s += buf[i];
   const float mean = block_sum(s, red) / (float)C;
   float q = 0.f;
   for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    float d = out[i] - mean;
+    const float d = buf[i] - mean;
     q += d * d;
   }
-  const float var = block_sum(q, red) / (float)C;
-  const float rstd = rsqrtf(var + 1e-5f);
-  for (int i = threadIdx.x; i < C; i += blockDim.x) out[i] = (out[i] - mean) * rstd * w[i] + b[i];
-  __syncthreads();
+  const float rstd = rsqrtf(block_sum(q, red) / (float)C + 1e-5f);
+  stage4(buf, C >> 2, [&](int i) {
+    const float4 x = reinterpret_cast<const float4*>(buf)[i];
+    const float4 ww = ldg4(w + 4 * i), bb = ldg4(b + 4 * i);
+    return make_float4((x.x - mean) * rstd * ww.x + bb.x, (x.y - mean) * rstd * ww.y + bb.y,
+                       (x.z - mean) * rstd * ww.z + bb.z, (x.w - mean) * rstd * ww.w + bb.w);
+  });
 }
 
-// Shared-memory carve-up for ring phases: [ring slots][bars][partials][ln]
+// buf = LayerNorm(x) for a mutable global vector x (read through L2).
+__device__ __forceinline__ void layer_norm_global(const float* x, const float* w, const float* b, int C, float* buf,
+                                                  float* red) {
+  stage4(buf, C >> 2, [&](int i) { return ldcg4(x + 4 * i); });
+  layer_norm_inplace(buf, w, b, C, red);
+}
+
+// buf = buf + (prev - buf) * mix, in place (token shift, rwkv7_linear.py:165-171).
+__device__ __forceinline__ void token_mix_inplace(float* buf, const float* prev, const float* mix, int C) {
+  stage4(buf, C >> 2, [&](int i) {
+    const float4 z = reinterpret_cast<const float4*>(buf)[i];
+    const float4 p = ldcg4(prev + 4 * i), m = ldg4(mix + 4 * i);
+    return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
+                       z.w + (p.w - z.w) * m.w);
+  });
+}
+
+__device__ __forceinline__ void store_vec(float* dst, const float* src, int C) {
+  for (int i = threadIdx.x; i < (C >> 2); i += blockDim.x)
+    reinterpret_cast<float4*>(dst)[i] = reinterpret_cast<const float4*>(src)[i];
+}
+
+// Shared-memory carve-up for ring phases: [ring slots][bars][partials][vec][resid]
 struct RingLayout {
-  uint32_t slots_off, bars_off, part_off, ln_off, total;
+  uint32_t slots_off, bars_off, part_off, vec_off, res_off, total;
 };
 
-__host__ inline RingLayout ring_layout(const RingPlan& P, int ln_floats) {
+__host__ inline RingLayout ring_layout(const RingPlan& P, int vec_floats, int res_floats) {
   RingLayout L;
   L.slots_off = 0;
   L.bars_off = (uint32_t)P.nst * P.slot_bytes;
   L.bars_off = (L.bars_off + 15) & ~15u;
   L.part_off = L.bars_off + 8 * kSlots;
-  L.ln_off = L.part_off + (uint32_t)(2 * P.rs * P.nseg * 4);
-  L.ln_off = (L.ln_off + 15) & ~15u;
-  L.total = L.ln_off + (uint32_t)ln_floats * 4 + 16;
+  L.vec_off = L.part_off + (uint32_t)(2 * P.rs * P.nseg * 4);
+  L.vec_off = (L.vec_off + 15) & ~15u;
+  L.res_off = L.vec_off + (uint32_t)vec_floats * 4;
+  L.res_off = (L.res_off + 15) & ~15u;
+  L.total = L.res_off + (uint32_t)res_floats * 4 + 16;
   return L;
 }
 
@@ -170,11 +193,12 @@ struct EmbedArgs {
   Bufs b;
   Dims d;
   Prefetch pf;
+  int fast;  // SG8 rows with whole groups, 16-byte aligned: stage the row with cp.async
 };
 
 __global__ void __launch_bounds__(kThreads) embed_kernel(EmbedArgs a) {
   __shared__ float red[32];
-  extern __shared__ __align__(16) float sm[];
+  extern __shared__ __align__(16) uint8_t smb[];
   pdl_launch_dependents();
   issue_prefetch(a.pf);
   pdl_wait();
@@ -184,21 +208,26 @@ __global__ void __launch_bounds__(kThreads) embed_kernel(EmbedArgs a) {
     if (threadIdx.x == 0) atomicOr(a.b.err, kErrToken);
     tok = 0;
   }
-  float* row = sm;
-  float s = 0.f;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const float v = packed_at(a.emb, tok, i);
-    row[i] = v;
-    s += v;
+  float* row = reinterpret_cast<float*>(smb);
+  if (a.fast) {
+    uint8_t* q = smb + (size_t)C * 4;
+    float2* sc = reinterpret_cast<float2*>(q + C);
+    const int gpr = C >> a.emb.lg;
+    cp_async_block(q, a.emb.payload + (size_t)tok * C, (uint32_t)C);
+    cp_async_block(sc, a.emb.meta + (size_t)tok * gpr * 8, (uint32_t)gpr * 8u);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+      const float2 s = sc[i >> a.emb.lg];
+      row[i] = sg8_dequant(q[i], s.x, s.y);
+    }
+  } else {
+    for (int i = threadIdx.x; i < C; i += blockDim.x) row[i] = packed_at(a.emb, tok, i);
   }
-  const float mean = block_sum(s, red) / (float)C;
-  float q = 0.f;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const float dd = row[i] - mean;
-    q += dd * dd;
-  }
-  const float rstd = rsqrtf(block_sum(q, red) / (float)C + 1e-5f);
-  for (int i = threadIdx.x; i < C; i += blockDim.x) a.b.xa[i] = (row[i] - mean) * rstd * a.ln0_w[i] + a.ln0_b[i];
+  __syncthreads();
+  layer_norm_inplace(row, a.ln0_w, a.ln0_b, C, red);
+  store_vec(a.b.xa, row, C);
 }
 
 // ------------------------------------------------------------ att_in
@@ -220,8 +249,8 @@ __global__ void __launch_bounds__(kThreads, 2) att_in_kernel(AttInArgs a) {
   __shared__ float red[32];
   extern __shared__ __align__(16) uint8_t smb[];
   const int C = a.d.C;
-  const bool rkv = (int)blockIdx.x < 3 * a.gm;
-  if (rkv) {
+  const float* prev = a.b.att_x + (size_t)a.layer * C;
+  if ((int)blockIdx.x < 3 * a.gm) {
     const int m = blockIdx.x / a.gm, cb = blockIdx.x % a.gm;
     const PackedView& W = m == 0 ? a.l.r : (m == 1 ? a.l.k : a.l.v);
     const float* mix = m == 0 ? a.l.x_r : (m == 1 ? a.l.x_k : a.l.x_v);
@@ -230,29 +259,25 @@ __global__ void __launch_bounds__(kThreads, 2) att_in_kernel(AttInArgs a) {
     P.row0 = cb * a.plan.row1;  // plan.row1 holds rows per CTA
     P.row1 = min(C, P.row0 + a.plan.row1);
     RingSmem S = ring_smem(smb, a.lay);
-    float* ln = reinterpret_cast<float*>(smb + a.lay.ln_off);
+    float* xv = reinterpret_cast<float*>(smb + a.lay.vec_off);
     if (a.ring && P.row0 < P.row1) ring_start(W, P, S);
     pdl_launch_dependents();
     issue_prefetch(a.pf);
     pdl_wait();
-    layer_norm_to_smem(a.b.xa, a.l.ln1_w, a.l.ln1_b, C, ln, red);
-    if (blockIdx.x == 0)
-      for (int i = threadIdx.x; i < C; i += blockDim.x) a.b.xln1[i] = ln[i];
+    layer_norm_global(a.b.xa, a.l.ln1_w, a.l.ln1_b, C, xv, red);
+    if (blockIdx.x == 0) store_vec(a.b.xln1, xv, C);
+    __syncthreads();
     if (P.row0 >= P.row1) return;
-    const float* prev = a.b.att_x + (size_t)a.layer * C;
+    token_mix_inplace(xv, prev, mix, C);
     if (a.ring) {
-      ring_dispatch(a.cpl, W, P, S, [&](int i) { return ln[i] + (__ldcg(prev + i) - ln[i]) * __ldg(mix + i); },
-                    [&](int row, float v) { out[row] = v; }, a.b.err);
+      ring_dispatch(a.cpl, W, P, S, [&](int i) { return xv[i]; }, [&](int row, float v) { out[row] = v; },
+                    a.b.err);
     } else {
-      float* sx = ln + C;
-      float* sxc = sx + C;
+      float* sxc = xv + C;
       if (a.mode[m] == 1) {
-        stage_input(C, sx, sxc, [&](int i) { return ln[i] + (__ldcg(prev + i) - ln[i]) * mix[i]; });
-      } else {
-        for (int i = threadIdx.x; i < C; i += blockDim.x) sx[i] = ln[i] + (__ldcg(prev + i) - ln[i]) * mix[i];
-        __syncthreads();
+        stage_input(C, xv, sxc, [&](int i) { return xv[i]; });
       }
-      packed_rows(W, a.mode[m], a.lg[m], sx, sxc, P.row0, P.row1, [&](int row, float v) { out[row] = v; });
+      packed_rows(W, a.mode[m], a.lg[m], xv, sxc, P.row0, P.row1, [&](int row, float v) { out[row] = v; });
     }
     return;
   }
@@ -265,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 2) att_in_kernel(AttInArgs a) {
   const int off = m == 0 ? 0 : (m == 1 ? a.d.rw : (m == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
   const int R = W.cols;
   const int i0 = s * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows);
-  float* ln = reinterpret_cast<float*>(smb);
+  float* xv = reinterpret_cast<float*>(smb);
   uint8_t* tq = smb + (size_t)C * 4;                                   // codes [rows][R]
   float2* tsc = reinterpret_cast<float2*>(tq + kAdpRowsMax * R + 16);  // scale pairs
   const bool tiled = W.kind == RWKVB_KIND_SG8 && W.lg >= 0 && (R % 16) == 0 &&
@@ -283,9 +308,8 @@ __global__ void __launch_bounds__(kThreads, 2) att_in_kernel(AttInArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   if (!active) return;
-  layer_norm_to_smem(a.b.xa, a.l.ln1_w, a.l.ln1_b, C, ln, red);
-  const float* prev = a.b.att_x + (size_t)a.layer * C;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) ln[i] = ln[i] + (__ldcg(prev + i) - ln[i]) * mix[i];
+  layer_norm_global(a.b.xa, a.l.ln1_w, a.l.ln1_b, C, xv, red);
+  token_mix_inplace(xv, prev, mix, C);
   if (tiled) cp_async_wait_all();
   __syncthreads();
   float* outp = a.b.adp + (size_t)s * a.d.rtot + off;
@@ -295,10 +319,10 @@ __global__ void __launch_bounds__(kThreads, 2) att_in_kernel(AttInArgs a) {
       for (int i = i0; i < i1; ++i) {
         const uint32_t e = (uint32_t)i * (uint32_t)R + (uint32_t)j;
         const float2 sc = tsc[(e >> W.lg) - g0];
-        acc = fmaf(ln[i], sg8_dequant(tq[(i - i0) * R + j], sc.x, sc.y), acc);
+        acc = fmaf(xv[i], sg8_dequant(tq[(i - i0) * R + j], sc.x, sc.y), acc);
       }
     } else {
-      for (int i = i0; i < i1; ++i) acc = fmaf(ln[i], packed_at(W, i, j), acc);
+      for (int i = i0; i < i1; ++i) acc = fmaf(xv[i], packed_at(W, i, j), acc);
     }
     outp[j] = acc;
   }
@@ -319,8 +343,6 @@ __global__ void __launch_bounds__(kWkvThreads) wkv_kernel(WkvArgs a) {
   extern __shared__ __align__(16) uint8_t smb[];
   const int h = blockIdx.x, C = a.d.C, t = threadIdx.x;
   const int nm = a.layer == 0 ? 3 : 4;
-  const int R[4] = {a.d.rw, a.d.ra, a.d.rg, a.d.rv};
-  const int off[4] = {0, a.d.rw, a.d.rw + a.d.ra, a.d.rw + a.d.ra + a.d.rg};
   float* S = reinterpret_cast<float*>(smb);                          // [64][64] state
   float* mid = S + 4096;                                            // [rtot]
   float* vec = mid + ((a.d.rtot + 3) & ~3);                         // 4 x 64
@@ -335,14 +357,16 @@ __global__ void __launch_bounds__(kWkvThreads) wkv_kernel(WkvArgs a) {
   uint8_t* tq = reinterpret_cast<uint8_t*>(tsc + a.d.rtot);         // [rtot][64] codes
   // constant weights first: this head's 64 columns of W2/A2/G2/V2
   if (a.tiled) {
+    int off = 0;
     for (int m = 0; m < nm; ++m) {
       const PackedView& W = m == 0 ? a.l.w2 : (m == 1 ? a.l.a2 : (m == 2 ? a.l.g2 : a.l.v2));
-      for (int u = t; u < R[m] * 4; u += blockDim.x) {
+      for (int u = t; u < W.rows * 4; u += blockDim.x) {
         const int i = u >> 2, p = u & 3;
-        cp_async16(tq + (size_t)(off[m] + i) * 64 + p * 16, W.payload + (size_t)i * C + h * 64 + p * 16);
+        cp_async16(tq + (size_t)(off + i) * 64 + p * 16, W.payload + (size_t)i * C + h * 64 + p * 16);
       }
-      for (int i = t; i < R[m]; i += blockDim.x)
-        tsc[off[m] + i] = __ldg(reinterpret_cast<const float2*>(W.meta) + (((size_t)i * C + h * 64) >> W.lg));
+      for (int i = t; i < W.rows; i += blockDim.x)
+        tsc[off + i] = __ldg(reinterpret_cast<const float2*>(W.meta) + (((size_t)i * C + h * 64) >> W.lg));
+      off += W.rows;
     }
     cp_async_commit();
   }
@@ -353,30 +377,48 @@ __global__ void __launch_bounds__(kWkvThreads) wkv_kernel(WkvArgs a) {
   float* Sg = a.b.wkv + ((size_t)a.layer * a.d.H + h) * 4096;
   for (int u = t; u < 1024; u += blockDim.x) cp_async16(S + u * 4, Sg + u * 4);
   cp_async_commit();
-  // reduce the first-projection partial sums (fixed order) and activate
+  // reduce the first-projection partial sums (fixed order, loads batched) and activate
   const int used = a.layer == 0 ? a.d.rw + a.d.ra + a.d.rg : a.d.rtot;
   for (int j = t; j < used; j += blockDim.x) {
     float acc = 0.f;
-    for (int s = 0; s < a.d.adp_splits; ++s) acc += __ldcg(a.b.adp + (size_t)s * a.d.rtot + j);
+    for (int s0 = 0; s0 < a.d.adp_splits; s0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[u] = s0 + u < a.d.adp_splits ? __ldcg(a.b.adp + (size_t)(s0 + u) * a.d.rtot + j) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc += v[u];
+    }
     if (j < a.d.rw) acc = tanhf(acc);
     else if (j >= a.d.rw + a.d.ra && j < a.d.rw + a.d.ra + a.d.rg) acc = sigmoidf_(acc);
     mid[j] = acc;
+  }
+  // per-channel activations of this head (threads 0..63), loaded while the copies land
+  float r = 0.f, k = 0.f, v = 0.f, vf = 0.f;
+  if (t < 64) {
+    const int ch = h * 64 + t;
+    r = __ldcg(a.b.rkv + ch);
+    k = __ldcg(a.b.rkv + C + ch);
+    v = __ldcg(a.b.rkv + 2 * C + ch);
+    if (a.layer != 0) vf = __ldcg(a.b.v_first + ch);
   }
   cp_async_wait_all();
   __syncthreads();
   // second projections for the head's 64 channels: thread -> (matrix, channel, quarter)
   {
     const int q = t & 3, c = (t >> 2) & 63, m = t >> 8;
+    const int off = m == 0 ? 0 : (m == 1 ? a.d.rw : (m == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
+    const int R = m == 0 ? a.d.rw : (m == 1 ? a.d.ra : (m == 2 ? a.d.rg : a.d.rv));
     float acc = 0.f;
     if (m < nm) {
       if (a.tiled) {
-        for (int i = q; i < R[m]; i += 4) {
-          const float2 sc = tsc[off[m] + i];
-          acc = fmaf(mid[off[m] + i], sg8_dequant(tq[(size_t)(off[m] + i) * 64 + c], sc.x, sc.y), acc);
+        for (int i = q; i < R; i += 4) {
+          const float2 sc = tsc[off + i];
+          acc = fmaf(mid[off + i], sg8_dequant(tq[(size_t)(off + i) * 64 + c], sc.x, sc.y), acc);
         }
       } else {
         const PackedView& W = m == 0 ? a.l.w2 : (m == 1 ? a.l.a2 : (m == 2 ? a.l.g2 : a.l.v2));
-        for (int i = q; i < R[m]; i += 4) acc = fmaf(mid[off[m] + i], packed_at(W, i, h * 64 + c), acc);
+        for (int i = q; i < R; i += 4) acc = fmaf(mid[off + i], packed_at(W, i, h * 64 + c), acc);
       }
     }
     acc += __shfl_xor_sync(0xffffffffu, acc, 1);
@@ -384,21 +426,17 @@ __global__ void __launch_bounds__(kWkvThreads) wkv_kernel(WkvArgs a) {
     if (q == 0 && m < nm) vec[m * 64 + c] = acc;
   }
   __syncthreads();
-  float kkv = 0.f;
-  if (t < 64) kkv = __ldcg(a.b.rkv + C + h * 64 + t) * a.l.k_k[h * 64 + t];
+  const float kkv = t < 64 ? k * a.l.k_k[h * 64 + t] : 0.f;
   const float nrm = sqrtf(block_sum(kkv * kkv, red));
   if (t < 64) {
     const int ch = h * 64 + t;
-    const float r = __ldcg(a.b.rkv + ch);
-    const float k = __ldcg(a.b.rkv + C + ch);
-    float v = __ldcg(a.b.rkv + 2 * C + ch);
     const float aa = sigmoidf_(a.l.a0[ch] + vec[64 + t]);
     const float kk = kkv / fmaxf(nrm, 1e-12f);
     const float kn = k * (1.0f + (aa - 1.0f) * a.l.k_a[ch]);
     if (a.layer == 0) {
       a.b.v_first[ch] = v;
     } else {
-      v = v + (__ldcg(a.b.v_first + ch) - v) * sigmoidf_(a.l.v0[ch] + vec[192 + t]);
+      v = v + (vf - v) * sigmoidf_(a.l.v0[ch] + vec[192 + t]);
     }
     sr[t] = r;
     sd[t] = expf(-0.606531f * sigmoidf_(a.l.w0[ch] + vec[t]));
@@ -452,56 +490,57 @@ __global__ void __launch_bounds__(kThreads, 2) phase_kernel(PhaseArgs a) {
   P.row0 = blockIdx.x * a.plan.row1;
   P.row1 = min(a.w.rows, P.row0 + a.plan.row1);
   RingSmem S = ring_smem(smb, a.lay);
-  float* ln = reinterpret_cast<float*>(smb + a.lay.ln_off);
+  float* xv = reinterpret_cast<float*>(smb + a.lay.vec_off);
+  float* rsd = reinterpret_cast<float*>(smb + a.lay.res_off);
   if (a.ring && P.row0 < P.row1) ring_start(a.w, P, S);
   pdl_launch_dependents();
   issue_prefetch(a.pf);
   pdl_wait();
   const Bufs& b = a.b;
   const int kind = a.kind;
-  // input vector
-  const float* src = kind == 0 ? b.att_y : (kind == 1 ? b.xb : (kind == 2 ? b.h : b.xa));
-  if (kind == 1 || kind == 3) {
-    layer_norm_to_smem(src, a.ln_w, a.ln_b, K, ln, red);
-    if (kind == 1 && blockIdx.x == 0)
-      for (int i = threadIdx.x; i < K; i += blockDim.x) b.xln2[i] = ln[i];
+  // input vector, staged once into shared memory
+  if (kind == 0 || kind == 2) {
+    const float* src = kind == 0 ? b.att_y : b.h;
+    stage4(xv, K >> 2, [&](int i) { return ldcg4(src + 4 * i); });
+  } else {
+    layer_norm_global(kind == 1 ? b.xb : b.xa, a.ln_w, a.ln_b, K, xv, red);
+    if (kind == 1) {
+      if (blockIdx.x == 0) store_vec(b.xln2, xv, K);
+      __syncthreads();
+      token_mix_inplace(xv, b.ffn_x + (size_t)a.layer * C, a.mixv, K);
+    }
   }
-  if (P.row0 >= P.row1) return;
-  // recurrent-state copies for this CTA's rows (their readers ran in earlier phases)
-  if (kind == 0)
-    for (int i = P.row0 + threadIdx.x; i < P.row1; i += blockDim.x) b.att_x[(size_t)a.layer * C + i] = __ldcg(b.xln1 + i);
-  if (kind == 2)
-    for (int i = P.row0 + threadIdx.x; i < P.row1; i += blockDim.x) b.ffn_x[(size_t)a.layer * C + i] = __ldcg(b.xln2 + i);
-  const float* prev = b.ffn_x + (size_t)a.layer * C;
-  const float* mixv = a.mixv;
-  auto xin = [&](int i) -> float {
-    if (kind == 1) return ln[i] + (__ldcg(prev + i) - ln[i]) * __ldg(mixv + i);
-    if (kind == 3) return ln[i];
-    return __ldcg(src + i);
-  };
+  const int nr = P.row1 - P.row0;
+  if (nr <= 0) return;
+  // residual rows and recurrent-state copies for this CTA's rows
+  if (kind == 0 || kind == 2) {
+    const float* res = kind == 0 ? b.xa : b.xb;
+    const float* ln = kind == 0 ? b.xln1 : b.xln2;
+    float* st = (kind == 0 ? b.att_x : b.ffn_x) + (size_t)a.layer * C;
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+      rsd[i] = __ldcg(res + P.row0 + i);
+      st[P.row0 + i] = __ldcg(ln + P.row0 + i);
+    }
+    __syncthreads();
+  }
   float best = -INFINITY;
   int besti = 0x7fffffff;
+  const int r0 = P.row0;
   auto epi = [&](int row, float v) {
-    if (kind == 0) b.xb[row] = __ldcg(b.xa + row) + v;
+    if (kind == 0) b.xb[row] = rsd[row - r0] + v;
     else if (kind == 1) b.h[row] = v > 0.f ? v * v : 0.f;
-    else if (kind == 2) b.xa[row] = __ldcg(b.xb + row) + v;
+    else if (kind == 2) b.xa[row] = rsd[row - r0] + v;
     else {
       b.logits[row] = v;
       if (v > best || (v == best && row < besti)) { best = v; besti = row; }
     }
   };
   if (a.ring) {
-    ring_dispatch(a.cpl, a.w, P, S, xin, epi, b.err);
+    ring_dispatch(a.cpl, a.w, P, S, [&](int i) { return xv[i]; }, epi, b.err);
   } else {
-    float* sx = ln + K;
-    float* sxc = sx + K;
-    if (a.mode == 1) {
-      stage_input(K, sx, sxc, xin);
-    } else {
-      for (int i = threadIdx.x; i < K; i += blockDim.x) sx[i] = xin(i);
-      __syncthreads();
-    }
-    packed_rows(a.w, a.mode, a.lg, sx, sxc, P.row0, P.row1, epi);
+    float* sxc = xv + K;
+    if (a.mode == 1) stage_input(K, xv, sxc, [&](int i) { return xv[i]; });
+    packed_rows(a.w, a.mode, a.lg, xv, sxc, P.row0, P.row1, epi);
   }
   if (kind != 3) return;
   // per-CTA argmax, then the last CTA to finish reduces and records the token
@@ -509,8 +548,8 @@ __global__ void __launch_bounds__(kThreads, 2) phase_kernel(PhaseArgs a) {
   int wi = besti;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    float ov = __shfl_xor_sync(0xffffffffu, wb, o);
-    int oi = __shfl_xor_sync(0xffffffffu, wi, o);
+    const float ov = __shfl_xor_sync(0xffffffffu, wb, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, wi, o);
     if (ov > wb || (ov == wb && oi < wi)) { wb = ov; wi = oi; }
   }
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -642,11 +681,14 @@ cudaError_t launch(void (*k)(Arg), int grid, int block, size_t smem, cudaStream_
 }
 
 // Phase plan for a packed GEMV over `ctas` CTAs: ring when the layout allows.
-void plan_phase(const PackedView& w, int ctas, int ln_floats, RingPlan* plan, RingLayout* lay, int* cpl,
-                int* ring, int* mode, int* lg, size_t* smem) {
+// Shared memory: ring slots, the staged input vector (K floats, plus 16-wide
+// chunk sums on the direct path) and the CTA's residual rows.
+void plan_phase(const PackedView& w, int ctas, RingPlan* plan, RingLayout* lay, int* cpl, int* ring, int* mode,
+                int* lg, size_t* smem) {
   memset(plan, 0, sizeof(*plan));
   *mode = gemv_mode(w);
   *lg = ilog2u(w.group);
+  const int K = w.cols;
   *ring = ring_plan(w, ctas, kSlotBudget, kSlots, cpl, plan) ? 1 : 0;
   if (!*ring) {
     *cpl = 0;
@@ -655,13 +697,9 @@ void plan_phase(const PackedView& w, int ctas, int ln_floats, RingPlan* plan, Ri
     plan->rs = 1;
     plan->nseg = 1;
     plan->slot_bytes = 0;
-    *lay = ring_layout(*plan, 0);
-    // direct path: ln [K] + x [K] + chunk sums [K/16]
-    const int K = w.cols;
-    *smem = lay->ln_off + (size_t)(ln_floats + 2 * K + K / 16 + 8) * 4;
-    return;
   }
-  *lay = ring_layout(*plan, ln_floats);
+  const int rpc = plan->row1;
+  *lay = ring_layout(*plan, K + (*ring ? 0 : K / 16 + 8), (rpc + 3) & ~3);
   *smem = lay->total;
 }
 
@@ -679,7 +717,12 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
   {
     EmbedArgs a;
     a.emb = e->emb; a.ln0_w = e->ln0_w; a.ln0_b = e->ln0_b; a.b = e->b; a.d = d; a.pf = pf_for(phase++);
-    chk(launch(embed_kernel, 1, kThreads, d.C * sizeof(float), s, e->pdl, a));
+    const PackedView& w = e->emb;
+    const int gpr = w.lg >= 0 ? d.C >> w.lg : 1;
+    a.fast = w.kind == RWKVB_KIND_SG8 && w.lg >= 4 && (d.C % (int)w.group) == 0 && gpr % 2 == 0 &&
+             (reinterpret_cast<uintptr_t>(w.payload) & 15u) == 0 && (reinterpret_cast<uintptr_t>(w.meta) & 15u) == 0;
+    const size_t smem = (size_t)d.C * 5 + (size_t)gpr * 8 + 64;
+    chk(launch(embed_kernel, 1, kThreads, smem, s, e->pdl, a));
     ++e->launches;
   }
   const int gm = e->sms / 3 > 0 ? e->sms / 3 : 1;
@@ -691,7 +734,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
       a.l = l; a.b = e->b; a.d = d; a.pf = pf_for(phase++); a.layer = li; a.gm = gm;
       size_t smem = 0;
       int mode = 0, lg = 0;
-      plan_phase(l.r, gm, d.C, &a.plan, &a.lay, &a.cpl, &a.ring, &mode, &lg, &smem);
+      plan_phase(l.r, gm, &a.plan, &a.lay, &a.cpl, &a.ring, &mode, &lg, &smem);
       const PackedView* mats[3] = {&l.r, &l.k, &l.v};
       for (int m = 0; m < 3; ++m) { a.mode[m] = gemv_mode(*mats[m]); a.lg[m] = ilog2u(mats[m]->group); }
       const int maxr = d.rw > d.ra ? (d.rw > d.rg ? d.rw : d.rg) : (d.ra > d.rg ? d.ra : d.rg);
@@ -730,7 +773,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
       a.b = e->b;
       a.d = d;
       size_t smem = 0;
-      plan_phase(a.w, e->sms, k == 1 ? d.C : 0, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
+      plan_phase(a.w, e->sms, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
       const int grid = (a.w.rows + a.plan.row1 - 1) / a.plan.row1;
       chk(launch(phase_kernel, grid, kThreads, smem, s, e->pdl, a));
     }
@@ -742,7 +785,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
     a.w = e->head; a.kind = 3; a.ln_w = e->lnout_w; a.ln_b = e->lnout_b;
     a.pf = pf_for(phase++); a.b = e->b; a.d = d;
     size_t smem = 0;
-    plan_phase(a.w, e->head_grid, d.C, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
+    plan_phase(a.w, e->head_grid, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
     const int grid = (a.w.rows + a.plan.row1 - 1) / a.plan.row1;
     chk(launch(phase_kernel, grid, kThreads, smem, s, e->pdl, a));
     ++e->launches;

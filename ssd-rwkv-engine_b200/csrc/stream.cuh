@@ -74,6 +74,32 @@ __device__ __forceinline__ void cp_async_block(void* dst, const void* src, uint3
   for (uint32_t o = threadIdx.x * 16u; o < bytes; o += blockDim.x * 16u) cp_async16(d + o, s + o);
 }
 
+// ------------------------------------------------ vector staging
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// dst4[i] = f(i) for i < n4 with all threads, eight independent loads in
+// flight per thread (one memory round trip for vectors up to 8 KB per 256
+// threads); ends with __syncthreads().
+template <class F>
+__device__ __forceinline__ void stage4(float* dst, int n4, F f) {
+  float4* d4 = reinterpret_cast<float4*>(dst);
+  for (int base = threadIdx.x; base < n4; base += 8 * blockDim.x) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < n4) v[u] = f(i);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < n4) d4[i] = v[u];
+    }
+  }
+  __syncthreads();
+}
+
 // ======================================================= ring-streamed GEMV
 // One CTA computes rows [row0, row1) of an SG8 W [rows, K] (row-aligned
 // groups, gpr = K/group even, payload and metadata 16-byte aligned).
