@@ -205,7 +205,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=1024)
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="2.9b", choices=["tiny", "0.1b", "2.9b", "7.2b"])
+    ap.add_argument("--config", default="2.9b", choices=["tiny", "0.1b", "2.9b", "7.2b", "2.9b-l4"])
     ap.add_argument("--policy", default="sg8", choices=["sg8", "lut2"])
     ap.add_argument("--prefetch", type=int, default=None)
     ap.add_argument("--e2e-steps", type=int, default=256)
