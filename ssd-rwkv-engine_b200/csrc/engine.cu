@@ -36,7 +36,7 @@ namespace rwkvb {
 constexpr int kThreads = 256;
 constexpr int kWkvThreads = 1024;
 constexpr int kMaxPf = 8;
-constexpr int kSlotBudget = 20 * 1024;
+constexpr int kSlotBudget = 44 * 1024;
 constexpr int kSlots = 4;
 constexpr int kAdpRowsMax = 128;  // rows of a first-adapter matrix per CTA (upper bound)
 
@@ -270,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 2) att_in_kernel(AttInArgs a) {
     if (P.row0 >= P.row1) return;
     token_mix_inplace(xv, prev, mix, C);
     if (a.ring) {
-      ring_dispatch(a.cpl, W, P, S, [&](int i) { return xv[i]; }, [&](int row, float v) { out[row] = v; },
-                    a.b.err);
+      ring_dispatch(a.cpl, W, P, S, [&](int i) { return *reinterpret_cast<const float4*>(xv + i); },
+                    [&](int row, float v) { out[row] = v; }, a.b.err);
     } else {
       float* sxc = xv + C;
       if (a.mode[m] == 1) {
@@ -499,9 +499,9 @@ __global__ void __launch_bounds__(kThreads, 2) phase_kernel(PhaseArgs a) {
   const Bufs& b = a.b;
   const int kind = a.kind;
   // input vector, staged once into shared memory
+  const float* gsrc = kind == 0 ? b.att_y : b.h;
   if (kind == 0 || kind == 2) {
-    const float* src = kind == 0 ? b.att_y : b.h;
-    stage4(xv, K >> 2, [&](int i) { return ldcg4(src + 4 * i); });
+    if (!a.ring) stage4(xv, K >> 2, [&](int i) { return ldcg4(gsrc + 4 * i); });
   } else {
     layer_norm_global(kind == 1 ? b.xb : b.xa, a.ln_w, a.ln_b, K, xv, red);
     if (kind == 1) {
@@ -536,7 +536,10 @@ __global__ void __launch_bounds__(kThreads, 2) phase_kernel(PhaseArgs a) {
     }
   };
   if (a.ring) {
-    ring_dispatch(a.cpl, a.w, P, S, [&](int i) { return xv[i]; }, epi, b.err);
+    if (kind == 0 || kind == 2)
+      ring_dispatch(a.cpl, a.w, P, S, [&](int i) { return ldcg4(gsrc + i); }, epi, b.err);
+    else
+      ring_dispatch(a.cpl, a.w, P, S, [&](int i) { return *reinterpret_cast<const float4*>(xv + i); }, epi, b.err);
   } else {
     float* sxc = xv + K;
     if (a.mode == 1) stage_input(K, xv, sxc, [&](int i) { return xv[i]; });
@@ -683,8 +686,8 @@ cudaError_t launch(void (*k)(Arg), int grid, int block, size_t smem, cudaStream_
 // Phase plan for a packed GEMV over `ctas` CTAs: ring when the layout allows.
 // Shared memory: ring slots, the staged input vector (K floats, plus 16-wide
 // chunk sums on the direct path) and the CTA's residual rows.
-void plan_phase(const PackedView& w, int ctas, RingPlan* plan, RingLayout* lay, int* cpl, int* ring, int* mode,
-                int* lg, size_t* smem) {
+void plan_phase(const PackedView& w, int ctas, bool ln_input, RingPlan* plan, RingLayout* lay, int* cpl, int* ring,
+                int* mode, int* lg, size_t* smem) {
   memset(plan, 0, sizeof(*plan));
   *mode = gemv_mode(w);
   *lg = ilog2u(w.group);
@@ -699,7 +702,13 @@ void plan_phase(const PackedView& w, int ctas, RingPlan* plan, RingLayout* lay, 
     plan->slot_bytes = 0;
   }
   const int rpc = plan->row1;
-  *lay = ring_layout(*plan, K + (*ring ? 0 : K / 16 + 8), (rpc + 3) & ~3);
+  const int vecf = *ring ? (ln_input ? K : 0) : K + K / 16 + 8;
+  *lay = ring_layout(*plan, vecf, (rpc + 3) & ~3);
+  // two CTAs per SM: shrink the ring until both fit (227 KB per SM)
+  while (*ring && plan->nst > 2 && lay->total > 110 * 1024) {
+    plan->nst -= 1;
+    *lay = ring_layout(*plan, vecf, (rpc + 3) & ~3);
+  }
   *smem = lay->total;
 }
 
@@ -725,7 +734,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
     chk(launch(embed_kernel, 1, kThreads, smem, s, e->pdl, a));
     ++e->launches;
   }
-  const int gm = e->sms / 3 > 0 ? e->sms / 3 : 1;
+  const int gm = (2 * e->sms) / 3 > 0 ? (2 * e->sms) / 3 : 1;
   for (int li = 0; li < d.L; ++li) {
     const LayerDev& l = e->layers[li];
     {
@@ -734,7 +743,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
       a.l = l; a.b = e->b; a.d = d; a.pf = pf_for(phase++); a.layer = li; a.gm = gm;
       size_t smem = 0;
       int mode = 0, lg = 0;
-      plan_phase(l.r, gm, &a.plan, &a.lay, &a.cpl, &a.ring, &mode, &lg, &smem);
+      plan_phase(l.r, gm, true, &a.plan, &a.lay, &a.cpl, &a.ring, &mode, &lg, &smem);
       const PackedView* mats[3] = {&l.r, &l.k, &l.v};
       for (int m = 0; m < 3; ++m) { a.mode[m] = gemv_mode(*mats[m]); a.lg[m] = ilog2u(mats[m]->group); }
       const int maxr = d.rw > d.ra ? (d.rw > d.rg ? d.rw : d.rg) : (d.ra > d.rg ? d.ra : d.rg);
@@ -773,7 +782,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
       a.b = e->b;
       a.d = d;
       size_t smem = 0;
-      plan_phase(a.w, e->sms, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
+      plan_phase(a.w, 2 * e->sms, k == 1, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
       const int grid = (a.w.rows + a.plan.row1 - 1) / a.plan.row1;
       chk(launch(phase_kernel, grid, kThreads, smem, s, e->pdl, a));
     }
@@ -785,7 +794,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
     a.w = e->head; a.kind = 3; a.ln_w = e->lnout_w; a.ln_b = e->lnout_b;
     a.pf = pf_for(phase++); a.b = e->b; a.d = d;
     size_t smem = 0;
-    plan_phase(a.w, e->head_grid, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
+    plan_phase(a.w, e->head_grid, true, &a.plan, &a.lay, &a.cpl, &a.ring, &a.mode, &a.lg, &smem);
     const int grid = (a.w.rows + a.plan.row1 - 1) / a.plan.row1;
     chk(launch(phase_kernel, grid, kThreads, smem, s, e->pdl, a));
     ++e->launches;
@@ -865,19 +874,19 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   e->emb = make_view(m->emb);
   e->head = make_view(m->head);
   e->ln0_w = m->ln0_w; e->ln0_b = m->ln0_b; e->lnout_w = m->ln_out_w; e->lnout_b = m->ln_out_b;
-  e->head_grid = e->sms;
+  e->head_grid = 2 * e->sms;
 
   const size_t H = d.H;
   size_t fl[] = {(size_t)L * C, (size_t)L * H * 4096, (size_t)L * C, (size_t)C, (size_t)C, (size_t)C, (size_t)C,
                  (size_t)3 * C, (size_t)d.adp_splits * d.rtot, (size_t)C, (size_t)F, (size_t)C, (size_t)V,
-                 (size_t)e->sms * 4 + 8};
+                 (size_t)e->head_grid * 2 + 8};
   size_t total = 0, offs[16];
   for (int i = 0; i < 14; ++i) {
     offs[i] = total;
     total += ((fl[i] * 4 + 255) / 256) * 256;
   }
   const size_t ints_off = total;
-  total += ((size_t)(e->sms * 4 + 8) * 4 + 255) / 256 * 256;
+  total += ((size_t)(e->head_grid * 2 + 8) * 4 + 255) / 256 * 256;
   const size_t misc_off = total;
   total += 256;
   const size_t hist_off = total;

@@ -148,30 +148,37 @@ __device__ __forceinline__ void ring_start(const PackedView& W, const RingPlan& 
   __syncthreads();
 }
 
-// Consume every stage.  xin(i) gives input element i of the row (called once
-// per element per lane, after pdl_wait).  epi(row, value) receives each row.
+// Consume every stage.  xin4(i) gives input elements i..i+3 of the row (i a
+// multiple of 4; called after pdl_wait).  epi(row, value) receives each row.
 // Returns false (and sets err) if a bounded wait gave up.
 template <int CPL, class XIn, class Epi>
-__device__ __forceinline__ bool ring_run(const PackedView& W, const RingPlan& P, const RingSmem& S, XIn xin,
+__device__ __forceinline__ bool ring_run(const PackedView& W, const RingPlan& P, const RingSmem& S, XIn xin4,
                                          Epi epi, int* err) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int seg = warp % P.nseg, wsub = warp / P.nseg, wper = nw / P.nseg;
   const int nchunk = P.kseg >> 4;
   const int gshift = P.lg - 4;
-  // input values of this lane's chunks, and their sums
+  // input values of this lane's chunks (16-wide, 16-byte loads issued together), and their sums
   float xr[CPL][16];
   float xs[CPL];
 #pragma unroll
   for (int j = 0; j < CPL; ++j) {
     const int c = lane + 32 * j;
-    float s = 0.f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      float v = c < nchunk ? xin(seg * P.kseg + c * 16 + e) : 0.f;
-      xr[j][e] = v;
-      s += v;
+    for (int u = 0; u < 4; ++u) {
+      const float4 v = c < nchunk ? xin4(seg * P.kseg + c * 16 + 4 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+      xr[j][4 * u] = v.x;
+      xr[j][4 * u + 1] = v.y;
+      xr[j][4 * u + 2] = v.z;
+      xr[j][4 * u + 3] = v.w;
     }
-    xs[j] = s;
+  }
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    float sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) sum += xr[j][e];
+    xs[j] = sum;
   }
   const int nstage = (P.row1 - P.row0 + P.rs - 1) / P.rs;
   bool ok = true;
@@ -190,27 +197,46 @@ __device__ __forceinline__ bool ring_run(const PackedView& W, const RingPlan& P,
     const uint8_t* sq = S.slots + (size_t)slot * P.slot_bytes;
     const float2* ss = reinterpret_cast<const float2*>(sq + (size_t)P.rs * P.K);
     float* part = S.part + (t & 1) * P.rs * P.nseg;
-    for (int ri = wsub; ri < nr; ri += wper) {
-      const uint8_t* q = sq + (size_t)ri * P.K + seg * P.kseg;
-      const float2* sc = ss + ri * P.gpr + ((seg * P.kseg) >> P.lg);
-      float acc = 0.f;
+    // two rows per warp pass: independent dependency chains for more ILP
+    for (int ri = wsub; ri < nr; ri += 2 * wper) {
+      const int rj = ri + wper;
+      const bool two = rj < nr;
+      const uint8_t* q0 = sq + (size_t)ri * P.K + seg * P.kseg;
+      const uint8_t* q1 = sq + (size_t)(two ? rj : ri) * P.K + seg * P.kseg;
+      const float2* sc0 = ss + ri * P.gpr + ((seg * P.kseg) >> P.lg);
+      const float2* sc1 = ss + (two ? rj : ri) * P.gpr + ((seg * P.kseg) >> P.lg);
+      float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
       for (int j = 0; j < CPL; ++j) {
         const int c = lane + 32 * j;
         if (c < nchunk) {
-          const uint4 qq = *reinterpret_cast<const uint4*>(q + c * 16);
-          const float2 s = sc[c >> gshift];
-          float2 a = make_float2(0.f, 0.f);
-          a = dot4_u8(qq.x, make_float4(xr[j][0], xr[j][1], xr[j][2], xr[j][3]), a);
-          a = dot4_u8(qq.y, make_float4(xr[j][4], xr[j][5], xr[j][6], xr[j][7]), a);
-          a = dot4_u8(qq.z, make_float4(xr[j][8], xr[j][9], xr[j][10], xr[j][11]), a);
-          a = dot4_u8(qq.w, make_float4(xr[j][12], xr[j][13], xr[j][14], xr[j][15]), a);
-          const float d = (s.y - s.x) * kInv255;
-          acc = fmaf(d, a.x + a.y, fmaf(s.x, xs[j], acc));
+          const uint4 qa = *reinterpret_cast<const uint4*>(q0 + c * 16);
+          const uint4 qb = *reinterpret_cast<const uint4*>(q1 + c * 16);
+          const float2 sa = sc0[c >> gshift];
+          const float2 sb = sc1[c >> gshift];
+          const float4 x0 = make_float4(xr[j][0], xr[j][1], xr[j][2], xr[j][3]);
+          const float4 x1 = make_float4(xr[j][4], xr[j][5], xr[j][6], xr[j][7]);
+          const float4 x2 = make_float4(xr[j][8], xr[j][9], xr[j][10], xr[j][11]);
+          const float4 x3 = make_float4(xr[j][12], xr[j][13], xr[j][14], xr[j][15]);
+          float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+          a = dot4_u8(qa.x, x0, a);
+          b = dot4_u8(qb.x, x0, b);
+          a = dot4_u8(qa.y, x1, a);
+          b = dot4_u8(qb.y, x1, b);
+          a = dot4_u8(qa.z, x2, a);
+          b = dot4_u8(qb.z, x2, b);
+          a = dot4_u8(qa.w, x3, a);
+          b = dot4_u8(qb.w, x3, b);
+          acc0 = fmaf((sa.y - sa.x) * kInv255, a.x + a.y, fmaf(sa.x, xs[j], acc0));
+          acc1 = fmaf((sb.y - sb.x) * kInv255, b.x + b.y, fmaf(sb.x, xs[j], acc1));
         }
       }
-      acc = warp_sum(acc);
-      if (lane == 0) part[ri * P.nseg + seg] = acc;
+      acc0 = warp_sum(acc0);
+      acc1 = warp_sum(acc1);
+      if (lane == 0) {
+        part[ri * P.nseg + seg] = acc0;
+        if (two) part[rj * P.nseg + seg] = acc1;
+      }
     }
     __syncthreads();
     if (threadIdx.x == 0 && t + P.nst < nstage) ring_issue(W, P, S, t + P.nst);
@@ -251,8 +277,9 @@ __host__ inline bool ring_plan(const PackedView& W, int ctas, int slot_budget, i
   const int kseg = K / nseg;
   const int row_bytes = K + gpr * 8;
   const int wper = 8 / nseg;
-  int rs = wper;
-  while ((rs + wper) * row_bytes <= slot_budget) rs += wper;
+  // two rows per warp pass: slots hold a multiple of 2 * wper rows
+  int rs = 2 * wper;
+  while ((rs + 2 * wper) * row_bytes <= slot_budget) rs += 2 * wper;
   const int rpc = (W.rows + ctas - 1) / ctas;
   if (rs > rpc) rs = ((rpc + wper - 1) / wper) * wper;
   if (rs > 256) rs = 256;
