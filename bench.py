@@ -326,7 +326,8 @@ def main() -> None:
                        "codec": "SG8 g128" if args.policy == "sg8" else "TR2x04 g64 (+SG8 g128 adapters/emb)",
                        "parallelism": f"replicas x{world}",
                        "l2": "weights per token (%.2f GB) >> 126 MB L2; no flush needed" % (bpt / 1e9)},
-            "gpu_launches": eng.launches_per_step * args.steps + 1,
+            "gpu_launches": (eng.launches_per_step * args.steps + 1) if eng.launches_per_step
+            else (args.steps + 65535) // 65536,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "what": "whole token step (one CUDA-graph launch): algorithmic bytes/token "

@@ -160,8 +160,15 @@ typedef struct rwkvb_engine rwkvb_engine;
 
 /* Creates an engine on the current device.  The engine copies the descriptors,
  * owns the recurrent state, activations and scratch, and borrows the weights
- * (they must stay resident while the engine lives).  flags: bit0 = disable
- * CUDA-graph capture of the token step. */
+ * (they must stay resident while the engine lives).
+ * flags: bit0 = no CUDA-graph capture of the multi-kernel token step;
+ *        bit1 = no programmatic dependent launch between phase kernels;
+ *        bit2 = no persistent kernel (always use the multi-kernel step);
+ *        bit8 = bits 4..7 give an explicit L2-prefetch distance in phases.
+ * When every projection is SG8 with one power-of-two group size and the
+ * 16-byte layout that rwkvb upload placement gives, decode runs as ONE
+ * cooperative persistent launch per call (all tokens, all layers); otherwise
+ * (LUT2, irregular shapes) each token step is a CUDA graph of phase kernels. */
 int rwkvb_engine_create(const rwkvb_model_desc* desc, uint32_t flags, rwkvb_engine** out);
 int rwkvb_engine_destroy(rwkvb_engine* e);
 

@@ -80,6 +80,10 @@ struct Dims {
   int hist_cap;
 };
 
+}  // namespace rwkvb
+#include "persistent.cuh"
+namespace rwkvb {
+
 // ------------------------------------------------------------ prefetch
 __device__ __forceinline__ void issue_prefetch(const Prefetch& pf) {
   if (pf.n == 0 || threadIdx.x >= 32) return;
@@ -614,6 +618,12 @@ struct rwkvb_engine {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   int launches = 0;
+  // persistent path
+  bool persistent = false;
+  PArgs pa{};
+  int pcpl = 0;
+  LayerDev* dlayers = nullptr;
+  int* dtokens = nullptr;  // forced-token staging [hist_cap]
 };
 
 namespace {
@@ -828,6 +838,131 @@ int run_step(rwkvb_engine* e, cudaStream_t s) {
   return cuda_status(cudaGraphLaunch(e->exec, s));
 }
 
+
+// ---------------------------------------------------------- persistent plan
+bool geom_for(int K, const PackedView& w, int cpl, PGeom* g) {
+  if (w.kind != RWKVB_KIND_SG8 || w.lg < 4 || K % (int)w.group != 0) return false;
+  const int gpr = K / (int)w.group;
+  if (gpr % 2 != 0) return false;
+  for (int nseg = 1; nseg <= kPWarps; nseg *= 2) {
+    if (K % nseg != 0) continue;
+    const int kseg = K / nseg;
+    if (kseg % (int)w.group != 0 || kseg % 16 != 0) continue;
+    if ((kseg / 16 + 31) / 32 != cpl) continue;
+    g->K = K;
+    g->gpr = gpr;
+    g->nseg = nseg;
+    g->kseg = kseg;
+    g->cpl = cpl;
+    g->row_bytes = (uint32_t)(K + gpr * 8);
+    const int wper = kPWarps / nseg;
+    int rs = wper;
+    while ((rs + wper) * (int)g->row_bytes <= 22 * 1024) rs += wper;
+    g->rs = rs;
+    return true;
+  }
+  return false;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Decide whether the persistent kernel can run this model and fill its
+// arguments (everything except the per-launch token fields).
+bool plan_persistent(rwkvb_engine* e) {
+  const Dims& d = e->d;
+  const LayerDev& l0 = e->layers[0];
+  const int lg = l0.r.lg;
+  if (lg < 4 || e->sms < d.H) return false;  // one CTA per head in the WKV phase
+  // every large projection: SG8, same group, row-aligned, 16-byte aligned payload + metadata
+  auto big_ok = [&](const PackedView& w) {
+    return w.kind == RWKVB_KIND_SG8 && w.lg == lg && aligned16(w.payload) && aligned16(w.meta);
+  };
+  auto adp1_ok = [&](const PackedView& w) {
+    return w.kind == RWKVB_KIND_SG8 && w.lg >= 0 && w.cols % 16 == 0 && w.cols <= kPThreads &&
+           aligned16(w.payload) && aligned16(w.meta);
+  };
+  auto adp2_ok = [&](const PackedView& w) {
+    return w.kind == RWKVB_KIND_SG8 && w.lg >= 6 && d.C % (int)w.group == 0 && aligned16(w.payload);
+  };
+  for (int i = 0; i < d.L; ++i) {
+    const LayerDev& l = e->layers[i];
+    if (!big_ok(l.r) || !big_ok(l.k) || !big_ok(l.v) || !big_ok(l.o) || !big_ok(l.fk) || !big_ok(l.fv)) return false;
+    if (!adp1_ok(l.w1) || !adp1_ok(l.a1) || !adp1_ok(l.g1) || (i > 0 && !adp1_ok(l.v1))) return false;
+    if (!adp2_ok(l.w2) || !adp2_ok(l.a2) || !adp2_ok(l.g2) || (i > 0 && !adp2_ok(l.v2))) return false;
+  }
+  if (!big_ok(e->head)) return false;
+  PGeom gc{}, gf{};
+  int cpl = 0;
+  for (int c : {3, 2, 1, 4}) {
+    if (geom_for(d.C, l0.r, c, &gc) && geom_for(d.F, l0.fv, c, &gf)) { cpl = c; break; }
+  }
+  if (!cpl) return false;
+  PArgs& a = e->pa;
+  memset(&a, 0, sizeof(a));
+  a.gc = gc;
+  a.gf = gf;
+  a.lg = lg;
+  a.nst = 4;
+  uint32_t slot = (uint32_t)gc.rs * gc.row_bytes;
+  slot = slot > (uint32_t)gf.rs * gf.row_bytes ? slot : (uint32_t)gf.rs * gf.row_bytes;
+  // first-adapter items share the slots
+  const int rmax = d.rw > d.ra ? (d.rw > d.rg ? d.rw : d.rg) : (d.ra > d.rg ? d.ra : d.rg);
+  const int rmax2 = rmax > d.rv ? rmax : d.rv;
+  const uint32_t adp_bytes = (uint32_t)(d.adp_rows * rmax2) + 16u + (uint32_t)((d.adp_rows * rmax2 >> l0.w1.lg) + 4) * 8u;
+  slot = slot > adp_bytes ? slot : adp_bytes;
+  slot = (slot + 127u) & ~127u;
+  a.slot_bytes = slot;
+  uint32_t off = (uint32_t)a.nst * slot;
+  a.o_bars = off;            off += 128;
+  a.o_part = off;            off += 2 * 512 * 4;
+  a.o_x = off;               off += (uint32_t)d.C * 4;
+  a.o_ln = off;              off += (uint32_t)d.C * 4;
+  a.o_wkv = off;
+  const uint32_t wkv_bytes = (uint32_t)(4096 + ((d.rtot + 3) & ~3) + 256 + 7 * 64) * 4 + (uint32_t)d.rtot * 8 +
+                             (uint32_t)d.rtot * 64;
+  a.o_xb = off;
+  a.o_ln2 = off + (uint32_t)d.C * 4;
+  const uint32_t wk = wkv_bytes > 2u * d.C * 4 ? wkv_bytes : 2u * d.C * 4;
+  off += (wk + 127u) & ~127u;
+  a.o_misc = off;            off += 1024 * 4;
+  a.smem_total = off;
+  if (off > 227 * 1024) return false;
+  a.layers = e->dlayers;
+  a.emb = e->emb;
+  a.head = e->head;
+  a.ln0_w = e->ln0_w; a.ln0_b = e->ln0_b; a.lnout_w = e->lnout_w; a.lnout_b = e->lnout_b;
+  a.b = e->b;
+  a.d = d;
+  a.spin_limit = 1u << 22;
+  const PackedView& E = e->emb;
+  a.emb_fast = E.kind == RWKVB_KIND_SG8 && E.lg >= 4 && d.C % (int)E.group == 0 && ((d.C >> E.lg) % 2) == 0 &&
+               aligned16(E.payload) && aligned16(E.meta);
+  e->pcpl = cpl;
+  return true;
+}
+
+const void* persistent_fn(int cpl) {
+  switch (cpl) {
+    case 1: return (const void*)persistent_kernel<1>;
+    case 2: return (const void*)persistent_kernel<2>;
+    case 3: return (const void*)persistent_kernel<3>;
+    default: return (const void*)persistent_kernel<4>;
+  }
+}
+
+int launch_persistent(rwkvb_engine* e, int ntok, int mode, int first_tok, const int* forced, cudaStream_t s) {
+  PArgs a = e->pa;
+  a.ntok = ntok;
+  a.mode = mode;
+  a.first_tok = first_tok;
+  a.forced = forced;
+  a.gbar = e->b.ticket;  // the argmax ticket word doubles as the grid-barrier counter here
+  cudaError_t err = cudaMemsetAsync(a.gbar, 0, sizeof(unsigned), s);
+  if (err != cudaSuccess) return cuda_status(err);
+  void* args[] = {&a};
+  err = cudaLaunchCooperativeKernel(persistent_fn(e->pcpl), dim3(e->sms), dim3(kPThreads), args, a.smem_total, s);
+  return cuda_status(err);
+}
 }  // namespace
 
 extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rwkvb_engine** out) {
@@ -867,7 +1002,13 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   Dims& d = e->d;
   d.L = L; d.C = C; d.H = C / 64; d.F = F; d.V = V;
   d.rw = rw; d.ra = ra; d.rg = rg; d.rv = rv; d.rtot = rw + ra + rg + rv;
-  d.adp_rows = C >= 2048 ? 128 : 64;
+  // first-adapter row chunk: as large as fits one ~22 KB ring slot (and a divisor of C)
+  {
+    const int rmax = rw > ra ? (rw > rg ? rw : rg) : (ra > rg ? ra : rg);
+    const int rmax2 = rmax > rv ? rmax : rv;
+    d.adp_rows = 128;
+    while (d.adp_rows > 16 && (d.adp_rows * rmax2 > 21 * 1024 || C % d.adp_rows != 0)) d.adp_rows /= 2;
+  }
   d.adp_splits = (C + d.adp_rows - 1) / d.adp_rows;
   d.hist_cap = 1 << 16;
   for (int i = 0; i < L; ++i) e->layers.push_back(make_layer(m->layers[i]));
@@ -933,6 +1074,24 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   }
 
   int st = RWKVB_OK;
+  // persistent decode path (one cooperative launch for the whole loop)
+  if (cudaMalloc((void**)&e->dlayers, sizeof(LayerDev) * (size_t)L) != cudaSuccess ||
+      cudaMalloc((void**)&e->dtokens, sizeof(int) * (size_t)d.hist_cap) != cudaSuccess) {
+    cudaGetLastError();
+    st = RWKVB_EALLOC;
+  }
+  if (st == RWKVB_OK)
+    st = cuda_status(cudaMemcpy(e->dlayers, e->layers.data(), sizeof(LayerDev) * (size_t)L, cudaMemcpyHostToDevice));
+  if (st == RWKVB_OK && !(flags & 0x4u) && plan_persistent(e)) {
+    const void* fn = persistent_fn(e->pcpl);
+    int per_sm = 0;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->pa.smem_total) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kPThreads, e->pa.smem_total) == cudaSuccess &&
+        per_sm >= 1) {
+      e->persistent = true;
+    }
+    cudaGetLastError();
+  }
   const void* kernels[] = {(const void*)phase_kernel, (const void*)att_in_kernel, (const void*)wkv_kernel,
                            (const void*)embed_kernel};
   for (const void* k : kernels)
@@ -953,6 +1112,8 @@ extern "C" int rwkvb_engine_destroy(rwkvb_engine* e) {
   if (e->graph) cudaGraphDestroy(e->graph);
   if (e->cap) cudaStreamDestroy(e->cap);
   if (e->arena) cudaFree(e->arena);
+  if (e->dlayers) cudaFree(e->dlayers);
+  if (e->dtokens) cudaFree(e->dtokens);
   delete e;
   return RWKVB_OK;
 }
@@ -995,6 +1156,16 @@ extern "C" int rwkvb_engine_forward(rwkvb_engine* e, const int32_t* tokens, int3
   for (int i = 0; i < n; ++i)
     if (tokens[i] < 0 || tokens[i] >= e->d.V) return RWKVB_EARG;
   cudaStream_t s = (cudaStream_t)stream;
+  if (e->persistent) {
+    int st = RWKVB_OK;
+    for (int done = 0; done < n && st == RWKVB_OK;) {
+      const int chunk = (n - done) < e->d.hist_cap ? (n - done) : e->d.hist_cap;
+      st = cuda_status(cudaMemcpyAsync(e->dtokens, tokens + done, sizeof(int32_t) * chunk, cudaMemcpyHostToDevice, s));
+      if (st == RWKVB_OK) st = launch_persistent(e, chunk, 1, 0, e->dtokens, s);
+      done += chunk;
+    }
+    return st;
+  }
   int st = ensure_graph(e);
   for (int i = 0; i < n && st == RWKVB_OK; ++i) {
     set_token_kernel<<<1, 1, 0, s>>>(e->b.tok, tokens[i], e->b.step, 0);
@@ -1008,6 +1179,18 @@ extern "C" int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first, 
                                                 void* stream) {
   if (!e || n < 0 || (n > 0 && !out_dev) || first < 0 || first >= e->d.V) return RWKVB_EARG;
   cudaStream_t s = (cudaStream_t)stream;
+  if (e->persistent) {
+    int st = RWKVB_OK;
+    for (int done = 0; done < n && st == RWKVB_OK;) {
+      const int chunk = (n - done) < e->d.hist_cap ? (n - done) : e->d.hist_cap;
+      st = launch_persistent(e, chunk, 0, done == 0 ? first : -1, nullptr, s);
+      if (st == RWKVB_OK)
+        st = cuda_status(cudaMemcpyAsync(out_dev + done, e->b.hist, sizeof(int32_t) * chunk,
+                                         cudaMemcpyDeviceToDevice, s));
+      done += chunk;
+    }
+    return st;
+  }
   int st = ensure_graph(e);
   if (st != RWKVB_OK) return st;
   set_token_kernel<<<1, 1, 0, s>>>(e->b.tok, first, e->b.step, 1);
@@ -1046,6 +1229,6 @@ extern "C" int rwkvb_engine_decode_greedy(rwkvb_engine* e, int32_t first, int32_
 
 extern "C" int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out) {
   if (!e || !out) return RWKVB_EARG;
-  *out = 2 + 5 * e->d.L;
+  *out = e->persistent ? 0 : 2 + 5 * e->d.L;  // persistent: one launch per decode call, not per step
   return RWKVB_OK;
 }

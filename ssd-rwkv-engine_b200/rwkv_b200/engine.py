@@ -63,7 +63,7 @@ class B200Engine:
     """A packed RWKV-7 model resident on one GPU, decoded by the fused engine."""
 
     def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
-                 prefetch_distance: int | None = None):
+                 prefetch_distance: int | None = None, persistent: bool = True):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
@@ -107,6 +107,8 @@ class B200Engine:
             md.ln_out_b = self.vectors.ptr("ln_out.bias")
             md.layers = self._layers
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
+            if not persistent:
+                flags |= native.FLAG_NO_PERSISTENT
             if prefetch_distance is not None:
                 flags |= native.FLAG_EXPLICIT_PREFETCH | ((int(prefetch_distance) & 0xF) << 4)
             h = ctypes.c_void_p()

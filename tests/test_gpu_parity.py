@@ -159,10 +159,10 @@ def _reference_pack(policy: str):
 
 
 @pytest.mark.parametrize("policy", ["sg8", "lut2"])
-@pytest.mark.parametrize("use_graph", [True, False])
-def test_engine_decode_matches_reference_forward(policy, use_graph):
+@pytest.mark.parametrize("path", ["persistent", "graph", "nograph"])
+def test_engine_decode_matches_reference_forward(policy, path):
     gold, shape, pack = _reference_pack(policy)
-    eng = B200Engine(pack, use_graph=use_graph)
+    eng = B200Engine(pack, use_graph=path != "nograph", persistent=path == "persistent")
     try:
         prompt = [int(t) for t in gold["prompt"]]
         ids, logits = eng.greedy(prompt, len(gold["ids"]), keep_logits=True)
@@ -222,7 +222,8 @@ def test_engine_rejects_out_of_range_token():
         eng.close()
 
 
-def test_engine_0p1b_shape_matches_oracle_first_tokens():
+@pytest.mark.parametrize("persistent", [True, False])
+def test_engine_0p1b_shape_matches_oracle_first_tokens(persistent):
     """Real 0.1B dimensions (12 layers, d_model 768, vocab 65536), seeded weights:
     the first decode steps against the oracle forward."""
     shape = synth.PRESETS["0.1b"]
@@ -231,7 +232,7 @@ def test_engine_0p1b_shape_matches_oracle_first_tokens():
     model = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size)
     prompt = synth.seeded_prompt(3, shape.vocab, 3)
     ids_ref, logits_ref, state_ref = model.greedy(prompt, 3)
-    eng = B200Engine(pack)
+    eng = B200Engine(pack, persistent=persistent)
     try:
         ids, logits = eng.greedy(prompt, 3, keep_logits=True)
         assert ids == ids_ref
