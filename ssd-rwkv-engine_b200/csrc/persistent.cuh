@@ -46,7 +46,10 @@ struct PArgs {
 // ---------------------------------------------------------------- cursor
 // Stage sequence of one CTA: per token, per layer phases A (r/k/v rows of the
 // concatenated [3C] rows, then first-adapter items), C (att_out rows),
-// D (ffn key rows), E (ffn value rows); then the head rows.
+// D (ffn key rows), E (ffn value rows); then the head rows.  The per-CTA row
+// ranges and stage counts are computed once into shared memory (PTable); only
+// thread 0 walks the issue cursor, and each issued stage's descriptor is kept
+// beside its ring slot for the consumers.
 struct Cursor {
   int tok, layer, phase, j;  // phase 0 A, 1 C, 2 D, 3 E, 4 head
 };
@@ -61,6 +64,17 @@ struct Stage {
   int item;         // adapter split index
 };
 
+constexpr int kMaxItems = 8;
+
+struct PTable {
+  int npiece;                  // phase A r/k/v pieces (<= 3)
+  int pm[3], pr0[3], pr1[3], pn[3];
+  int nrkv;                    // phase A r/k/v stages
+  int nitem[2];                // adapter items: [0] layer 0 (3 matrices), [1] other layers
+  int item[kMaxItems];         // global item ids (matrix * splits + split), ascending
+  int r0[4], r1[4], n[4];      // phases C, D, E, head
+};
+
 __device__ __forceinline__ void split_rows(int n, int parts, int i, int* a, int* b) {
   const int base = n / parts, rem = n % parts;
   *a = i * base + min(i, rem);
@@ -69,26 +83,40 @@ __device__ __forceinline__ void split_rows(int n, int parts, int i, int* a, int*
 
 __device__ __forceinline__ int nstages(int rows, int rs) { return rows > 0 ? (rows + rs - 1) / rs : 0; }
 
-// Number of ring stages of phase `ph` in layer `l` for this CTA.
-__device__ __forceinline__ int phase_stages(const PArgs& a, int l, int ph) {
+// Fill the table (thread 0).
+__device__ __forceinline__ void build_table(const PArgs& a, PTable& T) {
   const int G = gridDim.x, bx = blockIdx.x, C = a.d.C;
   int r0, r1;
-  if (ph == 0) {
-    split_rows(3 * C, G, bx, &r0, &r1);
-    int n = 0;
-    for (int m = 0; m < 3; ++m) {
-      const int lo = max(r0, m * C), hi = min(r1, (m + 1) * C);
-      n += nstages(hi - lo, a.gc.rs);
+  split_rows(3 * C, G, bx, &r0, &r1);
+  T.npiece = 0;
+  T.nrkv = 0;
+  for (int m = 0; m < 3; ++m) {
+    const int lo = max(r0, m * C), hi = min(r1, (m + 1) * C);
+    if (hi > lo) {
+      const int k = T.npiece++;
+      T.pm[k] = m;
+      T.pr0[k] = lo - m * C;
+      T.pr1[k] = hi - m * C;
+      T.pn[k] = nstages(hi - lo, a.gc.rs);
+      T.nrkv += T.pn[k];
     }
-    const int items = (l == 0 ? 3 : 4) * a.d.adp_splits;
-    n += bx < items ? (items - 1 - bx) / G + 1 : 0;
-    return n;
   }
-  if (ph == 1) { split_rows(C, G, bx, &r0, &r1); return nstages(r1 - r0, a.gc.rs); }
-  if (ph == 2) { split_rows(a.d.F, G, bx, &r0, &r1); return nstages(r1 - r0, a.gc.rs); }
-  if (ph == 3) { split_rows(C, G, bx, &r0, &r1); return nstages(r1 - r0, a.gf.rs); }
-  split_rows(a.d.V, G, bx, &r0, &r1);
-  return nstages(r1 - r0, a.gc.rs);
+  const int items3 = 3 * a.d.adp_splits, items4 = 4 * a.d.adp_splits;
+  T.nitem[0] = T.nitem[1] = 0;
+  for (int it = bx; it < items4 && T.nitem[1] < kMaxItems; it += G) {
+    T.item[T.nitem[1]++] = it;
+    if (it < items3) T.nitem[0] = T.nitem[1];
+  }
+  const int rows[4] = {C, a.d.F, C, a.d.V};
+  const int rs[4] = {a.gc.rs, a.gc.rs, a.gf.rs, a.gc.rs};
+  for (int p = 0; p < 4; ++p) {
+    split_rows(rows[p], G, bx, &T.r0[p], &T.r1[p]);
+    T.n[p] = nstages(T.r1[p] - T.r0[p], rs[p]);
+  }
+}
+
+__device__ __forceinline__ int phase_count(const PTable& T, int l, int ph) {
+  return ph == 0 ? T.nrkv + T.nitem[l == 0 ? 0 : 1] : T.n[ph - 1];
 }
 
 __device__ __forceinline__ const PackedView& gemv_mat(const PArgs& a, int l, int mat) {
@@ -109,12 +137,10 @@ __device__ __forceinline__ const PackedView& adp_mat(const PArgs& a, int l, int 
   return m == 0 ? L.w1 : (m == 1 ? L.a1 : (m == 2 ? L.g1 : L.v1));
 }
 
-// Move to the first stage at or after `c` (skipping empty phases).  Returns
-// false when the launch's stage sequence is exhausted.
-__device__ __forceinline__ bool cursor_norm(const PArgs& a, Cursor& c) {
+// Move to the first stage at or after `c`; false when the launch is done.
+__device__ __forceinline__ bool cursor_norm(const PArgs& a, const PTable& T, Cursor& c) {
   while (c.tok < a.ntok) {
-    const int n = phase_stages(a, c.layer, c.phase);
-    if (c.j < n) return true;
+    if (c.j < phase_count(T, c.layer, c.phase)) return true;
     c.j = 0;
     if (c.phase == 4) {
       c.phase = 0;
@@ -134,34 +160,25 @@ __device__ __forceinline__ bool cursor_norm(const PArgs& a, Cursor& c) {
   return false;
 }
 
-__device__ __forceinline__ Stage stage_of(const PArgs& a, const Cursor& c) {
+__device__ __forceinline__ Stage stage_of(const PArgs& a, const PTable& T, const Cursor& c) {
   Stage s;
-  const int G = gridDim.x, bx = blockIdx.x, C = a.d.C;
   s.kind = 0;
   s.item = 0;
-  int r0, r1, mat = 0, rs = a.gc.rs, j = c.j;
+  int r0 = 0, r1 = 0, mat = 0, j = c.j;
+  const PGeom* g = &a.gc;
   if (c.phase == 0) {
-    split_rows(3 * C, G, bx, &r0, &r1);
-    bool found = false;
-    for (int m = 0; m < 3 && !found; ++m) {
-      const int lo = max(r0, m * C), hi = min(r1, (m + 1) * C);
-      const int n = nstages(hi - lo, rs);
-      if (j < n) {
-        mat = m;
-        r0 = lo - m * C + j * rs;
-        r1 = min(hi - m * C, r0 + rs);
-        found = true;
-      } else {
-        j -= n;
-      }
-    }
-    if (!found) {
-      // first-adapter item
-      const int item = bx + G * j;
-      const int m = item / a.d.adp_splits, sp = item % a.d.adp_splits;
+    if (j < T.nrkv) {
+      int k = 0;
+      while (j >= T.pn[k]) j -= T.pn[k++];
+      mat = T.pm[k];
+      r0 = T.pr0[k] + j * a.gc.rs;
+      r1 = min(T.pr1[k], r0 + a.gc.rs);
+    } else {
+      const int item = T.item[j - T.nrkv];
+      const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
       const PackedView& W = adp_mat(a, c.layer, m);
       const int R = W.cols;
-      const int i0 = sp * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows);
+      const int i0 = sp * a.d.adp_rows, i1 = min(a.d.C, i0 + a.d.adp_rows);
       const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg);
       const uint32_t g1 = (uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) + 1);
       const uint32_t g0a = g0 & ~1u, g1a = (g1 + 1) & ~1u;  // 16-byte aligned pair range
@@ -177,22 +194,21 @@ __device__ __forceinline__ Stage stage_of(const PArgs& a, const Cursor& c) {
       return s;
     }
   } else {
-    const int rows = c.phase == 1 ? C : (c.phase == 2 ? a.d.F : (c.phase == 3 ? C : a.d.V));
-    split_rows(rows, G, bx, &r0, &r1);
-    mat = c.phase == 1 ? 3 : (c.phase == 2 ? 4 : (c.phase == 3 ? 5 : 6));
-    if (c.phase == 3) rs = a.gf.rs;
-    r0 += j * rs;
-    r1 = min(r1, r0 + rs);
+    const int p = c.phase - 1;
+    const int rs = p == 2 ? a.gf.rs : a.gc.rs;
+    if (p == 2) g = &a.gf;
+    mat = p == 0 ? 3 : (p == 1 ? 4 : (p == 2 ? 5 : 6));
+    r0 = T.r0[p] + j * rs;
+    r1 = min(T.r1[p], r0 + rs);
   }
   const PackedView& W = gemv_mat(a, c.layer, mat);
-  const PGeom& g = c.phase == 3 ? a.gf : a.gc;
   s.mat = mat;
   s.row0 = r0;
   s.nrows = r1 - r0;
-  s.q = W.payload + (size_t)r0 * g.K;
-  s.qb = (uint32_t)(s.nrows * g.K);
-  s.s = W.meta + (size_t)r0 * g.gpr * 8;
-  s.sb = (uint32_t)s.nrows * (uint32_t)g.gpr * 8u;
+  s.q = W.payload + (size_t)r0 * g->K;
+  s.qb = (uint32_t)(s.nrows * g->K);
+  s.s = W.meta + (size_t)r0 * g->gpr * 8;
+  s.sb = (uint32_t)s.nrows * (uint32_t)g->gpr * 8u;
   return s;
 }
 
@@ -299,6 +315,8 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
   __shared__ int s_tok;
   __shared__ float s_bv[kPWarps];
   __shared__ int s_bi[kPWarps];
+  __shared__ PTable T;
+  __shared__ Stage sdesc[8];  // descriptor of the stage held by each ring slot
 
   const int C = a.d.C, F = a.d.F, G = gridDim.x, bx = blockIdx.x, t = threadIdx.x;
   const int lane = t & 31, wid = t >> 5;
@@ -314,13 +332,15 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
   bool alive = true;
 
   // ---- ring prologue
-  Cursor ic{0, 0, 0, 0}, cc{0, 0, 0, 0};
+  Cursor ic{0, 0, 0, 0};
   if (t == 0) {
+    build_table(a, T);
     for (int i = 0; i < a.nst; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
     for (int i = 0; i < a.nst; ++i) {
-      if (!cursor_norm(a, ic)) break;
-      issue_stage(a, smb, bars, i, stage_of(a, ic));
+      if (!cursor_norm(a, T, ic)) break;
+      sdesc[i] = stage_of(a, T, ic);
+      issue_stage(a, smb, bars, i, sdesc[i]);
       ++ic.j;
     }
   }
@@ -331,8 +351,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
   float xs[CPL];
   int xr_tag = -1;  // which input the registers hold
 
-  // wait for the next stage, compute it (body), refill its slot
-  auto consume = [&](auto body) -> bool {
+  // Wait for the next stage, run compute(stage, slot, partials) while the slot
+  // is live, refill the slot, then run epi(stage, partials).
+  auto consume = [&](auto compute, auto epi) -> bool {
     const int slot = seq % a.nst;
     if (t == 0) {
       const bool got = mbar_wait_bounded(&bars[slot], (uint32_t)((seq / a.nst) & 1), a.spin_limit);
@@ -341,18 +362,17 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
     }
     __syncthreads();
     if (flag) return false;
-    const Stage st = stage_of(a, cc);
-    body(st, smb + (size_t)slot * a.slot_bytes, part + (seq & 1) * 512);
+    const Stage st = sdesc[slot];
+    float* pt = part + (seq & 1) * 512;
+    compute(st, smb + (size_t)slot * a.slot_bytes, pt);
     __syncthreads();
-    if (t == 0) {
-      if (cursor_norm(a, ic)) {
-        issue_stage(a, smb, bars, slot, stage_of(a, ic));
-        ++ic.j;
-      }
+    if (t == 0 && cursor_norm(a, T, ic)) {
+      sdesc[slot] = stage_of(a, T, ic);
+      issue_stage(a, smb, bars, slot, sdesc[slot]);
+      ++ic.j;
     }
+    epi(st, pt);
     ++seq;
-    ++cc.j;
-    cursor_norm(a, cc);
     return true;
   };
 
@@ -416,62 +436,68 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
       __syncthreads();
       layer_norm(LN, Ly.ln1_w, Ly.ln1_b);
       xr_tag = -1;
-      const int nA = phase_stages(a, l, 0);
+      const int nA = phase_count(T, l, 0);
       for (int k = 0; k < nA && alive; ++k) {
-        alive = consume([&](const Stage& st, const uint8_t* slot, float* pt) {
-          if (st.kind == 0) {
-            const float* mix = st.mat == 0 ? Ly.x_r : (st.mat == 1 ? Ly.x_k : Ly.x_v);
-            if (xr_tag != st.mat) {
-              load_x<CPL>(a.gc, [&](int i) {
-                const float4 z = *reinterpret_cast<const float4*>(LN + i);
-                const float4 p = ldcg4(prev_att + i), m = ldg4(mix + i);
-                return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
-                                   z.w + (p.w - z.w) * m.w);
-              }, xr, xs);
-              xr_tag = st.mat;
-            }
-            gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
-            __syncthreads();
-            if (t < st.nrows) {
-              float v = 0.f;
-              for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
-              a.b.rkv[(size_t)st.mat * C + st.row0 + t] = v;
-            }
-          } else {
-            // first adapter item: rows [row0, row0+nrows) of W [C, R] (x @ W)
-            const PackedView& W = adp_mat(a, l, st.mat);
-            const float* mix = st.mat == 0 ? Ly.x_w : (st.mat == 1 ? Ly.x_a : (st.mat == 2 ? Ly.x_g : Ly.x_v));
-            const int R = W.cols, nr = st.nrows;
-            float* xm = misc;          // [nr] mixed input
-            float* pr = misc + 256;    // [nrg][R] partials
-            for (int i = t; i < nr; i += kPThreads) {
-              const int gi = st.row0 + i;
-              xm[i] = LN[gi] + (__ldcg(prev_att + gi) - LN[gi]) * __ldg(mix + gi);
-            }
-            __syncthreads();
-            const uint8_t* cq = slot;
-            const float2* cs = reinterpret_cast<const float2*>(slot + ((st.qb + 15u) & ~15u));
-            const uint32_t g0 = ((uint32_t)(((uint64_t)st.row0 * R) >> W.lg)) & ~1u;
-            const int nrg = kPThreads / R;  // row groups
-            if (t < nrg * R) {
-              const int j = t % R, rg = t / R;
-              float acc = 0.f;
-              for (int i = rg; i < nr; i += nrg) {
-                const uint32_t e = (uint32_t)(st.row0 + i) * (uint32_t)R + (uint32_t)j;
-                const float2 sc = cs[(e >> W.lg) - g0];
-                acc = fmaf(xm[i], sg8_dequant(cq[i * R + j], sc.x, sc.y), acc);
+        alive = consume(
+            [&](const Stage& st, const uint8_t* slot, float* pt) {
+              if (st.kind == 0) {
+                const float* mix = st.mat == 0 ? Ly.x_r : (st.mat == 1 ? Ly.x_k : Ly.x_v);
+                if (xr_tag != st.mat) {
+                  load_x<CPL>(a.gc, [&](int i) {
+                    const float4 z = *reinterpret_cast<const float4*>(LN + i);
+                    const float4 p = ldcg4(prev_att + i), m = ldg4(mix + i);
+                    return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
+                                       z.w + (p.w - z.w) * m.w);
+                  }, xr, xs);
+                  xr_tag = st.mat;
+                }
+                gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
+              } else {
+                // first adapter item: rows [row0, row0+nrows) of W [C, R] (x @ W)
+                const PackedView& W = adp_mat(a, l, st.mat);
+                const float* mix = st.mat == 0 ? Ly.x_w : (st.mat == 1 ? Ly.x_a : (st.mat == 2 ? Ly.x_g : Ly.x_v));
+                const int R = W.cols, nr = st.nrows;
+                float* xm = misc;  // [nr] mixed input
+                for (int i = t; i < nr; i += kPThreads) {
+                  const int gi = st.row0 + i;
+                  xm[i] = LN[gi] + (__ldcg(prev_att + gi) - LN[gi]) * __ldg(mix + gi);
+                }
+                __syncthreads();
+                const uint8_t* cq = slot;
+                const float2* cs = reinterpret_cast<const float2*>(slot + ((st.qb + 15u) & ~15u));
+                const uint32_t g0 = ((uint32_t)(((uint64_t)st.row0 * R) >> W.lg)) & ~1u;
+                const int nrg = kPThreads / R;  // row groups
+                if (t < nrg * R) {
+                  const int j = t % R, rg = t / R;
+                  float acc = 0.f;
+                  for (int i = rg; i < nr; i += nrg) {
+                    const uint32_t e = (uint32_t)(st.row0 + i) * (uint32_t)R + (uint32_t)j;
+                    const float2 sc = cs[(e >> W.lg) - g0];
+                    acc = fmaf(xm[i], sg8_dequant(cq[i * R + j], sc.x, sc.y), acc);
+                  }
+                  misc[256 + rg * R + j] = acc;
+                }
               }
-              pr[rg * R + j] = acc;
-            }
-            __syncthreads();
-            const int off = st.mat == 0 ? 0 : (st.mat == 1 ? a.d.rw : (st.mat == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
-            for (int j = t; j < R; j += kPThreads) {
-              float v = 0.f;
-              for (int rg = 0; rg < nrg; ++rg) v += pr[rg * R + j];
-              a.b.adp[(size_t)st.item * a.d.rtot + off + j] = v;
-            }
-          }
-        });
+            },
+            [&](const Stage& st, float* pt) {
+              if (st.kind == 0) {
+                if (t < st.nrows) {
+                  float v = 0.f;
+                  for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
+                  a.b.rkv[(size_t)st.mat * C + st.row0 + t] = v;
+                }
+              } else {
+                const int R = adp_mat(a, l, st.mat).cols;
+                const int nrg = kPThreads / R;
+                const int off = st.mat == 0 ? 0 : (st.mat == 1 ? a.d.rw : (st.mat == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
+                for (int j = t; j < R; j += kPThreads) {
+                  float v = 0.f;
+                  for (int rg = 0; rg < nrg; ++rg) v += misc[256 + rg * R + j];
+                  a.b.adp[(size_t)st.item * a.d.rtot + off + j] = v;
+                }
+                __syncthreads();  // misc is reused by the next adapter item
+              }
+            });
       }
       if (!alive) break;
       // ======== phase B: one head per CTA (head h = bx)
@@ -588,23 +614,25 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
       if (!grid_sync(a, target, &flag)) { alive = false; break; }
       // ======== phase C: output projection + residual; x_prev(att) <- ln1
       xr_tag = -1;
-      const int nC = phase_stages(a, l, 1);
+      const int nC = phase_count(T, l, 1);
       for (int k = 0; k < nC && alive; ++k) {
-        alive = consume([&](const Stage& st, const uint8_t* slot, float* pt) {
-          if (xr_tag != 3) {
-            load_x<CPL>(a.gc, [&](int i) { return ldcg4(a.b.att_y + i); }, xr, xs);
-            xr_tag = 3;
-          }
-          gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
-          __syncthreads();
-          if (t < st.nrows) {
-            float v = 0.f;
-            for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
-            const int row = st.row0 + t;
-            a.b.xb[row] = X[row] + v;
-            a.b.att_x[(size_t)l * C + row] = LN[row];
-          }
-        });
+        alive = consume(
+            [&](const Stage& st, const uint8_t* slot, float* pt) {
+              if (xr_tag != 3) {
+                load_x<CPL>(a.gc, [&](int i) { return ldcg4(a.b.att_y + i); }, xr, xs);
+                xr_tag = 3;
+              }
+              gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
+            },
+            [&](const Stage& st, float* pt) {
+              if (t < st.nrows) {
+                float v = 0.f;
+                for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
+                const int row = st.row0 + t;
+                a.b.xb[row] = X[row] + v;
+                a.b.att_x[(size_t)l * C + row] = LN[row];
+              }
+            });
       }
       if (!alive) break;
       if (!grid_sync(a, target, &flag)) { alive = false; break; }
@@ -615,48 +643,52 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
       layer_norm(LN2, Ly.ln2_w, Ly.ln2_b);
       const float* prev_ffn = a.b.ffn_x + (size_t)l * C;
       xr_tag = -1;
-      const int nD = phase_stages(a, l, 2);
+      const int nD = phase_count(T, l, 2);
       for (int k = 0; k < nD && alive; ++k) {
-        alive = consume([&](const Stage& st, const uint8_t* slot, float* pt) {
-          if (xr_tag != 4) {
-            load_x<CPL>(a.gc, [&](int i) {
-              const float4 z = *reinterpret_cast<const float4*>(LN2 + i);
-              const float4 p = ldcg4(prev_ffn + i), m = ldg4(Ly.ffn_x_k + i);
-              return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
-                                 z.w + (p.w - z.w) * m.w);
-            }, xr, xs);
-            xr_tag = 4;
-          }
-          gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
-          __syncthreads();
-          if (t < st.nrows) {
-            float v = 0.f;
-            for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
-            a.b.h[st.row0 + t] = v > 0.f ? v * v : 0.f;
-          }
-        });
+        alive = consume(
+            [&](const Stage& st, const uint8_t* slot, float* pt) {
+              if (xr_tag != 4) {
+                load_x<CPL>(a.gc, [&](int i) {
+                  const float4 z = *reinterpret_cast<const float4*>(LN2 + i);
+                  const float4 p = ldcg4(prev_ffn + i), m = ldg4(Ly.ffn_x_k + i);
+                  return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
+                                     z.w + (p.w - z.w) * m.w);
+                }, xr, xs);
+                xr_tag = 4;
+              }
+              gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
+            },
+            [&](const Stage& st, float* pt) {
+              if (t < st.nrows) {
+                float v = 0.f;
+                for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
+                a.b.h[st.row0 + t] = v > 0.f ? v * v : 0.f;
+              }
+            });
       }
       if (!alive) break;
       if (!grid_sync(a, target, &flag)) { alive = false; break; }
       // ======== phase E: FFN value rows + residual; x_prev(ffn) <- ln2
       xr_tag = -1;
-      const int nE = phase_stages(a, l, 3);
+      const int nE = phase_count(T, l, 3);
       for (int k = 0; k < nE && alive; ++k) {
-        alive = consume([&](const Stage& st, const uint8_t* slot, float* pt) {
-          if (xr_tag != 5) {
-            load_x<CPL>(a.gf, [&](int i) { return ldcg4(a.b.h + i); }, xr, xs);
-            xr_tag = 5;
-          }
-          gemv_stage<CPL>(slot, a.gf, a.lg, st.nrows, xr, xs, pt);
-          __syncthreads();
-          if (t < st.nrows) {
-            float v = 0.f;
-            for (int s = 0; s < a.gf.nseg; ++s) v += pt[t * a.gf.nseg + s];
-            const int row = st.row0 + t;
-            a.b.xa[row] = XB[row] + v;
-            a.b.ffn_x[(size_t)l * C + row] = LN2[row];
-          }
-        });
+        alive = consume(
+            [&](const Stage& st, const uint8_t* slot, float* pt) {
+              if (xr_tag != 5) {
+                load_x<CPL>(a.gf, [&](int i) { return ldcg4(a.b.h + i); }, xr, xs);
+                xr_tag = 5;
+              }
+              gemv_stage<CPL>(slot, a.gf, a.lg, st.nrows, xr, xs, pt);
+            },
+            [&](const Stage& st, float* pt) {
+              if (t < st.nrows) {
+                float v = 0.f;
+                for (int s = 0; s < a.gf.nseg; ++s) v += pt[t * a.gf.nseg + s];
+                const int row = st.row0 + t;
+                a.b.xa[row] = XB[row] + v;
+                a.b.ffn_x[(size_t)l * C + row] = LN2[row];
+              }
+            });
       }
     }
     if (!alive) break;
@@ -667,23 +699,25 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
     xr_tag = -1;
     float best = -INFINITY;
     int besti = 0x7fffffff;
-    const int nH = phase_stages(a, 0, 4);
+    const int nH = phase_count(T, 0, 4);
     for (int k = 0; k < nH && alive; ++k) {
-      alive = consume([&](const Stage& st, const uint8_t* slot, float* pt) {
-        if (xr_tag != 6) {
-          load_x<CPL>(a.gc, [&](int i) { return *reinterpret_cast<const float4*>(X + i); }, xr, xs);
-          xr_tag = 6;
-        }
-        gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
-        __syncthreads();
-        if (t < st.nrows) {
-          float v = 0.f;
-          for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
-          const int row = st.row0 + t;
-          a.b.logits[row] = v;
-          if (v > best || (v == best && row < besti)) { best = v; besti = row; }
-        }
-      });
+      alive = consume(
+          [&](const Stage& st, const uint8_t* slot, float* pt) {
+            if (xr_tag != 6) {
+              load_x<CPL>(a.gc, [&](int i) { return *reinterpret_cast<const float4*>(X + i); }, xr, xs);
+              xr_tag = 6;
+            }
+            gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
+          },
+          [&](const Stage& st, float* pt) {
+            if (t < st.nrows) {
+              float v = 0.f;
+              for (int s = 0; s < a.gc.nseg; ++s) v += pt[t * a.gc.nseg + s];
+              const int row = st.row0 + t;
+              a.b.logits[row] = v;
+              if (v > best || (v == best && row < besti)) { best = v; besti = row; }
+            }
+          });
     }
     if (!alive) break;
     // per-CTA argmax -> global partials -> every CTA reduces (first maximum)
