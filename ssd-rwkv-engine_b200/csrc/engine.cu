@@ -872,7 +872,7 @@ bool plan_persistent(rwkvb_engine* e) {
   const Dims& d = e->d;
   const LayerDev& l0 = e->layers[0];
   const int lg = l0.r.lg;
-  if (lg < 4 || e->sms < d.H) return false;  // one CTA per head in the WKV phase
+  if (lg < 4 || e->sms < d.H || d.L > kMaxLayers) return false;  // one CTA per head in the WKV phase
   // every large projection: SG8, same group, row-aligned, 16-byte aligned payload + metadata
   auto big_ok = [&](const PackedView& w) {
     return w.kind == RWKVB_KIND_SG8 && w.lg == lg && aligned16(w.payload) && aligned16(w.meta);
@@ -926,7 +926,7 @@ bool plan_persistent(rwkvb_engine* e) {
   off += (wk + 127u) & ~127u;
   a.o_misc = off;            off += 1024 * 4;
   a.smem_total = off;
-  if (off > 227 * 1024) return false;
+  if (off + 16 * 1024 > 227 * 1024) return false;  // static shared memory of the kernel included
   a.layers = e->dlayers;
   a.emb = e->emb;
   a.head = e->head;

@@ -65,6 +65,17 @@ struct Stage {
 };
 
 constexpr int kMaxItems = 8;
+constexpr int kMaxLayers = 64;
+
+// Per-layer source pointers used by the issue cursor, kept in shared memory so
+// that refilling a slot never waits on a global load.
+struct LayerSrc {
+  const uint8_t* pay[6];   // r, k, v, o, fk, fv code payloads
+  const uint8_t* meta[6];  // their scale pairs
+  const uint8_t* apay[4];  // first adapters w1, a1, g1, v1
+  const uint8_t* ameta[4];
+  int acols[4], alg[4];
+};
 
 struct PTable {
   int npiece;                  // phase A r/k/v pieces (<= 3)
@@ -160,7 +171,7 @@ __device__ __forceinline__ bool cursor_norm(const PArgs& a, const PTable& T, Cur
   return false;
 }
 
-__device__ __forceinline__ Stage stage_of(const PArgs& a, const PTable& T, const Cursor& c) {
+__device__ __forceinline__ Stage stage_of(const PArgs& a, const PTable& T, const LayerSrc* LS, const Cursor& c) {
   Stage s;
   s.kind = 0;
   s.item = 0;
@@ -176,20 +187,20 @@ __device__ __forceinline__ Stage stage_of(const PArgs& a, const PTable& T, const
     } else {
       const int item = T.item[j - T.nrkv];
       const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
-      const PackedView& W = adp_mat(a, c.layer, m);
-      const int R = W.cols;
+      const LayerSrc& ls = LS[c.layer];
+      const int R = ls.acols[m], lgm = ls.alg[m];
       const int i0 = sp * a.d.adp_rows, i1 = min(a.d.C, i0 + a.d.adp_rows);
-      const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg);
-      const uint32_t g1 = (uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) + 1);
+      const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> lgm);
+      const uint32_t g1 = (uint32_t)((((uint64_t)i1 * R - 1) >> lgm) + 1);
       const uint32_t g0a = g0 & ~1u, g1a = (g1 + 1) & ~1u;  // 16-byte aligned pair range
       s.kind = 1;
       s.mat = m;
       s.item = sp;
       s.row0 = i0;
       s.nrows = i1 - i0;
-      s.q = W.payload + (size_t)i0 * R;
+      s.q = ls.apay[m] + (size_t)i0 * R;
       s.qb = (uint32_t)((i1 - i0) * R);
-      s.s = W.meta + (size_t)g0a * 8;
+      s.s = ls.ameta[m] + (size_t)g0a * 8;
       s.sb = (g1a - g0a) * 8u;
       return s;
     }
@@ -201,13 +212,14 @@ __device__ __forceinline__ Stage stage_of(const PArgs& a, const PTable& T, const
     r0 = T.r0[p] + j * rs;
     r1 = min(T.r1[p], r0 + rs);
   }
-  const PackedView& W = gemv_mat(a, c.layer, mat);
+  const uint8_t* pay = mat == 6 ? a.head.payload : LS[c.layer].pay[mat];
+  const uint8_t* meta = mat == 6 ? a.head.meta : LS[c.layer].meta[mat];
   s.mat = mat;
   s.row0 = r0;
   s.nrows = r1 - r0;
-  s.q = W.payload + (size_t)r0 * g->K;
+  s.q = pay + (size_t)r0 * g->K;
   s.qb = (uint32_t)(s.nrows * g->K);
-  s.s = W.meta + (size_t)r0 * g->gpr * 8;
+  s.s = meta + (size_t)r0 * g->gpr * 8;
   s.sb = (uint32_t)s.nrows * (uint32_t)g->gpr * 8u;
   return s;
 }
@@ -317,6 +329,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
   __shared__ int s_bi[kPWarps];
   __shared__ PTable T;
   __shared__ Stage sdesc[8];  // descriptor of the stage held by each ring slot
+  __shared__ LayerSrc LS[kMaxLayers];
 
   const int C = a.d.C, F = a.d.F, G = gridDim.x, bx = blockIdx.x, t = threadIdx.x;
   const int lane = t & 31, wid = t >> 5;
@@ -331,7 +344,20 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
   unsigned target = 0;
   bool alive = true;
 
-  // ---- ring prologue
+  // ---- per-layer source table, then the ring prologue
+  for (int l = t; l < a.d.L; l += kPThreads) {
+    const LayerDev& L = a.layers[l];
+    const PackedView* gm[6] = {&L.r, &L.k, &L.v, &L.o, &L.fk, &L.fv};
+    for (int m = 0; m < 6; ++m) { LS[l].pay[m] = gm[m]->payload; LS[l].meta[m] = gm[m]->meta; }
+    const PackedView* am[4] = {&L.w1, &L.a1, &L.g1, &L.v1};
+    for (int m = 0; m < 4; ++m) {
+      LS[l].apay[m] = am[m]->payload;
+      LS[l].ameta[m] = am[m]->meta;
+      LS[l].acols[m] = am[m]->cols;
+      LS[l].alg[m] = am[m]->lg;
+    }
+  }
+  __syncthreads();
   Cursor ic{0, 0, 0, 0};
   if (t == 0) {
     build_table(a, T);
@@ -339,7 +365,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
     fence_mbar_init();
     for (int i = 0; i < a.nst; ++i) {
       if (!cursor_norm(a, T, ic)) break;
-      sdesc[i] = stage_of(a, T, ic);
+      sdesc[i] = stage_of(a, T, LS, ic);
       issue_stage(a, smb, bars, i, sdesc[i]);
       ++ic.j;
     }
@@ -355,19 +381,18 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
   // is live, refill the slot, then run epi(stage, partials).
   auto consume = [&](auto compute, auto epi) -> bool {
     const int slot = seq % a.nst;
-    if (t == 0) {
-      const bool got = mbar_wait_bounded(&bars[slot], (uint32_t)((seq / a.nst) & 1), a.spin_limit);
-      flag = got ? 0 : 1;
-      if (!got) atomicOr(a.b.err, kErrTimeout);
+    // every thread polls the slot's barrier (bounded); the CTA agrees on the outcome
+    const bool got = mbar_wait_bounded(&bars[slot], (uint32_t)((seq / a.nst) & 1), a.spin_limit);
+    if (!__syncthreads_and(got)) {
+      if (t == 0) atomicOr(a.b.err, kErrTimeout);
+      return false;
     }
-    __syncthreads();
-    if (flag) return false;
     const Stage st = sdesc[slot];
     float* pt = part + (seq & 1) * 512;
     compute(st, smb + (size_t)slot * a.slot_bytes, pt);
     __syncthreads();
     if (t == 0 && cursor_norm(a, T, ic)) {
-      sdesc[slot] = stage_of(a, T, ic);
+      sdesc[slot] = stage_of(a, T, LS, ic);
       issue_stage(a, smb, bars, slot, sdesc[slot]);
       ++ic.j;
     }
@@ -454,9 +479,8 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
                 gemv_stage<CPL>(slot, a.gc, a.lg, st.nrows, xr, xs, pt);
               } else {
                 // first adapter item: rows [row0, row0+nrows) of W [C, R] (x @ W)
-                const PackedView& W = adp_mat(a, l, st.mat);
                 const float* mix = st.mat == 0 ? Ly.x_w : (st.mat == 1 ? Ly.x_a : (st.mat == 2 ? Ly.x_g : Ly.x_v));
-                const int R = W.cols, nr = st.nrows;
+                const int R = LS[l].acols[st.mat], nr = st.nrows, wlg = LS[l].alg[st.mat];
                 float* xm = misc;  // [nr] mixed input
                 for (int i = t; i < nr; i += kPThreads) {
                   const int gi = st.row0 + i;
@@ -465,14 +489,14 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
                 __syncthreads();
                 const uint8_t* cq = slot;
                 const float2* cs = reinterpret_cast<const float2*>(slot + ((st.qb + 15u) & ~15u));
-                const uint32_t g0 = ((uint32_t)(((uint64_t)st.row0 * R) >> W.lg)) & ~1u;
+                const uint32_t g0 = ((uint32_t)(((uint64_t)st.row0 * R) >> wlg)) & ~1u;
                 const int nrg = kPThreads / R;  // row groups
                 if (t < nrg * R) {
                   const int j = t % R, rg = t / R;
                   float acc = 0.f;
                   for (int i = rg; i < nr; i += nrg) {
                     const uint32_t e = (uint32_t)(st.row0 + i) * (uint32_t)R + (uint32_t)j;
-                    const float2 sc = cs[(e >> W.lg) - g0];
+                    const float2 sc = cs[(e >> wlg) - g0];
                     acc = fmaf(xm[i], sg8_dequant(cq[i * R + j], sc.x, sc.y), acc);
                   }
                   misc[256 + rg * R + j] = acc;
@@ -487,7 +511,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
                   a.b.rkv[(size_t)st.mat * C + st.row0 + t] = v;
                 }
               } else {
-                const int R = adp_mat(a, l, st.mat).cols;
+                const int R = LS[l].acols[st.mat];
                 const int nrg = kPThreads / R;
                 const int off = st.mat == 0 ? 0 : (st.mat == 1 ? a.d.rw : (st.mat == 2 ? a.d.rw + a.d.ra : a.d.rw + a.d.ra + a.d.rg));
                 for (int j = t; j < R; j += kPThreads) {
@@ -539,13 +563,13 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
         const int used = l == 0 ? a.d.rw + a.d.ra + a.d.rg : a.d.rtot;
         for (int j = t; j < used; j += kPThreads) {
           float acc = 0.f;
-          for (int s0 = 0; s0 < a.d.adp_splits; s0 += 8) {
-            float v[8];
+          for (int s0 = 0; s0 < a.d.adp_splits; s0 += 24) {
+            float v[24];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < 24; ++u)
               v[u] = s0 + u < a.d.adp_splits ? __ldcg(a.b.adp + (size_t)(s0 + u) * a.d.rtot + j) : 0.f;
 #pragma unroll
-            for (int u = 0; u < 8; ++u) acc += v[u];
+            for (int u = 0; u < 24; ++u) acc += v[u];
           }
           if (j < a.d.rw) acc = tanhf(acc);
           else if (j >= a.d.rw + a.d.ra && j < a.d.rw + a.d.ra + a.d.rg) acc = sigmoidf_(acc);
