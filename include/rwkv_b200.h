@@ -164,6 +164,7 @@ typedef struct rwkvb_engine rwkvb_engine;
  * flags: bit0 = no CUDA-graph capture of the multi-kernel token step;
  *        bit1 = no programmatic dependent launch between phase kernels;
  *        bit2 = no persistent kernel (always use the multi-kernel step);
+ *        bit3 = record persistent-kernel phase timestamps (rwkvb_engine_trace);
  *        bit8 = bits 4..7 give an explicit L2-prefetch distance in phases.
  * When every projection is SG8 with one power-of-two group size and the
  * 16-byte layout that rwkvb upload placement gives, decode runs as ONE
@@ -198,6 +199,14 @@ int rwkvb_engine_decode_greedy(rwkvb_engine* e, int32_t first_token, int32_t n_t
  * (`out_tokens_dev`, n_tokens int32) and does not synchronise. */
 int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first_token, int32_t n_tokens,
                                      int32_t* out_tokens_dev, void* stream);
+
+/* Phase timestamps (ns, %globaltimer) of the last persistent launch, recorded
+ * when the engine was created with flag bit 3: [2][65536] (first CTA, last CTA),
+ * per token: token start, then per layer A start, A done, B barrier, B done,
+ * C barrier, C done, D barrier, D done, E barrier, E done; then head barrier,
+ * head done.  The GPU counterpart of the reference's per-layer LayerTiming rows
+ * (runtime/metrics.py:26-58).  Copies min(cap, 131072) values to host `out`. */
+int rwkvb_engine_trace(rwkvb_engine* e, uint64_t* out, int32_t cap, int32_t* n_out);
 
 /* Kernel launches per token step (for launch accounting). */
 int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out);

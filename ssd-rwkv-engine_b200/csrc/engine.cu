@@ -624,6 +624,8 @@ struct rwkvb_engine {
   int pcpl = 0;
   LayerDev* dlayers = nullptr;
   int* dtokens = nullptr;  // forced-token staging [hist_cap]
+  unsigned long long* dtrace = nullptr;  // phase timestamps (flag bit 3)
+  int trace_cap = 0;
 };
 
 namespace {
@@ -957,6 +959,8 @@ int launch_persistent(rwkvb_engine* e, int ntok, int mode, int first_tok, const 
   a.first_tok = first_tok;
   a.forced = forced;
   a.gbar = e->b.ticket;  // the argmax ticket word doubles as the grid-barrier counter here
+  a.trace = e->dtrace;
+  a.trace_cap = e->trace_cap;
   cudaError_t err = cudaMemsetAsync(a.gbar, 0, sizeof(unsigned), s);
   if (err != cudaSuccess) return cuda_status(err);
   void* args[] = {&a};
@@ -1082,6 +1086,13 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   }
   if (st == RWKVB_OK)
     st = cuda_status(cudaMemcpy(e->dlayers, e->layers.data(), sizeof(LayerDev) * (size_t)L, cudaMemcpyHostToDevice));
+  if (st == RWKVB_OK && (flags & 0x8u)) {
+    e->trace_cap = 1 << 16;
+    if (cudaMalloc((void**)&e->dtrace, sizeof(unsigned long long) * 2 * (size_t)e->trace_cap) != cudaSuccess) {
+      cudaGetLastError();
+      st = RWKVB_EALLOC;
+    }
+  }
   if (st == RWKVB_OK && !(flags & 0x4u) && plan_persistent(e)) {
     const void* fn = persistent_fn(e->pcpl);
     int per_sm = 0;
@@ -1114,6 +1125,7 @@ extern "C" int rwkvb_engine_destroy(rwkvb_engine* e) {
   if (e->arena) cudaFree(e->arena);
   if (e->dlayers) cudaFree(e->dlayers);
   if (e->dtokens) cudaFree(e->dtokens);
+  if (e->dtrace) cudaFree(e->dtrace);
   delete e;
   return RWKVB_OK;
 }
@@ -1231,4 +1243,13 @@ extern "C" int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out) {
   if (!e || !out) return RWKVB_EARG;
   *out = e->persistent ? 0 : 2 + 5 * e->d.L;  // persistent: one launch per decode call, not per step
   return RWKVB_OK;
+}
+
+extern "C" int rwkvb_engine_trace(rwkvb_engine* e, uint64_t* out, int32_t cap, int32_t* n_out) {
+  if (!e || !out || cap <= 0 || !n_out) return RWKVB_EARG;
+  if (!e->dtrace) return RWKVB_EUNSUPPORTED;
+  const int n = cap < 2 * e->trace_cap ? cap : 2 * e->trace_cap;
+  const int st = cuda_status(cudaMemcpy(out, e->dtrace, sizeof(uint64_t) * (size_t)n, cudaMemcpyDeviceToHost));
+  *n_out = n;
+  return st;
 }

@@ -39,6 +39,8 @@ struct PArgs {
   unsigned* gbar;     // grid barrier counter, zero at launch
   uint32_t spin_limit;
   int emb_fast;
+  unsigned long long* trace;  // optional phase timestamps: [2][trace_cap] (CTA 0, last CTA)
+  int trace_cap;
   // shared-memory offsets (bytes)
   uint32_t o_bars, o_part, o_x, o_ln, o_wkv, o_xb, o_ln2, o_misc, smem_total;
 };
@@ -232,6 +234,12 @@ __device__ __forceinline__ void issue_stage(const PArgs& a, uint8_t* smb, uint64
   bulk_g2s(dst + ((s.qb + 15u) & ~15u), s.s, s.sb, &bars[slot]);
 }
 
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long v;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(v));
+  return v;
+}
+
 // --------------------------------------------------------- grid barrier
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -343,6 +351,12 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
   float* misc = reinterpret_cast<float*>(smb + a.o_misc);
   unsigned target = 0;
   bool alive = true;
+  int tr = 0;  // trace slot
+  const int trow = bx == 0 ? 0 : (bx == G - 1 ? 1 : -1);
+  auto mark = [&]() {
+    if (a.trace && trow >= 0 && t == 0 && tr < a.trace_cap) a.trace[(size_t)trow * a.trace_cap + tr] = global_ns();
+    ++tr;
+  };
 
   // ---- per-layer source table, then the ring prologue
   for (int l = t; l < a.d.L; l += kPThreads) {
@@ -426,6 +440,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
       if (t == 0) atomicOr(a.b.err, kErrToken);
       tok = 0;
     }
+    mark();  // token start
     // ---- embedding + ln0 (every CTA, locally)
     {
       const PackedView& E = a.emb;
@@ -456,6 +471,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
         if (!grid_sync(a, target, &flag)) { alive = false; break; }
         load_vec(X, a.b.xa, C);
       }
+      mark();  // A start (x ready)
       // ======== phase A: ln1, mixes, r/k/v rows, first adapters
       for (int i = t; i < C; i += kPThreads) LN[i] = X[i];
       __syncthreads();
@@ -524,6 +540,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
             });
       }
       if (!alive) break;
+      mark();  // phase A done
       // ======== phase B: one head per CTA (head h = bx)
       const int H = a.d.H;
       const bool has_head = bx < H;
@@ -558,6 +575,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
         cp_async_commit();
       }
       if (!grid_sync(a, target, &flag)) { alive = false; break; }
+      mark();  // B barrier
       if (has_head) {
         const int h = bx;
         const int used = l == 0 ? a.d.rw + a.d.ra + a.d.rg : a.d.rtot;
@@ -635,7 +653,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
           a.b.att_y[ch] = o * vec[128 + t];
         }
       }
+      mark();  // B compute done
       if (!grid_sync(a, target, &flag)) { alive = false; break; }
+      mark();  // C barrier
       // ======== phase C: output projection + residual; x_prev(att) <- ln1
       xr_tag = -1;
       const int nC = phase_count(T, l, 1);
@@ -659,7 +679,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
             });
       }
       if (!alive) break;
+      mark();  // C done
       if (!grid_sync(a, target, &flag)) { alive = false; break; }
+      mark();  // D barrier
       // ======== phase D: ln2 + mix, FFN key rows, relu^2
       load_vec(XB, a.b.xb, C);
       for (int i = t; i < C; i += kPThreads) LN2[i] = XB[i];
@@ -691,7 +713,9 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
             });
       }
       if (!alive) break;
+      mark();  // D done
       if (!grid_sync(a, target, &flag)) { alive = false; break; }
+      mark();  // E barrier
       // ======== phase E: FFN value rows + residual; x_prev(ffn) <- ln2
       xr_tag = -1;
       const int nE = phase_count(T, l, 3);
@@ -714,10 +738,12 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
               }
             });
       }
+      mark();  // E done
     }
     if (!alive) break;
     // ======== head: ln_out, logits, argmax
     if (!grid_sync(a, target, &flag)) { alive = false; break; }
+    mark();  // head barrier
     load_vec(X, a.b.xa, C);
     layer_norm(X, a.lnout_w, a.lnout_b);
     xr_tag = -1;
@@ -744,6 +770,7 @@ __global__ void __launch_bounds__(kPThreads, 1) persistent_kernel(PArgs a) {
           });
     }
     if (!alive) break;
+    mark();  // head done
     // per-CTA argmax -> global partials -> every CTA reduces (first maximum)
     {
       float wb = best;

@@ -63,7 +63,7 @@ class B200Engine:
     """A packed RWKV-7 model resident on one GPU, decoded by the fused engine."""
 
     def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
-                 prefetch_distance: int | None = None, persistent: bool = True):
+                 prefetch_distance: int | None = None, persistent: bool = True, trace: bool = False):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
@@ -109,6 +109,8 @@ class B200Engine:
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
             if not persistent:
                 flags |= native.FLAG_NO_PERSISTENT
+            if trace:
+                flags |= native.FLAG_TRACE
             if prefetch_distance is not None:
                 flags |= native.FLAG_EXPLICIT_PREFETCH | ((int(prefetch_distance) & 0xF) << 4)
             h = ctypes.c_void_p()
@@ -144,6 +146,15 @@ class B200Engine:
     def _stream(self, stream=None) -> int:
         st = stream if stream is not None else torch.cuda.current_stream(self.device)
         return st.cuda_stream
+
+    def phase_trace(self) -> np.ndarray:
+        """Phase timestamps of the last persistent launch, ``[2, 65536]`` ns
+        (first CTA, last CTA); zeros where nothing was recorded."""
+        cap = 2 * 65536
+        buf = (ctypes.c_uint64 * cap)()
+        n = ctypes.c_int32()
+        native.check(self.lib.rwkvb_engine_trace(self._h, buf, cap, ctypes.byref(n)), "rwkvb_engine_trace")
+        return np.frombuffer(buf, dtype=np.uint64, count=n.value).reshape(2, -1).copy()
 
     # --------------------------------------------------------------- state
     def reset(self, stream=None) -> None:

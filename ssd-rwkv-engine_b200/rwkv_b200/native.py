@@ -35,6 +35,7 @@ LUT2_KINDS = (3, 4, 5, 6, 7)
 FLAG_NO_GRAPH = 0x1
 FLAG_NO_PDL = 0x2
 FLAG_NO_PERSISTENT = 0x4
+FLAG_TRACE = 0x8
 FLAG_EXPLICIT_PREFETCH = 0x100
 
 
@@ -107,6 +108,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_engine_decode_greedy": (ctypes.c_int, [vp, i32, i32, P(i32), vp]),
         "rwkvb_engine_decode_greedy_async": (ctypes.c_int, [vp, i32, i32, vp, vp]),
         "rwkvb_engine_launches_per_step": (ctypes.c_int, [vp, P(i32)]),
+        "rwkvb_engine_trace": (ctypes.c_int, [vp, P(u64), i32, P(i32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(h, name)  # AttributeError if the build lacks a declared symbol
