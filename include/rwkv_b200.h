@@ -45,6 +45,7 @@ extern "C" {
 #define RWKVB_ECUDA 3       /* a CUDA runtime call failed */
 #define RWKVB_ETIMEOUT 4    /* a bounded device wait gave up */
 #define RWKVB_EUNSUPPORTED 5
+#define RWKVB_ESCRATCH 6     /* request larger than a fixed static scratch buffer */
 
 /* blob kinds: the 4th magic byte ("SG8\x01" is kind 1, "TR2\xNN" is kind NN) */
 #define RWKVB_KIND_SG8 1u
@@ -118,6 +119,28 @@ int rwkvb_tmix_adapters_f32(float* w_out, float* a_out, float* g_out, float* v_o
  * Replaces scale_u8_grouped_cmix_gemv_f32_export (lut2_gather.c:505-610). */
 int rwkvb_cmix_gemv_f32(float* y, const rwkvb_packed* key, const rwkvb_packed* value,
                         const float* x, void* stream);
+
+/* Same result as rwkvb_cmix_gemv_f32, without any device allocation: the
+ * ffn-wide intermediate lives in a file-scope static device buffer of
+ * RWKVB_CMIX_NOALLOC_MAX_FFN floats (64 KiB) per device.
+ *   - key->rows (the ffn width) above RWKVB_CMIX_NOALLOC_MAX_FFN returns
+ *     RWKVB_ESCRATCH before touching the device.
+ *   - The first call on a device (with that device current) resolves the
+ *     buffer's address with cudaGetSymbolAddress; make that first call before
+ *     any stream capture.  Later calls make no allocating CUDA call.
+ *   - Nothing has to start at zero: the key GEMV writes every intermediate
+ *     element before the value GEMV reads it.
+ *   - One buffer per device: calls that overlap on one device (different
+ *     streams, or threads without ordering) race on it.  Serialise them.
+ * For callers that must not allocate device memory per call: a decode loop
+ * whose HBM is fully committed to resident weight arenas (a per-call
+ * allocation can fail mid-generation), and processes on devices or drivers
+ * without stream-ordered memory pools.
+ * No counterpart in the reference (its C kernel mallocs the intermediate on
+ * every call, lut2_gather.c:542-568). */
+#define RWKVB_CMIX_NOALLOC_MAX_FFN 16384
+int rwkvb_cmix_gemv_f32_noalloc(float* y, const rwkvb_packed* key, const rwkvb_packed* value,
+                                const float* x, void* stream);
 
 /* WKV7 recurrent state update for `batch` x `n_head` heads of size N = head_size (64):
  *   d = decay(w);  S = S * diag(d) + (S @ -kk) (kk*a)^T + v k^T;  y = S @ r

@@ -1,7 +1,9 @@
 // Op-level C-ABI entry points: dequant, GEMV family, fused adapters, fused
 // channel mix, WKV7.  Each mirrors one export of the reference's native
 // library (rwkv_ssd/native/lut2_gather.c); see include/rwkv_b200.h.
+#include <atomic>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -169,6 +171,7 @@ extern "C" const char* rwkvb_status_string(int st) {
     case RWKVB_ECUDA: return "CUDA runtime error";
     case RWKVB_ETIMEOUT: return "bounded device wait timed out";
     case RWKVB_EUNSUPPORTED: return "unsupported shape or configuration";
+    case RWKVB_ESCRATCH: return "request exceeds the fixed static scratch buffer";
     default: return "unknown status";
   }
 }
@@ -312,4 +315,51 @@ extern "C" int rwkvb_wkv7_f32(float* state, float* y, const float* r, const floa
   if (head_size != 64 || (decay_mode != 0 && decay_mode != 1)) return RWKVB_EUNSUPPORTED;
   wkv7_kernel<<<batch * n_head, 256, 0, (cudaStream_t)stream>>>(state, y, r, w, k, v, kk, a, n_head, decay_mode);
   return cuda_status(cudaGetLastError());
+}
+
+// ------------------------------------------------- no-allocation channel mix
+// The intermediate of rwkvb_cmix_gemv_f32_noalloc: one fixed buffer per device
+// (a __device__ variable is instantiated in every device's context).
+static __device__ __align__(256) float g_cmix_scratch[RWKVB_CMIX_NOALLOC_MAX_FFN];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::atomic<float*> g_cmix_scratch_ptr[kMaxDevices];
+std::mutex g_cmix_scratch_mu;
+
+// Address of g_cmix_scratch on the current device; resolved once per device.
+int cmix_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= kMaxDevices) return RWKVB_EUNSUPPORTED;
+  float* p = g_cmix_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
+    std::lock_guard<std::mutex> lock(g_cmix_scratch_mu);
+    p = g_cmix_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (!p) {
+      e = cudaGetSymbolAddress((void**)&p, g_cmix_scratch);
+      if (e != cudaSuccess) return cuda_status(e);
+      g_cmix_scratch_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return RWKVB_OK;
+}
+}  // namespace
+
+extern "C" int rwkvb_cmix_gemv_f32_noalloc(float* y, const rwkvb_packed* key, const rwkvb_packed* value,
+                                           const float* x, void* stream) {
+  if (!y || !x || !packed_ok(key) || !packed_ok(value)) return RWKVB_EARG;
+  if (value->cols != key->rows) return RWKVB_EARG;
+  if (key->rows > RWKVB_CMIX_NOALLOC_MAX_FFN) return RWKVB_ESCRATCH;
+  float* h = nullptr;
+  int st = cmix_scratch(&h);
+  if (st != RWKVB_OK) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  PackedView kv = make_view(*key), vv = make_view(*value);
+  st = launch_gemv(&kv, &x, &h, 1, 1, s);
+  const float* hc = h;
+  if (st == RWKVB_OK) st = launch_gemv(&vv, &hc, &y, 1, 0, s);
+  return st;
 }

@@ -27,6 +27,8 @@ RWKVB_EALLOC = 2
 RWKVB_ECUDA = 3
 RWKVB_ETIMEOUT = 4
 RWKVB_EUNSUPPORTED = 5
+RWKVB_ESCRATCH = 6
+CMIX_NOALLOC_MAX_FFN = 16384
 
 KIND_SG8 = 1
 LUT2_KINDS = (3, 4, 5, 6, 7)
@@ -98,6 +100,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_tmix_qkv_gemv_f32": (ctypes.c_int, [vp, P(P(Packed)), P(vp), vp]),
         "rwkvb_tmix_adapters_f32": (ctypes.c_int, [vp, vp, vp, vp, P(P(Packed)), P(vp), vp, ctypes.c_int, vp]),
         "rwkvb_cmix_gemv_f32": (ctypes.c_int, [vp, P(Packed), P(Packed), vp, vp]),
+        "rwkvb_cmix_gemv_f32_noalloc": (ctypes.c_int, [vp, P(Packed), P(Packed), vp, vp]),
         "rwkvb_wkv7_f32": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, vp]),
         "rwkvb_engine_create": (ctypes.c_int, [P(ModelDesc), u32, P(vp)]),
