@@ -64,6 +64,8 @@ struct Bufs {
   float *h;                    // [F]
   float *v_first;              // [C]
   float *logits;               // [V]
+  float *ao, *fo;              // [C] attention / ffn output accumulators (persistent kernel)
+  unsigned long long* adp64;   // [Rtot] first-adapter accumulators, 2^-32 fixed point (persistent kernel)
   float *amax_v;               // [grid] per-CTA argmax value
   int *amax_i;                 // [grid] per-CTA argmax index
   unsigned *ticket;            // last-CTA election for the argmax
@@ -81,7 +83,7 @@ struct Dims {
 };
 
 }  // namespace rwkvb
-#include "persistent.cuh"
+#include "decode.cuh"
 namespace rwkvb {
 
 // ------------------------------------------------------------ prefetch
@@ -620,8 +622,11 @@ struct rwkvb_engine {
   int launches = 0;
   // persistent path
   bool persistent = false;
-  PArgs pa{};
-  int pcpl = 0;
+  DArgs da{};
+  int lfk = 2;
+  size_t dsmem = 0;
+  DLayerMaps* dmaps = nullptr;
+  CUtensorMap* dhead = nullptr;
   LayerDev* dlayers = nullptr;
   int* dtokens = nullptr;  // forced-token staging [hist_cap]
   unsigned long long* dtrace = nullptr;  // phase timestamps (flag bit 3)
@@ -842,49 +847,47 @@ int run_step(rwkvb_engine* e, cudaStream_t s) {
 
 
 // ---------------------------------------------------------- persistent plan
-bool geom_for(int K, const PackedView& w, int cpl, PGeom* g) {
-  if (w.kind != RWKVB_KIND_SG8 || w.lg < 4 || K % (int)w.group != 0) return false;
-  const int gpr = K / (int)w.group;
-  if (gpr % 2 != 0) return false;
-  for (int nseg = 1; nseg <= kPWarps; nseg *= 2) {
-    if (K % nseg != 0) continue;
-    const int kseg = K / nseg;
-    if (kseg % (int)w.group != 0 || kseg % 16 != 0) continue;
-    if ((kseg / 16 + 31) / 32 != cpl) continue;
-    g->K = K;
-    g->gpr = gpr;
-    g->nseg = nseg;
-    g->kseg = kseg;
-    g->cpl = cpl;
-    g->row_bytes = (uint32_t)(K + gpr * 8);
-    const int wper = kPWarps / nseg;
-    int rs = wper;
-    while ((rs + wper) * (int)g->row_bytes <= 22 * 1024) rs += wper;
-    g->rs = rs;
-    return true;
-  }
-  return false;
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Decide whether the persistent kernel can run this model and fill its
-// arguments (everything except the per-launch token fields).
-bool plan_persistent(rwkvb_engine* e) {
+int encode_big(const PackedView& w, const DArgs& a, CUtensorMap* q, CUtensorMap* p) {
+  const uint64_t K = (uint64_t)w.cols, rows = (uint64_t)w.rows, gpr = K >> w.lg;
+  const uint64_t qd[3] = {128, rows, K / 128}, qs[2] = {K, 128};
+  const uint32_t qb[3] = {128, 16, (uint32_t)a.nb};
+  int st = encode_u8_map(q, 3, w.payload, qd, qs, qb, true);
+  const uint64_t pd[2] = {gpr * 8, rows}, ps[1] = {gpr * 8};
+  const uint32_t pb[2] = {(uint32_t)a.pr * 8u, 16};
+  if (st == RWKVB_OK) st = encode_u8_map(p, 2, w.meta, pd, ps, pb, false);
+  return st;
+}
+
+int encode_adp2(const PackedView& w, int box_rows, CUtensorMap* q, CUtensorMap* p) {
+  const uint64_t C = (uint64_t)w.cols, R = (uint64_t)w.rows, gpr = C >> w.lg;
+  const uint64_t qd[2] = {C, R}, qs[1] = {C};
+  const uint32_t qb[2] = {64, (uint32_t)box_rows};
+  int st = encode_u8_map(q, 2, w.payload, qd, qs, qb, false);
+  const uint64_t pd[2] = {gpr * 8, R}, ps[1] = {gpr * 8};
+  const uint32_t pb[2] = {16, (uint32_t)box_rows};
+  if (st == RWKVB_OK) st = encode_u8_map(p, 2, w.meta, pd, ps, pb, false);
+  return st;
+}
+
+// Decide whether the persistent decode kernel can run this model, fill its
+// arguments (everything except the per-launch token fields) and encode its
+// tensor maps.
+bool plan_decode(rwkvb_engine* e) {
   const Dims& d = e->d;
   const LayerDev& l0 = e->layers[0];
   const int lg = l0.r.lg;
-  if (lg < 4 || e->sms < d.H || d.L > kMaxLayers) return false;  // one CTA per head in the WKV phase
-  // every large projection: SG8, same group, row-aligned, 16-byte aligned payload + metadata
+  if ((lg != 6 && lg != 7) || d.C % 128 != 0 || d.F % 128 != 0 || e->sms < d.H) return false;
   auto big_ok = [&](const PackedView& w) {
     return w.kind == RWKVB_KIND_SG8 && w.lg == lg && aligned16(w.payload) && aligned16(w.meta);
   };
   auto adp1_ok = [&](const PackedView& w) {
-    return w.kind == RWKVB_KIND_SG8 && w.lg >= 0 && w.cols % 16 == 0 && w.cols <= kPThreads &&
-           aligned16(w.payload) && aligned16(w.meta);
+    return w.kind == RWKVB_KIND_SG8 && w.lg >= 0 && w.cols % 16 == 0 && aligned16(w.payload) && aligned16(w.meta);
   };
   auto adp2_ok = [&](const PackedView& w) {
-    return w.kind == RWKVB_KIND_SG8 && w.lg >= 6 && d.C % (int)w.group == 0 && aligned16(w.payload);
+    return w.kind == RWKVB_KIND_SG8 && w.lg >= 6 && d.C % (int)w.group == 0 && ((d.C >> w.lg) % 2) == 0 &&
+           aligned16(w.payload) && aligned16(w.meta);
   };
   for (int i = 0; i < d.L; ++i) {
     const LayerDev& l = e->layers[i];
@@ -893,67 +896,105 @@ bool plan_persistent(rwkvb_engine* e) {
     if (!adp2_ok(l.w2) || !adp2_ok(l.a2) || !adp2_ok(l.g2) || (i > 0 && !adp2_ok(l.v2))) return false;
   }
   if (!big_ok(e->head)) return false;
-  PGeom gc{}, gf{};
-  int cpl = 0;
-  for (int c : {3, 2, 1, 4}) {
-    if (geom_for(d.C, l0.r, c, &gc) && geom_for(d.F, l0.fv, c, &gf)) { cpl = c; break; }
-  }
-  if (!cpl) return false;
-  PArgs& a = e->pa;
+  int nb = 0;
+  for (int c = kDW; c >= 1 && !nb; --c)
+    if ((d.C / 128) % c == 0 && (d.F / 128) % c == 0 && (((c * 128) >> lg) % 2) == 0) nb = c;
+  if (!nb) return false;
+  DArgs& a = e->da;
   memset(&a, 0, sizeof(a));
-  a.gc = gc;
-  a.gf = gf;
+  a.nb = nb;
+  a.kc = nb * 128;
+  a.pr = a.kc >> lg;
   a.lg = lg;
-  a.nst = 4;
-  uint32_t slot = (uint32_t)gc.rs * gc.row_bytes;
-  slot = slot > (uint32_t)gf.rs * gf.row_bytes ? slot : (uint32_t)gf.rs * gf.row_bytes;
-  // first-adapter items share the slots
-  const int rmax = d.rw > d.ra ? (d.rw > d.rg ? d.rw : d.rg) : (d.ra > d.rg ? d.ra : d.rg);
-  const int rmax2 = rmax > d.rv ? rmax : d.rv;
-  const uint32_t adp_bytes = (uint32_t)(d.adp_rows * rmax2) + 16u + (uint32_t)((d.adp_rows * rmax2 >> l0.w1.lg) + 4) * 8u;
-  slot = slot > adp_bytes ? slot : adp_bytes;
-  slot = (slot + 127u) & ~127u;
-  a.slot_bytes = slot;
-  uint32_t off = (uint32_t)a.nst * slot;
-  a.o_bars = off;            off += 128;
-  a.o_part = off;            off += 2 * 512 * 4;
-  a.o_x = off;               off += (uint32_t)d.C * 4;
-  a.o_ln = off;              off += (uint32_t)d.C * 4;
-  a.o_wkv = off;
-  const uint32_t wkv_bytes = (uint32_t)(4096 + ((d.rtot + 3) & ~3) + 256 + 7 * 64) * 4 + (uint32_t)d.rtot * 8 +
-                             (uint32_t)d.rtot * 64;
-  a.o_xb = off;
-  a.o_ln2 = off + (uint32_t)d.C * 4;
-  const uint32_t wk = wkv_bytes > 2u * d.C * 4 ? wkv_bytes : 2u * d.C * 4;
-  off += (wk + 127u) & ~127u;
-  a.o_misc = off;            off += 1024 * 4;
+  a.fg = lg >= 7 ? 128 : 64;
+  e->lfk = a.fg == 128 ? 2 : 1;
+  a.code_b = 16u * (uint32_t)a.kc;
+  a.pair_b = 16u * (uint32_t)a.pr * 8u;
+  const int ranks[4] = {d.rw, d.ra, d.rg, d.rv};
+  const LayerDev& lr = e->layers[d.L > 1 ? 1 : 0];
+  const PackedView* w2s[4] = {&lr.w2, &lr.a2, &lr.g2, &lr.v2};
+  int rmax = 0;
+  for (int m = 0; m < 4; ++m) {
+    a.abr[m] = ranks[m] < 256 ? (ranks[m] > 0 ? ranks[m] : 1) : 256;
+    a.alg[m] = w2s[m]->lg;
+    rmax = ranks[m] > rmax ? ranks[m] : rmax;
+  }
+  if (rmax > kDMisc - 256) return false;
+  // slot: one GEMV unit, one adapter first-stage item, one adapter second-stage piece
+  uint32_t slot = a.code_b + a.pair_b;
+  const uint32_t item = (uint32_t)(d.adp_rows * rmax + 15) / 16 * 16 + (uint32_t)((d.adp_rows * rmax >> 4) + 4) * 8u;
+  slot = slot > item ? slot : item;
+  for (int m = 0; m < 4; ++m) slot = slot > (uint32_t)a.abr[m] * 80u ? slot : (uint32_t)a.abr[m] * 80u;
+  a.slot = (slot + 1023u) / 1024u * 1024u;
+  auto set_bytes = [&](int K) { return ((uint32_t)K * 3u + 2u * (uint32_t)(K / a.fg) * 4u + 15u) & ~15u; };
+  a.dig_set = set_bytes(d.C);
+  uint32_t dig = 3u * a.dig_set;
+  dig = dig > set_bytes(d.F) ? dig : set_bytes(d.F);
+  const uint32_t wkv = (uint32_t)(4096 + ((d.rtot + 3) & ~3) + 256 + 7 * 64) * 4u;
+  dig = dig > wkv ? dig : wkv;
+  dig = (dig + 127u) & ~127u;
+  const uint32_t vec = ((uint32_t)d.C * 4u + 127u) & ~127u;
+  const uint32_t rest = dig + 4u * vec + 2u * kDW * 16u * 4u + (uint32_t)kDMisc * 4u;
+  const uint32_t budget = 227u * 1024u - 1024u - 3u * 1024u;  // dynamic-smem alignment slack, static shared
+  int nst = kDMaxSt;
+  while (nst > 3 && (uint32_t)nst * a.slot + rest > budget) --nst;
+  if ((uint32_t)nst * a.slot + rest > budget) return false;
+  a.nst = nst;
+  uint32_t off = (uint32_t)nst * a.slot;
+  a.o_dig = off;  off += dig;
+  a.o_x = off;    off += vec;
+  a.o_xb = off;   off += vec;
+  a.o_t = off;    off += vec;
+  a.o_p = off;    off += vec;
+  a.o_part = off; off += 2u * kDW * 16u * 4u;
+  a.o_misc = off; off += (uint32_t)kDMisc * 4u;
   a.smem_total = off;
-  if (off + 16 * 1024 > 227 * 1024) return false;  // static shared memory of the kernel included
+  // tensor maps
+  std::vector<DLayerMaps> hm((size_t)d.L);
+  memset(hm.data(), 0, sizeof(DLayerMaps) * hm.size());
+  CUtensorMap hh[2];
+  for (int i = 0; i < d.L; ++i) {
+    const LayerDev& l = e->layers[i];
+    const PackedView* big[6] = {&l.r, &l.k, &l.v, &l.o, &l.fk, &l.fv};
+    for (int m = 0; m < 6; ++m)
+      if (encode_big(*big[m], a, &hm[i].q[m], &hm[i].p[m]) != RWKVB_OK) return false;
+    const PackedView* w2[4] = {&l.w2, &l.a2, &l.g2, &l.v2};
+    for (int m = 0; m < (i > 0 ? 4 : 3); ++m)
+      if (encode_adp2(*w2[m], a.abr[m], &hm[i].aq[m], &hm[i].ap[m]) != RWKVB_OK) return false;
+  }
+  if (encode_big(e->head, a, &hh[0], &hh[1]) != RWKVB_OK) return false;
+  if (cudaMalloc((void**)&e->dmaps, sizeof(DLayerMaps) * (size_t)d.L) != cudaSuccess ||
+      cudaMalloc((void**)&e->dhead, sizeof(CUtensorMap) * 2) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (cudaMemcpy(e->dmaps, hm.data(), sizeof(DLayerMaps) * (size_t)d.L, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(e->dhead, hh, sizeof(hh), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
   a.layers = e->dlayers;
+  a.lmaps = e->dmaps;
+  a.head_maps = e->dhead;
   a.emb = e->emb;
-  a.head = e->head;
   a.ln0_w = e->ln0_w; a.ln0_b = e->ln0_b; a.lnout_w = e->lnout_w; a.lnout_b = e->lnout_b;
   a.b = e->b;
   a.d = d;
   a.spin_limit = 1u << 22;
+  a.pf_dist = (e->flags & 0x100u) ? e->pf_dist * 4 : 0;  // L2 prefetch stages (explicit: 4 x the flag's distance)
   const PackedView& E = e->emb;
   a.emb_fast = E.kind == RWKVB_KIND_SG8 && E.lg >= 4 && d.C % (int)E.group == 0 && ((d.C >> E.lg) % 2) == 0 &&
                aligned16(E.payload) && aligned16(E.meta);
-  e->pcpl = cpl;
+  e->dsmem = (size_t)a.smem_total + 1024;
   return true;
 }
 
-const void* persistent_fn(int cpl) {
-  switch (cpl) {
-    case 1: return (const void*)persistent_kernel<1>;
-    case 2: return (const void*)persistent_kernel<2>;
-    case 3: return (const void*)persistent_kernel<3>;
-    default: return (const void*)persistent_kernel<4>;
-  }
+const void* decode_fn(int lfk) {
+  return lfk == 2 ? (const void*)decode_kernel<2> : (const void*)decode_kernel<1>;
 }
 
 int launch_persistent(rwkvb_engine* e, int ntok, int mode, int first_tok, const int* forced, cudaStream_t s) {
-  PArgs a = e->pa;
+  DArgs a = e->da;
   a.ntok = ntok;
   a.mode = mode;
   a.first_tok = first_tok;
@@ -964,7 +1005,7 @@ int launch_persistent(rwkvb_engine* e, int ntok, int mode, int first_tok, const 
   cudaError_t err = cudaMemsetAsync(a.gbar, 0, sizeof(unsigned), s);
   if (err != cudaSuccess) return cuda_status(err);
   void* args[] = {&a};
-  err = cudaLaunchCooperativeKernel(persistent_fn(e->pcpl), dim3(e->sms), dim3(kPThreads), args, a.smem_total, s);
+  err = cudaLaunchCooperativeKernel(decode_fn(e->lfk), dim3(e->sms), dim3(kDThreads), args, e->dsmem, s);
   return cuda_status(err);
 }
 }  // namespace
@@ -1024,9 +1065,9 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   const size_t H = d.H;
   size_t fl[] = {(size_t)L * C, (size_t)L * H * 4096, (size_t)L * C, (size_t)C, (size_t)C, (size_t)C, (size_t)C,
                  (size_t)3 * C, (size_t)d.adp_splits * d.rtot, (size_t)C, (size_t)F, (size_t)C, (size_t)V,
-                 (size_t)e->head_grid * 2 + 8};
-  size_t total = 0, offs[16];
-  for (int i = 0; i < 14; ++i) {
+                 (size_t)e->head_grid * 2 + 8, (size_t)C, (size_t)C, (size_t)d.rtot * 2};
+  size_t total = 0, offs[20];
+  for (int i = 0; i < 17; ++i) {
     offs[i] = total;
     total += ((fl[i] * 4 + 255) / 256) * 256;
   }
@@ -1046,6 +1087,9 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   float** fb[] = {&e->b.att_x, &e->b.wkv, &e->b.ffn_x, &e->b.xa, &e->b.xb, &e->b.xln1, &e->b.xln2,
                   &e->b.rkv, &e->b.adp, &e->b.att_y, &e->b.h, &e->b.v_first, &e->b.logits, &e->b.amax_v};
   for (int i = 0; i < 14; ++i) *fb[i] = (float*)(base + offs[i]);
+  e->b.ao = (float*)(base + offs[14]);
+  e->b.fo = (float*)(base + offs[15]);
+  e->b.adp64 = (unsigned long long*)(base + offs[16]);
   e->b.amax_i = (int*)(base + ints_off);
   e->b.ticket = (unsigned*)(base + misc_off);
   e->b.tok = (int*)(base + misc_off + 16);
@@ -1093,11 +1137,11 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
       st = RWKVB_EALLOC;
     }
   }
-  if (st == RWKVB_OK && !(flags & 0x4u) && plan_persistent(e)) {
-    const void* fn = persistent_fn(e->pcpl);
+  if (st == RWKVB_OK && !(flags & 0x4u) && plan_decode(e)) {
+    const void* fn = decode_fn(e->lfk);
     int per_sm = 0;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->pa.smem_total) == cudaSuccess &&
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kPThreads, e->pa.smem_total) == cudaSuccess &&
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->dsmem) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDThreads, e->dsmem) == cudaSuccess &&
         per_sm >= 1) {
       e->persistent = true;
     }
@@ -1124,6 +1168,8 @@ extern "C" int rwkvb_engine_destroy(rwkvb_engine* e) {
   if (e->cap) cudaStreamDestroy(e->cap);
   if (e->arena) cudaFree(e->arena);
   if (e->dlayers) cudaFree(e->dlayers);
+  if (e->dmaps) cudaFree(e->dmaps);
+  if (e->dhead) cudaFree(e->dhead);
   if (e->dtokens) cudaFree(e->dtokens);
   if (e->dtrace) cudaFree(e->dtrace);
   delete e;

@@ -1,0 +1,199 @@
+// SG8 dot products on the integer tensor cores (mma.sync m16n8k32, u8 x s8 -> s32).
+//
+// A (16 rows x 32 k) is the raw u8 weight codes: no conversion at all.
+// B (32 k x 8 columns) carries the activation as three signed 8-bit digits in
+// columns 0..2 (columns 3..7 are zero): per flush group f of FG columns
+// (FG = min(group, 128)) the input is scaled by 2^-e_f (e_f = exponent of the
+// group's largest |x|, so |x| 2^-e_f < 1) and written
+//     x = c_f (X0 + X1/254 + X2/254^2),   c_f = 2^e_f / 127,   X0, X1, X2 in [-127, 127]
+// (reconstruction error <= c_f / 2 / 254^2, i.e. below 6.2e-8 of the group's
+// largest |x|).  The three integer sums D_n = sum q X_n are exact, and per
+// flush group (weights (min, max), d = (max - min) / 255)
+//     sum_k w_k x_k = min * sum_k x_k + d * c_f * (D0 + D1/254 + D2/254^2)
+// which is the per-group algebra of the reference's SG8 row dot
+// (rwkv_ssd/native/lut2_gather.c:344-381).
+//
+// k order inside one 32-wide k-step: lane (g, t) of a quad group reads the 8
+// contiguous code bytes [8t, 8t+8) of its rows and feeds them as logical k
+// {4t..4t+3} (register a0/a1) and {16+4t..16+4t+3} (a2/a3).  The B fragment of
+// lane (n, t) is digit n of x[8t .. 8t+8) in the same order, so the product is
+// the plain dot product; only the pairing inside the k-step is permuted.
+#pragma once
+
+#include "common.cuh"
+
+namespace rwkvb {
+
+constexpr float kInv254 = 1.0f / 254.0f;
+constexpr float kInv254sq = 1.0f / 64516.0f;
+
+__device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Named barrier over the `n` consumer threads (barrier 0 is __syncthreads).
+__device__ __forceinline__ void bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) | ((uint32_t)(c & 0xff) << 16) | ((uint32_t)d << 24);
+}
+
+// Digit form of one input vector.
+//   xd[s*12 + n*4 + t] (uint2) = digit n of x[32s + 8t .. +8)   (k-step s, n < 3, t < 4)
+//   xc[f] = 2^e_f / 127,  xsum[f] = sum of x over flush group f (FG columns)
+struct XDigits {
+  uint2* xd;
+  float* xc;
+  float* xsum;
+};
+
+// Build the digit form of x[0..K): item it = (k-step it / 4, quarter it % 4)
+// covers x[8 it .. 8 it + 8); thread ct of the `nthreads` consumers takes
+// items ct, ct + nthreads, ... (at most 8 passes), issuing every pass's loads
+// (get4(i) = x[i..i+4), i % 4 == 0) before any arithmetic.  The flush-group
+// maximum and sum (FG = 32 << lfk columns = 4 << lfk items, on adjacent
+// lanes) are reduced with shuffles.  K % FG == 0, K / 8 <= 8 * nthreads,
+// nthreads % 32 == 0.  Ends with the consumer barrier `bar_id`.
+template <class Get4>
+__device__ __forceinline__ void build_digits(int K, int lfk, Get4 get4, XDigits X, int ct, int nthreads, int bar_id) {
+  const int items = K >> 3, gl = 4 << lfk;
+  const int npass = (items + nthreads - 1) / nthreads;
+  float4 va[8], vb[8];
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    const int it = p * nthreads + ct;
+    va[p] = vb[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p < npass && it < items) {
+      va[p] = get4(it * 8);
+      vb[p] = get4(it * 8 + 4);
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    if (p < npass) {
+      const int it = p * nthreads + ct;
+      const float v[8] = {va[p].x, va[p].y, va[p].z, va[p].w, vb[p].x, vb[p].y, vb[p].z, vb[p].w};
+      float m = 0.f, sum = 0.f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        m = fmaxf(m, fabsf(v[u]));
+        sum += v[u];
+      }
+      for (int o = 1; o < gl; o <<= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      }
+      if (it < items) {
+        int e = 0;
+        if (m > 0.f) frexpf(m, &e);  // m = frac * 2^e, frac in [0.5, 1): |x| * 2^-e < 1
+        const float inv = ldexpf(127.0f, -e);  // exact
+        if ((ct & (gl - 1)) == 0) {
+          X.xc[it >> (lfk + 2)] = ldexpf(1.0f, e) / 127.0f;
+          X.xsum[it >> (lfk + 2)] = sum;
+        }
+        int d0[8], d1[8], d2[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float y0 = v[u] * inv;
+          const float x0 = rintf(y0);
+          const float y1 = (y0 - x0) * 254.0f;
+          const float x1 = rintf(y1);
+          const float x2 = rintf((y1 - x1) * 254.0f);
+          d0[u] = (int)x0;
+          d1[u] = (int)x1;
+          d2[u] = (int)x2;
+        }
+        const int s = it >> 2, t = it & 3;
+        X.xd[s * 12 + t] = make_uint2(pack_s8x4(d0[0], d0[1], d0[2], d0[3]), pack_s8x4(d0[4], d0[5], d0[6], d0[7]));
+        X.xd[s * 12 + 4 + t] =
+            make_uint2(pack_s8x4(d1[0], d1[1], d1[2], d1[3]), pack_s8x4(d1[4], d1[5], d1[6], d1[7]));
+        X.xd[s * 12 + 8 + t] =
+            make_uint2(pack_s8x4(d2[0], d2[1], d2[2], d2[3]), pack_s8x4(d2[4], d2[5], d2[6], d2[7]));
+      }
+    }
+  }
+  bar_sync(bar_id, nthreads);
+}
+
+// A-operand row g of the mma is tile row 2 (g & 3) + (g >> 2) (and g + 8 ->
+// 8 + that): with the 128-byte swizzle (tma.cuh: chunk c of row r stored at
+// c ^ (r & 7)) each half-warp's 8-byte loads then hit 8 distinct 16-byte
+// chunks.  acc0 / acc1 of lane (g, t) belong to tile rows imma_tile_row(g) and
+// imma_tile_row(g) + 8.
+__device__ __forceinline__ int imma_tile_row(int g) { return 2 * (g & 3) + (g >> 2); }
+
+// Per-lane constants of the swizzled A loads.
+struct ImmaLane {
+  int ra;          // tile row of acc0 (acc1: ra + 8)
+  uint32_t roff;   // ra * 128 + 8 * (t & 1)
+  uint32_t c[4];   // chunk offset of k-step j of a 128-column block
+};
+
+__device__ __forceinline__ ImmaLane imma_lane() {
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  ImmaLane L;
+  L.ra = imma_tile_row(g);
+  L.roff = (uint32_t)(L.ra * 128 + 8 * (t & 1));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) L.c[j] = (uint32_t)(((2 * j + (t >> 1)) ^ (L.ra & 7)) << 4);
+  return L;
+}
+
+// One warp: 16 rows x one 128-column block of a swizzled tile.
+//   blk:    tile + block * 2048 (the block's 16 lines)
+//   pa, pb: (min, max) pairs of rows ra and ra + 8 for the block's first flush
+//           group; flush group f uses pa[f] (a flush group never spans two
+//           weight groups: FG = min(group, 128))
+//   ks:     whole-row k-step index of the block's first k-step
+// LFK = log2(flush group in k-steps): 2 for 128-column groups, 1 for 64.
+// Only lanes with t < 2 carry values (t == 0: min terms and digits 0, 1;
+// t == 1: digit 2); sum lanes t = 0 and 1 for the row totals.
+template <int LFK>
+__device__ __forceinline__ void imma_block(const uint8_t* blk, const float2* pa, const float2* pb, int ks,
+                                           const XDigits& X, const ImmaLane& L, float& acc0, float& acc1) {
+  const int lane = threadIdx.x & 31, t = lane & 3;
+  const uint8_t* base = blk + L.roff;
+  const uint2* xb = X.xd + ks * 12 + lane;
+  uint2 w0[4], w1[4], bb[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    w0[j] = *reinterpret_cast<const uint2*>(base + L.c[j]);
+    w1[j] = *reinterpret_cast<const uint2*>(base + L.c[j] + 1024);
+    bb[j] = lane < 12 ? xb[j * 12] : make_uint2(0u, 0u);
+  }
+  constexpr int KPF = 1 << LFK, NF = 4 >> LFK;
+#pragma unroll
+  for (int f = 0; f < NF; ++f) {
+    int d[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = f * KPF; j < (f + 1) * KPF; ++j) imma_16832(d, w0[j].x, w1[j].x, w0[j].y, w1[j].y, bb[j].x, bb[j].y);
+    if (t < 2) {
+      const int fg = (ks >> LFK) + f;
+      const float c = X.xc[fg];
+      const float2 p0 = pa[f], p1 = pb[f];
+      const float da = (p0.y - p0.x) * kInv255 * c, db = (p1.y - p1.x) * kInv255 * c;
+      if (t == 0) {
+        const float xs = X.xsum[fg];
+        acc0 = fmaf(da, fmaf((float)d[1], kInv254, (float)d[0]), fmaf(p0.x, xs, acc0));
+        acc1 = fmaf(db, fmaf((float)d[3], kInv254, (float)d[2]), fmaf(p1.x, xs, acc1));
+      } else {
+        acc0 = fmaf(da * kInv254sq, (float)d[0], acc0);
+        acc1 = fmaf(db * kInv254sq, (float)d[2], acc1);
+      }
+    }
+  }
+}
+
+}  // namespace rwkvb

@@ -1,7 +1,10 @@
 // Host-side helpers shared by the library's translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
+
+#include <cstdint>
 
 #include "rwkv_b200.h"
 
@@ -20,5 +23,11 @@ inline int cuda_status(cudaError_t e) {
 
 // Raise a kernel's dynamic shared-memory limit to kMaxSmem once per device.
 int allow_big_smem(const void* kernel);
+
+// Tiled TMA tensor map over a u8 array (dims innermost first, strides in bytes
+// for dims 1..rank-1), no interleave, optional 128-byte swizzle, zero OOB fill.
+// The driver entry point is resolved through the runtime (no libcuda link).
+int encode_u8_map(CUtensorMap* out, int rank, const void* addr, const uint64_t* dims, const uint64_t* strides,
+                  const uint32_t* box, bool swizzle128);
 
 }  // namespace rwkvb

@@ -129,6 +129,8 @@ class B200Engine:
             n = ctypes.c_int32()
             native.check(self.lib.rwkvb_engine_launches_per_step(h, ctypes.byref(n)), "launches_per_step")
             self.launches_per_step = int(n.value)
+            # 0: the whole decode loop runs as one persistent launch
+            self.persistent_active = self.launches_per_step == 0
 
     # ------------------------------------------------------------ lifecycle
     def close(self) -> None:

@@ -164,6 +164,8 @@ def test_engine_decode_matches_reference_forward(policy, path):
     gold, shape, pack = _reference_pack(policy)
     eng = B200Engine(pack, use_graph=path != "nograph", persistent=path == "persistent")
     try:
+        # SG8 packs run the persistent kernel when asked; LUT2 packs always use the graph path
+        assert eng.persistent_active == (path == "persistent" and policy == "sg8")
         prompt = [int(t) for t in gold["prompt"]]
         ids, logits = eng.greedy(prompt, len(gold["ids"]), keep_logits=True)
         assert ids == [int(t) for t in gold["ids"]]
@@ -234,6 +236,7 @@ def test_engine_0p1b_shape_matches_oracle_first_tokens(persistent):
     ids_ref, logits_ref, state_ref = model.greedy(prompt, 3)
     eng = B200Engine(pack, persistent=persistent)
     try:
+        assert eng.persistent_active == persistent
         ids, logits = eng.greedy(prompt, 3, keep_logits=True)
         assert ids == ids_ref
         np.testing.assert_allclose(_np(logits), logits_ref, rtol=0, atol=LOGIT_TOL)
