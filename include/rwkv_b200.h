@@ -223,12 +223,18 @@ int rwkvb_engine_decode_greedy(rwkvb_engine* e, int32_t first_token, int32_t n_t
 int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first_token, int32_t n_tokens,
                                      int32_t* out_tokens_dev, void* stream);
 
-/* Phase timestamps (ns, %globaltimer) of the last persistent launch, recorded
- * when the engine was created with flag bit 3: [2][65536] (first CTA, last CTA),
- * per token: token start, then per layer A start, A done, B barrier, B done,
- * C barrier, C done, D barrier, D done, E barrier, E done; then head barrier,
- * head done.  The GPU counterpart of the reference's per-layer LayerTiming rows
- * (runtime/metrics.py:26-58).  Copies min(cap, 131072) values to host `out`. */
+/* Timestamps (ns, %globaltimer) of the last persistent launch, recorded when
+ * the engine was created with flag bit 3; copies min(cap, 262144) values to
+ * host `out`:
+ *   [0, 131072): phase marks, [2][65536] (first CTA, last CTA): per token the
+ *     token start, per layer 22 marks (A start, ln1, shift state, r/k/v digits,
+ *     A units, A items, B barrier, B done, C barrier, C prep, C units, D
+ *     barrier, D loads, ln2, D prep, D units, E barrier, E slices, E prep,
+ *     E units), then head barrier, head prep, head units;
+ *   [131072, 262144): ring events of the first CTA, 3 per stage s (s < 43690):
+ *     producer issue, consumer wait end, consumer release.
+ * The GPU counterpart of the reference's per-layer LayerTiming rows
+ * (runtime/metrics.py:26-58). */
 int rwkvb_engine_trace(rwkvb_engine* e, uint64_t* out, int32_t cap, int32_t* n_out);
 
 /* Kernel launches per token step (for launch accounting). */

@@ -95,7 +95,7 @@ struct DArgs {
   Dims d;
   int nb, kc, pr;    // 128-column blocks per chunk, chunk columns, pairs per chunk row
   int lg, fg;        // log2 group of the big matrices, flush group columns
-  int nst, pf_dist;  // ring slots, L2 prefetch distance in stages
+  int nst;  // ring slots
   uint32_t slot, code_b, pair_b;
   int abr[4];  // adapter second stage: box rows per matrix
   int alg[4];  // adapter second stage: log2 group
@@ -119,9 +119,10 @@ struct DTable {
   int zc0, zc1, zf0, zf1, z3c0, z3c1, zv0, zv1, zr0, zr1;  // zeroing slices (C, F, 3C, V, rtot)
 };
 
-__device__ __forceinline__ void d_split(int n, int parts, int i, int* a, int* b) {
-  *a = (int)((long long)n * i / parts);
-  *b = (int)((long long)n * (i + 1) / parts);
+// [a, b) = part i of [0, n) split into `parts` (n * parts < 2^32).
+__device__ __noinline__ void d_split(int n, int parts, int i, int* a, int* b) {
+  *a = (int)((unsigned)n * (unsigned)i / (unsigned)parts);
+  *b = (int)((unsigned)n * (unsigned)(i + 1) / (unsigned)parts);
 }
 
 __device__ __forceinline__ void d_range(int tiles, int nch, int G, int b, DRange& R) {
@@ -181,153 +182,180 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
 }
 
 // ------------------------------------------------------------- producer
-// The stage sequence of one CTA, exactly as the consumers consume it: per
-// token, per layer [r/k/v units, adapter items, adapter-2 pieces, o units,
-// ffn key units, ffn value units], then the head units (every token in greedy
-// mode, the last one in forced mode).
-struct DWalk {
-  int tok, l, ph, i;  // ph: 0 r/k/v, 1 items, 2 pieces, 3 o, 4 ffn key, 5 ffn value, 6 head
-};
-
-__device__ __forceinline__ int d_phase_len(const DArgs& a, const DTable& T, const DWalk& w) {
-  switch (w.ph) {
-    case 0: return T.r[0].u1 - T.r[0].u0;
-    case 1: return T.nitem[w.l == 0 ? 0 : 1];
-    case 2: return T.npc[w.l == 0 ? 0 : 1];
-    case 3: return T.r[1].u1 - T.r[1].u0;
-    case 4: return T.r[2].u1 - T.r[2].u0;
-    case 5: return T.r[3].u1 - T.r[3].u0;
-    default: return (a.mode == 0 || w.tok == a.ntok - 1) ? T.r[4].u1 - T.r[4].u0 : 0;
-  }
+// Bring layer l's small operands into L2: its fp32 vectors, this layer's rows
+// of the token-shift state and (head CTAs) this CTA's WKV state.  They are
+// read after the weight stream has evicted them, on the latency-bound path
+// between phases.
+__device__ void d_prefetch_layer(const DArgs& a, int l) {
+  const LayerDev& Ly = a.layers[l];
+  const uint32_t vb = (uint32_t)a.d.C * 4u;
+  const float* vecs[19] = {Ly.ln1_w, Ly.ln1_b, Ly.ln2_w, Ly.ln2_b, Ly.x_r, Ly.x_w, Ly.x_k, Ly.x_v, Ly.x_a, Ly.x_g,
+                           Ly.w0,    Ly.a0,    Ly.v0,    Ly.k_k,   Ly.k_a, Ly.r_k, Ly.lnx_w, Ly.lnx_b, Ly.ffn_x_k};
+  for (int i = 0; i < 19; ++i)
+    if (vecs[i] && (i != 12 || l > 0)) prefetch_l2_bulk(vecs[i], vb);
+  prefetch_l2_bulk(a.b.att_x + (size_t)l * a.d.C, vb);
+  prefetch_l2_bulk(a.b.ffn_x + (size_t)l * a.d.C, vb);
+  if ((int)blockIdx.x < a.d.H) prefetch_l2_bulk(a.b.wkv + ((size_t)l * a.d.H + blockIdx.x) * 4096, 16384u);
 }
 
-// Move `w` to the first stage at or after it; false at the end of the launch.
-__device__ __forceinline__ bool d_norm(const DArgs& a, const DTable& T, DWalk& w) {
-  while (w.tok < a.ntok) {
-    if (w.i < d_phase_len(a, T, w)) return true;
-    w.i = 0;
-    if (w.ph < 5) {
-      ++w.ph;
-    } else if (w.ph == 5) {
-      if (w.l + 1 < a.d.L) {
-        ++w.l;
-        w.ph = 0;
-      } else {
-        w.ph = 6;
+__device__ __forceinline__ void d_prefetch_map(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+
+// Producer: the ring slot of stage `seq` once it is free; -1 when the launch
+// is aborting (another wait gave up) or this wait gave up.
+__device__ __noinline__ int d_acquire(const DArgs& a, uint64_t* empty, volatile int* abort_flag, int seq) {
+  const int slot = seq % a.nst;
+  if (seq >= a.nst) {
+    const uint32_t par = (uint32_t)((seq / a.nst - 1) & 1);
+    uint32_t i = 0;
+    while (!mbar_try_wait(&empty[slot], par)) {
+      if (*abort_flag) return -1;
+      if (++i > a.spin_limit) {
+        atomicOr(a.b.err, kErrTimeout);
+        *abort_flag = 1;
+        return -1;
       }
-    } else {
-      ++w.tok;
-      w.l = 0;
-      w.ph = 0;
     }
   }
-  return false;
+  return slot;
 }
 
-// Issue stage `w` into a slot (bar != nullptr: expect its bytes, then copy),
-// or only bring it into L2 (bar == nullptr).
-__device__ void d_stage(const DArgs& a, const DTable& T, const DWalk& w, uint8_t* dst, uint64_t* bar) {
-  const int C = a.d.C, bx = blockIdx.x;
-  if (w.ph == 1) {  // adapter first-stage item: rows [i0, i1) of W1 [C][R] and their pairs
-    const LayerDev& Ly = a.layers[w.l];
-    const int item = T.item[w.i];
-    const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
-    const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
-    const int R = W.cols;
-    const int i0 = sp * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows);
-    const uint32_t qb = (uint32_t)((i1 - i0) * R);
-    const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg) & ~1u;
-    const uint32_t g1 = ((uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) + 1) + 1u) & ~1u;
-    const uint32_t sb = (g1 - g0) * 8u;
-    if (bar) {
-      mbar_expect_tx(bar, qb + sb);
-      bulk_g2s(dst, W.payload + (size_t)i0 * R, qb, bar);
-      bulk_g2s(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, bar);
-    } else {
-      prefetch_l2_bulk(W.payload + (size_t)i0 * R, qb);
-      prefetch_l2_bulk(W.meta + (size_t)g0 * 8, sb);
-    }
-    return;
-  }
-  if (w.ph == 2) {  // adapter second-stage piece of this CTA's head
-    const DLayerMaps& M = a.lmaps[w.l];
-    const int m = T.pm[w.i], br = a.abr[m], r0 = T.pr0[w.i];
-    const int px = (((bx * 64) >> a.alg[m]) & ~1) * 8;
-    if (bar) {
-      mbar_expect_tx(bar, (uint32_t)br * 80u);
-      tma_load_2d(dst, &M.aq[m], bx * 64, r0, bar);
-      tma_load_2d(dst + br * 64, &M.ap[m], px, r0, bar);
-    } else {
-      tma_prefetch_2d(&M.aq[m], bx * 64, r0);
-      tma_prefetch_2d(&M.ap[m], px, r0);
-    }
-    return;
-  }
-  // GEMV unit: 16 rows x one chunk
-  const DRange& R = T.r[w.ph == 0 ? 0 : (w.ph == 6 ? 4 : w.ph - 2)];
-  const int u = R.u0 + w.i;
-  const int tile = u / R.nch, chunk = u - tile * R.nch;
-  const CUtensorMap* q;
-  const CUtensorMap* p;
-  int row0;
-  if (w.ph == 6) {
-    q = a.head_maps;
-    p = q + 1;
-    row0 = tile * 16;
-  } else {
-    const DLayerMaps& M = a.lmaps[w.l];
-    const int ct = C / 16;
-    const int m = w.ph == 0 ? tile / ct : w.ph;  // phases 3, 4, 5 are matrices o, ffn key, ffn value
-    q = &M.q[m];
-    p = &M.p[m];
-    row0 = (w.ph == 0 ? tile - (tile / ct) * ct : tile) * 16;
-  }
-  if (bar) {
-    mbar_expect_tx(bar, a.code_b + a.pair_b);
-    tma_load_3d(dst, q, 0, row0, chunk * a.nb, bar);
-    tma_load_2d(dst + a.code_b, p, chunk * a.pr * 8, row0, bar);
-  } else {
-    tma_prefetch_3d(q, 0, row0, chunk * a.nb);
-    tma_prefetch_2d(p, chunk * a.pr * 8, row0);
-  }
+__device__ __forceinline__ void d_issued(const DArgs& a, int& seq) {
+  if (a.trace && blockIdx.x == 0 && 3 * seq + 2 < 2 * a.trace_cap) a.trace[2 * (size_t)a.trace_cap + 3 * seq] = global_ns();
+  ++seq;
 }
 
-// Lane 0 of the producer warp: fill the ring in sequence order, gated by the
-// slots' empty barriers, and keep an L2 prefetch cursor `pf_dist` stages ahead.
-__device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                           volatile int* abort_flag) {
-  int seq = 0, pseq = 0;
-  DWalk w{0, 0, 0, 0}, pf{0, 0, 0, 0};
-  bool have = d_norm(a, T, w), pf_have = d_norm(a, T, pf);
-  while (have) {
-    const int slot = seq % a.nst;
-    if (seq >= a.nst) {
-      const uint32_t par = (uint32_t)((seq / a.nst - 1) & 1);
+// Producer: GEMV units [R.u0, R.u1); per_map > 0: tile t uses map t / per_map
+// (the r, k, v maps of phase A), row (t % per_map) * 16.  Every argument the
+// loop needs is copied to registers first (the loop stores to shared memory,
+// so reads through `a` would be repeated each iteration).
+__device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, const CUtensorMap* q, const CUtensorMap* p,
+                                           int per_map, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                                           volatile int* abort_flag, int& seq_io) {
+  const int nst = a.nst, nb = a.nb, pr8 = a.pr * 8, u0 = R.u0, u1 = R.u1, nch = R.nch;
+  const uint32_t slot_b = a.slot, code_b = a.code_b, bytes = a.code_b + a.pair_b, limit = a.spin_limit;
+  unsigned long long* tr = (a.trace && blockIdx.x == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
+  const int tr_n = 2 * a.trace_cap;
+  int seq = seq_io;
+  int tile = u0 / nch, chunk = u0 - tile * nch;
+  int mi = per_map ? tile / per_map : 0, row0 = (tile - mi * per_map) * 16;
+  bool ok = true;
+#pragma unroll 1
+  for (int u = u0; u < u1; ++u) {
+    const int slot = seq % nst;
+    if (seq >= nst) {
+      const uint32_t par = (uint32_t)((seq / nst - 1) & 1);
       uint32_t i = 0;
-      bool ok = true;
       while (!mbar_try_wait(&empty[slot], par)) {
-        if (*abort_flag) {
-          ok = false;
-          break;
-        }
-        if (++i > a.spin_limit) {
-          atomicOr(a.b.err, kErrTimeout);
-          *abort_flag = 1;
+        if (*abort_flag || ++i > limit) {
+          if (!*abort_flag) {
+            atomicOr(a.b.err, kErrTimeout);
+            *abort_flag = 1;
+          }
           ok = false;
           break;
         }
       }
       if (!ok) break;
     }
-    d_stage(a, T, w, ring + (size_t)slot * a.slot, &full[slot]);
+    uint8_t* dst = ring + (size_t)slot * slot_b;
+    mbar_expect_tx(&full[slot], bytes);
+    tma_load_3d(dst, q + mi, 0, row0, chunk * nb, &full[slot]);
+    tma_load_2d(dst + code_b, p + mi, chunk * pr8, row0, &full[slot]);
+    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq] = global_ns();
     ++seq;
-    ++w.i;
-    have = d_norm(a, T, w);
-    while (pf_have && pseq < seq + a.pf_dist) {
-      if (pseq >= seq) d_stage(a, T, pf, nullptr, nullptr);
-      ++pseq;
-      ++pf.i;
-      pf_have = d_norm(a, T, pf);
+    if (++chunk == nch) {
+      chunk = 0;
+      row0 += 16;
+      if (per_map && row0 == per_map * 16) {
+        row0 = 0;
+        ++mi;
+      }
+    }
+  }
+  seq_io = seq;
+  return ok;
+}
+
+// Lane 0 of the producer warp: fill the ring in the consumers' order (per
+// token, per layer: r/k/v units, adapter items, adapter-2 pieces, o units,
+// ffn key units, ffn value units; then the head units), gated by the slots'
+// empty barriers.  When it starts a layer it prefetches the next layer's small
+// operands and this layer's tensor maps.
+__device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                           volatile int* abort_flag) {
+  int seq = 0;
+  auto acquire = [&]() -> int { return d_acquire(a, empty, abort_flag, seq); };
+  auto issued = [&]() { d_issued(a, seq); };
+  auto layer_start = [&](int l) {
+    const DLayerMaps& M = a.lmaps[l];
+    for (int m = 0; m < 6; ++m) {
+      d_prefetch_map(&M.q[m]);
+      d_prefetch_map(&M.p[m]);
+    }
+    if ((int)blockIdx.x < a.d.H)
+      for (int m = 0; m < 4; ++m) {
+        d_prefetch_map(&M.aq[m]);
+        d_prefetch_map(&M.ap[m]);
+      }
+    d_prefetch_layer(a, l + 1 < a.d.L ? l + 1 : 0);
+  };
+  d_prefetch_layer(a, 0);
+  {
+    const int C = a.d.C, ct = C / 16, bx = blockIdx.x;
+    bool ok = true;
+    auto units = [&](const DRange& R, const CUtensorMap* q, const CUtensorMap* p, int per_map) -> bool {
+      return d_issue_units(a, R, q, p, per_map, ring, full, empty, abort_flag, seq);
+    };
+    for (int tok = 0; tok < a.ntok && ok; ++tok) {
+      const bool head = a.mode == 0 || tok == a.ntok - 1;
+      for (int l = 0; l < a.d.L && ok; ++l) {
+        const DLayerMaps& M = a.lmaps[l];
+        const LayerDev& Ly = a.layers[l];
+        layer_start(l);
+        ok = units(T.r[0], M.q, M.p, ct);
+        for (int k = 0; ok && k < T.nitem[l == 0 ? 0 : 1]; ++k) {
+          const int item = T.item[k];
+          const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
+          const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
+          const int R = W.cols;
+          const int i0 = sp * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows);
+          const uint32_t qb = (uint32_t)((i1 - i0) * R);
+          const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg) & ~1u;
+          const uint32_t g1 = ((uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) + 1) + 1u) & ~1u;
+          const uint32_t sb = (g1 - g0) * 8u;
+          const int slot = acquire();
+          ok = slot >= 0;
+          if (ok) {
+            uint8_t* dst = ring + (size_t)slot * a.slot;
+            mbar_expect_tx(&full[slot], qb + sb);
+            bulk_g2s(dst, W.payload + (size_t)i0 * R, qb, &full[slot]);
+            bulk_g2s(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, &full[slot]);
+            issued();
+          }
+        }
+        for (int k = 0; ok && k < T.npc[l == 0 ? 0 : 1]; ++k) {
+          const int m = T.pm[k], br = a.abr[m];
+          const int slot = acquire();
+          ok = slot >= 0;
+          if (ok) {
+            uint8_t* dst = ring + (size_t)slot * a.slot;
+            mbar_expect_tx(&full[slot], (uint32_t)br * 80u);
+            tma_load_2d(dst, &M.aq[m], bx * 64, T.pr0[k], &full[slot]);
+            tma_load_2d(dst + br * 64, &M.ap[m], (((bx * 64) >> a.alg[m]) & ~1) * 8, T.pr0[k], &full[slot]);
+            issued();
+          }
+        }
+        if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0);
+        if (ok) ok = units(T.r[2], M.q + 4, M.p + 4, 0);
+        if (ok) ok = units(T.r[3], M.q + 5, M.p + 5, 0);
+      }
+      if (ok && head) {
+        d_prefetch_map(a.head_maps);
+        d_prefetch_map(a.head_maps + 1);
+        ok = units(T.r[4], a.head_maps, a.head_maps + 1, 0);
+      }
     }
   }
   // every issued copy has landed before the CTA may exit
@@ -335,9 +363,601 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
     mbar_wait_bounded(&full[s % a.nst], (uint32_t)((s / a.nst) & 1), 1u << 20);
 }
 
+// ------------------------------------------------------------ consumers
+// The consumer side is a set of non-inlined subroutines shared by all phases
+// (one digit builder, one GEMV unit loop, one LayerNorm, ...), so the code a
+// layer executes stays small enough to remain in the instruction caches while
+// the weight stream sweeps L2.
+
+// Consumer state shared by the subroutines.
+struct DCons {
+  uint8_t* sm;  // 1024-aligned dynamic shared memory (ring at offset 0)
+  uint64_t* full;
+  uint64_t* empty;
+  float* red;  // [32] reduction scratch
+  volatile int* abort;
+  int* flag;
+  int seq, pbuf, dead, tr, trow;
+  unsigned target;
+};
+
+__device__ __forceinline__ void d_csync() { bar_sync(kDBar, kDT); }
+
+__device__ __forceinline__ void d_mark(const DArgs& a, DCons& c) {
+  if (a.trace && c.trow >= 0 && threadIdx.x == 0 && c.tr < a.trace_cap)
+    a.trace[(size_t)c.trow * a.trace_cap + c.tr] = global_ns();
+  ++c.tr;
+}
+
+// Sum over the consumer threads (all of them get the result).
+__device__ __noinline__ float d_csum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  d_csync();
+  float r = 0.f;
+#pragma unroll
+  for (int w = 0; w < kDW; ++w) r += red[w];
+  d_csync();
+  return r;
+}
+
+// Grid barrier of the consumers; false (CTA-uniform) when it gave up or an
+// earlier wait of this CTA failed.
+__device__ __noinline__ bool d_gsync(const DArgs& a, DCons& c) {
+  d_csync();
+  c.target += gridDim.x;
+  if (threadIdx.x == 0) {
+    bool ok = !*c.abort;
+    if (ok) {
+      __threadfence();
+      atomicAdd(a.gbar, 1u);
+      ok = false;
+      for (uint32_t i = 0; i < a.spin_limit; ++i) {
+        if (d_ld_acquire(a.gbar) >= c.target) {
+          ok = true;
+          break;
+        }
+        __nanosleep(32);
+      }
+      if (!ok) {
+        atomicOr(a.b.err, kErrTimeout);
+        *c.abort = 1;
+      }
+    }
+    *c.flag = ok ? 0 : 1;
+  }
+  d_csync();
+  return *c.flag == 0;
+}
+
+__device__ __forceinline__ void d_zero(float* p, int i0, int i1) {
+  #pragma unroll 1
+  for (int i = i0 + (int)threadIdx.x; i < i1; i += kDT) p[i] = 0.f;
+}
+
+// dst = LayerNorm(src) over C (eps 1e-5, F.layer_norm); stat (optional) <- mean, rstd
+__device__ __noinline__ void d_layer_norm(float* dst, const float* src, const float* w, const float* bb, int C,
+                                          float* stat, float* red) {
+  const int t = threadIdx.x;
+  float s = 0.f;
+  #pragma unroll 1
+  for (int i = t; i < C; i += kDT) s += src[i];
+  const float mean = d_csum(s, red) / (float)C;
+  float q = 0.f;
+  #pragma unroll 1
+  for (int i = t; i < C; i += kDT) {
+    const float dv = src[i] - mean;
+    q += dv * dv;
+  }
+  const float rstd = rsqrtf(d_csum(q, red) / (float)C + 1e-5f);
+  #pragma unroll 1
+  for (int i = t; i < C; i += kDT) dst[i] = ln_val(src[i], mean, rstd, __ldg(w + i), __ldg(bb + i));
+  if (stat && t == 0) {
+    stat[0] = mean;
+    stat[1] = rstd;
+  }
+  d_csync();
+}
+
+__device__ __forceinline__ XDigits d_digits_at(uint8_t* base, int K, int lfk) {
+  XDigits Xd;
+  Xd.xd = reinterpret_cast<uint2*>(base);
+  Xd.xc = reinterpret_cast<float*>(base + (size_t)K * 3);
+  Xd.xsum = Xd.xc + (K >> (lfk + 5));
+  return Xd;
+}
+
+// Input of a digit build: kind 0  z + (p - z) * mix (z, p shared, mix global);
+// 1  z (shared); 2  g (global, read through L2); 3  relu(g)^2.
+struct DSrc {
+  int kind;
+  const float* z;
+  const float* p;
+  const float* g;
+};
+
+template <int LFK>
+__device__ __noinline__ void d_build(const DSrc& src, int K, uint8_t* base) {
+  const DSrc S = src;
+  build_digits(
+      K, LFK,
+      [&](int i) -> float4 {
+        if (S.kind == 0) {
+          const float4 z = *reinterpret_cast<const float4*>(S.z + i), p = *reinterpret_cast<const float4*>(S.p + i);
+          const float4 m = ldg4(S.g + i);
+          return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
+                             z.w + (p.w - z.w) * m.w);
+        }
+        if (S.kind == 1) return *reinterpret_cast<const float4*>(S.z + i);
+        const float4 v = ldcg4(S.g + i);
+        if (S.kind == 2) return v;
+        return make_float4(v.x > 0.f ? v.x * v.x : 0.f, v.y > 0.f ? v.y * v.y : 0.f, v.z > 0.f ? v.z * v.z : 0.f,
+                           v.w > 0.f ? v.w * v.w : 0.f);
+      },
+      d_digits_at(base, K, LFK), threadIdx.x, kDT, kDBar);
+}
+
+__device__ __forceinline__ void ld8(float (&v)[8], const float* p) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void ldg8(float (&v)[8], const float* p) {
+  const float4 a = ldg4(p), b = ldg4(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void ldcg8(float (&v)[8], const float* p) {
+  const float4 a = ldcg4(p), b = ldcg4(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Operands of one fused LayerNorm + token-shift prep (d_ln_mix).
+struct DLnMix {
+  const float* xs;   // shared input vector
+  const float* add;  // global vector added to it (nullptr: none)
+  float* xo;         // shared copy of the sum (nullptr: not kept)
+  const float *w, *b;  // LayerNorm weight, bias (global)
+  const float* prev;   // previous-token vector (global; nullptr: mixes are the LayerNorm output itself)
+  float* pv;           // shared copy of prev (nullptr: not kept)
+  const float* mix[3];  // token-shift mixes (global), one digit set each
+  int nmix;
+  float* ln;     // shared LayerNorm output
+  float* stat;   // mean, rstd (nullptr: not kept)
+};
+
+// y = LayerNorm(xs + add); for each mix m: digits of y + (prev - y) * mix_m
+// into dig + m * stride.  One item of 8 columns per consumer thread (C <= 8 *
+// kDT): every global operand of the phase is loaded in one round.
+template <int LFK>
+__device__ __noinline__ void d_ln_mix(const DArgs& a, DCons& c, const DLnMix& q, uint8_t* dig, uint32_t stride) {
+  const int t = threadIdx.x, C = a.d.C, items = C >> 3;
+  const bool act = t < items;
+  const int i0 = act ? t * 8 : 0;
+  float x[8], w[8], b[8], pv[8], mx[3][8];
+  ld8(x, q.xs + i0);
+  if (q.add) {
+    float ad[8];
+    ldcg8(ad, q.add + i0);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] += ad[u];
+  }
+  ldg8(w, q.w + i0);
+  ldg8(b, q.b + i0);
+  if (q.prev) ldcg8(pv, q.prev + i0);
+#pragma unroll
+  for (int m = 0; m < 3; ++m)
+    if (m < q.nmix && q.mix[m]) ldg8(mx[m], q.mix[m] + i0);
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) s += act ? x[u] : 0.f;
+  const float mean = d_csum(s, c.red) / (float)C;
+  float qq = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float dv = x[u] - mean;
+    qq += act ? dv * dv : 0.f;
+  }
+  const float rstd = rsqrtf(d_csum(qq, c.red) / (float)C + 1e-5f);
+  float y[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) y[u] = ln_val(x[u], mean, rstd, w[u], b[u]);
+  if (act) {
+    if (q.xo) st8(q.xo + i0, x);
+    st8(q.ln + i0, y);
+    if (q.pv && q.prev) st8(q.pv + i0, pv);
+  }
+  if (q.stat && t == 0) {
+    q.stat[0] = mean;
+    q.stat[1] = rstd;
+  }
+#pragma unroll
+  for (int m = 0; m < 3; ++m) {
+    if (m < q.nmix) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = q.prev ? y[u] + (pv[u] - y[u]) * mx[m][u] : y[u];
+      emit_digits(v, t, act, LFK, d_digits_at(dig + (size_t)m * stride, C, LFK));
+    }
+  }
+  d_csync();
+}
+
+// Wait for the next ring slot; a warp whose wait gives up stops waiting for good.
+__device__ __forceinline__ const uint8_t* d_slot_wait(const DArgs& a, DCons& c) {
+  const int slot = c.seq % a.nst;
+  if (!c.dead) {
+    const bool got = mbar_wait_bounded(&c.full[slot], (uint32_t)((c.seq / a.nst) & 1), a.spin_limit);
+    if (!__all_sync(0xffffffffu, got)) {
+      c.dead = 1;
+      if ((threadIdx.x & 31) == 0) {
+        atomicOr(a.b.err, kErrTimeout);
+        *c.abort = 1;
+      }
+    }
+  }
+  if (a.trace && blockIdx.x == 0 && threadIdx.x == 0 && 3 * c.seq + 2 < 2 * a.trace_cap)
+    a.trace[2 * (size_t)a.trace_cap + 3 * c.seq + 1] = global_ns();
+  return c.sm + (size_t)slot * a.slot;
+}
+
+__device__ __forceinline__ void d_slot_release(const DArgs& a, DCons& c) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&c.empty[c.seq % a.nst]);
+  if (a.trace && blockIdx.x == 0 && threadIdx.x == 0 && 3 * c.seq + 2 < 2 * a.trace_cap)
+    a.trace[2 * (size_t)a.trace_cap + 3 * c.seq + 2] = global_ns();
+  ++c.seq;
+}
+
+// GEMV units of one phase: out[row] += W[row, :] @ x for this CTA's units.
+// The input of tile `tile` is the digit set at dig + (tile / per_set) * stride
+// (per_set = 0: one input).  Arguments and ring counters live in registers
+// for the loop (it stores to shared memory, so reads through `a` or `c` would
+// be repeated each iteration).
+template <int LFK>
+__device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, uint8_t* dig, uint32_t stride, int K,
+                                     int per_set, float* out, int rows_total) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const ImmaLane L = imma_lane();
+  const int nst = a.nst, nb = a.nb, pr = a.pr, lg = a.lg, kch = a.kc >> 5, u0 = R.u0, u1 = R.u1, nch = R.nch;
+  const uint32_t slot_b = a.slot, code_b = a.code_b, limit = a.spin_limit;
+  uint8_t* const sm = c.sm;
+  uint64_t* const full = c.full;
+  uint64_t* const empty = c.empty;
+  float* const part = reinterpret_cast<float*>(sm + a.o_part);
+  unsigned long long* tr = (a.trace && blockIdx.x == 0 && t == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
+  const int tr_n = 2 * a.trace_cap;
+  int seq = c.seq, pbuf = c.pbuf;
+  bool dead = c.dead;
+  const int pofs = L.ra * pr + ((warp << 7) >> lg);
+  float acc0 = 0.f, acc1 = 0.f;
+  int cur_set = -1;
+  XDigits X{};
+  int tile = u0 / nch, chunk = u0 - tile * nch;
+#pragma unroll 1
+  for (int u = u0; u < u1; ++u) {
+    const int set = per_set ? tile / per_set : 0;
+    if (set != cur_set) {
+      X = d_digits_at(dig + (size_t)set * stride, K, LFK);
+      cur_set = set;
+    }
+    const int slot = seq % nst;
+    const uint8_t* sl = sm + (size_t)slot * slot_b;
+    if (!dead) {
+      const bool got = mbar_wait_bounded(&full[slot], (uint32_t)((seq / nst) & 1), limit);
+      if (!__all_sync(0xffffffffu, got)) {
+        dead = true;
+        if (lane == 0) {
+          atomicOr(a.b.err, kErrTimeout);
+          *c.abort = 1;
+        }
+      }
+    }
+    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 1] = global_ns();
+    if (!dead && warp < nb) {
+      const float2* pp = reinterpret_cast<const float2*>(sl + code_b) + pofs;
+      imma_block<LFK>(sl + warp * 2048, pp, pp + 8 * pr, chunk * kch + warp * 4, X, L, acc0, acc1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 2] = global_ns();
+    ++seq;
+    if (chunk == nch - 1 || u == u1 - 1) {
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      float* pt = part + pbuf * (kDW * 16);
+      if ((lane & 3) == 0) {
+        pt[warp * 16 + L.ra] = acc0;
+        pt[warp * 16 + L.ra + 8] = acc1;
+      }
+      acc0 = acc1 = 0.f;
+      d_csync();
+      if (t < 16) {
+        float v = 0.f;
+        for (int w = 0; w < nb; ++w) v += pt[w * 16 + t];
+        const int row = tile * 16 + t;
+        if (row < rows_total && !dead) atomicAdd(out + row, v);
+      }
+      pbuf ^= 1;
+    }
+    if (++chunk == nch) {
+      chunk = 0;
+      ++tile;
+    }
+  }
+  c.seq = seq;
+  c.pbuf = pbuf;
+  c.dead = dead;
+}
+
+// Adapter first stages of this CTA (rows [i0, i1) of W1 [C][R] times the
+// mixed input), accumulated in 2^-32 fixed point.
+__device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, int l, const float* TV,
+                                     const float* PV, float* misc) {
+  const int t = threadIdx.x, C = a.d.C;
+  const LayerDev& Ly = a.layers[l];
+  for (int k = 0; k < T.nitem[l == 0 ? 0 : 1]; ++k) {
+    const int item = T.item[k];
+    const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
+    const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
+    const float* mix = m == 0 ? Ly.x_w : (m == 1 ? Ly.x_a : (m == 2 ? Ly.x_g : Ly.x_v));
+    const int R = W.cols, wlg = W.lg;
+    const int i0 = sp * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows), nr = i1 - i0;
+    float* xm = misc;          // [adp_rows]
+    float* pacc = misc + 256;  // [nrg][R]
+    #pragma unroll 1
+    for (int i = t; i < nr; i += kDT) xm[i] = TV[i0 + i] + (PV[i0 + i] - TV[i0 + i]) * __ldg(mix + i0 + i);
+    d_csync();
+    const uint8_t* sl = d_slot_wait(a, c);
+    const int nrg = R < kDT ? kDT / R : 1;
+    if (!c.dead) {
+      const uint32_t qb = (uint32_t)(nr * R);
+      const float2* cs = reinterpret_cast<const float2*>(sl + ((qb + 15u) & ~15u));
+      const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> wlg) & ~1u;
+      #pragma unroll 1
+      for (int jw = t; jw < nrg * R; jw += kDT) {
+        const int j = jw % R, rg = jw / R;
+        float acc = 0.f;
+        for (int i = rg; i < nr; i += nrg) {
+          const uint32_t e = (uint32_t)(i0 + i) * (uint32_t)R + (uint32_t)j;
+          const float2 sc = cs[(e >> wlg) - g0];
+          acc = fmaf(xm[i], sg8_dequant(sl[i * R + j], sc.x, sc.y), acc);
+        }
+        pacc[rg * R + j] = acc;
+      }
+    }
+    d_slot_release(a, c);
+    d_csync();
+    if (!c.dead) {
+      const int off = d_rank_off(a.d, m);
+      #pragma unroll 1
+      for (int j = t; j < R; j += kDT) {
+        float v = 0.f;
+        for (int rg = 0; rg < nrg; ++rg) v += pacc[rg * R + j];
+        atomicAdd(a.b.adp64 + off + j, (unsigned long long)__float2ll_rn(v * kFix));
+      }
+    }
+    d_csync();
+  }
+}
+
+// Phase B for head h = blockIdx.x: adapter second stages, kk-normalize, decay,
+// WKV7 update of S (already in shared memory), GroupNorm, bonus, gate.
+__device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& T, int l, float* S, float* misc) {
+  const int t = threadIdx.x, C = a.d.C, H = a.d.H, h = blockIdx.x;
+  const LayerDev& Ly = a.layers[l];
+  float* mid = S + 4096;                     // [rtot]
+  float* vec = mid + ((a.d.rtot + 3) & ~3);  // [4][64]
+  float* sr = vec + 256;
+  float* sd = sr + 64;
+  float* sk = sd + 64;
+  float* sv = sk + 64;
+  float* skk = sv + 64;
+  float* ska = skk + 64;
+  float* sy = ska + 64;
+  float* Sg = a.b.wkv + ((size_t)l * H + h) * 4096;
+  const int nm = l == 0 ? 3 : 4;
+  const int used = l == 0 ? a.d.rw + a.d.ra + a.d.rg : a.d.rtot;
+  #pragma unroll 1
+  for (int j = t; j < used; j += kDT) {
+    float v = (float)(long long)__ldcg(a.b.adp64 + j) * kUnfix;
+    if (j < a.d.rw) v = tanhf(v);
+    else if (j >= a.d.rw + a.d.ra && j < a.d.rw + a.d.ra + a.d.rg) v = sigmoidf_(v);
+    mid[j] = v;
+  }
+  // every global operand of the head in one round
+  float r = 0.f, k = 0.f, v = 0.f, vf = 0.f, kk_w = 0.f, a0 = 0.f, ka = 0.f, v0 = 0.f, w0 = 0.f, rk = 0.f, lw = 0.f,
+        lb = 0.f;
+  if (t < 64) {
+    const int ch = h * 64 + t;
+    r = __ldcg(a.b.rkv + ch);
+    k = __ldcg(a.b.rkv + C + ch);
+    v = __ldcg(a.b.rkv + 2 * C + ch);
+    if (l != 0) {
+      vf = __ldcg(a.b.v_first + ch);
+      v0 = __ldg(Ly.v0 + ch);
+    }
+    kk_w = __ldg(Ly.k_k + ch);
+    a0 = __ldg(Ly.a0 + ch);
+    ka = __ldg(Ly.k_a + ch);
+    w0 = __ldg(Ly.w0 + ch);
+    rk = __ldg(Ly.r_k + ch);
+    lw = __ldg(Ly.lnx_w + ch);
+    lb = __ldg(Ly.lnx_b + ch);
+  }
+  float* vp = misc;  // [5][4][64] per-thread partials
+  #pragma unroll 1
+  for (int i = t; i < 5 * 256; i += kDT) vp[i] = 0.f;
+  cp_async_wait_all();
+  d_csync();
+  {
+    const int cc = t & 63, q = t >> 6;  // 5 row phases x 64 columns
+    for (int pc = 0; pc < T.npc[l == 0 ? 0 : 1]; ++pc) {
+      const uint8_t* sl = d_slot_wait(a, c);
+      if (!c.dead) {
+        const int m = T.pm[pc], br = a.abr[m], r0 = T.pr0[pc];
+        const int nr = min(br, d_rank(a.d, m) - r0);
+        const float2* pairs = reinterpret_cast<const float2*>(sl + br * 64);
+        const int sel = ((h * 64) >> a.alg[m]) & 1;
+        const float* mm = mid + d_rank_off(a.d, m) + r0;
+        float acc = 0.f;
+        for (int i = q; i < nr; i += 5) {
+          const float2 pq = pairs[i * 2 + sel];
+          acc = fmaf(mm[i], sg8_dequant(sl[i * 64 + cc], pq.x, pq.y), acc);
+        }
+        vp[(q * 4 + m) * 64 + cc] += acc;
+      }
+      d_slot_release(a, c);
+    }
+  }
+  d_csync();
+  if (t < 256) {
+    const int m = t >> 6, cc = t & 63;
+    float s = 0.f;
+    if (m < nm)
+      for (int q = 0; q < 5; ++q) s += vp[(q * 4 + m) * 64 + cc];
+    vec[m * 64 + cc] = s;
+  }
+  d_csync();
+  const float kkv = t < 64 ? k * kk_w : 0.f;
+  const float nrm = sqrtf(d_csum(kkv * kkv, c.red));
+  if (t < 64) {
+    const int ch = h * 64 + t;
+    const float aa = sigmoidf_(a0 + vec[64 + t]);
+    const float kk = kkv / fmaxf(nrm, 1e-12f);
+    const float kn = k * (1.0f + (aa - 1.0f) * ka);
+    if (l == 0) a.b.v_first[ch] = v;
+    else v = v + (vf - v) * sigmoidf_(v0 + vec[192 + t]);
+    sr[t] = r;
+    sd[t] = expf(-0.606531f * sigmoidf_(w0 + vec[t]));
+    sk[t] = kn;
+    sv[t] = v;
+    skk[t] = kk;
+    ska[t] = kk * aa;
+  }
+  d_csync();
+  if (t < 256) wkv7_head64(S, sr, sd, sk, sv, skk, ska, sy);
+  d_csync();
+  #pragma unroll 1
+  for (int u = t; u < 1024; u += kDT) reinterpret_cast<float4*>(Sg)[u] = reinterpret_cast<const float4*>(S)[u];
+  const float yv = t < 64 ? sy[t] : 0.f;
+  const float mean = d_csum(yv, c.red) / 64.f;
+  const float dv = t < 64 ? yv - mean : 0.f;
+  const float var = d_csum(dv * dv, c.red) / 64.f;
+  const float bon = t < 64 ? sr[t] * sk[t] * rk : 0.f;
+  const float bonus = d_csum(bon, c.red);
+  if (t < 64) {
+    const int ch = h * 64 + t;
+    float o = dv * rsqrtf(var + 64e-5f) * lw + lb;
+    o = o + bonus * sv[t];
+    a.b.att_y[ch] = o * vec[128 + t];
+  }
+}
+
+// X = LayerNorm0(emb[tok]).
+__device__ __noinline__ void d_embed(const DArgs& a, DCons& c, int tok, float* X, float* TV, float* PV) {
+  const int t = threadIdx.x, C = a.d.C;
+  const PackedView& E = a.emb;
+  if (a.emb_fast) {
+    const int gpr = C >> E.lg;
+    uint8_t* q = reinterpret_cast<uint8_t*>(TV);
+    float2* sc = reinterpret_cast<float2*>(PV);
+    #pragma unroll 1
+    for (int o = t * 16; o < C; o += kDT * 16) cp_async16(q + o, E.payload + (size_t)tok * C + o);
+    #pragma unroll 1
+    for (int o = t * 16; o < gpr * 8; o += kDT * 16)
+      cp_async16(reinterpret_cast<uint8_t*>(sc) + o, E.meta + (size_t)tok * gpr * 8 + o);
+    cp_async_commit();
+    cp_async_wait_all();
+    d_csync();
+    #pragma unroll 1
+    for (int i = t; i < C; i += kDT) {
+      const float2 s = sc[i >> E.lg];
+      X[i] = sg8_dequant(q[i], s.x, s.y);
+    }
+  } else {
+    #pragma unroll 1
+    for (int i = t; i < C; i += kDT) X[i] = packed_at(E, tok, i);
+  }
+  d_csync();
+  d_layer_norm(X, X, a.ln0_w, a.ln0_b, C, nullptr, c.red);
+}
+
+// This CTA's slice of the logits: first maximum -> amax partials.
+__device__ __noinline__ void d_argmax_part(const DArgs& a, const DTable& T, float* s_bv, int* s_bi) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  #pragma unroll 1
+  for (int i = T.zv0 + t; i < T.zv1; i += kDT) {
+    const float v = __ldcg(a.b.logits + i);
+    if (v > best) {
+      best = v;
+      besti = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ov > best || (ov == best && oi < besti)) {
+      best = ov;
+      besti = oi;
+    }
+  }
+  if (lane == 0) {
+    s_bv[warp] = best;
+    s_bi[warp] = besti;
+  }
+  d_csync();
+  if (t == 0) {
+    float cb = -INFINITY;
+    int ci = 0x7fffffff;
+    for (int w = 0; w < kDW; ++w)
+      if (s_bv[w] > cb || (s_bv[w] == cb && s_bi[w] < ci)) {
+        cb = s_bv[w];
+        ci = s_bi[w];
+      }
+    a.b.amax_v[blockIdx.x] = cb;
+    a.b.amax_i[blockIdx.x] = ci;
+  }
+}
+
+// First maximum over all CTAs' partials (every CTA computes the same token).
+__device__ __noinline__ int d_argmax_all(const DArgs& a, int* s_tok) {
+  const int t = threadIdx.x, lane = t & 31;
+  if (t < 32) {
+    float gb = -INFINITY;
+    int gi = 0x7fffffff;
+    for (int cta = lane; cta < (int)gridDim.x; cta += 32) {
+      const float v = __ldcg(a.b.amax_v + cta);
+      const int i = __ldcg(a.b.amax_i + cta);
+      if (v > gb || (v == gb && i < gi)) {
+        gb = v;
+        gi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, gb, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
+      if (ov > gb || (ov == gb && oi < gi)) {
+        gb = ov;
+        gi = oi;
+      }
+    }
+    if (t == 0) *s_tok = gi == 0x7fffffff ? 0 : gi;
+  }
+  d_csync();
+  return *s_tok;
+}
+
 // --------------------------------------------------------------- kernel
 template <int LFK>
-__global__ void __launch_bounds__(kDThreads, 1) decode_kernel(DArgs a) {
+__global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_constant__ DArgs a) {
   extern __shared__ __align__(1024) uint8_t d_smraw[];
   uint8_t* sm = d_smraw + ((1024u - (smem_u32(d_smraw) & 1023u)) & 1023u);
   __shared__ DTable T;
@@ -365,172 +985,41 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(DArgs a) {
     return;
   }
 
-  // ------------------------------------------------------------ consumers
   const int C = a.d.C, F = a.d.F, H = a.d.H, G = gridDim.x, bx = blockIdx.x;
+  const bool fused = C <= 8 * kDT;  // one 8-column item per consumer thread: single-round preps
   float* X = reinterpret_cast<float*>(sm + a.o_x);    // layer input (residual stream)
   float* XB = reinterpret_cast<float*>(sm + a.o_xb);  // after attention
   float* TV = reinterpret_cast<float*>(sm + a.o_t);   // normalised vector
   float* PV = reinterpret_cast<float*>(sm + a.o_p);   // previous-token vector
-  float* part = reinterpret_cast<float*>(sm + a.o_part);
   float* misc = reinterpret_cast<float*>(sm + a.o_misc);
   uint8_t* dig = sm + a.o_dig;
-  const ImmaLane L = imma_lane();
-  int seq = 0, pbuf = 0;
-  bool dead = false;
-  unsigned target = 0;
-  int tr = 0;
-  const int trow = bx == 0 ? 0 : (bx == G - 1 ? 1 : -1);
-  auto mark = [&]() {
-    if (a.trace && trow >= 0 && t == 0 && tr < a.trace_cap) a.trace[(size_t)trow * a.trace_cap + tr] = global_ns();
-    ++tr;
-  };
-  auto csync = [&]() { bar_sync(kDBar, kDT); };
-  auto csum = [&](float v) -> float {
-    v = warp_sum(v);
-    if (lane == 0) red[warp] = v;
-    csync();
-    float r = 0.f;
-#pragma unroll
-    for (int w = 0; w < kDW; ++w) r += red[w];
-    csync();
-    return r;
-  };
-  // grid barrier of the consumers; false (CTA-uniform) when it gave up or another wait failed
-  auto gsync = [&]() -> bool {
-    csync();
-    target += G;
-    if (t == 0) {
-      bool ok = !s_abort;
-      if (ok) {
-        __threadfence();
-        atomicAdd(a.gbar, 1u);
-        ok = false;
-        for (uint32_t i = 0; i < a.spin_limit; ++i) {
-          if (d_ld_acquire(a.gbar) >= target) {
-            ok = true;
-            break;
-          }
-          __nanosleep(32);
-        }
-        if (!ok) {
-          atomicOr(a.b.err, kErrTimeout);
-          s_abort = 1;
-        }
-      }
-      s_flag = ok ? 0 : 1;
-    }
-    csync();
-    return s_flag == 0;
-  };
-  auto zero = [&](float* p, int i0, int i1) {
-    for (int i = i0 + t; i < i1; i += kDT) p[i] = 0.f;
-  };
-  // dst = LayerNorm(src) over C (eps 1e-5, F.layer_norm); optionally keep mean / rstd
-  auto layer_norm = [&](float* dst, const float* src, const float* w, const float* bb, float* stat) {
-    float s = 0.f;
-    for (int i = t; i < C; i += kDT) s += src[i];
-    const float mean = csum(s) / (float)C;
-    float q = 0.f;
-    for (int i = t; i < C; i += kDT) {
-      const float dv = src[i] - mean;
-      q += dv * dv;
-    }
-    const float rstd = rsqrtf(csum(q) / (float)C + 1e-5f);
-    for (int i = t; i < C; i += kDT) dst[i] = ln_val(src[i], mean, rstd, __ldg(w + i), __ldg(bb + i));
-    if (stat && t == 0) {
-      stat[0] = mean;
-      stat[1] = rstd;
-    }
-    csync();
-  };
-  auto ln_at = [&](const float* src, int i, const float* stat, const float* w, const float* bb) {
-    return ln_val(src[i], stat[0], stat[1], __ldg(w + i), __ldg(bb + i));
-  };
-  auto digits_at = [&](uint32_t off, int K) -> XDigits {
-    uint8_t* base = dig + off;
-    XDigits Xd;
-    Xd.xd = reinterpret_cast<uint2*>(base);
-    Xd.xc = reinterpret_cast<float*>(base + (size_t)K * 3);
-    Xd.xsum = Xd.xc + (K >> (LFK + 5));
-    return Xd;
-  };
-  auto build = [&](uint32_t off, int K, auto get4) { build_digits(K, LFK, get4, digits_at(off, K), t, kDT, kDBar); };
-  auto f4 = [](const float* p, int i) { return *reinterpret_cast<const float4*>(p + i); };
-  auto mix4 = [](float4 z, float4 p, float4 m) {
-    return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
-                       z.w + (p.w - z.w) * m.w);
-  };
-  // wait for the next ring slot; a warp whose wait gives up stops waiting for good
-  auto slot_wait = [&]() -> const uint8_t* {
-    const int slot = seq % a.nst;
-    if (!dead) {
-      const bool got = mbar_wait_bounded(&full[slot], (uint32_t)((seq / a.nst) & 1), a.spin_limit);
-      if (!__all_sync(0xffffffffu, got)) {
-        dead = true;
-        if (lane == 0) {
-          atomicOr(a.b.err, kErrTimeout);
-          s_abort = 1;
-        }
-      }
-    }
-    return sm + (size_t)slot * a.slot;
-  };
-  auto slot_release = [&]() {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[seq % a.nst]);
-    ++seq;
-  };
-  // GEMV units of one phase: rows of `out` (rows_total) += W[rows, :] @ x;
-  // xs[tile / per_set] is the input of a tile (per_set = 0: one input)
-  auto run_units = [&](const DRange& R, const XDigits* xs, int per_set, float* out, int rows_total) {
-    float acc0 = 0.f, acc1 = 0.f;
-    const int kch = a.kc >> 5;
-    for (int u = R.u0; u < R.u1; ++u) {
-      const int tile = u / R.nch, chunk = u - tile * R.nch;
-      const uint8_t* sl = slot_wait();
-      if (!dead && warp < a.nb) {
-        const float2* pp = reinterpret_cast<const float2*>(sl + a.code_b) + L.ra * a.pr + ((warp << 7) >> a.lg);
-        imma_block<LFK>(sl + warp * 2048, pp, pp + 8 * a.pr, chunk * kch + warp * 4, xs[per_set ? tile / per_set : 0], L,
-                        acc0, acc1);
-      }
-      slot_release();
-      if (chunk == R.nch - 1 || u == R.u1 - 1) {
-        acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-        acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-        float* pt = part + pbuf * (kDW * 16);
-        if ((lane & 3) == 0) {
-          pt[warp * 16 + L.ra] = acc0;
-          pt[warp * 16 + L.ra + 8] = acc1;
-        }
-        acc0 = acc1 = 0.f;
-        csync();
-        if (t < 16) {
-          float v = 0.f;
-          for (int w = 0; w < a.nb; ++w) v += pt[w * 16 + t];
-          const int row = tile * 16 + t;
-          if (row < rows_total && !dead) atomicAdd(out + row, v);
-        }
-        pbuf ^= 1;
-      }
-    }
-  };
+  DCons c;
+  c.sm = sm;
+  c.full = full;
+  c.empty = empty;
+  c.red = red;
+  c.abort = &s_abort;
+  c.flag = &s_flag;
+  c.seq = c.pbuf = c.dead = c.tr = 0;
+  c.trow = bx == 0 ? 0 : (bx == G - 1 ? 1 : -1);
+  c.target = 0;
 
   float* acc_rkv = a.b.rkv;
   float* acc_ao = a.b.ao;
   float* acc_hk = a.b.h;
   float* acc_fo = a.b.fo;
-  unsigned long long* acc_adp = a.b.adp64;
   float* logits = a.b.logits;
 
   // accumulators start from zero in every launch (a failed launch may leave partial sums)
-  zero(acc_rkv, T.z3c0, T.z3c1);
-  zero(acc_hk, T.zf0, T.zf1);
-  zero(acc_ao, T.zc0, T.zc1);
-  zero(acc_fo, T.zc0, T.zc1);
-  zero(logits, T.zv0, T.zv1);
-  for (int i = T.zr0 + t; i < T.zr1; i += kDT) acc_adp[i] = 0ull;
+  d_zero(acc_rkv, T.z3c0, T.z3c1);
+  d_zero(acc_hk, T.zf0, T.zf1);
+  d_zero(acc_ao, T.zc0, T.zc1);
+  d_zero(acc_fo, T.zc0, T.zc1);
+  d_zero(logits, T.zv0, T.zv1);
+  #pragma unroll 1
+  for (int i = T.zr0 + t; i < T.zr1; i += kDT) a.b.adp64[i] = 0ull;
   int tok = a.mode == 0 ? (a.first_tok >= 0 ? a.first_tok : __ldcg(a.b.tok)) : __ldg(a.forced);
-  bool alive = gsync();
+  bool alive = d_gsync(a, c);
   for (int step = 0; step < a.ntok && alive; ++step) {
     const bool head = a.mode == 0 || step == a.ntok - 1;
     if (a.mode == 1) tok = __ldg(a.forced + step);
@@ -538,354 +1027,174 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(DArgs a) {
       if (t == 0) atomicOr(a.b.err, kErrToken);
       tok = 0;
     }
-    mark();  // token start
-    // ---- embedding + ln0 (every CTA)
-    {
-      const PackedView& E = a.emb;
-      if (a.emb_fast) {
-        const int gpr = C >> E.lg;
-        uint8_t* q = reinterpret_cast<uint8_t*>(TV);
-        float2* sc = reinterpret_cast<float2*>(PV);
-        for (int o = t * 16; o < C; o += kDT * 16) cp_async16(q + o, E.payload + (size_t)tok * C + o);
-        for (int o = t * 16; o < gpr * 8; o += kDT * 16)
-          cp_async16(reinterpret_cast<uint8_t*>(sc) + o, E.meta + (size_t)tok * gpr * 8 + o);
-        cp_async_commit();
-        cp_async_wait_all();
-        csync();
-        for (int i = t; i < C; i += kDT) {
-          const float2 s = sc[i >> E.lg];
-          X[i] = sg8_dequant(q[i], s.x, s.y);
-        }
-      } else {
-        for (int i = t; i < C; i += kDT) X[i] = packed_at(E, tok, i);
-      }
-      csync();
-      layer_norm(X, X, a.ln0_w, a.ln0_b, nullptr);
-    }
+    d_mark(a, c);  // token start
+    d_embed(a, c, tok, X, TV, PV);
 
     for (int l = 0; l < a.d.L && alive; ++l) {
       const LayerDev& Ly = a.layers[l];
-      const float* prev_att = a.b.att_x + (size_t)l * C;
-      const float* prev_ffn = a.b.ffn_x + (size_t)l * C;
-      if (l > 0) {
-        if (!gsync()) {
-          alive = false;
-          break;
-        }
-        for (int i = t; i < C; i += kDT) X[i] = XB[i] + __ldcg(acc_fo + i);
-        csync();
+      if (l > 0 && !d_gsync(a, c)) {
+        alive = false;
+        break;
       }
-      mark();  // A start
+      d_mark(a, c);  // A start
       // ================= A: ln1, mixes, r/k/v rows, adapter first stages
-      layer_norm(TV, X, Ly.ln1_w, Ly.ln1_b, s_stat);
-      for (int i = t; i < C; i += kDT) PV[i] = __ldcg(prev_att + i);
-      csync();
-      build(0, C, [&](int i) { return mix4(f4(TV, i), f4(PV, i), ldg4(Ly.x_r + i)); });
-      build(a.dig_set, C, [&](int i) { return mix4(f4(TV, i), f4(PV, i), ldg4(Ly.x_k + i)); });
-      build(2 * a.dig_set, C, [&](int i) { return mix4(f4(TV, i), f4(PV, i), ldg4(Ly.x_v + i)); });
-      mark();  // A prep done
-      {
-        const XDigits xs3[3] = {digits_at(0, C), digits_at(a.dig_set, C), digits_at(2 * a.dig_set, C)};
-        run_units(T.r[0], xs3, C / 16, acc_rkv, 3 * C);
-      }
-      mark();  // A units done
-      for (int k = 0; k < T.nitem[l == 0 ? 0 : 1]; ++k) {
-        const int item = T.item[k];
-        const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
-        const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
-        const float* mix = m == 0 ? Ly.x_w : (m == 1 ? Ly.x_a : (m == 2 ? Ly.x_g : Ly.x_v));
-        const int R = W.cols, wlg = W.lg;
-        const int i0 = sp * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows), nr = i1 - i0;
-        float* xm = misc;          // [adp_rows]
-        float* pacc = misc + 256;  // [nrg][R]
-        for (int i = t; i < nr; i += kDT) xm[i] = TV[i0 + i] + (PV[i0 + i] - TV[i0 + i]) * __ldg(mix + i0 + i);
-        csync();
-        const uint8_t* sl = slot_wait();
-        const int nrg = R < kDT ? kDT / R : 1;
-        if (!dead) {
-          const uint8_t* cq = sl;
-          const uint32_t qb = (uint32_t)(nr * R);
-          const float2* cs = reinterpret_cast<const float2*>(sl + ((qb + 15u) & ~15u));
-          const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> wlg) & ~1u;
-          for (int jw = t; jw < nrg * R; jw += kDT) {
-            const int j = jw % R, rg = jw / R;
-            float acc = 0.f;
-            for (int i = rg; i < nr; i += nrg) {
-              const uint32_t e = (uint32_t)(i0 + i) * (uint32_t)R + (uint32_t)j;
-              const float2 sc = cs[(e >> wlg) - g0];
-              acc = fmaf(xm[i], sg8_dequant(cq[i * R + j], sc.x, sc.y), acc);
-            }
-            pacc[rg * R + j] = acc;
-          }
+      if (fused) {
+        DLnMix q{};
+        q.xs = l > 0 ? XB : X;
+        q.add = l > 0 ? acc_fo : nullptr;
+        q.xo = X;
+        q.w = Ly.ln1_w;
+        q.b = Ly.ln1_b;
+        q.prev = a.b.att_x + (size_t)l * C;
+        q.pv = PV;
+        q.mix[0] = Ly.x_r;
+        q.mix[1] = Ly.x_k;
+        q.mix[2] = Ly.x_v;
+        q.nmix = 3;
+        q.ln = TV;
+        q.stat = s_stat;
+        d_ln_mix<LFK>(a, c, q, dig, a.dig_set);
+      } else {
+        if (l > 0) {
+#pragma unroll 1
+          for (int i = t; i < C; i += kDT) X[i] = XB[i] + __ldcg(acc_fo + i);
+          d_csync();
         }
-        slot_release();
-        csync();
-        if (!dead) {
-          const int off = d_rank_off(a.d, m);
-          for (int j = t; j < R; j += kDT) {
-            float v = 0.f;
-            for (int rg = 0; rg < nrg; ++rg) v += pacc[rg * R + j];
-            atomicAdd(acc_adp + off + j, (unsigned long long)__float2ll_rn(v * kFix));
-          }
-        }
-        csync();
+        d_layer_norm(TV, X, Ly.ln1_w, Ly.ln1_b, C, s_stat, red);
+#pragma unroll 1
+        for (int i = t; i < C; i += kDT) PV[i] = __ldcg(a.b.att_x + (size_t)l * C + i);
+        d_csync();
+        d_build<LFK>(DSrc{0, TV, PV, Ly.x_r}, C, dig);
+        d_build<LFK>(DSrc{0, TV, PV, Ly.x_k}, C, dig + a.dig_set);
+        d_build<LFK>(DSrc{0, TV, PV, Ly.x_v}, C, dig + 2 * a.dig_set);
       }
-      mark();  // A done
+      d_mark(a, c);  // A prep done
+      d_units<LFK>(a, c, T.r[0], dig, a.dig_set, C, C / 16, acc_rkv, 3 * C);
+      d_mark(a, c);  // A units done
+      d_items(a, c, T, l, TV, PV, misc);
+      d_mark(a, c);  // A done
       // ================= B: one CTA per head
       const bool is_head = bx < H;
-      float* S = reinterpret_cast<float*>(dig);  // [64][64] (digit sets are dead in B)
-      float* mid = S + 4096;                     // [rtot]
-      float* vec = mid + ((a.d.rtot + 3) & ~3);  // [4][64]
-      float* sr = vec + 256;
-      float* sd = sr + 64;
-      float* sk = sd + 64;
-      float* sv = sk + 64;
-      float* skk = sv + 64;
-      float* ska = skk + 64;
-      float* sy = ska + 64;
-      float* Sg = a.b.wkv + ((size_t)l * H + bx) * 4096;
+      float* S = reinterpret_cast<float*>(dig);  // digit sets are dead in B
       if (is_head) {
+        const float* Sg = a.b.wkv + ((size_t)l * H + bx) * 4096;
+        #pragma unroll 1
         for (int u = t; u < 1024; u += kDT) cp_async16(S + u * 4, Sg + u * 4);
         cp_async_commit();
       }
-      if (!gsync()) {
+      if (!d_gsync(a, c)) {
         alive = false;
         break;
       }
-      mark();  // B barrier
-      zero(acc_hk, T.zf0, T.zf1);
-      if (l == 0) zero(logits, T.zv0, T.zv1);
-      if (is_head) {
-        const int h = bx;
-        const int nm = l == 0 ? 3 : 4;
-        const int used = l == 0 ? a.d.rw + a.d.ra + a.d.rg : a.d.rtot;
-        for (int j = t; j < used; j += kDT) {
-          float v = (float)(long long)__ldcg(acc_adp + j) * kUnfix;
-          if (j < a.d.rw) v = tanhf(v);
-          else if (j >= a.d.rw + a.d.ra && j < a.d.rw + a.d.ra + a.d.rg) v = sigmoidf_(v);
-          mid[j] = v;
-        }
-        float r = 0.f, k = 0.f, v = 0.f, vf = 0.f;
-        if (t < 64) {
-          const int ch = h * 64 + t;
-          r = __ldcg(acc_rkv + ch);
-          k = __ldcg(acc_rkv + C + ch);
-          v = __ldcg(acc_rkv + 2 * C + ch);
-          if (l != 0) vf = __ldcg(a.b.v_first + ch);
-        }
-        float* vp = misc;  // [5][4][64] per-thread partials
-        for (int i = t; i < 5 * 256; i += kDT) vp[i] = 0.f;
-        cp_async_wait_all();
-        csync();
-        {
-          const int c = t & 63, q = t >> 6;  // 5 row phases x 64 columns
-          for (int pc = 0; pc < T.npc[l == 0 ? 0 : 1]; ++pc) {
-            const uint8_t* sl = slot_wait();
-            if (!dead) {
-              const int m = T.pm[pc], br = a.abr[m], r0 = T.pr0[pc];
-              const int nr = min(br, d_rank(a.d, m) - r0);
-              const float2* pairs = reinterpret_cast<const float2*>(sl + br * 64);
-              const int sel = ((h * 64) >> a.alg[m]) & 1;
-              const float* mm = mid + d_rank_off(a.d, m) + r0;
-              float acc = 0.f;
-              for (int i = q; i < nr; i += 5) {
-                const float2 pq = pairs[i * 2 + sel];
-                acc = fmaf(mm[i], sg8_dequant(sl[i * 64 + c], pq.x, pq.y), acc);
-              }
-              vp[(q * 4 + m) * 64 + c] += acc;
-            }
-            slot_release();
-          }
-        }
-        csync();
-        if (t < 256) {
-          const int m = t >> 6, c = t & 63;
-          float s = 0.f;
-          if (m < nm)
-            for (int q = 0; q < 5; ++q) s += vp[(q * 4 + m) * 64 + c];
-          vec[m * 64 + c] = s;
-        }
-        csync();
-        const float kkv = t < 64 ? k * __ldg(Ly.k_k + h * 64 + t) : 0.f;
-        const float nrm = sqrtf(csum(kkv * kkv));
-        if (t < 64) {
-          const int ch = h * 64 + t;
-          const float aa = sigmoidf_(__ldg(Ly.a0 + ch) + vec[64 + t]);
-          const float kk = kkv / fmaxf(nrm, 1e-12f);
-          const float kn = k * (1.0f + (aa - 1.0f) * __ldg(Ly.k_a + ch));
-          if (l == 0) a.b.v_first[ch] = v;
-          else v = v + (vf - v) * sigmoidf_(__ldg(Ly.v0 + ch) + vec[192 + t]);
-          sr[t] = r;
-          sd[t] = expf(-0.606531f * sigmoidf_(__ldg(Ly.w0 + ch) + vec[t]));
-          sk[t] = kn;
-          sv[t] = v;
-          skk[t] = kk;
-          ska[t] = kk * aa;
-        }
-        csync();
-        if (t < 256) wkv7_head64(S, sr, sd, sk, sv, skk, ska, sy);
-        csync();
-        for (int u = t; u < 1024; u += kDT) reinterpret_cast<float4*>(Sg)[u] = reinterpret_cast<const float4*>(S)[u];
-        const float yv = t < 64 ? sy[t] : 0.f;
-        const float mean = csum(yv) / 64.f;
-        const float dv = t < 64 ? yv - mean : 0.f;
-        const float var = csum(dv * dv) / 64.f;
-        const float bon = t < 64 ? sr[t] * sk[t] * __ldg(Ly.r_k + h * 64 + t) : 0.f;
-        const float bonus = csum(bon);
-        if (t < 64) {
-          const int ch = h * 64 + t;
-          float o = dv * rsqrtf(var + 64e-5f) * __ldg(Ly.lnx_w + ch) + __ldg(Ly.lnx_b + ch);
-          o = o + bonus * sv[t];
-          a.b.att_y[ch] = o * vec[128 + t];
-        }
-      }
-      mark();  // B done
-      if (!gsync()) {
+      d_mark(a, c);  // B barrier
+      d_zero(acc_hk, T.zf0, T.zf1);
+      if (l == 0) d_zero(logits, T.zv0, T.zv1);
+      if (is_head) d_head_wkv(a, c, T, l, S, misc);
+      d_mark(a, c);  // B done
+      if (!d_gsync(a, c)) {
         alive = false;
         break;
       }
-      mark();  // C barrier
+      d_mark(a, c);  // C barrier
       // ================= C: output projection; att_x[l] <- ln1 slice
-      zero(acc_fo, T.zc0, T.zc1);
+      d_zero(acc_fo, T.zc0, T.zc1);
+      #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
-        a.b.att_x[(size_t)l * C + i] = ln_at(X, i, s_stat, Ly.ln1_w, Ly.ln1_b);
-      build(0, C, [&](int i) { return ldcg4(a.b.att_y + i); });
-      mark();  // C prep done
-      {
-        const XDigits x1 = digits_at(0, C);
-        run_units(T.r[1], &x1, 0, acc_ao, C);
-      }
-      mark();  // C done
-      if (!gsync()) {
+        a.b.att_x[(size_t)l * C + i] = ln_val(X[i], s_stat[0], s_stat[1], __ldg(Ly.ln1_w + i), __ldg(Ly.ln1_b + i));
+      d_build<LFK>(DSrc{2, nullptr, nullptr, a.b.att_y}, C, dig);
+      d_mark(a, c);  // C prep done
+      d_units<LFK>(a, c, T.r[1], dig, 0, C, 0, acc_ao, C);
+      d_mark(a, c);  // C done
+      if (!d_gsync(a, c)) {
         alive = false;
         break;
       }
-      mark();  // D barrier
+      d_mark(a, c);  // D barrier
       // ================= D: x += att; ln2 + mix; ffn key rows
-      zero(acc_rkv, T.z3c0, T.z3c1);
-      for (int i = T.zr0 + t; i < T.zr1; i += kDT) acc_adp[i] = 0ull;
-      for (int i = t; i < C; i += kDT) {
-        XB[i] = X[i] + __ldcg(acc_ao + i);
-        PV[i] = __ldcg(prev_ffn + i);
+      d_zero(acc_rkv, T.z3c0, T.z3c1);
+      #pragma unroll 1
+      for (int i = T.zr0 + t; i < T.zr1; i += kDT) a.b.adp64[i] = 0ull;
+            if (fused) {
+        DLnMix q{};
+        q.xs = X;
+        q.add = acc_ao;
+        q.xo = XB;
+        q.w = Ly.ln2_w;
+        q.b = Ly.ln2_b;
+        q.prev = a.b.ffn_x + (size_t)l * C;
+        q.mix[0] = Ly.ffn_x_k;
+        q.nmix = 1;
+        q.ln = TV;
+        q.stat = s_stat + 2;
+        d_ln_mix<LFK>(a, c, q, dig, 0);
+      } else {
+#pragma unroll 1
+        for (int i = t; i < C; i += kDT) {
+          XB[i] = X[i] + __ldcg(acc_ao + i);
+          PV[i] = __ldcg(a.b.ffn_x + (size_t)l * C + i);
+        }
+        d_csync();
+        d_layer_norm(TV, XB, Ly.ln2_w, Ly.ln2_b, C, s_stat + 2, red);
+        d_build<LFK>(DSrc{0, TV, PV, Ly.ffn_x_k}, C, dig);
       }
-      csync();
-      layer_norm(TV, XB, Ly.ln2_w, Ly.ln2_b, s_stat + 2);
-      build(0, C, [&](int i) { return mix4(f4(TV, i), f4(PV, i), ldg4(Ly.ffn_x_k + i)); });
-      mark();  // D prep done
-      {
-        const XDigits x1 = digits_at(0, C);
-        run_units(T.r[2], &x1, 0, acc_hk, F);
-      }
-      mark();  // D done
-      if (!gsync()) {
+      d_mark(a, c);  // D prep done
+      d_units<LFK>(a, c, T.r[2], dig, 0, C, 0, acc_hk, F);
+      d_mark(a, c);  // D done
+      if (!d_gsync(a, c)) {
         alive = false;
         break;
       }
-      mark();  // E barrier
+      d_mark(a, c);  // E barrier
       // ================= E: relu^2; ffn value rows; ffn_x[l] <- ln2 slice
-      zero(acc_ao, T.zc0, T.zc1);
+      d_zero(acc_ao, T.zc0, T.zc1);
+      #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
-        a.b.ffn_x[(size_t)l * C + i] = ln_at(XB, i, s_stat + 2, Ly.ln2_w, Ly.ln2_b);
-      build(0, F, [&](int i) {
-        const float4 v = ldcg4(acc_hk + i);
-        return make_float4(v.x > 0.f ? v.x * v.x : 0.f, v.y > 0.f ? v.y * v.y : 0.f, v.z > 0.f ? v.z * v.z : 0.f,
-                           v.w > 0.f ? v.w * v.w : 0.f);
-      });
-      mark();  // E prep done
-      {
-        const XDigits x1 = digits_at(0, F);
-        run_units(T.r[3], &x1, 0, acc_fo, C);
-      }
-      mark();  // E done
+        a.b.ffn_x[(size_t)l * C + i] = ln_val(XB[i], s_stat[2], s_stat[3], __ldg(Ly.ln2_w + i), __ldg(Ly.ln2_b + i));
+      d_mark(a, c);  // E slices stored
+      d_build<LFK>(DSrc{3, nullptr, nullptr, acc_hk}, F, dig);
+      d_mark(a, c);  // E prep done
+      d_units<LFK>(a, c, T.r[3], dig, 0, F, 0, acc_fo, C);
+      d_mark(a, c);  // E done
     }
     if (!alive) break;
     if (!head) continue;
     // ================= head: ln_out, logits, argmax (first maximum)
-    if (!gsync()) {
+    if (!d_gsync(a, c)) {
       alive = false;
       break;
     }
-    mark();  // head barrier
-    zero(acc_hk, T.zf0, T.zf1);
-    for (int i = t; i < C; i += kDT) PV[i] = XB[i] + __ldcg(acc_fo + i);
-    csync();
-    layer_norm(TV, PV, a.lnout_w, a.lnout_b, nullptr);
-    build(0, C, [&](int i) { return f4(TV, i); });
-    mark();  // head prep done
-    {
-      const XDigits x1 = digits_at(0, C);
-      run_units(T.r[4], &x1, 0, logits, a.d.V);
+    d_mark(a, c);  // head barrier
+    d_zero(acc_hk, T.zf0, T.zf1);
+        if (fused) {
+      DLnMix q{};
+      q.xs = XB;
+      q.add = acc_fo;
+      q.w = a.lnout_w;
+      q.b = a.lnout_b;
+      q.nmix = 1;
+      q.ln = TV;
+      d_ln_mix<LFK>(a, c, q, dig, 0);
+    } else {
+#pragma unroll 1
+      for (int i = t; i < C; i += kDT) PV[i] = XB[i] + __ldcg(acc_fo + i);
+      d_csync();
+      d_layer_norm(TV, PV, a.lnout_w, a.lnout_b, C, nullptr, red);
+      d_build<LFK>(DSrc{1, TV, nullptr, nullptr}, C, dig);
     }
-    mark();  // head done
-    if (!gsync()) {
+    d_mark(a, c);  // head prep done
+    d_units<LFK>(a, c, T.r[4], dig, 0, C, 0, logits, a.d.V);
+    d_mark(a, c);  // head done
+    if (!d_gsync(a, c)) {
       alive = false;
       break;
     }
-    zero(acc_fo, T.zc0, T.zc1);
-    {
-      float best = -INFINITY;
-      int besti = 0x7fffffff;
-      for (int i = T.zv0 + t; i < T.zv1; i += kDT) {
-        const float v = __ldcg(logits + i);
-        if (v > best) {
-          best = v;
-          besti = i;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
-        if (ov > best || (ov == best && oi < besti)) {
-          best = ov;
-          besti = oi;
-        }
-      }
-      if (lane == 0) {
-        s_bv[warp] = best;
-        s_bi[warp] = besti;
-      }
-      csync();
-      if (t == 0) {
-        float cb = -INFINITY;
-        int ci = 0x7fffffff;
-        for (int w = 0; w < kDW; ++w)
-          if (s_bv[w] > cb || (s_bv[w] == cb && s_bi[w] < ci)) {
-            cb = s_bv[w];
-            ci = s_bi[w];
-          }
-        a.b.amax_v[bx] = cb;
-        a.b.amax_i[bx] = ci;
-      }
-    }
-    if (!gsync()) {
+    d_zero(acc_fo, T.zc0, T.zc1);
+    d_argmax_part(a, T, s_bv, s_bi);
+    if (!d_gsync(a, c)) {
       alive = false;
       break;
     }
-    if (t < 32) {
-      float gb = -INFINITY;
-      int gi = 0x7fffffff;
-      for (int c = lane; c < G; c += 32) {
-        const float v = __ldcg(a.b.amax_v + c);
-        const int i = __ldcg(a.b.amax_i + c);
-        if (v > gb || (v == gb && i < gi)) {
-          gb = v;
-          gi = i;
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, gb, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
-        if (ov > gb || (ov == gb && oi < gi)) {
-          gb = ov;
-          gi = oi;
-        }
-      }
-      if (t == 0) s_tok = gi == 0x7fffffff ? 0 : gi;
-    }
-    csync();
-    tok = s_tok;
+    tok = d_argmax_all(a, &s_tok);
     if (bx == 0 && t == 0) {
       a.b.hist[step % a.d.hist_cap] = tok;
       *a.b.tok = tok;

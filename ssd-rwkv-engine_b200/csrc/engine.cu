@@ -981,7 +981,6 @@ bool plan_decode(rwkvb_engine* e) {
   a.b = e->b;
   a.d = d;
   a.spin_limit = 1u << 22;
-  a.pf_dist = (e->flags & 0x100u) ? e->pf_dist * 4 : 0;  // L2 prefetch stages (explicit: 4 x the flag's distance)
   const PackedView& E = e->emb;
   a.emb_fast = E.kind == RWKVB_KIND_SG8 && E.lg >= 4 && d.C % (int)E.group == 0 && ((d.C >> E.lg) % 2) == 0 &&
                aligned16(E.payload) && aligned16(E.meta);
@@ -1002,6 +1001,7 @@ int launch_persistent(rwkvb_engine* e, int ntok, int mode, int first_tok, const 
   a.gbar = e->b.ticket;  // the argmax ticket word doubles as the grid-barrier counter here
   a.trace = e->dtrace;
   a.trace_cap = e->trace_cap;
+  if (e->dtrace) cudaMemsetAsync(e->dtrace + 2 * (size_t)e->trace_cap, 0, sizeof(unsigned long long) * 2 * (size_t)e->trace_cap, s);
   cudaError_t err = cudaMemsetAsync(a.gbar, 0, sizeof(unsigned), s);
   if (err != cudaSuccess) return cuda_status(err);
   void* args[] = {&a};
@@ -1132,7 +1132,7 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
     st = cuda_status(cudaMemcpy(e->dlayers, e->layers.data(), sizeof(LayerDev) * (size_t)L, cudaMemcpyHostToDevice));
   if (st == RWKVB_OK && (flags & 0x8u)) {
     e->trace_cap = 1 << 16;
-    if (cudaMalloc((void**)&e->dtrace, sizeof(unsigned long long) * 2 * (size_t)e->trace_cap) != cudaSuccess) {
+    if (cudaMalloc((void**)&e->dtrace, sizeof(unsigned long long) * 4 * (size_t)e->trace_cap) != cudaSuccess) {
       cudaGetLastError();
       st = RWKVB_EALLOC;
     }
@@ -1294,7 +1294,7 @@ extern "C" int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out) {
 extern "C" int rwkvb_engine_trace(rwkvb_engine* e, uint64_t* out, int32_t cap, int32_t* n_out) {
   if (!e || !out || cap <= 0 || !n_out) return RWKVB_EARG;
   if (!e->dtrace) return RWKVB_EUNSUPPORTED;
-  const int n = cap < 2 * e->trace_cap ? cap : 2 * e->trace_cap;
+  const int n = cap < 4 * e->trace_cap ? cap : 4 * e->trace_cap;
   const int st = cuda_status(cudaMemcpy(out, e->dtrace, sizeof(uint64_t) * (size_t)n, cudaMemcpyDeviceToHost));
   *n_out = n;
   return st;

@@ -59,70 +59,73 @@ struct XDigits {
   float* xsum;
 };
 
+// Digits of one item (x[8 it .. 8 it + 8) held in v) into X.  All 32 lanes of
+// the warp call it together (shuffles): the flush-group maximum and sum (FG =
+// 32 << lfk columns = 4 << lfk items on adjacent lanes) are reduced across
+// lanes; `act` = this lane holds a real item.
+__device__ __forceinline__ void emit_digits(const float (&v)[8], int it, bool act, int lfk, const XDigits& X) {
+  const int gl = 4 << lfk;
+  float m = 0.f, sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    m = fmaxf(m, fabsf(v[u]));
+    sum += v[u];
+  }
+  for (int o = 1; o < gl; o <<= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  if (!act) return;
+  int e = 0;
+  if (m > 0.f) frexpf(m, &e);  // m = frac * 2^e, frac in [0.5, 1): |x| * 2^-e < 1
+  const float inv = ldexpf(127.0f, -e);  // exact
+  if ((it & (gl - 1)) == 0) {
+    X.xc[it >> (lfk + 2)] = ldexpf(1.0f, e) / 127.0f;
+    X.xsum[it >> (lfk + 2)] = sum;
+  }
+  int d0[8], d1[8], d2[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const float y0 = v[u] * inv;
+    const float x0 = rintf(y0);
+    const float y1 = (y0 - x0) * 254.0f;
+    const float x1 = rintf(y1);
+    const float x2 = rintf((y1 - x1) * 254.0f);
+    d0[u] = (int)x0;
+    d1[u] = (int)x1;
+    d2[u] = (int)x2;
+  }
+  const int s = it >> 2, t = it & 3;
+  X.xd[s * 12 + t] = make_uint2(pack_s8x4(d0[0], d0[1], d0[2], d0[3]), pack_s8x4(d0[4], d0[5], d0[6], d0[7]));
+  X.xd[s * 12 + 4 + t] = make_uint2(pack_s8x4(d1[0], d1[1], d1[2], d1[3]), pack_s8x4(d1[4], d1[5], d1[6], d1[7]));
+  X.xd[s * 12 + 8 + t] = make_uint2(pack_s8x4(d2[0], d2[1], d2[2], d2[3]), pack_s8x4(d2[4], d2[5], d2[6], d2[7]));
+}
+
 // Build the digit form of x[0..K): item it = (k-step it / 4, quarter it % 4)
 // covers x[8 it .. 8 it + 8); thread ct of the `nthreads` consumers takes
-// items ct, ct + nthreads, ... (at most 8 passes), issuing every pass's loads
-// (get4(i) = x[i..i+4), i % 4 == 0) before any arithmetic.  The flush-group
-// maximum and sum (FG = 32 << lfk columns = 4 << lfk items, on adjacent
-// lanes) are reduced with shuffles.  K % FG == 0, K / 8 <= 8 * nthreads,
-// nthreads % 32 == 0.  Ends with the consumer barrier `bar_id`.
+// items ct, ct + nthreads, ...; the loads of the next item are in flight while
+// the current one is converted (get4(i) = x[i..i+4), i % 4 == 0).  The
+// flush-group maximum and sum (FG = 32 << lfk columns = 4 << lfk items, on
+// adjacent lanes) are reduced with shuffles.  K % FG == 0, nthreads % 32 == 0.
+// Ends with the consumer barrier `bar_id`.
 template <class Get4>
 __device__ __forceinline__ void build_digits(int K, int lfk, Get4 get4, XDigits X, int ct, int nthreads, int bar_id) {
-  const int items = K >> 3, gl = 4 << lfk;
-  const int npass = (items + nthreads - 1) / nthreads;
-  float4 va[8], vb[8];
-#pragma unroll
-  for (int p = 0; p < 8; ++p) {
-    const int it = p * nthreads + ct;
-    va[p] = vb[p] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (p < npass && it < items) {
-      va[p] = get4(it * 8);
-      vb[p] = get4(it * 8 + 4);
-    }
+  const int items = K >> 3;
+  float4 na = make_float4(0.f, 0.f, 0.f, 0.f), nb = na;
+  if (ct < items) {
+    na = get4(ct * 8);
+    nb = get4(ct * 8 + 4);
   }
-#pragma unroll
-  for (int p = 0; p < 8; ++p) {
-    if (p < npass) {
-      const int it = p * nthreads + ct;
-      const float v[8] = {va[p].x, va[p].y, va[p].z, va[p].w, vb[p].x, vb[p].y, vb[p].z, vb[p].w};
-      float m = 0.f, sum = 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        m = fmaxf(m, fabsf(v[u]));
-        sum += v[u];
-      }
-      for (int o = 1; o < gl; o <<= 1) {
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      }
-      if (it < items) {
-        int e = 0;
-        if (m > 0.f) frexpf(m, &e);  // m = frac * 2^e, frac in [0.5, 1): |x| * 2^-e < 1
-        const float inv = ldexpf(127.0f, -e);  // exact
-        if ((ct & (gl - 1)) == 0) {
-          X.xc[it >> (lfk + 2)] = ldexpf(1.0f, e) / 127.0f;
-          X.xsum[it >> (lfk + 2)] = sum;
-        }
-        int d0[8], d1[8], d2[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float y0 = v[u] * inv;
-          const float x0 = rintf(y0);
-          const float y1 = (y0 - x0) * 254.0f;
-          const float x1 = rintf(y1);
-          const float x2 = rintf((y1 - x1) * 254.0f);
-          d0[u] = (int)x0;
-          d1[u] = (int)x1;
-          d2[u] = (int)x2;
-        }
-        const int s = it >> 2, t = it & 3;
-        X.xd[s * 12 + t] = make_uint2(pack_s8x4(d0[0], d0[1], d0[2], d0[3]), pack_s8x4(d0[4], d0[5], d0[6], d0[7]));
-        X.xd[s * 12 + 4 + t] =
-            make_uint2(pack_s8x4(d1[0], d1[1], d1[2], d1[3]), pack_s8x4(d1[4], d1[5], d1[6], d1[7]));
-        X.xd[s * 12 + 8 + t] =
-            make_uint2(pack_s8x4(d2[0], d2[1], d2[2], d2[3]), pack_s8x4(d2[4], d2[5], d2[6], d2[7]));
-      }
+#pragma unroll 1
+  for (int base = 0; base < items; base += nthreads) {
+    const int it = base + ct;
+    const float v[8] = {na.x, na.y, na.z, na.w, nb.x, nb.y, nb.z, nb.w};
+    const int nx = it + nthreads;
+    if (nx < items) {
+      na = get4(nx * 8);
+      nb = get4(nx * 8 + 4);
     }
+    emit_digits(v, it, it < items, lfk, X);
   }
   bar_sync(bar_id, nthreads);
 }

@@ -149,14 +149,24 @@ class B200Engine:
         st = stream if stream is not None else torch.cuda.current_stream(self.device)
         return st.cuda_stream
 
-    def phase_trace(self) -> np.ndarray:
-        """Phase timestamps of the last persistent launch, ``[2, 65536]`` ns
-        (first CTA, last CTA); zeros where nothing was recorded."""
-        cap = 2 * 65536
+    def _trace_raw(self) -> np.ndarray:
+        cap = 4 * 65536
         buf = (ctypes.c_uint64 * cap)()
         n = ctypes.c_int32()
         native.check(self.lib.rwkvb_engine_trace(self._h, buf, cap, ctypes.byref(n)), "rwkvb_engine_trace")
-        return np.frombuffer(buf, dtype=np.uint64, count=n.value).reshape(2, -1).copy()
+        return np.frombuffer(buf, dtype=np.uint64, count=n.value).copy()
+
+    def phase_trace(self) -> np.ndarray:
+        """Phase timestamps of the last persistent launch, ``[2, 65536]`` ns
+        (first CTA, last CTA); zeros where nothing was recorded."""
+        return self._trace_raw()[: 2 * 65536].reshape(2, -1)
+
+    def ring_trace(self) -> np.ndarray:
+        """Ring events of the first CTA in the last persistent launch,
+        ``[stages, 3]`` ns: producer issue, consumer wait end, consumer release."""
+        raw = self._trace_raw()[2 * 65536:]
+        n = len(raw) // 3
+        return raw[: 3 * n].reshape(n, 3)
 
     # --------------------------------------------------------------- state
     def reset(self, stream=None) -> None:
