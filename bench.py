@@ -10,6 +10,12 @@ Multi-GPU (torchrun): decode does not shard at batch 1 — every rank runs an
 independent replica (its own model copy and session), ``scaling: "weak"``;
 ``value`` = tokens decoded by all ranks / max-over-ranks device time.
 
+``e2e`` is the same metric through the drop-in plugin
+(``create_backend("cuda_b200").decode_greedy`` with a token callback): every
+token's argmax is read back to the host and the token is sent to the device
+through the C ABI before the next step.  The timed regions sit inside NVTX
+ranges ``timed`` and ``e2e``.
+
 ``--impl reference`` times the reference's own C kernels (built from its
 sources into ``oracle/_ref``) driving the packed RWKV-7 forward on the host
 cores, on the same workload and metric (rank 0 only).
@@ -43,6 +49,21 @@ def _env_int(k: str, d: int) -> int:
         return int(os.environ.get(k, d))
     except ValueError:
         return d
+
+
+def _nvtx_push(name: str) -> None:
+    """Named range around a timed region, so a profiler can select its launches."""
+    try:
+        torch.cuda.nvtx.range_push(name)
+    except Exception:
+        pass
+
+
+def _nvtx_pop() -> None:
+    try:
+        torch.cuda.nvtx.range_pop()
+    except Exception:
+        pass
 
 
 def _peaks() -> tuple[float, str]:
@@ -207,7 +228,6 @@ def main() -> None:
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="2.9b", choices=["tiny", "0.1b", "2.9b", "7.2b", "2.9b-l4"])
     ap.add_argument("--policy", default="sg8", choices=["sg8", "lut2"])
-    ap.add_argument("--prefetch", type=int, default=None)
     ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--ref-budget-s", type=float, default=60.0)
@@ -237,13 +257,19 @@ def main() -> None:
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    from rwkv_b200.engine import B200Engine
+    from rwkv_b200.backend import PackProvider, create_backend
 
     pack = synth.make_pack_streaming(shape, SEED + rank, dev, policy=args.policy)
     bpt = bytes_per_token(pack, shape)
-    eng = B200Engine(pack, device=local, prefetch_distance=args.prefetch)
+    # the engine under test is the one the drop-in plugin builds from a provider
+    backend = create_backend("cuda_b200")
+    backend.load_pack(None, f"cuda:{local}")
+    provider = PackProvider(pack)
+    backend.prepare_provider(provider)
+    eng = backend._engine
     cpu_pack = pack if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     del pack
+    provider.pack, provider._fused = {}, {}
     torch.cuda.empty_cache()
 
     stream = torch.cuda.current_stream(dev)
@@ -264,10 +290,12 @@ def main() -> None:
         time.sleep(0.3)
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    _nvtx_push("timed")
     t0.record(stream)
     eng.decode_greedy_async(nxt, args.steps, out)
     t1.record(stream)
     torch.cuda.synchronize(dev)
+    _nvtx_pop()
     ms = t0.elapsed_time(t1)
     clk = clocks.stop() if rank == 0 else {}
     if world > 1:
@@ -279,24 +307,25 @@ def main() -> None:
     value = total_tokens / (ms / 1e3)
     ms_step = ms / args.steps
 
-    # end to end through the host API: every step copies its input token
-    # host->device and its argmax device->host (pinned), synchronising per token
+    # end to end through the plugin: CudaB200Backend.decode_greedy with a
+    # per-token callback, so every step reads its argmax back to the host
+    # (int64, 8 bytes) and sends the token to the device through the C ABI
+    # (int32, 4 bytes) before the next step starts
     e2e_steps = min(args.e2e_steps, args.steps)
-    tok_h = torch.empty(1, dtype=torch.int32, pin_memory=True)
-    tok_h[0] = nxt
+    state = backend.prefill_tokens(prompt)
+    emitted: list[int] = []
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    _nvtx_push("e2e")
     e0.record(stream)
-    for _ in range(e2e_steps):
-        eng.forward([int(tok_h[0])])
-        am = torch.argmax(eng.logits).to(torch.int32)
-        tok_h.copy_(am.reshape(1), non_blocking=True)
-        stream.synchronize()
+    backend.decode_greedy(state, provider, e2e_steps, None, token_callback=emitted.append)
     e1.record(stream)
     torch.cuda.synchronize(dev)
+    _nvtx_pop()
+    assert len(emitted) == e2e_steps
     e2e_ms = e0.elapsed_time(e1)
     if world > 1:
         tt = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
@@ -307,11 +336,13 @@ def main() -> None:
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = bpt / (ms_step / 1e3) / 1e9
+        # DRAM bytes of the launch from the committed ncu capture (per token x
+        # tokens of this launch), null when no capture exists for this workload
         traffic = None
         tf = REPO / "profiles" / f"decode_{args.config}_{args.policy}_traffic.json"
         if tf.is_file():
             try:
-                traffic = json.loads(tf.read_text()).get("dram_bytes_per_step")
+                traffic = int(json.loads(tf.read_text())["dram_bytes_per_step"]) * args.steps
             except Exception:
                 traffic = None
         res = {
@@ -329,18 +360,21 @@ def main() -> None:
             "gpu_launches": (eng.launches_per_step * args.steps + 1) if eng.launches_per_step
             else (args.steps + 65535) // 65536,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "what": "whole token step (one CUDA-graph launch): algorithmic bytes/token "
-                                 f"{bpt} / device time per token; peak {peak_kind}"},
-            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
-                    "steps": e2e_steps, "how": "B200Engine.forward(host token) + argmax D2H per token"},
+                         "frac": achieved / peak, "traffic": traffic, "algorithmic_bytes": bpt * args.steps,
+                         "what": f"decode_kernel, one persistent launch decoding {args.steps} tokens: "
+                                 f"algorithmic bytes/token {bpt} x tokens / CUDA-event duration of the launch; "
+                                 f"peak: {peak_kind} HBM copy bandwidth"},
+            "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8,
+                    "steps": e2e_steps,
+                    "how": "cuda_b200 plugin decode_greedy with a token callback: per token argmax read to the "
+                           "host, token sent back through rwkvb_engine_forward (one persistent launch per token)"},
             "clocks": clk,
         }
         if cpu_pack is not None:
-            eng.close()
+            backend.close()
             res["cpu_baseline"] = cpu_baseline(cpu_pack, shape, args)
         print(json.dumps(res), flush=True)
-    eng.close()
+    backend.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
