@@ -142,6 +142,19 @@ int rwkvb_cmix_gemv_f32(float* y, const rwkvb_packed* key, const rwkvb_packed* v
 int rwkvb_cmix_gemv_f32_noalloc(float* y, const rwkvb_packed* key, const rwkvb_packed* value,
                                 const float* x, void* stream);
 
+/* Batched SG8 product on the tcgen05 tensor cores:
+ *   y[b][n] = sum_k W[n][k] x[b][k],   x [batch][cols] fp32, y [batch][rows] fp32
+ * for 1 <= batch <= 64.  W: SG8 with group 64 or 128, rows and cols multiples
+ * of 128, code payload 16-byte aligned (else RWKVB_EUNSUPPORTED).  Integer MMA
+ * on the raw codes and a 3-digit split of x (error <= 6.2e-8 of each group's
+ * largest |x|), per-group fp32 scaling, deterministic split-K reduction.
+ * `err_word` (device int, may be NULL) gets RWKVB_ETIMEOUT's flag bit if a
+ * bounded device wait gave up.  Replaces the batched (2-D x) branch of
+ * lut2_linear_forward (rwkv_ssd/runtime/lut_gemm_fused.py:1820-1851), which
+ * decodes W and calls torch.nn.functional.linear. */
+int rwkvb_gemm_sg8_f32(float* y, const rwkvb_packed* w, const float* x, int32_t batch,
+                       int32_t* err_word, void* stream);
+
 /* WKV7 recurrent state update for `batch` x `n_head` heads of size N = head_size (64):
  *   d = decay(w);  S = S * diag(d) + (S @ -kk) (kk*a)^T + v k^T;  y = S @ r
  * state [batch][n_head][N][N] fp32 (value index major), vectors [batch][n_head*N].

@@ -1,0 +1,378 @@
+// Batched SG8 GEMM on the 5th-generation tensor cores (tcgen05, kind::i8):
+//     Y[b][n] = sum_k W[n][k] x[b][k]      (b < nb <= 64 sessions)
+// for the batched decode step (r/k/v/o projections, FFN key/value, head).
+//
+// Operands, all exact integers:
+//   A = the raw u8 weight codes of a 128-row x 128-column tile (TMA, 128-byte
+//       swizzle), no conversion;
+//   B = the activations as three unsigned 8-bit digit rows per session plus a
+//       row of ones: per flush group f (FG = weight group, 64 or 128 columns)
+//           x = c_f (X0 + X1/254 + X2/254^2),  c_f = 2^e_f / 127,
+//       X_i in [-127, 127] stored as X_i + 127 in [0, 254]; rows
+//       [0,bp) = digit 0, [bp,2bp) = digit 1, [2bp,3bp) = digit 2, 3bp = ones.
+// The MMA (M 128, N = digit rows) accumulates D'_i = sum q (X_i + 127) and
+// Q = sum q (the ones row) in TMEM; per flush group the epilogue recovers
+// D_i = D'_i - 127 Q exactly and adds
+//     min * sum_x + d * c_f * (D0 + D1/254 + D2/254^2),   d = (max - min) / 255
+// which is the per-group algebra of the reference's SG8 row dot
+// (rwkv_ssd/native/lut2_gather.c:344-381) for every session at once.
+// |D_i| <= 128 * 255 * 127 < 2^22, so a D_i becomes a float exactly through
+// the 1.5 * 2^23 bias (one integer add and one float subtract).
+//
+// Work split: the (tile, 128-column stage) pairs of all matrices of a launch
+// are numbered in order and every CTA takes a contiguous, equal share, so
+// each SM streams the same bytes.  A CTA writes the partial sums of each tile
+// it touches into piece slot (cta - first cta of the tile); consumers add the
+// pieces of a tile in slot order (deterministic).
+//
+// Roles (10 warps): warp 0 lane 0 issues the TMA loads into a ring of stages;
+// warp 1 allocates TMEM (two accumulators of up to 256 columns) and lane 0
+// issues the MMAs, one commit per flush group to the accumulator's "full"
+// barrier and one per stage to the slot's "empty" barrier; warps 2..9 are the
+// epilogue (TMEM lane quarter = warp % 4, sessions split in two halves).
+// Every wait is bounded: on a limit the CTA sets the error word, drains the
+// copies it issued and returns.
+#pragma once
+
+#include <cuda.h>
+
+#include "imma.cuh"
+#include "tma.cuh"
+#include "umma.cuh"
+
+namespace rwkvb {
+
+constexpr int kBgWarps = 10;
+constexpr int kBgThreads = kBgWarps * 32;
+constexpr int kBgMaxMats = 4;
+constexpr int kBgMaxSessions = 64;
+constexpr int kBgTileBytes = 128 * 128;  // A stage: 128 rows x 128 codes
+constexpr int kBgTmemCols = 512;
+constexpr int kBgAccStride = 256;        // TMEM columns between the two accumulators
+constexpr int kBgMaxStages = 6;
+constexpr int kBgBias = 0x4B400000;      // bits of 1.5 * 2^23
+constexpr float kBgBiasF = 12582912.0f;  // 1.5 * 2^23
+
+struct BgMat {
+  const float2* pairs;  // (min, max) per (row, group): [rows][k / group]
+  float* out;           // partial sums [pieces][nb][rows]
+  int rows, k;          // N, K (multiples of 128)
+  int lg;               // log2(group): 6 or 7
+  int digits;           // digit matrix (B operand) index
+  int tiles;            // rows / 128
+  int stage0;           // first global stage index of this matrix
+};
+
+struct BgArgs {
+  CUtensorMap amap[kBgMaxMats];   // codes {k, rows}, box {128, 128}, 128-byte swizzle
+  CUtensorMap bmap[kBgMaxMats];   // digit rows {k, nrows}, box {128, nrows}, 128-byte swizzle
+  BgMat mat[kBgMaxMats];
+  const float2* cs[kBgMaxMats];   // per digit matrix: (c_f, sum_x) [k / group][bp]
+  int nmat;
+  int total;                      // stages over all matrices
+  int nb, bp, nrows;              // sessions, padded sessions, digit rows (= MMA N)
+  int stages;                     // ring slots
+  uint32_t idesc;
+  uint32_t spin_limit;
+  int* err;
+};
+
+// CTA owning global stage x when `total` stages are split evenly over n CTAs
+// (CTA c owns [floor(c total / n), floor((c+1) total / n))).
+__host__ __device__ __forceinline__ int bg_cta_of(long long x, int total, int n) {
+  return (int)(((x + 1) * (long long)n - 1) / total);
+}
+__host__ __device__ __forceinline__ int bg_range_lo(int c, int total, int n) {
+  return (int)(((long long)c * total) / n);
+}
+
+// One segment: stages [s0, s1) of tile t of matrix m, piece p.
+struct BgSeg {
+  int m, t, s0, s1, p;
+};
+
+// Next segment of [x, hi) (x < hi), in stage order.
+__device__ __forceinline__ BgSeg bg_segment(const BgArgs& a, int x, int hi) {
+  int m = 0;
+#pragma unroll 1
+  while (m + 1 < a.nmat && x >= a.mat[m + 1].stage0) ++m;
+  const BgMat& M = a.mat[m];
+  const int G = M.k >> 7;
+  const int local = x - M.stage0;
+  BgSeg s;
+  s.m = m;
+  s.t = local / G;
+  s.s0 = local - s.t * G;
+  const int tile_hi = M.stage0 + (s.t + 1) * G;
+  s.s1 = s.s0 + (min(hi, tile_hi) - x);
+  s.p = (int)blockIdx.x - bg_cta_of(M.stage0 + (long long)s.t * G, a.total, gridDim.x);
+  return s;
+}
+
+// Bounded wait by lane 0 of the calling warp, result broadcast to the warp
+// (the whole warp calls it, so its lanes stay converged).
+__device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, const BgArgs& a, volatile int* abort_flag) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) {
+    if (!*abort_flag) {
+      ok = mbar_wait_bounded(bar, parity, a.spin_limit) ? 1 : 0;
+      if (!ok) {
+        atomicOr(a.err, kErrTimeout);
+        *abort_flag = 1;
+      }
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__global__ void __launch_bounds__(kBgThreads, 1) bgemm_kernel(const __grid_constant__ BgArgs a) {
+  extern __shared__ __align__(1024) uint8_t bg_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bg_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stage_bytes = kBgTileBytes + a.nrows * 128;
+  __shared__ __align__(8) uint64_t full[kBgMaxStages], empty[kBgMaxStages], tfull[2], tempty[2], done_bar;
+  __shared__ uint32_t s_tbase;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lo = bg_range_lo(blockIdx.x, a.total, gridDim.x);
+  const int hi = bg_range_lo(blockIdx.x + 1, a.total, gridDim.x);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);
+    }
+    mbar_init(&done_bar, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tbase, kBgTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = s_tbase;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    uint32_t use = 0;
+    const uint32_t bytes = (uint32_t)stage_bytes;
+    for (int x = lo; x < hi;) {
+      const BgSeg sg = bg_segment(a, x, hi);
+      const BgMat& M = a.mat[sg.m];
+      for (int st = sg.s0; st < sg.s1; ++st, ++use) {
+        const uint32_t slot = use % a.stages, n = use / a.stages;
+        if (!bg_wait(&empty[slot], (n & 1) ^ 1, a, &s_abort)) goto producer_drain;
+        if (lane == 0) {
+          uint8_t* sa = smem + slot * stage_bytes;
+          mbar_expect_tx(&full[slot], bytes);
+          tma_load_2d(sa, &a.amap[sg.m], st * 128, sg.t * 128, &full[slot]);
+          tma_load_2d(sa + kBgTileBytes, &a.bmap[M.digits], st * 128, 0, &full[slot]);
+        }
+        __syncwarp();
+      }
+      x += sg.s1 - sg.s0;
+    }
+  producer_drain:
+    // the copies still in flight are among the last min(stages, use) issues
+    if (lane == 0)
+      for (uint32_t u = use > (uint32_t)a.stages ? use - a.stages : 0; u < use; ++u)
+        mbar_wait_bounded(&full[u % a.stages], (u / a.stages) & 1, a.spin_limit);
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    uint32_t use = 0, fl = 0;
+    for (int x = lo; x < hi;) {
+      const BgSeg sg = bg_segment(a, x, hi);
+      const BgMat& M = a.mat[sg.m];
+      const int nfl = 128 >> M.lg;  // flush groups per stage (1 or 2)
+      const int kpf = 4 / nfl;      // 32-column k-steps per flush group
+      for (int st = sg.s0; st < sg.s1; ++st, ++use) {
+        const uint32_t slot = use % a.stages, n = use / a.stages;
+        if (!bg_wait(&full[slot], n & 1, a, &s_abort)) goto mma_done;
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + slot * stage_bytes);
+        const uint32_t sb = sa + kBgTileBytes;
+        for (int f = 0; f < nfl; ++f, ++fl) {
+          const uint32_t tb = fl & 1;
+          if (!bg_wait(&tempty[tb], ((fl >> 1) & 1) ^ 1, a, &s_abort)) goto mma_done;
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t dt = tbase + tb * kBgAccStride;
+            for (int j = 0; j < kpf; ++j) {
+              const uint32_t ko = (uint32_t)((f * kpf + j) * 32);
+              umma_u8(dt, sdesc_k128(sa + ko), sdesc_k128(sb + ko), a.idesc, j > 0 ? 1u : 0u);
+            }
+            umma_commit(&tfull[tb]);
+          }
+          __syncwarp();
+        }
+        if (lane == 0) umma_commit(&empty[slot]);
+        __syncwarp();
+      }
+      x += sg.s1 - sg.s0;
+    }
+  mma_done:
+    // every MMA issued so far has completed once done_bar's phase 0 ends
+    if (lane == 0) {
+      umma_commit(&done_bar);
+      mbar_wait_bounded(&done_bar, 0, a.spin_limit);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2, q4 = warp & 3, half = ew >> 2;
+    const int nch = a.bp >> 4;              // 16-session chunks
+    const int c0 = half ? (nch + 1) >> 1 : 0;
+    const int c1 = half ? nch : (nch + 1) >> 1;
+    const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16);
+    uint32_t fl = 0;
+    for (int x = lo; x < hi;) {
+      const BgSeg sg = bg_segment(a, x, hi);
+      const BgMat& M = a.mat[sg.m];
+      const int row = sg.t * 128 + q4 * 32 + lane;
+      const int gpr = M.k >> M.lg;
+      const float2* prow = M.pairs + (size_t)row * gpr;
+      const float2* csm = a.cs[M.digits];
+      const int nfl = 128 >> M.lg;
+      float acc[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+      for (int st = sg.s0; st < sg.s1; ++st) {
+        for (int f = 0; f < nfl; ++f, ++fl) {
+          const int g = st * nfl + f;
+          const float2 pr = __ldg(prow + g);
+          const uint32_t tb = fl & 1;
+          if (!bg_wait(&tfull[tb], (fl >> 1) & 1, a, &s_abort)) goto epi_done;
+          tc_fence_after();
+          const uint32_t ta = tl + tb * kBgAccStride;
+          const int q = (int)tmem_ld1_sync(ta + 3 * a.bp);
+          const int kq = kBgBias - 127 * q;
+          const float dg = (pr.y - pr.x) * kInv255, mn = pr.x;
+          const float2* csg = csm + (size_t)g * a.bp;
+#pragma unroll
+          for (int ci = 0; ci < 2; ++ci) {
+            const int cc = c0 + ci;
+            if (cc < c1) {
+              uint32_t d0[16], d1[16], d2[16];
+              tmem_ld16x3_sync(ta + cc * 16, ta + a.bp + cc * 16, ta + 2 * a.bp + cc * 16, d0, d1, d2);
+#pragma unroll
+              for (int s = 0; s < 16; ++s) {
+                const float2 cx = csg[cc * 16 + s];
+                const float f0 = __int_as_float((int)d0[s] + kq) - kBgBiasF;
+                const float f1 = __int_as_float((int)d1[s] + kq) - kBgBiasF;
+                const float f2 = __int_as_float((int)d2[s] + kq) - kBgBiasF;
+                const float t = fmaf(fmaf(f2, kInv254, f1), kInv254, f0);
+                acc[ci * 16 + s] = fmaf(dg * cx.x, t, fmaf(mn, cx.y, acc[ci * 16 + s]));
+              }
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[tb]);
+        }
+      }
+      {
+        float* out = M.out + (size_t)sg.p * a.nb * M.rows + row;
+#pragma unroll
+        for (int ci = 0; ci < 2; ++ci) {
+          const int cc = c0 + ci;
+          if (cc < c1) {
+#pragma unroll
+            for (int s = 0; s < 16; ++s) {
+              const int b = cc * 16 + s;
+              if (b < a.nb) out[(size_t)b * M.rows] = acc[ci * 16 + s];
+            }
+          }
+        }
+      }
+      x += sg.s1 - sg.s0;
+    }
+  epi_done:;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kBgTmemCols);
+  }
+}
+
+// Digit rows of nb input vectors (row b of x at x + b * ldx, k columns) for
+// flush groups of 1 << lfk columns (64 or 128): one warp per (session, group).
+__global__ void __launch_bounds__(256) bg_digits_kernel(uint8_t* dig, float2* cs, const float* x, int ldx, int k,
+                                                        int nb, int bp, int lfk) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int G = k >> lfk;
+  if (gw >= nb * G) return;
+  const int b = gw / G, g = gw - b * G;
+  const int per = 1 << (lfk - 5);  // 2 or 4 values per lane
+  const float* src = x + (size_t)b * ldx + ((size_t)g << lfk) + lane * per;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (per == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(src);
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  } else {
+    const float2 t = *reinterpret_cast<const float2*>(src);
+    v[0] = t.x, v[1] = t.y;
+  }
+  float m = 0.f, sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    m = fmaxf(m, fabsf(v[u]));
+    sum += v[u];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  }
+  int e = 0;
+  if (m > 0.f) frexpf(m, &e);  // |x| 2^-e < 1
+  const float inv = ldexpf(127.0f, -e);
+  uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float y0 = v[u] * inv;
+    const float x0 = rintf(y0);
+    const float y1 = (y0 - x0) * 254.0f;
+    const float x1 = rintf(y1);
+    const float x2 = rintf((y1 - x1) * 254.0f);
+    w0 |= (uint32_t)((int)x0 + 127) << (8 * u);
+    w1 |= (uint32_t)((int)x1 + 127) << (8 * u);
+    w2 |= (uint32_t)((int)x2 + 127) << (8 * u);
+  }
+  const size_t col = ((size_t)g << lfk) + lane * per;
+  if (per == 4) {
+    *reinterpret_cast<uint32_t*>(dig + (size_t)b * k + col) = w0;
+    *reinterpret_cast<uint32_t*>(dig + (size_t)(bp + b) * k + col) = w1;
+    *reinterpret_cast<uint32_t*>(dig + (size_t)(2 * bp + b) * k + col) = w2;
+  } else {
+    *reinterpret_cast<uint16_t*>(dig + (size_t)b * k + col) = (uint16_t)w0;
+    *reinterpret_cast<uint16_t*>(dig + (size_t)(bp + b) * k + col) = (uint16_t)w1;
+    *reinterpret_cast<uint16_t*>(dig + (size_t)(2 * bp + b) * k + col) = (uint16_t)w2;
+  }
+  if (lane == 0) cs[(size_t)g * bp + b] = make_float2(ldexpf(1.0f, e) / 127.0f, sum);
+}
+
+// y[b][n] = sum over the pieces of n's tile of part[p][b][n], in piece order.
+__global__ void bg_reduce_kernel(float* y, const float* part, int nb, int rows, int stage0, int G, int total,
+                                 int ncta) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nb * rows) return;
+  const int b = i / rows, n = i - b * rows;
+  const int t = n >> 7;
+  const long long first = stage0 + (long long)t * G;
+  const int np = bg_cta_of(first + G - 1, total, ncta) - bg_cta_of(first, total, ncta) + 1;
+  float s = 0.f;
+  for (int p = 0; p < np; ++p) s += part[((size_t)p * nb + b) * rows + n];
+  y[i] = s;
+}
+
+}  // namespace rwkvb

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 
 #include "rwkv_b200.h"
 
@@ -17,6 +19,7 @@ int device_sms();
 
 inline int cuda_status(cudaError_t e) {
   if (e == cudaSuccess) return RWKVB_OK;
+  if (std::getenv("RWKVB_DEBUG")) std::fprintf(stderr, "rwkvb: CUDA error %d: %s\n", (int)e, cudaGetErrorString(e));
   cudaGetLastError();  // clear a non-sticky error so the next call starts clean
   return e == cudaErrorMemoryAllocation ? RWKVB_EALLOC : RWKVB_ECUDA;
 }

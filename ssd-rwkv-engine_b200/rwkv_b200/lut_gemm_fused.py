@@ -83,6 +83,37 @@ def lut2_gemv(weight_blob, x: torch.Tensor, *, out_features: int, in_features: i
     return y
 
 
+def lut2_linear_forward(weight_blob, x: torch.Tensor, shape: tuple[int, ...]) -> torch.Tensor:
+    """``x @ W.T`` for a packed ``W [out, in]`` (``lut_gemm_fused.py:1820-1851``).
+
+    1-D ``x`` is one GEMV.  2-D ``x [batch, in]`` with an SG8 ``W`` (batch <= 64)
+    runs the tcgen05 batched product (``rwkvb_gemm_sg8_f32``); other 2-D cases
+    run one GEMV per row."""
+    if len(shape) != 2:
+        raise ValueError("lut2_linear_forward expects a 2-D weight shape")
+    out_f, in_f = int(shape[0]), int(shape[1])
+    if x.dim() == 1:
+        return lut2_gemv(weight_blob, x, out_features=out_f, in_features=in_f)
+    if x.dim() != 2 or x.shape[1] != in_f:
+        raise ValueError(f"x shape {tuple(x.shape)} does not match in_features {in_f}")
+    keep: list = []
+    w = _resident(weight_blob, out_f, in_f, keep)
+    nb = int(x.shape[0])
+    if w.codec == "sg8" and 1 <= nb <= 64 and out_f % 128 == 0 and in_f % 128 == 0:
+        xv = x.detach().to(device=_dev(), dtype=torch.float32).contiguous()
+        y = torch.empty((nb, out_f), dtype=torch.float32, device=_dev())
+        err = torch.zeros(1, dtype=torch.int32, device=_dev())
+        native.check(native.lib().rwkvb_gemm_sg8_f32(y.data_ptr(), ctypes.byref(w.desc), xv.data_ptr(), nb,
+                                                     err.data_ptr(), _stream()), "rwkvb_gemm_sg8_f32")
+        if int(err.item()) != 0:
+            native.check(native.RWKVB_ETIMEOUT, "rwkvb_gemm_sg8_f32 (device wait)")
+        return y
+    rows = [lut2_gemv(w, x[i], out_features=out_f, in_features=in_f) for i in range(nb)]
+    if keep:
+        torch.cuda.current_stream().synchronize()
+    return torch.stack(rows)
+
+
 def lut2_tmix_qkv_gemv_batched(blobs, xs, *, out_features: int, in_features: int):
     """Three attention projections (r, k, v) with distinct inputs in one launch."""
     if isinstance(xs, torch.Tensor):

@@ -101,6 +101,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_tmix_adapters_f32": (ctypes.c_int, [vp, vp, vp, vp, P(P(Packed)), P(vp), vp, ctypes.c_int, vp]),
         "rwkvb_cmix_gemv_f32": (ctypes.c_int, [vp, P(Packed), P(Packed), vp, vp]),
         "rwkvb_cmix_gemv_f32_noalloc": (ctypes.c_int, [vp, P(Packed), P(Packed), vp, vp]),
+        "rwkvb_gemm_sg8_f32": (ctypes.c_int, [vp, P(Packed), vp, i32, vp, vp]),
         "rwkvb_wkv7_f32": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_int, vp]),
         "rwkvb_engine_create": (ctypes.c_int, [P(ModelDesc), u32, P(vp)]),
