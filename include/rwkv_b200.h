@@ -253,6 +253,41 @@ int rwkvb_engine_trace(rwkvb_engine* e, uint64_t* out, int32_t cap, int32_t* n_o
 /* Kernel launches per token step (for launch accounting). */
 int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out);
 
+/* ------------------------------------------------------------------------------
+ * Batched decode: `batch` (1..64) independent sessions of one model advance one
+ * token per step together, every projection (r/k/v/o, FFN key/value, head) a
+ * tcgen05 batched GEMM (as rwkvb_gemm_sg8_f32), the adapters, WKV7, LayerNorms
+ * and argmax in small kernels; one step is a CUDA graph.  Per session the step
+ * is forward_block_packed for every layer + head + greedy argmax, as the
+ * reference runs it session by session (its batched path, rwkv7_batch, lives in
+ * the un-vendored ChatRWKV package).
+ * Requirements: every r/k/v/o/FFN/head matrix SG8 with one group size (64 or
+ * 128), n_embd, ffn and vocab multiples of 128; adapters and embedding any codec.
+ * ------------------------------------------------------------------------------ */
+typedef struct rwkvb_batch rwkvb_batch;
+
+/* flags: bit0 = run the step as plain launches (no CUDA graph). */
+int rwkvb_batch_create(const rwkvb_model_desc* desc, int32_t batch, uint32_t flags, rwkvb_batch** out);
+int rwkvb_batch_destroy(rwkvb_batch* e);
+
+/* Device state, per layer l and session b (each block as in rwkvb_engine_buffers):
+ *   att_x + (l*batch + b)*n_embd,  wkv + (l*batch + b)*n_head*N*N,  ffn_x + (l*batch + b)*n_embd;
+ * logits [batch][vocab] of the last step. */
+int rwkvb_batch_buffers(rwkvb_batch* e, float** att_x, float** wkv, float** ffn_x, float** logits);
+int rwkvb_batch_reset(rwkvb_batch* e, void* stream);
+
+/* One step: session b consumes tokens[b] (HOST array of `batch` ids). */
+int rwkvb_batch_forward(rwkvb_batch* e, const int32_t* tokens, void* stream);
+
+/* n greedy steps; step 0 consumes the argmax of the current logits of every
+ * session, step i > 0 the argmax of step i-1.  ids [n][batch] to HOST memory
+ * (synchronises) or device memory (_async, does not synchronise). */
+int rwkvb_batch_decode_greedy(rwkvb_batch* e, int32_t n, int32_t* out_tokens, void* stream);
+int rwkvb_batch_decode_greedy_async(rwkvb_batch* e, int32_t n, int32_t* out_tokens_dev, void* stream);
+
+/* Kernel launches per batched step. */
+int rwkvb_batch_launches_per_step(rwkvb_batch* e, int32_t* out);
+
 #ifdef __cplusplus
 }
 #endif

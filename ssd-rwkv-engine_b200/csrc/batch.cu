@@ -6,10 +6,13 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <new>
+#include <vector>
 
 #include "bgemm.cuh"
 #include "common.cuh"
 #include "internal.h"
+#include "wkv7.cuh"
 
 namespace rwkvb {
 
@@ -202,4 +205,967 @@ extern "C" int rwkvb_gemm_sg8_f32(float* y, const rwkvb_packed* w, const float* 
   if (part) cudaFreeAsync(part, s);
   cudaFreeAsync(dig, s);
   return st;
+}
+
+// ==========================================================================
+// Batched decode engine: nb <= 64 independent sessions of one packed RWKV-7
+// model advance one token per step together.  Every big projection is a
+// tcgen05 batched GEMM (bgemm.cuh); LayerNorms, token shift, digit rows, the
+// LoRA-style adapters, WKV7 and the argmax are small kernels around them.  One
+// step is captured as a CUDA graph and replayed.
+// Per layer (packed_block_forward.py:76-166, rwkv7_linear.py:125-435):
+//   in      x (+ folded FFN value pieces); ln1; six token-shift mixes; digit
+//           rows of the r/k/v inputs; fp32 w/a/g/v adapter inputs
+//   rkv     GEMM r, k, v
+//   adp1    first adapter stages x @ W1 (split over input rows) -> partials
+//   adpr    reduce the partials, tanh (w) / sigmoid (g)
+//   adp2    second adapter stages (mid @ W2)
+//   wkv     per (head, session): kk-normalize, decay, WKV7, GroupNorm, bonus, gate
+//   ydig    digit rows of the gated output
+//   o       GEMM output projection
+//   ffn     x + attention; ln2; mix; digit rows
+//   key     GEMM ffn key
+//   hdig    relu^2 and digit rows of the FFN hidden vector
+//   value   GEMM ffn value (folded into the next layer's input)
+// then ln_out, the head GEMM and a first-maximum argmax per session.
+// ==========================================================================
+namespace rwkvb {
+
+constexpr int kBtThreads = 256;
+constexpr int kBtAdpCols = 32;  // first-stage adapter columns per CTA
+constexpr int kBtAdpKc = 128;   // first-stage input rows per CTA
+
+struct BtPieces {
+  int stage0, G, total, ncta;
+};
+
+__device__ __forceinline__ int bt_npieces(const BtPieces& p, int n) {
+  const long long f = p.stage0 + (long long)(n >> 7) * p.G;
+  return bg_cta_of(f + p.G - 1, p.total, p.ncta) - bg_cta_of(f, p.total, p.ncta) + 1;
+}
+
+// Sum of the pieces of element (b, n) of a GEMM output [pieces][nb][rows].
+__device__ __forceinline__ float bt_fold(const float* part, const BtPieces& p, int nb, int rows, int b, int n) {
+  const int np = bt_npieces(p, n);
+  float s = 0.f;
+  for (int q = 0; q < np; ++q) s += part[((size_t)q * nb + b) * rows + n];
+  return s;
+}
+
+// Digit rows of the block's shared-memory vector src[0..K) for session b.
+__device__ __forceinline__ void bt_digits_block(const float* src, int K, int lfk, uint8_t* dig, float2* cs, int b,
+                                                int bp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int per = 1 << (lfk - 5);
+  for (int g = warp; g < (K >> lfk); g += nw) {
+    const float* p = src + ((size_t)g << lfk) + lane * per;
+    float v[4] = {p[0], p[1], per == 4 ? p[2] : 0.f, per == 4 ? p[3] : 0.f};
+    bg_emit_group(v, per, dig, cs, (size_t)K, ((size_t)g << lfk) + lane * per, b, bp, g);
+  }
+}
+
+// Two-pass LayerNorm of buf[0..C) in place (eps 1e-5, F.layer_norm).
+__device__ __forceinline__ void bt_layer_norm(float* buf, const float* w, const float* bias, int C, float* red) {
+  float s = 0.f;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) s += buf[i];
+  const float mean = block_sum(s, red) / (float)C;
+  float q = 0.f;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float d = buf[i] - mean;
+    q += d * d;
+  }
+  const float rstd = rsqrtf(block_sum(q, red) / (float)C + 1e-5f);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) buf[i] = (buf[i] - mean) * rstd * w[i] + bias[i];
+  __syncthreads();
+}
+
+// --------------------------------------------------------------- embed
+struct BtEmbedArgs {
+  PackedView emb;
+  const float *ln0_w, *ln0_b;
+  const int* tok;  // [nb]
+  float* x;        // [nb][C]
+  int* step;       // incremented once per step (by block 0)
+  int* err;
+  int C, V;
+};
+
+__global__ void __launch_bounds__(kBtThreads) bt_embed_kernel(BtEmbedArgs a) {
+  __shared__ float red[32];
+  extern __shared__ __align__(16) float bt_sm[];
+  const int b = blockIdx.x, C = a.C;
+  int tok = a.tok[b];
+  if (tok < 0 || tok >= a.V) {
+    if (threadIdx.x == 0) atomicOr(a.err, kErrToken);
+    tok = 0;
+  }
+  if (b == 0 && threadIdx.x == 0) *a.step += 1;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) bt_sm[i] = packed_at(a.emb, tok, i);
+  __syncthreads();
+  bt_layer_norm(bt_sm, a.ln0_w, a.ln0_b, C, red);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) a.x[(size_t)b * C + i] = bt_sm[i];
+}
+
+// ------------------------------------------------------- layer / head input
+struct BtInArgs {
+  float* x;              // [nb][C] residual stream (written when folding)
+  const float* xm;       // [nb][C] stream after the previous attention (fold source)
+  const float* part;     // previous FFN value pieces, or null (x already complete)
+  BtPieces pp;
+  const float *ln_w, *ln_b;
+  float* state;          // att_x[l] [nb][C], or null for the head input
+  const float* mix[6];   // x_r, x_w, x_k, x_v, x_a, x_g
+  uint8_t* dig[3];       // r, k, v digit rows (head: dig[0] = ln_out rows)
+  float2* cs[3];
+  float* xa4;            // [4][nb][C]: w, a, g, v adapter inputs
+  int C, nb, bp, lfk;
+};
+
+__global__ void __launch_bounds__(kBtThreads) bt_in_kernel(BtInArgs a) {
+  __shared__ float red[32];
+  extern __shared__ __align__(16) float bt_sm[];
+  const int b = blockIdx.x, C = a.C;
+  float* xl = bt_sm;       // ln output
+  float* prev = xl + C;    // previous ln output (token shift)
+  float* tmp = prev + C;   // one mix
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    float v;
+    if (a.part) {
+      v = a.xm[(size_t)b * C + i] + bt_fold(a.part, a.pp, a.nb, C, b, i);
+      a.x[(size_t)b * C + i] = v;
+    } else {
+      v = a.x[(size_t)b * C + i];
+    }
+    xl[i] = v;
+  }
+  __syncthreads();
+  bt_layer_norm(xl, a.ln_w, a.ln_b, C, red);
+  if (!a.state) {  // head input: ln_out only
+    bt_digits_block(xl, C, a.lfk, a.dig[0], a.cs[0], b, a.bp);
+    return;
+  }
+  float* st = a.state + (size_t)b * C;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    prev[i] = st[i];
+    st[i] = xl[i];
+  }
+  __syncthreads();
+  // r, k, v (mix 0, 2, 3): digit rows
+  const int dmix[3] = {0, 2, 3};
+  for (int j = 0; j < 3; ++j) {
+    const float* mx = a.mix[dmix[j]];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) tmp[i] = xl[i] + (prev[i] - xl[i]) * mx[i];
+    __syncthreads();
+    bt_digits_block(tmp, C, a.lfk, a.dig[j], a.cs[j], b, a.bp);
+    __syncthreads();
+  }
+  // w, a, g, v adapter inputs (mix 1, 4, 5, 3), fp32
+  const int amix[4] = {1, 4, 5, 3};
+  for (int j = 0; j < 4; ++j) {
+    const float* mx = a.mix[amix[j]];
+    float* o = a.xa4 + ((size_t)j * a.nb + b) * C;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) o[i] = xl[i] + (prev[i] - xl[i]) * mx[i];
+  }
+}
+
+// ------------------------------------------------ adapter first stages
+// out[s][b][off_m + c] = sum_{i in rows of split s} x_m[b][i] W1_m[i][c]
+struct BtAdp1Args {
+  PackedView w[4];  // w1, a1, g1, v1: [C][R_m] (x @ W convention)
+  int R[4], off[4];
+  int blk0[5];      // first column block of each adapter; blk0[nm] = blocks
+  int nm;
+  const float* xa4; // [4][nb][C]
+  float* out;       // [splits][nb][rtot]
+  int C, nb, rtot;
+};
+
+__global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
+  __shared__ __align__(16) float xs[kBtAdpKc * 64];          // [kc][64 sessions]
+  __shared__ __align__(16) float ws[kBtAdpKc * kBtAdpCols];  // [kc][32 columns]
+  const int t = threadIdx.x;
+  int m = 0;
+  while (m + 1 < a.nm && (int)blockIdx.x >= a.blk0[m + 1]) ++m;
+  const PackedView& W = a.w[m];
+  const int R = a.R[m];
+  const int c0 = ((int)blockIdx.x - a.blk0[m]) * kBtAdpCols;
+  const int k0 = blockIdx.y * kBtAdpKc;
+  const float* xsrc = a.xa4 + (size_t)m * a.nb * a.C;
+  for (int idx = t; idx < kBtAdpKc * 64; idx += blockDim.x) {
+    const int b = idx / kBtAdpKc, kk = idx - b * kBtAdpKc;
+    xs[kk * 64 + b] = b < a.nb ? xsrc[(size_t)b * a.C + k0 + kk] : 0.f;
+  }
+  for (int idx = t; idx < kBtAdpKc * kBtAdpCols; idx += blockDim.x) {
+    const int kk = idx / kBtAdpCols, j = idx - kk * kBtAdpCols;
+    ws[idx] = c0 + j < R ? packed_at(W, k0 + kk, c0 + j) : 0.f;
+  }
+  __syncthreads();
+  const int bq = t & 15, jq = t >> 4;
+  float acc[4][2] = {};
+#pragma unroll 4
+  for (int kk = 0; kk < kBtAdpKc; ++kk) {
+    const float4 xv = *reinterpret_cast<const float4*>(xs + kk * 64 + 4 * bq);
+    const float2 wv = *reinterpret_cast<const float2*>(ws + kk * kBtAdpCols + 2 * jq);
+    acc[0][0] = fmaf(xv.x, wv.x, acc[0][0]);
+    acc[0][1] = fmaf(xv.x, wv.y, acc[0][1]);
+    acc[1][0] = fmaf(xv.y, wv.x, acc[1][0]);
+    acc[1][1] = fmaf(xv.y, wv.y, acc[1][1]);
+    acc[2][0] = fmaf(xv.z, wv.x, acc[2][0]);
+    acc[2][1] = fmaf(xv.z, wv.y, acc[2][1]);
+    acc[3][0] = fmaf(xv.w, wv.x, acc[3][0]);
+    acc[3][1] = fmaf(xv.w, wv.y, acc[3][1]);
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int b = 4 * bq + u;
+    if (b >= a.nb) continue;
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      const int c = c0 + 2 * jq + v;
+      if (c < R) a.out[((size_t)blockIdx.y * a.nb + b) * a.rtot + a.off[m] + c] = acc[u][v];
+    }
+  }
+}
+
+// mid[b][j] = act(sum over splits of out[s][b][j]): tanh for w, sigmoid for g.
+__global__ void bt_adpr_kernel(float* mid, const float* part, int splits, int nb, int rtot, int used, int rw,
+                               int ra, int rg) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nb * used) return;
+  const int b = i / used, j = i - b * used;
+  float s = 0.f;
+  for (int q = 0; q < splits; ++q) s += part[((size_t)q * nb + b) * rtot + j];
+  if (j < rw) s = tanhf(s);
+  else if (j >= rw + ra && j < rw + ra + rg) s = sigmoidf_(s);
+  mid[(size_t)b * rtot + j] = s;
+}
+
+// ------------------------------------------------ adapter second stages
+// out[m][b][c] = sum_r mid[b][off_m + r] W2_m[r][c], 64 columns per CTA.
+struct BtAdp2Args {
+  PackedView w[4];  // w2, a2, g2, v2: [R_m][C]
+  int R[4], off[4];
+  const float* mid; // [nb][rtot]
+  float* out;       // [4][nb][C]
+  int C, nb, rtot;
+};
+
+constexpr int kBtAdp2Rc = 128;  // second-stage rows staged per round
+
+__global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
+  extern __shared__ __align__(16) float bt_sm[];
+  const int m = blockIdx.y, c0 = blockIdx.x * 64, t = threadIdx.x;
+  const int R = a.R[m];
+  const PackedView& W = a.w[m];
+  float* ms = bt_sm;                  // [rc][64 sessions]
+  float* ws = ms + kBtAdp2Rc * 64;    // [rc][64 columns]
+  const int bq = t & 15, cq = t >> 4;
+  float acc[4][4] = {};
+  for (int r0 = 0; r0 < R; r0 += kBtAdp2Rc) {
+    const int rc = min(kBtAdp2Rc, R - r0);
+    __syncthreads();
+    for (int idx = t; idx < rc * 64; idx += blockDim.x) {
+      const int b = idx / rc, r = idx - b * rc;
+      ms[r * 64 + b] = b < a.nb ? a.mid[(size_t)b * a.rtot + a.off[m] + r0 + r] : 0.f;
+    }
+    for (int idx = t; idx < rc * 64; idx += blockDim.x) {
+      const int r = idx >> 6, j = idx & 63;
+      ws[idx] = packed_at(W, r0 + r, c0 + j);
+    }
+    __syncthreads();
+    for (int r = 0; r < rc; ++r) {
+      const float4 mv = *reinterpret_cast<const float4*>(ms + r * 64 + 4 * bq);
+      const float4 wv = *reinterpret_cast<const float4*>(ws + r * 64 + 4 * cq);
+      const float mm[4] = {mv.x, mv.y, mv.z, mv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(mm[u], ww[v], acc[u][v]);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int b = 4 * bq + u;
+    if (b >= a.nb) continue;
+    *reinterpret_cast<float4*>(a.out + ((size_t)m * a.nb + b) * a.C + c0 + 4 * cq) =
+        make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
+  }
+}
+
+// ------------------------------------------------------------------ wkv
+struct BtWkvArgs {
+  const float* part[3];  // r, k, v GEMM pieces [pieces][nb][C]
+  BtPieces pp[3];
+  const float* adp2;     // [4][nb][C]: w, a, g, v second stages (pre-activation)
+  float* wkv;            // this layer's state [nb][H][64][64]
+  float* vfirst;         // [nb][C]
+  float* att_y;          // [nb][C]
+  const float *w0, *a0, *v0, *k_k, *k_a, *r_k, *lnx_w, *lnx_b;
+  int C, H, nb, layer0;
+};
+
+__global__ void __launch_bounds__(kBtThreads) bt_wkv_kernel(BtWkvArgs a) {
+  __shared__ float red[32];
+  __shared__ __align__(16) float sv6[7 * 64];
+  float *sr = sv6, *sd = sv6 + 64, *sk = sv6 + 128, *sv = sv6 + 192, *skk = sv6 + 256, *ska = sv6 + 320,
+        *sy = sv6 + 384;
+  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x, C = a.C;
+  const int ch = h * 64 + (t & 63);
+  float r = 0.f, k = 0.f, v = 0.f, wv = 0.f, av = 0.f, gv = 0.f, vv = 0.f;
+  if (t < 64) {
+    r = bt_fold(a.part[0], a.pp[0], a.nb, C, b, ch);
+    k = bt_fold(a.part[1], a.pp[1], a.nb, C, b, ch);
+    v = bt_fold(a.part[2], a.pp[2], a.nb, C, b, ch);
+    wv = a.adp2[((size_t)0 * a.nb + b) * C + ch];
+    av = a.adp2[((size_t)1 * a.nb + b) * C + ch];
+    gv = a.adp2[((size_t)2 * a.nb + b) * C + ch];
+    if (!a.layer0) vv = a.adp2[((size_t)3 * a.nb + b) * C + ch];
+  }
+  const float kkv = t < 64 ? k * a.k_k[ch] : 0.f;
+  const float nrm = sqrtf(block_sum(kkv * kkv, red));
+  if (t < 64) {
+    const float aa = sigmoidf_(a.a0[ch] + av);
+    const float kk = kkv / fmaxf(nrm, 1e-12f);
+    const float kn = k * (1.0f + (aa - 1.0f) * a.k_a[ch]);
+    if (a.layer0) {
+      a.vfirst[(size_t)b * C + ch] = v;
+    } else {
+      const float vf = a.vfirst[(size_t)b * C + ch];
+      v = v + (vf - v) * sigmoidf_(a.v0[ch] + vv);
+    }
+    sr[t] = r;
+    sd[t] = expf(-0.606531f * sigmoidf_(a.w0[ch] + wv));
+    sk[t] = kn;
+    sv[t] = v;
+    skk[t] = kk;
+    ska[t] = kk * aa;
+  }
+  __syncthreads();
+  wkv7_head64(a.wkv + ((size_t)b * a.H + h) * 4096, sr, sd, sk, sv, skk, ska, sy);
+  __syncthreads();
+  const float yv = t < 64 ? sy[t] : 0.f;
+  const float mean = block_sum(yv, red) / 64.f;
+  const float dv = t < 64 ? yv - mean : 0.f;
+  const float var = block_sum(dv * dv, red) / 64.f;
+  const float bon = t < 64 ? sr[t] * sk[t] * a.r_k[ch] : 0.f;
+  const float bonus = block_sum(bon, red);
+  if (t < 64) {
+    float o = dv * rsqrtf(var + 64e-5f) * a.lnx_w[ch] + a.lnx_b[ch];
+    o = o + bonus * sv[t];
+    a.att_y[(size_t)b * C + ch] = o * gv;
+  }
+}
+
+// ------------------------------------------------------------ ffn input
+struct BtFfnArgs {
+  const float* x;       // [nb][C] layer input
+  float* xm;            // [nb][C] x + attention (written)
+  const float* part;    // output-projection pieces
+  BtPieces pp;
+  const float *ln_w, *ln_b, *mix;
+  float* state;         // ffn_x[l] [nb][C]
+  uint8_t* dig;
+  float2* cs;
+  int C, nb, bp, lfk;
+};
+
+__global__ void __launch_bounds__(kBtThreads) bt_ffn_kernel(BtFfnArgs a) {
+  __shared__ float red[32];
+  extern __shared__ __align__(16) float bt_sm[];
+  const int b = blockIdx.x, C = a.C;
+  float* xl = bt_sm;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float v = a.x[(size_t)b * C + i] + bt_fold(a.part, a.pp, a.nb, C, b, i);
+    a.xm[(size_t)b * C + i] = v;
+    xl[i] = v;
+  }
+  __syncthreads();
+  bt_layer_norm(xl, a.ln_w, a.ln_b, C, red);
+  float* st = a.state + (size_t)b * C;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float p = st[i], z = xl[i];
+    st[i] = z;
+    xl[i] = z + (p - z) * a.mix[i];
+  }
+  __syncthreads();
+  bt_digits_block(xl, C, a.lfk, a.dig, a.cs, b, a.bp);
+}
+
+// h = relu(key)^2 and its digit rows: one warp per (session, group).
+__global__ void __launch_bounds__(kBtThreads) bt_hdig_kernel(uint8_t* dig, float2* cs, const float* part, BtPieces pp,
+                                                             int nb, int F, int bp, int lfk) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int G = F >> lfk;
+  if (gw >= nb * G) return;
+  const int b = gw / G, g = gw - b * G;
+  const int per = 1 << (lfk - 5);
+  const int n0 = (g << lfk) + lane * per;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int u = 0; u < per; ++u) {
+    const float y = bt_fold(part, pp, nb, F, b, n0 + u);
+    v[u] = y > 0.f ? y * y : 0.f;
+  }
+  bg_emit_group(v, per, dig, cs, (size_t)F, (size_t)n0, b, bp, g);
+}
+
+// ------------------------------------------------------------- argmax
+__global__ void __launch_bounds__(1024) bt_argmax_kernel(float* logits, const float* part, BtPieces pp, int nb,
+                                                         int V, int* tok, int* hist, const int* step, int hist_cap) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int b = blockIdx.x;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int n = threadIdx.x; n < V; n += blockDim.x) {
+    const float v = bt_fold(part, pp, nb, V, b, n);
+    logits[(size_t)b * V + n] = v;
+    if (v > best || (v == best && n < besti)) {
+      best = v;
+      besti = n;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ov > best || (ov == best && oi < besti)) {
+      best = ov;
+      besti = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) {
+    bv[wid] = best;
+    bi[wid] = besti;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float cb = -INFINITY;
+    int ci = 0x7fffffff;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w)
+      if (bv[w] > cb || (bv[w] == cb && bi[w] < ci)) {
+        cb = bv[w];
+        ci = bi[w];
+      }
+    if (ci == 0x7fffffff) ci = 0;  // every logit NaN
+    tok[b] = ci;
+    const int s = *step;
+    hist[(size_t)((s % hist_cap + hist_cap) % hist_cap) * nb + b] = ci;
+  }
+}
+
+}  // namespace rwkvb
+
+// ------------------------------------------------------------ host engine
+namespace rwkvb {
+namespace {
+
+struct BtLayer {
+  PackedView ad1[4], ad2[4];  // w1 a1 g1 v1, w2 a2 g2 v2
+  const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
+  const float* mix[6];
+  const float *w0, *a0, *v0, *k_k, *k_a, *r_k, *lnx_w, *lnx_b, *ffn_x_k;
+  BgArgs rkv, o, key, value;
+};
+
+bool bt_desc_ok(const rwkvb_packed& p, int rows, int cols) {
+  return p.data && p.rows == rows && p.cols == cols && p.group_size > 0 &&
+         (p.kind == RWKVB_KIND_SG8 || (p.kind >= RWKVB_KIND_LUT2_F32 && p.kind <= RWKVB_KIND_LUT2_IN_RES));
+}
+
+}  // namespace
+}  // namespace rwkvb
+
+struct rwkvb_batch {
+  int dev = 0, sms = 0;
+  int nb = 0, bp = 0, nrows = 0, lfk = 7, group = 128;
+  int L = 0, C = 0, H = 0, F = 0, V = 0, rw = 0, ra = 0, rg = 0, rv = 0, rtot = 0;
+  int adp_splits = 0, hist_cap = 1024;
+  std::vector<rwkvb::BtLayer> layers;
+  rwkvb::PackedView emb;
+  const float *ln0_w = nullptr, *ln0_b = nullptr, *lnout_w = nullptr, *lnout_b = nullptr;
+  rwkvb::BgArgs head;
+  int g_rkv = 0, g_o = 0, g_key = 0, g_value = 0, g_head = 0;
+  size_t smem_bg = 0;
+  rwkvb::BtPieces pp_rkv[3], pp_o, pp_key, pp_value, pp_head;
+  void* arena = nullptr;
+  float *att_x = nullptr, *wkv = nullptr, *ffn_x = nullptr, *x = nullptr, *xm = nullptr, *xa4 = nullptr;
+  float *adp1 = nullptr, *mid = nullptr, *adp2 = nullptr, *vfirst = nullptr, *att_y = nullptr, *logits = nullptr;
+  float *part_r = nullptr, *part_k = nullptr, *part_v = nullptr, *part_o = nullptr, *part_key = nullptr;
+  float *part_val = nullptr, *part_head = nullptr;
+  uint8_t *dig_r = nullptr, *dig_k = nullptr, *dig_v = nullptr, *dig_y = nullptr, *dig_f = nullptr;
+  uint8_t *dig_h = nullptr, *dig_o = nullptr;
+  float2 *cs_r = nullptr, *cs_k = nullptr, *cs_v = nullptr, *cs_y = nullptr, *cs_f = nullptr, *cs_h = nullptr;
+  float2* cs_o = nullptr;
+  int *tok = nullptr, *hist = nullptr, *step = nullptr, *err = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  bool use_graph = true;
+  int launches = 0;
+};
+
+namespace rwkvb {
+namespace {
+
+BtPieces bt_pieces(const BgArgs& a, int job, int grid) {
+  BtPieces p;
+  p.stage0 = a.mat[job].stage0;
+  p.G = a.mat[job].k / 128;
+  p.total = a.total;
+  p.ncta = grid;
+  return p;
+}
+
+// Launch one token step of every session (tokens already in e->tok).
+int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
+  const int C = e->C, nb = e->nb;
+  int n = 0;
+#define BT_CHECK()                                  \
+  do {                                              \
+    const int st_ = cuda_status(cudaGetLastError()); \
+    if (st_ != RWKVB_OK) return st_;                \
+    ++n;                                            \
+  } while (0)
+  {
+    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, e->tok, e->x, e->step, e->err, C, e->V};
+    bt_embed_kernel<<<nb, kBtThreads, sizeof(float) * C, s>>>(a);
+    BT_CHECK();
+  }
+  for (int l = 0; l < e->L; ++l) {
+    const BtLayer& ly = e->layers[l];
+    const bool l0 = l == 0;
+    {
+      BtInArgs a;
+      std::memset(&a, 0, sizeof(a));
+      a.x = e->x;
+      a.xm = e->xm;
+      a.part = l0 ? nullptr : e->part_val;
+      a.pp = e->pp_value;
+      a.ln_w = ly.ln1_w;
+      a.ln_b = ly.ln1_b;
+      a.state = e->att_x + (size_t)l * nb * C;
+      for (int j = 0; j < 6; ++j) a.mix[j] = ly.mix[j];
+      a.dig[0] = e->dig_r, a.dig[1] = e->dig_k, a.dig[2] = e->dig_v;
+      a.cs[0] = e->cs_r, a.cs[1] = e->cs_k, a.cs[2] = e->cs_v;
+      a.xa4 = e->xa4;
+      a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
+      bt_in_kernel<<<nb, kBtThreads, sizeof(float) * 3 * C, s>>>(a);
+      BT_CHECK();
+    }
+    if (bg_launch(ly.rkv, e->g_rkv, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    ++n;
+    const int nm = l0 ? 3 : 4;
+    {
+      BtAdp1Args a;
+      std::memset(&a, 0, sizeof(a));
+      const int Rm[4] = {e->rw, e->ra, e->rg, e->rv};
+      int off = 0, blk = 0;
+      for (int m = 0; m < 4; ++m) {
+        a.w[m] = ly.ad1[m];
+        a.R[m] = Rm[m];
+        a.off[m] = off;
+        a.blk0[m] = blk;
+        off += Rm[m];
+        if (m < nm) blk += (Rm[m] + kBtAdpCols - 1) / kBtAdpCols;
+      }
+      a.blk0[nm] = blk;
+      a.nm = nm;
+      a.xa4 = e->xa4;
+      a.out = e->adp1;
+      a.C = C, a.nb = nb, a.rtot = e->rtot;
+      bt_adp1_kernel<<<dim3(blk, e->adp_splits), kBtThreads, 0, s>>>(a);
+      BT_CHECK();
+      const int used = l0 ? e->rw + e->ra + e->rg : e->rtot;
+      bt_adpr_kernel<<<(nb * used + 255) / 256, 256, 0, s>>>(e->mid, e->adp1, e->adp_splits, nb, e->rtot, used,
+                                                              e->rw, e->ra, e->rg);
+      BT_CHECK();
+    }
+    {
+      BtAdp2Args a;
+      std::memset(&a, 0, sizeof(a));
+      const int Rm[4] = {e->rw, e->ra, e->rg, e->rv};
+      int off = 0;
+      for (int m = 0; m < 4; ++m) {
+        a.w[m] = ly.ad2[m];
+        a.R[m] = Rm[m];
+        a.off[m] = off;
+        off += Rm[m];
+      }
+      a.mid = e->mid;
+      a.out = e->adp2;
+      a.C = C, a.nb = nb, a.rtot = e->rtot;
+      bt_adp2_kernel<<<dim3(C / 64, nm), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
+      BT_CHECK();
+    }
+    {
+      BtWkvArgs a;
+      std::memset(&a, 0, sizeof(a));
+      a.part[0] = e->part_r, a.part[1] = e->part_k, a.part[2] = e->part_v;
+      for (int j = 0; j < 3; ++j) a.pp[j] = e->pp_rkv[j];
+      a.adp2 = e->adp2;
+      a.wkv = e->wkv + (size_t)l * nb * e->H * 4096;
+      a.vfirst = e->vfirst;
+      a.att_y = e->att_y;
+      a.w0 = ly.w0, a.a0 = ly.a0, a.v0 = ly.v0, a.k_k = ly.k_k, a.k_a = ly.k_a, a.r_k = ly.r_k;
+      a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
+      a.C = C, a.H = e->H, a.nb = nb, a.layer0 = l0 ? 1 : 0;
+      bt_wkv_kernel<<<dim3(e->H, nb), kBtThreads, 0, s>>>(a);
+      BT_CHECK();
+    }
+    if (bg_digits(e->dig_y, e->cs_y, e->att_y, C, C, nb, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
+    ++n;
+    if (bg_launch(ly.o, e->g_o, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    ++n;
+    {
+      BtFfnArgs a{e->x, e->xm, e->part_o, e->pp_o, ly.ln2_w, ly.ln2_b, ly.ffn_x_k,
+                  e->ffn_x + (size_t)l * nb * C, e->dig_f, e->cs_f, C, nb, e->bp, e->lfk};
+      bt_ffn_kernel<<<nb, kBtThreads, sizeof(float) * C, s>>>(a);
+      BT_CHECK();
+    }
+    if (bg_launch(ly.key, e->g_key, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    ++n;
+    {
+      const int warps = nb * (e->F >> e->lfk);
+      bt_hdig_kernel<<<(warps + 7) / 8, kBtThreads, 0, s>>>(e->dig_h, e->cs_h, e->part_key, e->pp_key, nb, e->F,
+                                                           e->bp, e->lfk);
+      BT_CHECK();
+    }
+    if (bg_launch(ly.value, e->g_value, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    ++n;
+  }
+  {
+    BtInArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.x = e->x;
+    a.xm = e->xm;
+    a.part = e->part_val;
+    a.pp = e->pp_value;
+    a.ln_w = e->lnout_w;
+    a.ln_b = e->lnout_b;
+    a.state = nullptr;
+    a.dig[0] = e->dig_o;
+    a.cs[0] = e->cs_o;
+    a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
+    bt_in_kernel<<<nb, kBtThreads, sizeof(float) * 3 * C, s>>>(a);
+    BT_CHECK();
+  }
+  if (bg_launch(e->head, e->g_head, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+  ++n;
+  bt_argmax_kernel<<<nb, 1024, 0, s>>>(e->logits, e->part_head, e->pp_head, nb, e->V, e->tok, e->hist, e->step,
+                                       e->hist_cap);
+  BT_CHECK();
+#undef BT_CHECK
+  e->launches = n;
+  return RWKVB_OK;
+}
+
+int bt_run_step(rwkvb_batch* e, cudaStream_t s) {
+  if (e->use_graph && !e->exec) {
+    cudaStream_t cs = nullptr;
+    if (cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking) != cudaSuccess) return RWKVB_ECUDA;
+    cudaGraph_t g = nullptr;
+    int st = cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    if (st == RWKVB_OK) {
+      st = bt_record_step(e, cs);
+      const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+      if (st == RWKVB_OK) st = cuda_status(ce);
+    }
+    if (st == RWKVB_OK) st = cuda_status(cudaGraphInstantiate(&e->exec, g, 0));
+    if (g) cudaGraphDestroy(g);
+    cudaStreamDestroy(cs);
+    if (st != RWKVB_OK) {
+      e->exec = nullptr;
+      return st;
+    }
+  }
+  if (e->use_graph) return cuda_status(cudaGraphLaunch(e->exec, s));
+  return bt_record_step(e, s);
+}
+
+int bt_check_err(rwkvb_batch* e, cudaStream_t s) {
+  int h = 0;
+  cudaError_t err = cudaMemcpyAsync(&h, e->err, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  if (err != cudaSuccess) return cuda_status(err);
+  if (h) {
+    cudaMemsetAsync(e->err, 0, sizeof(int), s);
+    cudaStreamSynchronize(s);
+    return (h & kErrTimeout) ? RWKVB_ETIMEOUT : RWKVB_EARG;
+  }
+  return RWKVB_OK;
+}
+
+}  // namespace
+}  // namespace rwkvb
+
+extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, rwkvb_batch** out) {
+  if (!m || !out || !m->layers || batch <= 0 || batch > kBgMaxSessions) return RWKVB_EARG;
+  *out = nullptr;
+  const int L = m->n_layer, C = m->n_embd, N = m->head_size, F = m->ffn, V = m->vocab;
+  if (L <= 0 || C <= 0 || F <= 0 || V <= 0 || N != 64 || C % 128 || F % 128 || V % 128) return RWKVB_EUNSUPPORTED;
+  if (!bt_desc_ok(m->emb, V, C) || !bg_matrix_ok(m->head) || m->head.rows != V || m->head.cols != C)
+    return m->head.kind == RWKVB_KIND_SG8 ? RWKVB_EUNSUPPORTED : RWKVB_EARG;
+  if (!m->ln0_w || !m->ln0_b || !m->ln_out_w || !m->ln_out_b) return RWKVB_EARG;
+  const rwkvb_layer_desc& l0 = m->layers[0];
+  const int rw = l0.w1.cols, ra = l0.a1.cols, rg = l0.g1.cols;
+  const int rv = L > 1 ? m->layers[1].v1.cols : 0;
+  const uint32_t group = m->head.group_size;
+  for (int i = 0; i < L; ++i) {
+    const rwkvb_layer_desc& s = m->layers[i];
+    const rwkvb_packed* big[] = {&s.att_r, &s.att_k, &s.att_v, &s.att_o, &s.ffn_key, &s.ffn_value};
+    for (const rwkvb_packed* p : big)
+      if (!bg_matrix_ok(*p) || p->group_size != group) return RWKVB_EUNSUPPORTED;
+    if (s.att_r.rows != C || s.att_r.cols != C || s.att_k.rows != C || s.att_k.cols != C || s.att_v.rows != C ||
+        s.att_v.cols != C || s.att_o.rows != C || s.att_o.cols != C || s.ffn_key.rows != F ||
+        s.ffn_key.cols != C || s.ffn_value.rows != C || s.ffn_value.cols != F)
+      return RWKVB_EARG;
+    if (!bt_desc_ok(s.w1, C, rw) || !bt_desc_ok(s.w2, rw, C) || !bt_desc_ok(s.a1, C, ra) ||
+        !bt_desc_ok(s.a2, ra, C) || !bt_desc_ok(s.g1, C, rg) || !bt_desc_ok(s.g2, rg, C))
+      return RWKVB_EARG;
+    if (i > 0 && (!bt_desc_ok(s.v1, C, rv) || !bt_desc_ok(s.v2, rv, C))) return RWKVB_EARG;
+    const float* vecs[] = {s.ln1_w, s.ln1_b, s.ln2_w, s.ln2_b, s.x_r, s.x_w, s.x_k, s.x_v, s.x_a, s.x_g,
+                           s.w0, s.a0, s.k_k, s.k_a, s.r_k, s.lnx_w, s.lnx_b, s.ffn_x_k};
+    for (const float* p : vecs)
+      if (!p) return RWKVB_EARG;
+    if (i > 0 && !s.v0) return RWKVB_EARG;
+  }
+  if (rw <= 0 || ra <= 0 || rg <= 0) return RWKVB_EUNSUPPORTED;
+
+  rwkvb_batch* e = new (std::nothrow) rwkvb_batch();
+  if (!e) return RWKVB_EALLOC;
+  cudaGetDevice(&e->dev);
+  e->sms = device_sms();
+  e->use_graph = !(flags & 0x1u);
+  e->nb = batch;
+  e->bp = bg_padded_sessions(batch);
+  e->nrows = bg_digit_rows(batch);
+  e->group = (int)group;
+  e->lfk = group == 64 ? 6 : 7;
+  e->L = L, e->C = C, e->H = C / 64, e->F = F, e->V = V;
+  e->rw = rw, e->ra = ra, e->rg = rg, e->rv = rv, e->rtot = rw + ra + rg + rv;
+  e->adp_splits = C / kBtAdpKc;
+  e->emb = make_view(m->emb);
+  e->ln0_w = m->ln0_w, e->ln0_b = m->ln0_b, e->lnout_w = m->ln_out_w, e->lnout_b = m->ln_out_b;
+
+  // ---------------------------------------------------------------- arena
+  const size_t nbC = (size_t)batch * C;
+  const int bp = e->bp, nr = e->nrows;
+  // generous piece bounds: a tile never spans more CTAs than its stages
+  const int Pk = C / 128, Pf = F / 128;
+  struct Item {
+    void** p;
+    size_t bytes;
+  };
+  std::vector<Item> items = {
+      {(void**)&e->att_x, 4 * (size_t)L * nbC},
+      {(void**)&e->wkv, 4 * (size_t)L * batch * e->H * 4096},
+      {(void**)&e->ffn_x, 4 * (size_t)L * nbC},
+      {(void**)&e->x, 4 * nbC},
+      {(void**)&e->xm, 4 * nbC},
+      {(void**)&e->xa4, 4 * 4 * nbC},
+      {(void**)&e->adp1, 4 * (size_t)e->adp_splits * batch * e->rtot},
+      {(void**)&e->mid, 4 * (size_t)batch * e->rtot},
+      {(void**)&e->adp2, 4 * 4 * nbC},
+      {(void**)&e->vfirst, 4 * nbC},
+      {(void**)&e->att_y, 4 * nbC},
+      {(void**)&e->logits, 4 * (size_t)batch * V},
+      {(void**)&e->part_r, 4 * (size_t)Pk * nbC},
+      {(void**)&e->part_k, 4 * (size_t)Pk * nbC},
+      {(void**)&e->part_v, 4 * (size_t)Pk * nbC},
+      {(void**)&e->part_o, 4 * (size_t)Pk * nbC},
+      {(void**)&e->part_key, 4 * (size_t)Pk * batch * F},
+      {(void**)&e->part_val, 4 * (size_t)Pf * nbC},
+      {(void**)&e->part_head, 4 * (size_t)Pk * batch * V},
+      {(void**)&e->dig_r, (size_t)nr * C},
+      {(void**)&e->dig_k, (size_t)nr * C},
+      {(void**)&e->dig_v, (size_t)nr * C},
+      {(void**)&e->dig_y, (size_t)nr * C},
+      {(void**)&e->dig_f, (size_t)nr * C},
+      {(void**)&e->dig_h, (size_t)nr * F},
+      {(void**)&e->dig_o, (size_t)nr * C},
+      {(void**)&e->cs_r, 8 * (size_t)(C / group) * bp},
+      {(void**)&e->cs_k, 8 * (size_t)(C / group) * bp},
+      {(void**)&e->cs_v, 8 * (size_t)(C / group) * bp},
+      {(void**)&e->cs_y, 8 * (size_t)(C / group) * bp},
+      {(void**)&e->cs_f, 8 * (size_t)(C / group) * bp},
+      {(void**)&e->cs_h, 8 * (size_t)(F / group) * bp},
+      {(void**)&e->cs_o, 8 * (size_t)(C / group) * bp},
+      {(void**)&e->tok, 4 * (size_t)batch},
+      {(void**)&e->hist, 4 * (size_t)e->hist_cap * batch},
+      {(void**)&e->step, 16},
+      {(void**)&e->err, 16},
+  };
+  size_t total = 0;
+  std::vector<size_t> offs;
+  for (const Item& it : items) {
+    offs.push_back(total);
+    total += (it.bytes + 1023) & ~size_t(1023);
+  }
+  if (cudaMalloc(&e->arena, total) != cudaSuccess) {
+    cudaGetLastError();
+    delete e;
+    return RWKVB_EALLOC;
+  }
+  cudaMemset(e->arena, 0, total);
+  for (size_t i = 0; i < items.size(); ++i) *items[i].p = (char*)e->arena + offs[i];
+  {
+    uint8_t* digs[] = {e->dig_r, e->dig_k, e->dig_v, e->dig_y, e->dig_f, e->dig_o};
+    int st = RWKVB_OK;
+    for (uint8_t* d : digs)
+      if (st == RWKVB_OK) st = bg_digits_init(d, C, batch, nullptr);
+    if (st == RWKVB_OK) st = bg_digits_init(e->dig_h, F, batch, nullptr);
+    if (st == RWKVB_OK) st = cuda_status(cudaMemset(e->step, 0xff, sizeof(int)));
+    if (st == RWKVB_OK) st = cuda_status(cudaDeviceSynchronize());
+    if (st != RWKVB_OK) {
+      cudaFree(e->arena);
+      delete e;
+      return st;
+    }
+  }
+
+  // ------------------------------------------------------- GEMM launch plans
+  const BgDigits d_rkv[3] = {{e->dig_r, e->cs_r, C}, {e->dig_k, e->cs_k, C}, {e->dig_v, e->cs_v, C}};
+  const BgDigits d_y{e->dig_y, e->cs_y, C}, d_f{e->dig_f, e->cs_f, C}, d_h{e->dig_h, e->cs_h, F},
+      d_o{e->dig_o, e->cs_o, C};
+  int pieces = 0, st = RWKVB_OK;
+  size_t smem = 0;
+  for (int i = 0; i < L && st == RWKVB_OK; ++i) {
+    const rwkvb_layer_desc& s = m->layers[i];
+    BtLayer ly;
+    std::memset(&ly, 0, sizeof(ly));
+    const rwkvb_packed* a1[4] = {&s.w1, &s.a1, &s.g1, &s.v1};
+    const rwkvb_packed* a2[4] = {&s.w2, &s.a2, &s.g2, &s.v2};
+    for (int j = 0; j < 4; ++j) {
+      if (j == 3 && i == 0) continue;
+      ly.ad1[j] = make_view(*a1[j]);
+      ly.ad2[j] = make_view(*a2[j]);
+    }
+    ly.ln1_w = s.ln1_w, ly.ln1_b = s.ln1_b, ly.ln2_w = s.ln2_w, ly.ln2_b = s.ln2_b;
+    ly.mix[0] = s.x_r, ly.mix[1] = s.x_w, ly.mix[2] = s.x_k, ly.mix[3] = s.x_v, ly.mix[4] = s.x_a, ly.mix[5] = s.x_g;
+    ly.w0 = s.w0, ly.a0 = s.a0, ly.v0 = s.v0, ly.k_k = s.k_k, ly.k_a = s.k_a, ly.r_k = s.r_k;
+    ly.lnx_w = s.lnx_w, ly.lnx_b = s.lnx_b, ly.ffn_x_k = s.ffn_x_k;
+    const BgJob jr[3] = {{&s.att_r, 0, e->part_r}, {&s.att_k, 1, e->part_k}, {&s.att_v, 2, e->part_v}};
+    st = bg_setup(&ly.rkv, jr, 3, d_rkv, 3, batch, e->sms, &e->g_rkv, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
+    const BgJob jo{&s.att_o, 0, e->part_o};
+    if (st == RWKVB_OK) st = bg_setup(&ly.o, &jo, 1, &d_y, 1, batch, e->sms, &e->g_o, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
+    const BgJob jk{&s.ffn_key, 0, e->part_key};
+    if (st == RWKVB_OK) st = bg_setup(&ly.key, &jk, 1, &d_f, 1, batch, e->sms, &e->g_key, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
+    const BgJob jv{&s.ffn_value, 0, e->part_val};
+    if (st == RWKVB_OK)
+      st = bg_setup(&ly.value, &jv, 1, &d_h, 1, batch, e->sms, &e->g_value, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pf) st = RWKVB_EUNSUPPORTED;
+    e->smem_bg = smem;
+    if (i == 0 && st == RWKVB_OK) {
+      for (int j = 0; j < 3; ++j) e->pp_rkv[j] = bt_pieces(ly.rkv, j, e->g_rkv);
+      e->pp_o = bt_pieces(ly.o, 0, e->g_o);
+      e->pp_key = bt_pieces(ly.key, 0, e->g_key);
+      e->pp_value = bt_pieces(ly.value, 0, e->g_value);
+    }
+    e->layers.push_back(ly);
+  }
+  if (st == RWKVB_OK) {
+    const BgJob jh{&m->head, 0, e->part_head};
+    st = bg_setup(&e->head, &jh, 1, &d_o, 1, batch, e->sms, &e->g_head, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
+    e->pp_head = bt_pieces(e->head, 0, e->g_head);
+  }
+  if (st == RWKVB_OK) st = bg_allow_smem(e->smem_bg);
+  if (st == RWKVB_OK) {
+    const cudaError_t ce =
+        cudaFuncSetAttribute(bt_adp2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * 2 * kBtAdp2Rc * 64));
+    st = cuda_status(ce);
+    if (st == RWKVB_OK)
+      st = cuda_status(cudaFuncSetAttribute(bt_in_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)(sizeof(float) * 3 * C)));
+  }
+  if (st != RWKVB_OK) {
+    cudaFree(e->arena);
+    delete e;
+    return st;
+  }
+  *out = e;
+  return RWKVB_OK;
+}
+
+extern "C" int rwkvb_batch_destroy(rwkvb_batch* e) {
+  if (!e) return RWKVB_EARG;
+  cudaDeviceSynchronize();
+  if (e->exec) cudaGraphExecDestroy(e->exec);
+  if (e->arena) cudaFree(e->arena);
+  delete e;
+  return RWKVB_OK;
+}
+
+extern "C" int rwkvb_batch_buffers(rwkvb_batch* e, float** att_x, float** wkv, float** ffn_x, float** logits) {
+  if (!e) return RWKVB_EARG;
+  if (att_x) *att_x = e->att_x;
+  if (wkv) *wkv = e->wkv;
+  if (ffn_x) *ffn_x = e->ffn_x;
+  if (logits) *logits = e->logits;
+  return RWKVB_OK;
+}
+
+extern "C" int rwkvb_batch_reset(rwkvb_batch* e, void* stream) {
+  if (!e) return RWKVB_EARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t nbC = (size_t)e->nb * e->C;
+  cudaError_t err = cudaMemsetAsync(e->att_x, 0, sizeof(float) * e->L * nbC, s);
+  if (err == cudaSuccess) err = cudaMemsetAsync(e->wkv, 0, sizeof(float) * (size_t)e->L * e->nb * e->H * 4096, s);
+  if (err == cudaSuccess) err = cudaMemsetAsync(e->ffn_x, 0, sizeof(float) * e->L * nbC, s);
+  if (err == cudaSuccess) err = cudaMemsetAsync(e->err, 0, sizeof(int), s);
+  return cuda_status(err);
+}
+
+extern "C" int rwkvb_batch_forward(rwkvb_batch* e, const int32_t* tokens, void* stream) {
+  if (!e || !tokens) return RWKVB_EARG;
+  for (int i = 0; i < e->nb; ++i)
+    if (tokens[i] < 0 || tokens[i] >= e->V) return RWKVB_EARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = cuda_status(cudaMemcpyAsync(e->tok, tokens, sizeof(int32_t) * e->nb, cudaMemcpyHostToDevice, s));
+  if (st == RWKVB_OK) st = bt_run_step(e, s);
+  return st;
+}
+
+extern "C" int rwkvb_batch_decode_greedy_async(rwkvb_batch* e, int32_t n, int32_t* out_dev, void* stream) {
+  if (!e || n < 0 || (n > 0 && !out_dev)) return RWKVB_EARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = RWKVB_OK;
+  for (int done = 0; done < n && st == RWKVB_OK;) {
+    const int chunk = (n - done) < e->hist_cap ? (n - done) : e->hist_cap;
+    st = cuda_status(cudaMemsetAsync(e->step, 0xff, sizeof(int), s));
+    for (int i = 0; i < chunk && st == RWKVB_OK; ++i) st = bt_run_step(e, s);
+    if (st == RWKVB_OK)
+      st = cuda_status(cudaMemcpyAsync(out_dev + (size_t)done * e->nb, e->hist, sizeof(int32_t) * chunk * e->nb,
+                                       cudaMemcpyDeviceToDevice, s));
+    done += chunk;
+  }
+  return st;
+}
+
+extern "C" int rwkvb_batch_decode_greedy(rwkvb_batch* e, int32_t n, int32_t* out_host, void* stream) {
+  if (!e || n < 0 || (n > 0 && !out_host)) return RWKVB_EARG;
+  cudaStream_t s = (cudaStream_t)stream;
+  int32_t* dev = nullptr;
+  if (n > 0 && cudaMallocAsync((void**)&dev, sizeof(int32_t) * (size_t)n * e->nb, s) != cudaSuccess) {
+    cudaGetLastError();
+    return RWKVB_EALLOC;
+  }
+  int st = rwkvb_batch_decode_greedy_async(e, n, dev, s);
+  if (st == RWKVB_OK && n > 0)
+    st = cuda_status(
+        cudaMemcpyAsync(out_host, dev, sizeof(int32_t) * (size_t)n * e->nb, cudaMemcpyDeviceToHost, s));
+  if (dev) cudaFreeAsync(dev, s);
+  const int st2 = cuda_status(cudaStreamSynchronize(s));
+  if (st == RWKVB_OK) st = st2;
+  if (st == RWKVB_OK) st = bt_check_err(e, s);
+  return st;
+}
+
+extern "C" int rwkvb_batch_launches_per_step(rwkvb_batch* e, int32_t* out) {
+  if (!e || !out) return RWKVB_EARG;
+  *out = 3 + 11 * e->L + 1;  // embed; 11 per layer; head input, head GEMM, argmax
+  return RWKVB_OK;
 }

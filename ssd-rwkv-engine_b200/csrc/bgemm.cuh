@@ -304,24 +304,13 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_kernel(const __grid_const
   }
 }
 
-// Digit rows of nb input vectors (row b of x at x + b * ldx, k columns) for
-// flush groups of 1 << lfk columns (64 or 128): one warp per (session, group).
-__global__ void __launch_bounds__(256) bg_digits_kernel(uint8_t* dig, float2* cs, const float* x, int ldx, int k,
-                                                        int nb, int bp, int lfk) {
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int G = k >> lfk;
-  if (gw >= nb * G) return;
-  const int b = gw / G, g = gw - b * G;
-  const int per = 1 << (lfk - 5);  // 2 or 4 values per lane
-  const float* src = x + (size_t)b * ldx + ((size_t)g << lfk) + lane * per;
-  float v[4] = {0.f, 0.f, 0.f, 0.f};
-  if (per == 4) {
-    const float4 t = *reinterpret_cast<const float4*>(src);
-    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
-  } else {
-    const float2 t = *reinterpret_cast<const float2*>(src);
-    v[0] = t.x, v[1] = t.y;
-  }
+// Digits of one flush group (1 << lfk = 64 or 128 columns, `per` = 2 or 4
+// values per lane in v) for session b: the whole warp calls it.  Writes the
+// three digit bytes (X + 127) of its values at column `col` of rows b, bp + b
+// and 2 bp + b of dig [rows][k], and (c_f, sum_x) to cs[g][b].
+__device__ __forceinline__ void bg_emit_group(const float (&v)[4], int per, uint8_t* dig, float2* cs, size_t k,
+                                              size_t col, int b, int bp, int g) {
+  const int lane = threadIdx.x & 31;
   float m = 0.f, sum = 0.f;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
@@ -348,7 +337,6 @@ __global__ void __launch_bounds__(256) bg_digits_kernel(uint8_t* dig, float2* cs
     w1 |= (uint32_t)((int)x1 + 127) << (8 * u);
     w2 |= (uint32_t)((int)x2 + 127) << (8 * u);
   }
-  const size_t col = ((size_t)g << lfk) + lane * per;
   if (per == 4) {
     *reinterpret_cast<uint32_t*>(dig + (size_t)b * k + col) = w0;
     *reinterpret_cast<uint32_t*>(dig + (size_t)(bp + b) * k + col) = w1;
@@ -359,6 +347,27 @@ __global__ void __launch_bounds__(256) bg_digits_kernel(uint8_t* dig, float2* cs
     *reinterpret_cast<uint16_t*>(dig + (size_t)(2 * bp + b) * k + col) = (uint16_t)w2;
   }
   if (lane == 0) cs[(size_t)g * bp + b] = make_float2(ldexpf(1.0f, e) / 127.0f, sum);
+}
+
+// Digit rows of nb input vectors (row b of x at x + b * ldx, k columns) for
+// flush groups of 1 << lfk columns (64 or 128): one warp per (session, group).
+__global__ void __launch_bounds__(256) bg_digits_kernel(uint8_t* dig, float2* cs, const float* x, int ldx, int k,
+                                                        int nb, int bp, int lfk) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int G = k >> lfk;
+  if (gw >= nb * G) return;
+  const int b = gw / G, g = gw - b * G;
+  const int per = 1 << (lfk - 5);  // 2 or 4 values per lane
+  const float* src = x + (size_t)b * ldx + ((size_t)g << lfk) + lane * per;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (per == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(src);
+    v[0] = t.x, v[1] = t.y, v[2] = t.z, v[3] = t.w;
+  } else {
+    const float2 t = *reinterpret_cast<const float2*>(src);
+    v[0] = t.x, v[1] = t.y;
+  }
+  bg_emit_group(v, per, dig, cs, (size_t)k, ((size_t)g << lfk) + lane * per, b, bp, g);
 }
 
 // y[b][n] = sum over the pieces of n's tile of part[p][b][n], in piece order.

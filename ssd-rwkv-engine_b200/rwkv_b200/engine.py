@@ -59,6 +59,50 @@ def infer_shape(pack) -> RWKV7Shape:
     return RWKV7Shape(L, int(C), int(N), int(F), int(V), int(rw), int(ra), int(rv), int(rg))
 
 
+class ModelUpload:
+    """A packed model resident in HBM plus its ``rwkvb_model_desc`` (weights in one
+    ``WeightArena``, fp32 vectors in one ``VectorArena``)."""
+
+    def __init__(self, pack, device: torch.device):
+        s = infer_shape(pack)
+        mats, vecs = [], {}
+        for name, e in pack.items():
+            if e.codec in ("sg8", "lut2"):
+                mats.append((name, e.payload, (int(e.shape[0]), int(e.shape[1])), e.codec))
+            else:
+                vecs[name] = np.asarray(e.payload, dtype=np.float32).reshape(-1) \
+                    if not isinstance(e.payload, torch.Tensor) else e.payload
+        self.weights = WeightArena(mats, device)
+        self.vectors = VectorArena(vecs, device)
+        for i in range(s.n_layer):
+            nm = f"blocks.{i}.att.r_k"
+            if nm in self.weights:
+                self.vectors.add_decoded(nm, self.weights[nm])
+        torch.cuda.synchronize(device)
+        self.layers = (native.LayerDesc * s.n_layer)()
+        for i in range(s.n_layer):
+            d = self.layers[i]
+            for suffix in _MATS:
+                name = f"blocks.{i}.{suffix}"
+                if name in self.weights:
+                    setattr(d, _DESC_FIELD[suffix], self.weights[name].desc)
+            for suffix, field in _VEC_FIELD.items():
+                name = f"blocks.{i}.{suffix}"
+                if name in self.vectors.offs or name in self.vectors.extra:
+                    setattr(d, field, self.vectors.ptr(name))
+            d.r_k = self.vectors.ptr(f"blocks.{i}.att.r_k")
+        md = native.ModelDesc()
+        md.n_layer, md.n_embd, md.head_size, md.ffn, md.vocab = s.n_layer, s.n_embd, s.head_size, s.ffn, s.vocab
+        md.emb = self.weights["emb.weight"].desc
+        md.head = self.weights["head.weight"].desc
+        md.ln0_w = self.vectors.ptr("blocks.0.ln0.weight")
+        md.ln0_b = self.vectors.ptr("blocks.0.ln0.bias")
+        md.ln_out_w = self.vectors.ptr("ln_out.weight")
+        md.ln_out_b = self.vectors.ptr("ln_out.bias")
+        md.layers = self.layers
+        self.md = md
+
+
 class B200Engine:
     """A packed RWKV-7 model resident on one GPU, decoded by the fused engine."""
 
@@ -71,41 +115,8 @@ class B200Engine:
         self.shape = infer_shape(pack)
         s = self.shape
         with torch.cuda.device(self.device):
-            mats, vecs = [], {}
-            for name, e in pack.items():
-                if e.codec in ("sg8", "lut2"):
-                    mats.append((name, e.payload, (int(e.shape[0]), int(e.shape[1])), e.codec))
-                else:
-                    vecs[name] = np.asarray(e.payload, dtype=np.float32).reshape(-1) \
-                        if not isinstance(e.payload, torch.Tensor) else e.payload
-            self.weights = WeightArena(mats, self.device)
-            self.vectors = VectorArena(vecs, self.device)
-            for i in range(s.n_layer):
-                nm = f"blocks.{i}.att.r_k"
-                if nm in self.weights:
-                    self.vectors.add_decoded(nm, self.weights[nm])
-            torch.cuda.synchronize(self.device)
-            self._layers = (native.LayerDesc * s.n_layer)()
-            for i in range(s.n_layer):
-                d = self._layers[i]
-                for suffix in _MATS:
-                    name = f"blocks.{i}.{suffix}"
-                    if name in self.weights:
-                        setattr(d, _DESC_FIELD[suffix], self.weights[name].desc)
-                for suffix, field in _VEC_FIELD.items():
-                    name = f"blocks.{i}.{suffix}"
-                    if name in self.vectors.offs or name in self.vectors.extra:
-                        setattr(d, field, self.vectors.ptr(name))
-                d.r_k = self.vectors.ptr(f"blocks.{i}.att.r_k")
-            md = native.ModelDesc()
-            md.n_layer, md.n_embd, md.head_size, md.ffn, md.vocab = s.n_layer, s.n_embd, s.head_size, s.ffn, s.vocab
-            md.emb = self.weights["emb.weight"].desc
-            md.head = self.weights["head.weight"].desc
-            md.ln0_w = self.vectors.ptr("blocks.0.ln0.weight")
-            md.ln0_b = self.vectors.ptr("blocks.0.ln0.bias")
-            md.ln_out_w = self.vectors.ptr("ln_out.weight")
-            md.ln_out_b = self.vectors.ptr("ln_out.bias")
-            md.layers = self._layers
+            self._model = ModelUpload(pack, self.device)
+            md = self._model.md
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
             if not persistent:
                 flags |= native.FLAG_NO_PERSISTENT
@@ -228,3 +239,99 @@ class B200Engine:
         if n_new > 1:
             ids += self.decode_greedy(first, n_new - 1)
         return ids, None
+
+
+class B200BatchEngine:
+    """``batch`` (<= 64) independent sessions of one packed RWKV-7 model decoded
+    together: one token step advances every session, with every projection a
+    tcgen05 batched GEMM (``rwkvb_batch_*`` in the C ABI).
+
+    The reference batches sessions with ``rwkv7_batch`` (ChatRWKV, not vendored)
+    and otherwise loops sessions through ``forward_block_packed``; per session
+    the result is that loop's, token for token.  State per layer and session
+    keeps the ``RecurrentState.rwkv7_state`` triple."""
+
+    def __init__(self, pack, batch: int, *, device: int | torch.device = 0, use_graph: bool = True):
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("B200BatchEngine needs a CUDA device; there is no CPU path")
+        self.lib = native.lib()
+        self.shape = infer_shape(pack)
+        self.batch = int(batch)
+        s = self.shape
+        with torch.cuda.device(self.device):
+            self._model = ModelUpload(pack, self.device)
+            flags = 0 if use_graph else native.FLAG_NO_GRAPH
+            h = ctypes.c_void_p()
+            native.check(self.lib.rwkvb_batch_create(ctypes.byref(self._model.md), self.batch, flags,
+                                                     ctypes.byref(h)), "rwkvb_batch_create")
+            self._h = h
+            att, wkv, ffn, logits = (ctypes.c_void_p() for _ in range(4))
+            native.check(self.lib.rwkvb_batch_buffers(h, ctypes.byref(att), ctypes.byref(wkv), ctypes.byref(ffn),
+                                                      ctypes.byref(logits)), "rwkvb_batch_buffers")
+            L, C, H, N, B = s.n_layer, s.n_embd, s.n_head, s.head_size, self.batch
+            dev = self.device
+            self.att_x = torch.as_tensor(_CudaArray(att.value, (L, B, C)), device=dev)
+            self.wkv = torch.as_tensor(_CudaArray(wkv.value, (L, B, H, N, N)), device=dev)
+            self.ffn_x = torch.as_tensor(_CudaArray(ffn.value, (L, B, C)), device=dev)
+            self.logits = torch.as_tensor(_CudaArray(logits.value, (B, s.vocab)), device=dev)
+            n = ctypes.c_int32()
+            native.check(self.lib.rwkvb_batch_launches_per_step(h, ctypes.byref(n)), "launches_per_step")
+            self.launches_per_step = int(n.value)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            torch.cuda.synchronize(self.device)
+            self.lib.rwkvb_batch_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _stream(self, stream=None) -> int:
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        return st.cuda_stream
+
+    def reset(self, stream=None) -> None:
+        native.check(self.lib.rwkvb_batch_reset(self._h, self._stream(stream)), "rwkvb_batch_reset")
+
+    def forward(self, tokens, stream=None) -> torch.Tensor:
+        """One step: session b consumes ``tokens[b]``; returns the device logits ``[batch, vocab]``."""
+        if len(tokens) != self.batch:
+            raise ValueError(f"expected {self.batch} tokens, got {len(tokens)}")
+        toks = (ctypes.c_int32 * self.batch)(*[int(t) for t in tokens])
+        native.check(self.lib.rwkvb_batch_forward(self._h, toks, self._stream(stream)), "rwkvb_batch_forward")
+        return self.logits
+
+    def decode_greedy(self, n: int, stream=None) -> np.ndarray:
+        """``n`` greedy steps from the argmax of the current logits: ids ``[n, batch]``."""
+        out = np.zeros((max(n, 1), self.batch), dtype=np.int32)
+        native.check(self.lib.rwkvb_batch_decode_greedy(self._h, int(n),
+                                                        out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                                        self._stream(stream)), "rwkvb_batch_decode_greedy")
+        return out[:n]
+
+    def decode_greedy_async(self, n: int, out: torch.Tensor, stream=None) -> None:
+        if out.dtype != torch.int32 or not out.is_cuda or out.numel() < n * self.batch:
+            raise ValueError("out must be a CUDA int32 tensor with at least n * batch elements")
+        native.check(self.lib.rwkvb_batch_decode_greedy_async(self._h, int(n), out.data_ptr(),
+                                                              self._stream(stream)),
+                     "rwkvb_batch_decode_greedy_async")
+
+    def get_state(self, b: int) -> list[torch.Tensor]:
+        """Clone of session ``b``'s state as ``RecurrentState.rwkv7_state`` (3 tensors per layer)."""
+        out = []
+        for i in range(self.shape.n_layer):
+            out += [self.att_x[i, b].clone(), self.wkv[i, b].clone(), self.ffn_x[i, b].clone()]
+        return out
+
+    def set_state(self, b: int, state: list[torch.Tensor]) -> None:
+        if len(state) != 3 * self.shape.n_layer:
+            raise ValueError(f"expected {3 * self.shape.n_layer} state tensors, got {len(state)}")
+        for i in range(self.shape.n_layer):
+            self.att_x[i, b].copy_(state[3 * i].reshape(-1).to(self.device, torch.float32))
+            self.wkv[i, b].copy_(state[3 * i + 1].reshape(self.wkv[i, b].shape).to(self.device, torch.float32))
+            self.ffn_x[i, b].copy_(state[3 * i + 2].reshape(-1).to(self.device, torch.float32))

@@ -113,6 +113,14 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_engine_decode_greedy_async": (ctypes.c_int, [vp, i32, i32, vp, vp]),
         "rwkvb_engine_launches_per_step": (ctypes.c_int, [vp, P(i32)]),
         "rwkvb_engine_trace": (ctypes.c_int, [vp, P(u64), i32, P(i32)]),
+        "rwkvb_batch_create": (ctypes.c_int, [P(ModelDesc), i32, u32, P(vp)]),
+        "rwkvb_batch_destroy": (ctypes.c_int, [vp]),
+        "rwkvb_batch_buffers": (ctypes.c_int, [vp, P(vp), P(vp), P(vp), P(vp)]),
+        "rwkvb_batch_reset": (ctypes.c_int, [vp, vp]),
+        "rwkvb_batch_forward": (ctypes.c_int, [vp, P(i32), vp]),
+        "rwkvb_batch_decode_greedy": (ctypes.c_int, [vp, i32, P(i32), vp]),
+        "rwkvb_batch_decode_greedy_async": (ctypes.c_int, [vp, i32, vp, vp]),
+        "rwkvb_batch_launches_per_step": (ctypes.c_int, [vp, P(i32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(h, name)  # AttributeError if the build lacks a declared symbol
