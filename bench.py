@@ -16,6 +16,10 @@ token's argmax is read back to the host and the token is sent to the device
 through the C ABI before the next step.  The timed regions sit inside NVTX
 ranges ``timed`` and ``e2e``.
 
+``batched`` (key of the same line) is the bs64 leg: ``--sessions`` sessions
+decoded together through ``B200BatchEngine`` (tcgen05 batched GEMMs), one
+step = one token for every session.
+
 ``--impl reference`` times the reference's own C kernels (built from its
 sources into ``oracle/_ref``) driving the packed RWKV-7 forward on the host
 cores, on the same workload and metric (rank 0 only).
@@ -193,6 +197,84 @@ def run_reference(args, shape, rank: int) -> dict:
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def run_batched(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) -> dict:
+    """The batched leg: ``args.sessions`` sessions decoded together (tcgen05 GEMMs).
+
+    One step = one token for every session.  Algorithmic bytes per step: the
+    weights once (the batch-1 token bytes less its state traffic), plus the
+    recurrent state read and written for every session and one embedding row
+    per session."""
+    import torch.distributed as dist
+
+    nb = eng.batch
+    C, L, H = shape.n_embd, shape.n_layer, shape.n_head
+    state = L * (2 * C + H * 64 * 64) * 4
+    emb_row = C + (C // 128) * 8
+    step_bytes = bpt - 2 * state + nb * 2 * state + (nb - 1) * emb_row
+    prompts = [synth_prompt(PROMPT, shape.vocab, SEED + 7 * b + rank) for b in range(nb)]
+    for pos in range(PROMPT):
+        eng.forward([p[pos] for p in prompts])
+    out = torch.empty((max(args.batch_steps, args.warmup) + 1) * nb, dtype=torch.int32, device=dev)
+    eng.decode_greedy_async(args.warmup, out)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    _nvtx_push("timed_batched")
+    t0.record(stream)
+    eng.decode_greedy_async(args.batch_steps, out)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    _nvtx_pop()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    ms_step = ms / args.batch_steps
+    # end to end: per step the session tokens go host->device through the C ABI
+    # and the argmax ids come back device->host
+    e_steps = min(16, args.batch_steps)
+    toks = eng.logits.argmax(dim=1).to(torch.int32).cpu().tolist()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        eng.forward(toks)
+        toks = eng.logits.argmax(dim=1).to(torch.int32).cpu().tolist()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    peak, peak_kind = _peaks()
+    achieved = step_bytes / (ms_step / 1e3) / 1e9
+    eng.close()
+    return {"metric": f"RWKV-7 {args.config} U8 decode tok/s (bs{nb})", "value": nb * world / (ms_step / 1e3),
+            "unit": "tok/s", "sessions_per_gpu": nb, "steps": args.batch_steps, "warmup": args.warmup,
+            "ms_per_step": ms_step, "gpu_launches": eng.launches_per_step * args.batch_steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "algorithmic_bytes_per_step": step_bytes,
+                         "what": f"whole batched step ({eng.launches_per_step} launches in one CUDA graph): "
+                                 f"weights once + {nb} sessions' state read and written; peak: {peak_kind} "
+                                 "HBM copy bandwidth"},
+            "e2e": {"value": e_steps * nb * world / (e_ms / 1e3), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * nb, "d2h_bytes_per_step": 4 * nb, "steps": e_steps,
+                    "how": "B200BatchEngine.forward(host ids) + per-session argmax read back each step"}}
+
+
+def synth_prompt(n: int, vocab: int, seed: int) -> list[int]:
+    from rwkv_b200 import synth
+
+    return synth.seeded_prompt(n, vocab, seed)
+
+
 def cpu_baseline(pack_dev, shape, args) -> dict:
     from oracle import kernels as ok
     from oracle.forward import OracleRWKV7
@@ -232,6 +314,8 @@ def main() -> None:
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--ref-budget-s", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sessions", type=int, default=64, help="batched-decode sessions (0: skip the batched leg)")
+    ap.add_argument("--batch-steps", type=int, default=64)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -268,6 +352,11 @@ def main() -> None:
     backend.prepare_provider(provider)
     eng = backend._engine
     cpu_pack = pack if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    batch_eng = None
+    if args.sessions > 0 and args.policy == "sg8":
+        from rwkv_b200.engine import B200BatchEngine
+
+        batch_eng = B200BatchEngine(pack, args.sessions, device=local)
     del pack
     provider.pack, provider._fused = {}, {}
     torch.cuda.empty_cache()
@@ -333,6 +422,8 @@ def main() -> None:
         e2e_ms = float(tt.item())
     e2e_val = e2e_steps * world / (e2e_ms / 1e3)
 
+    batched = run_batched(batch_eng, args, shape, bpt, dev, stream, world, rank) if batch_eng is not None else None
+
     if rank == 0:
         peak, peak_kind = _peaks()
         achieved = bpt / (ms_step / 1e3) / 1e9
@@ -370,6 +461,8 @@ def main() -> None:
                            "host, token sent back through rwkvb_engine_forward (one persistent launch per token)"},
             "clocks": clk,
         }
+        if batched is not None:
+            res["batched"] = batched
         if cpu_pack is not None:
             backend.close()
             res["cpu_baseline"] = cpu_baseline(cpu_pack, shape, args)
