@@ -85,7 +85,7 @@ int bg_setup(BgArgs* a, const BgJob* jobs, int njobs, const BgDigits* dg, int nd
     const uint32_t box[2] = {128, (uint32_t)a->nrows};
     const int st = encode_u8_map(&a->bmap[d], 2, dg[d].rows, dims, strides, box, true);
     if (st != RWKVB_OK) return st;
-    a->cs[d] = dg[d].cs;
+    a->cs[d] = reinterpret_cast<const float*>(dg[d].cs);
   }
   int total = 0;
   for (int j = 0; j < njobs; ++j) {
@@ -244,11 +244,20 @@ __device__ __forceinline__ int bt_npieces(const BtPieces& p, int n) {
   return bg_cta_of(f + p.G - 1, p.total, p.ncta) - bg_cta_of(f, p.total, p.ncta) + 1;
 }
 
-// Sum of the pieces of element (b, n) of a GEMM output [pieces][nb][rows].
+// Sum of the pieces of element (b, n) of a GEMM output [pieces][nb][rows], in
+// piece order; the loads are independent and issued together.
 __device__ __forceinline__ float bt_fold(const float* part, const BtPieces& p, int nb, int rows, int b, int n) {
   const int np = bt_npieces(p, n);
-  float s = 0.f;
-  for (int q = 0; q < np; ++q) s += part[((size_t)q * nb + b) * rows + n];
+  const float* q = part + (size_t)b * rows + n;
+  const size_t st = (size_t)nb * rows;
+  float v[12];
+#pragma unroll
+  for (int u = 0; u < 12; ++u) v[u] = u < np ? q[u * st] : 0.f;
+  float s = v[0];
+#pragma unroll
+  for (int u = 1; u < 12; ++u)
+    if (u < np) s += v[u];
+  for (int u = 12; u < np; ++u) s += q[u * st];
   return s;
 }
 
@@ -321,13 +330,15 @@ struct BtInArgs {
   int C, nb, bp, lfk;
 };
 
-__global__ void __launch_bounds__(kBtThreads) bt_in_kernel(BtInArgs a) {
+constexpr int kBtRowThreads = 1024;  // per-session row kernels (one CTA per session)
+
+__global__ void __launch_bounds__(kBtRowThreads) bt_in_kernel(BtInArgs a) {
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
   const int b = blockIdx.x, C = a.C;
   float* xl = bt_sm;       // ln output
   float* prev = xl + C;    // previous ln output (token shift)
-  float* tmp = prev + C;   // one mix
+  float* mixed = prev + C; // r, k, v inputs [3][C]
   for (int i = threadIdx.x; i < C; i += blockDim.x) {
     float v;
     if (a.part) {
@@ -345,26 +356,32 @@ __global__ void __launch_bounds__(kBtThreads) bt_in_kernel(BtInArgs a) {
     return;
   }
   float* st = a.state + (size_t)b * C;
+  const float *mr = a.mix[0], *mw = a.mix[1], *mk = a.mix[2], *mv = a.mix[3], *ma = a.mix[4], *mg = a.mix[5];
+  float* xw = a.xa4 + (size_t)b * C;
+  float* xa = xw + (size_t)a.nb * C;
+  float* xg = xa + (size_t)a.nb * C;
+  float* xv = xg + (size_t)a.nb * C;
   for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    prev[i] = st[i];
-    st[i] = xl[i];
+    const float z = xl[i], p = st[i], d = p - z;
+    st[i] = z;
+    mixed[i] = z + d * mr[i];
+    mixed[C + i] = z + d * mk[i];
+    const float vv = z + d * mv[i];
+    mixed[2 * C + i] = vv;
+    xw[i] = z + d * mw[i];
+    xa[i] = z + d * ma[i];
+    xg[i] = z + d * mg[i];
+    xv[i] = vv;
   }
   __syncthreads();
-  // r, k, v (mix 0, 2, 3): digit rows
-  const int dmix[3] = {0, 2, 3};
-  for (int j = 0; j < 3; ++j) {
-    const float* mx = a.mix[dmix[j]];
-    for (int i = threadIdx.x; i < C; i += blockDim.x) tmp[i] = xl[i] + (prev[i] - xl[i]) * mx[i];
-    __syncthreads();
-    bt_digits_block(tmp, C, a.lfk, a.dig[j], a.cs[j], b, a.bp);
-    __syncthreads();
-  }
-  // w, a, g, v adapter inputs (mix 1, 4, 5, 3), fp32
-  const int amix[4] = {1, 4, 5, 3};
-  for (int j = 0; j < 4; ++j) {
-    const float* mx = a.mix[amix[j]];
-    float* o = a.xa4 + ((size_t)j * a.nb + b) * C;
-    for (int i = threadIdx.x; i < C; i += blockDim.x) o[i] = xl[i] + (prev[i] - xl[i]) * mx[i];
+  // digit rows of r, k, v: one warp per (input, group)
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int G = C >> a.lfk, per = 1 << (a.lfk - 5);
+  for (int w = warp; w < 3 * G; w += nw) {
+    const int j = w / G, g = w - j * G;
+    const float* src = mixed + (size_t)j * C + ((size_t)g << a.lfk) + lane * per;
+    float v[4] = {src[0], src[1], per == 4 ? src[2] : 0.f, per == 4 ? src[3] : 0.f};
+    bg_emit_group(v, per, a.dig[j], a.cs[j], (size_t)C, ((size_t)g << a.lfk) + lane * per, b, a.bp, g);
   }
 }
 
@@ -375,14 +392,18 @@ struct BtAdp1Args {
   int R[4], off[4];
   int blk0[5];      // first column block of each adapter; blk0[nm] = blocks
   int nm;
+  int fast[4];      // SG8, R % 32 == 0, 16-byte aligned codes, group >= 32: vector tile loads
   const float* xa4; // [4][nb][C]
   float* out;       // [splits][nb][rtot]
   int C, nb, rtot;
 };
 
+constexpr int kBtXsStride = 68;  // padded session stride of the staged inputs (bank spread, float4 aligned)
+
 __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
-  __shared__ __align__(16) float xs[kBtAdpKc * 64];          // [kc][64 sessions]
-  __shared__ __align__(16) float ws[kBtAdpKc * kBtAdpCols];  // [kc][32 columns]
+  extern __shared__ __align__(16) float bt_sm[];
+  float* xs = bt_sm;                          // [kc][68]: inputs of 64 sessions
+  float* ws = xs + kBtAdpKc * kBtXsStride;    // [kc][32]: dequantised weights
   const int t = threadIdx.x;
   int m = 0;
   while (m + 1 < a.nm && (int)blockIdx.x >= a.blk0[m + 1]) ++m;
@@ -393,18 +414,38 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
   const float* xsrc = a.xa4 + (size_t)m * a.nb * a.C;
   for (int idx = t; idx < kBtAdpKc * 64; idx += blockDim.x) {
     const int b = idx / kBtAdpKc, kk = idx - b * kBtAdpKc;
-    xs[kk * 64 + b] = b < a.nb ? xsrc[(size_t)b * a.C + k0 + kk] : 0.f;
+    xs[kk * kBtXsStride + b] = b < a.nb ? xsrc[(size_t)b * a.C + k0 + kk] : 0.f;
   }
-  for (int idx = t; idx < kBtAdpKc * kBtAdpCols; idx += blockDim.x) {
-    const int kk = idx / kBtAdpCols, j = idx - kk * kBtAdpCols;
-    ws[idx] = c0 + j < R ? packed_at(W, k0 + kk, c0 + j) : 0.f;
+  if (a.fast[m]) {
+    // one thread per (row, 16 codes): the row's 32 codes are contiguous
+    for (int idx = t; idx < kBtAdpKc * 2; idx += blockDim.x) {
+      const int kk = idx >> 1, hlf = idx & 1;
+      const uint64_t e0 = (uint64_t)(k0 + kk) * R + c0 + 16 * hlf;
+      const uint4 q = *reinterpret_cast<const uint4*>(W.payload + e0);
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+      const float2* pr = reinterpret_cast<const float2*>(W.meta);
+      const uint64_t g0 = e0 >> W.lg, g1 = (e0 + 15) >> W.lg;
+      const float2 p0 = __ldg(pr + g0), p1 = __ldg(pr + g1);
+      const uint64_t split = (g1 << W.lg) - e0;  // first element of group g1 (<= 16 when g1 != g0)
+      float* dst = ws + kk * kBtAdpCols + 16 * hlf;
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const float2 pp = (g1 != g0 && (uint64_t)u >= split) ? p1 : p0;
+        dst[u] = sg8_dequant((qw[u >> 2] >> (8 * (u & 3))) & 0xffu, pp.x, pp.y);
+      }
+    }
+  } else {
+    for (int idx = t; idx < kBtAdpKc * kBtAdpCols; idx += blockDim.x) {
+      const int kk = idx / kBtAdpCols, j = idx - kk * kBtAdpCols;
+      ws[idx] = c0 + j < R ? packed_at(W, k0 + kk, c0 + j) : 0.f;
+    }
   }
   __syncthreads();
   const int bq = t & 15, jq = t >> 4;
   float acc[4][2] = {};
 #pragma unroll 4
   for (int kk = 0; kk < kBtAdpKc; ++kk) {
-    const float4 xv = *reinterpret_cast<const float4*>(xs + kk * 64 + 4 * bq);
+    const float4 xv = *reinterpret_cast<const float4*>(xs + kk * kBtXsStride + 4 * bq);
     const float2 wv = *reinterpret_cast<const float2*>(ws + kk * kBtAdpCols + 2 * jq);
     acc[0][0] = fmaf(xv.x, wv.x, acc[0][0]);
     acc[0][1] = fmaf(xv.x, wv.y, acc[0][1]);
@@ -427,8 +468,9 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
   }
 }
 
-// mid[b][j] = act(sum over splits of out[s][b][j]): tanh for w, sigmoid for g.
-__global__ void bt_adpr_kernel(float* mid, const float* part, int splits, int nb, int rtot, int used, int rw,
+// midT[j][b] = act(sum over splits of out[s][b][j]): tanh for w, sigmoid for g
+// (transposed, 64 sessions per row, for the second stages).
+__global__ void bt_adpr_kernel(float* midT, const float* part, int splits, int nb, int rtot, int used, int rw,
                                int ra, int rg) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nb * used) return;
@@ -437,7 +479,7 @@ __global__ void bt_adpr_kernel(float* mid, const float* part, int splits, int nb
   for (int q = 0; q < splits; ++q) s += part[((size_t)q * nb + b) * rtot + j];
   if (j < rw) s = tanhf(s);
   else if (j >= rw + ra && j < rw + ra + rg) s = sigmoidf_(s);
-  mid[(size_t)b * rtot + j] = s;
+  midT[(size_t)j * 64 + b] = s;
 }
 
 // ------------------------------------------------ adapter second stages
@@ -445,7 +487,8 @@ __global__ void bt_adpr_kernel(float* mid, const float* part, int splits, int nb
 struct BtAdp2Args {
   PackedView w[4];  // w2, a2, g2, v2: [R_m][C]
   int R[4], off[4];
-  const float* mid; // [nb][rtot]
+  int fast[4];      // SG8, group >= 64, 16-byte aligned codes: vector tile loads
+  const float* midT; // [rtot][64]
   float* out;       // [4][nb][C]
   int C, nb, rtot;
 };
@@ -464,13 +507,25 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
   for (int r0 = 0; r0 < R; r0 += kBtAdp2Rc) {
     const int rc = min(kBtAdp2Rc, R - r0);
     __syncthreads();
-    for (int idx = t; idx < rc * 64; idx += blockDim.x) {
-      const int b = idx / rc, r = idx - b * rc;
-      ms[r * 64 + b] = b < a.nb ? a.mid[(size_t)b * a.rtot + a.off[m] + r0 + r] : 0.f;
-    }
-    for (int idx = t; idx < rc * 64; idx += blockDim.x) {
-      const int r = idx >> 6, j = idx & 63;
-      ws[idx] = packed_at(W, r0 + r, c0 + j);
+    for (int idx = t; idx < rc * 16; idx += blockDim.x)
+      reinterpret_cast<float4*>(ms)[idx] =
+          reinterpret_cast<const float4*>(a.midT + (size_t)(a.off[m] + r0) * 64)[idx];
+    if (a.fast[m]) {
+      for (int idx = t; idx < rc * 4; idx += blockDim.x) {
+        const int r = idx >> 2, p = idx & 3;
+        const uint64_t e0 = (uint64_t)(r0 + r) * a.C + c0 + 16 * p;
+        const uint4 q = *reinterpret_cast<const uint4*>(W.payload + e0);
+        const float2 pp = __ldg(reinterpret_cast<const float2*>(W.meta) + (e0 >> W.lg));
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        float* dst = ws + r * 64 + 16 * p;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) dst[u] = sg8_dequant((qw[u >> 2] >> (8 * (u & 3))) & 0xffu, pp.x, pp.y);
+      }
+    } else {
+      for (int idx = t; idx < rc * 64; idx += blockDim.x) {
+        const int r = idx >> 6, j = idx & 63;
+        ws[idx] = packed_at(W, r0 + r, c0 + j);
+      }
     }
     __syncthreads();
     for (int r = 0; r < rc; ++r) {
@@ -504,56 +559,106 @@ struct BtWkvArgs {
   int C, H, nb, layer0;
 };
 
-__global__ void __launch_bounds__(kBtThreads) bt_wkv_kernel(BtWkvArgs a) {
-  __shared__ float red[32];
-  __shared__ __align__(16) float sv6[7 * 64];
-  float *sr = sv6, *sd = sv6 + 64, *sk = sv6 + 128, *sv = sv6 + 192, *skk = sv6 + 256, *ska = sv6 + 320,
-        *sy = sv6 + 384;
-  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x, C = a.C;
-  const int ch = h * 64 + (t & 63);
-  float r = 0.f, k = 0.f, v = 0.f, wv = 0.f, av = 0.f, gv = 0.f, vv = 0.f;
-  if (t < 64) {
-    r = bt_fold(a.part[0], a.pp[0], a.nb, C, b, ch);
-    k = bt_fold(a.part[1], a.pp[1], a.nb, C, b, ch);
-    v = bt_fold(a.part[2], a.pp[2], a.nb, C, b, ch);
-    wv = a.adp2[((size_t)0 * a.nb + b) * C + ch];
-    av = a.adp2[((size_t)1 * a.nb + b) * C + ch];
-    gv = a.adp2[((size_t)2 * a.nb + b) * C + ch];
-    if (!a.layer0) vv = a.adp2[((size_t)3 * a.nb + b) * C + ch];
+constexpr int kBtWkvSess = 4;  // sessions per CTA (64 threads each: thread = state row = channel)
+
+// Named barrier 1 + j over the 64 threads of session slot j (ids as immediates).
+__device__ __forceinline__ void bt_bar64(int j) {
+  switch (j) {
+    case 0: asm volatile("bar.sync 1, 64;" ::: "memory"); break;
+    case 1: asm volatile("bar.sync 2, 64;" ::: "memory"); break;
+    case 2: asm volatile("bar.sync 3, 64;" ::: "memory"); break;
+    default: asm volatile("bar.sync 4, 64;" ::: "memory"); break;
   }
-  const float kkv = t < 64 ? k * a.k_k[ch] : 0.f;
-  const float nrm = sqrtf(block_sum(kkv * kkv, red));
-  if (t < 64) {
-    const float aa = sigmoidf_(a.a0[ch] + av);
-    const float kk = kkv / fmaxf(nrm, 1e-12f);
-    const float kn = k * (1.0f + (aa - 1.0f) * a.k_a[ch]);
-    if (a.layer0) {
-      a.vfirst[(size_t)b * C + ch] = v;
-    } else {
-      const float vf = a.vfirst[(size_t)b * C + ch];
-      v = v + (vf - v) * sigmoidf_(a.v0[ch] + vv);
-    }
-    sr[t] = r;
-    sd[t] = expf(-0.606531f * sigmoidf_(a.w0[ch] + wv));
-    sk[t] = kn;
-    sv[t] = v;
-    skk[t] = kk;
-    ska[t] = kk * aa;
+}
+
+// Sum over the 64 threads of session slot j (two warps).
+__device__ __forceinline__ float bt_sum64(float v, float* red, int j) {
+  const int lane = threadIdx.x & 31, wg = (threadIdx.x >> 5) & 1;
+  v = warp_sum(v);
+  if (lane == 0) red[j * 2 + wg] = v;
+  bt_bar64(j);
+  const float r = red[j * 2] + red[j * 2 + 1];
+  bt_bar64(j);
+  return r;
+}
+
+__global__ void __launch_bounds__(kBtThreads, 2) bt_wkv_kernel(BtWkvArgs a) {
+  __shared__ float red[2 * kBtWkvSess];
+  __shared__ __align__(16) float vecs[kBtWkvSess][5][64];  // decay, -kk, kk*a, k, r
+  const int h = blockIdx.x, t = threadIdx.x, j = t >> 6, i = t & 63;
+  const int b = blockIdx.y * kBtWkvSess + j;
+  if (b >= a.nb) return;  // whole 64-thread group: it owns its named barrier
+  const int C = a.C, ch = h * 64 + i;
+  // state row i of (session b, head h), loaded first
+  float4* Srow = reinterpret_cast<float4*>(a.wkv + ((size_t)b * a.H + h) * 4096 + (size_t)i * 64);
+  float4 s4[16];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) s4[u] = Srow[u];
+  const float wv = a.adp2[((size_t)0 * a.nb + b) * C + ch];
+  const float av = a.adp2[((size_t)1 * a.nb + b) * C + ch];
+  const float gv = a.adp2[((size_t)2 * a.nb + b) * C + ch];
+  float vv = 0.f, vf = 0.f;
+  if (!a.layer0) {
+    vv = a.adp2[((size_t)3 * a.nb + b) * C + ch];
+    vf = a.vfirst[(size_t)b * C + ch];
   }
-  __syncthreads();
-  wkv7_head64(a.wkv + ((size_t)b * a.H + h) * 4096, sr, sd, sk, sv, skk, ska, sy);
-  __syncthreads();
-  const float yv = t < 64 ? sy[t] : 0.f;
-  const float mean = block_sum(yv, red) / 64.f;
-  const float dv = t < 64 ? yv - mean : 0.f;
-  const float var = block_sum(dv * dv, red) / 64.f;
-  const float bon = t < 64 ? sr[t] * sk[t] * a.r_k[ch] : 0.f;
-  const float bonus = block_sum(bon, red);
-  if (t < 64) {
-    float o = dv * rsqrtf(var + 64e-5f) * a.lnx_w[ch] + a.lnx_b[ch];
-    o = o + bonus * sv[t];
-    a.att_y[(size_t)b * C + ch] = o * gv;
+  const float r = bt_fold(a.part[0], a.pp[0], a.nb, C, b, ch);
+  const float k = bt_fold(a.part[1], a.pp[1], a.nb, C, b, ch);
+  float v = bt_fold(a.part[2], a.pp[2], a.nb, C, b, ch);
+  const float kkv = k * a.k_k[ch];
+  const float nrm = sqrtf(bt_sum64(kkv * kkv, red, j));
+  const float aa = sigmoidf_(a.a0[ch] + av);
+  const float kk = kkv / fmaxf(nrm, 1e-12f);
+  const float kn = k * (1.0f + (aa - 1.0f) * a.k_a[ch]);
+  if (a.layer0) a.vfirst[(size_t)b * C + ch] = v;
+  else v = v + (vf - v) * sigmoidf_(a.v0[ch] + vv);
+  float* vd = vecs[j][0];
+  float* vkk = vecs[j][1];
+  float* vka = vecs[j][2];
+  float* vk = vecs[j][3];
+  float* vr = vecs[j][4];
+  vd[i] = expf(-0.606531f * sigmoidf_(a.w0[ch] + wv));
+  vkk[i] = -kk;
+  vka[i] = kk * aa;
+  vk[i] = kn;
+  vr[i] = r;
+  bt_bar64(j);
+  // row i:  sa = S (-kk);  S = S diag(d) + sa (kk a)^T + v_i k^T;  y_i = S r
+  float sa = 0.f;
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    const float4 n4 = reinterpret_cast<const float4*>(vkk)[u];
+    sa = fmaf(s4[u].x, n4.x, sa);
+    sa = fmaf(s4[u].y, n4.y, sa);
+    sa = fmaf(s4[u].z, n4.z, sa);
+    sa = fmaf(s4[u].w, n4.w, sa);
   }
+  float y = 0.f;
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    const float4 d4 = reinterpret_cast<const float4*>(vd)[u];
+    const float4 a4 = reinterpret_cast<const float4*>(vka)[u];
+    const float4 k4 = reinterpret_cast<const float4*>(vk)[u];
+    const float4 r4 = reinterpret_cast<const float4*>(vr)[u];
+    float4 n;
+    n.x = s4[u].x * d4.x + sa * a4.x + v * k4.x;
+    n.y = s4[u].y * d4.y + sa * a4.y + v * k4.y;
+    n.z = s4[u].z * d4.z + sa * a4.z + v * k4.z;
+    n.w = s4[u].w * d4.w + sa * a4.w + v * k4.w;
+    y = fmaf(n.x, r4.x, y);
+    y = fmaf(n.y, r4.y, y);
+    y = fmaf(n.z, r4.z, y);
+    y = fmaf(n.w, r4.w, y);
+    Srow[u] = n;
+  }
+  // GroupNorm over the head (eps 64e-5), bonus, gate
+  const float mean = bt_sum64(y, red, j) / 64.f;
+  const float dv = y - mean;
+  const float var = bt_sum64(dv * dv, red, j) / 64.f;
+  const float bonus = bt_sum64(r * kn * a.r_k[ch], red, j);
+  float o = dv * rsqrtf(var + 64e-5f) * a.lnx_w[ch] + a.lnx_b[ch];
+  o = o + bonus * v;
+  a.att_y[(size_t)b * C + ch] = o * gv;
 }
 
 // ------------------------------------------------------------ ffn input
@@ -569,7 +674,7 @@ struct BtFfnArgs {
   int C, nb, bp, lfk;
 };
 
-__global__ void __launch_bounds__(kBtThreads) bt_ffn_kernel(BtFfnArgs a) {
+__global__ void __launch_bounds__(kBtRowThreads) bt_ffn_kernel(BtFfnArgs a) {
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
   const int b = blockIdx.x, C = a.C;
@@ -668,6 +773,18 @@ struct BtLayer {
   BgArgs rkv, o, key, value;
 };
 
+constexpr size_t kBtAdp1Smem = sizeof(float) * (kBtAdpKc * kBtXsStride + kBtAdpKc * kBtAdpCols);
+
+bool bt_aligned16(const uint8_t* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool bt_fast_adp1(const PackedView& w, int R) {
+  return w.kind == RWKVB_KIND_SG8 && w.lg >= 5 && R % 32 == 0 && bt_aligned16(w.payload);
+}
+
+bool bt_fast_adp2(const PackedView& w, int C) {
+  return w.kind == RWKVB_KIND_SG8 && w.lg >= 6 && C % 64 == 0 && bt_aligned16(w.payload);
+}
+
 bool bt_desc_ok(const rwkvb_packed& p, int rows, int cols) {
   return p.data && p.rows == rows && p.cols == cols && p.group_size > 0 &&
          (p.kind == RWKVB_KIND_SG8 || (p.kind >= RWKVB_KIND_LUT2_F32 && p.kind <= RWKVB_KIND_LUT2_IN_RES));
@@ -719,11 +836,14 @@ BtPieces bt_pieces(const BgArgs& a, int job, int grid) {
 int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
   const int C = e->C, nb = e->nb;
   int n = 0;
-#define BT_CHECK()                                  \
-  do {                                              \
-    const int st_ = cuda_status(cudaGetLastError()); \
-    if (st_ != RWKVB_OK) return st_;                \
-    ++n;                                            \
+#define BT_CHECK()                                                                           \
+  do {                                                                                       \
+    const int st_ = cuda_status(cudaGetLastError());                                         \
+    if (st_ != RWKVB_OK) {                                                                   \
+      if (std::getenv("RWKVB_DEBUG")) std::fprintf(stderr, "rwkvb: batched launch at line %d\n", __LINE__); \
+      return st_;                                                                            \
+    }                                                                                        \
+    ++n;                                                                                     \
   } while (0)
   {
     BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, e->tok, e->x, e->step, e->err, C, e->V};
@@ -748,7 +868,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.cs[0] = e->cs_r, a.cs[1] = e->cs_k, a.cs[2] = e->cs_v;
       a.xa4 = e->xa4;
       a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
-      bt_in_kernel<<<nb, kBtThreads, sizeof(float) * 3 * C, s>>>(a);
+      bt_in_kernel<<<nb, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
       BT_CHECK();
     }
     if (bg_launch(ly.rkv, e->g_rkv, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
@@ -769,10 +889,11 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       }
       a.blk0[nm] = blk;
       a.nm = nm;
+      for (int m = 0; m < nm; ++m) a.fast[m] = bt_fast_adp1(a.w[m], a.R[m]);
       a.xa4 = e->xa4;
       a.out = e->adp1;
       a.C = C, a.nb = nb, a.rtot = e->rtot;
-      bt_adp1_kernel<<<dim3(blk, e->adp_splits), kBtThreads, 0, s>>>(a);
+      bt_adp1_kernel<<<dim3(blk, e->adp_splits), kBtThreads, kBtAdp1Smem, s>>>(a);
       BT_CHECK();
       const int used = l0 ? e->rw + e->ra + e->rg : e->rtot;
       bt_adpr_kernel<<<(nb * used + 255) / 256, 256, 0, s>>>(e->mid, e->adp1, e->adp_splits, nb, e->rtot, used,
@@ -790,7 +911,8 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
         a.off[m] = off;
         off += Rm[m];
       }
-      a.mid = e->mid;
+      for (int m = 0; m < nm; ++m) a.fast[m] = bt_fast_adp2(a.w[m], C);
+      a.midT = e->mid;
       a.out = e->adp2;
       a.C = C, a.nb = nb, a.rtot = e->rtot;
       bt_adp2_kernel<<<dim3(C / 64, nm), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
@@ -808,7 +930,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.w0 = ly.w0, a.a0 = ly.a0, a.v0 = ly.v0, a.k_k = ly.k_k, a.k_a = ly.k_a, a.r_k = ly.r_k;
       a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
       a.C = C, a.H = e->H, a.nb = nb, a.layer0 = l0 ? 1 : 0;
-      bt_wkv_kernel<<<dim3(e->H, nb), kBtThreads, 0, s>>>(a);
+      bt_wkv_kernel<<<dim3(e->H, (nb + kBtWkvSess - 1) / kBtWkvSess), kBtThreads, 0, s>>>(a);
       BT_CHECK();
     }
     if (bg_digits(e->dig_y, e->cs_y, e->att_y, C, C, nb, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
@@ -818,7 +940,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     {
       BtFfnArgs a{e->x, e->xm, e->part_o, e->pp_o, ly.ln2_w, ly.ln2_b, ly.ffn_x_k,
                   e->ffn_x + (size_t)l * nb * C, e->dig_f, e->cs_f, C, nb, e->bp, e->lfk};
-      bt_ffn_kernel<<<nb, kBtThreads, sizeof(float) * C, s>>>(a);
+      bt_ffn_kernel<<<nb, kBtRowThreads, sizeof(float) * C, s>>>(a);
       BT_CHECK();
     }
     if (bg_launch(ly.key, e->g_key, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
@@ -845,7 +967,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     a.dig[0] = e->dig_o;
     a.cs[0] = e->cs_o;
     a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
-    bt_in_kernel<<<nb, kBtThreads, sizeof(float) * 3 * C, s>>>(a);
+    bt_in_kernel<<<nb, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
     BT_CHECK();
   }
   if (bg_launch(e->head, e->g_head, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
@@ -963,7 +1085,7 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
       {(void**)&e->xm, 4 * nbC},
       {(void**)&e->xa4, 4 * 4 * nbC},
       {(void**)&e->adp1, 4 * (size_t)e->adp_splits * batch * e->rtot},
-      {(void**)&e->mid, 4 * (size_t)batch * e->rtot},
+      {(void**)&e->mid, 4 * (size_t)64 * e->rtot},
       {(void**)&e->adp2, 4 * 4 * nbC},
       {(void**)&e->vfirst, 4 * nbC},
       {(void**)&e->att_y, 4 * nbC},
@@ -1071,7 +1193,36 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
     if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
     e->pp_head = bt_pieces(e->head, 0, e->g_head);
   }
+  if (st == RWKVB_OK) {
+    // every kernel must be launchable with the block size the step uses
+    struct {
+      const void* fn;
+      int threads;
+      const char* name;
+    } ks[] = {{(const void*)bgemm_kernel, kBgThreads, "bgemm_kernel"},
+              {(const void*)bt_embed_kernel, kBtThreads, "bt_embed_kernel"},
+              {(const void*)bt_in_kernel, kBtRowThreads, "bt_in_kernel"},
+              {(const void*)bt_adp1_kernel, kBtThreads, "bt_adp1_kernel"},
+              {(const void*)bt_adp2_kernel, kBtThreads, "bt_adp2_kernel"},
+              {(const void*)bt_wkv_kernel, kBtThreads, "bt_wkv_kernel"},
+              {(const void*)bt_ffn_kernel, kBtRowThreads, "bt_ffn_kernel"},
+              {(const void*)bt_hdig_kernel, kBtThreads, "bt_hdig_kernel"},
+              {(const void*)bt_argmax_kernel, 1024, "bt_argmax_kernel"}};
+    for (const auto& k : ks) {
+      cudaFuncAttributes fa;
+      if (cudaFuncGetAttributes(&fa, k.fn) != cudaSuccess || fa.maxThreadsPerBlock < k.threads) {
+        if (std::getenv("RWKVB_DEBUG"))
+          std::fprintf(stderr, "rwkvb: %s: max %d threads per block (needs %d), %d registers\n", k.name,
+                       fa.maxThreadsPerBlock, k.threads, fa.numRegs);
+        cudaGetLastError();
+        st = RWKVB_EUNSUPPORTED;
+      }
+    }
+  }
   if (st == RWKVB_OK) st = bg_allow_smem(e->smem_bg);
+  if (st == RWKVB_OK)
+    st = cuda_status(
+        cudaFuncSetAttribute(bt_adp1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBtAdp1Smem));
   if (st == RWKVB_OK) {
     const cudaError_t ce =
         cudaFuncSetAttribute(bt_adp2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1079,7 +1230,7 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
     st = cuda_status(ce);
     if (st == RWKVB_OK)
       st = cuda_status(cudaFuncSetAttribute(bt_in_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)(sizeof(float) * 3 * C)));
+                                            (int)(sizeof(float) * 5 * C)));
   }
   if (st != RWKVB_OK) {
     cudaFree(e->arena);

@@ -25,11 +25,11 @@
 // it touches into piece slot (cta - first cta of the tile); consumers add the
 // pieces of a tile in slot order (deterministic).
 //
-// Roles (10 warps): warp 0 lane 0 issues the TMA loads into a ring of stages;
+// Roles (18 warps): warp 0 lane 0 issues the TMA loads into a ring of stages;
 // warp 1 allocates TMEM (two accumulators of up to 256 columns) and lane 0
 // issues the MMAs, one commit per flush group to the accumulator's "full"
-// barrier and one per stage to the slot's "empty" barrier; warps 2..9 are the
-// epilogue (TMEM lane quarter = warp % 4, sessions split in two halves).
+// barrier and one per stage to the slot's "empty" barrier; warps 2..17 are the
+// epilogue (TMEM lane quarter = warp % 4, 16 sessions per warp).
 // Every wait is bounded: on a limit the CTA sets the error word, drains the
 // copies it issued and returns.
 #pragma once
@@ -42,7 +42,32 @@
 
 namespace rwkvb {
 
-constexpr int kBgWarps = 10;
+// Packed pairs of fp32 (Blackwell f32x2 arithmetic on 64-bit registers).
+__device__ __forceinline__ uint64_t fx2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void fx2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+constexpr int kBgWarps = 18;
 constexpr int kBgThreads = kBgWarps * 32;
 constexpr int kBgMaxMats = 4;
 constexpr int kBgMaxSessions = 64;
@@ -67,7 +92,7 @@ struct BgArgs {
   CUtensorMap amap[kBgMaxMats];   // codes {k, rows}, box {128, 128}, 128-byte swizzle
   CUtensorMap bmap[kBgMaxMats];   // digit rows {k, nrows}, box {128, nrows}, 128-byte swizzle
   BgMat mat[kBgMaxMats];
-  const float2* cs[kBgMaxMats];   // per digit matrix: (c_f, sum_x) [k / group][bp]
+  const float* cs[kBgMaxMats];    // per digit matrix: c_f [k / group][bp] then sum_x (row + bp)
   int nmat;
   int total;                      // stages over all matrices
   int nb, bp, nrows;              // sessions, padded sessions, digit rows (= MMA N)
@@ -125,7 +150,7 @@ __device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, const Bg
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__global__ void __launch_bounds__(kBgThreads, 1) bgemm_kernel(const __grid_constant__ BgArgs a) {
+__global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
   extern __shared__ __align__(1024) uint8_t bg_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bg_smem_raw) + 1023) & ~uintptr_t(1023));
   const int stage_bytes = kBgTileBytes + a.nrows * 128;
@@ -144,7 +169,7 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_kernel(const __grid_const
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 8);
+      mbar_init(&tempty[i], kBgWarps - 2);
     }
     mbar_init(&done_bar, 1);
     s_abort = 0;
@@ -227,11 +252,12 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_kernel(const __grid_const
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2, q4 = warp & 3, half = ew >> 2;
-    const int nch = a.bp >> 4;              // 16-session chunks
-    const int c0 = half ? (nch + 1) >> 1 : 0;
-    const int c1 = half ? nch : (nch + 1) >> 1;
+    // warp w: TMEM lane quarter w % 4, sessions [16 ch, 16 ch + 16) with
+    // ch = (w - 2) / 4; pairs of sessions go through packed f32x2 arithmetic.
+    const int q4 = warp & 3, ch = (warp - 2) >> 2;
+    const bool active = ch < (a.bp >> 4);
     const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16);
+    const uint64_t neg_bias = fx2(-kBgBiasF, -kBgBiasF), inv254 = fx2(kInv254, kInv254);
     uint32_t fl = 0;
     for (int x = lo; x < hi;) {
       const BgSeg sg = bg_segment(a, x, hi);
@@ -239,57 +265,63 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_kernel(const __grid_const
       const int row = sg.t * 128 + q4 * 32 + lane;
       const int gpr = M.k >> M.lg;
       const float2* prow = M.pairs + (size_t)row * gpr;
-      const float2* csm = a.cs[M.digits];
+      const float* csm = a.cs[M.digits] + ch * 16;
       const int nfl = 128 >> M.lg;
-      float acc[32];
+      uint64_t acc[8];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc[i] = 0.f;
-      for (int st = sg.s0; st < sg.s1; ++st) {
-        for (int f = 0; f < nfl; ++f, ++fl) {
-          const int g = st * nfl + f;
-          const float2 pr = __ldg(prow + g);
-          const uint32_t tb = fl & 1;
-          if (!bg_wait(&tfull[tb], (fl >> 1) & 1, a, &s_abort)) goto epi_done;
-          tc_fence_after();
+      for (int i = 0; i < 8; ++i) acc[i] = 0ull;
+      // (min, max) of this row's flush groups, loaded two groups ahead
+      const int g_end = sg.s1 * nfl;
+      float2 pr_a = __ldg(prow + sg.s0 * nfl);
+      float2 pr_b = sg.s0 * nfl + 1 < g_end ? __ldg(prow + sg.s0 * nfl + 1) : make_float2(0.f, 0.f);
+      for (int g = sg.s0 * nfl; g < g_end; ++g, ++fl) {
+        const float2 pr = pr_a;
+        pr_a = pr_b;
+        if (g + 2 < g_end) pr_b = __ldg(prow + g + 2);
+        const uint32_t tb = fl & 1;
+        if (!bg_wait(&tfull[tb], (fl >> 1) & 1, a, &s_abort)) goto epi_done;
+        tc_fence_after();
+        if (active) {
           const uint32_t ta = tl + tb * kBgAccStride;
           const int q = (int)tmem_ld1_sync(ta + 3 * a.bp);
           const int kq = kBgBias - 127 * q;
-          const float dg = (pr.y - pr.x) * kInv255, mn = pr.x;
-          const float2* csg = csm + (size_t)g * a.bp;
+          const float dg = (pr.y - pr.x) * kInv255;
+          const uint64_t dg2 = fx2(dg, dg), mn2 = fx2(pr.x, pr.x);
+          const float* cg = csm + (size_t)g * 2 * a.bp;  // c_f of the chunk's sessions; sum_x at + bp
 #pragma unroll
-          for (int ci = 0; ci < 2; ++ci) {
-            const int cc = c0 + ci;
-            if (cc < c1) {
-              uint32_t d0[16], d1[16], d2[16];
-              tmem_ld16x3_sync(ta + cc * 16, ta + a.bp + cc * 16, ta + 2 * a.bp + cc * 16, d0, d1, d2);
+          for (int hf = 0; hf < 2; ++hf) {  // two rounds of 8 sessions (register budget)
+            const uint32_t co = (uint32_t)(ch * 16 + hf * 8);
+            uint32_t d0[8], d1[8], d2[8];
+            tmem_ld8x3_sync(ta + co, ta + a.bp + co, ta + 2 * a.bp + co, d0, d1, d2);
 #pragma unroll
-              for (int s = 0; s < 16; ++s) {
-                const float2 cx = csg[cc * 16 + s];
-                const float f0 = __int_as_float((int)d0[s] + kq) - kBgBiasF;
-                const float f1 = __int_as_float((int)d1[s] + kq) - kBgBiasF;
-                const float f2 = __int_as_float((int)d2[s] + kq) - kBgBiasF;
-                const float t = fmaf(fmaf(f2, kInv254, f1), kInv254, f0);
-                acc[ci * 16 + s] = fmaf(dg * cx.x, t, fmaf(mn, cx.y, acc[ci * 16 + s]));
-              }
+            for (int s = 0; s < 4; ++s) {
+              const int sp = hf * 4 + s;  // session pair
+              const uint64_t c2 = *reinterpret_cast<const uint64_t*>(cg + 2 * sp);
+              const uint64_t x2 = *reinterpret_cast<const uint64_t*>(cg + a.bp + 2 * sp);
+              const uint64_t f0 = fadd2(
+                  fx2(__int_as_float((int)d0[2 * s] + kq), __int_as_float((int)d0[2 * s + 1] + kq)), neg_bias);
+              const uint64_t f1 = fadd2(
+                  fx2(__int_as_float((int)d1[2 * s] + kq), __int_as_float((int)d1[2 * s + 1] + kq)), neg_bias);
+              const uint64_t f2 = fadd2(
+                  fx2(__int_as_float((int)d2[2 * s] + kq), __int_as_float((int)d2[2 * s + 1] + kq)), neg_bias);
+              const uint64_t t = ffma2(ffma2(f2, inv254, f1), inv254, f0);
+              acc[sp] = ffma2(fmul2(dg2, c2), t, ffma2(mn2, x2, acc[sp]));
             }
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[tb]);
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[tb]);
       }
-      {
+      if (active) {
         float* out = M.out + (size_t)sg.p * a.nb * M.rows + row;
 #pragma unroll
-        for (int ci = 0; ci < 2; ++ci) {
-          const int cc = c0 + ci;
-          if (cc < c1) {
-#pragma unroll
-            for (int s = 0; s < 16; ++s) {
-              const int b = cc * 16 + s;
-              if (b < a.nb) out[(size_t)b * M.rows] = acc[ci * 16 + s];
-            }
-          }
+        for (int s = 0; s < 8; ++s) {
+          float lo_v, hi_v;
+          fx2_unpack(acc[s], lo_v, hi_v);
+          const int b = ch * 16 + 2 * s;
+          if (b < a.nb) out[(size_t)b * M.rows] = lo_v;
+          if (b + 1 < a.nb) out[(size_t)(b + 1) * M.rows] = hi_v;
         }
       }
       x += sg.s1 - sg.s0;
@@ -307,7 +339,8 @@ __global__ void __launch_bounds__(kBgThreads, 1) bgemm_kernel(const __grid_const
 // Digits of one flush group (1 << lfk = 64 or 128 columns, `per` = 2 or 4
 // values per lane in v) for session b: the whole warp calls it.  Writes the
 // three digit bytes (X + 127) of its values at column `col` of rows b, bp + b
-// and 2 bp + b of dig [rows][k], and (c_f, sum_x) to cs[g][b].
+// and 2 bp + b of dig [rows][k], c_f to cs[g][0][b] and sum_x to cs[g][1][b]
+// (cs viewed as float [k / group][2][bp]).
 __device__ __forceinline__ void bg_emit_group(const float (&v)[4], int per, uint8_t* dig, float2* cs, size_t k,
                                               size_t col, int b, int bp, int g) {
   const int lane = threadIdx.x & 31;
@@ -346,7 +379,11 @@ __device__ __forceinline__ void bg_emit_group(const float (&v)[4], int per, uint
     *reinterpret_cast<uint16_t*>(dig + (size_t)(bp + b) * k + col) = (uint16_t)w1;
     *reinterpret_cast<uint16_t*>(dig + (size_t)(2 * bp + b) * k + col) = (uint16_t)w2;
   }
-  if (lane == 0) cs[(size_t)g * bp + b] = make_float2(ldexpf(1.0f, e) / 127.0f, sum);
+  if (lane == 0) {
+    float* cg = reinterpret_cast<float*>(cs) + (size_t)g * 2 * bp;
+    cg[b] = ldexpf(1.0f, e) / 127.0f;
+    cg[bp + b] = sum;
+  }
 }
 
 // Digit rows of nb input vectors (row b of x at x + b * ldx, k columns) for

@@ -90,6 +90,21 @@ __device__ __forceinline__ uint32_t tmem_ld1_sync(uint32_t taddr) {
   return r;
 }
 
+// Three 8-column loads (columns t0.., t1.., t2..) and one wait.
+__device__ __forceinline__ void tmem_ld8x3_sync(uint32_t t0, uint32_t t1, uint32_t t2, uint32_t (&a)[8],
+                                                uint32_t (&b)[8], uint32_t (&c)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%24];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%25];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%26];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(b[0]),
+        "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(c[0]), "=r"(c[1]),
+        "=r"(c[2]), "=r"(c[3]), "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7])
+      : "r"(t0), "r"(t1), "r"(t2)
+      : "memory");
+}
+
 // Three 16-column loads (columns t0.., t1.., t2..) and one wait.
 __device__ __forceinline__ void tmem_ld16x3_sync(uint32_t t0, uint32_t t1, uint32_t t2, uint32_t (&a)[16],
                                                  uint32_t (&b)[16], uint32_t (&c)[16]) {
