@@ -44,6 +44,8 @@ os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
+from rwkv_b200 import replicas  # noqa: E402
+
 SEED = 2026
 PROMPT = 8
 
@@ -211,7 +213,9 @@ def run_batched(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) 
     state = L * (2 * C + H * 64 * 64) * 4
     emb_row = C + (C // 128) * 8
     step_bytes = bpt - 2 * state + nb * 2 * state + (nb - 1) * emb_row
-    prompts = [synth_prompt(PROMPT, shape.vocab, SEED + 7 * b + rank) for b in range(nb)]
+    # global sessions [rank * nb, (rank + 1) * nb): a session's prompt does not depend on the world size
+    prompts = [synth_prompt(PROMPT, shape.vocab, replicas.session_seed(SEED, g))
+               for g in replicas.session_range(nb, rank, world)]
     for pos in range(PROMPT):
         eng.forward([p[pos] for p in prompts])
     out = torch.empty((max(args.batch_steps, args.warmup) + 1) * nb, dtype=torch.int32, device=dev)
@@ -227,11 +231,7 @@ def run_batched(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) 
     t1.record(stream)
     torch.cuda.synchronize(dev)
     _nvtx_pop()
-    ms = t0.elapsed_time(t1)
-    if world > 1:
-        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+    ms = replicas.max_over_ranks(t0.elapsed_time(t1))
     ms_step = ms / args.batch_steps
     # end to end: per step the session tokens go host->device through the C ABI
     # and the argmax ids come back device->host
@@ -248,11 +248,7 @@ def run_batched(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) 
         toks = eng.logits.argmax(dim=1).to(torch.int32).cpu().tolist()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        tt = torch.tensor([e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e_ms = float(tt.item())
+    e_ms = replicas.max_over_ranks(e0.elapsed_time(e1))
     peak, peak_kind = _peaks()
     achieved = step_bytes / (ms_step / 1e3) / 1e9
     eng.close()
@@ -387,10 +383,8 @@ def main() -> None:
     _nvtx_pop()
     ms = t0.elapsed_time(t1)
     clk = clocks.stop() if rank == 0 else {}
+    ms = replicas.max_over_ranks(ms)
     if world > 1:
-        tt = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
         dist.barrier()
     total_tokens = args.steps * world
     value = total_tokens / (ms / 1e3)
@@ -415,11 +409,7 @@ def main() -> None:
     torch.cuda.synchronize(dev)
     _nvtx_pop()
     assert len(emitted) == e2e_steps
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        tt = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
+    e2e_ms = replicas.max_over_ranks(e0.elapsed_time(e1))
     e2e_val = e2e_steps * world / (e2e_ms / 1e3)
 
     batched = run_batched(batch_eng, args, shape, bpt, dev, stream, world, rank) if batch_eng is not None else None

@@ -175,6 +175,8 @@ class CudaB200Backend:
         self._manifest = None
         self._device = torch.device("cuda", 0)
         self._engine = None
+        self._model = None
+        self._batch_engines: dict[int, Any] = {}
         self._last_state: RecurrentState | None = None
         self._lock = threading.Lock()
 
@@ -196,8 +198,12 @@ class CudaB200Backend:
             return
         if not torch.cuda.is_available():
             raise BackendNotAvailableError("cuda_b200 needs a CUDA device")
+        from .engine import ModelUpload
+
         pack = packed_tensors_from_provider(provider)
-        self._engine = B200Engine(pack, device=self._device, use_graph=self.use_graph)
+        with torch.cuda.device(self._device):
+            self._model = ModelUpload(pack, self._device)
+        self._engine = B200Engine(self._model, device=self._device, use_graph=self.use_graph)
 
     @property
     def num_layers(self) -> int:
@@ -384,12 +390,47 @@ class CudaB200Backend:
         return self.generate(prompt, provider, max_tokens, metrics)
 
     def generate_greedy_batch(self, prompts: list[str], provider, max_tokens: int, metrics) -> list[list[int]]:
-        return [self.generate(p, provider, max_tokens, metrics) for p in prompts]
+        """Greedy ids for every prompt.  Prompts of equal token length (up to 64,
+        SG8 projections) decode together through the batched engine (one step
+        advances every session); other batches run prompt by prompt.  Each
+        session's ids equal those of ``generate`` on that prompt alone."""
+        self.prepare_provider(provider)
+        ids = [self._encode(p) for p in prompts]
+        n = max(0, int(max_tokens))
+        if not ids:
+            return []
+        same = len({len(t) for t in ids}) == 1 and len(ids[0]) > 0
+        if not (same and 2 <= len(ids) <= 64 and n > 0 and self._model.sg8_projections):
+            return [self.generate(p, provider, max_tokens, metrics) for p in prompts]
+        from .engine import B200BatchEngine
+
+        nb = len(ids)
+        with self._lock:
+            eng = self._batch_engines.get(nb)
+            if eng is None:
+                eng = B200BatchEngine(self._model, nb, device=self._device)
+                self._batch_engines[nb] = eng
+            t0 = time.perf_counter()
+            eng.reset()
+            for pos in range(len(ids[0])):
+                eng.forward([t[pos] for t in ids])
+            first = eng.logits.argmax(dim=1).tolist()
+            rest = eng.decode_greedy(n - 1) if n > 1 else np.zeros((0, nb), np.int32)
+            torch.cuda.synchronize(self._device)
+            if metrics is not None and hasattr(metrics, "tokens_generated"):
+                metrics.tokens_generated = n * nb
+            if metrics is not None and hasattr(metrics, "decode_wall_s"):
+                metrics.decode_wall_s = time.perf_counter() - t0
+        return [[int(first[b])] + [int(v) for v in rest[:, b]] for b in range(nb)]
 
     def close(self) -> None:
+        for eng in self._batch_engines.values():
+            eng.close()
+        self._batch_engines = {}
         if self._engine is not None:
             self._engine.close()
             self._engine = None
+        self._model = None
 
 
 # ------------------------------------------------------------- factory

@@ -65,6 +65,11 @@ class ModelUpload:
 
     def __init__(self, pack, device: torch.device):
         s = infer_shape(pack)
+        self.shape = s
+        self.device = device
+        proj = ("att.receptance.weight", "att.key.weight", "att.value.weight", "att.output.weight",
+                "ffn.key.weight", "ffn.value.weight")
+        self.sg8_projections = all(e.codec == "sg8" for n, e in pack.items() if n.endswith(proj) or n == "head.weight")
         mats, vecs = [], {}
         for name, e in pack.items():
             if e.codec in ("sg8", "lut2"):
@@ -104,7 +109,10 @@ class ModelUpload:
 
 
 class B200Engine:
-    """A packed RWKV-7 model resident on one GPU, decoded by the fused engine."""
+    """A packed RWKV-7 model resident on one GPU, decoded by the fused engine.
+
+    ``pack`` is the packed model, or a ``ModelUpload`` already resident on the
+    device (shared with a ``B200BatchEngine``)."""
 
     def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
                  prefetch_distance: int | None = None, persistent: bool = True, trace: bool = False):
@@ -112,10 +120,9 @@ class B200Engine:
         if self.device.type != "cuda":
             raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
         self.lib = native.lib()
-        self.shape = infer_shape(pack)
-        s = self.shape
         with torch.cuda.device(self.device):
-            self._model = ModelUpload(pack, self.device)
+            self._model = pack if isinstance(pack, ModelUpload) else ModelUpload(pack, self.device)
+            self.shape = s = self._model.shape
             md = self._model.md
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
             if not persistent:
@@ -256,11 +263,10 @@ class B200BatchEngine:
         if self.device.type != "cuda":
             raise ValueError("B200BatchEngine needs a CUDA device; there is no CPU path")
         self.lib = native.lib()
-        self.shape = infer_shape(pack)
         self.batch = int(batch)
-        s = self.shape
         with torch.cuda.device(self.device):
-            self._model = ModelUpload(pack, self.device)
+            self._model = pack if isinstance(pack, ModelUpload) else ModelUpload(pack, self.device)
+            self.shape = s = self._model.shape
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
             h = ctypes.c_void_p()
             native.check(self.lib.rwkvb_batch_create(ctypes.byref(self._model.md), self.batch, flags,

@@ -87,3 +87,16 @@ def test_state_roundtrip_through_recurrent_state(model):
     assert a == c
     assert len(st.rwkv7_state) == 3 * shape.n_layer
     assert tuple(st.rwkv7_state[1].shape) == (shape.n_head, shape.head_size, shape.head_size)
+
+
+def test_generate_greedy_batch_uses_batched_engine_and_matches_generate(model):
+    shape, pack, oracle, b, prov = model
+    prompts = ["alpha-1", "bravo-2", "charli3"]
+    out = b.generate_greedy_batch(prompts, prov, 7, metrics=None)
+    assert 3 in b._batch_engines  # equal-length prompts ran through the batched engine
+    for p, ids in zip(prompts, out):
+        ref, _, _ = oracle.greedy(list(p.encode()), 7)
+        assert ids == ref
+    # unequal lengths fall back to prompt-by-prompt generation with the same results
+    mixed = b.generate_greedy_batch(["ab", "abcd"], prov, 4, metrics=None)
+    assert mixed == [oracle.greedy(list(p.encode()), 4)[0] for p in ("ab", "abcd")]
