@@ -149,7 +149,10 @@ int rwkvb_cmix_gemv_f32_noalloc(float* y, const rwkvb_packed* key, const rwkvb_p
  * on the raw codes and a 3-digit split of x (error <= 6.2e-8 of each group's
  * largest |x|), per-group fp32 scaling, deterministic split-K reduction.
  * `err_word` (device int, may be NULL) gets RWKVB_ETIMEOUT's flag bit if a
- * bounded device wait gave up.  Replaces the batched (2-D x) branch of
+ * bounded device wait gave up.  The tensor maps and the device workspace of a
+ * (weight, batch) pair are built on its first call and kept (up to 32 pairs per
+ * process); calls with the same weight and batch on different streams at the
+ * same time share that workspace and must be serialised by the caller.  Replaces the batched (2-D x) branch of
  * lut2_linear_forward (rwkv_ssd/runtime/lut_gemm_fused.py:1820-1851), which
  * decodes W and calls torch.nn.functional.linear. */
 int rwkvb_gemm_sg8_f32(float* y, const rwkvb_packed* w, const float* x, int32_t batch,

@@ -133,6 +133,17 @@ int bg_setup(BgArgs* a, const BgJob* jobs, int njobs, const BgDigits* dg, int nd
   return RWKVB_OK;
 }
 
+// Pieces per tile of a single-matrix launch (tiles x G stages over min(sms, total) CTAs).
+int bg_pieces_single(int tiles, int G, int sms) {
+  const int total = tiles * G, n = std::min(sms, total);
+  int pmax = 1;
+  for (int t = 0; t < tiles; ++t) {
+    const long long f = (long long)t * G;
+    pmax = std::max(pmax, bg_cta_of(f + G - 1, total, n) - bg_cta_of(f, total, n) + 1);
+  }
+  return pmax;
+}
+
 int bg_launch(const BgArgs& a, int grid, size_t smem, cudaStream_t s) {
   int st = bg_allow_smem(smem);
   if (st != RWKVB_OK) return st;
@@ -159,51 +170,109 @@ int bg_digits(uint8_t* rows, float2* cs, const float* x, int ldx, int k, int nb,
 
 using namespace rwkvb;
 
+namespace rwkvb {
+namespace {
+// Launch description and workspace of one (weight, batch) pair on one device,
+// built on first use and kept: tensor maps, digit rows (constant rows written
+// once), per-session constants, partial sums and an error word.
+struct BgOpEntry {
+  const uint8_t* wdata;
+  int rows, cols, nb, dev;
+  BgArgs a;
+  int grid, pieces;
+  size_t smem;
+  uint8_t* dig;
+  float2* cs;
+  float* part;
+  int* err;
+  uint64_t last_use;
+};
+
+constexpr size_t kBgOpCacheMax = 32;
+std::mutex g_bgop_mu;
+std::vector<BgOpEntry*> g_bgop;
+uint64_t g_bgop_clock = 0;
+
+void bgop_free(BgOpEntry* e) {
+  if (e->dig) cudaFree(e->dig);
+  delete e;
+}
+
+int bgop_get(const rwkvb_packed& w, int nb, cudaStream_t s, BgOpEntry** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RWKVB_ECUDA;
+  std::lock_guard<std::mutex> lock(g_bgop_mu);
+  for (BgOpEntry* e : g_bgop)
+    if (e->wdata == w.data && e->rows == w.rows && e->cols == w.cols && e->nb == nb && e->dev == dev) {
+      e->last_use = ++g_bgop_clock;
+      *out = e;
+      return RWKVB_OK;
+    }
+  BgOpEntry* e = new (std::nothrow) BgOpEntry();
+  if (!e) return RWKVB_EALLOC;
+  e->wdata = w.data, e->rows = w.rows, e->cols = w.cols, e->nb = nb, e->dev = dev;
+  const int K = w.cols, N = w.rows, bp = bg_padded_sessions(nb), nrows = bg_digit_rows(nb);
+  const size_t dig_bytes = (size_t)nrows * K;
+  const size_t cs_off = (dig_bytes + 255) & ~size_t(255);
+  const size_t cs_bytes = sizeof(float2) * (size_t)(K / w.group_size) * bp;
+  const size_t err_off = (cs_off + cs_bytes + 255) & ~size_t(255);
+  const size_t part_off = err_off + 256;
+  // partial sums sized by the pieces per tile of the launch plan
+  const int sms = device_sms();
+  const int pieces = bg_pieces_single(N / 128, K / 128, sms);
+  const size_t part_bytes = sizeof(float) * (size_t)pieces * nb * N;
+  if (cudaMalloc((void**)&e->dig, part_off + part_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    delete e;
+    return RWKVB_EALLOC;
+  }
+  e->cs = reinterpret_cast<float2*>(e->dig + cs_off);
+  e->err = reinterpret_cast<int*>(e->dig + err_off);
+  e->part = reinterpret_cast<float*>(e->dig + part_off);
+  BgDigits dg{e->dig, e->cs, K};
+  BgJob job{&w, 0, e->part};
+  int st = bg_setup(&e->a, &job, 1, &dg, 1, nb, sms, &e->grid, &e->pieces, &e->smem, e->err);
+  if (st == RWKVB_OK && e->pieces != pieces) st = RWKVB_EUNSUPPORTED;
+  if (st == RWKVB_OK) st = bg_digits_init(e->dig, K, nb, s);
+  if (st == RWKVB_OK) st = cuda_status(cudaMemsetAsync(e->err, 0, sizeof(int), s));
+  if (st != RWKVB_OK) {
+    bgop_free(e);
+    return st;
+  }
+  if (g_bgop.size() >= kBgOpCacheMax) {  // evict the least recently used entry
+    size_t victim = 0;
+    for (size_t i = 1; i < g_bgop.size(); ++i)
+      if (g_bgop[i]->last_use < g_bgop[victim]->last_use) victim = i;
+    cudaStreamSynchronize(s);
+    bgop_free(g_bgop[victim]);
+    g_bgop.erase(g_bgop.begin() + (long)victim);
+  }
+  e->last_use = ++g_bgop_clock;
+  g_bgop.push_back(e);
+  *out = e;
+  return RWKVB_OK;
+}
+}  // namespace
+}  // namespace rwkvb
+
 extern "C" int rwkvb_gemm_sg8_f32(float* y, const rwkvb_packed* w, const float* x, int32_t batch, int32_t* err_word,
                                   void* stream) {
   if (!y || !w || !x || batch <= 0 || batch > kBgMaxSessions) return RWKVB_EARG;
   if (!bg_matrix_ok(*w)) return w->kind == RWKVB_KIND_SG8 ? RWKVB_EUNSUPPORTED : RWKVB_EARG;
   if (reinterpret_cast<uintptr_t>(x) % 16) return RWKVB_EARG;
   cudaStream_t s = (cudaStream_t)stream;
-  const int K = w->cols, N = w->rows, nb = batch;
-  const int bp = bg_padded_sessions(nb), nrows = bg_digit_rows(nb);
-  const size_t dig_bytes = (size_t)nrows * K;
-  const size_t cs_bytes = sizeof(float2) * (size_t)(K / w->group_size) * bp;
-  uint8_t* dig = nullptr;
-  const size_t cs_off = (dig_bytes + 255) & ~size_t(255);
-  const size_t err_off = (cs_off + cs_bytes + 255) & ~size_t(255);
-  if (cudaMallocAsync((void**)&dig, err_off + 256, s) != cudaSuccess) {
-    cudaGetLastError();
-    return RWKVB_EALLOC;
-  }
-  float2* cs = reinterpret_cast<float2*>(dig + cs_off);
-  if (!err_word) {  // no caller word: timeouts still stop the kernel, unreported
-    err_word = reinterpret_cast<int32_t*>(dig + err_off);
-    cudaMemsetAsync(err_word, 0, sizeof(int32_t), s);
-  }
-  BgDigits dg{dig, cs, K};
-  BgArgs a;
-  int grid = 0, pieces = 0;
-  size_t smem = 0;
-  BgJob job{w, 0, nullptr};
-  int st = bg_setup(&a, &job, 1, &dg, 1, nb, device_sms(), &grid, &pieces, &smem, err_word);
-  float* part = nullptr;
-  if (st == RWKVB_OK && cudaMallocAsync((void**)&part, sizeof(float) * (size_t)pieces * nb * N, s) != cudaSuccess) {
-    cudaGetLastError();
-    st = RWKVB_EALLOC;
-  }
+  BgOpEntry* e = nullptr;
+  int st = bgop_get(*w, batch, s, &e);
+  if (st != RWKVB_OK) return st;
+  const int K = w->cols, N = w->rows;
+  BgArgs a = e->a;
+  if (err_word) a.err = err_word;
+  st = bg_digits(e->dig, e->cs, x, K, K, batch, (int)w->group_size, s);
+  if (st == RWKVB_OK) st = bg_launch(a, e->grid, e->smem, s);
   if (st == RWKVB_OK) {
-    a.mat[0].out = part;
-    st = bg_digits_init(dig, K, nb, s);
-    if (st == RWKVB_OK) st = bg_digits(dig, cs, x, K, K, nb, (int)w->group_size, s);
-    if (st == RWKVB_OK) st = bg_launch(a, grid, smem, s);
-    if (st == RWKVB_OK) {
-      bg_reduce_kernel<<<(nb * N + 255) / 256, 256, 0, s>>>(y, part, nb, N, 0, K / 128, a.total, grid);
-      st = cuda_status(cudaGetLastError());
-    }
+    bg_reduce_kernel<<<(batch * N + 255) / 256, 256, 0, s>>>(y, e->part, batch, N, 0, K / 128, a.total, e->grid);
+    st = cuda_status(cudaGetLastError());
   }
-  if (part) cudaFreeAsync(part, s);
-  cudaFreeAsync(dig, s);
   return st;
 }
 
