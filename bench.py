@@ -20,6 +20,9 @@ ranges ``timed`` and ``e2e``.
 decoded together through ``B200BatchEngine`` (tcgen05 batched GEMMs), one
 step = one token for every session.
 
+``prefill`` is the sequence-prefill leg (``--prefill-sessions`` sessions x
+``--prefill-tokens`` tokens through ``B200BatchEngine.prefill``).
+
 ``--impl reference`` times the reference's own C kernels (built from its
 sources into ``oracle/_ref``) driving the packed RWKV-7 forward on the host
 cores, on the same workload and metric (rank 0 only).
@@ -265,6 +268,49 @@ def run_batched(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) 
                     "how": "B200BatchEngine.forward(host ids) + per-session argmax read back each step"}}
 
 
+def run_prefill(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) -> dict:
+    """Sequence prefill leg: ``args.prefill_sessions`` sessions consume
+    ``args.prefill_tokens`` seeded tokens each (``B200BatchEngine.prefill``:
+    chunks of 64 / sessions positions per GEMM), timed from the host call
+    (tokens copied to the device per chunk) to the last position's logits."""
+    nb, n = eng.batch, args.prefill_tokens
+    prompts = [synth_prompt(n, shape.vocab, replicas.session_seed(SEED + 1, g))
+               for g in replicas.session_range(nb, rank, world)]
+    warm = [p[:64] for p in prompts]
+    eng.prefill(warm)  # builds the chunk plan and graph
+    eng.reset()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    _nvtx_push("timed_prefill")
+    t0.record(stream)
+    eng.prefill(prompts)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    _nvtx_pop()
+    ms = replicas.max_over_ranks(t0.elapsed_time(t1))
+    chunk = max(1, 64 // nb)
+    chunks = n // chunk if chunk > 1 else 0
+    C, L, H = shape.n_embd, shape.n_layer, shape.n_head
+    state = L * (2 * C + H * 64 * 64) * 4
+    emb_row = C + (C // 128) * 8
+    head = shape.vocab * C + shape.vocab * (C // 128) * 8
+    weights = bpt - 2 * state - emb_row - head  # projections and adapters, once per chunk
+    alg = chunks * (weights + nb * 2 * state + nb * chunk * emb_row) + head
+    peak, peak_kind = _peaks()
+    achieved = alg / (ms * 1e-3) / 1e9
+    eng.close()
+    return {"metric": f"RWKV-7 {args.config} U8 prefill tok/s ({nb} sessions x {n} tokens)",
+            "value": nb * n * world / (ms * 1e-3), "unit": "tok/s", "ms": ms, "sessions_per_gpu": nb,
+            "tokens_per_session": n, "chunk_positions": chunk,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "algorithmic_bytes": alg,
+                         "what": f"weights once per chunk of {chunk} positions x {nb} sessions (tcgen05 GEMM rows), "
+                                 f"state read and written per chunk and session, head once; peak: {peak_kind}"},
+            "e2e": {"value": nb * n * world / (ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4 * nb * chunk,
+                    "d2h_bytes_per_step": 0, "how": "B200BatchEngine.prefill(host prompts): tokens copied per chunk"}}
+
+
 def synth_prompt(n: int, vocab: int, seed: int) -> list[int]:
     from rwkv_b200 import synth
 
@@ -312,6 +358,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sessions", type=int, default=64, help="batched-decode sessions (0: skip the batched leg)")
     ap.add_argument("--batch-steps", type=int, default=64)
+    ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill leg: tokens per session (0: skip)")
+    ap.add_argument("--prefill-sessions", type=int, default=8)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -348,11 +396,14 @@ def main() -> None:
     backend.prepare_provider(provider)
     eng = backend._engine
     cpu_pack = pack if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
-    batch_eng = None
-    if args.sessions > 0 and args.policy == "sg8":
+    batch_eng = prefill_eng = None
+    if args.policy == "sg8" and (args.sessions > 0 or args.prefill_tokens > 0):
         from rwkv_b200.engine import B200BatchEngine
 
-        batch_eng = B200BatchEngine(pack, args.sessions, device=local)
+        if args.sessions > 0:
+            batch_eng = B200BatchEngine(backend._model, args.sessions, device=local)
+        if args.prefill_tokens > 0:
+            prefill_eng = B200BatchEngine(backend._model, args.prefill_sessions, device=local)
     del pack
     provider.pack, provider._fused = {}, {}
     torch.cuda.empty_cache()
@@ -413,6 +464,7 @@ def main() -> None:
     e2e_val = e2e_steps * world / (e2e_ms / 1e3)
 
     batched = run_batched(batch_eng, args, shape, bpt, dev, stream, world, rank) if batch_eng is not None else None
+    prefill = run_prefill(prefill_eng, args, shape, bpt, dev, stream, world, rank) if prefill_eng is not None else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -453,6 +505,8 @@ def main() -> None:
         }
         if batched is not None:
             res["batched"] = batched
+        if prefill is not None:
+            res["prefill"] = prefill
         if cpu_pack is not None:
             backend.close()
             res["cpu_baseline"] = cpu_baseline(cpu_pack, shape, args)

@@ -282,6 +282,17 @@ int rwkvb_batch_reset(rwkvb_batch* e, void* stream);
 /* One step: session b consumes tokens[b] (HOST array of `batch` ids). */
 int rwkvb_batch_forward(rwkvb_batch* e, const int32_t* tokens, void* stream);
 
+/* Sequence prefill: session b consumes tokens[b*n .. b*n+n) (HOST, row-major
+ * [batch][n]) in order, with the result of n rwkvb_batch_forward steps.
+ * Positions run in chunks of P = 64 / batch: every projection of a chunk is ONE
+ * tcgen05 GEMM over batch * P rows (session, position); the token shift and
+ * WKV7 follow positions in order inside the chunk (state in registers); the
+ * head runs once, for the last position.  Positions past the last full chunk
+ * (and every position when P < 2) run as single steps.  Replaces the prompt
+ * loop of the reference's sequence prefill (rwkv7_forward.py:1046-1175,
+ * rwkv7_batch.py:94-220) for packed models. */
+int rwkvb_batch_prefill(rwkvb_batch* e, const int32_t* tokens, int32_t n, void* stream);
+
 /* n greedy steps; step 0 consumes the argmax of the current logits of every
  * session, step i > 0 the argmax of step i-1.  ids [n][batch] to HOST memory
  * (synchronises) or device memory (_async, does not synchronise). */

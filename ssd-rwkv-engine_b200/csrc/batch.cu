@@ -783,6 +783,237 @@ __global__ void __launch_bounds__(kBtThreads) bt_hdig_kernel(uint8_t* dig, float
 }
 
 // ------------------------------------------------------------- argmax
+// ============================================================ prefill rows
+// Sequence prefill runs the same layer with rows = (session s, position j) of a
+// chunk of P positions: row = s * P + j.  Rows are independent everywhere
+// except the token shift (prev of (s, j) is the LayerNorm output of (s, j-1), or
+// the state for j = 0) and WKV7 (positions in order), handled below.
+
+// LayerNorm of every row: x[row] (+ folded pieces of the previous layer's
+// value projection onto xm) -> x[row] and xln[row].
+struct BtLnRowsArgs {
+  float* x;           // [rows][C]
+  const float* xm;    // fold source, or null (x complete)
+  const float* part;
+  BtPieces pp;
+  const float *ln_w, *ln_b;
+  float* xln;         // [rows][C]
+  int C, rows;
+};
+
+__global__ void __launch_bounds__(kBtRowThreads) bt_lnrows_kernel(BtLnRowsArgs a) {
+  __shared__ float red[32];
+  extern __shared__ __align__(16) float bt_sm[];
+  const int row = blockIdx.x, C = a.C;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    float v;
+    if (a.part) {
+      v = a.xm[(size_t)row * C + i] + bt_fold(a.part, a.pp, a.rows, C, row, i);
+      a.x[(size_t)row * C + i] = v;
+    } else {
+      v = a.x[(size_t)row * C + i];
+    }
+    bt_sm[i] = v;
+  }
+  __syncthreads();
+  bt_layer_norm(bt_sm, a.ln_w, a.ln_b, C, red);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) a.xln[(size_t)row * C + i] = bt_sm[i];
+}
+
+// Token-shift mixes of every row.  mode 0 (time mix): six mixes; digit rows of
+// r, k, v and fp32 w/a/g/v adapter inputs.  mode 1 (channel mix): the key mix's
+// digit rows.  The CTA of row (s, 0) reads the state of session s and then
+// stores the LayerNorm output of (s, P-1) as the new state.
+struct BtMixRowsArgs {
+  const float* xln;    // [rows][C]
+  float* state;        // [nb][C]
+  const float* mix[6]; // mode 0: x_r, x_w, x_k, x_v, x_a, x_g; mode 1: mix[0] = x_k
+  uint8_t* dig[3];
+  float2* cs[3];
+  float* xa4;          // [4][rows][C] (mode 0)
+  int C, rows, P, bp, lfk, mode;
+};
+
+__global__ void __launch_bounds__(kBtRowThreads) bt_mixrows_kernel(BtMixRowsArgs a) {
+  extern __shared__ __align__(16) float bt_sm[];
+  const int row = blockIdx.x, C = a.C, s = row / a.P, j = row - s * a.P;
+  float* xl = bt_sm;
+  float* prev = xl + C;
+  float* mixed = prev + C;  // [3][C]
+  const float* own = a.xln + (size_t)row * C;
+  const float* pv = j > 0 ? a.xln + (size_t)(row - 1) * C : a.state + (size_t)s * C;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    xl[i] = own[i];
+    prev[i] = pv[i];
+  }
+  __syncthreads();
+  if (j == 0) {
+    const float* last = a.xln + (size_t)(row + a.P - 1) * C;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) a.state[(size_t)s * C + i] = last[i];
+  }
+  const int nd = a.mode == 0 ? 3 : 1;
+  if (a.mode == 0) {
+    const float *mr = a.mix[0], *mw = a.mix[1], *mk = a.mix[2], *mv = a.mix[3], *ma = a.mix[4], *mg = a.mix[5];
+    float* xw = a.xa4 + (size_t)row * C;
+    float* xa = xw + (size_t)a.rows * C;
+    float* xg = xa + (size_t)a.rows * C;
+    float* xv = xg + (size_t)a.rows * C;
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+      const float z = xl[i], d = prev[i] - z;
+      mixed[i] = z + d * mr[i];
+      mixed[C + i] = z + d * mk[i];
+      const float vv = z + d * mv[i];
+      mixed[2 * C + i] = vv;
+      xw[i] = z + d * mw[i];
+      xa[i] = z + d * ma[i];
+      xg[i] = z + d * mg[i];
+      xv[i] = vv;
+    }
+  } else {
+    for (int i = threadIdx.x; i < C; i += blockDim.x) mixed[i] = xl[i] + (prev[i] - xl[i]) * a.mix[0][i];
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int G = C >> a.lfk, per = 1 << (a.lfk - 5);
+  for (int w = warp; w < nd * G; w += nw) {
+    const int m = w / G, g = w - m * G;
+    const float* src = mixed + (size_t)m * C + ((size_t)g << a.lfk) + lane * per;
+    float v[4] = {src[0], src[1], per == 4 ? src[2] : 0.f, per == 4 ? src[3] : 0.f};
+    bg_emit_group(v, per, a.dig[m], a.cs[m], (size_t)C, ((size_t)g << a.lfk) + lane * per, row, a.bp, g);
+  }
+}
+
+// x + attention output for every row, then LayerNorm 2 -> xln2.
+struct BtFfnLnArgs {
+  const float* x;
+  float* xm;
+  const float* part;
+  BtPieces pp;
+  const float *ln_w, *ln_b;
+  float* xln;
+  int C, rows;
+};
+
+__global__ void __launch_bounds__(kBtRowThreads) bt_ffnln_kernel(BtFfnLnArgs a) {
+  __shared__ float red[32];
+  extern __shared__ __align__(16) float bt_sm[];
+  const int row = blockIdx.x, C = a.C;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float v = a.x[(size_t)row * C + i] + bt_fold(a.part, a.pp, a.rows, C, row, i);
+    a.xm[(size_t)row * C + i] = v;
+    bt_sm[i] = v;
+  }
+  __syncthreads();
+  bt_layer_norm(bt_sm, a.ln_w, a.ln_b, C, red);
+  for (int i = threadIdx.x; i < C; i += blockDim.x) a.xln[(size_t)row * C + i] = bt_sm[i];
+}
+
+// WKV7 over the P positions of a chunk, in order, state rows in registers:
+// CTA = (head, 4 sessions), 64 threads per session (thread = state row = channel).
+struct BtWkvRowsArgs {
+  const float* part[3];
+  BtPieces pp[3];
+  const float* adp2;   // [4][rows][C]
+  float* wkv;          // this layer's state [nb][H][64][64]
+  float* vfirst;       // [rows][C]
+  float* att_y;        // [rows][C]
+  const float *w0, *a0, *v0, *k_k, *k_a, *r_k, *lnx_w, *lnx_b;
+  int C, H, nb, rows, P, layer0;
+};
+
+__global__ void __launch_bounds__(kBtThreads, 2) bt_wkvrows_kernel(BtWkvRowsArgs a) {
+  __shared__ float red[2 * kBtWkvSess];
+  __shared__ __align__(16) float vecs[kBtWkvSess][5][64];
+  const int h = blockIdx.x, t = threadIdx.x, js = t >> 6, i = t & 63;
+  const int s = blockIdx.y * kBtWkvSess + js;
+  if (s >= a.nb) return;  // whole 64-thread group: it owns its named barrier
+  const int C = a.C, ch = h * 64 + i;
+  float4* Srow = reinterpret_cast<float4*>(a.wkv + ((size_t)s * a.H + h) * 4096 + (size_t)i * 64);
+  float4 s4[16];
+#pragma unroll
+  for (int u = 0; u < 16; ++u) s4[u] = Srow[u];
+  const float kkw = a.k_k[ch], a0 = a.a0[ch], ka = a.k_a[ch], w0 = a.w0[ch], rk = a.r_k[ch], lw = a.lnx_w[ch],
+              lb = a.lnx_b[ch], v0 = a.layer0 ? 0.f : a.v0[ch];
+  float* vd = vecs[js][0];
+  float* vkk = vecs[js][1];
+  float* vka = vecs[js][2];
+  float* vk = vecs[js][3];
+  float* vr = vecs[js][4];
+  for (int j = 0; j < a.P; ++j) {
+    const int row = s * a.P + j;
+    const float wv = a.adp2[((size_t)0 * a.rows + row) * C + ch];
+    const float av = a.adp2[((size_t)1 * a.rows + row) * C + ch];
+    const float gv = a.adp2[((size_t)2 * a.rows + row) * C + ch];
+    float vv = 0.f, vf = 0.f;
+    if (!a.layer0) {
+      vv = a.adp2[((size_t)3 * a.rows + row) * C + ch];
+      vf = a.vfirst[(size_t)row * C + ch];
+    }
+    const float r = bt_fold(a.part[0], a.pp[0], a.rows, C, row, ch);
+    const float k = bt_fold(a.part[1], a.pp[1], a.rows, C, row, ch);
+    float v = bt_fold(a.part[2], a.pp[2], a.rows, C, row, ch);
+    const float kkv = k * kkw;
+    const float nrm = sqrtf(bt_sum64(kkv * kkv, red, js));
+    const float aa = sigmoidf_(a0 + av);
+    const float kk = kkv / fmaxf(nrm, 1e-12f);
+    const float kn = k * (1.0f + (aa - 1.0f) * ka);
+    if (a.layer0) a.vfirst[(size_t)row * C + ch] = v;
+    else v = v + (vf - v) * sigmoidf_(v0 + vv);
+    vd[i] = expf(-0.606531f * sigmoidf_(w0 + wv));
+    vkk[i] = -kk;
+    vka[i] = kk * aa;
+    vk[i] = kn;
+    vr[i] = r;
+    bt_bar64(js);
+    float sa = 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const float4 n4 = reinterpret_cast<const float4*>(vkk)[u];
+      sa = fmaf(s4[u].x, n4.x, sa);
+      sa = fmaf(s4[u].y, n4.y, sa);
+      sa = fmaf(s4[u].z, n4.z, sa);
+      sa = fmaf(s4[u].w, n4.w, sa);
+    }
+    float y = 0.f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const float4 d4 = reinterpret_cast<const float4*>(vd)[u];
+      const float4 a4 = reinterpret_cast<const float4*>(vka)[u];
+      const float4 k4 = reinterpret_cast<const float4*>(vk)[u];
+      const float4 r4 = reinterpret_cast<const float4*>(vr)[u];
+      float4 n;
+      n.x = s4[u].x * d4.x + sa * a4.x + v * k4.x;
+      n.y = s4[u].y * d4.y + sa * a4.y + v * k4.y;
+      n.z = s4[u].z * d4.z + sa * a4.z + v * k4.z;
+      n.w = s4[u].w * d4.w + sa * a4.w + v * k4.w;
+      y = fmaf(n.x, r4.x, y);
+      y = fmaf(n.y, r4.y, y);
+      y = fmaf(n.z, r4.z, y);
+      y = fmaf(n.w, r4.w, y);
+      s4[u] = n;
+    }
+    const float mean = bt_sum64(y, red, js) / 64.f;
+    const float dv = y - mean;
+    const float var = bt_sum64(dv * dv, red, js) / 64.f;
+    const float bonus = bt_sum64(r * kn * rk, red, js);  // also orders this position's reads of vecs
+    float o = dv * rsqrtf(var + 64e-5f) * lw + lb;
+    o = o + bonus * v;
+    a.att_y[(size_t)row * C + ch] = o * gv;
+  }
+#pragma unroll
+  for (int u = 0; u < 16; ++u) Srow[u] = s4[u];
+}
+
+// Head input of each session after a prefill chunk: the last position's
+// residual stream (with the last value projection folded in), in decode rows.
+__global__ void bt_pick_last_kernel(float* xs, const float* xm, const float* part, BtPieces pp, int C, int rows,
+                                    int P, int nb) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nb * C) return;
+  const int s = i / C, c = i - s * C, row = s * P + P - 1;
+  xs[(size_t)s * C + c] = xm[(size_t)row * C + c] + bt_fold(part, pp, rows, C, row, c);
+}
+
 __global__ void __launch_bounds__(1024) bt_argmax_kernel(float* logits, const float* part, BtPieces pp, int nb,
                                                          int V, int* tok, int* hist, const int* step, int hist_cap) {
   __shared__ float bv[32];
@@ -840,6 +1071,26 @@ struct BtLayer {
   const float* mix[6];
   const float *w0, *a0, *v0, *k_k, *k_a, *r_k, *lnx_w, *lnx_b, *ffn_x_k;
   BgArgs rkv, o, key, value;
+  rwkvb_packed big[6];  // att r, k, v, o, ffn key, ffn value (for further launch plans)
+};
+
+// Sequence prefill: rows = (session, position) of a chunk of P positions, with
+// its own activation buffers, digit rows and GEMM launch plans.
+struct BtPrefill {
+  int P = 0, rows = 0, bp = 0, nrows = 0;
+  void* arena = nullptr;
+  float *x = nullptr, *xm = nullptr, *xln = nullptr, *xln2 = nullptr, *xa4 = nullptr, *adp1 = nullptr;
+  float *mid = nullptr, *adp2 = nullptr, *vfirst = nullptr, *att_y = nullptr, *xhead = nullptr;
+  float *part_r = nullptr, *part_k = nullptr, *part_v = nullptr, *part_o = nullptr, *part_key = nullptr;
+  float* part_val = nullptr;
+  uint8_t *dig_r = nullptr, *dig_k = nullptr, *dig_v = nullptr, *dig_y = nullptr, *dig_f = nullptr, *dig_h = nullptr;
+  float2 *cs_r = nullptr, *cs_k = nullptr, *cs_v = nullptr, *cs_y = nullptr, *cs_f = nullptr, *cs_h = nullptr;
+  int *tok = nullptr, *step = nullptr;
+  std::vector<BgArgs> rkv, o, key, value;
+  int g_rkv = 0, g_o = 0, g_key = 0, g_value = 0;
+  size_t smem_bg = 0;
+  BtPieces pp_rkv[3], pp_o, pp_key, pp_value;
+  cudaGraphExec_t exec = nullptr;
 };
 
 constexpr size_t kBtAdp1Smem = sizeof(float) * (kBtAdpKc * kBtXsStride + kBtAdpKc * kBtAdpCols);
@@ -887,6 +1138,7 @@ struct rwkvb_batch {
   cudaGraphExec_t exec = nullptr;
   bool use_graph = true;
   int launches = 0;
+  rwkvb::BtPrefill* pf = nullptr;
 };
 
 namespace rwkvb {
@@ -899,6 +1151,31 @@ BtPieces bt_pieces(const BgArgs& a, int job, int grid) {
   p.total = a.total;
   p.ncta = grid;
   return p;
+}
+
+// ln_out of x (+ folded value pieces onto xm when `part` is set), the head
+// GEMM and the per-session first-maximum argmax (-> e->tok, e->logits).
+int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part, const BtPieces& pp, cudaStream_t s) {
+  const int C = e->C, nb = e->nb;
+  BtInArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.x = x;
+  a.xm = xm;
+  a.part = part;
+  a.pp = pp;
+  a.ln_w = e->lnout_w;
+  a.ln_b = e->lnout_b;
+  a.state = nullptr;
+  a.dig[0] = e->dig_o;
+  a.cs[0] = e->cs_o;
+  a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
+  bt_in_kernel<<<nb, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
+  int st = cuda_status(cudaGetLastError());
+  if (st == RWKVB_OK) st = bg_launch(e->head, e->g_head, e->smem_bg, s);
+  if (st != RWKVB_OK) return st;
+  bt_argmax_kernel<<<nb, 1024, 0, s>>>(e->logits, e->part_head, e->pp_head, nb, e->V, e->tok, e->hist, e->step,
+                                       e->hist_cap);
+  return cuda_status(cudaGetLastError());
 }
 
 // Launch one token step of every session (tokens already in e->tok).
@@ -1024,26 +1301,10 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     ++n;
   }
   {
-    BtInArgs a;
-    std::memset(&a, 0, sizeof(a));
-    a.x = e->x;
-    a.xm = e->xm;
-    a.part = e->part_val;
-    a.pp = e->pp_value;
-    a.ln_w = e->lnout_w;
-    a.ln_b = e->lnout_b;
-    a.state = nullptr;
-    a.dig[0] = e->dig_o;
-    a.cs[0] = e->cs_o;
-    a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
-    bt_in_kernel<<<nb, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
-    BT_CHECK();
+    const int st = bt_record_head(e, e->x, e->xm, e->part_val, e->pp_value, s);
+    if (st != RWKVB_OK) return st;
+    n += 3;
   }
-  if (bg_launch(e->head, e->g_head, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
-  ++n;
-  bt_argmax_kernel<<<nb, 1024, 0, s>>>(e->logits, e->part_head, e->pp_head, nb, e->V, e->tok, e->hist, e->step,
-                                       e->hist_cap);
-  BT_CHECK();
 #undef BT_CHECK
   e->launches = n;
   return RWKVB_OK;
@@ -1085,8 +1346,293 @@ int bt_check_err(rwkvb_batch* e, cudaStream_t s) {
   return RWKVB_OK;
 }
 
+// Build the prefill plan: chunk P = 64 / nb positions (at least 2).
+int bt_prefill_setup(rwkvb_batch* e) {
+  if (e->pf) return RWKVB_OK;
+  const int P = kBgMaxSessions / e->nb;
+  if (P < 2) return RWKVB_EUNSUPPORTED;
+  BtPrefill* f = new (std::nothrow) BtPrefill();
+  if (!f) return RWKVB_EALLOC;
+  const int rows = e->nb * P, C = e->C, F = e->F, V = e->V;
+  f->P = P, f->rows = rows, f->bp = bg_padded_sessions(rows), f->nrows = bg_digit_rows(rows);
+  const size_t rC = (size_t)rows * C;
+  const int Pk = C / 128, Pf = F / 128;
+  struct Item {
+    void** p;
+    size_t bytes;
+  };
+  const size_t csC = 8 * (size_t)(C / e->group) * f->bp, csF = 8 * (size_t)(F / e->group) * f->bp;
+  std::vector<Item> items = {
+      {(void**)&f->x, 4 * rC},          {(void**)&f->xm, 4 * rC},
+      {(void**)&f->xln, 4 * rC},        {(void**)&f->xln2, 4 * rC},
+      {(void**)&f->xa4, 4 * 4 * rC},    {(void**)&f->adp1, 4 * (size_t)e->adp_splits * rows * e->rtot},
+      {(void**)&f->mid, 4 * (size_t)64 * e->rtot}, {(void**)&f->adp2, 4 * 4 * rC},
+      {(void**)&f->vfirst, 4 * rC},     {(void**)&f->att_y, 4 * rC},
+      {(void**)&f->xhead, 4 * (size_t)e->nb * C},
+      {(void**)&f->part_r, 4 * (size_t)Pk * rC}, {(void**)&f->part_k, 4 * (size_t)Pk * rC},
+      {(void**)&f->part_v, 4 * (size_t)Pk * rC}, {(void**)&f->part_o, 4 * (size_t)Pk * rC},
+      {(void**)&f->part_key, 4 * (size_t)Pk * rows * F}, {(void**)&f->part_val, 4 * (size_t)Pf * rC},
+      {(void**)&f->dig_r, (size_t)f->nrows * C}, {(void**)&f->dig_k, (size_t)f->nrows * C},
+      {(void**)&f->dig_v, (size_t)f->nrows * C}, {(void**)&f->dig_y, (size_t)f->nrows * C},
+      {(void**)&f->dig_f, (size_t)f->nrows * C}, {(void**)&f->dig_h, (size_t)f->nrows * F},
+      {(void**)&f->cs_r, csC}, {(void**)&f->cs_k, csC}, {(void**)&f->cs_v, csC}, {(void**)&f->cs_y, csC},
+      {(void**)&f->cs_f, csC}, {(void**)&f->cs_h, csF},
+      {(void**)&f->tok, 4 * (size_t)rows}, {(void**)&f->step, 16},
+  };
+  (void)V;
+  size_t total = 0;
+  std::vector<size_t> offs;
+  for (const Item& it : items) {
+    offs.push_back(total);
+    total += (it.bytes + 1023) & ~size_t(1023);
+  }
+  if (cudaMalloc(&f->arena, total) != cudaSuccess) {
+    cudaGetLastError();
+    delete f;
+    return RWKVB_EALLOC;
+  }
+  cudaMemset(f->arena, 0, total);
+  for (size_t i = 0; i < items.size(); ++i) *items[i].p = (char*)f->arena + offs[i];
+  int st = RWKVB_OK;
+  uint8_t* digs[] = {f->dig_r, f->dig_k, f->dig_v, f->dig_y, f->dig_f};
+  for (uint8_t* d : digs)
+    if (st == RWKVB_OK) st = bg_digits_init(d, C, rows, nullptr);
+  if (st == RWKVB_OK) st = bg_digits_init(f->dig_h, F, rows, nullptr);
+  if (st == RWKVB_OK) st = cuda_status(cudaDeviceSynchronize());
+  const BgDigits d_rkv[3] = {{f->dig_r, f->cs_r, C}, {f->dig_k, f->cs_k, C}, {f->dig_v, f->cs_v, C}};
+  const BgDigits d_y{f->dig_y, f->cs_y, C}, d_f{f->dig_f, f->cs_f, C}, d_h{f->dig_h, f->cs_h, F};
+  int pieces = 0;
+  size_t smem = 0;
+  for (int l = 0; l < e->L && st == RWKVB_OK; ++l) {
+    const BtLayer& ly = e->layers[l];
+    BgArgs rkv, o, key, value;
+    const BgJob jr[3] = {{&ly.big[0], 0, f->part_r}, {&ly.big[1], 1, f->part_k}, {&ly.big[2], 2, f->part_v}};
+    st = bg_setup(&rkv, jr, 3, d_rkv, 3, rows, e->sms, &f->g_rkv, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
+    f->smem_bg = std::max(f->smem_bg, smem);
+    const BgJob jo{&ly.big[3], 0, f->part_o};
+    if (st == RWKVB_OK) st = bg_setup(&o, &jo, 1, &d_y, 1, rows, e->sms, &f->g_o, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
+    const BgJob jk{&ly.big[4], 0, f->part_key};
+    if (st == RWKVB_OK) st = bg_setup(&key, &jk, 1, &d_f, 1, rows, e->sms, &f->g_key, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
+    const BgJob jv{&ly.big[5], 0, f->part_val};
+    if (st == RWKVB_OK) st = bg_setup(&value, &jv, 1, &d_h, 1, rows, e->sms, &f->g_value, &pieces, &smem, e->err);
+    if (st == RWKVB_OK && pieces > Pf) st = RWKVB_EUNSUPPORTED;
+    if (st == RWKVB_OK && l == 0) {
+      for (int j = 0; j < 3; ++j) f->pp_rkv[j] = bt_pieces(rkv, j, f->g_rkv);
+      f->pp_o = bt_pieces(o, 0, f->g_o);
+      f->pp_key = bt_pieces(key, 0, f->g_key);
+      f->pp_value = bt_pieces(value, 0, f->g_value);
+    }
+    f->rkv.push_back(rkv), f->o.push_back(o), f->key.push_back(key), f->value.push_back(value);
+  }
+  if (st == RWKVB_OK) st = bg_allow_smem(f->smem_bg);
+  if (st == RWKVB_OK) {
+    const void* fns[] = {(const void*)bt_mixrows_kernel, (const void*)bt_lnrows_kernel, (const void*)bt_ffnln_kernel};
+    const int sm[] = {(int)(sizeof(float) * 5 * C), (int)(sizeof(float) * C), (int)(sizeof(float) * C)};
+    for (int i = 0; i < 3 && st == RWKVB_OK; ++i)
+      st = cuda_status(cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, sm[i]));
+  }
+  if (st != RWKVB_OK) {
+    cudaFree(f->arena);
+    delete f;
+    return st;
+  }
+  e->pf = f;
+  return RWKVB_OK;
+}
+
+// One prefill chunk of every session (tokens in pf->tok, row order s * P + j).
+int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
+  BtPrefill& f = *e->pf;
+  const int C = e->C, rows = f.rows, nb = e->nb;
+#define PF_CHECK()                                  \
+  do {                                              \
+    const int st_ = cuda_status(cudaGetLastError()); \
+    if (st_ != RWKVB_OK) return st_;                \
+  } while (0)
+  {
+    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, f.tok, f.x, f.step, e->err, C, e->V};
+    bt_embed_kernel<<<rows, kBtThreads, sizeof(float) * C, s>>>(a);
+    PF_CHECK();
+  }
+  for (int l = 0; l < e->L; ++l) {
+    const BtLayer& ly = e->layers[l];
+    const bool l0 = l == 0;
+    {
+      BtLnRowsArgs a{f.x, l0 ? nullptr : f.xm, l0 ? nullptr : f.part_val, f.pp_value, ly.ln1_w, ly.ln1_b, f.xln,
+                     C, rows};
+      bt_lnrows_kernel<<<rows, kBtRowThreads, sizeof(float) * C, s>>>(a);
+      PF_CHECK();
+    }
+    {
+      BtMixRowsArgs a;
+      std::memset(&a, 0, sizeof(a));
+      a.xln = f.xln;
+      a.state = e->att_x + (size_t)l * nb * C;
+      for (int j = 0; j < 6; ++j) a.mix[j] = ly.mix[j];
+      a.dig[0] = f.dig_r, a.dig[1] = f.dig_k, a.dig[2] = f.dig_v;
+      a.cs[0] = f.cs_r, a.cs[1] = f.cs_k, a.cs[2] = f.cs_v;
+      a.xa4 = f.xa4;
+      a.C = C, a.rows = rows, a.P = f.P, a.bp = f.bp, a.lfk = e->lfk, a.mode = 0;
+      bt_mixrows_kernel<<<rows, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
+      PF_CHECK();
+    }
+    if (bg_launch(f.rkv[l], f.g_rkv, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    const int nm = l0 ? 3 : 4;
+    {
+      BtAdp1Args a;
+      std::memset(&a, 0, sizeof(a));
+      const int Rm[4] = {e->rw, e->ra, e->rg, e->rv};
+      int off = 0, blk = 0;
+      for (int m = 0; m < 4; ++m) {
+        a.w[m] = ly.ad1[m];
+        a.R[m] = Rm[m];
+        a.off[m] = off;
+        a.blk0[m] = blk;
+        off += Rm[m];
+        if (m < nm) blk += (Rm[m] + kBtAdpCols - 1) / kBtAdpCols;
+      }
+      a.blk0[nm] = blk;
+      a.nm = nm;
+      for (int m = 0; m < nm; ++m) a.fast[m] = bt_fast_adp1(a.w[m], a.R[m]);
+      a.xa4 = f.xa4;
+      a.out = f.adp1;
+      a.C = C, a.nb = rows, a.rtot = e->rtot;
+      bt_adp1_kernel<<<dim3(blk, e->adp_splits), kBtThreads, kBtAdp1Smem, s>>>(a);
+      PF_CHECK();
+      const int used = l0 ? e->rw + e->ra + e->rg : e->rtot;
+      bt_adpr_kernel<<<(rows * used + 255) / 256, 256, 0, s>>>(f.mid, f.adp1, e->adp_splits, rows, e->rtot, used,
+                                                                e->rw, e->ra, e->rg);
+      PF_CHECK();
+    }
+    {
+      BtAdp2Args a;
+      std::memset(&a, 0, sizeof(a));
+      const int Rm[4] = {e->rw, e->ra, e->rg, e->rv};
+      int off = 0;
+      for (int m = 0; m < 4; ++m) {
+        a.w[m] = ly.ad2[m];
+        a.R[m] = Rm[m];
+        a.off[m] = off;
+        off += Rm[m];
+      }
+      for (int m = 0; m < nm; ++m) a.fast[m] = bt_fast_adp2(a.w[m], C);
+      a.midT = f.mid;
+      a.out = f.adp2;
+      a.C = C, a.nb = rows, a.rtot = e->rtot;
+      bt_adp2_kernel<<<dim3(C / 64, nm), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
+      PF_CHECK();
+    }
+    {
+      BtWkvRowsArgs a;
+      std::memset(&a, 0, sizeof(a));
+      a.part[0] = f.part_r, a.part[1] = f.part_k, a.part[2] = f.part_v;
+      for (int j = 0; j < 3; ++j) a.pp[j] = f.pp_rkv[j];
+      a.adp2 = f.adp2;
+      a.wkv = e->wkv + (size_t)l * nb * e->H * 4096;
+      a.vfirst = f.vfirst;
+      a.att_y = f.att_y;
+      a.w0 = ly.w0, a.a0 = ly.a0, a.v0 = ly.v0, a.k_k = ly.k_k, a.k_a = ly.k_a, a.r_k = ly.r_k;
+      a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
+      a.C = C, a.H = e->H, a.nb = nb, a.rows = rows, a.P = f.P, a.layer0 = l0 ? 1 : 0;
+      bt_wkvrows_kernel<<<dim3(e->H, (nb + kBtWkvSess - 1) / kBtWkvSess), kBtThreads, 0, s>>>(a);
+      PF_CHECK();
+    }
+    if (bg_digits(f.dig_y, f.cs_y, f.att_y, C, C, rows, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(f.o[l], f.g_o, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    {
+      BtFfnLnArgs a{f.x, f.xm, f.part_o, f.pp_o, ly.ln2_w, ly.ln2_b, f.xln2, C, rows};
+      bt_ffnln_kernel<<<rows, kBtRowThreads, sizeof(float) * C, s>>>(a);
+      PF_CHECK();
+    }
+    {
+      BtMixRowsArgs a;
+      std::memset(&a, 0, sizeof(a));
+      a.xln = f.xln2;
+      a.state = e->ffn_x + (size_t)l * nb * C;
+      a.mix[0] = ly.ffn_x_k;
+      a.dig[0] = f.dig_f;
+      a.cs[0] = f.cs_f;
+      a.C = C, a.rows = rows, a.P = f.P, a.bp = f.bp, a.lfk = e->lfk, a.mode = 1;
+      bt_mixrows_kernel<<<rows, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
+      PF_CHECK();
+    }
+    if (bg_launch(f.key[l], f.g_key, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    {
+      const int warps = rows * (e->F >> e->lfk);
+      bt_hdig_kernel<<<(warps + 7) / 8, kBtThreads, 0, s>>>(f.dig_h, f.cs_h, f.part_key, f.pp_key, rows, e->F, f.bp,
+                                                           e->lfk);
+      PF_CHECK();
+    }
+    if (bg_launch(f.value[l], f.g_value, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+  }
+  bt_pick_last_kernel<<<(nb * C + 255) / 256, 256, 0, s>>>(f.xhead, f.xm, f.part_val, f.pp_value, C, rows, f.P, nb);
+  PF_CHECK();
+#undef PF_CHECK
+  return RWKVB_OK;
+}
+
+int bt_run_prefill_chunk(rwkvb_batch* e, cudaStream_t s) {
+  BtPrefill& f = *e->pf;
+  if (e->use_graph && !f.exec) {
+    cudaStream_t cs = nullptr;
+    if (cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking) != cudaSuccess) return RWKVB_ECUDA;
+    cudaGraph_t g = nullptr;
+    int st = cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+    if (st == RWKVB_OK) {
+      st = bt_record_prefill(e, cs);
+      const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+      if (st == RWKVB_OK) st = cuda_status(ce);
+    }
+    if (st == RWKVB_OK) st = cuda_status(cudaGraphInstantiate(&f.exec, g, 0));
+    if (g) cudaGraphDestroy(g);
+    cudaStreamDestroy(cs);
+    if (st != RWKVB_OK) {
+      f.exec = nullptr;
+      return st;
+    }
+  }
+  if (e->use_graph) return cuda_status(cudaGraphLaunch(f.exec, s));
+  return bt_record_prefill(e, s);
+}
+
 }  // namespace
 }  // namespace rwkvb
+
+extern "C" int rwkvb_batch_prefill(rwkvb_batch* e, const int32_t* tokens, int32_t n, void* stream) {
+  if (!e || (!tokens && n > 0) || n < 0) return RWKVB_EARG;
+  for (size_t i = 0; i < (size_t)n * e->nb; ++i)
+    if (tokens[i] < 0 || tokens[i] >= e->V) return RWKVB_EARG;
+  if (n == 0) return RWKVB_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  int st = bt_prefill_setup(e);
+  const int P = st == RWKVB_OK ? e->pf->P : 1;
+  if (st == RWKVB_EUNSUPPORTED) st = RWKVB_OK;  // chunk of one: every position is a decode step
+  if (st != RWKVB_OK) return st;
+  const int nb = e->nb, full = P > 1 ? n / P : 0;
+  std::vector<int32_t> chunk((size_t)nb * (P > 1 ? P : 1));
+  for (int c = 0; c < full && st == RWKVB_OK; ++c) {
+    for (int b = 0; b < nb; ++b)
+      for (int j = 0; j < P; ++j) chunk[(size_t)b * P + j] = tokens[(size_t)b * n + (size_t)c * P + j];
+    st = cuda_status(cudaMemcpyAsync(e->pf->tok, chunk.data(), sizeof(int32_t) * nb * P, cudaMemcpyHostToDevice, s));
+    if (st == RWKVB_OK) st = bt_run_prefill_chunk(e, s);
+    if (st == RWKVB_OK) st = cuda_status(cudaStreamSynchronize(s));  // the host chunk buffer is reused
+  }
+  const int done = full * P;
+  if (st == RWKVB_OK && done == n) {
+    BtPrefill& f = *e->pf;
+    st = bt_record_head(e, f.xhead, nullptr, nullptr, f.pp_value, s);
+  }
+  std::vector<int32_t> step(nb);
+  for (int pos = done; pos < n && st == RWKVB_OK; ++pos) {
+    for (int b = 0; b < nb; ++b) step[b] = tokens[(size_t)b * n + pos];
+    st = rwkvb_batch_forward(e, step.data(), s);
+    if (st == RWKVB_OK) st = cuda_status(cudaStreamSynchronize(s));
+  }
+  return st;
+}
 
 extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, rwkvb_batch** out) {
   if (!m || !out || !m->layers || batch <= 0 || batch > kBgMaxSessions) return RWKVB_EARG;
@@ -1234,6 +1780,8 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
     ly.mix[0] = s.x_r, ly.mix[1] = s.x_w, ly.mix[2] = s.x_k, ly.mix[3] = s.x_v, ly.mix[4] = s.x_a, ly.mix[5] = s.x_g;
     ly.w0 = s.w0, ly.a0 = s.a0, ly.v0 = s.v0, ly.k_k = s.k_k, ly.k_a = s.k_a, ly.r_k = s.r_k;
     ly.lnx_w = s.lnx_w, ly.lnx_b = s.lnx_b, ly.ffn_x_k = s.ffn_x_k;
+    ly.big[0] = s.att_r, ly.big[1] = s.att_k, ly.big[2] = s.att_v, ly.big[3] = s.att_o;
+    ly.big[4] = s.ffn_key, ly.big[5] = s.ffn_value;
     const BgJob jr[3] = {{&s.att_r, 0, e->part_r}, {&s.att_k, 1, e->part_k}, {&s.att_v, 2, e->part_v}};
     st = bg_setup(&ly.rkv, jr, 3, d_rkv, 3, batch, e->sms, &e->g_rkv, &pieces, &smem, e->err);
     if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
@@ -1314,6 +1862,11 @@ extern "C" int rwkvb_batch_destroy(rwkvb_batch* e) {
   if (!e) return RWKVB_EARG;
   cudaDeviceSynchronize();
   if (e->exec) cudaGraphExecDestroy(e->exec);
+  if (e->pf) {
+    if (e->pf->exec) cudaGraphExecDestroy(e->pf->exec);
+    if (e->pf->arena) cudaFree(e->pf->arena);
+    delete e->pf;
+  }
   if (e->arena) cudaFree(e->arena);
   delete e;
   return RWKVB_OK;

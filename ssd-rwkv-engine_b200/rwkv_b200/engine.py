@@ -312,6 +312,18 @@ class B200BatchEngine:
         native.check(self.lib.rwkvb_batch_forward(self._h, toks, self._stream(stream)), "rwkvb_batch_forward")
         return self.logits
 
+    def prefill(self, prompts, stream=None) -> torch.Tensor:
+        """Consume equal-length prompts (one per session) in order; returns the
+        device logits ``[batch, vocab]`` of the last position.  Chunks of
+        positions go through the tcgen05 GEMMs together (``rwkvb_batch_prefill``)."""
+        if len(prompts) != self.batch or len({len(p) for p in prompts}) != 1:
+            raise ValueError(f"expected {self.batch} prompts of equal length")
+        n = len(prompts[0])
+        toks = np.asarray(prompts, dtype=np.int32).reshape(-1)
+        native.check(self.lib.rwkvb_batch_prefill(self._h, toks.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), n,
+                                                  self._stream(stream)), "rwkvb_batch_prefill")
+        return self.logits
+
     def decode_greedy(self, n: int, stream=None) -> np.ndarray:
         """``n`` greedy steps from the argmax of the current logits: ids ``[n, batch]``."""
         out = np.zeros((max(n, 1), self.batch), dtype=np.int32)

@@ -118,6 +118,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_batch_buffers": (ctypes.c_int, [vp, P(vp), P(vp), P(vp), P(vp)]),
         "rwkvb_batch_reset": (ctypes.c_int, [vp, vp]),
         "rwkvb_batch_forward": (ctypes.c_int, [vp, P(i32), vp]),
+        "rwkvb_batch_prefill": (ctypes.c_int, [vp, P(i32), i32, vp]),
         "rwkvb_batch_decode_greedy": (ctypes.c_int, [vp, i32, P(i32), vp]),
         "rwkvb_batch_decode_greedy_async": (ctypes.c_int, [vp, i32, vp, vp]),
         "rwkvb_batch_launches_per_step": (ctypes.c_int, [vp, P(i32)]),

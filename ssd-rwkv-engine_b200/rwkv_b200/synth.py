@@ -69,6 +69,7 @@ PRESETS: dict[str, RWKV7Shape] = {
     "7.2b": RWKV7Shape(32, 4096, 64, 16384, 65536, 128, 128, 96, 480),
     # 2.9B widths with 4 layers: per-kernel profiling case (~0.5 GB, larger than L2)
     "2.9b-l4": RWKV7Shape(4, 2560, 64, 10240, 65536, 96, 96, 64, 320),
+    "7.2b-l4": RWKV7Shape(4, 4096, 64, 16384, 65536, 128, 128, 96, 480),
 }
 
 

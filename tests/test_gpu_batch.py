@@ -127,3 +127,76 @@ def test_batch_state_roundtrip_reset_and_errors():
             eng.forward([0] * 3)
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("nb,length", [(4, 37), (5, 24), (8, 16), (40, 7)])
+def test_prefill_matches_step_by_step(nb, length):
+    """Chunked prefill (positions of a chunk in one GEMM) against one forward step
+    per position: logits, state and the following greedy ids."""
+    shape, pack = _pack("tiny", 13)
+    prompts = _prompts(nb, length, shape.vocab, 13)
+    a = B200BatchEngine(pack, nb)
+    b = B200BatchEngine(pack, nb)
+    try:
+        a.prefill(prompts)
+        _prefill(b, prompts)
+        np.testing.assert_allclose(_np(a.logits), _np(b.logits), rtol=0, atol=TOL)
+        for t_a, t_b in ((a.att_x, b.att_x), (a.wkv, b.wkv), (a.ffn_x, b.ffn_x)):
+            np.testing.assert_allclose(_np(t_a), _np(t_b), rtol=0, atol=TOL)
+        assert np.array_equal(a.decode_greedy(5), b.decode_greedy(5))
+    finally:
+        a.close()
+        b.close()
+
+
+def test_prefill_matches_oracle_at_0p1b_width():
+    shape = synth.PRESETS["0.1b"]
+    sd = synth.generate_state_dict(shape, 17, "cpu")
+    pack = synth.make_pack(sd, policy="sg8")
+    oracle = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size)
+    nb, length = 2, 40
+    prompts = _prompts(nb, length, shape.vocab, 17)
+    eng = B200BatchEngine(pack, nb)
+    try:
+        eng.prefill(prompts)
+        logits = _np(eng.logits)
+        ids = eng.decode_greedy(2)
+        for s in range(nb):
+            ref_ids, ref_logits, _ = oracle.greedy(prompts[s], 3)
+            np.testing.assert_allclose(logits[s], ref_logits[length - 1], rtol=0, atol=TOL)
+            assert [int(t) for t in ids[:, s]] == ref_ids[1:]
+    finally:
+        eng.close()
+
+
+def test_7p2b_width_engines_match_oracle():
+    """7.2B width (d_model 4096, FFN 16384, 64 heads, ranks 128/128/96/480), 4 layers:
+    the batch-1 persistent engine against the oracle, then chunked prefill of 8
+    sessions against the batch-1 engine."""
+    shape = synth.PRESETS["7.2b-l4"]
+    sd = synth.generate_state_dict(shape, 23, "cuda")  # encoded on the GPU, host bytes for the oracle
+    pack = synth.make_pack(sd, policy="sg8")
+    del sd
+    torch.cuda.empty_cache()
+    oracle = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size)
+    prompt = synth.seeded_prompt(3, shape.vocab, 23)
+    ids_ref, logits_ref, _ = oracle.greedy(prompt, 2)
+    one = B200Engine(pack)
+    try:
+        ids, logits = one.greedy(prompt, 2, keep_logits=True)
+        assert ids == ids_ref
+        np.testing.assert_allclose(_np(logits), logits_ref, rtol=0, atol=TOL)
+        nb = 8
+        prompts = _prompts(nb, 20, shape.vocab, 23)
+        eng = B200BatchEngine(one._model, nb)
+        try:
+            eng.prefill(prompts)
+            got = _np(eng.logits)
+            for b in (0, nb - 1):
+                one.reset()
+                one.forward(prompts[b])
+                np.testing.assert_allclose(got[b], _np(one.logits), rtol=0, atol=TOL)
+        finally:
+            eng.close()
+    finally:
+        one.close()
