@@ -243,10 +243,10 @@ int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first_token, int32
  * the engine was created with flag bit 3; copies min(cap, 262144) values to
  * host `out`:
  *   [0, 131072): phase marks, [2][65536] (first CTA, last CTA): per token the
- *     token start, per layer 22 marks (A start, ln1, shift state, r/k/v digits,
- *     A units, A items, B barrier, B done, C barrier, C prep, C units, D
- *     barrier, D loads, ln2, D prep, D units, E barrier, E slices, E prep,
- *     E units), then head barrier, head prep, head units;
+ *     token start, per layer 16 marks (A start, A prep (ln1, shift state, r/k/v
+ *     digits), A units, A items, B barrier, B done, C barrier, C prep, C units,
+ *     D barrier, D prep (loads, ln2, digits), D units, E barrier, E slices,
+ *     E prep, E units), then head barrier, head prep, head units;
  *   [131072, 262144): ring events of the first CTA, 3 per stage s (s < 43690):
  *     producer issue, consumer wait end, consumer release.
  * The GPU counterpart of the reference's per-layer LayerTiming rows
@@ -271,11 +271,40 @@ typedef struct rwkvb_batch rwkvb_batch;
 
 /* flags: bit0 = run the step as plain launches (no CUDA graph). */
 int rwkvb_batch_create(const rwkvb_model_desc* desc, int32_t batch, uint32_t flags, rwkvb_batch** out);
+
+/* Tensor parallelism across the GPUs of one node (one process per GPU), the
+ * head-sharded split for models such as the 7.2B one: each rank holds the attention heads
+ * of its shard (r/k/v rows, the matching columns of the adapter second stages
+ * and of the output projection, the heads' per-channel vectors), a slice of the
+ * FFN (key rows, the matching value columns) and a slice of the vocabulary
+ * (head rows); embedding, LayerNorms, token-shift mixes and adapter first stages
+ * are replicated.  Per layer the output and value projections yield partial
+ * sums that the host's `collective` callback all-reduces (kind 0: sum of fp32 in
+ * place, send == recv); the per-session argmax bests (float value, int32 index
+ * bits, 8 bytes per session) are all-gathered (kind 1: `bytes` from every rank
+ * into recv in rank order).  The callback is called on the engine's stream
+ * while the step is recorded (it is captured into the step's CUDA graph when
+ * the collective library supports capture) and must issue the collective on
+ * that stream's order.  `local` describes this rank's shard: att r/k/v
+ * [Ca][n_embd], att_o [n_embd][Ca], w2/a2/g2/v2 [rank][Ca], ffn_key [ffn][n_embd],
+ * ffn_value [n_embd][ffn], head [vocab_local][n_embd]; n_embd the full width,
+ * vocab the full embedding vocabulary. */
+typedef void (*rwkvb_collective_fn)(int32_t kind, void* send, void* recv, int64_t bytes, void* stream, void* user);
+typedef struct rwkvb_tp_desc {
+  int32_t rank, size;        /* this rank, ranks (>= 2) */
+  int32_t vocab_offset;      /* first vocabulary row of this rank's head shard */
+  rwkvb_collective_fn collective;
+  void* user;
+} rwkvb_tp_desc;
+int rwkvb_batch_create_tp(const rwkvb_model_desc* local, int32_t batch, const rwkvb_tp_desc* tp, uint32_t flags,
+                          rwkvb_batch** out);
 int rwkvb_batch_destroy(rwkvb_batch* e);
 
 /* Device state, per layer l and session b (each block as in rwkvb_engine_buffers):
  *   att_x + (l*batch + b)*n_embd,  wkv + (l*batch + b)*n_head*N*N,  ffn_x + (l*batch + b)*n_embd;
- * logits [batch][vocab] of the last step. */
+ * logits [batch][vocab] of the last step.  Under tensor parallelism n_head is
+ * this rank's heads (Ca / 64) and logits hold this rank's vocabulary rows
+ * [vocab_offset, vocab_offset + vocab_local). */
 int rwkvb_batch_buffers(rwkvb_batch* e, float** att_x, float** wkv, float** ffn_x, float** logits);
 int rwkvb_batch_reset(rwkvb_batch* e, void* stream);
 

@@ -15,6 +15,12 @@ Restates, step for step and in fp32 activations:
 Packed GEMVs run through ``oracle.kernels`` (the restated C kernels, or the
 reference's own C kernels with ``impl="reference"``).
 
+The same class runs one rank's shard of a tensor-parallel split (heads, FFN
+rows and vocabulary rows, as ``rwkv_b200.tp.shard_pack`` makes it): widths are
+read from the pack, ``reduce`` sums the output and FFN value projections over
+the ranks and ``argmax`` picks the global first maximum.  With the defaults
+(identity, ``np.argmax``) and a full pack it is the single-device restatement.
+
 A *pack* is a mapping ``name -> entry`` where ``entry`` has ``codec``
 (``"sg8"``, ``"lut2"`` or ``"none"``), ``payload`` (wire bytes, or an fp32
 array for ``"none"``) and ``shape`` (checkpoint shape).
@@ -47,13 +53,18 @@ class OracleRWKV7:
     """Token-by-token RWKV-7 decode over a packed model, on the CPU."""
 
     def __init__(self, pack, *, n_layer: int, n_embd: int, head_size: int,
-                 impl: str = "oracle"):
+                 impl: str = "oracle", reduce=None, argmax=None):
         self.pack = pack
         self.L = int(n_layer)
         self.C = int(n_embd)
         self.N = int(head_size)
-        self.H = self.C // self.N
+        # attention heads held (all of them, or a tensor-parallel shard)
+        rk = pack.get("blocks.0.att.r_k")
+        self.H = int(rk.shape[0]) if rk is not None else self.C // self.N
+        self.Ca = self.H * self.N
         self.impl = impl
+        self.reduce = reduce if reduce is not None else (lambda v: v)
+        self.argmax = argmax if argmax is not None else (lambda logits: int(np.argmax(logits)))
         self._dense: dict[str, np.ndarray] = {}
         self.vocab = int(pack["head.weight"].shape[0])
 
@@ -114,7 +125,7 @@ class OracleRWKV7:
              S: np.ndarray):
         """``tmix_one_fused`` (rwkv7_linear.py:125-356). Returns
         ``(out, new_x_prev, new_S, v_first)``."""
-        H, N, C = self.H, self.N, self.C
+        H, N, C = self.H, self.N, self.Ca
         p = f"blocks.{layer}.att."
         xx = x_prev - x
         xr = x + xx * self.vec(p + "x_r")
@@ -129,7 +140,7 @@ class OracleRWKV7:
 
         names = ["w1", "w2", "a1", "a2", "g1", "g2"] + (["v1", "v2"] if layer != 0 else [])
         ents = [self.pack[p + n] for n in names]
-        if all(e.codec == "sg8" for e in ents):
+        if all(e.codec == "sg8" for e in ents) and self.Ca == self.C:
             ranks = [ents[0].shape[1], ents[2].shape[1], ents[4].shape[1],
                      ents[6].shape[1] if layer != 0 else 0]
             xs = [xw, xa, xg] + ([xv] if layer != 0 else [])
@@ -167,7 +178,7 @@ class OracleRWKV7:
         y = y * self.vec(p + "ln_x.weight") + self.vec(p + "ln_x.bias")
         bonus = (r * k * self.vec(p + "r_k")).reshape(H, N).sum(axis=1, keepdims=True, dtype=np.float32)
         y = (y + (bonus * v.reshape(H, N)).reshape(C)).astype(np.float32)
-        out = self.gemv(p + "output.weight", (y * g).astype(np.float32))
+        out = self.reduce(self.gemv(p + "output.weight", (y * g).astype(np.float32)))
         return out, x, S, v_first
 
     def cmix(self, layer: int, x: np.ndarray, x_prev: np.ndarray):
@@ -182,7 +193,7 @@ class OracleRWKV7:
             h = self.gemv(p + "key.weight", k)
             h = np.maximum(h, np.float32(0.0)) ** 2
             out = self.gemv(p + "value.weight", h.astype(np.float32))
-        return out, x
+        return self.reduce(out), x
 
     def block(self, layer: int, x: np.ndarray, state: list, v_first):
         """``forward_block_packed`` (packed_block_forward.py:76-166)."""
@@ -221,7 +232,7 @@ class OracleRWKV7:
             rows.append(logits)
         ids = []
         for i in range(n_new):
-            nxt = int(np.argmax(logits))
+            nxt = self.argmax(logits)
             ids.append(nxt)
             if i + 1 < n_new:
                 logits = self.forward_token(nxt, st)

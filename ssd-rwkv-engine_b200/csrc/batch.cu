@@ -397,6 +397,7 @@ struct BtInArgs {
   float2* cs[3];
   float* xa4;            // [4][nb][C]: w, a, g, v adapter inputs
   int C, nb, bp, lfk;
+  const float* add;      // tensor parallel: all-reduced value projection [nb][C] (x = xm + add), or null
 };
 
 constexpr int kBtRowThreads = 1024;  // per-session row kernels (one CTA per session)
@@ -412,6 +413,9 @@ __global__ void __launch_bounds__(kBtRowThreads) bt_in_kernel(BtInArgs a) {
     float v;
     if (a.part) {
       v = a.xm[(size_t)b * C + i] + bt_fold(a.part, a.pp, a.nb, C, b, i);
+      a.x[(size_t)b * C + i] = v;
+    } else if (a.add) {
+      v = a.xm[(size_t)b * C + i] + a.add[(size_t)b * C + i];
       a.x[(size_t)b * C + i] = v;
     } else {
       v = a.x[(size_t)b * C + i];
@@ -741,6 +745,7 @@ struct BtFfnArgs {
   uint8_t* dig;
   float2* cs;
   int C, nb, bp, lfk;
+  const float* add;     // tensor parallel: all-reduced output projection [nb][C], or null (fold `part`)
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_ffn_kernel(BtFfnArgs a) {
@@ -749,7 +754,8 @@ __global__ void __launch_bounds__(kBtRowThreads) bt_ffn_kernel(BtFfnArgs a) {
   const int b = blockIdx.x, C = a.C;
   float* xl = bt_sm;
   for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const float v = a.x[(size_t)b * C + i] + bt_fold(a.part, a.pp, a.nb, C, b, i);
+    const float o = a.add ? a.add[(size_t)b * C + i] : bt_fold(a.part, a.pp, a.nb, C, b, i);
+    const float v = a.x[(size_t)b * C + i] + o;
     a.xm[(size_t)b * C + i] = v;
     xl[i] = v;
   }
@@ -1014,8 +1020,12 @@ __global__ void bt_pick_last_kernel(float* xs, const float* xm, const float* par
   xs[(size_t)s * C + c] = xm[(size_t)row * C + c] + bt_fold(part, pp, rows, C, row, c);
 }
 
+// Per-session first-maximum argmax of the logits; with `loc` set (tensor
+// parallel: this rank holds vocabulary [v0, v0 + V)) the session's best
+// (value, global index) goes to loc[b] for the cross-rank merge instead.
 __global__ void __launch_bounds__(1024) bt_argmax_kernel(float* logits, const float* part, BtPieces pp, int nb,
-                                                         int V, int* tok, int* hist, const int* step, int hist_cap) {
+                                                         int V, int* tok, int* hist, const int* step, int hist_cap,
+                                                         int v0, float2* loc) {
   __shared__ float bv[32];
   __shared__ int bi[32];
   const int b = blockIdx.x;
@@ -1053,10 +1063,36 @@ __global__ void __launch_bounds__(1024) bt_argmax_kernel(float* logits, const fl
         ci = bi[w];
       }
     if (ci == 0x7fffffff) ci = 0;  // every logit NaN
+    if (loc) {
+      loc[b] = make_float2(cb, __int_as_float(ci + v0));
+      return;
+    }
     tok[b] = ci;
     const int s = *step;
     hist[(size_t)((s % hist_cap + hist_cap) % hist_cap) * nb + b] = ci;
   }
+}
+
+// Merge the ranks' per-session bests all[r][b] (ranks hold increasing
+// vocabulary ranges): the largest value, the smallest index among equals.
+__global__ void bt_argmax_merge_kernel(const float2* all, int ranks, int nb, int* tok, int* hist, const int* step,
+                                       int hist_cap) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nb) return;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int r = 0; r < ranks; ++r) {
+    const float2 c = all[(size_t)r * nb + b];
+    const int ci = __float_as_int(c.y);
+    if (c.x > best || (c.x == best && ci < bi)) {
+      best = c.x;
+      bi = ci;
+    }
+  }
+  if (bi == 0x7fffffff) bi = 0;
+  tok[b] = bi;
+  const int s = *step;
+  hist[(size_t)((s % hist_cap + hist_cap) % hist_cap) * nb + b] = bi;
 }
 
 }  // namespace rwkvb
@@ -1139,6 +1175,15 @@ struct rwkvb_batch {
   bool use_graph = true;
   int launches = 0;
   rwkvb::BtPrefill* pf = nullptr;
+  // tensor parallel: this rank holds attention channels [., . + Ca) (H = Ca / 64
+  // heads), F FFN rows and vocabulary [V0, V0 + V) of Vfull; partial output and
+  // value projections are all-reduced (collective kind 0), per-session argmax
+  // bests all-gathered (kind 1) through the host's collective callback
+  int Ca = 0, Vfull = 0, V0 = 0, tp_rank = 0, tp_size = 1;
+  rwkvb_collective_fn collective = nullptr;
+  void* collective_user = nullptr;
+  float *ored = nullptr, *vred = nullptr;
+  float2 *amax_loc = nullptr, *amax_all = nullptr;
 };
 
 namespace rwkvb {
@@ -1155,7 +1200,8 @@ BtPieces bt_pieces(const BgArgs& a, int job, int grid) {
 
 // ln_out of x (+ folded value pieces onto xm when `part` is set), the head
 // GEMM and the per-session first-maximum argmax (-> e->tok, e->logits).
-int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part, const BtPieces& pp, cudaStream_t s) {
+int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part, const BtPieces& pp, cudaStream_t s,
+                   const float* add = nullptr) {
   const int C = e->C, nb = e->nb;
   BtInArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -1163,6 +1209,7 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
   a.xm = xm;
   a.part = part;
   a.pp = pp;
+  a.add = add;
   a.ln_w = e->lnout_w;
   a.ln_b = e->lnout_b;
   a.state = nullptr;
@@ -1173,14 +1220,31 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
   int st = cuda_status(cudaGetLastError());
   if (st == RWKVB_OK) st = bg_launch(e->head, e->g_head, e->smem_bg, s);
   if (st != RWKVB_OK) return st;
+  const bool tp = e->tp_size > 1;
   bt_argmax_kernel<<<nb, 1024, 0, s>>>(e->logits, e->part_head, e->pp_head, nb, e->V, e->tok, e->hist, e->step,
-                                       e->hist_cap);
+                                       e->hist_cap, e->V0, tp ? e->amax_loc : nullptr);
+  st = cuda_status(cudaGetLastError());
+  if (st != RWKVB_OK || !tp) return st;
+  e->collective(1, e->amax_loc, e->amax_all, (int64_t)sizeof(float2) * nb, s, e->collective_user);
+  bt_argmax_merge_kernel<<<(nb + 127) / 128, 128, 0, s>>>(e->amax_all, e->tp_size, nb, e->tok, e->hist, e->step,
+                                                          e->hist_cap);
   return cuda_status(cudaGetLastError());
+}
+
+// Tensor parallel: fold a projection's pieces into `red` [nb][C] and all-reduce it.
+int bt_reduce(rwkvb_batch* e, float* red, const float* part, const BtPieces& pp, cudaStream_t s) {
+  const int n = e->nb * e->C;
+  bg_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(red, part, e->nb, e->C, pp.stage0, pp.G, pp.total, pp.ncta);
+  const int st = cuda_status(cudaGetLastError());
+  if (st != RWKVB_OK) return st;
+  e->collective(0, red, red, (int64_t)sizeof(float) * n, s, e->collective_user);
+  return RWKVB_OK;
 }
 
 // Launch one token step of every session (tokens already in e->tok).
 int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
-  const int C = e->C, nb = e->nb;
+  const int C = e->C, Ca = e->Ca, nb = e->nb;
+  const bool tp = e->tp_size > 1;
   int n = 0;
 #define BT_CHECK()                                                                           \
   do {                                                                                       \
@@ -1192,7 +1256,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     ++n;                                                                                     \
   } while (0)
   {
-    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, e->tok, e->x, e->step, e->err, C, e->V};
+    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, e->tok, e->x, e->step, e->err, C, e->Vfull};
     bt_embed_kernel<<<nb, kBtThreads, sizeof(float) * C, s>>>(a);
     BT_CHECK();
   }
@@ -1204,7 +1268,8 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       std::memset(&a, 0, sizeof(a));
       a.x = e->x;
       a.xm = e->xm;
-      a.part = l0 ? nullptr : e->part_val;
+      a.part = (l0 || tp) ? nullptr : e->part_val;
+      a.add = (!l0 && tp) ? e->vred : nullptr;
       a.pp = e->pp_value;
       a.ln_w = ly.ln1_w;
       a.ln_b = ly.ln1_b;
@@ -1260,8 +1325,8 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       for (int m = 0; m < nm; ++m) a.fast[m] = bt_fast_adp2(a.w[m], C);
       a.midT = e->mid;
       a.out = e->adp2;
-      a.C = C, a.nb = nb, a.rtot = e->rtot;
-      bt_adp2_kernel<<<dim3(C / 64, nm), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
+      a.C = Ca, a.nb = nb, a.rtot = e->rtot;
+      bt_adp2_kernel<<<dim3(Ca / 64, nm), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
       BT_CHECK();
     }
     {
@@ -1275,17 +1340,21 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.att_y = e->att_y;
       a.w0 = ly.w0, a.a0 = ly.a0, a.v0 = ly.v0, a.k_k = ly.k_k, a.k_a = ly.k_a, a.r_k = ly.r_k;
       a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
-      a.C = C, a.H = e->H, a.nb = nb, a.layer0 = l0 ? 1 : 0;
+      a.C = Ca, a.H = e->H, a.nb = nb, a.layer0 = l0 ? 1 : 0;
       bt_wkv_kernel<<<dim3(e->H, (nb + kBtWkvSess - 1) / kBtWkvSess), kBtThreads, 0, s>>>(a);
       BT_CHECK();
     }
-    if (bg_digits(e->dig_y, e->cs_y, e->att_y, C, C, nb, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_digits(e->dig_y, e->cs_y, e->att_y, Ca, Ca, nb, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     if (bg_launch(ly.o, e->g_o, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
+    if (tp) {
+      if (bt_reduce(e, e->ored, e->part_o, e->pp_o, s) != RWKVB_OK) return RWKVB_ECUDA;
+      ++n;
+    }
     {
       BtFfnArgs a{e->x, e->xm, e->part_o, e->pp_o, ly.ln2_w, ly.ln2_b, ly.ffn_x_k,
-                  e->ffn_x + (size_t)l * nb * C, e->dig_f, e->cs_f, C, nb, e->bp, e->lfk};
+                  e->ffn_x + (size_t)l * nb * C, e->dig_f, e->cs_f, C, nb, e->bp, e->lfk, tp ? e->ored : nullptr};
       bt_ffn_kernel<<<nb, kBtRowThreads, sizeof(float) * C, s>>>(a);
       BT_CHECK();
     }
@@ -1299,11 +1368,16 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     }
     if (bg_launch(ly.value, e->g_value, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
+    if (tp) {
+      if (bt_reduce(e, e->vred, e->part_val, e->pp_value, s) != RWKVB_OK) return RWKVB_ECUDA;
+      ++n;
+    }
   }
   {
-    const int st = bt_record_head(e, e->x, e->xm, e->part_val, e->pp_value, s);
+    const int st = tp ? bt_record_head(e, e->x, e->xm, nullptr, e->pp_value, s, e->vred)
+                      : bt_record_head(e, e->x, e->xm, e->part_val, e->pp_value, s);
     if (st != RWKVB_OK) return st;
-    n += 3;
+    n += tp ? 4 : 3;
   }
 #undef BT_CHECK
   e->launches = n;
@@ -1349,6 +1423,7 @@ int bt_check_err(rwkvb_batch* e, cudaStream_t s) {
 // Build the prefill plan: chunk P = 64 / nb positions (at least 2).
 int bt_prefill_setup(rwkvb_batch* e) {
   if (e->pf) return RWKVB_OK;
+  if (e->tp_size > 1) return RWKVB_EUNSUPPORTED;  // positions then run as (tensor-parallel) decode steps
   const int P = kBgMaxSessions / e->nb;
   if (P < 2) return RWKVB_EUNSUPPORTED;
   BtPrefill* f = new (std::nothrow) BtPrefill();
@@ -1453,7 +1528,7 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
     if (st_ != RWKVB_OK) return st_;                \
   } while (0)
   {
-    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, f.tok, f.x, f.step, e->err, C, e->V};
+    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, f.tok, f.x, f.step, e->err, C, e->Vfull};
     bt_embed_kernel<<<rows, kBtThreads, sizeof(float) * C, s>>>(a);
     PF_CHECK();
   }
@@ -1604,7 +1679,7 @@ int bt_run_prefill_chunk(rwkvb_batch* e, cudaStream_t s) {
 extern "C" int rwkvb_batch_prefill(rwkvb_batch* e, const int32_t* tokens, int32_t n, void* stream) {
   if (!e || (!tokens && n > 0) || n < 0) return RWKVB_EARG;
   for (size_t i = 0; i < (size_t)n * e->nb; ++i)
-    if (tokens[i] < 0 || tokens[i] >= e->V) return RWKVB_EARG;
+    if (tokens[i] < 0 || tokens[i] >= e->Vfull) return RWKVB_EARG;
   if (n == 0) return RWKVB_OK;
   cudaStream_t s = (cudaStream_t)stream;
   int st = bt_prefill_setup(e);
@@ -1634,12 +1709,21 @@ extern "C" int rwkvb_batch_prefill(rwkvb_batch* e, const int32_t* tokens, int32_
   return st;
 }
 
-extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, rwkvb_batch** out) {
+namespace rwkvb {
+namespace {
+int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rwkvb_tp_desc* tp, rwkvb_batch** out) {
   if (!m || !out || !m->layers || batch <= 0 || batch > kBgMaxSessions) return RWKVB_EARG;
   *out = nullptr;
-  const int L = m->n_layer, C = m->n_embd, N = m->head_size, F = m->ffn, V = m->vocab;
-  if (L <= 0 || C <= 0 || F <= 0 || V <= 0 || N != 64 || C % 128 || F % 128 || V % 128) return RWKVB_EUNSUPPORTED;
-  if (!bt_desc_ok(m->emb, V, C) || !bg_matrix_ok(m->head) || m->head.rows != V || m->head.cols != C)
+  // V: vocabulary rows of this engine's head (a shard under tensor parallelism); Vfull: embedding rows
+  const int L = m->n_layer, C = m->n_embd, N = m->head_size, F = m->ffn, Vfull = m->vocab, V = m->head.rows;
+  const int Ca = m->layers[0].att_r.rows;  // attention channels held here
+  if (L <= 0 || C <= 0 || F <= 0 || V <= 0 || N != 64 || C % 128 || F % 128 || V % 128 || Ca <= 0 || Ca % 128)
+    return RWKVB_EUNSUPPORTED;
+  if (!tp && (Ca != C || V != Vfull)) return RWKVB_EARG;
+  if (tp && (tp->size < 2 || tp->rank < 0 || tp->rank >= tp->size || !tp->collective || tp->vocab_offset < 0 ||
+             tp->vocab_offset + V > Vfull))
+    return RWKVB_EARG;
+  if (!bt_desc_ok(m->emb, Vfull, C) || !bg_matrix_ok(m->head) || m->head.cols != C)
     return m->head.kind == RWKVB_KIND_SG8 ? RWKVB_EUNSUPPORTED : RWKVB_EARG;
   if (!m->ln0_w || !m->ln0_b || !m->ln_out_w || !m->ln_out_b) return RWKVB_EARG;
   const rwkvb_layer_desc& l0 = m->layers[0];
@@ -1651,14 +1735,14 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
     const rwkvb_packed* big[] = {&s.att_r, &s.att_k, &s.att_v, &s.att_o, &s.ffn_key, &s.ffn_value};
     for (const rwkvb_packed* p : big)
       if (!bg_matrix_ok(*p) || p->group_size != group) return RWKVB_EUNSUPPORTED;
-    if (s.att_r.rows != C || s.att_r.cols != C || s.att_k.rows != C || s.att_k.cols != C || s.att_v.rows != C ||
-        s.att_v.cols != C || s.att_o.rows != C || s.att_o.cols != C || s.ffn_key.rows != F ||
+    if (s.att_r.rows != Ca || s.att_r.cols != C || s.att_k.rows != Ca || s.att_k.cols != C || s.att_v.rows != Ca ||
+        s.att_v.cols != C || s.att_o.rows != C || s.att_o.cols != Ca || s.ffn_key.rows != F ||
         s.ffn_key.cols != C || s.ffn_value.rows != C || s.ffn_value.cols != F)
       return RWKVB_EARG;
-    if (!bt_desc_ok(s.w1, C, rw) || !bt_desc_ok(s.w2, rw, C) || !bt_desc_ok(s.a1, C, ra) ||
-        !bt_desc_ok(s.a2, ra, C) || !bt_desc_ok(s.g1, C, rg) || !bt_desc_ok(s.g2, rg, C))
+    if (!bt_desc_ok(s.w1, C, rw) || !bt_desc_ok(s.w2, rw, Ca) || !bt_desc_ok(s.a1, C, ra) ||
+        !bt_desc_ok(s.a2, ra, Ca) || !bt_desc_ok(s.g1, C, rg) || !bt_desc_ok(s.g2, rg, Ca))
       return RWKVB_EARG;
-    if (i > 0 && (!bt_desc_ok(s.v1, C, rv) || !bt_desc_ok(s.v2, rv, C))) return RWKVB_EARG;
+    if (i > 0 && (!bt_desc_ok(s.v1, C, rv) || !bt_desc_ok(s.v2, rv, Ca))) return RWKVB_EARG;
     const float* vecs[] = {s.ln1_w, s.ln1_b, s.ln2_w, s.ln2_b, s.x_r, s.x_w, s.x_k, s.x_v, s.x_a, s.x_g,
                            s.w0, s.a0, s.k_k, s.k_a, s.r_k, s.lnx_w, s.lnx_b, s.ffn_x_k};
     for (const float* p : vecs)
@@ -1677,7 +1761,12 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
   e->nrows = bg_digit_rows(batch);
   e->group = (int)group;
   e->lfk = group == 64 ? 6 : 7;
-  e->L = L, e->C = C, e->H = C / 64, e->F = F, e->V = V;
+  e->L = L, e->C = C, e->H = Ca / 64, e->F = F, e->V = V;
+  e->Ca = Ca, e->Vfull = Vfull;
+  if (tp) {
+    e->tp_rank = tp->rank, e->tp_size = tp->size, e->V0 = tp->vocab_offset;
+    e->collective = tp->collective, e->collective_user = tp->user;
+  }
   e->rw = rw, e->ra = ra, e->rg = rg, e->rv = rv, e->rtot = rw + ra + rg + rv;
   e->adp_splits = C / kBtAdpKc;
   e->emb = make_view(m->emb);
@@ -1730,6 +1819,10 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
       {(void**)&e->hist, 4 * (size_t)e->hist_cap * batch},
       {(void**)&e->step, 16},
       {(void**)&e->err, 16},
+      {(void**)&e->ored, 4 * nbC},
+      {(void**)&e->vred, 4 * nbC},
+      {(void**)&e->amax_loc, 8 * (size_t)batch},
+      {(void**)&e->amax_all, 8 * (size_t)batch * e->tp_size},
   };
   size_t total = 0;
   std::vector<size_t> offs;
@@ -1745,10 +1838,12 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
   cudaMemset(e->arena, 0, total);
   for (size_t i = 0; i < items.size(); ++i) *items[i].p = (char*)e->arena + offs[i];
   {
-    uint8_t* digs[] = {e->dig_r, e->dig_k, e->dig_v, e->dig_y, e->dig_f, e->dig_o};
+    // constant rows (the ones row at 3 * bp * K) laid out for each GEMM's own K
+    uint8_t* digs[] = {e->dig_r, e->dig_k, e->dig_v, e->dig_f, e->dig_o};
     int st = RWKVB_OK;
     for (uint8_t* d : digs)
       if (st == RWKVB_OK) st = bg_digits_init(d, C, batch, nullptr);
+    if (st == RWKVB_OK) st = bg_digits_init(e->dig_y, Ca, batch, nullptr);
     if (st == RWKVB_OK) st = bg_digits_init(e->dig_h, F, batch, nullptr);
     if (st == RWKVB_OK) st = cuda_status(cudaMemset(e->step, 0xff, sizeof(int)));
     if (st == RWKVB_OK) st = cuda_status(cudaDeviceSynchronize());
@@ -1761,7 +1856,7 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
 
   // ------------------------------------------------------- GEMM launch plans
   const BgDigits d_rkv[3] = {{e->dig_r, e->cs_r, C}, {e->dig_k, e->cs_k, C}, {e->dig_v, e->cs_v, C}};
-  const BgDigits d_y{e->dig_y, e->cs_y, C}, d_f{e->dig_f, e->cs_f, C}, d_h{e->dig_h, e->cs_h, F},
+  const BgDigits d_y{e->dig_y, e->cs_y, Ca}, d_f{e->dig_f, e->cs_f, C}, d_h{e->dig_h, e->cs_h, F},
       d_o{e->dig_o, e->cs_o, C};
   int pieces = 0, st = RWKVB_OK;
   size_t smem = 0;
@@ -1857,6 +1952,18 @@ extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint
   *out = e;
   return RWKVB_OK;
 }
+}  // namespace
+}  // namespace rwkvb
+
+extern "C" int rwkvb_batch_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, rwkvb_batch** out) {
+  return bt_create(m, batch, flags, nullptr, out);
+}
+
+extern "C" int rwkvb_batch_create_tp(const rwkvb_model_desc* local, int32_t batch, const rwkvb_tp_desc* tp,
+                                     uint32_t flags, rwkvb_batch** out) {
+  if (!tp) return RWKVB_EARG;
+  return bt_create(local, batch, flags, tp, out);
+}
 
 extern "C" int rwkvb_batch_destroy(rwkvb_batch* e) {
   if (!e) return RWKVB_EARG;
@@ -1895,7 +2002,7 @@ extern "C" int rwkvb_batch_reset(rwkvb_batch* e, void* stream) {
 extern "C" int rwkvb_batch_forward(rwkvb_batch* e, const int32_t* tokens, void* stream) {
   if (!e || !tokens) return RWKVB_EARG;
   for (int i = 0; i < e->nb; ++i)
-    if (tokens[i] < 0 || tokens[i] >= e->V) return RWKVB_EARG;
+    if (tokens[i] < 0 || tokens[i] >= e->Vfull) return RWKVB_EARG;
   cudaStream_t s = (cudaStream_t)stream;
   int st = cuda_status(cudaMemcpyAsync(e->tok, tokens, sizeof(int32_t) * e->nb, cudaMemcpyHostToDevice, s));
   if (st == RWKVB_OK) st = bt_run_step(e, s);
@@ -1939,6 +2046,10 @@ extern "C" int rwkvb_batch_decode_greedy(rwkvb_batch* e, int32_t n, int32_t* out
 
 extern "C" int rwkvb_batch_launches_per_step(rwkvb_batch* e, int32_t* out) {
   if (!e || !out) return RWKVB_EARG;
-  *out = 3 + 11 * e->L + 1;  // embed; 11 per layer; head input, head GEMM, argmax
+  // embed; per layer 12 (ln1/shift/digits, r/k/v GEMM, adapter stage 1, its
+  // activation, stage 2, WKV, y digits, output GEMM, ln2/digits, key GEMM,
+  // relu^2 digits, value GEMM) + 2 reductions under tensor parallelism; head
+  // input, head GEMM, argmax (+ merge)
+  *out = e->tp_size > 1 ? 1 + 14 * e->L + 4 : 1 + 12 * e->L + 3;
   return RWKVB_OK;
 }

@@ -76,6 +76,18 @@ class ModelDesc(ctypes.Structure):
                 ("layers", ctypes.POINTER(LayerDesc))]
 
 
+# void (*)(int32 kind, void* send, void* recv, int64 bytes, void* stream, void* user)
+COLLECTIVE_FN = ctypes.CFUNCTYPE(None, ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                 ctypes.c_void_p, ctypes.c_void_p)
+COLLECTIVE_ALLREDUCE_SUM_F32 = 0
+COLLECTIVE_ALLGATHER = 1
+
+
+class TPDesc(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int32), ("size", ctypes.c_int32), ("vocab_offset", ctypes.c_int32),
+                ("collective", COLLECTIVE_FN), ("user", ctypes.c_void_p)]
+
+
 def native_lib_path() -> Path | None:
     return _build.LIB if _build.LIB.is_file() else None
 
@@ -114,6 +126,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_engine_launches_per_step": (ctypes.c_int, [vp, P(i32)]),
         "rwkvb_engine_trace": (ctypes.c_int, [vp, P(u64), i32, P(i32)]),
         "rwkvb_batch_create": (ctypes.c_int, [P(ModelDesc), i32, u32, P(vp)]),
+        "rwkvb_batch_create_tp": (ctypes.c_int, [P(ModelDesc), i32, P(TPDesc), u32, P(vp)]),
         "rwkvb_batch_destroy": (ctypes.c_int, [vp]),
         "rwkvb_batch_buffers": (ctypes.c_int, [vp, P(vp), P(vp), P(vp), P(vp)]),
         "rwkvb_batch_reset": (ctypes.c_int, [vp, vp]),

@@ -1,7 +1,8 @@
 """Multi-GPU decode by replicas: one process per GPU, each holding its own copy
 of the model and decoding its own sessions, with no collective on the data
-path (the reference runs independent sessions per device; tensor splitting is
-only for models that do not fit, SURVEY's 7.2B row).
+path (the reference runs independent sessions per device; tensor splitting,
+``rwkv_b200.tp``, is for models whose step should be spread over several GPUs,
+such as the 7.2B one).
 
 The host logic here is what every rank runs around the device work:
 

@@ -298,9 +298,11 @@ def packed_nbytes(pack: dict[str, PackedTensor], names=None) -> int:
 
 
 def make_pack_streaming(s: RWKV7Shape, seed: int, device="cuda", *, policy: str = "sg8", sg8_group: int = 128,
-                        lut2_group: int = 64) -> dict[str, PackedTensor]:
+                        lut2_group: int = 64, transform=None) -> dict[str, PackedTensor]:
     """Draw and encode one tensor at a time on ``device`` (blobs stay uint8
-    tensors there), so multi-GB packs never hold the whole fp32 model."""
+    tensors there), so multi-GB packs never hold the whole fp32 model.
+    ``transform(name, entry) -> entry``, when given, is applied to each entry as
+    it is made (e.g. keeping one tensor-parallel shard of it)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(int(seed))
     out: dict[str, PackedTensor] = {}
@@ -313,8 +315,9 @@ def make_pack_streaming(s: RWKV7Shape, seed: int, device="cuda", *, policy: str 
             payload = encode_lut2(t, lut2_group)
         else:
             payload = t.reshape(-1).clone()
-        out[name] = PackedTensor(name, shp, codec, payload)
-        del t
+        entry = PackedTensor(name, shp, codec, payload)
+        out[name] = transform(name, entry) if transform is not None else entry
+        del t, payload, entry
     return out
 
 
