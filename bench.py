@@ -311,6 +311,88 @@ def run_prefill(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) 
                     "d2h_bytes_per_step": 0, "how": "B200BatchEngine.prefill(host prompts): tokens copied per chunk"}}
 
 
+def run_tp(args, dev, stream, world: int, rank: int) -> dict:
+    """Tensor-parallel leg: ``args.tp_sessions`` sessions of the ``args.tp_config``
+    model decoded with the model split over all ranks (heads, FFN rows and
+    vocabulary rows; two NCCL all-reduces per layer and one all-gather of the
+    argmax bests per step, captured with the step in one CUDA graph).  At one
+    GPU the same sessions run on the unsplit batched engine.  Total work is
+    fixed as the rank count grows (strong scaling).  Algorithmic bytes per step:
+    the weights once over all ranks plus every session's state read and
+    written; the peak is the ranks' summed HBM bandwidth."""
+    from rwkv_b200 import synth, tp
+    from rwkv_b200.engine import B200BatchEngine
+
+    shape = synth.PRESETS[args.tp_config]
+    nb = args.tp_sessions
+    if world > 1:
+        plan = tp.plan(shape, rank, world)
+        local = synth.make_pack_streaming(shape, SEED + 7, dev, policy="sg8",
+                                          transform=lambda n, e: tp.shard_entry(n, e, plan))
+        eng = tp.B200TPBatchEngine(local, nb, device=dev, shard_plan=plan, use_graph=True)
+    else:
+        local = synth.make_pack_streaming(shape, SEED + 7, dev, policy="sg8")
+        eng = B200BatchEngine(local, nb, device=dev)
+    bpt_local = bytes_per_token(local, shape) if world == 1 else None
+    del local
+    torch.cuda.empty_cache()
+    prompts = [synth_prompt(16, shape.vocab, replicas.session_seed(SEED + 7, g)) for g in range(nb)]
+    for pos in range(16):
+        eng.forward([p[pos] for p in prompts])
+    out = torch.empty((max(args.tp_steps, args.warmup) + 1) * nb, dtype=torch.int32, device=dev)
+    eng.decode_greedy_async(args.warmup, out)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    _nvtx_push("timed_tp")
+    t0.record(stream)
+    eng.decode_greedy_async(args.tp_steps, out)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    _nvtx_pop()
+    ms = replicas.max_over_ranks(t0.elapsed_time(t1))
+    ms_step = ms / args.tp_steps
+    # end to end: greedy ids of every step copied back to the host
+    e_steps = min(8, args.tp_steps)
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    ids = eng.decode_greedy(e_steps)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = replicas.max_over_ranks(e0.elapsed_time(e1))
+    C, L, H = shape.n_embd, shape.n_layer, shape.n_head
+    state = L * (2 * C + H * 64 * 64) * 4
+    emb_row = C + (C // 128) * 8
+    weights = shape.weights_per_token() * 1.0625  # SG8 g128, embedding row excluded
+    step_bytes = int(weights + nb * (2 * state + emb_row))
+    peak, peak_kind = _peaks()
+    achieved = step_bytes / (ms_step / 1e3) / 1e9
+    launches = eng.launches_per_step
+    eng.close()
+    return {"metric": f"RWKV-7 {args.tp_config} U8 decode tok/s (bs{nb}, tensor-parallel x{world})",
+            "value": nb / (ms_step / 1e3), "unit": "tok/s", "n_gpus": world, "sessions": nb, "scaling": "strong",
+            "steps": args.tp_steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "gpu_launches": launches * args.tp_steps,
+            "collectives_per_step": (2 * L + 1) if world > 1 else 0,
+            "allreduce_bytes": nb * C * 4 if world > 1 else 0,
+            "parallelism": f"tp{world}" if world > 1 else "single GPU (unsplit)",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
+                         "frac": achieved / (peak * world), "traffic": None, "algorithmic_bytes_per_step": step_bytes,
+                         "what": f"weights once over all ranks + {nb} sessions' state read and written per step; "
+                                 f"peak: {world} x {peak_kind} HBM copy bandwidth"},
+            "e2e": {"value": e_steps * nb / (e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 4 * nb, "steps": e_steps,
+                    "how": "decode_greedy: ids of every step copied to the host"},
+            "ids_checksum": int(ids.astype("int64").sum()), "bytes_per_token_unsplit": bpt_local}
+
+
 def synth_prompt(n: int, vocab: int, seed: int) -> list[int]:
     from rwkv_b200 import synth
 
@@ -360,6 +442,10 @@ def main() -> None:
     ap.add_argument("--batch-steps", type=int, default=64)
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill leg: tokens per session (0: skip)")
     ap.add_argument("--prefill-sessions", type=int, default=8)
+    ap.add_argument("--tp-config", default="7.2b", choices=["tiny", "7.2b", "7.2b-l4", "2.9b"],
+                    help="tensor-parallel leg: model split over all ranks")
+    ap.add_argument("--tp-sessions", type=int, default=8, help="tensor-parallel leg sessions (0: skip the leg)")
+    ap.add_argument("--tp-steps", type=int, default=32)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -465,6 +551,7 @@ def main() -> None:
 
     batched = run_batched(batch_eng, args, shape, bpt, dev, stream, world, rank) if batch_eng is not None else None
     prefill = run_prefill(prefill_eng, args, shape, bpt, dev, stream, world, rank) if prefill_eng is not None else None
+    tpres = run_tp(args, dev, stream, world, rank) if args.tp_sessions > 0 else None
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -507,6 +594,8 @@ def main() -> None:
             res["batched"] = batched
         if prefill is not None:
             res["prefill"] = prefill
+        if tpres is not None:
+            res["tp"] = tpres
         if cpu_pack is not None:
             backend.close()
             res["cpu_baseline"] = cpu_baseline(cpu_pack, shape, args)

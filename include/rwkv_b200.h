@@ -298,6 +298,12 @@ typedef struct rwkvb_tp_desc {
 } rwkvb_tp_desc;
 int rwkvb_batch_create_tp(const rwkvb_model_desc* local, int32_t batch, const rwkvb_tp_desc* tp, uint32_t flags,
                           rwkvb_batch** out);
+/* Record the token step as a CUDA graph now (once; a no-op without graphs),
+ * instead of at the first step.  Nothing runs.  Under tensor parallelism every
+ * rank calls it and the ranks agree that all captures succeeded before any
+ * rank launches a step: a graph holding collectives must never run on some
+ * ranks only. */
+int rwkvb_batch_prepare(rwkvb_batch* e, void* stream);
 int rwkvb_batch_destroy(rwkvb_batch* e);
 
 /* Device state, per layer l and session b (each block as in rwkvb_engine_buffers):

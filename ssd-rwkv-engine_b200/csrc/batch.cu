@@ -1384,27 +1384,34 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
   return RWKVB_OK;
 }
 
-int bt_run_step(rwkvb_batch* e, cudaStream_t s) {
-  if (e->use_graph && !e->exec) {
-    cudaStream_t cs = nullptr;
-    if (cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking) != cudaSuccess) return RWKVB_ECUDA;
-    cudaGraph_t g = nullptr;
-    int st = cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-    if (st == RWKVB_OK) {
-      st = bt_record_step(e, cs);
-      const cudaError_t ce = cudaStreamEndCapture(cs, &g);
-      if (st == RWKVB_OK) st = cuda_status(ce);
-    }
-    if (st == RWKVB_OK) st = cuda_status(cudaGraphInstantiate(&e->exec, g, 0));
-    if (g) cudaGraphDestroy(g);
-    cudaStreamDestroy(cs);
-    if (st != RWKVB_OK) {
-      e->exec = nullptr;
-      return st;
-    }
+// Capture the step into e->exec (once).  Under tensor parallelism the host
+// collective callback is called during the capture, on the capture stream.
+int bt_capture_step(rwkvb_batch* e) {
+  if (e->exec) return RWKVB_OK;
+  cudaStream_t cs = nullptr;
+  if (cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking) != cudaSuccess) return RWKVB_ECUDA;
+  cudaGraph_t g = nullptr;
+  int st = cuda_status(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  if (st == RWKVB_OK) {
+    st = bt_record_step(e, cs);
+    const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+    if (st == RWKVB_OK) st = cuda_status(ce);
   }
-  if (e->use_graph) return cuda_status(cudaGraphLaunch(e->exec, s));
-  return bt_record_step(e, s);
+  if (st == RWKVB_OK) st = cuda_status(cudaGraphInstantiate(&e->exec, g, 0));
+  if (g) cudaGraphDestroy(g);
+  cudaStreamDestroy(cs);
+  if (st != RWKVB_OK) {
+    cudaGetLastError();
+    e->exec = nullptr;
+  }
+  return st;
+}
+
+int bt_run_step(rwkvb_batch* e, cudaStream_t s) {
+  if (!e->use_graph) return bt_record_step(e, s);
+  const int st = bt_capture_step(e);
+  if (st != RWKVB_OK) return st;
+  return cuda_status(cudaGraphLaunch(e->exec, s));
 }
 
 int bt_check_err(rwkvb_batch* e, cudaStream_t s) {
@@ -1963,6 +1970,12 @@ extern "C" int rwkvb_batch_create_tp(const rwkvb_model_desc* local, int32_t batc
                                      uint32_t flags, rwkvb_batch** out) {
   if (!tp) return RWKVB_EARG;
   return bt_create(local, batch, flags, tp, out);
+}
+
+extern "C" int rwkvb_batch_prepare(rwkvb_batch* e, void* stream) {
+  (void)stream;
+  if (!e) return RWKVB_EARG;
+  return e->use_graph ? bt_capture_step(e) : RWKVB_OK;
 }
 
 extern "C" int rwkvb_batch_destroy(rwkvb_batch* e) {

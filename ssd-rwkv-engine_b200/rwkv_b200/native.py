@@ -127,6 +127,7 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_engine_trace": (ctypes.c_int, [vp, P(u64), i32, P(i32)]),
         "rwkvb_batch_create": (ctypes.c_int, [P(ModelDesc), i32, u32, P(vp)]),
         "rwkvb_batch_create_tp": (ctypes.c_int, [P(ModelDesc), i32, P(TPDesc), u32, P(vp)]),
+        "rwkvb_batch_prepare": (ctypes.c_int, [vp, vp]),
         "rwkvb_batch_destroy": (ctypes.c_int, [vp]),
         "rwkvb_batch_buffers": (ctypes.c_int, [vp, P(vp), P(vp), P(vp), P(vp)]),
         "rwkvb_batch_reset": (ctypes.c_int, [vp, vp]),

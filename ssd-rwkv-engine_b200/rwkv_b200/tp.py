@@ -226,6 +226,12 @@ class TPCollective:
         dist.all_reduce(t, group=self.group)
         torch.cuda.synchronize(self.device)
 
+    def agree(self, ok: bool) -> bool:
+        """True on every rank when ``ok`` holds on every rank (eager, on the host's order)."""
+        t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(int(t.item()))
+
     def run(self, kind: int, send: torch.Tensor, recv: torch.Tensor) -> None:
         if kind == native.COLLECTIVE_ALLREDUCE_SUM_F32:
             if send.data_ptr() != recv.data_ptr():
@@ -311,6 +317,20 @@ class B200TPBatchEngine:
                                                         ctypes.byref(desc), flags, ctypes.byref(h)),
                          "rwkvb_batch_create_tp")
             self._h = h
+            self.use_graph = bool(use_graph)
+            if self.use_graph:
+                # capture the step (collectives included) on every rank, then
+                # agree that all captures succeeded before any rank launches one
+                st = self.lib.rwkvb_batch_prepare(h, self._stream())
+                err, self._coll.error = self._coll.error, None
+                ok = self._coll.agree(st == native.RWKVB_OK and err is None)
+                if not ok:
+                    self.lib.rwkvb_batch_destroy(h)
+                    self._h = None
+                    if err is not None:
+                        raise RuntimeError("capturing the tensor-parallel step failed") from err
+                    native.check(st if st != native.RWKVB_OK else native.RWKVB_ECUDA,
+                                 "rwkvb_batch_prepare (on some rank)")
             att, wkv, ffn, logits = (ctypes.c_void_p() for _ in range(4))
             native.check(self.lib.rwkvb_batch_buffers(h, ctypes.byref(att), ctypes.byref(wkv), ctypes.byref(ffn),
                                                       ctypes.byref(logits)), "rwkvb_batch_buffers")
