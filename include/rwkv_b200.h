@@ -204,7 +204,10 @@ typedef struct rwkvb_engine rwkvb_engine;
  *        bit1 = no programmatic dependent launch between phase kernels;
  *        bit2 = no persistent kernel (always use the multi-kernel step);
  *        bit3 = record persistent-kernel phase timestamps (rwkvb_engine_trace);
- *        bit8 = bits 4..7 give an explicit L2-prefetch distance in phases.
+ *        bit8 = bits 4..7 give an explicit L2-prefetch distance in phases;
+ *        bit9 = load the persistent kernel's weight stream without the L2
+ *               evict-first policy (default: weights evict first, so the
+ *               state and activations re-read every layer stay in L2). 
  * When every projection is SG8 with one power-of-two group size and the
  * 16-byte layout that rwkvb upload placement gives, decode runs as ONE
  * cooperative persistent launch per call (all tokens, all layers); otherwise

@@ -197,7 +197,8 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
         if (lane == 0) {
           uint8_t* sa = smem + slot * stage_bytes;
           mbar_expect_tx(&full[slot], bytes);
-          tma_load_2d(sa, &a.amap[sg.m], st * 128, sg.t * 128, &full[slot]);
+          // weight codes are read once per step: evict first, keep the digit rows and per-row constants in L2
+          tma_load_2d_hint(sa, &a.amap[sg.m], st * 128, sg.t * 128, &full[slot], l2_evict_first());
           tma_load_2d(sa + kBgTileBytes, &a.bmap[M.digits], st * 128, 0, &full[slot]);
         }
         __syncwarp();
@@ -358,17 +359,23 @@ __device__ __forceinline__ void bg_emit_group(const float (&v)[4], int per, uint
   int e = 0;
   if (m > 0.f) frexpf(m, &e);  // |x| 2^-e < 1
   const float inv = ldexpf(127.0f, -e);
+  // rintf by the 1.5 * 2^23 shift (ties to even, |y| <= 127): the low byte of
+  // the sum's bits is the integer's two's-complement byte; no float->int
+  // conversion.  Stored digits are offset by 127 (u8).
+  constexpr float kShift = 12582912.0f;
   uint32_t w0 = 0, w1 = 0, w2 = 0;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     const float y0 = v[u] * inv;
-    const float x0 = rintf(y0);
+    const float s0 = __fadd_rn(y0, kShift);
+    const float x0 = __fsub_rn(s0, kShift);
     const float y1 = (y0 - x0) * 254.0f;
-    const float x1 = rintf(y1);
-    const float x2 = rintf((y1 - x1) * 254.0f);
-    w0 |= (uint32_t)((int)x0 + 127) << (8 * u);
-    w1 |= (uint32_t)((int)x1 + 127) << (8 * u);
-    w2 |= (uint32_t)((int)x2 + 127) << (8 * u);
+    const float s1 = __fadd_rn(y1, kShift);
+    const float x1 = __fsub_rn(s1, kShift);
+    const float s2 = __fadd_rn((y1 - x1) * 254.0f, kShift);
+    w0 |= ((__float_as_uint(s0) + 127u) & 0xffu) << (8 * u);
+    w1 |= ((__float_as_uint(s1) + 127u) & 0xffu) << (8 * u);
+    w2 |= ((__float_as_uint(s2) + 127u) & 0xffu) << (8 * u);
   }
   if (per == 4) {
     *reinterpret_cast<uint32_t*>(dig + (size_t)b * k + col) = w0;

@@ -54,6 +54,7 @@ constexpr int kDBar = 1;               // named barrier of the consumers
 constexpr int kDMaxItems = 8;          // adapter first-stage items per CTA
 constexpr int kDMaxPieces = 8;         // adapter second-stage tile pieces per layer
 constexpr int kDMisc = 2560;           // misc shared floats
+static_assert(kDW * 4 * 64 <= kDMisc, "phase-B adapter partials [warps][4][64] live in misc");
 constexpr float kFix = 4294967296.0f;  // 2^32 fixed-point scale of adapter partials
 constexpr float kUnfix = 1.0f / 4294967296.0f;
 
@@ -104,6 +105,7 @@ struct DArgs {
   unsigned* gbar;
   uint32_t spin_limit;
   int emb_fast;
+  int l2_first;  // weight stream loaded with the L2 evict-first policy
   unsigned long long* trace;
   int trace_cap;
   uint32_t o_dig, o_x, o_xb, o_t, o_p, o_part, o_misc, smem_total;
@@ -238,6 +240,8 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
   unsigned long long* tr = (a.trace && blockIdx.x == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
   const int tr_n = 2 * a.trace_cap;
   int seq = seq_io;
+  const bool hint = a.l2_first != 0;
+  const uint64_t pol = l2_evict_first();
   int tile = u0 / nch, chunk = u0 - tile * nch;
   int mi = per_map ? tile / per_map : 0, row0 = (tile - mi * per_map) * 16;
   bool ok = true;
@@ -261,8 +265,13 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     }
     uint8_t* dst = ring + (size_t)slot * slot_b;
     mbar_expect_tx(&full[slot], bytes);
-    tma_load_3d(dst, q + mi, 0, row0, chunk * nb, &full[slot]);
-    tma_load_2d(dst + code_b, p + mi, chunk * pr8, row0, &full[slot]);
+    if (hint) {
+      tma_load_3d_hint(dst, q + mi, 0, row0, chunk * nb, &full[slot], pol);
+      tma_load_2d_hint(dst + code_b, p + mi, chunk * pr8, row0, &full[slot], pol);
+    } else {
+      tma_load_3d(dst, q + mi, 0, row0, chunk * nb, &full[slot]);
+      tma_load_2d(dst + code_b, p + mi, chunk * pr8, row0, &full[slot]);
+    }
     if (tr && 3 * seq + 2 < tr_n) tr[3 * seq] = global_ns();
     ++seq;
     if (++chunk == nch) {
@@ -286,6 +295,8 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
 __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint64_t* full, uint64_t* empty,
                            volatile int* abort_flag) {
   int seq = 0;
+  const bool hint = a.l2_first != 0;
+  const uint64_t pol = l2_evict_first(), keep = l2_evict_last();
   auto acquire = [&]() -> int { return d_acquire(a, empty, abort_flag, seq); };
   auto issued = [&]() { d_issued(a, seq); };
   auto layer_start = [&](int l) {
@@ -330,8 +341,13 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
           if (ok) {
             uint8_t* dst = ring + (size_t)slot * a.slot;
             mbar_expect_tx(&full[slot], qb + sb);
-            bulk_g2s(dst, W.payload + (size_t)i0 * R, qb, &full[slot]);
-            bulk_g2s(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, &full[slot]);
+            if (hint) {
+              bulk_g2s_hint(dst, W.payload + (size_t)i0 * R, qb, &full[slot], pol);
+              bulk_g2s_hint(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, &full[slot], pol);
+            } else {
+              bulk_g2s(dst, W.payload + (size_t)i0 * R, qb, &full[slot]);
+              bulk_g2s(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, &full[slot]);
+            }
             issued();
           }
         }
@@ -342,8 +358,14 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
           if (ok) {
             uint8_t* dst = ring + (size_t)slot * a.slot;
             mbar_expect_tx(&full[slot], (uint32_t)br * 80u);
-            tma_load_2d(dst, &M.aq[m], bx * 64, T.pr0[k], &full[slot]);
-            tma_load_2d(dst + br * 64, &M.ap[m], (((bx * 64) >> a.alg[m]) & ~1) * 8, T.pr0[k], &full[slot]);
+            const int px = (((bx * 64) >> a.alg[m]) & ~1) * 8;
+            if (hint) {  // phase B waits on these: keep them in L2 across tokens
+              tma_load_2d_hint(dst, &M.aq[m], bx * 64, T.pr0[k], &full[slot], keep);
+              tma_load_2d_hint(dst + br * 64, &M.ap[m], px, T.pr0[k], &full[slot], keep);
+            } else {
+              tma_load_2d(dst, &M.aq[m], bx * 64, T.pr0[k], &full[slot]);
+              tma_load_2d(dst + br * 64, &M.ap[m], px, T.pr0[k], &full[slot]);
+            }
             issued();
           }
         }
@@ -480,22 +502,24 @@ struct DSrc {
 template <int LFK>
 __device__ __noinline__ void d_build(const DSrc& src, int K, uint8_t* base) {
   const DSrc S = src;
-  build_digits(
-      K, LFK,
-      [&](int i) -> float4 {
-        if (S.kind == 0) {
-          const float4 z = *reinterpret_cast<const float4*>(S.z + i), p = *reinterpret_cast<const float4*>(S.p + i);
-          const float4 m = ldg4(S.g + i);
-          return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
-                             z.w + (p.w - z.w) * m.w);
-        }
-        if (S.kind == 1) return *reinterpret_cast<const float4*>(S.z + i);
-        const float4 v = ldcg4(S.g + i);
-        if (S.kind == 2) return v;
-        return make_float4(v.x > 0.f ? v.x * v.x : 0.f, v.y > 0.f ? v.y * v.y : 0.f, v.z > 0.f ? v.z * v.z : 0.f,
-                           v.w > 0.f ? v.w * v.w : 0.f);
-      },
-      d_digits_at(base, K, LFK), threadIdx.x, kDT, kDBar);
+  auto get4 = [&](int i) -> float4 {
+    if (S.kind == 0) {
+      const float4 z = *reinterpret_cast<const float4*>(S.z + i), p = *reinterpret_cast<const float4*>(S.p + i);
+      const float4 m = ldg4(S.g + i);
+      return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z,
+                         z.w + (p.w - z.w) * m.w);
+    }
+    if (S.kind == 1) return *reinterpret_cast<const float4*>(S.z + i);
+    const float4 v = ldcg4(S.g + i);
+    if (S.kind == 2) return v;
+    return make_float4(v.x > 0.f ? v.x * v.x : 0.f, v.y > 0.f ? v.y * v.y : 0.f, v.z > 0.f ? v.z * v.z : 0.f,
+                       v.w > 0.f ? v.w * v.w : 0.f);
+  };
+  // up to 4 items per thread (K <= 10240): all loads in flight at once
+  if (K <= 32 * kDT)
+    build_digits_r1<4>(K, LFK, get4, d_digits_at(base, K, LFK), threadIdx.x, kDT, kDBar);
+  else
+    build_digits(K, LFK, get4, d_digits_at(base, K, LFK), threadIdx.x, kDT, kDBar);
 }
 
 __device__ __forceinline__ void ld8(float (&v)[8], const float* p) {
@@ -788,13 +812,16 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
     lw = __ldg(Ly.lnx_w + ch);
     lb = __ldg(Ly.lnx_b + ch);
   }
-  float* vp = misc;  // [5][4][64] per-thread partials
+  float* vp = misc;  // [10 warps][4 matrices][64 columns] partials
   #pragma unroll 1
-  for (int i = t; i < 5 * 256; i += kDT) vp[i] = 0.f;
+  for (int i = t; i < kDW * 256; i += kDT) vp[i] = 0.f;
   cp_async_wait_all();
   d_csync();
   {
-    const int cc = t & 63, q = t >> 6;  // 5 row phases x 64 columns
+    // 16 lanes per tile row, 4 columns each (one 32-bit code word); the two
+    // half-warps take alternate rows: row phase rp of 20.  Per row the scale
+    // is folded into the input: mid * (q * d + mn) = (mid * d) * q + mid * mn.
+    const int lane = t & 31, w = t >> 5, cg = lane & 15, rp = w * 2 + (lane >> 4);
     for (int pc = 0; pc < T.npc[l == 0 ? 0 : 1]; ++pc) {
       const uint8_t* sl = d_slot_wait(a, c);
       if (!c.dead) {
@@ -803,12 +830,35 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
         const float2* pairs = reinterpret_cast<const float2*>(sl + br * 64);
         const int sel = ((h * 64) >> a.alg[m]) & 1;
         const float* mm = mid + d_rank_off(a.d, m) + r0;
-        float acc = 0.f;
-        for (int i = q; i < nr; i += 5) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, bs = 0.f;
+        #pragma unroll 4
+        for (int i = rp; i < nr; i += 2 * kDW) {
           const float2 pq = pairs[i * 2 + sel];
-          acc = fmaf(mm[i], sg8_dequant(sl[i * 64 + cc], pq.x, pq.y), acc);
+          const float am = mm[i];
+          const float ad = am * __fmul_rn(__fsub_rn(pq.y, pq.x), kInv255);
+          bs = fmaf(am, pq.x, bs);
+          const uint32_t q4 = *reinterpret_cast<const uint32_t*>(sl + i * 64 + 4 * cg);
+          // code byte k as a float: bits 0x4B0000qq = 2^23 + q, minus 2^23 (exact)
+          a0 = fmaf(ad, __uint_as_float(__byte_perm(q4, 0x4B000000u, 0x7440)) - 8388608.0f, a0);
+          a1 = fmaf(ad, __uint_as_float(__byte_perm(q4, 0x4B000000u, 0x7441)) - 8388608.0f, a1);
+          a2 = fmaf(ad, __uint_as_float(__byte_perm(q4, 0x4B000000u, 0x7442)) - 8388608.0f, a2);
+          a3 = fmaf(ad, __uint_as_float(__byte_perm(q4, 0x4B000000u, 0x7443)) - 8388608.0f, a3);
         }
-        vp[(q * 4 + m) * 64 + cc] += acc;
+        // lanes l and l ^ 16 hold the same columns (alternate rows)
+        a0 += __shfl_xor_sync(0xffffffffu, a0, 16);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, 16);
+        a2 += __shfl_xor_sync(0xffffffffu, a2, 16);
+        a3 += __shfl_xor_sync(0xffffffffu, a3, 16);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 16);
+        if (lane < 16) {
+          float4* dst = reinterpret_cast<float4*>(vp + (w * 4 + m) * 64 + 4 * cg);
+          float4 v4 = *dst;
+          v4.x += a0 + bs;
+          v4.y += a1 + bs;
+          v4.z += a2 + bs;
+          v4.w += a3 + bs;
+          *dst = v4;
+        }
       }
       d_slot_release(a, c);
     }
@@ -818,7 +868,7 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
     const int m = t >> 6, cc = t & 63;
     float s = 0.f;
     if (m < nm)
-      for (int q = 0; q < 5; ++q) s += vp[(q * 4 + m) * 64 + cc];
+      for (int q = 0; q < kDW; ++q) s += vp[(q * 4 + m) * 64 + cc];
     vec[m * 64 + cc] = s;
   }
   d_csync();

@@ -981,6 +981,7 @@ bool plan_decode(rwkvb_engine* e) {
   a.b = e->b;
   a.d = d;
   a.spin_limit = 1u << 22;
+  a.l2_first = (e->flags & 0x200u) ? 0 : 1;  // bit 9: plain weight-stream loads (no L2 policy)
   const PackedView& E = e->emb;
   a.emb_fast = E.kind == RWKVB_KIND_SG8 && E.lg >= 4 && d.C % (int)E.group == 0 && ((d.C >> E.lg) % 2) == 0 &&
                aligned16(E.payload) && aligned16(E.meta);

@@ -83,22 +83,34 @@ __device__ __forceinline__ void emit_digits(const float (&v)[8], int it, bool ac
     X.xc[it >> (lfk + 2)] = ldexpf(1.0f, e) / 127.0f;
     X.xsum[it >> (lfk + 2)] = sum;
   }
-  int d0[8], d1[8], d2[8];
+  // Rounding by the 1.5 * 2^23 shift: for |y| < 2^22, (y + 1.5 * 2^23) rounds y
+  // to the nearest integer, ties to even (the rintf rule), into the low
+  // mantissa bits, so the low byte of the sum's bit pattern is the digit's
+  // two's-complement byte and subtracting the shift gives rintf(y) exactly.
+  // |y0| <= 127 and |y1|, |y2| <= 127 here.  No float->int conversion.
+  constexpr float kShift = 12582912.0f;
+  uint32_t b0[8], b1[8], b2[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
     const float y0 = v[u] * inv;
-    const float x0 = rintf(y0);
+    const float s0 = __fadd_rn(y0, kShift);
+    const float x0 = __fsub_rn(s0, kShift);
     const float y1 = (y0 - x0) * 254.0f;
-    const float x1 = rintf(y1);
-    const float x2 = rintf((y1 - x1) * 254.0f);
-    d0[u] = (int)x0;
-    d1[u] = (int)x1;
-    d2[u] = (int)x2;
+    const float s1 = __fadd_rn(y1, kShift);
+    const float x1 = __fsub_rn(s1, kShift);
+    const float s2 = __fadd_rn((y1 - x1) * 254.0f, kShift);
+    b0[u] = __float_as_uint(s0);
+    b1[u] = __float_as_uint(s1);
+    b2[u] = __float_as_uint(s2);
   }
+  // byte 0 of each word, four words per 32-bit result
+  auto pk = [](const uint32_t* w) {
+    return __byte_perm(__byte_perm(w[0], w[1], 0x0040), __byte_perm(w[2], w[3], 0x0040), 0x5410);
+  };
   const int s = it >> 2, t = it & 3;
-  X.xd[s * 12 + t] = make_uint2(pack_s8x4(d0[0], d0[1], d0[2], d0[3]), pack_s8x4(d0[4], d0[5], d0[6], d0[7]));
-  X.xd[s * 12 + 4 + t] = make_uint2(pack_s8x4(d1[0], d1[1], d1[2], d1[3]), pack_s8x4(d1[4], d1[5], d1[6], d1[7]));
-  X.xd[s * 12 + 8 + t] = make_uint2(pack_s8x4(d2[0], d2[1], d2[2], d2[3]), pack_s8x4(d2[4], d2[5], d2[6], d2[7]));
+  X.xd[s * 12 + t] = make_uint2(pk(b0), pk(b0 + 4));
+  X.xd[s * 12 + 4 + t] = make_uint2(pk(b1), pk(b1 + 4));
+  X.xd[s * 12 + 8 + t] = make_uint2(pk(b2), pk(b2 + 4));
 }
 
 // Build the digit form of x[0..K): item it = (k-step it / 4, quarter it % 4)
@@ -126,6 +138,34 @@ __device__ __forceinline__ void build_digits(int K, int lfk, Get4 get4, XDigits 
       nb = get4(nx * 8 + 4);
     }
     emit_digits(v, it, it < items, lfk, X);
+  }
+  bar_sync(bar_id, nthreads);
+}
+
+// build_digits with every round's operands loaded before the first emit
+// (K <= 8 * MAXR * nthreads): one memory round trip for the whole vector
+// instead of one per round of `nthreads` items.
+template <int MAXR, typename Get4>
+__device__ __forceinline__ void build_digits_r1(int K, int lfk, Get4 get4, XDigits X, int ct, int nthreads,
+                                                int bar_id) {
+  const int items = K >> 3;
+  float4 va[MAXR], vb[MAXR];
+#pragma unroll
+  for (int r = 0; r < MAXR; ++r) {
+    const int it = r * nthreads + ct;
+    va[r] = vb[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (it < items) {
+      va[r] = get4(it * 8);
+      vb[r] = get4(it * 8 + 4);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < MAXR; ++r) {
+    if (r * nthreads < items) {  // uniform: every lane of the warp emits together
+      const int it = r * nthreads + ct;
+      const float v[8] = {va[r].x, va[r].y, va[r].z, va[r].w, vb[r].x, vb[r].y, vb[r].z, vb[r].w};
+      emit_digits(v, it, it < items, lfk, X);
+    }
   }
   bar_sync(bar_id, nthreads);
 }

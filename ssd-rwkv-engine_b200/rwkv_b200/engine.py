@@ -115,7 +115,8 @@ class B200Engine:
     device (shared with a ``B200BatchEngine``)."""
 
     def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
-                 prefetch_distance: int | None = None, persistent: bool = True, trace: bool = False):
+                 prefetch_distance: int | None = None, persistent: bool = True, trace: bool = False,
+                 l2_policy: bool = True):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
@@ -129,6 +130,8 @@ class B200Engine:
                 flags |= native.FLAG_NO_PERSISTENT
             if trace:
                 flags |= native.FLAG_TRACE
+            if not l2_policy:
+                flags |= native.FLAG_NO_L2_POLICY
             if prefetch_distance is not None:
                 flags |= native.FLAG_EXPLICIT_PREFETCH | ((int(prefetch_distance) & 0xF) << 4)
             h = ctypes.c_void_p()

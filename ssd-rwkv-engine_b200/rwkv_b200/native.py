@@ -39,6 +39,7 @@ FLAG_NO_PDL = 0x2
 FLAG_NO_PERSISTENT = 0x4
 FLAG_TRACE = 0x8
 FLAG_EXPLICIT_PREFETCH = 0x100
+FLAG_NO_L2_POLICY = 0x200
 
 
 class RwkvbError(RuntimeError):
