@@ -306,12 +306,13 @@ constexpr int kBtAdpKc = 128;   // first-stage input rows per CTA
 
 struct BtPieces {
   int stage0, G, total, ncta;
+  const int* np;  // device: pieces of each 128-row tile (precomputed at plan time)
 };
 
-__device__ __forceinline__ int bt_npieces(const BtPieces& p, int n) {
-  const long long f = p.stage0 + (long long)(n >> 7) * p.G;
-  return bg_cta_of(f + p.G - 1, p.total, p.ncta) - bg_cta_of(f, p.total, p.ncta) + 1;
-}
+// Pieces of output row n's tile: one cached load (the CTA split of a tile's
+// stages is fixed by the launch plan, so it is tabulated once per engine
+// instead of two 64-bit divisions per element).
+__device__ __forceinline__ int bt_npieces(const BtPieces& p, int n) { return __ldg(p.np + (n >> 7)); }
 
 // Sum of the pieces of element (b, n) of a GEMM output [pieces][nb][rows], in
 // piece order; the loads are independent and issued together.
@@ -556,13 +557,42 @@ __global__ void bt_adpr_kernel(float* midT, const float* part, int splits, int n
 }
 
 // ------------------------------------------------ adapter second stages
-// out[m][b][c] = sum_r mid[b][off_m + r] W2_m[r][c], 64 columns per CTA.
+// Each adapter's rows are cut into chunks of at most kBtAdpChunkRows rows (the
+// 320-row g2 of 2.9B into four), so every CTA does about the same work; chunk
+// k writes out[slot_k][b][c] = sum over its rows r of mid[b][off_m + r] W2_m[r][c]
+// (64 columns per CTA).  The first chunk of adapter m writes slot m, later
+// chunks slots 4, 5, ...; a reader sums an adapter's slots in row order
+// (bt_adp_at), so the result does not depend on scheduling.
+constexpr int kBtAdpChunkRows = 96;
+constexpr int kBtMaxChunks = 24;
+
+struct BtAdpSlots {
+  int n[4];     // chunks of adapter m
+  int s[4][8];  // their output slots, in row order
+};
+
+struct BtAdpPlan {
+  int n = 0, n_l0 = 0;  // chunks of a layer; of layer 0 (no v2: the v chunks come last)
+  int m[kBtMaxChunks], r0[kBtMaxChunks], r1[kBtMaxChunks], slot[kBtMaxChunks];
+  int slots = 4;        // output slots
+  BtAdpSlots q;
+};
+
+// Adapter m's second-stage value at (row, ch): its chunk slots summed in order.
+__device__ __forceinline__ float bt_adp_at(const float* adp2, const BtAdpSlots& q, int m, int rows, int row, int C,
+                                           int ch) {
+  float v = adp2[((size_t)q.s[m][0] * rows + row) * C + ch];
+  for (int k = 1; k < q.n[m]; ++k) v += adp2[((size_t)q.s[m][k] * rows + row) * C + ch];
+  return v;
+}
+
 struct BtAdp2Args {
   PackedView w[4];  // w2, a2, g2, v2: [R_m][C]
   int R[4], off[4];
   int fast[4];      // SG8, group >= 64, 16-byte aligned codes: vector tile loads
+  int ck_m[kBtMaxChunks], ck_r0[kBtMaxChunks], ck_r1[kBtMaxChunks], ck_slot[kBtMaxChunks];
   const float* midT; // [rtot][64]
-  float* out;       // [4][nb][C]
+  float* out;       // [slots][nb][C]
   int C, nb, rtot;
 };
 
@@ -570,15 +600,15 @@ constexpr int kBtAdp2Rc = 128;  // second-stage rows staged per round
 
 __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
   extern __shared__ __align__(16) float bt_sm[];
-  const int m = blockIdx.y, c0 = blockIdx.x * 64, t = threadIdx.x;
-  const int R = a.R[m];
+  const int ck = blockIdx.y, m = a.ck_m[ck], c0 = blockIdx.x * 64, t = threadIdx.x;
+  const int R0 = a.ck_r0[ck], R1 = a.ck_r1[ck];
   const PackedView& W = a.w[m];
   float* ms = bt_sm;                  // [rc][64 sessions]
   float* ws = ms + kBtAdp2Rc * 64;    // [rc][64 columns]
   const int bq = t & 15, cq = t >> 4;
   float acc[4][4] = {};
-  for (int r0 = 0; r0 < R; r0 += kBtAdp2Rc) {
-    const int rc = min(kBtAdp2Rc, R - r0);
+  for (int r0 = R0; r0 < R1; r0 += kBtAdp2Rc) {
+    const int rc = min(kBtAdp2Rc, R1 - r0);
     __syncthreads();
     for (int idx = t; idx < rc * 16; idx += blockDim.x)
       reinterpret_cast<float4*>(ms)[idx] =
@@ -615,7 +645,7 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
   for (int u = 0; u < 4; ++u) {
     const int b = 4 * bq + u;
     if (b >= a.nb) continue;
-    *reinterpret_cast<float4*>(a.out + ((size_t)m * a.nb + b) * a.C + c0 + 4 * cq) =
+    *reinterpret_cast<float4*>(a.out + ((size_t)a.ck_slot[ck] * a.nb + b) * a.C + c0 + 4 * cq) =
         make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
   }
 }
@@ -624,7 +654,8 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
 struct BtWkvArgs {
   const float* part[3];  // r, k, v GEMM pieces [pieces][nb][C]
   BtPieces pp[3];
-  const float* adp2;     // [4][nb][C]: w, a, g, v second stages (pre-activation)
+  const float* adp2;     // [slots][nb][C]: w, a, g, v second-stage chunks (pre-activation)
+  BtAdpSlots q;
   float* wkv;            // this layer's state [nb][H][64][64]
   float* vfirst;         // [nb][C]
   float* att_y;          // [nb][C]
@@ -655,83 +686,160 @@ __device__ __forceinline__ float bt_sum64(float v, float* red, int j) {
   return r;
 }
 
-__global__ void __launch_bounds__(kBtThreads, 2) bt_wkv_kernel(BtWkvArgs a) {
-  __shared__ float red[2 * kBtWkvSess];
-  __shared__ __align__(16) float vecs[kBtWkvSess][5][64];  // decay, -kk, kk*a, k, r
-  const int h = blockIdx.x, t = threadIdx.x, j = t >> 6, i = t & 63;
-  const int b = blockIdx.y * kBtWkvSess + j;
-  if (b >= a.nb) return;  // whole 64-thread group: it owns its named barrier
-  const int C = a.C, ch = h * 64 + i;
-  // state row i of (session b, head h), loaded first
-  float4* Srow = reinterpret_cast<float4*>(a.wkv + ((size_t)b * a.H + h) * 4096 + (size_t)i * 64);
-  float4 s4[16];
+// Sum over the 64 channel threads (warps 0 and 1) of a 256-thread CTA; every
+// thread of the CTA must call it (it contains __syncthreads).
+__device__ __forceinline__ float bt_csum64(float v, float* red) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0 && w < 2) red[w] = v;
+  __syncthreads();
+  const float r = red[0] + red[1];
+  __syncthreads();
+  return r;
+}
+
+// Sum over the 16 lanes (a half-warp) that hold one state row.
+__device__ __forceinline__ float bt_sum16(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  return v;
+}
+
+// Inputs of channel ch of one (session b, head): what threads 0..63 need
+// before the state update (loaded one pair ahead, see bt_wkv_kernel).
+struct BtWkvChan {
+  float wv, av, gv, vg, vf, r, k, v;
+};
+
+__device__ __forceinline__ BtWkvChan bt_wkv_chan(const BtWkvArgs& a, int b, int ch) {
+  BtWkvChan c;
+  const int C = a.C;
+  c.wv = bt_adp_at(a.adp2, a.q, 0, a.nb, b, C, ch);
+  c.av = bt_adp_at(a.adp2, a.q, 1, a.nb, b, C, ch);
+  c.gv = bt_adp_at(a.adp2, a.q, 2, a.nb, b, C, ch);
+  c.vg = a.layer0 ? 0.f : bt_adp_at(a.adp2, a.q, 3, a.nb, b, C, ch);
+  c.vf = a.layer0 ? 0.f : a.vfirst[(size_t)b * C + ch];
+  c.r = bt_fold(a.part[0], a.pp[0], a.nb, C, b, ch);
+  c.k = bt_fold(a.part[1], a.pp[1], a.nb, C, b, ch);
+  c.v = bt_fold(a.part[2], a.pp[2], a.nb, C, b, ch);
+  return c;
+}
+
+constexpr int kBtWkvCtasPerSm = 4;
+
+// Persistent over (session, head) pairs, 256 threads per CTA, kBtWkvCtasPerSm
+// CTAs per SM.  The state of the next pair (16 KB) is copied into the other
+// shared-memory stage with cp.async while this pair is computed, and threads
+// 0..63 load the next pair's channel inputs into registers, so every SM keeps
+// ~128 KB of state reads in flight.  Stage layout = state layout: thread t
+// works on float4 f = t + 256 u (u < 4), i.e. rows (t >> 4) + 16 u, columns
+// 4 (t & 15) .. + 3; a row's dot products are summed over its 16 lanes; the
+// new state is stored straight to global memory (512 contiguous bytes per
+// warp instruction).
+__global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtWkvArgs a) {
+  extern __shared__ __align__(16) float4 bt_stage[];  // [2][1024]
+  __shared__ float red[2];
+  __shared__ __align__(16) float vd[64], vkk[64], vka[64], vk[64], vr[64], vv[64], sy[64];
+  const int t = threadIdx.x, i = t & 63;
+  const bool chan = t < 64;
+  const int npairs = a.nb * a.H, step = gridDim.x;
+  int p = blockIdx.x;
+  if (p >= npairs) return;
+  // pair q = session q / H, head q % H: its state is block q of [nb][H][64][64]
+  auto state_of = [&](int q) -> float4* { return reinterpret_cast<float4*>(a.wkv + (size_t)q * 4096); };
+  // stage 0 <- pair p; channel inputs of p
+  {
+    const float4* src = state_of(p);
 #pragma unroll
-  for (int u = 0; u < 16; ++u) s4[u] = Srow[u];
-  const float wv = a.adp2[((size_t)0 * a.nb + b) * C + ch];
-  const float av = a.adp2[((size_t)1 * a.nb + b) * C + ch];
-  const float gv = a.adp2[((size_t)2 * a.nb + b) * C + ch];
-  float vv = 0.f, vf = 0.f;
-  if (!a.layer0) {
-    vv = a.adp2[((size_t)3 * a.nb + b) * C + ch];
-    vf = a.vfirst[(size_t)b * C + ch];
+    for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[t + 256 * u], &src[t + 256 * u]);
+    cp_async_commit();
   }
-  const float r = bt_fold(a.part[0], a.pp[0], a.nb, C, b, ch);
-  const float k = bt_fold(a.part[1], a.pp[1], a.nb, C, b, ch);
-  float v = bt_fold(a.part[2], a.pp[2], a.nb, C, b, ch);
-  const float kkv = k * a.k_k[ch];
-  const float nrm = sqrtf(bt_sum64(kkv * kkv, red, j));
-  const float aa = sigmoidf_(a.a0[ch] + av);
-  const float kk = kkv / fmaxf(nrm, 1e-12f);
-  const float kn = k * (1.0f + (aa - 1.0f) * a.k_a[ch]);
-  if (a.layer0) a.vfirst[(size_t)b * C + ch] = v;
-  else v = v + (vf - v) * sigmoidf_(a.v0[ch] + vv);
-  float* vd = vecs[j][0];
-  float* vkk = vecs[j][1];
-  float* vka = vecs[j][2];
-  float* vk = vecs[j][3];
-  float* vr = vecs[j][4];
-  vd[i] = expf(-0.606531f * sigmoidf_(a.w0[ch] + wv));
-  vkk[i] = -kk;
-  vka[i] = kk * aa;
-  vk[i] = kn;
-  vr[i] = r;
-  bt_bar64(j);
-  // row i:  sa = S (-kk);  S = S diag(d) + sa (kk a)^T + v_i k^T;  y_i = S r
-  float sa = 0.f;
+  BtWkvChan cur{};
+  if (chan) cur = bt_wkv_chan(a, p / a.H, (p % a.H) * 64 + i);
+  for (int it = 0; p < npairs; p += step, ++it) {
+    const int st = it & 1, nx = p + step;
+    const int b = p / a.H, h = p % a.H, ch = h * 64 + i;
+    // prefetch the next pair into the other stage (an empty group when there is none)
+    if (nx < npairs) {
+      const float4* src = state_of(nx);
 #pragma unroll
-  for (int u = 0; u < 16; ++u) {
-    const float4 n4 = reinterpret_cast<const float4*>(vkk)[u];
-    sa = fmaf(s4[u].x, n4.x, sa);
-    sa = fmaf(s4[u].y, n4.y, sa);
-    sa = fmaf(s4[u].z, n4.z, sa);
-    sa = fmaf(s4[u].w, n4.w, sa);
-  }
-  float y = 0.f;
+      for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[(st ^ 1) * 1024 + t + 256 * u], &src[t + 256 * u]);
+    }
+    cp_async_commit();
+    BtWkvChan nxt{};
+    if (chan && nx < npairs) nxt = bt_wkv_chan(a, nx / a.H, (nx % a.H) * 64 + i);
+    // this pair's channel values
+    float kn = 0.f, v = cur.v;
+    float kkv = 0.f, aa = 0.f;
+    if (chan) {
+      kkv = cur.k * a.k_k[ch];
+      aa = sigmoidf_(a.a0[ch] + cur.av);
+      if (a.layer0) a.vfirst[(size_t)b * a.C + ch] = v;
+      else v = v + (cur.vf - v) * sigmoidf_(a.v0[ch] + cur.vg);
+      vd[i] = expf(-0.606531f * sigmoidf_(a.w0[ch] + cur.wv));
+    }
+    const float nrm = sqrtf(bt_csum64(chan ? kkv * kkv : 0.f, red));
+    if (chan) {
+      const float kk = kkv / fmaxf(nrm, 1e-12f);
+      kn = cur.k * (1.0f + (aa - 1.0f) * a.k_a[ch]);
+      vkk[i] = -kk;
+      vka[i] = kk * aa;
+      vk[i] = kn;
+      vr[i] = cur.r;
+      vv[i] = v;
+    }
+    cp_async_wait_group<1>();  // this pair's stage (the group before the prefetch just issued)
+    __syncthreads();
+    // rows:  sa = S (-kk);  S = S diag(d) + sa (kk a)^T + v_row k^T;  y_row = S r
+    const int cg = t & 15, row0 = t >> 4;
+    const float4 nkk = reinterpret_cast<const float4*>(vkk)[cg];
+    const float4 d4 = reinterpret_cast<const float4*>(vd)[cg];
+    const float4 a4 = reinterpret_cast<const float4*>(vka)[cg];
+    const float4 k4 = reinterpret_cast<const float4*>(vk)[cg];
+    const float4 r4 = reinterpret_cast<const float4*>(vr)[cg];
+    float4* S = state_of(p);
 #pragma unroll
-  for (int u = 0; u < 16; ++u) {
-    const float4 d4 = reinterpret_cast<const float4*>(vd)[u];
-    const float4 a4 = reinterpret_cast<const float4*>(vka)[u];
-    const float4 k4 = reinterpret_cast<const float4*>(vk)[u];
-    const float4 r4 = reinterpret_cast<const float4*>(vr)[u];
-    float4 n;
-    n.x = s4[u].x * d4.x + sa * a4.x + v * k4.x;
-    n.y = s4[u].y * d4.y + sa * a4.y + v * k4.y;
-    n.z = s4[u].z * d4.z + sa * a4.z + v * k4.z;
-    n.w = s4[u].w * d4.w + sa * a4.w + v * k4.w;
-    y = fmaf(n.x, r4.x, y);
-    y = fmaf(n.y, r4.y, y);
-    y = fmaf(n.z, r4.z, y);
-    y = fmaf(n.w, r4.w, y);
-    Srow[u] = n;
+    for (int u = 0; u < 4; ++u) {
+      const int row = row0 + 16 * u;
+      const float4 s4 = bt_stage[st * 1024 + t + 256 * u];
+      float sa = s4.x * nkk.x;
+      sa = fmaf(s4.y, nkk.y, sa);
+      sa = fmaf(s4.z, nkk.z, sa);
+      sa = fmaf(s4.w, nkk.w, sa);
+      sa = bt_sum16(sa);
+      const float vrow = vv[row];
+      float4 n;
+      n.x = s4.x * d4.x + sa * a4.x + vrow * k4.x;
+      n.y = s4.y * d4.y + sa * a4.y + vrow * k4.y;
+      n.z = s4.z * d4.z + sa * a4.z + vrow * k4.z;
+      n.w = s4.w * d4.w + sa * a4.w + vrow * k4.w;
+      float y = n.x * r4.x;
+      y = fmaf(n.y, r4.y, y);
+      y = fmaf(n.z, r4.z, y);
+      y = fmaf(n.w, r4.w, y);
+      y = bt_sum16(y);
+      S[t + 256 * u] = n;
+      if (cg == 0) sy[row] = y;
+    }
+    __syncthreads();
+    // GroupNorm over the head (eps 64e-5), bonus, gate
+    const float y = chan ? sy[i] : 0.f;
+    const float mean = bt_csum64(y, red) / 64.f;
+    const float dv = y - mean;
+    const float var = bt_csum64(chan ? dv * dv : 0.f, red) / 64.f;
+    const float bonus = bt_csum64(chan ? cur.r * kn * a.r_k[ch] : 0.f, red);
+    if (chan) {
+      float o = dv * rsqrtf(var + 64e-5f) * a.lnx_w[ch] + a.lnx_b[ch];
+      o = o + bonus * v;
+      a.att_y[(size_t)b * a.C + ch] = o * cur.gv;
+    }
+    cur = nxt;
+    // the next iteration writes vd/vkk/... and prefetches into this stage only
+    // after every thread is past its reads (bt_csum64 ends with __syncthreads)
   }
-  // GroupNorm over the head (eps 64e-5), bonus, gate
-  const float mean = bt_sum64(y, red, j) / 64.f;
-  const float dv = y - mean;
-  const float var = bt_sum64(dv * dv, red, j) / 64.f;
-  const float bonus = bt_sum64(r * kn * a.r_k[ch], red, j);
-  float o = dv * rsqrtf(var + 64e-5f) * a.lnx_w[ch] + a.lnx_b[ch];
-  o = o + bonus * v;
-  a.att_y[(size_t)b * C + ch] = o * gv;
+  cp_async_wait_all();
 }
 
 // ------------------------------------------------------------ ffn input
@@ -919,7 +1027,8 @@ __global__ void __launch_bounds__(kBtRowThreads) bt_ffnln_kernel(BtFfnLnArgs a) 
 struct BtWkvRowsArgs {
   const float* part[3];
   BtPieces pp[3];
-  const float* adp2;   // [4][rows][C]
+  const float* adp2;   // [slots][rows][C]
+  BtAdpSlots q;
   float* wkv;          // this layer's state [nb][H][64][64]
   float* vfirst;       // [rows][C]
   float* att_y;        // [rows][C]
@@ -947,12 +1056,12 @@ __global__ void __launch_bounds__(kBtThreads, 2) bt_wkvrows_kernel(BtWkvRowsArgs
   float* vr = vecs[js][4];
   for (int j = 0; j < a.P; ++j) {
     const int row = s * a.P + j;
-    const float wv = a.adp2[((size_t)0 * a.rows + row) * C + ch];
-    const float av = a.adp2[((size_t)1 * a.rows + row) * C + ch];
-    const float gv = a.adp2[((size_t)2 * a.rows + row) * C + ch];
+    const float wv = bt_adp_at(a.adp2, a.q, 0, a.rows, row, C, ch);
+    const float av = bt_adp_at(a.adp2, a.q, 1, a.rows, row, C, ch);
+    const float gv = bt_adp_at(a.adp2, a.q, 2, a.rows, row, C, ch);
     float vv = 0.f, vf = 0.f;
     if (!a.layer0) {
-      vv = a.adp2[((size_t)3 * a.rows + row) * C + ch];
+      vv = bt_adp_at(a.adp2, a.q, 3, a.rows, row, C, ch);
       vf = a.vfirst[(size_t)row * C + ch];
     }
     const float r = bt_fold(a.part[0], a.pp[0], a.rows, C, row, ch);
@@ -1126,6 +1235,7 @@ struct BtPrefill {
   int g_rkv = 0, g_o = 0, g_key = 0, g_value = 0;
   size_t smem_bg = 0;
   BtPieces pp_rkv[3], pp_o, pp_key, pp_value;
+  int* np_dev = nullptr;  // piece-count tables of the pp_* above
   cudaGraphExec_t exec = nullptr;
 };
 
@@ -1154,6 +1264,7 @@ struct rwkvb_batch {
   int nb = 0, bp = 0, nrows = 0, lfk = 7, group = 128;
   int L = 0, C = 0, H = 0, F = 0, V = 0, rw = 0, ra = 0, rg = 0, rv = 0, rtot = 0;
   int adp_splits = 0, hist_cap = 1024;
+  rwkvb::BtAdpPlan adp;  // adapter second-stage chunks
   std::vector<rwkvb::BtLayer> layers;
   rwkvb::PackedView emb;
   const float *ln0_w = nullptr, *ln0_b = nullptr, *lnout_w = nullptr, *lnout_b = nullptr;
@@ -1161,6 +1272,7 @@ struct rwkvb_batch {
   int g_rkv = 0, g_o = 0, g_key = 0, g_value = 0, g_head = 0;
   size_t smem_bg = 0;
   rwkvb::BtPieces pp_rkv[3], pp_o, pp_key, pp_value, pp_head;
+  int* np_dev = nullptr;  // piece-count tables of the pp_* above
   void* arena = nullptr;
   float *att_x = nullptr, *wkv = nullptr, *ffn_x = nullptr, *x = nullptr, *xm = nullptr, *xa4 = nullptr;
   float *adp1 = nullptr, *mid = nullptr, *adp2 = nullptr, *vfirst = nullptr, *att_y = nullptr, *logits = nullptr;
@@ -1189,13 +1301,74 @@ struct rwkvb_batch {
 namespace rwkvb {
 namespace {
 
+// Chunks of the adapter second stages: adapter m (w, a, g, v; v last so that
+// layer 0 uses a prefix) in ceil(R_m / kBtAdpChunkRows) near-equal row ranges.
+bool bt_adp_plan(const int (&R)[4], BtAdpPlan& P) {
+  P = BtAdpPlan();
+  int extra = 0;
+  for (int m = 0; m < 4; ++m) {
+    const int n = (R[m] + kBtAdpChunkRows - 1) / kBtAdpChunkRows;
+    if (n < 1 || n > 8 || P.n + n > kBtMaxChunks) return false;
+    P.q.n[m] = n;
+    for (int k = 0; k < n; ++k) {
+      const int c = P.n++;
+      P.m[c] = m;
+      P.r0[c] = (int)((long long)R[m] * k / n);
+      P.r1[c] = (int)((long long)R[m] * (k + 1) / n);
+      P.slot[c] = k == 0 ? m : 4 + extra++;
+      P.q.s[m][k] = P.slot[c];
+    }
+    if (m == 2) P.n_l0 = P.n;
+  }
+  P.slots = 4 + extra;
+  return true;
+}
+
+// Fill the chunk fields of an adapter second-stage launch; returns the chunk count.
+int bt_adp2_chunks(const BtAdpPlan& P, bool layer0, BtAdp2Args& a) {
+  const int n = layer0 ? P.n_l0 : P.n;
+  for (int c = 0; c < n; ++c) {
+    a.ck_m[c] = P.m[c];
+    a.ck_r0[c] = P.r0[c];
+    a.ck_r1[c] = P.r1[c];
+    a.ck_slot[c] = P.slot[c];
+  }
+  return n;
+}
+
 BtPieces bt_pieces(const BgArgs& a, int job, int grid) {
   BtPieces p;
   p.stage0 = a.mat[job].stage0;
   p.G = a.mat[job].k / 128;
   p.total = a.total;
   p.ncta = grid;
+  p.np = nullptr;
   return p;
+}
+
+// Tabulate the per-tile piece counts of each (pieces, output rows) job into
+// one device buffer (*dev, owned by the caller) and point the jobs at it.
+int bt_np_upload(const std::vector<std::pair<BtPieces*, int>>& jobs, int** dev) {
+  std::vector<int> host;
+  std::vector<size_t> off;
+  for (const auto& j : jobs) {
+    off.push_back(host.size());
+    const BtPieces& p = *j.first;
+    const int tiles = (j.second + 127) / 128;
+    for (int t = 0; t < tiles; ++t) {
+      const long long f = p.stage0 + (long long)t * p.G;
+      host.push_back(bg_cta_of(f + p.G - 1, p.total, p.ncta) - bg_cta_of(f, p.total, p.ncta) + 1);
+    }
+  }
+  if (cudaMalloc((void**)dev, sizeof(int) * std::max<size_t>(host.size(), 1)) != cudaSuccess) {
+    cudaGetLastError();
+    *dev = nullptr;
+    return RWKVB_EALLOC;
+  }
+  const int st = cuda_status(cudaMemcpy(*dev, host.data(), sizeof(int) * host.size(), cudaMemcpyHostToDevice));
+  if (st != RWKVB_OK) return st;
+  for (size_t i = 0; i < jobs.size(); ++i) jobs[i].first->np = *dev + off[i];
+  return RWKVB_OK;
 }
 
 // ln_out of x (+ folded value pieces onto xm when `part` is set), the head
@@ -1323,10 +1496,11 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
         off += Rm[m];
       }
       for (int m = 0; m < nm; ++m) a.fast[m] = bt_fast_adp2(a.w[m], C);
+      const int nck = bt_adp2_chunks(e->adp, l0, a);
       a.midT = e->mid;
       a.out = e->adp2;
       a.C = Ca, a.nb = nb, a.rtot = e->rtot;
-      bt_adp2_kernel<<<dim3(Ca / 64, nm), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
+      bt_adp2_kernel<<<dim3(Ca / 64, nck), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
       BT_CHECK();
     }
     {
@@ -1335,13 +1509,15 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.part[0] = e->part_r, a.part[1] = e->part_k, a.part[2] = e->part_v;
       for (int j = 0; j < 3; ++j) a.pp[j] = e->pp_rkv[j];
       a.adp2 = e->adp2;
+      a.q = e->adp.q;
       a.wkv = e->wkv + (size_t)l * nb * e->H * 4096;
       a.vfirst = e->vfirst;
       a.att_y = e->att_y;
       a.w0 = ly.w0, a.a0 = ly.a0, a.v0 = ly.v0, a.k_k = ly.k_k, a.k_a = ly.k_a, a.r_k = ly.r_k;
       a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
       a.C = Ca, a.H = e->H, a.nb = nb, a.layer0 = l0 ? 1 : 0;
-      bt_wkv_kernel<<<dim3(e->H, (nb + kBtWkvSess - 1) / kBtWkvSess), kBtThreads, 0, s>>>(a);
+      const int pairs = nb * e->H, grid = std::min(pairs, e->sms * kBtWkvCtasPerSm);
+      bt_wkv_kernel<<<grid, kBtThreads, 2 * 1024 * sizeof(float4), s>>>(a);
       BT_CHECK();
     }
     if (bg_digits(e->dig_y, e->cs_y, e->att_y, Ca, Ca, nb, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
@@ -1448,7 +1624,7 @@ int bt_prefill_setup(rwkvb_batch* e) {
       {(void**)&f->x, 4 * rC},          {(void**)&f->xm, 4 * rC},
       {(void**)&f->xln, 4 * rC},        {(void**)&f->xln2, 4 * rC},
       {(void**)&f->xa4, 4 * 4 * rC},    {(void**)&f->adp1, 4 * (size_t)e->adp_splits * rows * e->rtot},
-      {(void**)&f->mid, 4 * (size_t)64 * e->rtot}, {(void**)&f->adp2, 4 * 4 * rC},
+      {(void**)&f->mid, 4 * (size_t)64 * e->rtot}, {(void**)&f->adp2, 4 * (size_t)e->adp.slots * rC},
       {(void**)&f->vfirst, 4 * rC},     {(void**)&f->att_y, 4 * rC},
       {(void**)&f->xhead, 4 * (size_t)e->nb * C},
       {(void**)&f->part_r, 4 * (size_t)Pk * rC}, {(void**)&f->part_k, 4 * (size_t)Pk * rC},
@@ -1509,6 +1685,10 @@ int bt_prefill_setup(rwkvb_batch* e) {
     }
     f->rkv.push_back(rkv), f->o.push_back(o), f->key.push_back(key), f->value.push_back(value);
   }
+  if (st == RWKVB_OK)
+    st = bt_np_upload({{&f->pp_rkv[0], C}, {&f->pp_rkv[1], C}, {&f->pp_rkv[2], C}, {&f->pp_o, C},
+                       {&f->pp_key, e->F}, {&f->pp_value, C}},
+                      &f->np_dev);
   if (st == RWKVB_OK) st = bg_allow_smem(f->smem_bg);
   if (st == RWKVB_OK) {
     const void* fns[] = {(const void*)bt_mixrows_kernel, (const void*)bt_lnrows_kernel, (const void*)bt_ffnln_kernel};
@@ -1518,6 +1698,7 @@ int bt_prefill_setup(rwkvb_batch* e) {
   }
   if (st != RWKVB_OK) {
     cudaFree(f->arena);
+    if (f->np_dev) cudaFree(f->np_dev);
     delete f;
     return st;
   }
@@ -1601,10 +1782,11 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
         off += Rm[m];
       }
       for (int m = 0; m < nm; ++m) a.fast[m] = bt_fast_adp2(a.w[m], C);
+      const int nck = bt_adp2_chunks(e->adp, l0, a);
       a.midT = f.mid;
       a.out = f.adp2;
       a.C = C, a.nb = rows, a.rtot = e->rtot;
-      bt_adp2_kernel<<<dim3(C / 64, nm), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
+      bt_adp2_kernel<<<dim3(C / 64, nck), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
       PF_CHECK();
     }
     {
@@ -1613,6 +1795,7 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
       a.part[0] = f.part_r, a.part[1] = f.part_k, a.part[2] = f.part_v;
       for (int j = 0; j < 3; ++j) a.pp[j] = f.pp_rkv[j];
       a.adp2 = f.adp2;
+      a.q = e->adp.q;
       a.wkv = e->wkv + (size_t)l * nb * e->H * 4096;
       a.vfirst = f.vfirst;
       a.att_y = f.att_y;
@@ -1775,6 +1958,13 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
     e->collective = tp->collective, e->collective_user = tp->user;
   }
   e->rw = rw, e->ra = ra, e->rg = rg, e->rv = rv, e->rtot = rw + ra + rg + rv;
+  {
+    const int R[4] = {rw, ra, rg, rv};
+    if (!bt_adp_plan(R, e->adp)) {
+      delete e;
+      return RWKVB_EUNSUPPORTED;
+    }
+  }
   e->adp_splits = C / kBtAdpKc;
   e->emb = make_view(m->emb);
   e->ln0_w = m->ln0_w, e->ln0_b = m->ln0_b, e->lnout_w = m->ln_out_w, e->lnout_b = m->ln_out_b;
@@ -1797,7 +1987,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
       {(void**)&e->xa4, 4 * 4 * nbC},
       {(void**)&e->adp1, 4 * (size_t)e->adp_splits * batch * e->rtot},
       {(void**)&e->mid, 4 * (size_t)64 * e->rtot},
-      {(void**)&e->adp2, 4 * 4 * nbC},
+      {(void**)&e->adp2, 4 * (size_t)e->adp.slots * nbC},
       {(void**)&e->vfirst, 4 * nbC},
       {(void**)&e->att_y, 4 * nbC},
       {(void**)&e->logits, 4 * (size_t)batch * V},
@@ -1912,6 +2102,10 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
     if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
     e->pp_head = bt_pieces(e->head, 0, e->g_head);
   }
+  if (st == RWKVB_OK)
+    st = bt_np_upload({{&e->pp_rkv[0], Ca}, {&e->pp_rkv[1], Ca}, {&e->pp_rkv[2], Ca}, {&e->pp_o, C},
+                       {&e->pp_key, F}, {&e->pp_value, C}, {&e->pp_head, V}},
+                      &e->np_dev);
   if (st == RWKVB_OK) {
     // every kernel must be launchable with the block size the step uses
     struct {
@@ -1953,6 +2147,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   }
   if (st != RWKVB_OK) {
     cudaFree(e->arena);
+    if (e->np_dev) cudaFree(e->np_dev);
     delete e;
     return st;
   }
@@ -1985,9 +2180,11 @@ extern "C" int rwkvb_batch_destroy(rwkvb_batch* e) {
   if (e->pf) {
     if (e->pf->exec) cudaGraphExecDestroy(e->pf->exec);
     if (e->pf->arena) cudaFree(e->pf->arena);
+    if (e->pf->np_dev) cudaFree(e->pf->np_dev);
     delete e->pf;
   }
   if (e->arena) cudaFree(e->arena);
+  if (e->np_dev) cudaFree(e->np_dev);
   delete e;
   return RWKVB_OK;
 }
