@@ -272,7 +272,11 @@ int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out);
  * ------------------------------------------------------------------------------ */
 typedef struct rwkvb_batch rwkvb_batch;
 
-/* flags: bit0 = run the step as plain launches (no CUDA graph). */
+/* flags: bit0 = run the step as plain launches (no CUDA graph);
+ *        bit1 = no programmatic dependent launch between the step's kernels
+ *               (default: each kernel may start while the previous one
+ *               finishes; the GEMMs stream their first weight tiles before
+ *               waiting on it).  Always off under tensor parallelism. */
 int rwkvb_batch_create(const rwkvb_model_desc* desc, int32_t batch, uint32_t flags, rwkvb_batch** out);
 
 /* Tensor parallelism across the GPUs of one node (one process per GPU), the

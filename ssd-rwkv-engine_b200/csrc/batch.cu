@@ -144,11 +144,30 @@ int bg_pieces_single(int tiles, int G, int sms) {
   return pmax;
 }
 
-int bg_launch(const BgArgs& a, int grid, size_t smem, cudaStream_t s) {
+// Launch `k`, with programmatic stream serialization when `pdl` is set: the
+// kernel may start while the previous kernel of the stream finishes; every
+// kernel here begins with griddepcontrol.wait (a no-op without the attribute)
+// before it touches data the previous kernel writes or reads.
+template <typename... K, typename... A>
+int bt_go(bool pdl, void (*k)(K...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, A&&... args) {
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, k, std::forward<A>(args)...));
+}
+
+int bg_launch(const BgArgs& a, int grid, size_t smem, cudaStream_t s, bool pdl = false) {
   int st = bg_allow_smem(smem);
   if (st != RWKVB_OK) return st;
-  bgemm_kernel<<<grid, kBgThreads, smem, s>>>(a);
-  return cuda_status(cudaGetLastError());
+  return bt_go(pdl, bgemm_kernel, dim3(grid), dim3(kBgThreads), smem, s, a);
 }
 
 // Constant rows of a digit matrix: zero everything, then the ones row (3 bp).
@@ -159,11 +178,12 @@ int bg_digits_init(uint8_t* rows, int k, int nb, cudaStream_t s) {
   return cuda_status(e);
 }
 
-int bg_digits(uint8_t* rows, float2* cs, const float* x, int ldx, int k, int nb, int group, cudaStream_t s) {
+int bg_digits(uint8_t* rows, float2* cs, const float* x, int ldx, int k, int nb, int group, cudaStream_t s,
+              bool pdl = false) {
   const int lfk = group == 64 ? 6 : 7;
   const int warps = nb * (k >> lfk);
-  bg_digits_kernel<<<(warps + 7) / 8, 256, 0, s>>>(rows, cs, x, ldx, k, nb, bg_padded_sessions(nb), lfk);
-  return cuda_status(cudaGetLastError());
+  return bt_go(pdl, bg_digits_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, rows, cs, x, ldx, k, nb,
+               bg_padded_sessions(nb), lfk);
 }
 
 }  // namespace rwkvb
@@ -370,6 +390,8 @@ struct BtEmbedArgs {
 };
 
 __global__ void __launch_bounds__(kBtThreads) bt_embed_kernel(BtEmbedArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
   const int b = blockIdx.x, C = a.C;
@@ -404,6 +426,8 @@ struct BtInArgs {
 constexpr int kBtRowThreads = 1024;  // per-session row kernels (one CTA per session)
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_in_kernel(BtInArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
   const int b = blockIdx.x, C = a.C;
@@ -475,6 +499,8 @@ struct BtAdp1Args {
 constexpr int kBtXsStride = 68;  // padded session stride of the staged inputs (bank spread, float4 aligned)
 
 __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float bt_sm[];
   float* xs = bt_sm;                          // [kc][68]: inputs of 64 sessions
   float* ws = xs + kBtAdpKc * kBtXsStride;    // [kc][32]: dequantised weights
@@ -546,6 +572,8 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
 // (transposed, 64 sessions per row, for the second stages).
 __global__ void bt_adpr_kernel(float* midT, const float* part, int splits, int nb, int rtot, int used, int rw,
                                int ra, int rg) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nb * used) return;
   const int b = i / used, j = i - b * used;
@@ -599,6 +627,8 @@ struct BtAdp2Args {
 constexpr int kBtAdp2Rc = 128;  // second-stage rows staged per round
 
 __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float bt_sm[];
   const int ck = blockIdx.y, m = a.ck_m[ck], c0 = blockIdx.x * 64, t = threadIdx.x;
   const int R0 = a.ck_r0[ck], R1 = a.ck_r1[ck];
@@ -729,61 +759,84 @@ __device__ __forceinline__ BtWkvChan bt_wkv_chan(const BtWkvArgs& a, int b, int 
 
 constexpr int kBtWkvCtasPerSm = 4;
 
-// Persistent over (session, head) pairs, 256 threads per CTA, kBtWkvCtasPerSm
-// CTAs per SM.  The state of the next pair (16 KB) is copied into the other
-// shared-memory stage with cp.async while this pair is computed, and threads
-// 0..63 load the next pair's channel inputs into registers, so every SM keeps
-// ~128 KB of state reads in flight.  Stage layout = state layout: thread t
-// works on float4 f = t + 256 u (u < 4), i.e. rows (t >> 4) + 16 u, columns
-// 4 (t & 15) .. + 3; a row's dot products are summed over its 16 lanes; the
-// new state is stored straight to global memory (512 contiguous bytes per
-// warp instruction).
+// Sums of (x, y) over the 64 channel threads (warps 0 and 1) only: named
+// barrier 1 over 64 threads, so the other warps are not held.
+__device__ __forceinline__ float2 bt_chan_sum2(float x, float y, float2* red2) {
+  x = warp_sum(x);
+  y = warp_sum(y);
+  if ((threadIdx.x & 31) == 0) red2[threadIdx.x >> 5] = make_float2(x, y);
+  asm volatile("bar.sync 1, 64;" ::: "memory");
+  const float2 r = make_float2(red2[0].x + red2[1].x, red2[0].y + red2[1].y);
+  asm volatile("bar.sync 1, 64;" ::: "memory");
+  return r;
+}
+
+// Persistent over (head, session) pairs taken head-major (q = h * nb + b) in a
+// contiguous block per CTA, 256 threads per CTA, kBtWkvCtasPerSm CTAs per SM.
+//   - the next pair's state (16 KB) is copied into the other shared-memory
+//     stage with cp.async while this pair is computed, and threads 0..63 load
+//     its channel inputs into registers: ~128 KB of state reads per SM in flight;
+//   - the head's eight per-channel vectors are loaded when the head changes;
+//   - thread t works on float4 f = t + 256 u (u < 4) of the state: rows
+//     (t >> 4) + 16 u, columns 4 (t & 15) .. + 3; a row's dot products are
+//     summed over its 16 lanes; the new state is stored straight to global
+//     memory (512 contiguous bytes per warp instruction);
+//   - channel sums (k norm; GroupNorm mean with the bonus; variance) run on the
+//     64 channel threads under a 64-thread barrier; two CTA barriers per pair.
 __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtWkvArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float4 bt_stage[];  // [2][1024]
-  __shared__ float red[2];
+  __shared__ float2 red2[2];
   __shared__ __align__(16) float vd[64], vkk[64], vka[64], vk[64], vr[64], vv[64], sy[64];
   const int t = threadIdx.x, i = t & 63;
   const bool chan = t < 64;
-  const int npairs = a.nb * a.H, step = gridDim.x;
-  int p = blockIdx.x;
-  if (p >= npairs) return;
-  // pair q = session q / H, head q % H: its state is block q of [nb][H][64][64]
-  auto state_of = [&](int q) -> float4* { return reinterpret_cast<float4*>(a.wkv + (size_t)q * 4096); };
-  // stage 0 <- pair p; channel inputs of p
+  const int npairs = a.nb * a.H;
+  const int q0 = (int)((long long)blockIdx.x * npairs / gridDim.x);
+  const int q1 = (int)((long long)(blockIdx.x + 1) * npairs / gridDim.x);
+  if (q0 >= q1) return;
+  // pair q = (head q / nb, session q % nb); its state is block (b, h) of [nb][H][64][64]
+  auto state_of = [&](int q) -> float4* {
+    return reinterpret_cast<float4*>(a.wkv + ((size_t)(q % a.nb) * a.H + q / a.nb) * 4096);
+  };
   {
-    const float4* src = state_of(p);
+    const float4* src = state_of(q0);
 #pragma unroll
     for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[t + 256 * u], &src[t + 256 * u]);
     cp_async_commit();
   }
   BtWkvChan cur{};
-  if (chan) cur = bt_wkv_chan(a, p / a.H, (p % a.H) * 64 + i);
-  for (int it = 0; p < npairs; p += step, ++it) {
-    const int st = it & 1, nx = p + step;
-    const int b = p / a.H, h = p % a.H, ch = h * 64 + i;
-    // prefetch the next pair into the other stage (an empty group when there is none)
-    if (nx < npairs) {
+  if (chan) cur = bt_wkv_chan(a, q0 % a.nb, (q0 / a.nb) * 64 + i);
+  int vh = -1;  // head whose vectors are in registers
+  float kkw = 0.f, a0v = 0.f, v0v = 0.f, w0v = 0.f, kav = 0.f, rkv = 0.f, lw = 0.f, lb = 0.f;
+  for (int q = q0, it = 0; q < q1; ++q, ++it) {
+    const int st = it & 1, nx = q + 1;
+    const int b = q % a.nb, h = q / a.nb, ch = h * 64 + i;
+    if (nx < q1) {
       const float4* src = state_of(nx);
 #pragma unroll
       for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[(st ^ 1) * 1024 + t + 256 * u], &src[t + 256 * u]);
     }
-    cp_async_commit();
+    cp_async_commit();  // an empty group when there is no next pair
     BtWkvChan nxt{};
-    if (chan && nx < npairs) nxt = bt_wkv_chan(a, nx / a.H, (nx % a.H) * 64 + i);
-    // this pair's channel values
-    float kn = 0.f, v = cur.v;
-    float kkv = 0.f, aa = 0.f;
+    float kn = 0.f, v = 0.f;
     if (chan) {
-      kkv = cur.k * a.k_k[ch];
-      aa = sigmoidf_(a.a0[ch] + cur.av);
+      if (nx < q1) nxt = bt_wkv_chan(a, nx % a.nb, (nx / a.nb) * 64 + i);
+      if (h != vh) {
+        vh = h;
+        kkw = a.k_k[ch], a0v = a.a0[ch], w0v = a.w0[ch], kav = a.k_a[ch], rkv = a.r_k[ch];
+        lw = a.lnx_w[ch], lb = a.lnx_b[ch];
+        v0v = a.layer0 ? 0.f : a.v0[ch];
+      }
+      v = cur.v;
+      const float kkv = cur.k * kkw;
+      const float aa = sigmoidf_(a0v + cur.av);
       if (a.layer0) a.vfirst[(size_t)b * a.C + ch] = v;
-      else v = v + (cur.vf - v) * sigmoidf_(a.v0[ch] + cur.vg);
-      vd[i] = expf(-0.606531f * sigmoidf_(a.w0[ch] + cur.wv));
-    }
-    const float nrm = sqrtf(bt_csum64(chan ? kkv * kkv : 0.f, red));
-    if (chan) {
+      else v = v + (cur.vf - v) * sigmoidf_(v0v + cur.vg);
+      const float nrm = sqrtf(bt_chan_sum2(kkv * kkv, 0.f, red2).x);
       const float kk = kkv / fmaxf(nrm, 1e-12f);
-      kn = cur.k * (1.0f + (aa - 1.0f) * a.k_a[ch]);
+      kn = cur.k * (1.0f + (aa - 1.0f) * kav);
+      vd[i] = expf(-0.606531f * sigmoidf_(w0v + cur.wv));
       vkk[i] = -kk;
       vka[i] = kk * aa;
       vk[i] = kn;
@@ -793,51 +846,51 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
     cp_async_wait_group<1>();  // this pair's stage (the group before the prefetch just issued)
     __syncthreads();
     // rows:  sa = S (-kk);  S = S diag(d) + sa (kk a)^T + v_row k^T;  y_row = S r
-    const int cg = t & 15, row0 = t >> 4;
-    const float4 nkk = reinterpret_cast<const float4*>(vkk)[cg];
-    const float4 d4 = reinterpret_cast<const float4*>(vd)[cg];
-    const float4 a4 = reinterpret_cast<const float4*>(vka)[cg];
-    const float4 k4 = reinterpret_cast<const float4*>(vk)[cg];
-    const float4 r4 = reinterpret_cast<const float4*>(vr)[cg];
-    float4* S = state_of(p);
+    {
+      const int cg = t & 15, row0 = t >> 4;
+      const float4 nkk = reinterpret_cast<const float4*>(vkk)[cg];
+      const float4 d4 = reinterpret_cast<const float4*>(vd)[cg];
+      const float4 a4 = reinterpret_cast<const float4*>(vka)[cg];
+      const float4 k4 = reinterpret_cast<const float4*>(vk)[cg];
+      const float4 r4 = reinterpret_cast<const float4*>(vr)[cg];
+      float4* S = state_of(q);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int row = row0 + 16 * u;
-      const float4 s4 = bt_stage[st * 1024 + t + 256 * u];
-      float sa = s4.x * nkk.x;
-      sa = fmaf(s4.y, nkk.y, sa);
-      sa = fmaf(s4.z, nkk.z, sa);
-      sa = fmaf(s4.w, nkk.w, sa);
-      sa = bt_sum16(sa);
-      const float vrow = vv[row];
-      float4 n;
-      n.x = s4.x * d4.x + sa * a4.x + vrow * k4.x;
-      n.y = s4.y * d4.y + sa * a4.y + vrow * k4.y;
-      n.z = s4.z * d4.z + sa * a4.z + vrow * k4.z;
-      n.w = s4.w * d4.w + sa * a4.w + vrow * k4.w;
-      float y = n.x * r4.x;
-      y = fmaf(n.y, r4.y, y);
-      y = fmaf(n.z, r4.z, y);
-      y = fmaf(n.w, r4.w, y);
-      y = bt_sum16(y);
-      S[t + 256 * u] = n;
-      if (cg == 0) sy[row] = y;
+      for (int u = 0; u < 4; ++u) {
+        const int row = row0 + 16 * u;
+        const float4 s4 = bt_stage[st * 1024 + t + 256 * u];
+        float sa = s4.x * nkk.x;
+        sa = fmaf(s4.y, nkk.y, sa);
+        sa = fmaf(s4.z, nkk.z, sa);
+        sa = fmaf(s4.w, nkk.w, sa);
+        sa = bt_sum16(sa);
+        const float vrow = vv[row];
+        float4 n;
+        n.x = s4.x * d4.x + sa * a4.x + vrow * k4.x;
+        n.y = s4.y * d4.y + sa * a4.y + vrow * k4.y;
+        n.z = s4.z * d4.z + sa * a4.z + vrow * k4.z;
+        n.w = s4.w * d4.w + sa * a4.w + vrow * k4.w;
+        float y = n.x * r4.x;
+        y = fmaf(n.y, r4.y, y);
+        y = fmaf(n.z, r4.z, y);
+        y = fmaf(n.w, r4.w, y);
+        y = bt_sum16(y);
+        S[t + 256 * u] = n;
+        if (cg == 0) sy[row] = y;
+      }
     }
-    __syncthreads();
-    // GroupNorm over the head (eps 64e-5), bonus, gate
-    const float y = chan ? sy[i] : 0.f;
-    const float mean = bt_csum64(y, red) / 64.f;
-    const float dv = y - mean;
-    const float var = bt_csum64(chan ? dv * dv : 0.f, red) / 64.f;
-    const float bonus = bt_csum64(chan ? cur.r * kn * a.r_k[ch] : 0.f, red);
+    __syncthreads();  // sy complete; stage st and the vectors are free again
     if (chan) {
-      float o = dv * rsqrtf(var + 64e-5f) * a.lnx_w[ch] + a.lnx_b[ch];
-      o = o + bonus * v;
+      // GroupNorm over the head (eps 64e-5), bonus, gate
+      const float y = sy[i];
+      const float2 mb = bt_chan_sum2(y, cur.r * kn * rkv, red2);
+      const float mean = mb.x / 64.f;
+      const float dv = y - mean;
+      const float var = bt_chan_sum2(dv * dv, 0.f, red2).x / 64.f;
+      float o = dv * rsqrtf(var + 64e-5f) * lw + lb;
+      o = o + mb.y * v;
       a.att_y[(size_t)b * a.C + ch] = o * cur.gv;
     }
     cur = nxt;
-    // the next iteration writes vd/vkk/... and prefetches into this stage only
-    // after every thread is past its reads (bt_csum64 ends with __syncthreads)
   }
   cp_async_wait_all();
 }
@@ -857,6 +910,8 @@ struct BtFfnArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_ffn_kernel(BtFfnArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
   const int b = blockIdx.x, C = a.C;
@@ -882,6 +937,8 @@ __global__ void __launch_bounds__(kBtRowThreads) bt_ffn_kernel(BtFfnArgs a) {
 // h = relu(key)^2 and its digit rows: one warp per (session, group).
 __global__ void __launch_bounds__(kBtThreads) bt_hdig_kernel(uint8_t* dig, float2* cs, const float* part, BtPieces pp,
                                                              int nb, int F, int bp, int lfk) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int G = F >> lfk;
   if (gw >= nb * G) return;
@@ -916,6 +973,8 @@ struct BtLnRowsArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_lnrows_kernel(BtLnRowsArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
   const int row = blockIdx.x, C = a.C;
@@ -949,6 +1008,8 @@ struct BtMixRowsArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_mixrows_kernel(BtMixRowsArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   extern __shared__ __align__(16) float bt_sm[];
   const int row = blockIdx.x, C = a.C, s = row / a.P, j = row - s * a.P;
   float* xl = bt_sm;
@@ -1009,6 +1070,8 @@ struct BtFfnLnArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_ffnln_kernel(BtFfnLnArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
   const int row = blockIdx.x, C = a.C;
@@ -1037,6 +1100,8 @@ struct BtWkvRowsArgs {
 };
 
 __global__ void __launch_bounds__(kBtThreads, 2) bt_wkvrows_kernel(BtWkvRowsArgs a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   __shared__ float red[2 * kBtWkvSess];
   __shared__ __align__(16) float vecs[kBtWkvSess][5][64];
   const int h = blockIdx.x, t = threadIdx.x, js = t >> 6, i = t & 63;
@@ -1123,6 +1188,8 @@ __global__ void __launch_bounds__(kBtThreads, 2) bt_wkvrows_kernel(BtWkvRowsArgs
 // residual stream (with the last value projection folded in), in decode rows.
 __global__ void bt_pick_last_kernel(float* xs, const float* xm, const float* part, BtPieces pp, int C, int rows,
                                     int P, int nb) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nb * C) return;
   const int s = i / C, c = i - s * C, row = s * P + P - 1;
@@ -1135,6 +1202,8 @@ __global__ void bt_pick_last_kernel(float* xs, const float* xm, const float* par
 __global__ void __launch_bounds__(1024) bt_argmax_kernel(float* logits, const float* part, BtPieces pp, int nb,
                                                          int V, int* tok, int* hist, const int* step, int hist_cap,
                                                          int v0, float2* loc) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   __shared__ float bv[32];
   __shared__ int bi[32];
   const int b = blockIdx.x;
@@ -1186,6 +1255,8 @@ __global__ void __launch_bounds__(1024) bt_argmax_kernel(float* logits, const fl
 // vocabulary ranges): the largest value, the smallest index among equals.
 __global__ void bt_argmax_merge_kernel(const float2* all, int ranks, int nb, int* tok, int* hist, const int* step,
                                        int hist_cap) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= nb) return;
   float best = -INFINITY;
@@ -1264,6 +1335,7 @@ struct rwkvb_batch {
   int nb = 0, bp = 0, nrows = 0, lfk = 7, group = 128;
   int L = 0, C = 0, H = 0, F = 0, V = 0, rw = 0, ra = 0, rg = 0, rv = 0, rtot = 0;
   int adp_splits = 0, hist_cap = 1024;
+  bool pdl = true;       // programmatic dependent launch between the step's kernels
   rwkvb::BtAdpPlan adp;  // adapter second-stage chunks
   std::vector<rwkvb::BtLayer> layers;
   rwkvb::PackedView emb;
@@ -1389,17 +1461,17 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
   a.dig[0] = e->dig_o;
   a.cs[0] = e->cs_o;
   a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
-  bt_in_kernel<<<nb, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
+  bt_go(e->pdl, bt_in_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
   int st = cuda_status(cudaGetLastError());
-  if (st == RWKVB_OK) st = bg_launch(e->head, e->g_head, e->smem_bg, s);
+  if (st == RWKVB_OK) st = bg_launch(e->head, e->g_head, e->smem_bg, s, e->pdl);
   if (st != RWKVB_OK) return st;
   const bool tp = e->tp_size > 1;
-  bt_argmax_kernel<<<nb, 1024, 0, s>>>(e->logits, e->part_head, e->pp_head, nb, e->V, e->tok, e->hist, e->step,
+  bt_go(e->pdl, bt_argmax_kernel, dim3(nb), dim3(1024), 0, s, e->logits, e->part_head, e->pp_head, nb, e->V, e->tok, e->hist, e->step,
                                        e->hist_cap, e->V0, tp ? e->amax_loc : nullptr);
   st = cuda_status(cudaGetLastError());
   if (st != RWKVB_OK || !tp) return st;
   e->collective(1, e->amax_loc, e->amax_all, (int64_t)sizeof(float2) * nb, s, e->collective_user);
-  bt_argmax_merge_kernel<<<(nb + 127) / 128, 128, 0, s>>>(e->amax_all, e->tp_size, nb, e->tok, e->hist, e->step,
+  bt_go(e->pdl, bt_argmax_merge_kernel, dim3((nb + 127) / 128), dim3(128), 0, s, e->amax_all, e->tp_size, nb, e->tok, e->hist, e->step,
                                                           e->hist_cap);
   return cuda_status(cudaGetLastError());
 }
@@ -1430,7 +1502,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
   } while (0)
   {
     BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, e->tok, e->x, e->step, e->err, C, e->Vfull};
-    bt_embed_kernel<<<nb, kBtThreads, sizeof(float) * C, s>>>(a);
+    bt_go(e->pdl, bt_embed_kernel, dim3(nb), dim3(kBtThreads), sizeof(float) * C, s, a);
     BT_CHECK();
   }
   for (int l = 0; l < e->L; ++l) {
@@ -1452,10 +1524,10 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.cs[0] = e->cs_r, a.cs[1] = e->cs_k, a.cs[2] = e->cs_v;
       a.xa4 = e->xa4;
       a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
-      bt_in_kernel<<<nb, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
+      bt_go(e->pdl, bt_in_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
       BT_CHECK();
     }
-    if (bg_launch(ly.rkv, e->g_rkv, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(ly.rkv, e->g_rkv, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     const int nm = l0 ? 3 : 4;
     {
@@ -1477,10 +1549,10 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.xa4 = e->xa4;
       a.out = e->adp1;
       a.C = C, a.nb = nb, a.rtot = e->rtot;
-      bt_adp1_kernel<<<dim3(blk, e->adp_splits), kBtThreads, kBtAdp1Smem, s>>>(a);
+      bt_go(e->pdl, bt_adp1_kernel, dim3(blk, e->adp_splits), dim3(kBtThreads), kBtAdp1Smem, s, a);
       BT_CHECK();
       const int used = l0 ? e->rw + e->ra + e->rg : e->rtot;
-      bt_adpr_kernel<<<(nb * used + 255) / 256, 256, 0, s>>>(e->mid, e->adp1, e->adp_splits, nb, e->rtot, used,
+      bt_go(e->pdl, bt_adpr_kernel, dim3((nb * used + 255) / 256), dim3(256), 0, s, e->mid, e->adp1, e->adp_splits, nb, e->rtot, used,
                                                               e->rw, e->ra, e->rg);
       BT_CHECK();
     }
@@ -1500,7 +1572,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.midT = e->mid;
       a.out = e->adp2;
       a.C = Ca, a.nb = nb, a.rtot = e->rtot;
-      bt_adp2_kernel<<<dim3(Ca / 64, nck), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
+      bt_go(e->pdl, bt_adp2_kernel, dim3(Ca / 64, nck), dim3(kBtThreads), sizeof(float) * 2 * kBtAdp2Rc * 64, s, a);
       BT_CHECK();
     }
     {
@@ -1517,12 +1589,12 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
       a.C = Ca, a.H = e->H, a.nb = nb, a.layer0 = l0 ? 1 : 0;
       const int pairs = nb * e->H, grid = std::min(pairs, e->sms * kBtWkvCtasPerSm);
-      bt_wkv_kernel<<<grid, kBtThreads, 2 * 1024 * sizeof(float4), s>>>(a);
+      bt_go(e->pdl, bt_wkv_kernel, dim3(grid), dim3(kBtThreads), 2 * 1024 * sizeof(float4), s, a);
       BT_CHECK();
     }
-    if (bg_digits(e->dig_y, e->cs_y, e->att_y, Ca, Ca, nb, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_digits(e->dig_y, e->cs_y, e->att_y, Ca, Ca, nb, e->group, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
-    if (bg_launch(ly.o, e->g_o, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(ly.o, e->g_o, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     if (tp) {
       if (bt_reduce(e, e->ored, e->part_o, e->pp_o, s) != RWKVB_OK) return RWKVB_ECUDA;
@@ -1531,18 +1603,18 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     {
       BtFfnArgs a{e->x, e->xm, e->part_o, e->pp_o, ly.ln2_w, ly.ln2_b, ly.ffn_x_k,
                   e->ffn_x + (size_t)l * nb * C, e->dig_f, e->cs_f, C, nb, e->bp, e->lfk, tp ? e->ored : nullptr};
-      bt_ffn_kernel<<<nb, kBtRowThreads, sizeof(float) * C, s>>>(a);
+      bt_go(e->pdl, bt_ffn_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * C, s, a);
       BT_CHECK();
     }
-    if (bg_launch(ly.key, e->g_key, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(ly.key, e->g_key, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     {
       const int warps = nb * (e->F >> e->lfk);
-      bt_hdig_kernel<<<(warps + 7) / 8, kBtThreads, 0, s>>>(e->dig_h, e->cs_h, e->part_key, e->pp_key, nb, e->F,
+      bt_go(e->pdl, bt_hdig_kernel, dim3((warps + 7) / 8), dim3(kBtThreads), 0, s, e->dig_h, e->cs_h, e->part_key, e->pp_key, nb, e->F,
                                                            e->bp, e->lfk);
       BT_CHECK();
     }
-    if (bg_launch(ly.value, e->g_value, e->smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(ly.value, e->g_value, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     if (tp) {
       if (bt_reduce(e, e->vred, e->part_val, e->pp_value, s) != RWKVB_OK) return RWKVB_ECUDA;
@@ -1717,7 +1789,7 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
   } while (0)
   {
     BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, f.tok, f.x, f.step, e->err, C, e->Vfull};
-    bt_embed_kernel<<<rows, kBtThreads, sizeof(float) * C, s>>>(a);
+    bt_go(e->pdl, bt_embed_kernel, dim3(rows), dim3(kBtThreads), sizeof(float) * C, s, a);
     PF_CHECK();
   }
   for (int l = 0; l < e->L; ++l) {
@@ -1726,7 +1798,7 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
     {
       BtLnRowsArgs a{f.x, l0 ? nullptr : f.xm, l0 ? nullptr : f.part_val, f.pp_value, ly.ln1_w, ly.ln1_b, f.xln,
                      C, rows};
-      bt_lnrows_kernel<<<rows, kBtRowThreads, sizeof(float) * C, s>>>(a);
+      bt_go(e->pdl, bt_lnrows_kernel, dim3(rows), dim3(kBtRowThreads), sizeof(float) * C, s, a);
       PF_CHECK();
     }
     {
@@ -1739,10 +1811,10 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
       a.cs[0] = f.cs_r, a.cs[1] = f.cs_k, a.cs[2] = f.cs_v;
       a.xa4 = f.xa4;
       a.C = C, a.rows = rows, a.P = f.P, a.bp = f.bp, a.lfk = e->lfk, a.mode = 0;
-      bt_mixrows_kernel<<<rows, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
+      bt_go(e->pdl, bt_mixrows_kernel, dim3(rows), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
       PF_CHECK();
     }
-    if (bg_launch(f.rkv[l], f.g_rkv, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(f.rkv[l], f.g_rkv, f.smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     const int nm = l0 ? 3 : 4;
     {
       BtAdp1Args a;
@@ -1763,10 +1835,10 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
       a.xa4 = f.xa4;
       a.out = f.adp1;
       a.C = C, a.nb = rows, a.rtot = e->rtot;
-      bt_adp1_kernel<<<dim3(blk, e->adp_splits), kBtThreads, kBtAdp1Smem, s>>>(a);
+      bt_go(e->pdl, bt_adp1_kernel, dim3(blk, e->adp_splits), dim3(kBtThreads), kBtAdp1Smem, s, a);
       PF_CHECK();
       const int used = l0 ? e->rw + e->ra + e->rg : e->rtot;
-      bt_adpr_kernel<<<(rows * used + 255) / 256, 256, 0, s>>>(f.mid, f.adp1, e->adp_splits, rows, e->rtot, used,
+      bt_go(e->pdl, bt_adpr_kernel, dim3((rows * used + 255) / 256), dim3(256), 0, s, f.mid, f.adp1, e->adp_splits, rows, e->rtot, used,
                                                                 e->rw, e->ra, e->rg);
       PF_CHECK();
     }
@@ -1786,7 +1858,7 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
       a.midT = f.mid;
       a.out = f.adp2;
       a.C = C, a.nb = rows, a.rtot = e->rtot;
-      bt_adp2_kernel<<<dim3(C / 64, nck), kBtThreads, sizeof(float) * 2 * kBtAdp2Rc * 64, s>>>(a);
+      bt_go(e->pdl, bt_adp2_kernel, dim3(C / 64, nck), dim3(kBtThreads), sizeof(float) * 2 * kBtAdp2Rc * 64, s, a);
       PF_CHECK();
     }
     {
@@ -1802,14 +1874,14 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
       a.w0 = ly.w0, a.a0 = ly.a0, a.v0 = ly.v0, a.k_k = ly.k_k, a.k_a = ly.k_a, a.r_k = ly.r_k;
       a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
       a.C = C, a.H = e->H, a.nb = nb, a.rows = rows, a.P = f.P, a.layer0 = l0 ? 1 : 0;
-      bt_wkvrows_kernel<<<dim3(e->H, (nb + kBtWkvSess - 1) / kBtWkvSess), kBtThreads, 0, s>>>(a);
+      bt_go(e->pdl, bt_wkvrows_kernel, dim3(e->H, (nb + kBtWkvSess - 1) / kBtWkvSess), dim3(kBtThreads), 0, s, a);
       PF_CHECK();
     }
-    if (bg_digits(f.dig_y, f.cs_y, f.att_y, C, C, rows, e->group, s) != RWKVB_OK) return RWKVB_ECUDA;
-    if (bg_launch(f.o[l], f.g_o, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_digits(f.dig_y, f.cs_y, f.att_y, C, C, rows, e->group, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(f.o[l], f.g_o, f.smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     {
       BtFfnLnArgs a{f.x, f.xm, f.part_o, f.pp_o, ly.ln2_w, ly.ln2_b, f.xln2, C, rows};
-      bt_ffnln_kernel<<<rows, kBtRowThreads, sizeof(float) * C, s>>>(a);
+      bt_go(e->pdl, bt_ffnln_kernel, dim3(rows), dim3(kBtRowThreads), sizeof(float) * C, s, a);
       PF_CHECK();
     }
     {
@@ -1821,19 +1893,19 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
       a.dig[0] = f.dig_f;
       a.cs[0] = f.cs_f;
       a.C = C, a.rows = rows, a.P = f.P, a.bp = f.bp, a.lfk = e->lfk, a.mode = 1;
-      bt_mixrows_kernel<<<rows, kBtRowThreads, sizeof(float) * 5 * C, s>>>(a);
+      bt_go(e->pdl, bt_mixrows_kernel, dim3(rows), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
       PF_CHECK();
     }
-    if (bg_launch(f.key[l], f.g_key, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(f.key[l], f.g_key, f.smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     {
       const int warps = rows * (e->F >> e->lfk);
-      bt_hdig_kernel<<<(warps + 7) / 8, kBtThreads, 0, s>>>(f.dig_h, f.cs_h, f.part_key, f.pp_key, rows, e->F, f.bp,
+      bt_go(e->pdl, bt_hdig_kernel, dim3((warps + 7) / 8), dim3(kBtThreads), 0, s, f.dig_h, f.cs_h, f.part_key, f.pp_key, rows, e->F, f.bp,
                                                            e->lfk);
       PF_CHECK();
     }
-    if (bg_launch(f.value[l], f.g_value, f.smem_bg, s) != RWKVB_OK) return RWKVB_ECUDA;
+    if (bg_launch(f.value[l], f.g_value, f.smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
   }
-  bt_pick_last_kernel<<<(nb * C + 255) / 256, 256, 0, s>>>(f.xhead, f.xm, f.part_val, f.pp_value, C, rows, f.P, nb);
+  bt_go(e->pdl, bt_pick_last_kernel, dim3((nb * C + 255) / 256), dim3(256), 0, s, f.xhead, f.xm, f.part_val, f.pp_value, C, rows, f.P, nb);
   PF_CHECK();
 #undef PF_CHECK
   return RWKVB_OK;
@@ -1946,6 +2018,8 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   cudaGetDevice(&e->dev);
   e->sms = device_sms();
   e->use_graph = !(flags & 0x1u);
+  // bit 1: no programmatic dependent launch; off under tensor parallelism (collectives between kernels)
+  e->pdl = !(flags & 0x2u) && !tp;
   e->nb = batch;
   e->bp = bg_padded_sessions(batch);
   e->nrows = bg_digit_rows(batch);

@@ -188,16 +188,41 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
     // ------------------------------------------------------------ producer
     uint32_t use = 0;
     const uint32_t bytes = (uint32_t)stage_bytes;
+    // The weight codes of the first `stages` stages go out before the grid
+    // dependency wait (weights never depend on the previous kernel; under a
+    // programmatic dependent launch they stream while it finishes); their
+    // digit rows, written by the previous kernel, after it.  Weight codes are
+    // read once per step: evict first, keep digit rows and constants in L2.
+    uint32_t npre = 0;
+    if (lane == 0) {
+      for (int x = lo; x < hi && npre < (uint32_t)a.stages;) {
+        const BgSeg sg = bg_segment(a, x, hi);
+        for (int st = sg.s0; st < sg.s1 && npre < (uint32_t)a.stages; ++st, ++npre) {
+          mbar_expect_tx(&full[npre], bytes);
+          tma_load_2d_hint(smem + npre * stage_bytes, &a.amap[sg.m], st * 128, sg.t * 128, &full[npre],
+                           l2_evict_first());
+        }
+        x += sg.s1 - sg.s0;
+      }
+    }
+    npre = __shfl_sync(0xffffffffu, npre, 0);
+    pdl_wait();
+    pdl_launch_dependents();
     for (int x = lo; x < hi;) {
       const BgSeg sg = bg_segment(a, x, hi);
       const BgMat& M = a.mat[sg.m];
       for (int st = sg.s0; st < sg.s1; ++st, ++use) {
         const uint32_t slot = use % a.stages, n = use / a.stages;
+        if (use < npre) {  // weights already issued; ring slot fresh
+          if (lane == 0) tma_load_2d(smem + slot * stage_bytes + kBgTileBytes, &a.bmap[M.digits], st * 128, 0,
+                                     &full[slot]);
+          __syncwarp();
+          continue;
+        }
         if (!bg_wait(&empty[slot], (n & 1) ^ 1, a, &s_abort)) goto producer_drain;
         if (lane == 0) {
           uint8_t* sa = smem + slot * stage_bytes;
           mbar_expect_tx(&full[slot], bytes);
-          // weight codes are read once per step: evict first, keep the digit rows and per-row constants in L2
           tma_load_2d_hint(sa, &a.amap[sg.m], st * 128, sg.t * 128, &full[slot], l2_evict_first());
           tma_load_2d(sa + kBgTileBytes, &a.bmap[M.digits], st * 128, 0, &full[slot]);
         }
@@ -213,6 +238,7 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    pdl_launch_dependents();  // reads shared memory only (full barriers follow the producer's wait)
     uint32_t use = 0, fl = 0;
     for (int x = lo; x < hi;) {
       const BgSeg sg = bg_segment(a, x, hi);
@@ -253,6 +279,8 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    pdl_wait();  // per-session constants come from the previous kernel; outputs may be read by it
+    pdl_launch_dependents();
     // warp w: TMEM lane quarter w % 4, sessions [16 ch, 16 ch + 16) with
     // ch = (w - 2) / 4; pairs of sessions go through packed f32x2 arithmetic.
     const int q4 = warp & 3, ch = (warp - 2) >> 2;
@@ -397,6 +425,8 @@ __device__ __forceinline__ void bg_emit_group(const float (&v)[4], int per, uint
 // flush groups of 1 << lfk columns (64 or 128): one warp per (session, group).
 __global__ void __launch_bounds__(256) bg_digits_kernel(uint8_t* dig, float2* cs, const float* x, int ldx, int k,
                                                         int nb, int bp, int lfk) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int G = k >> lfk;
   if (gw >= nb * G) return;
@@ -417,6 +447,8 @@ __global__ void __launch_bounds__(256) bg_digits_kernel(uint8_t* dig, float2* cs
 // y[b][n] = sum over the pieces of n's tile of part[p][b][n], in piece order.
 __global__ void bg_reduce_kernel(float* y, const float* part, int nb, int rows, int stage0, int G, int total,
                                  int ncta) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nb * rows) return;
   const int b = i / rows, n = i - b * rows;

@@ -261,7 +261,8 @@ class B200BatchEngine:
     the result is that loop's, token for token.  State per layer and session
     keeps the ``RecurrentState.rwkv7_state`` triple."""
 
-    def __init__(self, pack, batch: int, *, device: int | torch.device = 0, use_graph: bool = True):
+    def __init__(self, pack, batch: int, *, device: int | torch.device = 0, use_graph: bool = True,
+                 pdl: bool = True):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200BatchEngine needs a CUDA device; there is no CPU path")
@@ -271,6 +272,8 @@ class B200BatchEngine:
             self._model = pack if isinstance(pack, ModelUpload) else ModelUpload(pack, self.device)
             self.shape = s = self._model.shape
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
+            if not pdl:
+                flags |= native.FLAG_NO_PDL
             h = ctypes.c_void_p()
             native.check(self.lib.rwkvb_batch_create(ctypes.byref(self._model.md), self.batch, flags,
                                                      ctypes.byref(h)), "rwkvb_batch_create")
