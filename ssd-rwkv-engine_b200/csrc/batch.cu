@@ -512,9 +512,27 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
   const int c0 = ((int)blockIdx.x - a.blk0[m]) * kBtAdpCols;
   const int k0 = blockIdx.y * kBtAdpKc;
   const float* xsrc = a.xa4 + (size_t)m * a.nb * a.C;
-  for (int idx = t; idx < kBtAdpKc * 64; idx += blockDim.x) {
-    const int b = idx / kBtAdpKc, kk = idx - b * kBtAdpKc;
-    xs[kk * kBtXsStride + b] = b < a.nb ? xsrc[(size_t)b * a.C + k0 + kk] : 0.f;
+  // inputs x[b][k0 .. k0 + 127] of the 64 session slots: 8 float4 loads per
+  // thread, all in flight before the first store; lanes take consecutive
+  // sessions, so the transposed stores xs[k][b] hit distinct banks
+  {
+    constexpr int kPer = kBtAdpKc * 64 / 4 / kBtThreads;
+    static_assert(kPer * 4 * kBtThreads == kBtAdpKc * 64, "x slice split");
+    float4 v[kPer];
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int idx = t + r * kBtThreads, b = idx & 63, k4 = idx >> 6;
+      v[r] = b < a.nb ? *reinterpret_cast<const float4*>(xsrc + (size_t)b * a.C + k0 + 4 * k4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int idx = t + r * kBtThreads, b = idx & 63, k4 = idx >> 6;
+      xs[(4 * k4 + 0) * kBtXsStride + b] = v[r].x;
+      xs[(4 * k4 + 1) * kBtXsStride + b] = v[r].y;
+      xs[(4 * k4 + 2) * kBtXsStride + b] = v[r].z;
+      xs[(4 * k4 + 3) * kBtXsStride + b] = v[r].w;
+    }
   }
   if (a.fast[m]) {
     // one thread per (row, 16 codes): the row's 32 codes are contiguous
@@ -640,9 +658,21 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
   for (int r0 = R0; r0 < R1; r0 += kBtAdp2Rc) {
     const int rc = min(kBtAdp2Rc, R1 - r0);
     __syncthreads();
-    for (int idx = t; idx < rc * 16; idx += blockDim.x)
-      reinterpret_cast<float4*>(ms)[idx] =
-          reinterpret_cast<const float4*>(a.midT + (size_t)(a.off[m] + r0) * 64)[idx];
+    {
+      // rows r0 .. r0 + rc of mid (64 sessions each): up to 8 float4 per thread, loads issued together
+      const float4* src = reinterpret_cast<const float4*>(a.midT + (size_t)(a.off[m] + r0) * 64);
+      float4 v[kBtAdp2Rc * 16 / kBtThreads];
+#pragma unroll
+      for (int q = 0; q < kBtAdp2Rc * 16 / kBtThreads; ++q) {
+        const int idx = t + q * kBtThreads;
+        if (idx < rc * 16) v[q] = src[idx];
+      }
+#pragma unroll
+      for (int q = 0; q < kBtAdp2Rc * 16 / kBtThreads; ++q) {
+        const int idx = t + q * kBtThreads;
+        if (idx < rc * 16) reinterpret_cast<float4*>(ms)[idx] = v[q];
+      }
+    }
     if (a.fast[m]) {
       for (int idx = t; idx < rc * 4; idx += blockDim.x) {
         const int r = idx >> 2, p = idx & 3;

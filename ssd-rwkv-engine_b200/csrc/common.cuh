@@ -48,6 +48,12 @@ __device__ __forceinline__ uint4 ldg_stream16(const void* p) {
   return r;
 }
 
+__device__ __forceinline__ uint32_t ldg_stream4(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+
 __device__ __forceinline__ float2 ldg_f2(const void* p) {
   return __ldg(reinterpret_cast<const float2*>(p));
 }

@@ -103,42 +103,84 @@ __device__ __forceinline__ float lut2_pick(uint32_t lo, uint32_t hi, uint32_t co
   return __half2float(__ushort_as_half((unsigned short)(__byte_perm(word, 0u, sel) & 0xffffu)));
 }
 
+// PRMT selector for a nibble of codes (two 2-bit codes, LSB first): bytes
+// 2c0, 2c0 + 1, 2c1, 2c1 + 1 of the 8-byte record {lo, hi}, i.e. centroids c0
+// and c1 as one half2.  0x1010 + 0x22 * (c0 + 256 c1).
+__host__ __device__ constexpr uint32_t lut2_nibble_sel(uint32_t n) {
+  return 0x1010u + 0x22u * ((n & 3u) | ((n & 0xCu) << 6));
+}
+
 // Rows [r0, r1) of a TR2\x04 W (fast-path layout: group >= 64, power of two,
-// row-aligned).  A lane's 16-byte code chunk covers 64 weights of one group.
+// row-aligned).  Lane l of a warp takes 32-bit code words u = l, l + 32, ...
+// of the row (16 weights each; 128 contiguous bytes per warp load; four words
+// per row in flight per lane) and the
+// matching 16 inputs as four float4 (contiguous across lanes: no bank
+// conflicts), reused for the warp's RPW rows.  Two codes at a time become a
+// half2 of centroids with one byte permute (selector per nibble from a 16-entry
+// shared table) and two FMAs in fp32; the centroids are the record's exact fp16
+// values.
 template <int RPW, class Epi>
 __device__ __forceinline__ void lut2_rows(const PackedView& W, int lg, const float* sx, int r0, int r1,
                                           Epi epi) {
+  __shared__ uint32_t s_sel[16];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int K = W.cols, nchunk = K >> 6;  // 64 weights per chunk
-  const int gshift = lg - 6;
+  if (lane < 16) s_sel[lane] = lut2_nibble_sel((uint32_t)lane);  // every warp writes the same values
+  __syncwarp();
+  const int K = W.cols, nword = K >> 4;  // 16 weights per code word
+  const int wshift = lg - 4;             // code words per group = 2^wshift
   const int gpr = K >> lg;
+  const uint32_t* codes = reinterpret_cast<const uint32_t*>(W.payload);
+  const uint2* recs = reinterpret_cast<const uint2*>(W.meta);
+  const float4* sx4 = reinterpret_cast<const float4*>(sx);
   for (int rb = r0 + warp * RPW; rb < r1; rb += nw * RPW) {
-    float acc[RPW];
+    float acc0[RPW], acc1[RPW];
+    int row[RPW];
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) acc[i] = 0.f;
-    for (int c = lane; c < nchunk; c += 32) {
-      const float* xs = sx + (c << 6);
+    for (int i = 0; i < RPW; ++i) {
+      acc0[i] = acc1[i] = 0.f;
+      row[i] = min(rb + i, r1 - 1);
+    }
+    // four code words per lane and row (u0, u0 + 32, u0 + 64, u0 + 96) are
+    // loaded before any is used: 16 bytes per lane and row in flight
+    for (int u0 = lane; u0 < nword; u0 += 128) {
+      uint32_t w[RPW][4];
+      uint2 rec[RPW][4];
 #pragma unroll
-      for (int i = 0; i < RPW; ++i) {
-        int row = min(rb + i, r1 - 1);
-        uint4 q = ldg_stream16(W.payload + ((size_t)row * K >> 2) + (c << 4));
-        uint2 rec = __ldg(reinterpret_cast<const uint2*>(W.meta) + (size_t)row * gpr + (c >> gshift));
-        uint32_t words[4] = {q.x, q.y, q.z, q.w};
-        float a = 0.f;
+      for (int j = 0; j < 4; ++j) {
+        const int u = u0 + 32 * j;
 #pragma unroll
-        for (int wv = 0; wv < 4; ++wv) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            uint32_t code = (words[wv] >> (2 * j)) & 3u;
-            a = fmaf(lut2_pick(rec.x, rec.y, code), xs[wv * 16 + j], a);
+        for (int i = 0; i < RPW; ++i) {
+          w[i][j] = 0u;
+          rec[i][j] = make_uint2(0u, 0u);
+          if (u < nword) {
+            w[i][j] = ldg_stream4(codes + (size_t)row[i] * nword + u);
+            rec[i][j] = __ldg(recs + (size_t)row[i] * gpr + (u >> wshift));
           }
         }
-        acc[i] += a;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int u = u0 + 32 * j;
+        if (u >= nword) break;
+        const float4 xa = sx4[4 * u], xb = sx4[4 * u + 1], xc = sx4[4 * u + 2], xd = sx4[4 * u + 3];
+        const float xv[16] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w,
+                              xc.x, xc.y, xc.z, xc.w, xd.x, xd.y, xd.z, xd.w};
+#pragma unroll
+        for (int i = 0; i < RPW; ++i) {
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            const uint32_t sel = s_sel[(w[i][j] >> (4 * p)) & 15u];
+            const uint32_t h2 = __byte_perm(rec[i][j].x, rec[i][j].y, sel);
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2));
+            acc0[i] = fmaf(f.x, xv[2 * p], acc0[i]);
+            acc1[i] = fmaf(f.y, xv[2 * p + 1], acc1[i]);
+          }
+        }
       }
     }
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
-      float v = warp_sum(acc[i]);
+      const float v = warp_sum(acc0[i] + acc1[i]);
       if (lane == 0 && rb + i < r1) epi(rb + i, v);
     }
   }
@@ -164,7 +206,7 @@ __device__ __forceinline__ void packed_rows(const PackedView& W, int mode, int l
   if (mode == 1) {
     sg8_rows<2>(W, lg, sx, sxc, r0, r1, epi);
   } else if (mode == 2) {
-    lut2_rows<2>(W, lg, sx, r0, r1, epi);
+    lut2_rows<4>(W, lg, sx, r0, r1, epi);
   } else {
     generic_rows(W, sx, r0, r1, epi);
   }
