@@ -329,7 +329,8 @@ def run_tp(args, dev, stream, world: int, rank: int) -> dict:
         plan = tp.plan(shape, rank, world)
         local = synth.make_pack_streaming(shape, SEED + 7, dev, policy="sg8",
                                           transform=lambda n, e: tp.shard_entry(n, e, plan))
-        eng = tp.B200TPBatchEngine(local, nb, device=dev, shard_plan=plan, use_graph=True)
+        eng = tp.B200TPBatchEngine(local, nb, device=dev, shard_plan=plan, use_graph=True,
+                                   exchange=args.tp_exchange)
     else:
         local = synth.make_pack_streaming(shape, SEED + 7, dev, policy="sg8")
         eng = B200BatchEngine(local, nb, device=dev)
@@ -381,6 +382,7 @@ def run_tp(args, dev, stream, world: int, rank: int) -> dict:
             "steps": args.tp_steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "gpu_launches": launches * args.tp_steps,
             "collectives_per_step": (2 * L + 1) if world > 1 else 0,
+            "exchange": args.tp_exchange if world > 1 else None,
             "allreduce_bytes": nb * C * 4 if world > 1 else 0,
             "parallelism": f"tp{world}" if world > 1 else "single GPU (unsplit)",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * world, "unit": "GB/s",
@@ -446,6 +448,8 @@ def main() -> None:
                     help="tensor-parallel leg: model split over all ranks")
     ap.add_argument("--tp-sessions", type=int, default=8, help="tensor-parallel leg sessions (0: skip the leg)")
     ap.add_argument("--tp-steps", type=int, default=32)
+    ap.add_argument("--tp-exchange", default="nccl", choices=["p2p", "nccl"],
+                    help="tensor-parallel exchange: the engine's peer-memory kernels or NCCL through the host callback")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -302,9 +302,26 @@ typedef struct rwkvb_tp_desc {
   int32_t vocab_offset;      /* first vocabulary row of this rank's head shard */
   rwkvb_collective_fn collective;
   void* user;
+  /* Optional (all ranks or none; size <= 8): peer[r] = rank r's exchange buffer
+   * (rwkvb_ipc_alloc on rank r, rwkvb_ipc_open elsewhere; peer[rank] is this
+   * rank's own), rwkvb_batch_tp_exchange_bytes bytes each.  When set, the
+   * all-reduces and the argmax gather run in the engine's own kernels over
+   * NVLink -- plain peer loads and stores, epoch flags with bounded waits
+   * (RWKVB_ETIMEOUT from the next synchronising call when a peer does not
+   * arrive), every rank summing in rank order -- and `collective` is unused. */
+  void* const* peer;
 } rwkvb_tp_desc;
 int rwkvb_batch_create_tp(const rwkvb_model_desc* local, int32_t batch, const rwkvb_tp_desc* tp, uint32_t flags,
                           rwkvb_batch** out);
+/* Bytes of one rank's exchange buffer for rwkvb_tp_desc.peer. */
+int rwkvb_batch_tp_exchange_bytes(const rwkvb_model_desc* local, int32_t batch, uint64_t* bytes);
+/* Device memory other processes of this node can map (CUDA IPC), zeroed:
+ * `handle` receives 64 opaque bytes to pass to them. */
+int rwkvb_ipc_alloc(uint64_t bytes, void** dev_ptr, uint8_t* handle);
+int rwkvb_ipc_free(void* dev_ptr);
+/* Map another process's rwkvb_ipc_alloc buffer into this one (current device). */
+int rwkvb_ipc_open(const uint8_t* handle, void** dev_ptr);
+int rwkvb_ipc_close(void* dev_ptr);
 /* Record the token step as a CUDA graph now (once; a no-op without graphs),
  * instead of at the first step.  Nothing runs.  Under tensor parallelism every
  * rank calls it and the ranks agree that all captures succeeded before any

@@ -387,6 +387,7 @@ struct BtEmbedArgs {
   int* step;       // incremented once per step (by block 0)
   int* err;
   int C, V;
+  unsigned long long* epoch;  // tensor-parallel exchange epoch (incremented once per step), or null
 };
 
 __global__ void __launch_bounds__(kBtThreads) bt_embed_kernel(BtEmbedArgs a) {
@@ -400,7 +401,10 @@ __global__ void __launch_bounds__(kBtThreads) bt_embed_kernel(BtEmbedArgs a) {
     if (threadIdx.x == 0) atomicOr(a.err, kErrToken);
     tok = 0;
   }
-  if (b == 0 && threadIdx.x == 0) *a.step += 1;
+  if (b == 0 && threadIdx.x == 0) {
+    *a.step += 1;
+    if (a.epoch) *a.epoch += 1;
+  }
   for (int i = threadIdx.x; i < C; i += blockDim.x) bt_sm[i] = packed_at(a.emb, tok, i);
   __syncthreads();
   bt_layer_norm(bt_sm, a.ln0_w, a.ln0_b, C, red);
@@ -1307,6 +1311,153 @@ __global__ void bt_argmax_merge_kernel(const float2* all, int ranks, int nb, int
 
 }  // namespace rwkvb
 
+namespace rwkvb {
+
+// --------------------------------------------- tensor-parallel peer exchange
+// Every rank owns one exchange buffer (CUDA IPC-mapped into the other ranks'
+// processes), identically laid out on every rank:
+//   flags [ninst][kBtMaxRanks][kBtXCtas] u32: written by the peers (epoch)
+//   data  [2 L][nb][C] f32: this rank's folded partial projection per all-reduce
+//   amax  [nb] float2: this rank's per-session (best logit, global index bits)
+// An all-reduce (instance i): every CTA folds its chunk of this rank's GEMM
+// pieces into data[i], releases flags[i][rank][cta] = epoch in every peer,
+// waits (bounded) until every peer released flags[i][peer][cta], and sums the
+// chunk over all ranks in rank order -- the same value on every rank.  Peers'
+// data are read with plain loads through the IPC mapping (no multicast).
+// A slot is rewritten one step later only after every peer has released a later
+// instance of that step, i.e. after the peer has finished reading it.
+constexpr int kBtMaxRanks = 8;
+constexpr int kBtXCtas = 128;
+constexpr int kBtXThreads = 256;
+
+struct BtXPeers {
+  char* base[kBtMaxRanks];  // exchange buffer of rank r as mapped in this process
+};
+
+struct BtXLayout {
+  size_t flags = 0, data = 0, amax = 0, bytes = 0;
+  int ninst = 0;
+};
+
+inline BtXLayout bt_x_layout(int L, int nb, int C) {
+  BtXLayout x;
+  x.ninst = 2 * L + 1;
+  x.flags = 0;
+  x.data = ((size_t)x.ninst * kBtMaxRanks * kBtXCtas * 4 + 255) & ~size_t(255);
+  x.amax = x.data + (((size_t)2 * L * nb * C * 4 + 255) & ~size_t(255));
+  x.bytes = x.amax + (((size_t)nb * 8 + 255) & ~size_t(255));
+  return x;
+}
+
+__device__ __forceinline__ void bt_st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t bt_ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t* bt_x_flag(char* base, size_t flags_off, int inst, int src, int cta) {
+  return reinterpret_cast<uint32_t*>(base + flags_off) + ((size_t)inst * kBtMaxRanks + src) * kBtXCtas + cta;
+}
+
+// Thread 0: release this CTA's flag of instance `inst` in every peer, then wait
+// (bounded) for every peer's flag; false when a wait gave up (error word set).
+__device__ bool bt_x_handshake(const BtXPeers& P, size_t flags_off, int inst, int cta, int rank, int size, uint32_t ep,
+                               uint32_t spin_limit, int* err) {
+  __threadfence_system();
+  for (int r = 0; r < size; ++r)
+    if (r != rank) bt_st_release_sys(bt_x_flag(P.base[r], flags_off, inst, rank, cta), ep);
+  for (int r = 0; r < size; ++r) {
+    if (r == rank) continue;
+    const uint32_t* f = bt_x_flag(P.base[rank], flags_off, inst, r, cta);
+    uint32_t i = 0;
+    while (bt_ld_acquire_sys(f) != ep) {
+      if (++i > spin_limit) {
+        atomicOr(err, kErrTimeout);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+struct BtXReduceArgs {
+  BtXPeers peers;
+  const float* part;  // this rank's GEMM pieces [pieces][nb][C]
+  BtPieces pp;
+  float* out;         // [nb][C]: the sum over ranks
+  const unsigned long long* epoch;
+  int* err;
+  size_t flags_off, data_off;
+  int nb, C, rank, size, inst;
+  uint32_t spin_limit;
+};
+
+__global__ void __launch_bounds__(kBtXThreads) bt_xreduce_kernel(BtXReduceArgs a) {
+  __shared__ int s_ok;
+  const int n = a.nb * a.C, c = blockIdx.x;
+  const int e0 = (int)((long long)n * c / kBtXCtas), e1 = (int)((long long)n * (c + 1) / kBtXCtas);
+  const uint32_t ep = (uint32_t)*a.epoch;
+  float* mine = reinterpret_cast<float*>(a.peers.base[a.rank] + a.data_off) + (size_t)a.inst * n;
+  for (int i = e0 + (int)threadIdx.x; i < e1; i += blockDim.x) {
+    const int b = i / a.C, col = i - b * a.C;
+    mine[i] = bt_fold(a.part, a.pp, a.nb, a.C, b, col);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    s_ok = bt_x_handshake(a.peers, a.flags_off, a.inst, c, a.rank, a.size, ep, a.spin_limit, a.err) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  for (int i = e0 + (int)threadIdx.x; i < e1; i += blockDim.x) {
+    float v = 0.f;
+    for (int r = 0; r < a.size; ++r)
+      v += __ldcg(reinterpret_cast<const float*>(a.peers.base[r] + a.data_off) + (size_t)a.inst * n + i);
+    a.out[i] = v;
+  }
+}
+
+struct BtXArgmaxArgs {
+  BtXPeers peers;
+  const unsigned long long* epoch;
+  int* err;
+  int *tok, *hist;
+  const int* step;
+  size_t flags_off, amax_off;
+  int nb, rank, size, inst, hist_cap;
+  uint32_t spin_limit;
+};
+
+// One CTA: every rank's per-session bests (written to its own amax slot by
+// bt_argmax_kernel) merged first-maximum-wins in rank order.
+__global__ void __launch_bounds__(kBtXThreads) bt_xargmax_kernel(BtXArgmaxArgs a) {
+  __shared__ int s_ok;
+  const uint32_t ep = (uint32_t)*a.epoch;
+  if (threadIdx.x == 0)
+    s_ok = bt_x_handshake(a.peers, a.flags_off, a.inst, 0, a.rank, a.size, ep, a.spin_limit, a.err) ? 1 : 0;
+  __syncthreads();
+  if (!s_ok) return;
+  const int st = *a.step;
+  for (int b = threadIdx.x; b < a.nb; b += blockDim.x) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < a.size; ++r) {
+      const float2 c = __ldcg(reinterpret_cast<const float2*>(a.peers.base[r] + a.amax_off) + b);
+      const int ci = __float_as_int(c.y);
+      if (c.x > best || (c.x == best && ci < bi)) {
+        best = c.x;
+        bi = ci;
+      }
+    }
+    if (bi == 0x7fffffff) bi = 0;
+    a.tok[b] = bi;
+    a.hist[(size_t)((st % a.hist_cap + a.hist_cap) % a.hist_cap) * a.nb + b] = bi;
+  }
+}
+
+}  // namespace rwkvb
+
 // ------------------------------------------------------------ host engine
 namespace rwkvb {
 namespace {
@@ -1398,6 +1549,11 @@ struct rwkvb_batch {
   void* collective_user = nullptr;
   float *ored = nullptr, *vred = nullptr;
   float2 *amax_loc = nullptr, *amax_all = nullptr;
+  // peer-memory exchange instead of the collective callback (tp->peer set)
+  bool xp = false;
+  rwkvb::BtXPeers xpeers{};
+  rwkvb::BtXLayout xl;
+  unsigned long long* epoch = nullptr;
 };
 
 namespace rwkvb {
@@ -1496,18 +1652,50 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
   if (st == RWKVB_OK) st = bg_launch(e->head, e->g_head, e->smem_bg, s, e->pdl);
   if (st != RWKVB_OK) return st;
   const bool tp = e->tp_size > 1;
+  float2* loc = !tp ? nullptr
+                    : (e->xp ? reinterpret_cast<float2*>(e->xpeers.base[e->tp_rank] + e->xl.amax) : e->amax_loc);
   bt_go(e->pdl, bt_argmax_kernel, dim3(nb), dim3(1024), 0, s, e->logits, e->part_head, e->pp_head, nb, e->V, e->tok, e->hist, e->step,
-                                       e->hist_cap, e->V0, tp ? e->amax_loc : nullptr);
+                                       e->hist_cap, e->V0, loc);
   st = cuda_status(cudaGetLastError());
   if (st != RWKVB_OK || !tp) return st;
+  if (e->xp) {
+    BtXArgmaxArgs x;
+    std::memset(&x, 0, sizeof(x));
+    x.peers = e->xpeers;
+    x.epoch = e->epoch;
+    x.err = e->err;
+    x.tok = e->tok, x.hist = e->hist, x.step = e->step;
+    x.flags_off = e->xl.flags, x.amax_off = e->xl.amax;
+    x.nb = nb, x.rank = e->tp_rank, x.size = e->tp_size, x.inst = e->xl.ninst - 1, x.hist_cap = e->hist_cap;
+    x.spin_limit = 1u << 20;  // about half a second of polling
+    bt_xargmax_kernel<<<1, kBtXThreads, 0, s>>>(x);
+    return cuda_status(cudaGetLastError());
+  }
   e->collective(1, e->amax_loc, e->amax_all, (int64_t)sizeof(float2) * nb, s, e->collective_user);
   bt_go(e->pdl, bt_argmax_merge_kernel, dim3((nb + 127) / 128), dim3(128), 0, s, e->amax_all, e->tp_size, nb, e->tok, e->hist, e->step,
                                                           e->hist_cap);
   return cuda_status(cudaGetLastError());
 }
 
-// Tensor parallel: fold a projection's pieces into `red` [nb][C] and all-reduce it.
-int bt_reduce(rwkvb_batch* e, float* red, const float* part, const BtPieces& pp, cudaStream_t s) {
+// Tensor parallel: fold a projection's pieces into `red` [nb][C] and all-reduce
+// it: in one peer-exchange kernel (instance `inst` of the step), or by the fold
+// kernel and the host's collective callback.
+int bt_reduce(rwkvb_batch* e, float* red, const float* part, const BtPieces& pp, cudaStream_t s, int inst) {
+  if (e->xp) {
+    BtXReduceArgs x;
+    std::memset(&x, 0, sizeof(x));
+    x.peers = e->xpeers;
+    x.part = part;
+    x.pp = pp;
+    x.out = red;
+    x.epoch = e->epoch;
+    x.err = e->err;
+    x.flags_off = e->xl.flags, x.data_off = e->xl.data;
+    x.nb = e->nb, x.C = e->C, x.rank = e->tp_rank, x.size = e->tp_size, x.inst = inst;
+    x.spin_limit = 1u << 20;  // about half a second of polling
+    bt_xreduce_kernel<<<kBtXCtas, kBtXThreads, 0, s>>>(x);
+    return cuda_status(cudaGetLastError());
+  }
   const int n = e->nb * e->C;
   bg_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(red, part, e->nb, e->C, pp.stage0, pp.G, pp.total, pp.ncta);
   const int st = cuda_status(cudaGetLastError());
@@ -1531,7 +1719,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     ++n;                                                                                     \
   } while (0)
   {
-    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, e->tok, e->x, e->step, e->err, C, e->Vfull};
+    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, e->tok, e->x, e->step, e->err, C, e->Vfull, e->xp ? e->epoch : nullptr};
     bt_go(e->pdl, bt_embed_kernel, dim3(nb), dim3(kBtThreads), sizeof(float) * C, s, a);
     BT_CHECK();
   }
@@ -1627,7 +1815,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     if (bg_launch(ly.o, e->g_o, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     if (tp) {
-      if (bt_reduce(e, e->ored, e->part_o, e->pp_o, s) != RWKVB_OK) return RWKVB_ECUDA;
+      if (bt_reduce(e, e->ored, e->part_o, e->pp_o, s, 2 * l) != RWKVB_OK) return RWKVB_ECUDA;
       ++n;
     }
     {
@@ -1647,7 +1835,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     if (bg_launch(ly.value, e->g_value, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     if (tp) {
-      if (bt_reduce(e, e->vred, e->part_val, e->pp_value, s) != RWKVB_OK) return RWKVB_ECUDA;
+      if (bt_reduce(e, e->vred, e->part_val, e->pp_value, s, 2 * l + 1) != RWKVB_OK) return RWKVB_ECUDA;
       ++n;
     }
   }
@@ -1818,7 +2006,7 @@ int bt_record_prefill(rwkvb_batch* e, cudaStream_t s) {
     if (st_ != RWKVB_OK) return st_;                \
   } while (0)
   {
-    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, f.tok, f.x, f.step, e->err, C, e->Vfull};
+    BtEmbedArgs a{e->emb, e->ln0_w, e->ln0_b, f.tok, f.x, f.step, e->err, C, e->Vfull, nullptr};
     bt_go(e->pdl, bt_embed_kernel, dim3(rows), dim3(kBtThreads), sizeof(float) * C, s, a);
     PF_CHECK();
   }
@@ -2012,8 +2200,8 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   if (L <= 0 || C <= 0 || F <= 0 || V <= 0 || N != 64 || C % 128 || F % 128 || V % 128 || Ca <= 0 || Ca % 128)
     return RWKVB_EUNSUPPORTED;
   if (!tp && (Ca != C || V != Vfull)) return RWKVB_EARG;
-  if (tp && (tp->size < 2 || tp->rank < 0 || tp->rank >= tp->size || !tp->collective || tp->vocab_offset < 0 ||
-             tp->vocab_offset + V > Vfull))
+  if (tp && (tp->size < 2 || tp->rank < 0 || tp->rank >= tp->size || (!tp->collective && !tp->peer) ||
+             tp->vocab_offset < 0 || tp->vocab_offset + V > Vfull || (tp->peer && tp->size > kBtMaxRanks)))
     return RWKVB_EARG;
   if (!bt_desc_ok(m->emb, Vfull, C) || !bg_matrix_ok(m->head) || m->head.cols != C)
     return m->head.kind == RWKVB_KIND_SG8 ? RWKVB_EUNSUPPORTED : RWKVB_EARG;
@@ -2060,6 +2248,17 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   if (tp) {
     e->tp_rank = tp->rank, e->tp_size = tp->size, e->V0 = tp->vocab_offset;
     e->collective = tp->collective, e->collective_user = tp->user;
+    if (tp->peer) {
+      e->xp = true;
+      e->xl = bt_x_layout(L, batch, C);
+      for (int r = 0; r < tp->size; ++r) {
+        if (!tp->peer[r]) {
+          delete e;
+          return RWKVB_EARG;
+        }
+        e->xpeers.base[r] = static_cast<char*>(tp->peer[r]);
+      }
+    }
   }
   e->rw = rw, e->ra = ra, e->rg = rg, e->rv = rv, e->rtot = rw + ra + rg + rv;
   {
@@ -2124,6 +2323,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
       {(void**)&e->vred, 4 * nbC},
       {(void**)&e->amax_loc, 8 * (size_t)batch},
       {(void**)&e->amax_all, 8 * (size_t)batch * e->tp_size},
+      {(void**)&e->epoch, 16},
   };
   size_t total = 0;
   std::vector<size_t> offs;
@@ -2269,6 +2469,45 @@ extern "C" int rwkvb_batch_create_tp(const rwkvb_model_desc* local, int32_t batc
                                      uint32_t flags, rwkvb_batch** out) {
   if (!tp) return RWKVB_EARG;
   return bt_create(local, batch, flags, tp, out);
+}
+
+extern "C" int rwkvb_batch_tp_exchange_bytes(const rwkvb_model_desc* local, int32_t batch, uint64_t* bytes) {
+  if (!local || !bytes || batch < 1 || batch > kBgMaxSessions) return RWKVB_EARG;
+  *bytes = (uint64_t)bt_x_layout(local->n_layer, batch, local->n_embd).bytes;
+  return RWKVB_OK;
+}
+
+extern "C" int rwkvb_ipc_alloc(uint64_t bytes, void** dev_ptr, uint8_t* handle) {
+  if (!dev_ptr || !handle || bytes == 0) return RWKVB_EARG;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return RWKVB_EALLOC;
+  }
+  cudaIpcMemHandle_t h;
+  int st = cuda_status(cudaMemset(p, 0, bytes));
+  if (st == RWKVB_OK) st = cuda_status(cudaIpcGetMemHandle(&h, p));
+  if (st != RWKVB_OK) {
+    cudaFree(p);
+    return st;
+  }
+  static_assert(sizeof(h) == 64, "CUDA IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return RWKVB_OK;
+}
+
+extern "C" int rwkvb_ipc_free(void* dev_ptr) { return dev_ptr ? cuda_status(cudaFree(dev_ptr)) : RWKVB_EARG; }
+
+extern "C" int rwkvb_ipc_open(const uint8_t* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return RWKVB_EARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+extern "C" int rwkvb_ipc_close(void* dev_ptr) {
+  return dev_ptr ? cuda_status(cudaIpcCloseMemHandle(dev_ptr)) : RWKVB_EARG;
 }
 
 extern "C" int rwkvb_batch_prepare(rwkvb_batch* e, void* stream) {

@@ -86,7 +86,8 @@ COLLECTIVE_ALLGATHER = 1
 
 class TPDesc(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int32), ("size", ctypes.c_int32), ("vocab_offset", ctypes.c_int32),
-                ("collective", COLLECTIVE_FN), ("user", ctypes.c_void_p)]
+                ("collective", COLLECTIVE_FN), ("user", ctypes.c_void_p),
+                ("peer", ctypes.POINTER(ctypes.c_void_p))]
 
 
 def native_lib_path() -> Path | None:
@@ -129,6 +130,11 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_batch_create": (ctypes.c_int, [P(ModelDesc), i32, u32, P(vp)]),
         "rwkvb_batch_create_tp": (ctypes.c_int, [P(ModelDesc), i32, P(TPDesc), u32, P(vp)]),
         "rwkvb_batch_prepare": (ctypes.c_int, [vp, vp]),
+        "rwkvb_batch_tp_exchange_bytes": (ctypes.c_int, [P(ModelDesc), i32, P(u64)]),
+        "rwkvb_ipc_alloc": (ctypes.c_int, [u64, P(vp), ctypes.c_char_p]),
+        "rwkvb_ipc_free": (ctypes.c_int, [vp]),
+        "rwkvb_ipc_open": (ctypes.c_int, [ctypes.c_char_p, P(vp)]),
+        "rwkvb_ipc_close": (ctypes.c_int, [vp]),
         "rwkvb_batch_destroy": (ctypes.c_int, [vp]),
         "rwkvb_batch_buffers": (ctypes.c_int, [vp, P(vp), P(vp), P(vp), P(vp)]),
         "rwkvb_batch_reset": (ctypes.c_int, [vp, vp]),

@@ -269,6 +269,51 @@ class TPCollective:
                 self.error = e
 
 
+class PeerExchange:
+    """One exchange buffer per rank, mapped into every rank's process (CUDA IPC
+    through the C ABI; the 64-byte handles travel through ``torch.distributed``).
+    ``peers`` is the ``rwkvb_tp_desc.peer`` array: rank r's buffer as mapped
+    here.  ``close`` is collective: every rank unmaps the others' buffers, then
+    frees its own after the others are done with it."""
+
+    def __init__(self, nbytes: int, group=None, device: torch.device | None = None):
+        self.lib = native.lib()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.size = dist.get_world_size(group)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        native.check(self.lib.rwkvb_ipc_alloc(int(nbytes), ctypes.byref(own), handle), "rwkvb_ipc_alloc")
+        self._own = own
+        mine = torch.tensor(list(handle.raw), dtype=torch.uint8, device=self.device)
+        allh = torch.empty(self.size * 64, dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(allh, mine, group=group)
+        raw = bytes(allh.cpu().numpy().tolist())
+        self._opened: list[ctypes.c_void_p] = []
+        self.peers = (ctypes.c_void_p * self.size)()
+        for r in range(self.size):
+            if r == self.rank:
+                self.peers[r] = own.value
+                continue
+            ptr = ctypes.c_void_p()
+            native.check(self.lib.rwkvb_ipc_open(raw[64 * r:64 * (r + 1)], ctypes.byref(ptr)), "rwkvb_ipc_open")
+            self._opened.append(ptr)
+            self.peers[r] = ptr.value
+
+    def close(self) -> None:
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every rank's kernels are done with every buffer
+        for ptr in self._opened:
+            self.lib.rwkvb_ipc_close(ptr)
+        self._opened = []
+        dist.barrier(group=self.group)  # nobody maps this rank's buffer any more
+        self.lib.rwkvb_ipc_free(self._own)
+        self._own = None
+
+
 # --------------------------------------------------------------------------
 # engine
 # --------------------------------------------------------------------------
@@ -276,12 +321,15 @@ class B200TPBatchEngine:
     """``batch`` (<= 64) sessions of one SG8 RWKV-7 model decoded with the model
     split over the ranks of ``group`` (every rank constructs it with the same
     full pack, or with its own shard and ``plan``, and calls the same methods
-    with the same arguments).  Logits are this rank's vocabulary rows
+    with the same arguments; ``exchange="p2p"`` runs the all-reduces and the
+    argmax gather in the engine's own kernels over NVLink peer memory instead of
+    NCCL through the host callback).  Logits are this rank's vocabulary rows
     ``[plan.v0, plan.v1)``; ``logits_full`` gathers them.  Greedy ids are the
     same on every rank."""
 
     def __init__(self, pack, batch: int, *, group=None, device: torch.device | None = None,
-                 use_graph: bool = False, shard_plan: ShardPlan | None = None, collective: TPCollective | None = None):
+                 use_graph: bool = False, shard_plan: ShardPlan | None = None, collective: TPCollective | None = None,
+                 exchange: str = "nccl"):
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         if self.device.type != "cuda":
             raise ValueError("B200TPBatchEngine needs a CUDA device; there is no CPU path")
@@ -310,7 +358,20 @@ class B200TPBatchEngine:
             self.shape = s
             self._coll.warmup()
             self._cfn = native.COLLECTIVE_FN(self._coll.callback)
-            desc = native.TPDesc(self.rank, self.size, shard_plan.v0, self._cfn, None)
+            desc = native.TPDesc(self.rank, self.size, shard_plan.v0, self._cfn, None, None)
+            self.exchange = exchange
+            self._x = None
+            if exchange == "p2p":
+                # the all-reduces and the argmax gather run in the engine's own
+                # kernels over peer memory (no host callback, no NCCL)
+                nbytes = ctypes.c_uint64()
+                native.check(self.lib.rwkvb_batch_tp_exchange_bytes(ctypes.byref(self._model.md), self.batch,
+                                                                    ctypes.byref(nbytes)),
+                             "rwkvb_batch_tp_exchange_bytes")
+                self._x = PeerExchange(int(nbytes.value), group, self.device)
+                desc.peer = self._x.peers
+            elif exchange != "nccl":
+                raise ValueError(f"exchange must be 'nccl' or 'p2p', not {exchange!r}")
             h = ctypes.c_void_p()
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
             native.check(self.lib.rwkvb_batch_create_tp(ctypes.byref(self._model.md), self.batch,
@@ -352,14 +413,22 @@ class B200TPBatchEngine:
         native.check(status, what)
 
     def close(self) -> None:
+        """Release the engine; collective when the peer exchange is in use."""
         if getattr(self, "_h", None):
             torch.cuda.synchronize(self.device)
             self.lib.rwkvb_batch_destroy(self._h)
             self._h = None
+        if getattr(self, "_x", None) is not None:
+            self._x.close()
+            self._x = None
 
     def __del__(self):
+        # not collective: release the engine only (the exchange buffers are
+        # released by close(), which every rank calls, or at process exit)
         try:
-            self.close()
+            if getattr(self, "_h", None):
+                self.lib.rwkvb_batch_destroy(self._h)
+                self._h = None
         except Exception:
             pass
 

@@ -135,7 +135,8 @@ def _worker(rank: int, world: int, port: int, case: dict, q) -> None:
         shape, local, plan = _make_pack(case["preset"], case["seed"], rank, world)
         nb, length, n_new = case["nb"], case["length"], case["n_new"]
         prompts = [synth.seeded_prompt(length, shape.vocab, case["seed"] + 101 * b) for b in range(nb)]
-        eng = B200TPBatchEngine(local, nb, shard_plan=plan, use_graph=case.get("graph", False))
+        eng = B200TPBatchEngine(local, nb, shard_plan=plan, use_graph=case.get("graph", False),
+                                exchange=case.get("exchange", "nccl"))
         try:
             eng.prefill(prompts)
             first = eng.logits_full().argmax(dim=1).cpu().numpy()
@@ -269,8 +270,10 @@ def test_tp2_as_threads_on_one_gpu_matches_single_engine(case):
 
 
 @two_gpus
-@pytest.mark.parametrize("case", CASES + [dict(c, graph=True) for c in CASES],
-                         ids=["tiny", "7.2b-l4", "tiny-graph", "7.2b-l4-graph"])
+@pytest.mark.parametrize("case", CASES + [dict(c, graph=True) for c in CASES]
+                         + [dict(c, exchange="p2p") for c in CASES] + [dict(c, graph=True, exchange="p2p") for c in CASES],
+                         ids=["tiny", "7.2b-l4", "tiny-graph", "7.2b-l4-graph", "tiny-p2p", "7.2b-l4-p2p",
+                              "tiny-p2p-graph", "7.2b-l4-p2p-graph"])
 def test_tp2_matches_single_gpu_batched_engine(case):
     got = _run_tp(case)
     ref = _single(case)
@@ -285,4 +288,6 @@ def test_tp2_matches_single_gpu_batched_engine(case):
         # two all-reduces per layer and one all-gather per step (logits_full's
         # gathers are not counted); a CUDA graph issues them once, at capture
         steps = 1 if case.get("graph") else case["length"] + case["n_new"]
-        assert res["calls"] == steps * (2 * shape.n_layer + 1), (r, res["calls"])
+        # the peer exchange does not call back at all
+        expect = 0 if case.get("exchange") == "p2p" else steps * (2 * shape.n_layer + 1)
+        assert res["calls"] == expect, (r, res["calls"])
