@@ -448,7 +448,7 @@ def main() -> None:
                     help="tensor-parallel leg: model split over all ranks")
     ap.add_argument("--tp-sessions", type=int, default=8, help="tensor-parallel leg sessions (0: skip the leg)")
     ap.add_argument("--tp-steps", type=int, default=32)
-    ap.add_argument("--tp-exchange", default="nccl", choices=["p2p", "nccl"],
+    ap.add_argument("--tp-exchange", default="p2p", choices=["p2p", "nccl"],
                     help="tensor-parallel exchange: the engine's peer-memory kernels or NCCL through the host callback")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
