@@ -555,7 +555,15 @@ def main() -> None:
 
     batched = run_batched(batch_eng, args, shape, bpt, dev, stream, world, rank) if batch_eng is not None else None
     prefill = run_prefill(prefill_eng, args, shape, bpt, dev, stream, world, rank) if prefill_eng is not None else None
-    tpres = run_tp(args, dev, stream, world, rank) if args.tp_sessions > 0 else None
+    tpres = None
+    if args.tp_sessions > 0:
+        # the tensor-parallel leg must not take the line's other results with it:
+        # a failure there is reported in the line instead
+        try:
+            tpres = run_tp(args, dev, stream, world, rank)
+        except Exception as exc:  # noqa: BLE001
+            tpres = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            torch.cuda.synchronize(dev)
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -606,8 +614,10 @@ def main() -> None:
         print(json.dumps(res), flush=True)
     backend.close()
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        try:
+            dist.barrier()
+        finally:
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":
