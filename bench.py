@@ -203,7 +203,8 @@ def run_reference(args, shape, rank: int) -> dict:
 
 
 def run_batched(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) -> dict:
-    """The batched leg: ``args.sessions`` sessions decoded together (tcgen05 GEMMs).
+    """The batched leg: ``args.sessions`` sessions decoded together (tcgen05 GEMMs
+    for SG8 packs, CUDA-core products for TR2\x04 packs).
 
     One step = one token for every session.  Algorithmic bytes per step: the
     weights once (the batch-1 token bytes less its state traffic), plus the
@@ -255,7 +256,8 @@ def run_batched(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) 
     peak, peak_kind = _peaks()
     achieved = step_bytes / (ms_step / 1e3) / 1e9
     eng.close()
-    return {"metric": f"RWKV-7 {args.config} U8 decode tok/s (bs{nb})", "value": nb * world / (ms_step / 1e3),
+    codec = "U8" if args.policy == "sg8" else "LUT2"
+    return {"metric": f"RWKV-7 {args.config} {codec} decode tok/s (bs{nb})", "value": nb * world / (ms_step / 1e3),
             "unit": "tok/s", "sessions_per_gpu": nb, "steps": args.batch_steps, "warmup": args.warmup,
             "ms_per_step": ms_step, "gpu_launches": eng.launches_per_step * args.batch_steps,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -487,12 +489,12 @@ def main() -> None:
     eng = backend._engine
     cpu_pack = pack if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
     batch_eng = prefill_eng = None
-    if args.policy == "sg8" and (args.sessions > 0 or args.prefill_tokens > 0):
+    if args.sessions > 0 or (args.policy == "sg8" and args.prefill_tokens > 0):
         from rwkv_b200.engine import B200BatchEngine
 
         if args.sessions > 0:
             batch_eng = B200BatchEngine(backend._model, args.sessions, device=local)
-        if args.prefill_tokens > 0:
+        if args.policy == "sg8" and args.prefill_tokens > 0:
             prefill_eng = B200BatchEngine(backend._model, args.prefill_sessions, device=local)
     del pack
     provider.pack, provider._fused = {}, {}

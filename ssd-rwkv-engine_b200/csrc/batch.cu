@@ -1313,6 +1313,121 @@ __global__ void bt_argmax_merge_kernel(const float2* all, int ranks, int nb, int
 
 namespace rwkvb {
 
+// ------------------------------------------------ LUT2 batched product
+// y[b][n] = sum_k W[n][k] x[b][k] for a TR2\x04 W (2-bit codes, one 4-entry fp16
+// codebook per 64 consecutive elements, row-aligned groups) on the CUDA cores:
+// LUT2 centroids are not an affine code grid, so the integer tcgen05 product of
+// the SG8 path does not apply.  The batched engine's inputs are its digit rows
+// (x = c_f (X0 + X1/254 + X2/254^2) per 64-column group, stored X + 127), the
+// same rows the SG8 product reads; they are turned back into fp32 here.
+// A CTA owns 64 rows and a contiguous range of 64-column chunks (k split `ks`
+// ways); per chunk the 64 x 64 weight tile is decoded once into shared memory
+// and every thread accumulates a 4-row x 4-session register tile.  Output:
+// piece p (= the CTA's k split) of the engine's pieces layout [ks][nb][rows],
+// summed in piece order by the readers like the SG8 product's pieces.
+constexpr int kL2Rows = 64;
+constexpr int kL2Kc = 64;
+constexpr int kL2Threads = 256;
+constexpr int kL2Stride = 68;  // padded row stride of the shared tiles (float4 aligned)
+constexpr int kL2MaxJobs = 3;
+
+struct BtL2Job {
+  const uint32_t* codes;  // 2-bit codes, 16 per word, row-major
+  const uint2* recs;      // per 64-element group: 4 fp16 centroids
+  float* out;             // pieces [ks][nb][rows]
+  const uint8_t* dig;     // digit rows [3 bp + 1][K]
+  const float* cs;        // [K / 64][2 bp]: c_f, then sum x
+  int rows, K, ks, cta0;  // k splits; first CTA of the job
+};
+
+struct BtL2Args {
+  BtL2Job job[kL2MaxJobs];
+  int njobs, nb, bp;
+};
+
+__global__ void __launch_bounds__(kL2Threads) bt_l2gemm_kernel(BtL2Args a) {
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
+  __shared__ __align__(16) float ws[kL2Kc * kL2Stride];  // [k][row]
+  __shared__ __align__(16) float xs[kL2Kc * kL2Stride];  // [k][session]
+  int j = 0;
+  while (j + 1 < a.njobs && (int)blockIdx.x >= a.job[j + 1].cta0) ++j;
+  const BtL2Job J = a.job[j];
+  const int local = (int)blockIdx.x - J.cta0, tile = local / J.ks, piece = local - tile * J.ks;
+  const int nch = J.K / kL2Kc;
+  const int ch0 = (int)((long long)nch * piece / J.ks), ch1 = (int)((long long)nch * (piece + 1) / J.ks);
+  const int t = threadIdx.x, r0 = tile * kL2Rows;
+  const int rq = t & 15, bq = t >> 4;  // rows 4 rq .. +3, sessions 4 bq .. +3
+  const int drow = t & 63, dq = t >> 6;  // decode / staging: row or session, 16-column quarter
+  const int words = J.K >> 4;
+  float acc[4][4] = {};
+  for (int ch = ch0; ch < ch1; ++ch) {
+    const int k0 = ch * kL2Kc;
+    // weights: row drow, columns k0 + 16 dq .. +15 (one code word)
+    {
+      const int row = r0 + drow;
+      const uint32_t w = __ldg(J.codes + (size_t)row * words + (k0 >> 4) + dq);
+      const uint2 rec = __ldg(J.recs + (((size_t)row * J.K + k0) >> 6));
+      const float2 c01 = __half22float2(*reinterpret_cast<const __half2*>(&rec.x));
+      const float2 c23 = __half22float2(*reinterpret_cast<const __half2*>(&rec.y));
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const uint32_t c = (w >> (2 * u)) & 3u;
+        const float v = c == 0 ? c01.x : (c == 1 ? c01.y : (c == 2 ? c23.x : c23.y));
+        ws[(16 * dq + u) * kL2Stride + drow] = v;
+      }
+    }
+    // inputs: session drow, columns k0 + 16 dq .. +15, from the three digit rows
+    {
+      const int b = drow;
+      float xv[16];
+      if (b < a.nb) {
+        const uint4 d0 = *reinterpret_cast<const uint4*>(J.dig + (size_t)b * J.K + k0 + 16 * dq);
+        const uint4 d1 = *reinterpret_cast<const uint4*>(J.dig + (size_t)(a.bp + b) * J.K + k0 + 16 * dq);
+        const uint4 d2 = *reinterpret_cast<const uint4*>(J.dig + (size_t)(2 * a.bp + b) * J.K + k0 + 16 * dq);
+        const float cf = J.cs[(size_t)ch * 2 * a.bp + b];
+        const uint32_t w0[4] = {d0.x, d0.y, d0.z, d0.w}, w1[4] = {d1.x, d1.y, d1.z, d1.w},
+                       w2[4] = {d2.x, d2.y, d2.z, d2.w};
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const float x0 = (float)(int)((w0[u >> 2] >> (8 * (u & 3))) & 0xffu) - 127.f;
+          const float x1 = (float)(int)((w1[u >> 2] >> (8 * (u & 3))) & 0xffu) - 127.f;
+          const float x2 = (float)(int)((w2[u >> 2] >> (8 * (u & 3))) & 0xffu) - 127.f;
+          xv[u] = cf * (x0 + (x1 + x2 * kInv254) * kInv254);
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) xv[u] = 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) xs[(16 * dq + u) * kL2Stride + b] = xv[u];
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kL2Kc; ++k) {
+      const float4 wv = *reinterpret_cast<const float4*>(ws + k * kL2Stride + 4 * rq);
+      const float4 xv = *reinterpret_cast<const float4*>(xs + k * kL2Stride + 4 * bq);
+      const float wr[4] = {wv.x, wv.y, wv.z, wv.w}, xr[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[i][q] = fmaf(wr[i], xr[q], acc[i][q]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int b = 4 * bq + q;
+    if (b >= a.nb) continue;
+    float* o = J.out + ((size_t)piece * a.nb + b) * J.rows + r0 + 4 * rq;
+    *reinterpret_cast<float4*>(o) = make_float4(acc[0][q], acc[1][q], acc[2][q], acc[3][q]);
+  }
+}
+
+}  // namespace rwkvb
+
+namespace rwkvb {
+
 // --------------------------------------------- tensor-parallel peer exchange
 // Every rank owns one exchange buffer (CUDA IPC-mapped into the other ranks'
 // processes), identically laid out on every rank:
@@ -1468,6 +1583,7 @@ struct BtLayer {
   const float* mix[6];
   const float *w0, *a0, *v0, *k_k, *k_a, *r_k, *lnx_w, *lnx_b, *ffn_x_k;
   BgArgs rkv, o, key, value;
+  BtL2Args l2rkv, l2o, l2key, l2value;  // LUT2 engines: CUDA-core products instead
   rwkvb_packed big[6];  // att r, k, v, o, ffn key, ffn value (for further launch plans)
 };
 
@@ -1516,6 +1632,9 @@ struct rwkvb_batch {
   int nb = 0, bp = 0, nrows = 0, lfk = 7, group = 128;
   int L = 0, C = 0, H = 0, F = 0, V = 0, rw = 0, ra = 0, rg = 0, rv = 0, rtot = 0;
   int adp_splits = 0, hist_cap = 1024;
+  bool lut2 = false;     // TR2\x04 projections and head: CUDA-core products (bt_l2gemm_kernel)
+  rwkvb::BtL2Args l2head;
+  int l2g_rkv = 0, l2g_o = 0, l2g_key = 0, l2g_value = 0, l2g_head = 0;
   bool pdl = true;       // programmatic dependent launch between the step's kernels
   rwkvb::BtAdpPlan adp;  // adapter second-stage chunks
   std::vector<rwkvb::BtLayer> layers;
@@ -1604,6 +1723,55 @@ BtPieces bt_pieces(const BgArgs& a, int job, int grid) {
   return p;
 }
 
+// LUT2 batched product (bt_l2gemm_kernel): TR2\x04 row-major, 64-element groups.
+bool bt_l2_ok(const rwkvb_packed& w) {
+  if (w.kind != RWKVB_KIND_LUT2_F16 || w.group_size != 64 || !w.data) return false;
+  if (w.rows <= 0 || w.cols <= 0 || w.rows % kL2Rows || w.cols % kL2Kc) return false;
+  const PackedView v = make_view(w);
+  const uint64_t n = (uint64_t)w.rows * w.cols, need = 8 + n / 64 * 8 + n / 4;
+  return w.bytes >= need && (reinterpret_cast<uintptr_t>(v.payload) & 3u) == 0 &&
+         (reinterpret_cast<uintptr_t>(v.meta) & 7u) == 0;
+}
+
+// Launch plan of one LUT2 product launch over `njobs` matrices; the k split
+// gives about two CTAs per SM and at most `pmax` pieces.
+int bt_l2_setup(BtL2Args* a, const rwkvb_packed* const* w, float* const* out, const uint8_t* const* dig,
+                const float2* const* cs, int njobs, int nb, int sms, int pmax, int* grid, int* ks_out) {
+  if (njobs < 1 || njobs > kL2MaxJobs || nb < 1 || nb > kBgMaxSessions) return RWKVB_EARG;
+  std::memset(a, 0, sizeof(*a));
+  a->njobs = njobs, a->nb = nb, a->bp = bg_padded_sessions(nb);
+  int tiles = 0, nch = 1 << 30;
+  for (int j = 0; j < njobs; ++j) {
+    if (!bt_l2_ok(*w[j])) return RWKVB_EUNSUPPORTED;
+    tiles += w[j]->rows / kL2Rows;
+    nch = std::min(nch, w[j]->cols / kL2Kc);
+  }
+  const int ks = std::max(1, std::min({(2 * sms + tiles - 1) / tiles, nch, pmax}));
+  int cta = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const PackedView v = make_view(*w[j]);
+    BtL2Job& J = a->job[j];
+    J.codes = reinterpret_cast<const uint32_t*>(v.payload);
+    J.recs = reinterpret_cast<const uint2*>(v.meta);
+    J.out = out[j];
+    J.dig = dig[j];
+    J.cs = reinterpret_cast<const float*>(cs[j]);
+    J.rows = w[j]->rows, J.K = w[j]->cols, J.ks = ks, J.cta0 = cta;
+    cta += (w[j]->rows / kL2Rows) * ks;
+  }
+  *grid = cta;
+  *ks_out = ks;
+  return RWKVB_OK;
+}
+
+// Pieces of a LUT2 product: every row's tile has `ks` pieces in k-split order.
+BtPieces bt_l2_pieces(int ks) {
+  BtPieces p;
+  p.stage0 = 0, p.G = ks, p.total = 1 << 20, p.ncta = 1 << 20;
+  p.np = nullptr;
+  return p;
+}
+
 // Tabulate the per-tile piece counts of each (pieces, output rows) job into
 // one device buffer (*dev, owned by the caller) and point the jobs at it.
 int bt_np_upload(const std::vector<std::pair<BtPieces*, int>>& jobs, int** dev) {
@@ -1649,7 +1817,9 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
   a.C = C, a.nb = nb, a.bp = e->bp, a.lfk = e->lfk;
   bt_go(e->pdl, bt_in_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
   int st = cuda_status(cudaGetLastError());
-  if (st == RWKVB_OK) st = bg_launch(e->head, e->g_head, e->smem_bg, s, e->pdl);
+  if (st == RWKVB_OK)
+    st = e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_head), dim3(kL2Threads), 0, s, e->l2head)
+                 : bg_launch(e->head, e->g_head, e->smem_bg, s, e->pdl);
   if (st != RWKVB_OK) return st;
   const bool tp = e->tp_size > 1;
   float2* loc = !tp ? nullptr
@@ -1745,7 +1915,9 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       bt_go(e->pdl, bt_in_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
       BT_CHECK();
     }
-    if (bg_launch(ly.rkv, e->g_rkv, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
+    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_rkv), dim3(kL2Threads), 0, s, ly.l2rkv)
+                 : bg_launch(ly.rkv, e->g_rkv, e->smem_bg, s, e->pdl)) != RWKVB_OK)
+      return RWKVB_ECUDA;
     ++n;
     const int nm = l0 ? 3 : 4;
     {
@@ -1812,7 +1984,9 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     }
     if (bg_digits(e->dig_y, e->cs_y, e->att_y, Ca, Ca, nb, e->group, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
-    if (bg_launch(ly.o, e->g_o, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
+    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_o), dim3(kL2Threads), 0, s, ly.l2o)
+                 : bg_launch(ly.o, e->g_o, e->smem_bg, s, e->pdl)) != RWKVB_OK)
+      return RWKVB_ECUDA;
     ++n;
     if (tp) {
       if (bt_reduce(e, e->ored, e->part_o, e->pp_o, s, 2 * l) != RWKVB_OK) return RWKVB_ECUDA;
@@ -1824,7 +1998,9 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       bt_go(e->pdl, bt_ffn_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * C, s, a);
       BT_CHECK();
     }
-    if (bg_launch(ly.key, e->g_key, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
+    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_key), dim3(kL2Threads), 0, s, ly.l2key)
+                 : bg_launch(ly.key, e->g_key, e->smem_bg, s, e->pdl)) != RWKVB_OK)
+      return RWKVB_ECUDA;
     ++n;
     {
       const int warps = nb * (e->F >> e->lfk);
@@ -1832,7 +2008,9 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
                                                            e->bp, e->lfk);
       BT_CHECK();
     }
-    if (bg_launch(ly.value, e->g_value, e->smem_bg, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
+    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_value), dim3(kL2Threads), 0, s, ly.l2value)
+                 : bg_launch(ly.value, e->g_value, e->smem_bg, s, e->pdl)) != RWKVB_OK)
+      return RWKVB_ECUDA;
     ++n;
     if (tp) {
       if (bt_reduce(e, e->vred, e->part_val, e->pp_value, s, 2 * l + 1) != RWKVB_OK) return RWKVB_ECUDA;
@@ -1897,6 +2075,7 @@ int bt_check_err(rwkvb_batch* e, cudaStream_t s) {
 int bt_prefill_setup(rwkvb_batch* e) {
   if (e->pf) return RWKVB_OK;
   if (e->tp_size > 1) return RWKVB_EUNSUPPORTED;  // positions then run as (tensor-parallel) decode steps
+  if (e->lut2) return RWKVB_EUNSUPPORTED;          // LUT2 engines: every position as a decode step
   const int P = kBgMaxSessions / e->nb;
   if (P < 2) return RWKVB_EUNSUPPORTED;
   BtPrefill* f = new (std::nothrow) BtPrefill();
@@ -2203,8 +2382,12 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   if (tp && (tp->size < 2 || tp->rank < 0 || tp->rank >= tp->size || (!tp->collective && !tp->peer) ||
              tp->vocab_offset < 0 || tp->vocab_offset + V > Vfull || (tp->peer && tp->size > kBtMaxRanks)))
     return RWKVB_EARG;
-  if (!bt_desc_ok(m->emb, Vfull, C) || !bg_matrix_ok(m->head) || m->head.cols != C)
-    return m->head.kind == RWKVB_KIND_SG8 ? RWKVB_EUNSUPPORTED : RWKVB_EARG;
+  // projections and head all SG8 (tcgen05 products) or all TR2\x04 (CUDA-core products)
+  const bool l2 = m->head.kind == RWKVB_KIND_LUT2_F16;
+  auto big_ok = [&](const rwkvb_packed& w) { return l2 ? bt_l2_ok(w) : bg_matrix_ok(w); };
+  if (l2 && tp) return RWKVB_EUNSUPPORTED;
+  if (!bt_desc_ok(m->emb, Vfull, C) || !big_ok(m->head) || m->head.cols != C)
+    return (m->head.kind == RWKVB_KIND_SG8 || l2) ? RWKVB_EUNSUPPORTED : RWKVB_EARG;
   if (!m->ln0_w || !m->ln0_b || !m->ln_out_w || !m->ln_out_b) return RWKVB_EARG;
   const rwkvb_layer_desc& l0 = m->layers[0];
   const int rw = l0.w1.cols, ra = l0.a1.cols, rg = l0.g1.cols;
@@ -2214,7 +2397,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
     const rwkvb_layer_desc& s = m->layers[i];
     const rwkvb_packed* big[] = {&s.att_r, &s.att_k, &s.att_v, &s.att_o, &s.ffn_key, &s.ffn_value};
     for (const rwkvb_packed* p : big)
-      if (!bg_matrix_ok(*p) || p->group_size != group) return RWKVB_EUNSUPPORTED;
+      if (!big_ok(*p) || p->group_size != group) return RWKVB_EUNSUPPORTED;
     if (s.att_r.rows != Ca || s.att_r.cols != C || s.att_k.rows != Ca || s.att_k.cols != C || s.att_v.rows != Ca ||
         s.att_v.cols != C || s.att_o.rows != C || s.att_o.cols != Ca || s.ffn_key.rows != F ||
         s.ffn_key.cols != C || s.ffn_value.rows != C || s.ffn_value.cols != F)
@@ -2236,6 +2419,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   cudaGetDevice(&e->dev);
   e->sms = device_sms();
   e->use_graph = !(flags & 0x1u);
+  e->lut2 = l2;
   // bit 1: no programmatic dependent launch; off under tensor parallelism (collectives between kernels)
   e->pdl = !(flags & 0x2u) && !tp;
   e->nb = batch;
@@ -2378,6 +2562,37 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
     ly.lnx_w = s.lnx_w, ly.lnx_b = s.lnx_b, ly.ffn_x_k = s.ffn_x_k;
     ly.big[0] = s.att_r, ly.big[1] = s.att_k, ly.big[2] = s.att_v, ly.big[3] = s.att_o;
     ly.big[4] = s.ffn_key, ly.big[5] = s.ffn_value;
+    if (l2) {
+      int ks = 0;
+      const rwkvb_packed* wr[3] = {&s.att_r, &s.att_k, &s.att_v};
+      float* orkv[3] = {e->part_r, e->part_k, e->part_v};
+      const uint8_t* drkv[3] = {e->dig_r, e->dig_k, e->dig_v};
+      const float2* crkv[3] = {e->cs_r, e->cs_k, e->cs_v};
+      st = bt_l2_setup(&ly.l2rkv, wr, orkv, drkv, crkv, 3, batch, e->sms, Pk, &e->l2g_rkv, &ks);
+      if (i == 0)
+        for (int j = 0; j < 3; ++j) e->pp_rkv[j] = bt_l2_pieces(ks);
+      const rwkvb_packed* wo = &s.att_o;
+      float* oo = e->part_o;
+      const uint8_t* dy = e->dig_y;
+      const float2* cy = e->cs_y;
+      if (st == RWKVB_OK) st = bt_l2_setup(&ly.l2o, &wo, &oo, &dy, &cy, 1, batch, e->sms, Pk, &e->l2g_o, &ks);
+      if (i == 0) e->pp_o = bt_l2_pieces(ks);
+      const rwkvb_packed* wk = &s.ffn_key;
+      float* ok = e->part_key;
+      const uint8_t* df = e->dig_f;
+      const float2* cf = e->cs_f;
+      if (st == RWKVB_OK) st = bt_l2_setup(&ly.l2key, &wk, &ok, &df, &cf, 1, batch, e->sms, Pk, &e->l2g_key, &ks);
+      if (i == 0) e->pp_key = bt_l2_pieces(ks);
+      const rwkvb_packed* wv = &s.ffn_value;
+      float* ov = e->part_val;
+      const uint8_t* dh = e->dig_h;
+      const float2* ch = e->cs_h;
+      if (st == RWKVB_OK)
+        st = bt_l2_setup(&ly.l2value, &wv, &ov, &dh, &ch, 1, batch, e->sms, Pf, &e->l2g_value, &ks);
+      if (i == 0) e->pp_value = bt_l2_pieces(ks);
+      e->layers.push_back(ly);
+      continue;
+    }
     const BgJob jr[3] = {{&s.att_r, 0, e->part_r}, {&s.att_k, 1, e->part_k}, {&s.att_v, 2, e->part_v}};
     st = bg_setup(&ly.rkv, jr, 3, d_rkv, 3, batch, e->sms, &e->g_rkv, &pieces, &smem, e->err);
     if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
@@ -2400,7 +2615,15 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
     }
     e->layers.push_back(ly);
   }
-  if (st == RWKVB_OK) {
+  if (st == RWKVB_OK && l2) {
+    int ks = 0;
+    const rwkvb_packed* wh = &m->head;
+    float* oh = e->part_head;
+    const uint8_t* doo = e->dig_o;
+    const float2* co = e->cs_o;
+    st = bt_l2_setup(&e->l2head, &wh, &oh, &doo, &co, 1, batch, e->sms, Pk, &e->l2g_head, &ks);
+    e->pp_head = bt_l2_pieces(ks);
+  } else if (st == RWKVB_OK) {
     const BgJob jh{&m->head, 0, e->part_head};
     st = bg_setup(&e->head, &jh, 1, &d_o, 1, batch, e->sms, &e->g_head, &pieces, &smem, e->err);
     if (st == RWKVB_OK && pieces > Pk) st = RWKVB_EUNSUPPORTED;
@@ -2436,7 +2659,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
       }
     }
   }
-  if (st == RWKVB_OK) st = bg_allow_smem(e->smem_bg);
+  if (st == RWKVB_OK && !l2) st = bg_allow_smem(e->smem_bg);
   if (st == RWKVB_OK)
     st = cuda_status(
         cudaFuncSetAttribute(bt_adp1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBtAdp1Smem));

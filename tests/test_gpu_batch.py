@@ -200,3 +200,66 @@ def test_7p2b_width_engines_match_oracle():
             eng.close()
     finally:
         one.close()
+
+
+# ------------------------------------------------------------ LUT2 (TR2\x04) packs
+def _lut2_pack(preset: str, seed: int):
+    shape = synth.PRESETS[preset]
+    return shape, synth.make_pack(synth.generate_state_dict(shape, seed, "cpu"), policy="lut2")
+
+
+def test_lut2_batch_sessions_match_oracle():
+    """Projections and head in TR2\\x04 (CUDA-core batched products): every
+    session against the oracle's per-session loop."""
+    shape, pack = _lut2_pack("tiny", 13)
+    nb, n_new = 6, 8
+    prompts = _prompts(nb, 5, shape.vocab, 13)
+    oracle = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size)
+    eng = B200BatchEngine(pack, nb)
+    try:
+        eng.prefill(prompts)  # LUT2 engines run each position as a decode step
+        ids = eng.decode_greedy(n_new)
+        logits = _np(eng.logits)
+        for b in range(nb):
+            ids_ref, logits_ref, state_ref = oracle.greedy(prompts[b], n_new + 1)
+            assert [int(t) for t in ids[:, b]] == ids_ref[1:], b
+            np.testing.assert_allclose(logits[b], logits_ref[-1], rtol=0, atol=TOL)
+            for j, s in enumerate(eng.get_state(b)):
+                np.testing.assert_allclose(_np(s).reshape(-1), state_ref[j].reshape(-1), rtol=0, atol=TOL)
+    finally:
+        eng.close()
+
+
+@pytest.mark.parametrize("preset,nb,steps", [("0.1b", 64, 3), ("2.9b-l4", 64, 2)])
+def test_lut2_batch_matches_batch1_engine(preset, nb, steps):
+    shape = synth.PRESETS[preset]
+    pack = synth.make_pack_streaming(shape, 6, "cuda", policy="lut2")
+    prompts = _prompts(nb, 3, shape.vocab, 6)
+    eng = B200BatchEngine(pack, nb)
+    one = B200Engine(pack)
+    try:
+        _prefill(eng, prompts)
+        ids = eng.decode_greedy(steps)
+        logits = _np(eng.logits)
+        for b in (0, 33, nb - 1):
+            one.reset()
+            ref_ids, _ = one.greedy(prompts[b], steps + 1)
+            assert [int(t) for t in ids[:, b]] == ref_ids[1:], b
+            np.testing.assert_allclose(logits[b], _np(one.logits), rtol=0, atol=TOL)
+            np.testing.assert_allclose(_np(eng.wkv[:, b]), _np(one.wkv), rtol=0, atol=TOL)
+    finally:
+        eng.close()
+        one.close()
+
+
+def test_lut2_and_sg8_projections_do_not_mix():
+    _, l2 = _lut2_pack("tiny", 3)
+    _, sg = _pack("tiny", 3)
+    mixed = dict(l2)
+    mixed["head.weight"] = sg["head.weight"]
+    with pytest.raises(RwkvbError):
+        B200BatchEngine(mixed, 2)
+    mixed = dict(sg)
+    mixed["blocks.1.ffn.key.weight"] = l2["blocks.1.ffn.key.weight"]
+    with pytest.raises(RwkvbError):
+        B200BatchEngine(mixed, 2)
