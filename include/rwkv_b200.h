@@ -268,7 +268,12 @@ int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out);
  * reference runs it session by session (its batched path, rwkv7_batch, lives in
  * the un-vendored ChatRWKV package).
  * Requirements: every r/k/v/o/FFN/head matrix SG8 with one group size (64 or
- * 128), n_embd, ffn and vocab multiples of 128; adapters and embedding any codec.
+ * 128), or every one TR2\x04 (LUT2, fp16 codebooks) with group 64; n_embd, ffn
+ * and vocab multiples of 128; adapters and embedding any codec.  SG8 products
+ * are integer tcgen05 GEMMs over digit rows; LUT2 products decode the 2-bit
+ * codes to fp16 tiles in shared memory for fp16 tcgen05 GEMMs (activations as
+ * two fp16 planes, fp32 accumulation).  LUT2 engines run prefill positions as
+ * decode steps; tensor parallelism needs SG8.
  * ------------------------------------------------------------------------------ */
 typedef struct rwkvb_batch rwkvb_batch;
 
@@ -276,7 +281,9 @@ typedef struct rwkvb_batch rwkvb_batch;
  *        bit1 = no programmatic dependent launch between the step's kernels
  *               (default: each kernel may start while the previous one
  *               finishes; the GEMMs stream their first weight tiles before
- *               waiting on it).  Always off under tensor parallelism. */
+ *               waiting on it).  Always off under tensor parallelism;
+ *        bit2 = LUT2 engines: products on the CUDA cores (fp32 FMA) instead
+ *               of the tensor cores (a cross-check path). */
 int rwkvb_batch_create(const rwkvb_model_desc* desc, int32_t batch, uint32_t flags, rwkvb_batch** out);
 
 /* Tensor parallelism across the GPUs of one node (one process per GPU), the

@@ -11,6 +11,7 @@
 
 #include "bgemm.cuh"
 #include "common.cuh"
+#include "l2mma.cuh"
 #include "internal.h"
 #include "wkv7.cuh"
 
@@ -1583,7 +1584,8 @@ struct BtLayer {
   const float* mix[6];
   const float *w0, *a0, *v0, *k_k, *k_a, *r_k, *lnx_w, *lnx_b, *ffn_x_k;
   BgArgs rkv, o, key, value;
-  BtL2Args l2rkv, l2o, l2key, l2value;  // LUT2 engines: CUDA-core products instead
+  BtL2Args l2rkv, l2o, l2key, l2value;  // LUT2 engines, CUDA-core products (flag bit 2)
+  LmArgs lmrkv, lmo, lmkey, lmvalue;     // LUT2 engines, tcgen05 products
   rwkvb_packed big[6];  // att r, k, v, o, ffn key, ffn value (for further launch plans)
 };
 
@@ -1633,8 +1635,12 @@ struct rwkvb_batch {
   int L = 0, C = 0, H = 0, F = 0, V = 0, rw = 0, ra = 0, rg = 0, rv = 0, rtot = 0;
   int adp_splits = 0, hist_cap = 1024;
   bool lut2 = false;     // TR2\x04 projections and head: CUDA-core products (bt_l2gemm_kernel)
+  bool l2_cores = false;  // LUT2 products on CUDA cores instead of tcgen05 (flag bit 2)
   rwkvb::BtL2Args l2head;
+  rwkvb::LmArgs lmhead;
   int l2g_rkv = 0, l2g_o = 0, l2g_key = 0, l2g_value = 0, l2g_head = 0;
+  int lmg_rkv = 0, lmg_o = 0, lmg_key = 0, lmg_value = 0, lmg_head = 0;
+  size_t smem_lm = 0;
   bool pdl = true;       // programmatic dependent launch between the step's kernels
   rwkvb::BtAdpPlan adp;  // adapter second-stage chunks
   std::vector<rwkvb::BtLayer> layers;
@@ -1772,6 +1778,91 @@ BtPieces bt_l2_pieces(int ks) {
   return p;
 }
 
+// tcgen05 LUT2 product (l2mma_kernel) launch plan over `njobs` matrices whose
+// digit rows / group scales are dig[j] / cs[j]; the grid is the SM count
+// unless that would give a tile more than `pcap` pieces.
+struct LmJob {
+  const rwkvb_packed* w;
+  float* out;
+  const uint8_t* dig;
+  const float2* cs;
+};
+
+int lm_pmax(const LmArgs& a, int n) {
+  int pmax = 1;
+  for (int j = 0; j < a.nmat; ++j) {
+    const LmMat& M = a.mat[j];
+    const int G = M.k / 64;
+    for (int t = 0; t < M.tiles; ++t) {
+      const long long f = M.stage0 + (long long)t * G;
+      pmax = std::max(pmax, bg_cta_of(f + G - 1, a.total, n) - bg_cta_of(f, a.total, n) + 1);
+    }
+  }
+  return pmax;
+}
+
+int lm_setup(LmArgs* a, const LmJob* jobs, int njobs, int nb, int sms, int pcap, int* grid, size_t* smem,
+             int* err_word) {
+  if (njobs < 1 || njobs > kLmMaxMats || nb < 1 || nb > kBgMaxSessions || pcap < 1) return RWKVB_EARG;
+  std::memset(a, 0, sizeof(*a));
+  a->nb = nb;
+  a->bp = bg_padded_sessions(nb);
+  const int nrows = bg_digit_rows(nb);
+  int total = 0;
+  for (int j = 0; j < njobs; ++j) {
+    const rwkvb_packed& w = *jobs[j].w;
+    if (!bt_l2_ok(w) || w.rows % 128 || w.cols % 128) return RWKVB_EUNSUPPORTED;
+    const PackedView v = make_view(w);
+    // TMA bases: 16-byte aligned codes and records (payloads are placed 16-byte
+    // aligned and an even group count keeps the records so)
+    if ((reinterpret_cast<uintptr_t>(v.payload) | reinterpret_cast<uintptr_t>(v.meta)) & 15u)
+      return RWKVB_EUNSUPPORTED;
+    LmMat& M = a->mat[j];
+    M.out = jobs[j].out;
+    M.cs = reinterpret_cast<const float*>(jobs[j].cs);
+    M.rows = w.rows;
+    M.k = w.cols;
+    M.tiles = w.rows / 128;
+    M.stage0 = total;
+    total += M.tiles * (w.cols / 64);
+    const uint64_t cdims[2] = {(uint64_t)w.cols / 4, (uint64_t)w.rows}, cstr[1] = {(uint64_t)w.cols / 4};
+    const uint64_t rdims[2] = {(uint64_t)w.cols / 8, (uint64_t)w.rows}, rstr[1] = {(uint64_t)w.cols / 8};
+    const uint64_t ddims[2] = {(uint64_t)w.cols, (uint64_t)nrows}, dstr[1] = {(uint64_t)w.cols};
+    const uint32_t box16[2] = {16, 128}, dbox[2] = {64, (uint32_t)(3 * a->bp)};
+    int st = encode_u8_map(&a->cmap[j], 2, v.payload, cdims, cstr, box16, false);
+    if (st == RWKVB_OK) st = encode_u8_map(&a->rmap[j], 2, v.meta, rdims, rstr, box16, false);
+    if (st == RWKVB_OK) st = encode_u8_map(&a->dmap[j], 2, jobs[j].dig, ddims, dstr, dbox, false);
+    if (st != RWKVB_OK) return st;
+  }
+  a->nmat = njobs;
+  a->total = total;
+  // slot: A tile | B tile (2 bp rows) | codes | records | digit rows | scales
+  a->off_b = kLmATile;
+  a->off_codes = a->off_b + 256 * a->bp;
+  a->off_recs = a->off_codes + 2048;
+  a->off_dig = a->off_recs + 2048;
+  a->off_cs = a->off_dig + 192 * a->bp;
+  a->slot_bytes = (a->off_cs + 4 * a->bp + 1023) & ~1023;
+  a->tx_bytes = (uint32_t)(2048 + 2048 + 192 * a->bp + 4 * a->bp);
+  a->stages = (int)std::min<size_t>(kLmMaxStages, (kBgSmemBudget - 1024) / (size_t)a->slot_bytes);
+  if (a->stages < 2) return RWKVB_EUNSUPPORTED;
+  a->idesc = idesc_f16f16_f32(128, 2 * a->bp);
+  a->spin_limit = 1u << 22;
+  a->err = err_word;
+  int n = std::min(sms, total);
+  while (n > 1 && lm_pmax(*a, n) > pcap) --n;
+  *grid = n;
+  *smem = (size_t)a->stages * a->slot_bytes + 1024;
+  return RWKVB_OK;
+}
+
+BtPieces lm_pieces(const LmArgs& a, int j, int grid) {
+  BtPieces p;
+  p.stage0 = a.mat[j].stage0, p.G = a.mat[j].k / 64, p.total = a.total, p.ncta = grid;
+  p.np = nullptr;
+  return p;
+}
+
 // Tabulate the per-tile piece counts of each (pieces, output rows) job into
 // one device buffer (*dev, owned by the caller) and point the jobs at it.
 int bt_np_upload(const std::vector<std::pair<BtPieces*, int>>& jobs, int** dev) {
@@ -1797,6 +1888,15 @@ int bt_np_upload(const std::vector<std::pair<BtPieces*, int>>& jobs, int** dev) 
   return RWKVB_OK;
 }
 
+// One projection launch of the step: the SG8 tcgen05 GEMM, or for LUT2
+// engines the tcgen05 LUT2 GEMM (or its CUDA-core counterpart, flag bit 2).
+int bt_product(rwkvb_batch* e, const BgArgs& bg, int bg_grid, const BtL2Args& l2, int l2_grid, const LmArgs& lm,
+               int lm_grid, cudaStream_t s) {
+  if (!e->lut2) return bg_launch(bg, bg_grid, e->smem_bg, s, e->pdl);
+  if (e->l2_cores) return bt_go(e->pdl, bt_l2gemm_kernel, dim3(l2_grid), dim3(kL2Threads), 0, s, l2);
+  return bt_go(e->pdl, l2mma_kernel, dim3(lm_grid), dim3(kLmThreads), e->smem_lm, s, lm);
+}
+
 // ln_out of x (+ folded value pieces onto xm when `part` is set), the head
 // GEMM and the per-session first-maximum argmax (-> e->tok, e->logits).
 int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part, const BtPieces& pp, cudaStream_t s,
@@ -1818,8 +1918,9 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
   bt_go(e->pdl, bt_in_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
   int st = cuda_status(cudaGetLastError());
   if (st == RWKVB_OK)
-    st = e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_head), dim3(kL2Threads), 0, s, e->l2head)
-                 : bg_launch(e->head, e->g_head, e->smem_bg, s, e->pdl);
+    st = !e->lut2     ? bg_launch(e->head, e->g_head, e->smem_bg, s, e->pdl)
+         : e->l2_cores ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_head), dim3(kL2Threads), 0, s, e->l2head)
+                       : bt_go(e->pdl, l2mma_kernel, dim3(e->lmg_head), dim3(kLmThreads), e->smem_lm, s, e->lmhead);
   if (st != RWKVB_OK) return st;
   const bool tp = e->tp_size > 1;
   float2* loc = !tp ? nullptr
@@ -1915,9 +2016,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       bt_go(e->pdl, bt_in_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * 5 * C, s, a);
       BT_CHECK();
     }
-    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_rkv), dim3(kL2Threads), 0, s, ly.l2rkv)
-                 : bg_launch(ly.rkv, e->g_rkv, e->smem_bg, s, e->pdl)) != RWKVB_OK)
-      return RWKVB_ECUDA;
+    if (bt_product(e, ly.rkv, e->g_rkv, ly.l2rkv, e->l2g_rkv, ly.lmrkv, e->lmg_rkv, s) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     const int nm = l0 ? 3 : 4;
     {
@@ -1984,9 +2083,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
     }
     if (bg_digits(e->dig_y, e->cs_y, e->att_y, Ca, Ca, nb, e->group, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
-    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_o), dim3(kL2Threads), 0, s, ly.l2o)
-                 : bg_launch(ly.o, e->g_o, e->smem_bg, s, e->pdl)) != RWKVB_OK)
-      return RWKVB_ECUDA;
+    if (bt_product(e, ly.o, e->g_o, ly.l2o, e->l2g_o, ly.lmo, e->lmg_o, s) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     if (tp) {
       if (bt_reduce(e, e->ored, e->part_o, e->pp_o, s, 2 * l) != RWKVB_OK) return RWKVB_ECUDA;
@@ -1998,9 +2095,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       bt_go(e->pdl, bt_ffn_kernel, dim3(nb), dim3(kBtRowThreads), sizeof(float) * C, s, a);
       BT_CHECK();
     }
-    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_key), dim3(kL2Threads), 0, s, ly.l2key)
-                 : bg_launch(ly.key, e->g_key, e->smem_bg, s, e->pdl)) != RWKVB_OK)
-      return RWKVB_ECUDA;
+    if (bt_product(e, ly.key, e->g_key, ly.l2key, e->l2g_key, ly.lmkey, e->lmg_key, s) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     {
       const int warps = nb * (e->F >> e->lfk);
@@ -2008,9 +2103,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
                                                            e->bp, e->lfk);
       BT_CHECK();
     }
-    if ((e->lut2 ? bt_go(e->pdl, bt_l2gemm_kernel, dim3(e->l2g_value), dim3(kL2Threads), 0, s, ly.l2value)
-                 : bg_launch(ly.value, e->g_value, e->smem_bg, s, e->pdl)) != RWKVB_OK)
-      return RWKVB_ECUDA;
+    if (bt_product(e, ly.value, e->g_value, ly.l2value, e->l2g_value, ly.lmvalue, e->lmg_value, s) != RWKVB_OK) return RWKVB_ECUDA;
     ++n;
     if (tp) {
       if (bt_reduce(e, e->vred, e->part_val, e->pp_value, s, 2 * l + 1) != RWKVB_OK) return RWKVB_ECUDA;
@@ -2420,6 +2513,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   e->sms = device_sms();
   e->use_graph = !(flags & 0x1u);
   e->lut2 = l2;
+  e->l2_cores = l2 && (flags & 0x4u);
   // bit 1: no programmatic dependent launch; off under tensor parallelism (collectives between kernels)
   e->pdl = !(flags & 0x2u) && !tp;
   e->nb = batch;
@@ -2590,6 +2684,28 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
       if (st == RWKVB_OK)
         st = bt_l2_setup(&ly.l2value, &wv, &ov, &dh, &ch, 1, batch, e->sms, Pf, &e->l2g_value, &ks);
       if (i == 0) e->pp_value = bt_l2_pieces(ks);
+      if (!e->l2_cores) {
+        size_t sm = 0;
+        const LmJob jr[3] = {{&s.att_r, e->part_r, e->dig_r, e->cs_r},
+                             {&s.att_k, e->part_k, e->dig_k, e->cs_k},
+                             {&s.att_v, e->part_v, e->dig_v, e->cs_v}};
+        const LmJob jo{&s.att_o, e->part_o, e->dig_y, e->cs_y}, jk{&s.ffn_key, e->part_key, e->dig_f, e->cs_f},
+            jv{&s.ffn_value, e->part_val, e->dig_h, e->cs_h};
+        if (st == RWKVB_OK) st = lm_setup(&ly.lmrkv, jr, 3, batch, e->sms, Pk, &e->lmg_rkv, &sm, e->err);
+        e->smem_lm = std::max(e->smem_lm, sm);
+        if (st == RWKVB_OK) st = lm_setup(&ly.lmo, &jo, 1, batch, e->sms, Pk, &e->lmg_o, &sm, e->err);
+        e->smem_lm = std::max(e->smem_lm, sm);
+        if (st == RWKVB_OK) st = lm_setup(&ly.lmkey, &jk, 1, batch, e->sms, Pk, &e->lmg_key, &sm, e->err);
+        e->smem_lm = std::max(e->smem_lm, sm);
+        if (st == RWKVB_OK) st = lm_setup(&ly.lmvalue, &jv, 1, batch, e->sms, Pf, &e->lmg_value, &sm, e->err);
+        e->smem_lm = std::max(e->smem_lm, sm);
+        if (i == 0 && st == RWKVB_OK) {
+          for (int j = 0; j < 3; ++j) e->pp_rkv[j] = lm_pieces(ly.lmrkv, j, e->lmg_rkv);
+          e->pp_o = lm_pieces(ly.lmo, 0, e->lmg_o);
+          e->pp_key = lm_pieces(ly.lmkey, 0, e->lmg_key);
+          e->pp_value = lm_pieces(ly.lmvalue, 0, e->lmg_value);
+        }
+      }
       e->layers.push_back(ly);
       continue;
     }
@@ -2623,6 +2739,16 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
     const float2* co = e->cs_o;
     st = bt_l2_setup(&e->l2head, &wh, &oh, &doo, &co, 1, batch, e->sms, Pk, &e->l2g_head, &ks);
     e->pp_head = bt_l2_pieces(ks);
+    if (st == RWKVB_OK && !e->l2_cores) {
+      size_t sm = 0;
+      const LmJob jh{&m->head, e->part_head, e->dig_o, e->cs_o};
+      st = lm_setup(&e->lmhead, &jh, 1, batch, e->sms, Pk, &e->lmg_head, &sm, e->err);
+      e->smem_lm = std::max(e->smem_lm, sm);
+      e->pp_head = lm_pieces(e->lmhead, 0, e->lmg_head);
+    }
+    if (st == RWKVB_OK && !e->l2_cores)
+      st = cuda_status(
+          cudaFuncSetAttribute(l2mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)e->smem_lm));
   } else if (st == RWKVB_OK) {
     const BgJob jh{&m->head, 0, e->part_head};
     st = bg_setup(&e->head, &jh, 1, &d_o, 1, batch, e->sms, &e->g_head, &pieces, &smem, e->err);
@@ -2647,7 +2773,9 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
               {(const void*)bt_wkv_kernel, kBtThreads, "bt_wkv_kernel"},
               {(const void*)bt_ffn_kernel, kBtRowThreads, "bt_ffn_kernel"},
               {(const void*)bt_hdig_kernel, kBtThreads, "bt_hdig_kernel"},
-              {(const void*)bt_argmax_kernel, 1024, "bt_argmax_kernel"}};
+              {(const void*)bt_argmax_kernel, 1024, "bt_argmax_kernel"},
+              {(const void*)bt_l2gemm_kernel, kL2Threads, "bt_l2gemm_kernel"},
+              {(const void*)l2mma_kernel, kLmThreads, "l2mma_kernel"}};
     for (const auto& k : ks) {
       cudaFuncAttributes fa;
       if (cudaFuncGetAttributes(&fa, k.fn) != cudaSuccess || fa.maxThreadsPerBlock < k.threads) {

@@ -1,0 +1,436 @@
+// Batched LUT2 (TR2\x04) GEMM on the 5th-generation tensor cores (tcgen05,
+// kind::f16):
+//     Y[b][n] = sum_k W[n][k] x[b][k]      (b < nb <= 64 sessions)
+// for the batched decode step of engines whose projections and head are LUT2
+// (the reference's per-row product is trinity_grouped_lut2_gemv_f32,
+// rwkv_ssd/native/lut2_gather.c:269-335).
+//
+// Operands:
+//   A = the weights: every weight IS one of its group's four fp16 codebook
+//       values, so the 2-bit codes decode to an exact fp16 tile (128 rows x
+//       64 columns = one code group per row, 128-byte swizzled rows);
+//   B = the activations, rebuilt per session from the engine's digit rows
+//       (x = c_g (X0 + X1/254 + X2/254^2) per 64-column group g) and split
+//       into two fp16 planes
+//           x / S = hi + lo,   hi = rn16(x / S),   lo = rn16(x / S - hi),
+//       S = the largest c_g of the session over the segment's K range, so
+//       |x / S| <= 1.004 (no fp16 overflow) and hi + lo keeps ~22 significant
+//       bits; rows [0, bp) hold hi, rows [bp, 2 bp) hold lo.
+// The MMA (M 128, N 2 bp, K 16) accumulates W hi and W lo in fp32 TMEM over
+// the whole segment -- the codebook values are the weights, so nothing is
+// flushed per group -- and the epilogue writes S (D_hi + D_lo).
+//
+// Work split: (tile, 64-column stage) pairs of all matrices of a launch are
+// numbered in order and every CTA takes a contiguous, equal share (as the SG8
+// GEMM); the partial sums of a tile's CTA go to piece slot (cta - first cta of
+// the tile) of [pieces][nb][rows], which consumers add in slot order.
+//
+// Roles (14 warps): warp 0 lane 0 issues the raw copies of a stage (codes,
+// codebook records, digit rows, group scales) into a ring; warp 1 allocates
+// TMEM (two accumulators of 128 columns) and lane 0 issues the MMAs; warps
+// 2..5 are the epilogue (TMEM lane quarter = warp % 4, one row per lane);
+// warps 6..13 decode the raw stage into the A and B operand tiles.  Every wait
+// is bounded: on a limit the CTA sets the error word, drains the copies it
+// issued and returns.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "bgemm.cuh"
+#include "imma.cuh"
+#include "stream.cuh"
+#include "tma.cuh"
+#include "umma.cuh"
+
+namespace rwkvb {
+
+constexpr int kLmWarps = 14;
+constexpr int kLmThreads = kLmWarps * 32;
+constexpr int kLmBuildWarps = 8;  // warps 6..13
+constexpr int kLmMaxMats = 3;
+constexpr int kLmMaxStages = 6;
+constexpr int kLmAccStride = 128;  // TMEM columns between the two accumulators
+constexpr int kLmTmemCols = 256;
+constexpr int kLmATile = 128 * 128;  // A: 128 rows x 64 fp16
+
+// Instruction descriptor, kind::f16: D f32 (c_format 1, bits [4,6)), A and B
+// f16 (a_format / b_format 0), both K-major, N >> 3 in [17,23), M >> 4 in
+// [24,29).
+__host__ __device__ constexpr uint32_t idesc_f16f16_f32(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T in fp16 with fp32 accumulation, issued by
+// ONE thread.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Generic-proxy shared-memory writes made visible to the async proxy (the
+// tensor cores read the operand tiles the decode warps wrote).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Two 16-column TMEM loads and one wait.
+__device__ __forceinline__ void tmem_ld16x2_sync(uint32_t t0, uint32_t t1, uint32_t (&a)[16], uint32_t (&b)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, "
+      "[%33];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(a[8]),
+        "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15]), "=r"(b[0]),
+        "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]),
+        "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15])
+      : "r"(t0), "r"(t1)
+      : "memory");
+}
+
+struct LmMat {
+  float* out;    // partial sums [pieces][nb][rows]
+  const float* cs;  // group scales of the digit rows: c_g at cs[g * 2 bp + b]
+  int rows, k;   // N, K (rows % 128 == 0, k % 128 == 0)
+  int tiles;     // rows / 128
+  int stage0;    // first global stage index of this matrix
+};
+
+struct LmArgs {
+  CUtensorMap cmap[kLmMaxMats];  // codes, bytes {k / 4, rows}, box {16, 128}
+  CUtensorMap rmap[kLmMaxMats];  // records, bytes {k / 8, rows}, box {16, 128} (two groups)
+  CUtensorMap dmap[kLmMaxMats];  // digit rows, bytes {k, nrows}, box {64, 3 bp}
+  LmMat mat[kLmMaxMats];
+  int nmat, total;               // matrices, stages over all matrices
+  int nb, bp;                    // sessions, padded sessions (MMA N = 2 bp)
+  int stages;                    // ring slots
+  int slot_bytes;                // ring slot stride (multiple of 1024)
+  int off_b, off_codes, off_recs, off_dig, off_cs;  // offsets inside a slot
+  uint32_t tx_bytes;             // bytes of the raw copies of one stage
+  uint32_t idesc;
+  uint32_t spin_limit;
+  int* err;
+};
+
+// One segment: stages [s0, s1) of tile t of matrix m, piece p.
+struct LmSeg {
+  int m, t, s0, s1, p;
+};
+
+__device__ __forceinline__ LmSeg lm_segment(const LmArgs& a, int x, int hi) {
+  int m = 0;
+#pragma unroll 1
+  while (m + 1 < a.nmat && x >= a.mat[m + 1].stage0) ++m;
+  const LmMat& M = a.mat[m];
+  const int G = M.k >> 6;
+  const int local = x - M.stage0;
+  LmSeg s;
+  s.m = m;
+  s.t = local / G;
+  s.s0 = local - s.t * G;
+  const int tile_hi = M.stage0 + (s.t + 1) * G;
+  s.s1 = s.s0 + (min(hi, tile_hi) - x);
+  s.p = (int)blockIdx.x - bg_cta_of(M.stage0 + (long long)s.t * G, a.total, gridDim.x);
+  return s;
+}
+
+__device__ __forceinline__ bool lm_wait(uint64_t* bar, uint32_t parity, const LmArgs& a, volatile int* abort_flag) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) {
+    if (!*abort_flag) {
+      ok = mbar_wait_bounded(bar, parity, a.spin_limit) ? 1 : 0;
+      if (!ok) {
+        atomicOr(a.err, kErrTimeout);
+        *abort_flag = 1;
+      }
+    }
+  }
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// Largest group scale c_g of session b over groups [g0, g1), the groups split
+// over `n` cooperating lanes (lane index i of n, adjacent lanes of one warp);
+// 1 for padded sessions.  Order-independent, so every caller gets the same S.
+__device__ __forceinline__ float lm_scale(const LmArgs& a, const LmMat& M, int b, int g0, int g1, int i, int n) {
+  float s = 0.f;
+  if (b < a.nb) {
+    const float* p = M.cs + b;
+    const size_t st = (size_t)2 * a.bp;
+    int g = g0 + i;
+    for (; g + 3 * n < g1; g += 4 * n) {  // four loads in flight
+      const float v0 = __ldcg(p + g * st), v1 = __ldcg(p + (g + n) * st);
+      const float v2 = __ldcg(p + (g + 2 * n) * st), v3 = __ldcg(p + (g + 3 * n) * st);
+      s = fmaxf(s, fmaxf(fmaxf(v0, v1), fmaxf(v2, v3)));
+    }
+    for (; g < g1; g += n) s = fmaxf(s, __ldcg(p + g * st));
+  }
+  for (int o = 1; o < n; o <<= 1) s = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, o));
+  return s > 0.f ? s : 1.f;
+}
+
+// PRMT selector of a nibble of codes (two 2-bit codes, LSB first): bytes
+// 2 c0, 2 c0 + 1, 2 c1, 2 c1 + 1 of the 8-byte record {lo, hi}, i.e. the two
+// fp16 codebook values as one half2.
+__device__ __forceinline__ uint32_t lm_sel(uint32_t n) { return 0x1010u + 0x22u * ((n & 3u) | ((n & 0xCu) << 6)); }
+
+__global__ void __launch_bounds__(kLmThreads, 1) l2mma_kernel(const __grid_constant__ LmArgs a) {
+  extern __shared__ __align__(1024) uint8_t lm_smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(lm_smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kLmMaxStages], built[kLmMaxStages], empty[kLmMaxStages], tfull[2],
+      tempty[2], done_bar;
+  __shared__ uint32_t s_tbase;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lo = bg_range_lo(blockIdx.x, a.total, gridDim.x);
+  const int hi = bg_range_lo(blockIdx.x + 1, a.total, gridDim.x);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < a.stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&built[i], kLmBuildWarps);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(&done_bar, 1);
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&s_tbase, kLmTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = s_tbase;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    // Codes and records of the first `stages` stages go out before the grid
+    // dependency wait (weights never depend on the previous kernel); digit
+    // rows and group scales, written by the previous kernel, after it.
+    uint32_t npre = 0;
+    if (lane == 0) {
+      for (int x = lo; x < hi && npre < (uint32_t)a.stages;) {
+        const LmSeg sg = lm_segment(a, x, hi);
+        for (int st = sg.s0; st < sg.s1 && npre < (uint32_t)a.stages; ++st, ++npre) {
+          uint8_t* slot = smem + npre * a.slot_bytes;
+          mbar_expect_tx(&full[npre], a.tx_bytes);
+          tma_load_2d_hint(slot + a.off_codes, &a.cmap[sg.m], st * 16, sg.t * 128, &full[npre], l2_evict_first());
+          tma_load_2d_hint(slot + a.off_recs, &a.rmap[sg.m], (st >> 1) * 16, sg.t * 128, &full[npre],
+                           l2_evict_first());
+        }
+        x += sg.s1 - sg.s0;
+      }
+    }
+    npre = __shfl_sync(0xffffffffu, npre, 0);
+    pdl_wait();
+    pdl_launch_dependents();
+    uint32_t use = 0;
+    for (int x = lo; x < hi;) {
+      const LmSeg sg = lm_segment(a, x, hi);
+      const LmMat& M = a.mat[sg.m];
+      for (int st = sg.s0; st < sg.s1; ++st, ++use) {
+        const uint32_t si = use % a.stages, n = use / a.stages;
+        uint8_t* slot = smem + si * a.slot_bytes;
+        if (use >= npre) {
+          if (!lm_wait(&empty[si], (n & 1) ^ 1, a, &s_abort)) goto producer_drain;
+          if (lane == 0) {
+            mbar_expect_tx(&full[si], a.tx_bytes);
+            tma_load_2d_hint(slot + a.off_codes, &a.cmap[sg.m], st * 16, sg.t * 128, &full[si], l2_evict_first());
+            tma_load_2d_hint(slot + a.off_recs, &a.rmap[sg.m], (st >> 1) * 16, sg.t * 128, &full[si],
+                             l2_evict_first());
+          }
+        }
+        if (lane == 0) {
+          tma_load_2d(slot + a.off_dig, &a.dmap[sg.m], st * 64, 0, &full[si]);
+          bulk_g2s(slot + a.off_cs, M.cs + (size_t)st * 2 * a.bp, (uint32_t)(4 * a.bp), &full[si]);
+        }
+        __syncwarp();
+      }
+      x += sg.s1 - sg.s0;
+    }
+  producer_drain:
+    // the copies still in flight are among the last min(stages, use) issues
+    if (lane == 0)
+      for (uint32_t u = use > (uint32_t)a.stages ? use - a.stages : 0; u < use; ++u)
+        mbar_wait_bounded(&full[u % a.stages], (u / a.stages) & 1, a.spin_limit);
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    pdl_launch_dependents();  // reads shared memory only
+    uint32_t use = 0, seg = 0;
+    for (int x = lo; x < hi; ++seg) {
+      const LmSeg sg = lm_segment(a, x, hi);
+      const uint32_t tb = seg & 1;
+      if (!lm_wait(&tempty[tb], ((seg >> 1) & 1) ^ 1, a, &s_abort)) goto mma_done;
+      tc_fence_after();
+      const uint32_t dt = tbase + tb * kLmAccStride;
+      for (int st = sg.s0; st < sg.s1; ++st, ++use) {
+        const uint32_t si = use % a.stages, n = use / a.stages;
+        if (!lm_wait(&built[si], n & 1, a, &s_abort)) goto mma_done;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = smem_u32(smem + si * a.slot_bytes);
+          const uint32_t sb = sa + (uint32_t)a.off_b;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            umma_f16(dt, sdesc_k128(sa + 32 * j), sdesc_k128(sb + 32 * j), a.idesc,
+                     (st > sg.s0 || j > 0) ? 1u : 0u);
+          umma_commit(&empty[si]);
+          if (st + 1 == sg.s1) umma_commit(&tfull[tb]);
+        }
+        __syncwarp();
+      }
+      x += sg.s1 - sg.s0;
+    }
+  mma_done:
+    // every MMA issued so far has completed once done_bar's phase 0 ends
+    if (lane == 0) {
+      umma_commit(&done_bar);
+      mbar_wait_bounded(&done_bar, 0, a.spin_limit);
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    pdl_wait();  // group scales come from the previous kernel; outputs may be read by it
+    pdl_launch_dependents();
+    const int q4 = warp & 3;
+    const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16);
+    uint32_t seg = 0;
+    for (int x = lo; x < hi; ++seg) {
+      const LmSeg sg = lm_segment(a, x, hi);
+      const LmMat& M = a.mat[sg.m];
+      // S of sessions lane and lane + 32 (the builders derive the same values)
+      const float s_a = lm_scale(a, M, lane, sg.s0, sg.s1, 0, 1);
+      const float s_b = lm_scale(a, M, lane + 32, sg.s0, sg.s1, 0, 1);
+      const uint32_t tb = seg & 1;
+      if (!lm_wait(&tfull[tb], (seg >> 1) & 1, a, &s_abort)) goto epi_done;
+      tc_fence_after();
+      const int row = sg.t * 128 + q4 * 32 + lane;
+      float* out = M.out + (size_t)sg.p * a.nb * M.rows + row;
+      const uint32_t ta = tl + tb * kLmAccStride;
+      for (int c0 = 0; c0 < a.bp; c0 += 16) {
+        uint32_t dh[16], dl[16];
+        tmem_ld16x2_sync(ta + c0, ta + a.bp + c0, dh, dl);
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+          const int b = c0 + s;
+          const float sc = __shfl_sync(0xffffffffu, b < 32 ? s_a : s_b, b & 31);
+          if (b < a.nb) out[(size_t)b * M.rows] = sc * (__uint_as_float(dh[s]) + __uint_as_float(dl[s]));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[tb]);
+      x += sg.s1 - sg.s0;
+    }
+  epi_done:;
+  } else {
+    // ------------------------------------------------------------ decode warps
+    // A: thread t decodes row t & 127, code words 2 h, 2 h + 1 (h = t >> 7) of
+    // the stage; B: thread t rebuilds session t >> 2, columns 16 (t & 3) ..+15.
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t = threadIdx.x - 6 * 32;
+    const int ar = t & 127, ah = t >> 7;
+    const int bb = t >> 2, bq = t & 3;
+    uint32_t use = 0;
+    for (int x = lo; x < hi;) {
+      const LmSeg sg = lm_segment(a, x, hi);
+      const LmMat& M = a.mat[sg.m];
+      const float S = lm_scale(a, M, bb, sg.s0, sg.s1, bq, 4);
+      for (int st = sg.s0; st < sg.s1; ++st, ++use) {
+        const uint32_t si = use % a.stages, n = use / a.stages;
+        if (!lm_wait(&full[si], n & 1, a, &s_abort)) goto build_done;
+        uint8_t* slot = smem + si * a.slot_bytes;
+        {
+          // A: 32 weights of row ar -> four swizzled 16-byte chunks 4 ah .. 4 ah + 3
+          const uint2 w = *reinterpret_cast<const uint2*>(slot + a.off_codes + ar * 16 + 8 * ah);
+          const uint2 rec = *reinterpret_cast<const uint2*>(slot + a.off_recs + ar * 16 + 8 * (st & 1));
+          uint8_t* arow = slot + ar * 128;
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const uint32_t word = i ? w.y : w.x;
+            uint32_t h2[8];
+#pragma unroll
+            for (int p = 0; p < 8; ++p) h2[p] = __byte_perm(rec.x, rec.y, lm_sel((word >> (4 * p)) & 15u));
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const int chunk = 4 * ah + 2 * i + c;
+              *reinterpret_cast<uint4*>(arow + ((chunk ^ (ar & 7)) << 4)) =
+                  make_uint4(h2[4 * c], h2[4 * c + 1], h2[4 * c + 2], h2[4 * c + 3]);
+            }
+          }
+        }
+        if (bb < a.bp) {
+          // B: hi plane at row bb, lo plane at row bp + bb; chunks 2 bq, 2 bq + 1
+          uint32_t ph[8], pl[8];
+          if (bb < a.nb) {
+            const uint8_t* dg = slot + a.off_dig + 16 * bq;
+            const uint4 d0 = *reinterpret_cast<const uint4*>(dg + (size_t)bb * 64);
+            const uint4 d1 = *reinterpret_cast<const uint4*>(dg + (size_t)(a.bp + bb) * 64);
+            const uint4 d2 = *reinterpret_cast<const uint4*>(dg + (size_t)(2 * a.bp + bb) * 64);
+            const float cf = reinterpret_cast<const float*>(slot + a.off_cs)[bb];
+            const float ratio = __fdiv_rn(cf, S);  // a power of two (both c = 2^e / 127)
+            const uint32_t w0[4] = {d0.x, d0.y, d0.z, d0.w}, w1[4] = {d1.x, d1.y, d1.z, d1.w},
+                           w2[4] = {d2.x, d2.y, d2.z, d2.w};
+#pragma unroll
+            for (int u = 0; u < 16; u += 2) {
+              float v[2];
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int k = u + e;
+                const float x0 = (float)(int)((w0[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
+                const float x1 = (float)(int)((w1[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
+                const float x2 = (float)(int)((w2[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
+                v[e] = ratio * (x0 + (x1 + x2 * kInv254) * kInv254);
+              }
+              const __half2 h = __floats2half2_rn(v[0], v[1]);
+              const float2 hf = __half22float2(h);
+              const __half2 l = __floats2half2_rn(v[0] - hf.x, v[1] - hf.y);
+              ph[u >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+              pl[u >> 1] = *reinterpret_cast<const uint32_t*>(&l);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) ph[i] = pl[i] = 0u;
+          }
+          uint8_t* brow_h = slot + a.off_b + (size_t)bb * 128;
+          uint8_t* brow_l = slot + a.off_b + (size_t)(a.bp + bb) * 128;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int chunk = 2 * bq + c;
+            *reinterpret_cast<uint4*>(brow_h + ((chunk ^ (bb & 7)) << 4)) =
+                make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+            *reinterpret_cast<uint4*>(brow_l + ((chunk ^ (bb & 7)) << 4)) =
+                make_uint4(pl[4 * c], pl[4 * c + 1], pl[4 * c + 2], pl[4 * c + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&built[si]);
+      }
+      x += sg.s1 - sg.s0;
+    }
+  build_done:;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, kLmTmemCols);
+  }
+}
+
+}  // namespace rwkvb

@@ -254,7 +254,9 @@ class B200Engine:
 class B200BatchEngine:
     """``batch`` (<= 64) independent sessions of one packed RWKV-7 model decoded
     together: one token step advances every session, with every projection a
-    tcgen05 batched GEMM (``rwkvb_batch_*`` in the C ABI).
+    tcgen05 batched GEMM (``rwkvb_batch_*`` in the C ABI): integer GEMMs over
+    digit rows for SG8 packs, fp16 GEMMs over decoded codebook tiles for LUT2
+    packs (``lut2_tensor_cores=False``: fp32 CUDA-core products instead).
 
     The reference batches sessions with ``rwkv7_batch`` (ChatRWKV, not vendored)
     and otherwise loops sessions through ``forward_block_packed``; per session
@@ -262,7 +264,7 @@ class B200BatchEngine:
     keeps the ``RecurrentState.rwkv7_state`` triple."""
 
     def __init__(self, pack, batch: int, *, device: int | torch.device = 0, use_graph: bool = True,
-                 pdl: bool = True):
+                 pdl: bool = True, lut2_tensor_cores: bool = True):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200BatchEngine needs a CUDA device; there is no CPU path")
@@ -274,6 +276,8 @@ class B200BatchEngine:
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
             if not pdl:
                 flags |= native.FLAG_NO_PDL
+            if not lut2_tensor_cores:
+                flags |= native.FLAG_LUT2_CUDA_CORES
             h = ctypes.c_void_p()
             native.check(self.lib.rwkvb_batch_create(ctypes.byref(self._model.md), self.batch, flags,
                                                      ctypes.byref(h)), "rwkvb_batch_create")

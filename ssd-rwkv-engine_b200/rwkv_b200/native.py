@@ -36,6 +36,7 @@ LUT2_KINDS = (3, 4, 5, 6, 7)
 # Engine flags (rwkvb_engine_create)
 FLAG_NO_GRAPH = 0x1
 FLAG_NO_PDL = 0x2
+FLAG_LUT2_CUDA_CORES = 0x4  # batch engines with LUT2 packs: fp32 CUDA-core products
 FLAG_NO_PERSISTENT = 0x4
 FLAG_TRACE = 0x8
 FLAG_EXPLICIT_PREFETCH = 0x100

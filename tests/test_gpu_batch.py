@@ -263,3 +263,25 @@ def test_lut2_and_sg8_projections_do_not_mix():
     mixed["blocks.1.ffn.key.weight"] = l2["blocks.1.ffn.key.weight"]
     with pytest.raises(RwkvbError):
         B200BatchEngine(mixed, 2)
+
+
+@pytest.mark.parametrize("preset,nb", [("tiny", 7), ("0.1b", 64)])
+def test_lut2_tensor_core_and_cuda_core_products_agree(preset, nb):
+    """The fp16 tcgen05 LUT2 GEMM (activations as two fp16 planes) against the
+    fp32 CUDA-core product on the same pack and prompts: ids identical, logits
+    within 1e-3."""
+    shape = synth.PRESETS[preset]
+    pack = synth.make_pack_streaming(shape, 8, "cuda", policy="lut2")
+    prompts = _prompts(nb, 4, shape.vocab, 8)
+    out = []
+    for tc in (True, False):
+        eng = B200BatchEngine(pack, nb, lut2_tensor_cores=tc)
+        try:
+            _prefill(eng, prompts)
+            ids = eng.decode_greedy(4)
+            out.append((ids, _np(eng.logits), _np(eng.wkv)))
+        finally:
+            eng.close()
+    assert np.array_equal(out[0][0], out[1][0])
+    np.testing.assert_allclose(out[0][1], out[1][1], rtol=0, atol=TOL)
+    np.testing.assert_allclose(out[0][2], out[1][2], rtol=0, atol=TOL)
