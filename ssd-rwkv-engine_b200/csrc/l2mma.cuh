@@ -25,11 +25,11 @@
 // GEMM); the partial sums of a tile's CTA go to piece slot (cta - first cta of
 // the tile) of [pieces][nb][rows], which consumers add in slot order.
 //
-// Roles (14 warps): warp 0 lane 0 issues the raw copies of a stage (codes,
+// Roles (22 warps): warp 0 lane 0 issues the raw copies of a stage (codes,
 // codebook records, digit rows, group scales) into a ring; warp 1 allocates
 // TMEM (two accumulators of 128 columns) and lane 0 issues the MMAs; warps
 // 2..5 are the epilogue (TMEM lane quarter = warp % 4, one row per lane);
-// warps 6..13 decode the raw stage into the A and B operand tiles.  Every wait
+// warps 6..21 decode the raw stage into the A and B operand tiles.  Every wait
 // is bounded: on a limit the CTA sets the error word, drains the copies it
 // issued and returns.
 #pragma once
@@ -46,9 +46,9 @@
 
 namespace rwkvb {
 
-constexpr int kLmWarps = 14;
+constexpr int kLmWarps = 22;
 constexpr int kLmThreads = kLmWarps * 32;
-constexpr int kLmBuildWarps = 8;  // warps 6..13
+constexpr int kLmBuildWarps = 16;  // warps 6..21
 constexpr int kLmMaxMats = 3;
 constexpr int kLmMaxStages = 6;
 constexpr int kLmAccStride = 128;  // TMEM columns between the two accumulators
@@ -338,62 +338,59 @@ __global__ void __launch_bounds__(kLmThreads, 1) l2mma_kernel(const __grid_const
   epi_done:;
   } else {
     // ------------------------------------------------------------ decode warps
-    // A: thread t decodes row t & 127, code words 2 h, 2 h + 1 (h = t >> 7) of
-    // the stage; B: thread t rebuilds session t >> 2, columns 16 (t & 3) ..+15.
+    // A: thread t decodes code word t & 3 (16 weights, two 16-byte chunks) of
+    // row t >> 2; B: thread t rebuilds session t >> 3, columns 8 (t & 7) ..+7
+    // (one 16-byte chunk of each plane).  Consecutive lanes read consecutive
+    // staging bytes and write distinct swizzled chunks: no bank conflicts.
     pdl_wait();
     pdl_launch_dependents();
     const int t = threadIdx.x - 6 * 32;
-    const int ar = t & 127, ah = t >> 7;
-    const int bb = t >> 2, bq = t & 3;
+    const int ar = t >> 2, aw = t & 3;
+    const int bb = t >> 3, bq = t & 7;
     uint32_t use = 0;
     for (int x = lo; x < hi;) {
       const LmSeg sg = lm_segment(a, x, hi);
       const LmMat& M = a.mat[sg.m];
-      const float S = lm_scale(a, M, bb, sg.s0, sg.s1, bq, 4);
+      // 1 / S: ratio c_g / S is then exact to one rounding (S is undone by the
+      // epilogue's multiply; the ~2^-24 relative slack is far below the planes'
+      // 22 bits)
+      const float inv_s = __frcp_rn(lm_scale(a, M, bb, sg.s0, sg.s1, bq, 8));
       for (int st = sg.s0; st < sg.s1; ++st, ++use) {
         const uint32_t si = use % a.stages, n = use / a.stages;
         if (!lm_wait(&full[si], n & 1, a, &s_abort)) goto build_done;
         uint8_t* slot = smem + si * a.slot_bytes;
         {
-          // A: 32 weights of row ar -> four swizzled 16-byte chunks 4 ah .. 4 ah + 3
-          const uint2 w = *reinterpret_cast<const uint2*>(slot + a.off_codes + ar * 16 + 8 * ah);
+          const uint32_t w = *reinterpret_cast<const uint32_t*>(slot + a.off_codes + ar * 16 + 4 * aw);
           const uint2 rec = *reinterpret_cast<const uint2*>(slot + a.off_recs + ar * 16 + 8 * (st & 1));
+          uint32_t h2[8];
+#pragma unroll
+          for (int p = 0; p < 8; ++p) h2[p] = __byte_perm(rec.x, rec.y, lm_sel((w >> (4 * p)) & 15u));
           uint8_t* arow = slot + ar * 128;
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const uint32_t word = i ? w.y : w.x;
-            uint32_t h2[8];
-#pragma unroll
-            for (int p = 0; p < 8; ++p) h2[p] = __byte_perm(rec.x, rec.y, lm_sel((word >> (4 * p)) & 15u));
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              const int chunk = 4 * ah + 2 * i + c;
-              *reinterpret_cast<uint4*>(arow + ((chunk ^ (ar & 7)) << 4)) =
-                  make_uint4(h2[4 * c], h2[4 * c + 1], h2[4 * c + 2], h2[4 * c + 3]);
-            }
+          for (int c = 0; c < 2; ++c) {
+            const int chunk = 2 * aw + c;
+            *reinterpret_cast<uint4*>(arow + ((chunk ^ (ar & 7)) << 4)) =
+                make_uint4(h2[4 * c], h2[4 * c + 1], h2[4 * c + 2], h2[4 * c + 3]);
           }
         }
         if (bb < a.bp) {
-          // B: hi plane at row bb, lo plane at row bp + bb; chunks 2 bq, 2 bq + 1
-          uint32_t ph[8], pl[8];
+          uint32_t ph[4] = {0u, 0u, 0u, 0u}, pl[4] = {0u, 0u, 0u, 0u};
           if (bb < a.nb) {
-            const uint8_t* dg = slot + a.off_dig + 16 * bq;
-            const uint4 d0 = *reinterpret_cast<const uint4*>(dg + (size_t)bb * 64);
-            const uint4 d1 = *reinterpret_cast<const uint4*>(dg + (size_t)(a.bp + bb) * 64);
-            const uint4 d2 = *reinterpret_cast<const uint4*>(dg + (size_t)(2 * a.bp + bb) * 64);
-            const float cf = reinterpret_cast<const float*>(slot + a.off_cs)[bb];
-            const float ratio = __fdiv_rn(cf, S);  // a power of two (both c = 2^e / 127)
-            const uint32_t w0[4] = {d0.x, d0.y, d0.z, d0.w}, w1[4] = {d1.x, d1.y, d1.z, d1.w},
-                           w2[4] = {d2.x, d2.y, d2.z, d2.w};
+            const uint8_t* dg = slot + a.off_dig + 8 * bq;
+            const uint2 d0 = *reinterpret_cast<const uint2*>(dg + (size_t)bb * 64);
+            const uint2 d1 = *reinterpret_cast<const uint2*>(dg + (size_t)(a.bp + bb) * 64);
+            const uint2 d2 = *reinterpret_cast<const uint2*>(dg + (size_t)(2 * a.bp + bb) * 64);
+            const float ratio = reinterpret_cast<const float*>(slot + a.off_cs)[bb] * inv_s;
+            const uint32_t w0[2] = {d0.x, d0.y}, w1[2] = {d1.x, d1.y}, w2[2] = {d2.x, d2.y};
 #pragma unroll
-            for (int u = 0; u < 16; u += 2) {
+            for (int u = 0; u < 8; u += 2) {
               float v[2];
 #pragma unroll
               for (int e = 0; e < 2; ++e) {
                 const int k = u + e;
-                const float x0 = (float)(int)((w0[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
-                const float x1 = (float)(int)((w1[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
-                const float x2 = (float)(int)((w2[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
+                const float x0 = (float)((w0[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
+                const float x1 = (float)((w1[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
+                const float x2 = (float)((w2[k >> 2] >> (8 * (k & 3))) & 0xffu) - 127.f;
                 v[e] = ratio * (x0 + (x1 + x2 * kInv254) * kInv254);
               }
               const __half2 h = __floats2half2_rn(v[0], v[1]);
@@ -402,20 +399,11 @@ __global__ void __launch_bounds__(kLmThreads, 1) l2mma_kernel(const __grid_const
               ph[u >> 1] = *reinterpret_cast<const uint32_t*>(&h);
               pl[u >> 1] = *reinterpret_cast<const uint32_t*>(&l);
             }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) ph[i] = pl[i] = 0u;
           }
-          uint8_t* brow_h = slot + a.off_b + (size_t)bb * 128;
-          uint8_t* brow_l = slot + a.off_b + (size_t)(a.bp + bb) * 128;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const int chunk = 2 * bq + c;
-            *reinterpret_cast<uint4*>(brow_h + ((chunk ^ (bb & 7)) << 4)) =
-                make_uint4(ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
-            *reinterpret_cast<uint4*>(brow_l + ((chunk ^ (bb & 7)) << 4)) =
-                make_uint4(pl[4 * c], pl[4 * c + 1], pl[4 * c + 2], pl[4 * c + 3]);
-          }
+          const int sw = (bq ^ (bb & 7)) << 4;  // rows bb and bp + bb share (row & 7)
+          *reinterpret_cast<uint4*>(slot + a.off_b + (size_t)bb * 128 + sw) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+          *reinterpret_cast<uint4*>(slot + a.off_b + (size_t)(a.bp + bb) * 128 + sw) =
+              make_uint4(pl[0], pl[1], pl[2], pl[3]);
         }
         fence_proxy_async_smem();
         __syncwarp();
