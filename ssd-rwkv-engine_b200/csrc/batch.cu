@@ -117,7 +117,6 @@ int bg_setup(BgArgs* a, const BgJob* jobs, int njobs, const BgDigits* dg, int nd
   a->stages = (int)std::min<size_t>(kBgMaxStages, (kBgSmemBudget - 1024) / stage_bytes);
   if (a->stages < 2) return RWKVB_EUNSUPPORTED;
   a->idesc = idesc_u8u8_s32(128, a->nrows);
-  a->spin_limit = 1u << 22;
   a->err = err_word;
   int pmax = 1;
   for (int j = 0; j < njobs; ++j) {
@@ -1836,23 +1835,22 @@ int lm_setup(LmArgs* a, const LmJob* jobs, int njobs, int nb, int sms, int pcap,
   }
   a->nmat = njobs;
   a->total = total;
-  // slot: A tile | B tile (2 bp rows) | codes | records | digit rows | scales
-  a->off_b = kLmATile;
-  a->off_codes = a->off_b + 256 * a->bp;
-  a->off_recs = a->off_codes + 2048;
-  a->off_dig = a->off_recs + 2048;
-  a->off_cs = a->off_dig + 192 * a->bp;
-  a->slot_bytes = (a->off_cs + 4 * a->bp + 1023) & ~1023;
+  // operand slot: A tile | B tile (3 bp rows); raw slot: codes | records |
+  // digit rows | scales
+  a->op_bytes = (kLmATile + 384 * a->bp + 1023) & ~1023;
+  a->r_dig = 4096;
+  a->r_cs = a->r_dig + 192 * a->bp;
+  a->raw_bytes = (a->r_cs + 4 * a->bp + 127) & ~127;
   a->tx_bytes = (uint32_t)(2048 + 2048 + 192 * a->bp + 4 * a->bp);
-  a->stages = (int)std::min<size_t>(kLmMaxStages, (kBgSmemBudget - 1024) / (size_t)a->slot_bytes);
-  if (a->stages < 2) return RWKVB_EUNSUPPORTED;
-  a->idesc = idesc_f16f16_f32(128, 2 * a->bp);
-  a->spin_limit = 1u << 22;
+  const size_t room = kBgSmemBudget - 1024 - (size_t)kLmOps * a->op_bytes;
+  a->rstages = (int)std::min<size_t>(kLmMaxRaw, room / (size_t)a->raw_bytes);
+  if (a->rstages < 2) return RWKVB_EUNSUPPORTED;
+  a->idesc = idesc_f16f16_f32(128, 3 * a->bp);
   a->err = err_word;
   int n = std::min(sms, total);
   while (n > 1 && lm_pmax(*a, n) > pcap) --n;
   *grid = n;
-  *smem = (size_t)a->stages * a->slot_bytes + 1024;
+  *smem = (size_t)kLmOps * a->op_bytes + (size_t)a->rstages * a->raw_bytes + 1024;
   return RWKVB_OK;
 }
 

@@ -98,7 +98,6 @@ struct BgArgs {
   int nb, bp, nrows;              // sessions, padded sessions, digit rows (= MMA N)
   int stages;                     // ring slots
   uint32_t idesc;
-  uint32_t spin_limit;
   int* err;
 };
 
@@ -140,7 +139,7 @@ __device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, const Bg
   int ok = 0;
   if ((threadIdx.x & 31) == 0) {
     if (!*abort_flag) {
-      ok = mbar_wait_bounded(bar, parity, a.spin_limit) ? 1 : 0;
+      ok = mbar_wait_suspend(bar, parity) ? 1 : 0;
       if (!ok) {
         atomicOr(a.err, kErrTimeout);
         *abort_flag = 1;
@@ -234,7 +233,7 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
     // the copies still in flight are among the last min(stages, use) issues
     if (lane == 0)
       for (uint32_t u = use > (uint32_t)a.stages ? use - a.stages : 0; u < use; ++u)
-        mbar_wait_bounded(&full[u % a.stages], (u / a.stages) & 1, a.spin_limit);
+        mbar_wait_suspend(&full[u % a.stages], (u / a.stages) & 1);
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -274,7 +273,7 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
     // every MMA issued so far has completed once done_bar's phase 0 ends
     if (lane == 0) {
       umma_commit(&done_bar);
-      mbar_wait_bounded(&done_bar, 0, a.spin_limit);
+      mbar_wait_suspend(&done_bar, 0);
     }
     __syncwarp();
   } else {
