@@ -57,7 +57,7 @@ constexpr int kLmThreads = kLmWarps * 32;
 constexpr int kLmBuildWarps = 16;  // warps 6..21
 constexpr int kLmMaxMats = 3;
 constexpr int kLmMaxRaw = 8;  // raw-copy ring slots (codes, records, digit rows, scales)
-constexpr int kLmOps = 3;     // operand ring slots (A and B tiles)
+constexpr int kLmOps = 4;     // operand ring slots (A and B tiles)
 constexpr int kLmAccStride = 256;  // TMEM columns between the two accumulators
 constexpr int kLmTmemCols = 512;
 constexpr int kLmATile = 128 * 128;  // A: 128 rows x 64 fp16
