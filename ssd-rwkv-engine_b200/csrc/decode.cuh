@@ -52,6 +52,7 @@ constexpr int kDThreads = kDT + 32;    // + producer warp
 constexpr int kDMaxSt = 8;             // ring slots (upper bound)
 constexpr int kDBar = 1;               // named barrier of the consumers
 constexpr int kDMaxItems = 8;          // adapter first-stage items per CTA
+constexpr int kDPartTiles = 8;         // GEMV tiles whose per-warp partial sums are buffered per CTA reduction
 constexpr int kDMaxPieces = 8;         // adapter second-stage tile pieces per layer
 constexpr int kDMisc = 2560;           // misc shared floats
 static_assert(kDW * 4 * 64 <= kDMisc, "phase-B adapter partials [warps][4][64] live in misc");
@@ -144,6 +145,13 @@ __device__ __forceinline__ int d_rank(const Dims& d, int m) {
   return m == 0 ? d.rw : (m == 1 ? d.ra : (m == 2 ? d.rg : d.rv));
 }
 
+// Adapter (0 w, 1 a, 2 g, 3 v) of first-stage item `item`.
+__device__ __forceinline__ int d_item_mat(const Dims& d, int item) {
+  int m = 0;
+  while (m < 3 && item >= d.abase[m + 1]) ++m;
+  return m;
+}
+
 __device__ __forceinline__ int d_rank_off(const Dims& d, int m) {
   return m == 0 ? 0 : (m == 1 ? d.rw : (m == 2 ? d.rw + d.ra : d.rw + d.ra + d.rg));
 }
@@ -156,7 +164,7 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
   d_range(F / 16, nc, G, bx, T.r[2]);
   d_range(C / 16, nf, G, bx, T.r[3]);
   d_range((a.d.V + 15) / 16, nc, G, bx, T.r[4]);
-  const int items3 = 3 * a.d.adp_splits, items4 = 4 * a.d.adp_splits;
+  const int items3 = a.d.abase[3], items4 = a.d.abase[4];
   T.nitem[0] = T.nitem[1] = 0;
   for (int it = bx; it < items4 && T.nitem[1] < kDMaxItems; it += G) {
     T.item[T.nitem[1]++] = it;
@@ -328,10 +336,10 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
         ok = units(T.r[0], M.q, M.p, ct);
         for (int k = 0; ok && k < T.nitem[l == 0 ? 0 : 1]; ++k) {
           const int item = T.item[k];
-          const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
+          const int m = d_item_mat(a.d, item);
           const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
           const int R = W.cols;
-          const int i0 = sp * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows);
+          const int i0 = (item - a.d.abase[m]) * a.d.arow[m], i1 = min(C, i0 + a.d.arow[m]);
           const uint32_t qb = (uint32_t)((i1 - i0) * R);
           const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg) & ~1u;
           const uint32_t g1 = ((uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) + 1) + 1u) & ~1u;
@@ -654,13 +662,14 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
   float* const part = reinterpret_cast<float*>(sm + a.o_part);
   unsigned long long* tr = (a.trace && blockIdx.x == 0 && t == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
   const int tr_n = 2 * a.trace_cap;
-  int seq = c.seq, pbuf = c.pbuf;
+  int seq = c.seq;
   bool dead = c.dead;
   const int pofs = L.ra * pr + ((warp << 7) >> lg);
   float acc0 = 0.f, acc1 = 0.f;
   int cur_set = -1;
   XDigits X{};
   int tile = u0 / nch, chunk = u0 - tile * nch;
+  int nt = 0, ftile = tile;  // tiles buffered in `part`, the first of them
 #pragma unroll 1
   for (int u = u0; u < u1; ++u) {
     const int set = per_set ? tile / per_set : 0;
@@ -690,22 +699,31 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
     if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 2] = global_ns();
     ++seq;
     if (chunk == nch - 1 || u == u1 - 1) {
+      // tile end: this warp's partial sums of the tile's 16 rows go to the
+      // buffer; the CTA sums them over warps (in warp order) and adds each row
+      // to `out` once per kDPartTiles tiles instead of meeting at every tile
       acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
       acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-      float* pt = part + pbuf * (kDW * 16);
+      float* pt = part + nt * (kDW * 16);
       if ((lane & 3) == 0) {
         pt[warp * 16 + L.ra] = acc0;
         pt[warp * 16 + L.ra + 8] = acc1;
       }
       acc0 = acc1 = 0.f;
-      d_csync();
-      if (t < 16) {
-        float v = 0.f;
-        for (int w = 0; w < nb; ++w) v += pt[w * 16 + t];
-        const int row = tile * 16 + t;
-        if (row < rows_total && !dead) atomicAdd(out + row, v);
+      if (++nt == kDPartTiles || u == u1 - 1) {
+        d_csync();
+#pragma unroll 1
+        for (int i = t; i < nt * 16; i += kDT) {
+          const float* q = part + (i >> 4) * (kDW * 16) + (i & 15);
+          float v = 0.f;
+          for (int w = 0; w < nb; ++w) v += q[w * 16];
+          const int row = (ftile + (i >> 4)) * 16 + (i & 15);
+          if (row < rows_total && !dead) atomicAdd(out + row, v);
+        }
+        d_csync();  // the buffer is rewritten next
+        nt = 0;
+        ftile = tile + 1;
       }
-      pbuf ^= 1;
     }
     if (++chunk == nch) {
       chunk = 0;
@@ -713,7 +731,6 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
     }
   }
   c.seq = seq;
-  c.pbuf = pbuf;
   c.dead = dead;
 }
 
@@ -725,12 +742,12 @@ __device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, 
   const LayerDev& Ly = a.layers[l];
   for (int k = 0; k < T.nitem[l == 0 ? 0 : 1]; ++k) {
     const int item = T.item[k];
-    const int m = item / a.d.adp_splits, sp = item - m * a.d.adp_splits;
+    const int m = d_item_mat(a.d, item);
     const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
     const float* mix = m == 0 ? Ly.x_w : (m == 1 ? Ly.x_a : (m == 2 ? Ly.x_g : Ly.x_v));
     const int R = W.cols, wlg = W.lg;
-    const int i0 = sp * a.d.adp_rows, i1 = min(C, i0 + a.d.adp_rows), nr = i1 - i0;
-    float* xm = misc;          // [adp_rows]
+    const int i0 = (item - a.d.abase[m]) * a.d.arow[m], i1 = min(C, i0 + a.d.arow[m]), nr = i1 - i0;
+    float* xm = misc;          // [arow[m] <= 256]
     float* pacc = misc + 256;  // [nrg][R]
     #pragma unroll 1
     for (int i = t; i < nr; i += kDT) xm[i] = TV[i0 + i] + (PV[i0 + i] - TV[i0 + i]) * __ldg(mix + i0 + i);

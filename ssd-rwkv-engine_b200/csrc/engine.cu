@@ -78,7 +78,10 @@ struct Bufs {
 struct Dims {
   int L, C, H, F, V;
   int rw, ra, rg, rv, rtot;  // adapter ranks, total
-  int adp_splits, adp_rows;  // first-adapter row chunks
+  int adp_splits, adp_rows;  // first-adapter row chunks (multi-kernel path)
+  // persistent kernel: first-adapter items of adapter m (w, a, g, v) are
+  // arow[m]-row chunks, numbered abase[m] .. abase[m + 1] - 1 (v last)
+  int arow[4], abase[5];
   int hist_cap;
 };
 
@@ -920,10 +923,32 @@ bool plan_decode(rwkvb_engine* e) {
     rmax = ranks[m] > rmax ? ranks[m] : rmax;
   }
   if (rmax > kDMisc - 256) return false;
+  // First-adapter items: per adapter the largest row chunk (a power of two up
+  // to 256 dividing C) whose codes and (min,max) pairs fit a GEMV unit's ring
+  // slot, so the slot stays the unit's size; items are numbered adapter by
+  // adapter (v last: layer 0 has none).  2.9B: 128/128/32/128 rows, 140 items,
+  // at most one per CTA.
+  int alg = 30;
+  for (int i = 0; i < d.L; ++i) {
+    const LayerDev& l = e->layers[i];
+    const PackedView* w1s[4] = {&l.w1, &l.a1, &l.g1, &l.v1};
+    for (int m = 0; m < (i > 0 ? 4 : 3); ++m) alg = w1s[m]->lg < alg ? w1s[m]->lg : alg;
+  }
+  auto item_bytes = [&](uint32_t nel) { return (nel + 15u) / 16u * 16u + ((nel >> alg) + 4u) * 8u; };
+  const uint32_t unit_b = a.code_b + a.pair_b;
+  e->d.abase[0] = 0;
+  for (int m = 0; m < 4; ++m) {
+    int r = 256;
+    while (r > 16 && (d.C % r != 0 || item_bytes((uint32_t)(r * ranks[m])) > unit_b)) r /= 2;
+    e->d.arow[m] = r;
+    e->d.abase[m + 1] = e->d.abase[m] + (ranks[m] > 0 ? (d.C + r - 1) / r : 0);
+  }
   // slot: one GEMV unit, one adapter first-stage item, one adapter second-stage piece
-  uint32_t slot = a.code_b + a.pair_b;
-  const uint32_t item = (uint32_t)(d.adp_rows * rmax + 15) / 16 * 16 + (uint32_t)((d.adp_rows * rmax >> 4) + 4) * 8u;
-  slot = slot > item ? slot : item;
+  uint32_t slot = unit_b;
+  for (int m = 0; m < 4; ++m) {
+    const uint32_t item = item_bytes((uint32_t)(d.arow[m] * ranks[m]));
+    slot = slot > item ? slot : item;
+  }
   for (int m = 0; m < 4; ++m) slot = slot > (uint32_t)a.abr[m] * 80u ? slot : (uint32_t)a.abr[m] * 80u;
   a.slot = (slot + 1023u) / 1024u * 1024u;
   auto set_bytes = [&](int K) { return ((uint32_t)K * 3u + 2u * (uint32_t)(K / a.fg) * 4u + 15u) & ~15u; };
@@ -934,7 +959,7 @@ bool plan_decode(rwkvb_engine* e) {
   dig = dig > wkv ? dig : wkv;
   dig = (dig + 127u) & ~127u;
   const uint32_t vec = ((uint32_t)d.C * 4u + 127u) & ~127u;
-  const uint32_t rest = dig + 4u * vec + 2u * kDW * 16u * 4u + (uint32_t)kDMisc * 4u;
+  const uint32_t rest = dig + 4u * vec + (uint32_t)kDPartTiles * kDW * 16u * 4u + (uint32_t)kDMisc * 4u;
   const uint32_t budget = 227u * 1024u - 1024u - 3u * 1024u;  // dynamic-smem alignment slack, static shared
   int nst = kDMaxSt;
   while (nst > 3 && (uint32_t)nst * a.slot + rest > budget) --nst;
@@ -946,7 +971,7 @@ bool plan_decode(rwkvb_engine* e) {
   a.o_xb = off;   off += vec;
   a.o_t = off;    off += vec;
   a.o_p = off;    off += vec;
-  a.o_part = off; off += 2u * kDW * 16u * 4u;
+  a.o_part = off; off += (uint32_t)kDPartTiles * kDW * 16u * 4u;
   a.o_misc = off; off += (uint32_t)kDMisc * 4u;
   a.smem_total = off;
   // tensor maps
