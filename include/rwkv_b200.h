@@ -207,7 +207,10 @@ typedef struct rwkvb_engine rwkvb_engine;
  *        bit8 = bits 4..7 give an explicit L2-prefetch distance in phases;
  *        bit9 = load the persistent kernel's weight stream without the L2
  *               evict-first policy (default: weights evict first, so the
- *               state and activations re-read every layer stay in L2). 
+ *               state and activations re-read every layer stay in L2);
+ *        bits 12..15 = ring slots of weight tiles in flight per SM in the
+ *               persistent kernel, 3..8 (0: the default, 3 -- deeper rings
+ *               delay the kernel's own small loads behind the weight stream). 
  * When every projection is SG8 with one power-of-two group size and the
  * 16-byte layout that rwkvb upload placement gives, decode runs as ONE
  * cooperative persistent launch per call (all tokens, all layers); otherwise

@@ -50,6 +50,7 @@ constexpr int kDW = 10;                // consumer warps
 constexpr int kDT = kDW * 32;          // consumer threads
 constexpr int kDThreads = kDT + 32;    // + producer warp
 constexpr int kDMaxSt = 8;             // ring slots (upper bound)
+constexpr int kDRingDefault = 3;       // ring slots unless the engine flags ask for more
 constexpr int kDBar = 1;               // named barrier of the consumers
 constexpr int kDMaxItems = 8;          // adapter first-stage items per CTA
 constexpr int kDPartTiles = 8;         // GEMV tiles whose per-warp partial sums are buffered per CTA reduction

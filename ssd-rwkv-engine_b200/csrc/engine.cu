@@ -961,7 +961,13 @@ bool plan_decode(rwkvb_engine* e) {
   const uint32_t vec = ((uint32_t)d.C * 4u + 127u) & ~127u;
   const uint32_t rest = dig + 4u * vec + (uint32_t)kDPartTiles * kDW * 16u * 4u + (uint32_t)kDMisc * 4u;
   const uint32_t budget = 227u * 1024u - 1024u - 3u * 1024u;  // dynamic-smem alignment slack, static shared
-  int nst = kDMaxSt;
+  // Ring depth: the consumers' own small loads (accumulators, vectors) queue
+  // behind the weight tiles in flight on their SM, so a deeper ring than the
+  // HBM latency needs lengthens every step of the per-layer dependency chain
+  // (2.9B bs1: 448 tok/s with 3 slots, 434 with 6).  Flag bits 12..15 set
+  // another depth (3..8).
+  const int nst_cap = (int)((e->flags >> 12) & 0xFu);
+  int nst = nst_cap ? (nst_cap < 3 ? 3 : (nst_cap < kDMaxSt ? nst_cap : kDMaxSt)) : kDRingDefault;
   while (nst > 3 && (uint32_t)nst * a.slot + rest > budget) --nst;
   if ((uint32_t)nst * a.slot + rest > budget) return false;
   a.nst = nst;

@@ -116,7 +116,7 @@ class B200Engine:
 
     def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
                  prefetch_distance: int | None = None, persistent: bool = True, trace: bool = False,
-                 l2_policy: bool = True):
+                 l2_policy: bool = True, ring_slots: int | None = None):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
@@ -134,6 +134,8 @@ class B200Engine:
                 flags |= native.FLAG_NO_L2_POLICY
             if prefetch_distance is not None:
                 flags |= native.FLAG_EXPLICIT_PREFETCH | ((int(prefetch_distance) & 0xF) << 4)
+            if ring_slots is not None:
+                flags |= (int(ring_slots) & 0xF) << native.FLAG_RING_SLOTS_SHIFT
             h = ctypes.c_void_p()
             native.check(self.lib.rwkvb_engine_create(ctypes.byref(md), flags, ctypes.byref(h)),
                          "rwkvb_engine_create")
