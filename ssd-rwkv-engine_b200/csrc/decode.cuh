@@ -1168,7 +1168,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_zero(acc_fo, T.zc0, T.zc1);
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
-        a.b.att_x[(size_t)l * C + i] = ln_val(X[i], s_stat[0], s_stat[1], __ldg(Ly.ln1_w + i), __ldg(Ly.ln1_b + i));
+        a.b.att_x[(size_t)l * C + i] = TV[i];  // ln1 output of phase A, still in shared memory
       d_build<LFK>(DSrc{2, nullptr, nullptr, a.b.att_y}, C, dig);
       d_mark(a, c);  // C prep done
       d_units<LFK>(a, c, T.r[1], dig, 0, C, 0, acc_ao, C);
@@ -1217,7 +1217,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_zero(acc_ao, T.zc0, T.zc1);
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
-        a.b.ffn_x[(size_t)l * C + i] = ln_val(XB[i], s_stat[2], s_stat[3], __ldg(Ly.ln2_w + i), __ldg(Ly.ln2_b + i));
+        a.b.ffn_x[(size_t)l * C + i] = TV[i];  // ln2 output of phase D, still in shared memory
       d_mark(a, c);  // E slices stored
       d_build<LFK>(DSrc{3, nullptr, nullptr, acc_hk}, F, dig);
       d_mark(a, c);  // E prep done
