@@ -219,10 +219,10 @@ __device__ __noinline__ int d_acquire(const DArgs& a, uint64_t* empty, volatile 
   const int slot = seq % a.nst;
   if (seq >= a.nst) {
     const uint32_t par = (uint32_t)((seq / a.nst - 1) & 1);
-    uint32_t i = 0;
-    while (!mbar_try_wait(&empty[slot], par)) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait_hint(&empty[slot], par, 20000u)) {  // suspended, not spinning, while the ring is full
       if (*abort_flag) return -1;
-      if (++i > a.spin_limit) {
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
         atomicOr(a.b.err, kErrTimeout);
         *abort_flag = 1;
         return -1;
@@ -245,7 +245,7 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
                                            int per_map, uint8_t* ring, uint64_t* full, uint64_t* empty,
                                            volatile int* abort_flag, int& seq_io) {
   const int nst = a.nst, nb = a.nb, pr8 = a.pr * 8, u0 = R.u0, u1 = R.u1, nch = R.nch;
-  const uint32_t slot_b = a.slot, code_b = a.code_b, bytes = a.code_b + a.pair_b, limit = a.spin_limit;
+  const uint32_t slot_b = a.slot, code_b = a.code_b, bytes = a.code_b + a.pair_b;
   unsigned long long* tr = (a.trace && blockIdx.x == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
   const int tr_n = 2 * a.trace_cap;
   int seq = seq_io;
@@ -259,9 +259,9 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     const int slot = seq % nst;
     if (seq >= nst) {
       const uint32_t par = (uint32_t)((seq / nst - 1) & 1);
-      uint32_t i = 0;
-      while (!mbar_try_wait(&empty[slot], par)) {
-        if (*abort_flag || ++i > limit) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait_hint(&empty[slot], par, 20000u)) {
+        if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
           if (!*abort_flag) {
             atomicOr(a.b.err, kErrTimeout);
             *abort_flag = 1;
@@ -623,7 +623,7 @@ __device__ __noinline__ void d_ln_mix(const DArgs& a, DCons& c, const DLnMix& q,
 __device__ __forceinline__ const uint8_t* d_slot_wait(const DArgs& a, DCons& c) {
   const int slot = c.seq % a.nst;
   if (!c.dead) {
-    const bool got = mbar_wait_bounded(&c.full[slot], (uint32_t)((c.seq / a.nst) & 1), a.spin_limit);
+    const bool got = mbar_wait_suspend(&c.full[slot], (uint32_t)((c.seq / a.nst) & 1));
     if (!__all_sync(0xffffffffu, got)) {
       c.dead = 1;
       if ((threadIdx.x & 31) == 0) {
@@ -656,7 +656,7 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const ImmaLane L = imma_lane();
   const int nst = a.nst, nb = a.nb, pr = a.pr, lg = a.lg, kch = a.kc >> 5, u0 = R.u0, u1 = R.u1, nch = R.nch;
-  const uint32_t slot_b = a.slot, code_b = a.code_b, limit = a.spin_limit;
+  const uint32_t slot_b = a.slot, code_b = a.code_b;
   uint8_t* const sm = c.sm;
   uint64_t* const full = c.full;
   uint64_t* const empty = c.empty;
@@ -681,7 +681,7 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
     const int slot = seq % nst;
     const uint8_t* sl = sm + (size_t)slot * slot_b;
     if (!dead) {
-      const bool got = mbar_wait_bounded(&full[slot], (uint32_t)((seq / nst) & 1), limit);
+      const bool got = mbar_wait_suspend(&full[slot], (uint32_t)((seq / nst) & 1));
       if (!__all_sync(0xffffffffu, got)) {
         dead = true;
         if (lane == 0) {

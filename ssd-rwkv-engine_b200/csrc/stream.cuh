@@ -78,6 +78,18 @@ __device__ __forceinline__ bool mbar_wait_suspend(uint64_t* bar, uint32_t parity
   }
 }
 
+// One poll of phase `parity` of `bar` that may suspend the thread in hardware
+// for up to `hint_ns` (it resumes as soon as the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // 1-D bulk copy global -> shared (this CTA), completion counted on `bar`.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
