@@ -42,7 +42,6 @@ from pathlib import Path
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "ssd-rwkv-engine_b200"))
 sys.path.insert(0, str(REPO))
-os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
@@ -137,6 +136,27 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sms)}
 
 
+def metric_name(args, bs: int = 1) -> str:
+    """The headline metric string, identical in both arms."""
+    codec = "U8" if args.policy == "sg8" else "LUT2"
+    return f"RWKV-7 {args.config} {codec} decode tok/s (bs{bs})"
+
+
+def cpu_threads() -> int:
+    """Set the CPU library's OpenMP threads to all physical host cores
+    explicitly (torchrun exports OMP_NUM_THREADS=1 to every rank) and return
+    the count in effect."""
+    from oracle import kernels as ok
+
+    impl = "reference" if ok.ref_available() else "oracle"
+    return ok.set_threads(ok.host_threads(), impl)
+
+
+CPU_SAMPLE = ("the oracle's restatement of forward_block_packed (NumPy fp32 glue; the reference's Python "
+              "package cannot travel to the GPU host) calling the reference's own lut2_gather.c kernels "
+              "(oracle/_ref, built -O3 -mavx2 -mfma -fopenmp from its source) for every GEMV")
+
+
 def bytes_per_token(pack, shape) -> int:
     """Algorithmic HBM bytes of one decode token: every packed matrix read once
     (embedding: one row; layer 0's unused v1/v2 excluded), skeleton vectors,
@@ -158,13 +178,16 @@ def bytes_per_token(pack, shape) -> int:
 
 
 def run_reference(args, shape, rank: int) -> dict:
-    """The reference's C kernels (oracle/_ref) driving the packed forward on the host."""
+    """The reference's C kernels (oracle/_ref) driving the packed forward on
+    all physical host cores: the same seeded model and prompt as the b200 arm,
+    then greedy decode steps, each step one token (bounded by a time budget)."""
     from oracle import kernels as ok
     from oracle.forward import OracleRWKV7
     from rwkv_b200 import synth
 
     if not ok.ref_available():
         return {"impl": "reference", "unavailable": "reference C kernels (oracle/_ref) not built"}
+    cores = cpu_threads()
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     pack = synth.pack_to_host(synth.make_pack_streaming(shape, SEED, dev, policy=args.policy))
     if dev == "cuda":
@@ -173,7 +196,7 @@ def run_reference(args, shape, rank: int) -> dict:
                         impl="reference")
     state = model.zero_state()
     prompt = synth.seeded_prompt(PROMPT, shape.vocab, SEED)
-    for t in prompt[:2]:
+    for t in prompt:
         logits = model.forward_token(t, state)
     tok = int(np.argmax(logits))
     for _ in range(args.warmup):
@@ -189,16 +212,15 @@ def run_reference(args, shape, rank: int) -> dict:
             break
     dt = time.perf_counter() - t0
     v = n / dt
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {"metric": f"RWKV-7 {args.config} {args.policy.upper()} decode tok/s (bs1)", "value": v,
+    return {"metric": metric_name(args), "value": v,
             "unit": "tok/s", "n_gpus": args.gpus, "steps": n, "warmup": args.warmup, "ms_per_step": 1e3 * dt / n,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"rwkv7-{args.config} {args.policy} bs1 greedy decode", "batch": 1},
-            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+            "config": {"workload": f"rwkv7-{args.config} {args.policy} bs1 greedy decode, {PROMPT}-token prompt",
+                       "batch": 1},
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
                              "sample": f"{n} decode tokens (time budget {args.ref_budget_s}s) after "
-                                       f"{args.warmup} warm-up tokens: reference lut2_gather.c GEMVs "
-                                       f"(oracle/_ref, -O3 -mavx2 -mfma -fopenmp) + NumPy fp32 glue"},
+                                       f"{args.warmup} warm-up tokens, {cores} OpenMP threads: " + CPU_SAMPLE},
             "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -403,31 +425,39 @@ def synth_prompt(n: int, vocab: int, seed: int) -> list[int]:
     return synth.seeded_prompt(n, vocab, seed)
 
 
-def cpu_baseline(pack_dev, shape, args) -> dict:
+def cpu_baseline(pack_dev, shape, args, gpu_ids: list[int]) -> dict:
+    """The same model on the host cores (reference C kernels inside the
+    oracle's forward), from the same prompt: greedy ids compared with the GPU
+    decode's ids (``ids_match_oracle``) and decode tokens per second."""
     from oracle import kernels as ok
     from oracle.forward import OracleRWKV7
     from rwkv_b200 import synth
 
     impl = "reference" if ok.ref_available() else "oracle"
+    cores = cpu_threads()
     pack = synth.pack_to_host(pack_dev)
     model = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size, impl=impl)
     st = model.zero_state()
-    logits = model.forward_token(1, st)
+    for t in synth.seeded_prompt(PROMPT, shape.vocab, SEED):
+        logits = model.forward_token(t, st)
     tok = int(np.argmax(logits))
+    ids = [tok]
     t0 = time.perf_counter()
     n = 0
     while n < 64:
         logits = model.forward_token(tok, st)
         tok = int(np.argmax(logits))
+        ids.append(tok)
         n += 1
         if time.perf_counter() - t0 > args.cpu_budget_s:
             break
     dt = time.perf_counter() - t0
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": "reference" if impl == "reference" else "port",
-            "sample": f"{n} decode tokens of the same {args.config} {args.policy} model "
-                      f"({dt:.1f}s) through the packed forward with "
-                      + ("the reference's lut2_gather.c GEMVs" if impl == "reference" else "the oracle C GEMVs")}
+    k = min(len(ids), len(gpu_ids))
+    return {"value": n / dt, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} decode tokens of the same {args.config} {args.policy} model after the same "
+                      f"{PROMPT}-token prompt ({dt:.1f}s), {cores} OpenMP threads: "
+                      + (CPU_SAMPLE if impl == "reference" else "the oracle's C GEMVs"),
+            "ids_compared": k, "ids_match": ids[:k] == [int(v) for v in gpu_ids[:k]]}
 
 
 def main() -> None:
@@ -508,6 +538,8 @@ def main() -> None:
     eng.decode_greedy_async(first, args.warmup, out)
     torch.cuda.synchronize(dev)
     nxt = int(out[args.warmup - 1].item())
+    # the greedy sequence after the prompt: first, the warm-up ids, then the timed ids
+    gpu_ids = [first] + [int(v) for v in out[:args.warmup].cpu().tolist()]
 
     if world > 1:
         dist.barrier()
@@ -525,6 +557,7 @@ def main() -> None:
     torch.cuda.synchronize(dev)
     _nvtx_pop()
     ms = t0.elapsed_time(t1)
+    gpu_ids += [int(v) for v in out[:args.steps].cpu().tolist()]
     clk = clocks.stop() if rank == 0 else {}
     ms = replicas.max_over_ranks(ms)
     if world > 1:
@@ -580,8 +613,7 @@ def main() -> None:
             except Exception:
                 traffic = None
         res = {
-            "metric": f"RWKV-7 {args.config} U8 decode tok/s (bs1)" if args.policy == "sg8"
-            else f"RWKV-7 {args.config} LUT2 decode tok/s (bs1)",
+            "metric": metric_name(args),
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (u8/2-bit weights)", "data": "synthetic (seeded random RWKV-7 weights, reference codecs)",
@@ -612,7 +644,10 @@ def main() -> None:
             res["tp"] = tpres
         if cpu_pack is not None:
             backend.close()
-            res["cpu_baseline"] = cpu_baseline(cpu_pack, shape, args)
+            cb = cpu_baseline(cpu_pack, shape, args, gpu_ids)
+            res["ids_match_oracle"] = cb.pop("ids_match")
+            res["ids_compared"] = cb.pop("ids_compared")
+            res["cpu_baseline"] = cb
         print(json.dumps(res), flush=True)
     backend.close()
     if world > 1:

@@ -127,7 +127,9 @@ int rwkvb_cmix_gemv_f32(float* y, const rwkvb_packed* key, const rwkvb_packed* v
  *     RWKVB_ESCRATCH before touching the device.
  *   - The first call on a device (with that device current) resolves the
  *     buffer's address with cudaGetSymbolAddress; make that first call before
- *     any stream capture.  Later calls make no allocating CUDA call.
+ *     any stream capture.  The address is kept per context: after a
+ *     cudaDeviceReset the next call resolves it again in the new context.
+ *     No call makes an allocating CUDA call.
  *   - Nothing has to start at zero: the key GEMV writes every intermediate
  *     element before the value GEMV reads it.
  *   - One buffer per device: calls that overlap on one device (different
@@ -286,7 +288,12 @@ typedef struct rwkvb_batch rwkvb_batch;
  *               finishes; the GEMMs stream their first weight tiles before
  *               waiting on it).  Always off under tensor parallelism;
  *        bit2 = LUT2 engines: products on the CUDA cores (fp32 FMA) instead
- *               of the tensor cores (a cross-check path). */
+ *               of the tensor cores (a cross-check path);
+ *        bits 16..19 = tensor parallelism with peer exchange: wall-time limit
+ *               of one exchange wait in units of 100 ms (0: 5 s).  When a
+ *               peer does not arrive in time the step's later exchanges return
+ *               at once and the next synchronising call reports RWKVB_ETIMEOUT
+ *               (clearing the error word). */
 int rwkvb_batch_create(const rwkvb_model_desc* desc, int32_t batch, uint32_t flags, rwkvb_batch** out);
 
 /* Tensor parallelism across the GPUs of one node (one process per GPU), the

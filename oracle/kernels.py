@@ -11,6 +11,7 @@ dispatch (``rwkv_ssd/runtime/lut_gemm_fused.py:467-724``, ``:1336-1373``,
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
@@ -43,6 +44,40 @@ def lib(impl: str = "oracle") -> ctypes.CDLL:
     h = ctypes.CDLL(str(path))
     _libs[impl] = h
     return h
+
+
+def host_threads() -> int:
+    """Threads a CPU run may use: the physical cores of the host, bounded by
+    this process's CPU affinity."""
+    try:
+        avail = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        avail = os.cpu_count() or 1
+    try:
+        import psutil
+
+        phys = psutil.cpu_count(logical=False) or avail
+    except Exception:  # noqa: BLE001
+        phys = avail
+    return max(1, min(avail, phys))
+
+
+def set_threads(n: int, impl: str = "reference") -> int:
+    """Set the OpenMP thread count of a CPU library explicitly (an inherited
+    ``OMP_NUM_THREADS``, e.g. torchrun's 1, would otherwise win) and return it.
+    ``omp_set_num_threads`` is looked up through the library's handle, so it is
+    the OpenMP runtime that library actually links."""
+    n = max(1, int(n))
+    os.environ["OMP_NUM_THREADS"] = str(n)
+    h = lib(impl)
+    try:
+        h.omp_set_num_threads(ctypes.c_int(n))
+    except AttributeError:
+        pass
+    try:
+        return int(h.omp_get_max_threads())
+    except AttributeError:
+        return n
 
 
 def ref_available() -> bool:

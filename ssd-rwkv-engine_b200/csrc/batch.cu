@@ -1476,23 +1476,31 @@ __device__ __forceinline__ uint32_t* bt_x_flag(char* base, size_t flags_off, int
   return reinterpret_cast<uint32_t*>(base + flags_off) + ((size_t)inst * kBtMaxRanks + src) * kBtXCtas + cta;
 }
 
+// Wall-time bound of one peer-exchange wait: well above the skew between the
+// rank processes' launches of their step graphs (scheduling, host jitter).
+constexpr uint64_t kTpWaitLimitNs = 5000000000ull;  // 5 s
+
 // Thread 0: release this CTA's flag of instance `inst` in every peer, then wait
-// (bounded) for every peer's flag; false when a wait gave up (error word set).
+// (bounded by `limit_ns` of wall time) for every peer's flag; false when a wait
+// gave up (error word set).  Once an exchange of the step has given up, the
+// later ones return at once instead of each waiting out the limit; the error
+// word stays set until the host reads and clears it.
 __device__ bool bt_x_handshake(const BtXPeers& P, size_t flags_off, int inst, int cta, int rank, int size, uint32_t ep,
-                               uint32_t spin_limit, int* err) {
+                               uint64_t limit_ns, int* err) {
+  if (*reinterpret_cast<volatile int*>(err) & kErrTimeout) return false;
   __threadfence_system();
   for (int r = 0; r < size; ++r)
     if (r != rank) bt_st_release_sys(bt_x_flag(P.base[r], flags_off, inst, rank, cta), ep);
+  const uint64_t t0 = globaltimer_ns();
   for (int r = 0; r < size; ++r) {
     if (r == rank) continue;
     const uint32_t* f = bt_x_flag(P.base[rank], flags_off, inst, r, cta);
-    uint32_t i = 0;
     while (bt_ld_acquire_sys(f) != ep) {
-      if (++i > spin_limit) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         atomicOr(err, kErrTimeout);
         return false;
       }
-      __nanosleep(64);
+      __nanosleep(128);
     }
   }
   return true;
@@ -1507,7 +1515,7 @@ struct BtXReduceArgs {
   int* err;
   size_t flags_off, data_off;
   int nb, C, rank, size, inst;
-  uint32_t spin_limit;
+  uint64_t limit_ns;
 };
 
 __global__ void __launch_bounds__(kBtXThreads) bt_xreduce_kernel(BtXReduceArgs a) {
@@ -1522,7 +1530,7 @@ __global__ void __launch_bounds__(kBtXThreads) bt_xreduce_kernel(BtXReduceArgs a
   }
   __syncthreads();
   if (threadIdx.x == 0)
-    s_ok = bt_x_handshake(a.peers, a.flags_off, a.inst, c, a.rank, a.size, ep, a.spin_limit, a.err) ? 1 : 0;
+    s_ok = bt_x_handshake(a.peers, a.flags_off, a.inst, c, a.rank, a.size, ep, a.limit_ns, a.err) ? 1 : 0;
   __syncthreads();
   if (!s_ok) return;
   for (int i = e0 + (int)threadIdx.x; i < e1; i += blockDim.x) {
@@ -1541,7 +1549,7 @@ struct BtXArgmaxArgs {
   const int* step;
   size_t flags_off, amax_off;
   int nb, rank, size, inst, hist_cap;
-  uint32_t spin_limit;
+  uint64_t limit_ns;
 };
 
 // One CTA: every rank's per-session bests (written to its own amax slot by
@@ -1550,7 +1558,7 @@ __global__ void __launch_bounds__(kBtXThreads) bt_xargmax_kernel(BtXArgmaxArgs a
   __shared__ int s_ok;
   const uint32_t ep = (uint32_t)*a.epoch;
   if (threadIdx.x == 0)
-    s_ok = bt_x_handshake(a.peers, a.flags_off, a.inst, 0, a.rank, a.size, ep, a.spin_limit, a.err) ? 1 : 0;
+    s_ok = bt_x_handshake(a.peers, a.flags_off, a.inst, 0, a.rank, a.size, ep, a.limit_ns, a.err) ? 1 : 0;
   __syncthreads();
   if (!s_ok) return;
   const int st = *a.step;
@@ -1678,6 +1686,7 @@ struct rwkvb_batch {
   rwkvb::BtXPeers xpeers{};
   rwkvb::BtXLayout xl;
   unsigned long long* epoch = nullptr;
+  uint64_t tp_wait_ns = 0;  // wall-time bound of one exchange wait
 };
 
 namespace rwkvb {
@@ -1936,7 +1945,7 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
     x.tok = e->tok, x.hist = e->hist, x.step = e->step;
     x.flags_off = e->xl.flags, x.amax_off = e->xl.amax;
     x.nb = nb, x.rank = e->tp_rank, x.size = e->tp_size, x.inst = e->xl.ninst - 1, x.hist_cap = e->hist_cap;
-    x.spin_limit = 1u << 20;  // about half a second of polling
+    x.limit_ns = e->tp_wait_ns;
     bt_xargmax_kernel<<<1, kBtXThreads, 0, s>>>(x);
     return cuda_status(cudaGetLastError());
   }
@@ -1961,7 +1970,7 @@ int bt_reduce(rwkvb_batch* e, float* red, const float* part, const BtPieces& pp,
     x.err = e->err;
     x.flags_off = e->xl.flags, x.data_off = e->xl.data;
     x.nb = e->nb, x.C = e->C, x.rank = e->tp_rank, x.size = e->tp_size, x.inst = inst;
-    x.spin_limit = 1u << 20;  // about half a second of polling
+    x.limit_ns = e->tp_wait_ns;
     bt_xreduce_kernel<<<kBtXCtas, kBtXThreads, 0, s>>>(x);
     return cuda_status(cudaGetLastError());
   }
@@ -2514,6 +2523,8 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   e->l2_cores = l2 && (flags & 0x4u);
   // bit 1: no programmatic dependent launch; off under tensor parallelism (collectives between kernels)
   e->pdl = !(flags & 0x2u) && !tp;
+  // bits 16..19: exchange wait limit in units of 100 ms (0: the 5 s default)
+  e->tp_wait_ns = ((flags >> 16) & 0xFu) ? (uint64_t)((flags >> 16) & 0xFu) * 100000000ull : rwkvb::kTpWaitLimitNs;
   e->nb = batch;
   e->bp = bg_padded_sessions(batch);
   e->nrows = bg_digit_rows(batch);

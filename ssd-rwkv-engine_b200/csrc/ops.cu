@@ -324,24 +324,64 @@ static __device__ __align__(256) float g_cmix_scratch[RWKVB_CMIX_NOALLOC_MAX_FFN
 
 namespace {
 constexpr int kMaxDevices = 64;
-std::atomic<float*> g_cmix_scratch_ptr[kMaxDevices];
+struct ScratchSlot {
+  float* ptr;
+  unsigned long long ctx_id;  // unique id of the context the address belongs to
+};
+ScratchSlot g_cmix_scratch_slot[kMaxDevices];
 std::mutex g_cmix_scratch_mu;
 
-// Address of g_cmix_scratch on the current device; resolved once per device.
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+
+// Unique id of the calling thread's current context (never reused within the
+// process, unlike the context handle); false when none is current or the
+// driver entry points are unavailable.
+bool current_ctx_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && p)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess && p)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    cudaGetLastError();
+  });
+  if (!get_cur || !get_id) return false;
+  void* ctx = nullptr;
+  if (get_cur(&ctx) != 0 || !ctx) return false;
+  return get_id(ctx, id) == 0;
+}
+
+// Address of g_cmix_scratch in the current device's context.  Resolved once
+// per context: a device reset (cudaDeviceReset) replaces the context and the
+// address is resolved again in the new one.
 int cmix_scratch(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_status(e);
   if (dev < 0 || dev >= kMaxDevices) return RWKVB_EUNSUPPORTED;
-  float* p = g_cmix_scratch_ptr[dev].load(std::memory_order_acquire);
-  if (!p) {
-    std::lock_guard<std::mutex> lock(g_cmix_scratch_mu);
-    p = g_cmix_scratch_ptr[dev].load(std::memory_order_relaxed);
-    if (!p) {
-      e = cudaGetSymbolAddress((void**)&p, g_cmix_scratch);
-      if (e != cudaSuccess) return cuda_status(e);
-      g_cmix_scratch_ptr[dev].store(p, std::memory_order_release);
-    }
+  unsigned long long id = 0;
+  const bool known = current_ctx_id(&id);
+  std::lock_guard<std::mutex> lock(g_cmix_scratch_mu);
+  ScratchSlot& s = g_cmix_scratch_slot[dev];
+  if (s.ptr && known && s.ctx_id == id) {
+    *out = s.ptr;
+    return RWKVB_OK;
+  }
+  float* p = nullptr;
+  e = cudaGetSymbolAddress((void**)&p, g_cmix_scratch);
+  if (e != cudaSuccess) return cuda_status(e);
+  unsigned long long id2 = 0;
+  if (current_ctx_id(&id2)) {  // the lookup made the context current if none was
+    s.ptr = p;
+    s.ctx_id = id2;
+  } else {
+    s.ptr = nullptr;  // no context id to key on: resolve again next call
   }
   *out = p;
   return RWKVB_OK;

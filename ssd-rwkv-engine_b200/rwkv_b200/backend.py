@@ -40,37 +40,51 @@ CUDA_B200_BACKENDS = frozenset({"cuda_b200", "b200"})
 SUPPORTED_CODECS = ("none", "scale_u8_grouped", "trinity_lut2")
 
 
-class BackendNotAvailableError(Exception):
-    """Mirror of ``rwkv_ssd.runtime.errors.BackendNotAvailableError``."""
+try:
+    # Inside the reference tree the backend uses the reference's own types, so
+    # its engine's isinstance checks (``is_pack_backend``), ``except`` clauses
+    # and state cache see this backend's objects as their own.
+    from rwkv_ssd.backends.pack_backend import PackBackend as _PackBase
+    from rwkv_ssd.runtime.errors import BackendNotAvailableError, CapabilityNotSupportedError
+    from rwkv_ssd.runtime.generation_control import GenerationCancelled
+    from rwkv_ssd.runtime.state_cache import RecurrentState
 
+    REFERENCE_TYPES = True
+except ImportError:
+    REFERENCE_TYPES = False
+    _PackBase = object
 
-class CapabilityNotSupportedError(Exception):
-    """Mirror of ``rwkv_ssd.runtime.errors.CapabilityNotSupportedError``."""
+    class BackendNotAvailableError(Exception):
+        """Mirror of ``rwkv_ssd.runtime.errors.BackendNotAvailableError``."""
 
-    def __init__(self, capability: str, backend: str, detail: str | None = None):
-        self.capability = capability
-        super().__init__(f"{backend} does not support {capability}" + (f": {detail}" if detail else ""))
+    class CapabilityNotSupportedError(Exception):
+        """Mirror of ``rwkv_ssd.runtime.errors.CapabilityNotSupportedError``."""
 
+        def __init__(self, capability: str, backend: str, detail: str | None = None):
+            self.capability = str(capability)
+            self.backend = str(backend)
+            msg = f"backend {self.backend!r} does not support capability {self.capability!r}"
+            super().__init__(msg + (f": {detail}" if detail else ""))
 
-class GenerationCancelled(RuntimeError):
-    """Mirror of ``rwkv_ssd.runtime.generation_control.GenerationCancelled``."""
+    class GenerationCancelled(RuntimeError):
+        """Mirror of ``rwkv_ssd.runtime.generation_control.GenerationCancelled``."""
 
+    @dataclass
+    class RecurrentState:
+        """Field-compatible with the reference ``RecurrentState`` (state_cache.py:38-56)."""
 
-@dataclass
-class RecurrentState:
-    """Field-compatible with the reference ``RecurrentState`` (state_cache.py:38-56)."""
+        last_token_id: int = 0
+        h: torch.Tensor | None = None
+        rwkv7_state: list[torch.Tensor] | None = None
+        external_state: object | None = None
 
-    last_token_id: int = 0
-    h: torch.Tensor | None = None
-    rwkv7_state: list[torch.Tensor] | None = None
-    external_state: object | None = None
-
-    def clone(self) -> "RecurrentState":
-        ext = self.external_state
-        if isinstance(ext, dict):
-            ext = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in ext.items()}
-        return RecurrentState(int(self.last_token_id), self.h.clone() if self.h is not None else None,
-                              [t.clone() for t in self.rwkv7_state] if self.rwkv7_state is not None else None, ext)
+        def clone(self) -> "RecurrentState":
+            ext = self.external_state
+            if isinstance(ext, dict):
+                ext = {k: (v.clone() if isinstance(v, torch.Tensor) else v) for k, v in ext.items()}
+            return RecurrentState(int(self.last_token_id), self.h.clone() if self.h is not None else None,
+                                  [t.clone() for t in self.rwkv7_state] if self.rwkv7_state is not None else None,
+                                  ext)
 
 
 class _Control:
@@ -164,8 +178,12 @@ def packed_tensors_from_provider(provider) -> dict[str, PackedTensor]:
 
 
 # ----------------------------------------------------------------- backend
-class CudaB200Backend:
-    """RWKV-7 packed decode on one B200 through the sm_100a library."""
+class CudaB200Backend(_PackBase):
+    """RWKV-7 packed decode on one B200 through the sm_100a library.
+
+    Subclasses the reference's ``PackBackend`` when the reference package is
+    importable (its engine then routes it through ``_generate_pack``), else
+    stands alone with the same method set."""
 
     supports_streaming: bool = True
 
@@ -225,13 +243,14 @@ class CudaB200Backend:
         return {
             "name": "cuda_b200",
             "declared": {
-                "pack_streaming": True, "skeleton": False, "resident": True, "state_snapshot": True,
+                "pack_streaming": False, "skeleton": False, "resident": True, "state_snapshot": True,
                 "batch": True, "prefix_cache": True, "tokenizer": self.tokenizer is not None,
                 "state_kind": "rwkv7", "supported_codecs": list(SUPPORTED_CODECS), "requires_ggml_bin": False,
                 "token_generation": True, "logits_probe": True, "state_transfer": True,
                 "followup_generation": True, "sampling": True, "incremental_streaming": True,
                 "cancellation": True, "deadlines": True, "process_workers": False,
                 "native_layer_streaming": False, "native_cached_layer_step": True,
+                "deepembed": False, "deepembed_streaming": False,
             },
             "runtime": {"loaded": self._engine is not None, "device": str(self._device)},
         }
@@ -383,8 +402,10 @@ class CudaB200Backend:
         return self.decode_greedy(state, provider, max_tokens, metrics, temperature=0.0 if greedy else temperature,
                                   token_callback=token_callback, cancel_event=cancel_event, deadline=deadline)
 
-    def generate_tokens(self, *a, **kw) -> list[int]:
-        return self.generate(*a, **kw)
+    def generate_tokens(self, prompt: str, provider, max_tokens: int, metrics, *, temperature: float = 0.0,
+                        greedy: bool = True, token_callback=None, cancel_event=None, deadline=None) -> list[int]:
+        return self.generate(prompt, provider, max_tokens, metrics, temperature=temperature, greedy=greedy,
+                             token_callback=token_callback, cancel_event=cancel_event, deadline=deadline)
 
     def generate_greedy(self, prompt: str, provider, max_tokens: int, metrics) -> list[int]:
         return self.generate(prompt, provider, max_tokens, metrics)
