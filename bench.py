@@ -567,9 +567,8 @@ def main() -> None:
     ms_step = ms / args.steps
 
     # end to end through the plugin: CudaB200Backend.decode_greedy with a
-    # per-token callback, so every step reads its argmax back to the host
-    # (int64, 8 bytes) and sends the token to the device through the C ABI
-    # (int32, 4 bytes) before the next step starts
+    # per-token callback; every step's id crosses to the host (mapped pinned
+    # memory) and the callback sees it before the call returns
     e2e_steps = min(args.e2e_steps, args.steps)
     state = backend.prefill_tokens(prompt)
     emitted: list[int] = []
@@ -632,8 +631,10 @@ def main() -> None:
                                  f"peak: {peak_kind} HBM copy bandwidth"},
             "e2e": {"value": e2e_val, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8,
                     "steps": e2e_steps,
-                    "how": "cuda_b200 plugin decode_greedy with a token callback: per token argmax read to the "
-                           "host, token sent back through rwkvb_engine_forward (one persistent launch per token)"},
+                    "how": "cuda_b200 plugin decode_greedy with a token callback: one persistent launch for the "
+                           "whole generation; per token the device writes the id and a count (8 B) into mapped "
+                           "pinned host memory and reads the host's cancel word (4 B); the callback runs on the "
+                           "host as each id arrives"},
             "clocks": clk,
         }
         if batched is not None:

@@ -247,6 +247,34 @@ int rwkvb_engine_decode_greedy(rwkvb_engine* e, int32_t first_token, int32_t n_t
 int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first_token, int32_t n_tokens,
                                      int32_t* out_tokens_dev, void* stream);
 
+/* Streamed greedy decode for callers that consume tokens as they are made
+ * (the token callback, cancellation and deadline of the reference's
+ * decode_greedy, pack_backend.py:71-84 and generation_control.py:19-35): the
+ * whole generation is ONE persistent launch, and the host learns of each token
+ * through mapped pinned host memory instead of a launch and a synchronisation
+ * per token.
+ *
+ * rwkvb_engine_host_ring: the engine's ring (allocated at the first call):
+ *   ids[cap]  each step's greedy id, written as soon as the step ends;
+ *   *count    ids written so far, stored after the ids (system-scope release);
+ *   *cancel   read by the device once per token: non-zero stops the decode at
+ *             the next token boundary.
+ * rwkvb_engine_decode_stream: greedy decode of n <= cap steps from first_token
+ * (step 0 consumes it, step i > 0 consumes step i-1's id), streamed into the
+ * ring; resets *count and *cancel, launches and returns without synchronising.
+ * The previous streamed decode of the engine must have finished (its stream
+ * synchronised) before the next call.  When cancelled, *count gives the steps
+ * that ran; the state is that after those steps.  out_tokens_dev (device, may be
+ * NULL) receives the n ids as well (valid up to *count).  Persistent engines
+ * only (RWKVB_EUNSUPPORTED otherwise).
+ * rwkvb_engine_check: synchronise `stream` and report (then clear) a device
+ * error of the engine's launches (RWKVB_ETIMEOUT, RWKVB_EARG for a bad token). */
+int rwkvb_engine_host_ring(rwkvb_engine* e, int32_t** ids, volatile uint32_t** count, volatile int32_t** cancel,
+                           int32_t* cap);
+int rwkvb_engine_decode_stream(rwkvb_engine* e, int32_t first_token, int32_t n_tokens, int32_t* out_tokens_dev,
+                               void* stream);
+int rwkvb_engine_check(rwkvb_engine* e, void* stream);
+
 /* Timestamps (ns, %globaltimer) of the last persistent launch, recorded when
  * the engine was created with flag bit 3; copies min(cap, 262144) values to
  * host `out`:

@@ -56,7 +56,9 @@ constexpr int kDMaxItems = 8;          // adapter first-stage items per CTA
 constexpr int kDPartTiles = 8;         // GEMV tiles whose per-warp partial sums are buffered per CTA reduction
 constexpr int kDMaxPieces = 8;         // adapter second-stage tile pieces per layer
 constexpr int kDMisc = 2560;           // misc shared floats
-static_assert(kDW * 4 * 64 <= kDMisc, "phase-B adapter partials [warps][4][64] live in misc");
+static_assert((kDW / 2) * 4 * 64 <= kDMisc, "phase-B adapter partials [warps / 2][4][64] live in misc");
+static_assert(256 + 4 * kDT <= kDMisc, "adapter item inputs and row-group partials live in misc");
+constexpr int kMidPer = (2048 + kDT - 1) / kDT;  // first-adapter sums per consumer thread (rtot <= 2048)
 constexpr float kFix = 4294967296.0f;  // 2^32 fixed-point scale of adapter partials
 constexpr float kUnfix = 1.0f / 4294967296.0f;
 
@@ -64,6 +66,16 @@ __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long v;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(v));
   return v;
+}
+
+__device__ __forceinline__ int d_ld_relaxed_sys(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void d_st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned d_ld_acquire(const unsigned* p) {
@@ -82,6 +94,15 @@ __device__ __forceinline__ float ln_val(float x, float mean, float rstd, float w
 // the four adapter second stages w2, a2, g2, v2 (64-column tiles, pairs).
 struct DLayerMaps {
   CUtensorMap q[6], p[6], aq[4], ap[4];
+  // streaming copy (null: load through the tensor maps): r/k/v (one region of
+  // 3C rows), o, ffn key, ffn value, each unit-major, a unit stored as the
+  // shared-memory image of its ring slot
+  const uint8_t* su[4];
+  // preload mode: this layer's adapter second-stage images, one per head
+  // (adp_b0 bytes on layer 0, adp_b1 on later layers): per adapter m (w, a,
+  // g, v) its R_m rows of the head's 64 columns, then the rows' two (min, max)
+  // pairs around those columns ([R_m][64] codes, [R_m][2] float2)
+  const uint8_t* ai;
 };
 
 struct DRange {
@@ -112,6 +133,18 @@ struct DArgs {
   int trace_cap;
   uint32_t o_dig, o_x, o_xb, o_t, o_p, o_part, o_misc, smem_total;
   uint32_t dig_set;  // bytes of one digit set of width C
+  // streamed greedy decode (mode 0; all null otherwise): mapped pinned host
+  // memory that receives each step's id (ring_ids[step], then ring_count =
+  // step + 1) and holds the host's cancel word, read between tokens
+  int* ring_ids;
+  unsigned* ring_count;
+  const int* ring_cancel;
+  const uint8_t* head_su;  // streaming copy of the head (null with the tensor maps)
+  // preload mode (pre != 0): the phase-B adapter image (head CTAs) and the
+  // adapter first-stage item (at most one per CTA) of each layer land in
+  // dedicated shared memory at the start of the layer instead of ring slots
+  int pre;
+  uint32_t o_adp, o_item, adp_b0, adp_b1;
 };
 
 struct DTable {
@@ -241,9 +274,11 @@ __device__ __forceinline__ void d_issued(const DArgs& a, int& seq) {
 // (the r, k, v maps of phase A), row (t % per_map) * 16.  Every argument the
 // loop needs is copied to registers first (the loop stores to shared memory,
 // so reads through `a` would be repeated each iteration).
+// su != null: unit u is one bulk copy of its slot image from the streaming
+// copy (a single TMA operation per unit instead of a code box and a pair box).
 __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, const CUtensorMap* q, const CUtensorMap* p,
                                            int per_map, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                           volatile int* abort_flag, int& seq_io) {
+                                           volatile int* abort_flag, int& seq_io, const uint8_t* su) {
   const int nst = a.nst, nb = a.nb, pr8 = a.pr * 8, u0 = R.u0, u1 = R.u1, nch = R.nch;
   const uint32_t slot_b = a.slot, code_b = a.code_b, bytes = a.code_b + a.pair_b;
   unsigned long long* tr = (a.trace && blockIdx.x == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
@@ -274,7 +309,11 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     }
     uint8_t* dst = ring + (size_t)slot * slot_b;
     mbar_expect_tx(&full[slot], bytes);
-    if (hint) {
+    if (su) {
+      const uint8_t* src = su + (size_t)u * bytes;
+      if (hint) bulk_g2s_hint(dst, src, bytes, &full[slot], pol);
+      else bulk_g2s(dst, src, bytes, &full[slot]);
+    } else if (hint) {
       tma_load_3d_hint(dst, q + mi, 0, row0, chunk * nb, &full[slot], pol);
       tma_load_2d_hint(dst + code_b, p + mi, chunk * pr8, row0, &full[slot], pol);
     } else {
@@ -296,14 +335,55 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
   return ok;
 }
 
+// One adapter first-stage item (rows [i0, i1) of W1 [C][R] and the (min, max)
+// pairs of the groups they touch) into `dst`, completing on `bar`.
+__device__ __noinline__ void d_issue_item(const DArgs& a, const LayerDev& Ly, int item, uint8_t* dst, uint64_t* bar) {
+  const int m = d_item_mat(a.d, item);
+  const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
+  const int R = W.cols, C = a.d.C;
+  const int i0 = (item - a.d.abase[m]) * a.d.arow[m], i1 = min(C, i0 + a.d.arow[m]);
+  const uint32_t qb = (uint32_t)((i1 - i0) * R);
+  const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg) & ~1u;
+  const uint32_t g1 = ((uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) + 1) + 1u) & ~1u;
+  const uint32_t sb = (g1 - g0) * 8u;
+  mbar_expect_tx(bar, qb + sb);
+  if (a.l2_first) {
+    const uint64_t pol = l2_evict_first();
+    bulk_g2s_hint(dst, W.payload + (size_t)i0 * R, qb, bar, pol);
+    bulk_g2s_hint(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, bar, pol);
+  } else {
+    bulk_g2s(dst, W.payload + (size_t)i0 * R, qb, bar);
+    bulk_g2s(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, bar);
+  }
+}
+
+// Producer: wait until the consumers released load n - 1 of a dedicated
+// buffer (its "empty" barrier); false when the launch aborts or the wait
+// gives up.
+__device__ __noinline__ bool d_pre_acquire(const DArgs& a, uint64_t* empty, int n, volatile int* abort_flag) {
+  if (n == 0) return true;
+  const uint32_t par = (uint32_t)((n - 1) & 1);
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait_hint(empty, par, 20000u)) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(a.b.err, kErrTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
 // Lane 0 of the producer warp: fill the ring in the consumers' order (per
 // token, per layer: r/k/v units, adapter items, adapter-2 pieces, o units,
 // ffn key units, ffn value units; then the head units), gated by the slots'
 // empty barriers.  When it starts a layer it prefetches the next layer's small
 // operands and this layer's tensor maps.
 __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                           volatile int* abort_flag) {
+                           volatile int* abort_flag, uint64_t* pbar) {
   int seq = 0;
+  int nadp = 0, nitm = 0;  // dedicated-buffer loads issued (preload mode)
   const bool hint = a.l2_first != 0;
   const uint64_t pol = l2_evict_first(), keep = l2_evict_last();
   auto acquire = [&]() -> int { return d_acquire(a, empty, abort_flag, seq); };
@@ -325,8 +405,9 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
   {
     const int C = a.d.C, ct = C / 16, bx = blockIdx.x;
     bool ok = true;
-    auto units = [&](const DRange& R, const CUtensorMap* q, const CUtensorMap* p, int per_map) -> bool {
-      return d_issue_units(a, R, q, p, per_map, ring, full, empty, abort_flag, seq);
+    auto units = [&](const DRange& R, const CUtensorMap* q, const CUtensorMap* p, int per_map,
+                     const uint8_t* su) -> bool {
+      return d_issue_units(a, R, q, p, per_map, ring, full, empty, abort_flag, seq, su);
     };
     for (int tok = 0; tok < a.ntok && ok; ++tok) {
       const bool head = a.mode == 0 || tok == a.ntok - 1;
@@ -334,8 +415,28 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
         const DLayerMaps& M = a.lmaps[l];
         const LayerDev& Ly = a.layers[l];
         layer_start(l);
-        ok = units(T.r[0], M.q, M.p, ct);
-        for (int k = 0; ok && k < T.nitem[l == 0 ? 0 : 1]; ++k) {
+        if (a.pre) {
+          // phase-B image and the item first: they land while phase A runs
+          if (bx < a.d.H) {
+            ok = d_pre_acquire(a, &pbar[1], nadp, abort_flag);
+            if (ok) {
+              const uint32_t b = l == 0 ? a.adp_b0 : a.adp_b1;
+              mbar_expect_tx(&pbar[0], b);
+              if (hint) bulk_g2s_hint(ring + a.o_adp, M.ai + (size_t)bx * b, b, &pbar[0], pol);
+              else bulk_g2s(ring + a.o_adp, M.ai + (size_t)bx * b, b, &pbar[0]);
+              ++nadp;
+            }
+          }
+          if (ok && T.nitem[l == 0 ? 0 : 1] > 0) {
+            ok = d_pre_acquire(a, &pbar[3], nitm, abort_flag);
+            if (ok) {
+              d_issue_item(a, Ly, T.item[0], ring + a.o_item, &pbar[2]);
+              ++nitm;
+            }
+          }
+        }
+        if (ok) ok = units(T.r[0], M.q, M.p, ct, M.su[0]);
+        for (int k = 0; ok && !a.pre && k < T.nitem[l == 0 ? 0 : 1]; ++k) {
           const int item = T.item[k];
           const int m = d_item_mat(a.d, item);
           const PackedView& W = m == 0 ? Ly.w1 : (m == 1 ? Ly.a1 : (m == 2 ? Ly.g1 : Ly.v1));
@@ -360,7 +461,7 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
             issued();
           }
         }
-        for (int k = 0; ok && k < T.npc[l == 0 ? 0 : 1]; ++k) {
+        for (int k = 0; ok && !a.pre && k < T.npc[l == 0 ? 0 : 1]; ++k) {
           const int m = T.pm[k], br = a.abr[m];
           const int slot = acquire();
           ok = slot >= 0;
@@ -378,20 +479,22 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
             issued();
           }
         }
-        if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0);
-        if (ok) ok = units(T.r[2], M.q + 4, M.p + 4, 0);
-        if (ok) ok = units(T.r[3], M.q + 5, M.p + 5, 0);
+        if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0, M.su[1]);
+        if (ok) ok = units(T.r[2], M.q + 4, M.p + 4, 0, M.su[2]);
+        if (ok) ok = units(T.r[3], M.q + 5, M.p + 5, 0, M.su[3]);
       }
       if (ok && head) {
         d_prefetch_map(a.head_maps);
         d_prefetch_map(a.head_maps + 1);
-        ok = units(T.r[4], a.head_maps, a.head_maps + 1, 0);
+        ok = units(T.r[4], a.head_maps, a.head_maps + 1, 0, a.head_su);
       }
     }
   }
   // every issued copy has landed before the CTA may exit
   for (int s = seq > a.nst ? seq - a.nst : 0; s < seq; ++s)
     mbar_wait_bounded(&full[s % a.nst], (uint32_t)((s / a.nst) & 1), 1u << 20);
+  if (nadp > 0) mbar_wait_bounded(&pbar[0], (uint32_t)((nadp - 1) & 1), 1u << 20);
+  if (nitm > 0) mbar_wait_bounded(&pbar[2], (uint32_t)((nitm - 1) & 1), 1u << 20);
 }
 
 // ------------------------------------------------------------ consumers
@@ -410,7 +513,23 @@ struct DCons {
   int* flag;
   int seq, pbuf, dead, tr, trow;
   unsigned target;
+  uint64_t* pbar;  // preload mode: adp full/empty, item full/empty
+  int nadp, nitm;  // dedicated-buffer loads consumed
 };
+
+// Consumers: wait for a dedicated-buffer load (all threads); a failed wait
+// marks this CTA dead like a ring wait.
+__device__ __forceinline__ void d_pre_wait(const DArgs& a, DCons& c, uint64_t* full, int n) {
+  if (c.dead) return;
+  const bool got = mbar_wait_suspend(full, (uint32_t)(n & 1));
+  if (!__all_sync(0xffffffffu, got)) {
+    c.dead = 1;
+    if ((threadIdx.x & 31) == 0) {
+      atomicOr(a.b.err, kErrTimeout);
+      *c.abort = 1;
+    }
+  }
+}
 
 __device__ __forceinline__ void d_csync() { bar_sync(kDBar, kDT); }
 
@@ -664,6 +783,8 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
   unsigned long long* tr = (a.trace && blockIdx.x == 0 && t == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
   const int tr_n = 2 * a.trace_cap;
   int seq = c.seq;
+  int slot = seq % nst;
+  uint32_t ph = (uint32_t)((seq / nst) & 1);
   bool dead = c.dead;
   const int pofs = L.ra * pr + ((warp << 7) >> lg);
   float acc0 = 0.f, acc1 = 0.f;
@@ -678,10 +799,10 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
       X = d_digits_at(dig + (size_t)set * stride, K, LFK);
       cur_set = set;
     }
-    const int slot = seq % nst;
     const uint8_t* sl = sm + (size_t)slot * slot_b;
     if (!dead) {
-      const bool got = mbar_wait_suspend(&full[slot], (uint32_t)((seq / nst) & 1));
+      bool got = mbar_try_wait(&full[slot], ph);  // usually already there: no timer, no suspend
+      if (!got) got = mbar_wait_suspend(&full[slot], ph);
       if (!__all_sync(0xffffffffu, got)) {
         dead = true;
         if (lane == 0) {
@@ -699,6 +820,10 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
     if (lane == 0) mbar_arrive(&empty[slot]);
     if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 2] = global_ns();
     ++seq;
+    if (++slot == nst) {
+      slot = 0;
+      ph ^= 1u;
+    }
     if (chunk == nch - 1 || u == u1 - 1) {
       // tile end: this warp's partial sums of the tile's 16 rows go to the
       // buffer; the CTA sums them over warps (in warp order) and adds each row
@@ -753,32 +878,53 @@ __device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, 
     #pragma unroll 1
     for (int i = t; i < nr; i += kDT) xm[i] = TV[i0 + i] + (PV[i0 + i] - TV[i0 + i]) * __ldg(mix + i0 + i);
     d_csync();
-    const uint8_t* sl = d_slot_wait(a, c);
-    const int nrg = R < kDT ? kDT / R : 1;
-    if (!c.dead) {
-      const uint32_t qb = (uint32_t)(nr * R);
-      const float2* cs = reinterpret_cast<const float2*>(sl + ((qb + 15u) & ~15u));
-      const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> wlg) & ~1u;
-      #pragma unroll 1
-      for (int jw = t; jw < nrg * R; jw += kDT) {
-        const int j = jw % R, rg = jw / R;
-        float acc = 0.f;
-        for (int i = rg; i < nr; i += nrg) {
-          const uint32_t e = (uint32_t)(i0 + i) * (uint32_t)R + (uint32_t)j;
-          const float2 sc = cs[(e >> wlg) - g0];
-          acc = fmaf(xm[i], sg8_dequant(sl[i * R + j], sc.x, sc.y), acc);
-        }
-        pacc[rg * R + j] = acc;
-      }
+    const uint8_t* sl;
+    if (a.pre) {
+      d_pre_wait(a, c, &c.pbar[2], c.nitm);
+      sl = c.sm + a.o_item;
+    } else {
+      sl = d_slot_wait(a, c);
     }
-    d_slot_release(a, c);
+    // four columns per thread (one 32-bit code word; a group holds whole
+    // quads: R % 16 == 0, group >= 4), rows split over `nrg` row groups; per
+    // row the scale is folded into the input: x (q d + mn) = (x d) q + x mn
+    const int q4 = R >> 2;
+    const int nrg = q4 < kDT ? kDT / q4 : 1;
+    const uint32_t qb = (uint32_t)(nr * R);
+    const float2* cs = reinterpret_cast<const float2*>(sl + ((qb + 15u) & ~15u));
+    const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> wlg) & ~1u;
+    #pragma unroll 1
+    for (int jw = t; !c.dead && jw < nrg * q4; jw += kDT) {
+      const int j = (jw % q4) * 4, rg = jw / q4;
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, bs = 0.f;
+      #pragma unroll 4
+      for (int i = rg; i < nr; i += nrg) {
+        const uint32_t e = (uint32_t)(i0 + i) * (uint32_t)R + (uint32_t)j;
+        const float2 sc = cs[(e >> wlg) - g0];
+        const float xv = xm[i];
+        const float ad = xv * __fmul_rn(__fsub_rn(sc.y, sc.x), kInv255);
+        bs = fmaf(xv, sc.x, bs);
+        const uint32_t w4 = *reinterpret_cast<const uint32_t*>(sl + i * R + j);
+        // code byte b as a float: bits 0x4B0000qq = 2^23 + q, minus 2^23 (exact)
+        a0 = fmaf(ad, __uint_as_float(__byte_perm(w4, 0x4B000000u, 0x7440)) - 8388608.0f, a0);
+        a1 = fmaf(ad, __uint_as_float(__byte_perm(w4, 0x4B000000u, 0x7441)) - 8388608.0f, a1);
+        a2 = fmaf(ad, __uint_as_float(__byte_perm(w4, 0x4B000000u, 0x7442)) - 8388608.0f, a2);
+        a3 = fmaf(ad, __uint_as_float(__byte_perm(w4, 0x4B000000u, 0x7443)) - 8388608.0f, a3);
+      }
+      *reinterpret_cast<float4*>(pacc + rg * R + j) = make_float4(a0 + bs, a1 + bs, a2 + bs, a3 + bs);
+    }
+    if (!a.pre) d_slot_release(a, c);
     d_csync();
+    if (a.pre) {
+      if (t == 0) mbar_arrive(&c.pbar[3]);  // the item buffer may be refilled
+      ++c.nitm;
+    }
     if (!c.dead) {
       const int off = d_rank_off(a.d, m);
       #pragma unroll 1
       for (int j = t; j < R; j += kDT) {
         float v = 0.f;
-        for (int rg = 0; rg < nrg; ++rg) v += pacc[rg * R + j];
+        for (int rg = 0; rg < (q4 < kDT ? kDT / q4 : 1); ++rg) v += pacc[rg * R + j];
         atomicAdd(a.b.adp64 + off + j, (unsigned long long)__float2ll_rn(v * kFix));
       }
     }
@@ -803,14 +949,15 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
   float* Sg = a.b.wkv + ((size_t)l * H + h) * 4096;
   const int nm = l == 0 ? 3 : 4;
   const int used = l == 0 ? a.d.rw + a.d.ra + a.d.rg : a.d.rtot;
-  #pragma unroll 1
-  for (int j = t; j < used; j += kDT) {
-    float v = (float)(long long)__ldcg(a.b.adp64 + j) * kUnfix;
-    if (j < a.d.rw) v = tanhf(v);
-    else if (j >= a.d.rw + a.d.ra && j < a.d.rw + a.d.ra + a.d.rg) v = sigmoidf_(v);
-    mid[j] = v;
+  // every global operand of the head in one round: the first-adapter sums
+  // (up to kMidPer per thread) and the head's per-channel vectors are loaded
+  // together, then used
+  unsigned long long mq[kMidPer];
+#pragma unroll
+  for (int q = 0; q < kMidPer; ++q) {
+    const int j = t + q * kDT;
+    mq[q] = j < used ? __ldcg(a.b.adp64 + j) : 0ull;
   }
-  // every global operand of the head in one round
   float r = 0.f, k = 0.f, v = 0.f, vf = 0.f, kk_w = 0.f, a0 = 0.f, ka = 0.f, v0 = 0.f, w0 = 0.f, rk = 0.f, lw = 0.f,
         lb = 0.f;
   if (t < 64) {
@@ -830,9 +977,17 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
     lw = __ldg(Ly.lnx_w + ch);
     lb = __ldg(Ly.lnx_b + ch);
   }
-  float* vp = misc;  // [10 warps][4 matrices][64 columns] partials
-  #pragma unroll 1
-  for (int i = t; i < kDW * 256; i += kDT) vp[i] = 0.f;
+#pragma unroll
+  for (int q = 0; q < kMidPer; ++q) {
+    const int j = t + q * kDT;
+    if (j < used) {
+      float mv = (float)(long long)mq[q] * kUnfix;
+      if (j < a.d.rw) mv = tanhf(mv);
+      else if (j >= a.d.rw + a.d.ra && j < a.d.rw + a.d.ra + a.d.rg) mv = sigmoidf_(mv);
+      mid[j] = mv;
+    }
+  }
+  float* vp = misc;  // [kDW / 2 warp pairs][4 matrices][64 columns] partials
   cp_async_wait_all();
   d_csync();
   {
@@ -840,10 +995,25 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
     // half-warps take alternate rows: row phase rp of 20.  Per row the scale
     // is folded into the input: mid * (q * d + mn) = (mid * d) * q + mid * mn.
     const int lane = t & 31, w = t >> 5, cg = lane & 15, rp = w * 2 + (lane >> 4);
-    for (int pc = 0; pc < T.npc[l == 0 ? 0 : 1]; ++pc) {
-      const uint8_t* sl = d_slot_wait(a, c);
+    float acc4[4][5];  // per adapter: this lane's four column partials and its min term
+#pragma unroll
+    for (int mm = 0; mm < 4; ++mm)
+#pragma unroll
+      for (int u = 0; u < 5; ++u) acc4[mm][u] = 0.f;
+    if (a.pre) d_pre_wait(a, c, &c.pbar[0], c.nadp);
+    uint32_t img_off = 0;  // preload mode: offset of adapter m's block in the head's image
+    const int npc = a.pre ? nm : T.npc[l == 0 ? 0 : 1];
+    for (int pc = 0; pc < npc; ++pc) {
+      const uint8_t* sl;
+      if (a.pre) {
+        sl = c.sm + a.o_adp + img_off;
+        img_off += 80u * (uint32_t)d_rank(a.d, pc);
+      } else {
+        sl = d_slot_wait(a, c);
+      }
       if (!c.dead) {
-        const int m = T.pm[pc], br = a.abr[m], r0 = T.pr0[pc];
+        const int m = a.pre ? pc : T.pm[pc];
+        const int br = a.pre ? d_rank(a.d, m) : a.abr[m], r0 = a.pre ? 0 : T.pr0[pc];
         const int nr = min(br, d_rank(a.d, m) - r0);
         const float2* pairs = reinterpret_cast<const float2*>(sl + br * 64);
         const int sel = ((h * 64) >> a.alg[m]) & 1;
@@ -868,25 +1038,50 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
         a2 += __shfl_xor_sync(0xffffffffu, a2, 16);
         a3 += __shfl_xor_sync(0xffffffffu, a3, 16);
         bs += __shfl_xor_sync(0xffffffffu, bs, 16);
-        if (lane < 16) {
-          float4* dst = reinterpret_cast<float4*>(vp + (w * 4 + m) * 64 + 4 * cg);
-          float4 v4 = *dst;
-          v4.x += a0 + bs;
-          v4.y += a1 + bs;
-          v4.z += a2 + bs;
-          v4.w += a3 + bs;
-          *dst = v4;
-        }
+#pragma unroll
+        for (int mm = 0; mm < 4; ++mm)
+          if (mm == m) {  // warp-uniform
+            acc4[mm][0] += a0;
+            acc4[mm][1] += a1;
+            acc4[mm][2] += a2;
+            acc4[mm][3] += a3;
+            acc4[mm][4] += bs;
+          }
       }
-      d_slot_release(a, c);
+      if (!a.pre) d_slot_release(a, c);
     }
+    // fixed-order fold of the warps' partials: warp w + kDW/2 stores, warp w adds
+    // its own, then the sum over the kDW/2 pairs (below) in pair order
+    constexpr int kHalf = kDW / 2;
+    if (w >= kHalf && lane < 16)
+#pragma unroll
+      for (int mm = 0; mm < 4; ++mm)
+        *reinterpret_cast<float4*>(vp + ((w - kHalf) * 4 + mm) * 64 + 4 * cg) =
+            make_float4(acc4[mm][0] + acc4[mm][4], acc4[mm][1] + acc4[mm][4], acc4[mm][2] + acc4[mm][4],
+                        acc4[mm][3] + acc4[mm][4]);
+    d_csync();
+    if (w < kHalf && lane < 16)
+#pragma unroll
+      for (int mm = 0; mm < 4; ++mm) {
+        float4* dst = reinterpret_cast<float4*>(vp + (w * 4 + mm) * 64 + 4 * cg);
+        float4 v4 = *dst;
+        v4.x += acc4[mm][0] + acc4[mm][4];
+        v4.y += acc4[mm][1] + acc4[mm][4];
+        v4.z += acc4[mm][2] + acc4[mm][4];
+        v4.w += acc4[mm][3] + acc4[mm][4];
+        *dst = v4;
+      }
   }
   d_csync();
+  if (a.pre) {
+    if (t == 0) mbar_arrive(&c.pbar[1]);  // the head image buffer may be refilled
+    ++c.nadp;
+  }
   if (t < 256) {
     const int m = t >> 6, cc = t & 63;
     float s = 0.f;
     if (m < nm)
-      for (int q = 0; q < kDW; ++q) s += vp[(q * 4 + m) * 64 + cc];
+      for (int q = 0; q < kDW / 2; ++q) s += vp[(q * 4 + m) * 64 + cc];
     vec[m * 64 + cc] = s;
   }
   d_csync();
@@ -1030,6 +1225,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   uint8_t* sm = d_smraw + ((1024u - (smem_u32(d_smraw) & 1023u)) & 1023u);
   __shared__ DTable T;
   __shared__ uint64_t full[kDMaxSt], empty[kDMaxSt];
+  __shared__ uint64_t pbar[4];  // preload mode: adp full / empty, item full / empty
   __shared__ float red[32];
   __shared__ int s_flag, s_tok;
   __shared__ volatile int s_abort;
@@ -1044,12 +1240,13 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kDW);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&pbar[i], 1);
     fence_mbar_init();
     s_abort = 0;
   }
   __syncthreads();
   if (warp == kDW) {
-    if (lane == 0) d_producer(a, T, sm, full, empty, &s_abort);
+    if (lane == 0) d_producer(a, T, sm, full, empty, &s_abort, pbar);
     return;
   }
 
@@ -1069,6 +1266,8 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   c.abort = &s_abort;
   c.flag = &s_flag;
   c.seq = c.pbuf = c.dead = c.tr = 0;
+  c.pbar = pbar;
+  c.nadp = c.nitm = 0;
   c.trow = bx == 0 ? 0 : (bx == G - 1 ? 1 : -1);
   c.target = 0;
 
@@ -1232,6 +1431,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       break;
     }
     d_mark(a, c);  // head barrier
+    // the host's cancel word crosses the bus once per token, read here so that
+    // its latency overlaps the head; published to every CTA before the last
+    // barrier of the token
+    int cancel_seen = 0;
+    if (a.ring_cancel && bx == 0 && t == 0) cancel_seen = d_ld_relaxed_sys(a.ring_cancel);
     d_zero(acc_hk, T.zf0, T.zf1);
         if (fused) {
       DLnMix q{};
@@ -1258,6 +1462,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     }
     d_zero(acc_fo, T.zc0, T.zc1);
     d_argmax_part(a, T, s_bv, s_bi);
+    if (a.ring_cancel && bx == 0 && t == 0) *a.b.stop = cancel_seen;
     if (!d_gsync(a, c)) {
       alive = false;
       break;
@@ -1266,6 +1471,18 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     if (bx == 0 && t == 0) {
       a.b.hist[step % a.d.hist_cap] = tok;
       *a.b.tok = tok;
+      if (a.ring_ids) {
+        a.ring_ids[step] = tok;
+        __threadfence_system();  // the id is visible to the host before the count that announces it
+        d_st_release_sys(a.ring_count, (unsigned)(step + 1));
+      }
+    }
+    if (a.ring_cancel && __ldcg(a.b.stop)) {
+      // cancelled by the host: every CTA stops after this token (the same
+      // word, read after the same barrier); the producer sees the abort flag
+      // in its slot waits, stops issuing and drains its copies in flight
+      if (t == 0) s_abort = 1;
+      break;
     }
   }
 }

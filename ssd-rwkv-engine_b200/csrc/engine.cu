@@ -21,6 +21,7 @@
 // (`launch_dependents`) so the next phase can start its own transfers while
 // this one computes.  Everything mutable (activations, recurrent state) is
 // read and written only after the wait.
+#include <atomic>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -73,6 +74,7 @@ struct Bufs {
   int *hist;                   // argmax history ring
   int *step;                   // steps since the last history reset
   int *err;                    // error flags (kErrToken | kErrTimeout)
+  int *stop;                   // streamed decode: the host's cancel word as CTA 0 read it this token
 };
 
 struct Dims {
@@ -634,6 +636,10 @@ struct rwkvb_engine {
   int* dtokens = nullptr;  // forced-token staging [hist_cap]
   unsigned long long* dtrace = nullptr;  // phase timestamps (flag bit 3)
   int trace_cap = 0;
+  // streamed decode: mapped pinned host ring (count at +0, cancel at +64, ids at +128)
+  uint8_t* hring = nullptr;
+  uint8_t* hring_dev = nullptr;  // the same memory as the device addresses it
+  uint8_t* dstream = nullptr;    // streaming copy of the big matrices (persistent kernel)
 };
 
 namespace {
@@ -852,6 +858,112 @@ int run_step(rwkvb_engine* e, cudaStream_t s) {
 // ---------------------------------------------------------- persistent plan
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Streaming copy of one SG8 matrix [rows][K] for the persistent kernel.  Unit u
+// = (16-row tile u / nch, column chunk u % nch of kc = nb * 128 columns) is
+// stored as the shared-memory image its ring slot receives from the two
+// tensor-map copies it replaces: codes [nb blocks][16 rows][128 B] with the
+// 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r & 7)), then the
+// rows' (min, max) pairs of the chunk, [16][pr] float2.  Rows past the matrix
+// are zero (min = max = 0: they contribute nothing).  One block per unit.
+__global__ void stream_layout_kernel(uint8_t* dst, PackedView w, int nb, int pr, uint32_t unit_b, int units) {
+  const int u = blockIdx.x;
+  if (u >= units) return;
+  const int K = w.cols, kc = nb * 128, nch = K / kc;
+  const int tile = u / nch, ch = u - tile * nch;
+  uint8_t* out = dst + (size_t)u * unit_b;
+  for (int i = threadIdx.x; i < 16 * nb * 8; i += blockDim.x) {
+    const int c = i & 7, r = (i >> 3) & 15, blk = i >> 7, row = tile * 16 + r;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < w.rows)
+      v = *reinterpret_cast<const uint4*>(w.payload + (size_t)row * K + (size_t)ch * kc + blk * 128 + c * 16);
+    *reinterpret_cast<uint4*>(out + blk * 2048 + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+  }
+  const int gpr = K >> w.lg;
+  float2* pd = reinterpret_cast<float2*>(out + 16 * kc);
+  for (int i = threadIdx.x; i < 16 * pr; i += blockDim.x) {
+    const int r = i / pr, j = i - r * pr, row = tile * 16 + r;
+    float2 v = make_float2(0.f, 0.f);
+    if (row < w.rows) v = reinterpret_cast<const float2*>(w.meta)[(size_t)row * gpr + (size_t)ch * pr + j];
+    pd[i] = v;
+  }
+}
+
+// Phase-B adapter images of one adapter second stage W2 [R][C] (SG8, group
+// 2^lg >= 64): for every head h (one block each) the block at
+// dst + h * img_b + off holds the R rows of columns [64 h, 64 h + 64), then per
+// row the two (min, max) pairs of the even-aligned group pair around them
+// ([R][64] codes, [R][16 B] pairs).
+__global__ void adp_image_kernel(uint8_t* dst, PackedView w, uint32_t img_b, uint32_t off) {
+  const int h = blockIdx.x, R = w.rows, C = w.cols;
+  uint8_t* out = dst + (size_t)h * img_b + off;
+  for (int i = threadIdx.x; i < R * 4; i += blockDim.x) {
+    const int r = i >> 2, q = i & 3;
+    *reinterpret_cast<uint4*>(out + r * 64 + q * 16) =
+        *reinterpret_cast<const uint4*>(w.payload + (size_t)r * C + h * 64 + q * 16);
+  }
+  const int gpr = C >> w.lg, px = ((h * 64) >> w.lg) & ~1;
+  for (int r = threadIdx.x; r < R; r += blockDim.x)
+    *reinterpret_cast<uint4*>(out + (size_t)R * 64 + r * 16) =
+        *reinterpret_cast<const uint4*>(w.meta + ((size_t)r * gpr + px) * 8);
+}
+
+uint64_t stream_units(const PackedView& w, int kc) { return (uint64_t)((w.rows + 15) / 16) * (uint64_t)(w.cols / kc); }
+
+// Build the streaming copy of every big matrix (bit 10 of the engine flags
+// keeps the tensor-map loads from the reference layout instead).  On an
+// allocation failure the tensor maps stay in use.
+void plan_stream_copy(rwkvb_engine* e, std::vector<DLayerMaps>& hm, bool pre) {
+  DArgs& a = e->da;
+  a.pre = 0;
+  if (e->flags & 0x400u) return;
+  const uint32_t ub = a.code_b + a.pair_b;
+  const int kc = a.kc;
+  uint64_t total = stream_units(e->head, kc) * ub;
+  for (const LayerDev& l : e->layers)
+    total += (stream_units(l.r, kc) + stream_units(l.k, kc) + stream_units(l.v, kc) + stream_units(l.o, kc) +
+              stream_units(l.fk, kc) + stream_units(l.fv, kc)) * ub;
+  const uint64_t img_total = (uint64_t)e->d.H * (a.adp_b0 + (uint64_t)(e->d.L - 1) * a.adp_b1);
+  if (pre) total += img_total;
+  if (cudaMalloc((void**)&e->dstream, total) != cudaSuccess) {
+    cudaGetLastError();
+    e->dstream = nullptr;
+    return;
+  }
+  uint8_t* cur = e->dstream;
+  auto lay = [&](const PackedView& w) {
+    const uint64_t n = stream_units(w, kc);
+    stream_layout_kernel<<<(unsigned)n, 256>>>(cur, w, a.nb, a.pr, ub, (int)n);
+    uint8_t* at = cur;
+    cur += n * ub;
+    return at;
+  };
+  for (size_t i = 0; i < e->layers.size(); ++i) {
+    const LayerDev& l = e->layers[i];
+    hm[i].su[0] = lay(l.r);  // r, k, v back to back: one region of 3C rows
+    lay(l.k);
+    lay(l.v);
+    hm[i].su[1] = lay(l.o);
+    hm[i].su[2] = lay(l.fk);
+    hm[i].su[3] = lay(l.fv);
+  }
+  a.head_su = lay(e->head);
+  if (pre) {
+    for (size_t i = 0; i < e->layers.size(); ++i) {
+      const LayerDev& l = e->layers[i];
+      const uint32_t ib = i == 0 ? a.adp_b0 : a.adp_b1;
+      const PackedView* w2[4] = {&l.w2, &l.a2, &l.g2, &l.v2};
+      uint32_t off = 0;
+      for (int m = 0; m < (i == 0 ? 3 : 4); ++m) {
+        adp_image_kernel<<<e->d.H, 256>>>(cur, *w2[m], ib, off);
+        off += 80u * (uint32_t)w2[m]->rows;
+      }
+      hm[i].ai = cur;
+      cur += (size_t)e->d.H * ib;
+    }
+    a.pre = 1;
+  }
+}
+
 int encode_big(const PackedView& w, const DArgs& a, CUtensorMap* q, CUtensorMap* p) {
   const uint64_t K = (uint64_t)w.cols, rows = (uint64_t)w.rows, gpr = K >> w.lg;
   const uint64_t qd[3] = {128, rows, K / 128}, qs[2] = {K, 128};
@@ -886,7 +998,7 @@ bool plan_decode(rwkvb_engine* e) {
     return w.kind == RWKVB_KIND_SG8 && w.lg == lg && aligned16(w.payload) && aligned16(w.meta);
   };
   auto adp1_ok = [&](const PackedView& w) {
-    return w.kind == RWKVB_KIND_SG8 && w.lg >= 0 && w.cols % 16 == 0 && aligned16(w.payload) && aligned16(w.meta);
+    return w.kind == RWKVB_KIND_SG8 && w.lg >= 2 && w.cols % 16 == 0 && aligned16(w.payload) && aligned16(w.meta);
   };
   auto adp2_ok = [&](const PackedView& w) {
     return w.kind == RWKVB_KIND_SG8 && w.lg >= 6 && d.C % (int)w.group == 0 && ((d.C >> w.lg) % 2) == 0 &&
@@ -979,6 +1091,19 @@ bool plan_decode(rwkvb_engine* e) {
   a.o_p = off;    off += vec;
   a.o_part = off; off += (uint32_t)kDPartTiles * kDW * 16u * 4u;
   a.o_misc = off; off += (uint32_t)kDMisc * 4u;
+  // Preload mode: the phase-B adapter image of a head CTA (80 B per adapter
+  // rank row) and the CTA's adapter first-stage item get dedicated shared
+  // memory, loaded at the start of each layer, when both fit beside the ring
+  // and no CTA has more than one item (bit 11 of the flags turns it off).
+  a.adp_b0 = 80u * (uint32_t)(d.rw + d.ra + d.rg);
+  a.adp_b1 = 80u * (uint32_t)(d.L > 1 ? d.rtot : d.rw + d.ra + d.rg);
+  const uint32_t adp_buf = ((a.adp_b1 > a.adp_b0 ? a.adp_b1 : a.adp_b0) + 127u) & ~127u;
+  const bool want_pre = !(e->flags & 0x400u) && !(e->flags & 0x800u) && e->d.abase[4] <= e->sms &&
+                        off + adp_buf + a.slot <= budget;
+  if (want_pre) {
+    a.o_adp = off;  off += adp_buf;
+    a.o_item = off; off += a.slot;
+  }
   a.smem_total = off;
   // tensor maps
   std::vector<DLayerMaps> hm((size_t)d.L);
@@ -994,6 +1119,9 @@ bool plan_decode(rwkvb_engine* e) {
       if (encode_adp2(*w2[m], a.abr[m], &hm[i].aq[m], &hm[i].ap[m]) != RWKVB_OK) return false;
   }
   if (encode_big(e->head, a, &hh[0], &hh[1]) != RWKVB_OK) return false;
+  plan_stream_copy(e, hm, want_pre);
+  if (!a.pre) a.smem_total = a.o_misc + (uint32_t)kDMisc * 4u;  // no dedicated buffers
+  if (e->dstream && cudaDeviceSynchronize() != cudaSuccess) return false;
   if (cudaMalloc((void**)&e->dmaps, sizeof(DLayerMaps) * (size_t)d.L) != cudaSuccess ||
       cudaMalloc((void**)&e->dhead, sizeof(CUtensorMap) * 2) != cudaSuccess) {
     cudaGetLastError();
@@ -1024,8 +1152,14 @@ const void* decode_fn(int lfk) {
   return lfk == 2 ? (const void*)decode_kernel<2> : (const void*)decode_kernel<1>;
 }
 
-int launch_persistent(rwkvb_engine* e, int ntok, int mode, int first_tok, const int* forced, cudaStream_t s) {
+int launch_persistent(rwkvb_engine* e, int ntok, int mode, int first_tok, const int* forced, cudaStream_t s,
+                      bool streamed = false) {
   DArgs a = e->da;
+  if (streamed) {
+    a.ring_count = reinterpret_cast<unsigned*>(e->hring_dev);
+    a.ring_cancel = reinterpret_cast<const int*>(e->hring_dev + 64);
+    a.ring_ids = reinterpret_cast<int*>(e->hring_dev + 128);
+  }
   a.ntok = ntok;
   a.mode = mode;
   a.first_tok = first_tok;
@@ -1127,6 +1261,7 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   e->b.tok = (int*)(base + misc_off + 16);
   e->b.step = (int*)(base + misc_off + 32);
   e->b.err = (int*)(base + misc_off + 48);
+  e->b.stop = (int*)(base + misc_off + 64);
   e->b.hist = (int*)(base + hist_off);
 
   // weights touched by each phase, in step order (embed, 5 per layer, head)
@@ -1204,6 +1339,8 @@ extern "C" int rwkvb_engine_destroy(rwkvb_engine* e) {
   if (e->dhead) cudaFree(e->dhead);
   if (e->dtokens) cudaFree(e->dtokens);
   if (e->dtrace) cudaFree(e->dtrace);
+  if (e->hring) cudaFreeHost(e->hring);
+  if (e->dstream) cudaFree(e->dstream);
   delete e;
   return RWKVB_OK;
 }
@@ -1315,6 +1452,64 @@ extern "C" int rwkvb_engine_decode_greedy(rwkvb_engine* e, int32_t first, int32_
   if (st == RWKVB_OK) st = st2;
   if (st == RWKVB_OK) st = check_err_flag(e, s);
   return st;
+}
+
+static int ensure_host_ring(rwkvb_engine* e) {
+  if (e->hring) return RWKVB_OK;
+  const size_t bytes = 128 + sizeof(int32_t) * (size_t)e->d.hist_cap;
+  void* h = nullptr;
+  if (cudaHostAlloc(&h, bytes, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    return RWKVB_EALLOC;
+  }
+  memset(h, 0, bytes);
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFreeHost(h);
+    return RWKVB_ECUDA;
+  }
+  e->hring = (uint8_t*)h;
+  e->hring_dev = (uint8_t*)d;
+  return RWKVB_OK;
+}
+
+extern "C" int rwkvb_engine_host_ring(rwkvb_engine* e, int32_t** ids, volatile uint32_t** count,
+                                      volatile int32_t** cancel, int32_t* cap) {
+  if (!e) return RWKVB_EARG;
+  if (!e->persistent) return RWKVB_EUNSUPPORTED;
+  const int st = ensure_host_ring(e);
+  if (st != RWKVB_OK) return st;
+  if (ids) *ids = reinterpret_cast<int32_t*>(e->hring + 128);
+  if (count) *count = reinterpret_cast<volatile uint32_t*>(e->hring);
+  if (cancel) *cancel = reinterpret_cast<volatile int32_t*>(e->hring + 64);
+  if (cap) *cap = e->d.hist_cap;
+  return RWKVB_OK;
+}
+
+extern "C" int rwkvb_engine_decode_stream(rwkvb_engine* e, int32_t first, int32_t n, int32_t* out_dev,
+                                          void* stream) {
+  if (!e || n < 0 || first < 0 || first >= e->d.V) return RWKVB_EARG;
+  if (!e->persistent) return RWKVB_EUNSUPPORTED;
+  if (n > e->d.hist_cap) return RWKVB_EARG;
+  int st = ensure_host_ring(e);
+  if (st != RWKVB_OK) return st;
+  // the previous streamed decode of this engine has finished (documented
+  // precondition), so nothing on the device writes the ring now
+  *reinterpret_cast<volatile uint32_t*>(e->hring) = 0u;
+  *reinterpret_cast<volatile int32_t*>(e->hring + 64) = 0;
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  if (n == 0) return RWKVB_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  st = launch_persistent(e, n, 0, first, nullptr, s, true);
+  if (st == RWKVB_OK && out_dev)
+    st = cuda_status(cudaMemcpyAsync(out_dev, e->b.hist, sizeof(int32_t) * (size_t)n, cudaMemcpyDeviceToDevice, s));
+  return st;
+}
+
+extern "C" int rwkvb_engine_check(rwkvb_engine* e, void* stream) {
+  if (!e) return RWKVB_EARG;
+  return check_err_flag(e, (cudaStream_t)stream);
 }
 
 extern "C" int rwkvb_engine_launches_per_step(rwkvb_engine* e, int32_t* out) {

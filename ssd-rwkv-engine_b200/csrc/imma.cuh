@@ -76,11 +76,19 @@ __device__ __forceinline__ void emit_digits(const float (&v)[8], int it, bool ac
     sum += __shfl_xor_sync(0xffffffffu, sum, o);
   }
   if (!act) return;
+  // m = f 2^e with f in [0.5, 1), so |x| 2^-e < 1; e, 127 * 2^-e and
+  // 2^e / 127 (= 2^e * f32(1/127) exactly: power-of-two scaling commutes with
+  // rounding) from the float bits, the library calls kept for the ends
   int e = 0;
-  if (m > 0.f) frexpf(m, &e);  // m = frac * 2^e, frac in [0.5, 1): |x| * 2^-e < 1
-  const float inv = ldexpf(127.0f, -e);  // exact
+  if (m > 0.f) {
+    const uint32_t be = __float_as_uint(m) >> 23;
+    if (be != 0u) e = (int)be - 126;
+    else frexpf(m, &e);  // subnormal m
+  }
+  const float inv = (e > -122 && e < 127) ? 127.0f * __uint_as_float((uint32_t)(127 - e) << 23) : ldexpf(127.0f, -e);
   if ((it & (gl - 1)) == 0) {
-    X.xc[it >> (lfk + 2)] = ldexpf(1.0f, e) / 127.0f;
+    X.xc[it >> (lfk + 2)] = (e > -127 && e < 128) ? __uint_as_float((uint32_t)(127 + e) << 23) * (1.0f / 127.0f)
+                                                   : ldexpf(1.0f, e) / 127.0f;
     X.xsum[it >> (lfk + 2)] = sum;
   }
   // Rounding by the 1.5 * 2^23 shift: for |y| < 2^22, (y + 1.5 * 2^23) rounds y

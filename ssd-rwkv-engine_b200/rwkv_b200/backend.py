@@ -313,10 +313,13 @@ class CudaB200Backend(_PackBase):
             else:
                 eng.reset()
             ids = [int(t) for t in token_ids] or [0]
+            done = self._chunked_prefill(ids, ctl)
+            rest = ids[done:]
             if ctl is None:
-                eng.forward(ids)
+                if rest:
+                    eng.forward(rest)
             else:
-                for t in ids:
+                for t in rest:
                     ctl.check()
                     eng.forward([t])
             state = self._snapshot(ids[-1])
@@ -325,6 +328,41 @@ class CudaB200Backend(_PackBase):
             metrics.prefill_wall_s = time.perf_counter() - t0
         self._last_state = state
         return state.clone()
+
+    PREFILL_CHUNK = 64  # positions per tcgen05 GEMM of the one-session prefill
+
+    def _chunked_prefill(self, ids: list[int], ctl) -> int:
+        """Whole ``PREFILL_CHUNK``-position chunks of a prompt through the
+        batched engine at one session (every projection of a chunk is one
+        tcgen05 GEMM over its positions, ``rwkvb_batch_prefill``), continuing
+        from and returning to the batch-1 engine's state; returns how many
+        prompt tokens it consumed (0 when the prompt is shorter than a chunk or
+        a projection is not SG8).  The rest of the prompt runs on the batch-1
+        engine.  Mirrors the reference's chunked prompt prefill
+        (rwkv7_forward.py:1046-1175)."""
+        P = self.PREFILL_CHUNK
+        full = len(ids) // P * P
+        if full == 0 or not self._model.sg8_projections:
+            return 0
+        from .engine import B200BatchEngine
+
+        eng = self._engine
+        pe = getattr(self, "_prefill_eng", None)
+        if pe is None:
+            pe = B200BatchEngine(self._model, 1, device=self._device)
+            self._prefill_eng = pe
+        pe.set_state(0, eng.get_state())
+        if ctl is None:
+            pe.prefill([ids[:full]])
+        else:
+            for c0 in range(0, full, P):
+                ctl.check()
+                pe.prefill([ids[c0:c0 + P]])
+        eng.att_x.copy_(pe.att_x[:, 0])
+        eng.wkv.copy_(pe.wkv[:, 0])
+        eng.ffn_x.copy_(pe.ffn_x[:, 0])
+        eng.logits.copy_(pe.logits[0])
+        return full
 
     def prefill_text(self, text: str, provider, metrics, initial_state: RecurrentState | None = None, *,
                      cancel_event=None, deadline=None) -> RecurrentState:
@@ -335,6 +373,16 @@ class CudaB200Backend(_PackBase):
     # -------------------------------------------------------------- decode
     def decode_greedy(self, state: RecurrentState, provider, max_tokens: int, metrics, *, temperature: float = 0.0,
                       token_callback=None, cancel_event=None, deadline=None) -> list[int]:
+        """Greedy (or sampled, ``temperature > 0``) continuation of ``state``.
+
+        Greedy decoding is ONE device launch for the whole generation: without
+        a callback/cancel/deadline the ids come back at the end; with them the
+        persistent kernel streams each id into mapped pinned host memory as it
+        is made, the callback runs on this thread as ids arrive, and a set
+        ``cancel_event`` or a passed ``deadline`` sets the device's cancel word
+        (the decode stops at the next token boundary and ``GenerationCancelled``
+        is raised, as the reference's token-boundary checks do).  The state
+        ends after every emitted token, with the next token's logits pending."""
         self.prepare_provider(provider)
         eng = self._engine_or_raise()
         n = max(0, int(max_tokens))
@@ -345,13 +393,43 @@ class CudaB200Backend(_PackBase):
             if isinstance(state.external_state, dict) and state.external_state.get("pending_logits") is None:
                 eng.forward([state.last_token_id])
             t0 = time.perf_counter()
-            if n and ctl is None and float(temperature) <= 0.0:
-                # whole greedy loop on the device: step i consumes step i-1's argmax
+            if n and float(temperature) <= 0.0 and (ctl is None or eng.persistent_active):
                 first = int(torch.argmax(eng.logits).item())
-                out = [first] + (eng.decode_greedy(first, n - 1) if n > 1 else [])
-                eng.forward([out[-1]])  # advance past the last emitted token (as the reference does)
-                lat = (time.perf_counter() - t0) * 1e3 / n
-                self._record(metrics, [lat] * n)
+                if ctl is None:
+                    # step i consumes emitted token i; the n-th step leaves the
+                    # logits after the last emitted token pending
+                    out = [first] + eng.decode_greedy(first, n)[: n - 1]
+                    lat = (time.perf_counter() - t0) * 1e3 / n
+                    self._record(metrics, [lat] * n)
+                else:
+                    lats: list[float] = []
+                    last = [time.perf_counter()]
+
+                    def emit(tok: int) -> None:
+                        ctl.emit(tok)
+                        out.append(int(tok))
+                        now = time.perf_counter()
+                        lats.append((now - last[0]) * 1e3)
+                        last[0] = now
+
+                    emit(first)
+
+                    def on_token(i: int, tok: int) -> None:
+                        if i < n - 1:
+                            emit(tok)
+
+                    def should_stop() -> bool:
+                        try:
+                            ctl.check()
+                        except GenerationCancelled:
+                            return True
+                        return False
+
+                    eng.decode_stream(first, n, on_token=on_token, should_stop=should_stop)
+                    self._record(metrics, lats)
+                    if len(out) < n:  # stopped at a token boundary by the cancel word
+                        ctl.check()
+                        raise GenerationCancelled("generation cancelled")
             else:
                 lats = []
                 for _ in range(n):
@@ -433,8 +511,7 @@ class CudaB200Backend(_PackBase):
                 self._batch_engines[nb] = eng
             t0 = time.perf_counter()
             eng.reset()
-            for pos in range(len(ids[0])):
-                eng.forward([t[pos] for t in ids])
+            eng.prefill(ids)  # chunks of positions as tcgen05 GEMM rows (rwkvb_batch_prefill)
             first = eng.logits.argmax(dim=1).tolist()
             rest = eng.decode_greedy(n - 1) if n > 1 else np.zeros((0, nb), np.int32)
             torch.cuda.synchronize(self._device)
@@ -448,6 +525,10 @@ class CudaB200Backend(_PackBase):
         for eng in self._batch_engines.values():
             eng.close()
         self._batch_engines = {}
+        pe = getattr(self, "_prefill_eng", None)
+        if pe is not None:
+            pe.close()
+            self._prefill_eng = None
         if self._engine is not None:
             self._engine.close()
             self._engine = None

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes
 import re
+import time
 
 import numpy as np
 import torch
@@ -230,6 +231,69 @@ class B200Engine:
         native.check(self.lib.rwkvb_engine_decode_greedy_async(self._h, int(first_token), int(n), out.data_ptr(),
                                                                self._stream(stream)),
                      "rwkvb_engine_decode_greedy_async")
+
+    def _host_ring(self):
+        ring = getattr(self, "_ring", None)
+        if ring is None:
+            ids, cnt, cancel, cap = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_int32()
+            native.check(self.lib.rwkvb_engine_host_ring(self._h, ctypes.byref(ids), ctypes.byref(cnt),
+                                                         ctypes.byref(cancel), ctypes.byref(cap)),
+                         "rwkvb_engine_host_ring")
+            ring = (np.ctypeslib.as_array((ctypes.c_int32 * cap.value).from_address(ids.value)),
+                    ctypes.c_uint32.from_address(cnt.value), ctypes.c_int32.from_address(cancel.value), cap.value)
+            self._ring = ring
+        return ring
+
+    def decode_stream(self, first_token: int, n: int, on_token=None, should_stop=None, stream=None,
+                      poll_s: float = 20e-6) -> list[int]:
+        """Greedy decode of ``n`` steps (step 0 consumes ``first_token``) as ONE
+        persistent launch whose ids reach the host through mapped pinned memory
+        as the device makes them (``rwkvb_engine_decode_stream``).
+
+        ``on_token(i, id)`` runs on this thread for every id in order;
+        ``should_stop()`` is polled meanwhile.  When it returns true, or
+        ``on_token`` raises, the device cancel word is set and the decode stops
+        at the next token boundary; the exception (if any) is re-raised after
+        the launch has ended.  Returns the ids the device produced."""
+        if not self.persistent_active:
+            raise native.RwkvbError(native.RWKVB_EUNSUPPORTED, "decode_stream (persistent engines only)")
+        ids_view, count, cancel, cap = self._host_ring()
+        if n > cap:
+            raise ValueError(f"n must be <= {cap}")
+        st = stream if stream is not None else torch.cuda.current_stream(self.device)
+        native.check(self.lib.rwkvb_engine_decode_stream(self._h, int(first_token), int(n), None, st.cuda_stream),
+                     "rwkvb_engine_decode_stream")
+        done = torch.cuda.Event()
+        done.record(st)
+        out: list[int] = []
+        err: BaseException | None = None
+        stopping = False
+        while True:
+            c = count.value
+            while len(out) < c:
+                tok = int(ids_view[len(out)])
+                out.append(tok)
+                if on_token is not None and err is None and not stopping:
+                    try:
+                        on_token(len(out) - 1, tok)
+                    except BaseException as e:  # noqa: BLE001 - re-raised below
+                        err = e
+                        cancel.value = 1
+            if not stopping and err is None and should_stop is not None and should_stop():
+                stopping = True
+                cancel.value = 1
+            if len(out) >= n:
+                break
+            if done.query():
+                if count.value <= len(out):
+                    break
+                continue
+            time.sleep(poll_s)
+        done.synchronize()
+        native.check(self.lib.rwkvb_engine_check(self._h, st.cuda_stream), "rwkvb_engine_decode_stream")
+        if err is not None:
+            raise err
+        return out
 
     def greedy(self, prompt: list[int], n_new: int, keep_logits: bool = False):
         """Prompt token by token, then ``n_new`` greedy ids (as the oracle's ``greedy``)."""

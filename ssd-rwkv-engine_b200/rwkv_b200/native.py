@@ -129,6 +129,9 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_engine_decode_greedy_async": (ctypes.c_int, [vp, i32, i32, vp, vp]),
         "rwkvb_engine_launches_per_step": (ctypes.c_int, [vp, P(i32)]),
         "rwkvb_engine_trace": (ctypes.c_int, [vp, P(u64), i32, P(i32)]),
+        "rwkvb_engine_host_ring": (ctypes.c_int, [vp, P(vp), P(vp), P(vp), P(i32)]),
+        "rwkvb_engine_decode_stream": (ctypes.c_int, [vp, i32, i32, vp, vp]),
+        "rwkvb_engine_check": (ctypes.c_int, [vp, vp]),
         "rwkvb_batch_create": (ctypes.c_int, [P(ModelDesc), i32, u32, P(vp)]),
         "rwkvb_batch_create_tp": (ctypes.c_int, [P(ModelDesc), i32, P(TPDesc), u32, P(vp)]),
         "rwkvb_batch_prepare": (ctypes.c_int, [vp, vp]),

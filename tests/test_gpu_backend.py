@@ -100,3 +100,58 @@ def test_generate_greedy_batch_uses_batched_engine_and_matches_generate(model):
     # unequal lengths fall back to prompt-by-prompt generation with the same results
     mixed = b.generate_greedy_batch(["ab", "abcd"], prov, 4, metrics=None)
     assert mixed == [oracle.greedy(list(p.encode()), 4)[0] for p in ("ab", "abcd")]
+
+
+def test_streamed_decode_is_one_launch_and_cancels_at_a_token_boundary(model):
+    """With a callback the whole generation is one persistent launch whose ids
+    arrive through mapped host memory; a cancel set from the callback stops it
+    at the next token boundary with ``GenerationCancelled``."""
+    shape, pack, oracle, b, prov = model
+    assert b._engine.persistent_active
+    text = "stream"
+    ref, _, _ = oracle.greedy(list(text.encode()), 10)
+    st = b.prefill_text(text, prov, metrics=None)
+    seen = []
+    ids = b.decode_greedy(st, prov, 10, metrics=None, token_callback=seen.append)
+    assert ids == ref and seen == ref
+    ev = threading.Event()
+    got = []
+
+    def cb(tok):
+        got.append(tok)
+        if len(got) == 3:
+            ev.set()
+
+    with pytest.raises(bk.GenerationCancelled):
+        b.decode_greedy(st, prov, 10, metrics=None, token_callback=cb, cancel_event=ev)
+    assert got == ref[:3]
+    import time as _time
+
+    with pytest.raises(bk.GenerationCancelled):
+        b.decode_greedy(st, prov, 5, metrics=None, token_callback=lambda t: None, deadline=_time.monotonic() - 1)
+    # the engine is usable afterwards and a fresh decode from the same state is unchanged
+    assert b.decode_greedy(st, prov, 10, metrics=None) == ref
+
+
+def test_long_prompt_prefill_runs_in_chunks_and_matches_oracle(model):
+    shape, pack, oracle, b, prov = model
+    prompt = synth.seeded_prompt(2 * b.PREFILL_CHUNK + 5, shape.vocab, 77)
+    st = b.prefill_tokens(prompt)
+    assert getattr(b, "_prefill_eng", None) is not None  # whole chunks went through the batched engine
+    ref_ids, ref_logits, ref_state = oracle.greedy(prompt, 6)
+    np.testing.assert_allclose(b.probe_logits(st).cpu().numpy(), ref_logits[len(prompt) - 1], atol=1e-3, rtol=0)
+    assert b.decode_greedy(st, prov, 6, metrics=None) == ref_ids
+
+
+def test_prefix_state_reuse_matches_full_prefill(model):
+    """The engine's prefix cache flow: a cached prefix state continued with a
+    suffix (``initial_state``) equals prefilling the whole text."""
+    shape, pack, oracle, b, prov = model
+    pre, suf = "system: be brief. ", "user: hi"
+    st_pre = b.prefill_text(pre, prov, metrics=None)
+    cached = st_pre.clone()
+    st_a = b.prefill_text(suf, prov, metrics=None, initial_state=cached)
+    a = b.decode_greedy(st_a, prov, 6, metrics=None)
+    st_b = b.prefill_text(pre + suf, prov, metrics=None)
+    c = b.decode_greedy(st_b, prov, 6, metrics=None)
+    assert a == c == oracle.greedy(list((pre + suf).encode()), 6)[0]
