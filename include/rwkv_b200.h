@@ -220,6 +220,31 @@ typedef struct rwkvb_engine rwkvb_engine;
 int rwkvb_engine_create(const rwkvb_model_desc* desc, uint32_t flags, rwkvb_engine** out);
 int rwkvb_engine_destroy(rwkvb_engine* e);
 
+/* Residency tiers: an engine whose streamed layers live in pinned host memory
+ * and are staged into a ring of device slots on every token step, for models
+ * larger than the HBM budget given to them.  Replaces the reference's staging
+ * ring and prefetch planner (rwkv_ssd/runtime/staging.py:40-129,
+ * prefetch.py:1-131) and its resident / streamed split (residency.py:1-118).
+ * `desc` describes every layer; a streamed layer's matrices point into the
+ * device slot slot_of_layer[i] (>= 0; -1: resident layer), at the offsets of
+ * its image host_src[i] (layer_bytes of PINNED host memory, the layer's blobs
+ * laid out as in the slot).  Per step, on a copy stream forked from the step's
+ * stream: the H2D copy of each streamed layer's image into its slot, after the
+ * kernels of the slot's previous user in the step; the layer's kernels wait
+ * for their copy.  With n_slots slots the copies run up to n_slots streamed
+ * layers ahead of the compute (2: one layer of lookahead).  The step is the
+ * multi-kernel step (and its CUDA graph, copies included).  The engine borrows
+ * the host images and the slots. */
+typedef struct rwkvb_stage_desc {
+  int32_t n_slots;
+  const int32_t* slot_of_layer;  /* HOST [n_layer] */
+  const void* const* host_src;   /* HOST [n_layer]; NULL for resident layers */
+  void* const* slot_dev;         /* HOST [n_slots] device pointers */
+  uint64_t layer_bytes;
+} rwkvb_stage_desc;
+int rwkvb_engine_create_staged(const rwkvb_model_desc* desc, const rwkvb_stage_desc* stage, uint32_t flags,
+                               rwkvb_engine** out);
+
 /* Device pointers of the recurrent state, laid out as RecurrentState.rwkv7_state
  * (state_cache.py:38-56, rwkv7_skeleton.py:121-131): per layer l
  *   att_x + l*n_embd              x_prev of the time mix   [n_embd]

@@ -640,6 +640,18 @@ struct rwkvb_engine {
   uint8_t* hring = nullptr;
   uint8_t* hring_dev = nullptr;  // the same memory as the device addresses it
   uint8_t* dstream = nullptr;    // streaming copy of the big matrices (persistent kernel)
+  // staged layers (rwkvb_engine_create_staged): layer li is streamed when
+  // stage_slot[li] >= 0; its image (stage_bytes) is copied from pinned host
+  // memory into device slot stage_slot[li] on the copy stream before the
+  // layer's kernels, after the slot's previous user in the step is done
+  bool staged = false;
+  std::vector<int> stage_slot;
+  std::vector<const void*> stage_src;
+  std::vector<void*> stage_dev;
+  uint64_t stage_bytes = 0;
+  cudaStream_t copy = nullptr;
+  cudaEvent_t ev_fork = nullptr;
+  std::vector<cudaEvent_t> ev_loaded, ev_done;  // per streamed layer, in step order
 };
 
 namespace {
@@ -749,6 +761,27 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
   cudaError_t err = cudaSuccess;
   auto chk = [&](cudaError_t x) { if (err == cudaSuccess && x != cudaSuccess) err = x; };
   e->launches = 0;
+  // staged layers: the copy stream forks from the step's stream, so the
+  // copies belong to the same step (and to its CUDA graph when captured)
+  const int nslots = (int)e->stage_dev.size();
+  int sj = 0;  // streamed layers met so far
+  if (e->staged) {
+    chk(cudaEventRecord(e->ev_fork, s));
+    chk(cudaStreamWaitEvent(e->copy, e->ev_fork, 0));
+  }
+  auto stage_in = [&](int li) {  // before layer li's kernels
+    if (!e->staged || e->stage_slot[li] < 0) return;
+    const int slot = e->stage_slot[li];
+    if (sj >= nslots) chk(cudaStreamWaitEvent(e->copy, e->ev_done[sj - nslots], 0));  // slot's previous user done
+    chk(cudaMemcpyAsync(e->stage_dev[slot], e->stage_src[li], e->stage_bytes, cudaMemcpyHostToDevice, e->copy));
+    chk(cudaEventRecord(e->ev_loaded[sj], e->copy));
+    chk(cudaStreamWaitEvent(s, e->ev_loaded[sj], 0));
+  };
+  auto stage_out = [&](int li) {  // after layer li's kernels
+    if (!e->staged || e->stage_slot[li] < 0) return;
+    chk(cudaEventRecord(e->ev_done[sj], s));
+    ++sj;
+  };
   {
     EmbedArgs a;
     a.emb = e->emb; a.ln0_w = e->ln0_w; a.ln0_b = e->ln0_b; a.b = e->b; a.d = d; a.pf = pf_for(phase++);
@@ -763,6 +796,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
   const int gm = (2 * e->sms) / 3 > 0 ? (2 * e->sms) / 3 : 1;
   for (int li = 0; li < d.L; ++li) {
     const LayerDev& l = e->layers[li];
+    stage_in(li);
     {
       AttInArgs a;
       memset(&a, 0, sizeof(a));
@@ -813,6 +847,7 @@ int record_step(rwkvb_engine* e, cudaStream_t s) {
       chk(launch(phase_kernel, grid, kThreads, smem, s, e->pdl, a));
     }
     e->launches += 5;
+    stage_out(li);
   }
   {
     PhaseArgs a;
@@ -1328,6 +1363,50 @@ extern "C" int rwkvb_engine_create(const rwkvb_model_desc* m, uint32_t flags, rw
   return RWKVB_OK;
 }
 
+extern "C" int rwkvb_engine_create_staged(const rwkvb_model_desc* m, const rwkvb_stage_desc* st, uint32_t flags,
+                                          rwkvb_engine** out) {
+  if (!m || !st || !out || st->n_slots <= 0 || !st->slot_of_layer || !st->host_src || !st->slot_dev ||
+      st->layer_bytes == 0)
+    return RWKVB_EARG;
+  *out = nullptr;
+  int streamed = 0;
+  for (int i = 0; i < m->n_layer; ++i) {
+    const int sl = st->slot_of_layer[i];
+    if (sl >= st->n_slots || sl < -1) return RWKVB_EARG;
+    if (sl >= 0) {
+      if (!st->host_src[i] || !st->slot_dev[sl]) return RWKVB_EARG;
+      ++streamed;
+    }
+  }
+  rwkvb_engine* e = nullptr;
+  // staged layers run as the multi-kernel step (bit 2: no persistent kernel)
+  const int rc = rwkvb_engine_create(m, flags | 0x4u, &e);
+  if (rc != RWKVB_OK) return rc;
+  e->staged = streamed > 0;
+  e->stage_bytes = st->layer_bytes;
+  e->stage_slot.assign(st->slot_of_layer, st->slot_of_layer + m->n_layer);
+  e->stage_src.assign(st->host_src, st->host_src + m->n_layer);
+  e->stage_dev.assign(st->slot_dev, st->slot_dev + st->n_slots);
+  cudaError_t err = cudaSuccess;
+  if (e->staged) {
+    err = cudaStreamCreateWithFlags(&e->copy, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming);
+    for (int j = 0; j < streamed && err == cudaSuccess; ++j) {
+      cudaEvent_t a = nullptr, b = nullptr;
+      err = cudaEventCreateWithFlags(&a, cudaEventDisableTiming);
+      if (err == cudaSuccess) err = cudaEventCreateWithFlags(&b, cudaEventDisableTiming);
+      if (a) e->ev_loaded.push_back(a);
+      if (b) e->ev_done.push_back(b);
+    }
+  }
+  if (err != cudaSuccess) {
+    rwkvb_engine_destroy(e);
+    return cuda_status(err);
+  }
+  *out = e;
+  return RWKVB_OK;
+}
+
 extern "C" int rwkvb_engine_destroy(rwkvb_engine* e) {
   if (!e) return RWKVB_EARG;
   if (e->exec) cudaGraphExecDestroy(e->exec);
@@ -1341,6 +1420,10 @@ extern "C" int rwkvb_engine_destroy(rwkvb_engine* e) {
   if (e->dtrace) cudaFree(e->dtrace);
   if (e->hring) cudaFreeHost(e->hring);
   if (e->dstream) cudaFree(e->dstream);
+  for (cudaEvent_t ev : e->ev_loaded) cudaEventDestroy(ev);
+  for (cudaEvent_t ev : e->ev_done) cudaEventDestroy(ev);
+  if (e->ev_fork) cudaEventDestroy(e->ev_fork);
+  if (e->copy) cudaStreamDestroy(e->copy);
   delete e;
   return RWKVB_OK;
 }

@@ -219,9 +219,41 @@ class CudaB200Backend(_PackBase):
         from .engine import ModelUpload
 
         pack = packed_tensors_from_provider(provider)
+        budget, resident, slots = self._residency(config, pack)
         with torch.cuda.device(self._device):
-            self._model = ModelUpload(pack, self._device)
+            self._model = ModelUpload(pack, self._device, hbm_budget=budget, resident_layers=resident,
+                                      stage_slots=slots)
         self._engine = B200Engine(self._model, device=self._device, use_graph=self.use_graph)
+
+    @staticmethod
+    def _residency(config, pack) -> tuple[int | None, list[int] | None, int]:
+        """Residency tiers from the engine config (``RuntimeConfig.mode`` and
+        ``residency_profile``, as the reference's ``apply_residency_policy``,
+        residency.py:13-44): "resident" keeps every layer in HBM, "partial" the
+        profile's ``resident_layer_ids`` (default: the first and last layers),
+        "streaming" none; an ``hbm_budget_bytes`` attribute keeps as many layers
+        as fit in that many bytes of HBM.  ``stage_slots`` (default 2) device
+        slots receive the streamed layers."""
+        if config is None:
+            return None, None, 2
+        slots = int(getattr(config, "stage_slots", 2) or 2)
+        budget = getattr(config, "hbm_budget_bytes", None)
+        if budget is not None:
+            return int(budget), None, slots
+        mode = str(getattr(config, "mode", "resident") or "resident").strip().lower()
+        n_layer = 1 + max(int(n.split(".")[1]) for n in pack if n.startswith("blocks."))
+        if mode == "streaming":
+            return None, [], slots
+        if mode == "partial":
+            prof = getattr(config, "residency_profile", None)
+            if prof:
+                import json
+                from pathlib import Path
+
+                ids = json.loads(Path(prof).read_text(encoding="utf-8")).get("resident_layer_ids", [])
+                return None, [int(i) for i in ids], slots
+            return None, sorted({0, n_layer - 1}), slots
+        return None, None, slots
 
     @property
     def num_layers(self) -> int:
@@ -243,7 +275,7 @@ class CudaB200Backend(_PackBase):
         return {
             "name": "cuda_b200",
             "declared": {
-                "pack_streaming": False, "skeleton": False, "resident": True, "state_snapshot": True,
+                "pack_streaming": True, "skeleton": False, "resident": True, "state_snapshot": True,
                 "batch": True, "prefix_cache": True, "tokenizer": self.tokenizer is not None,
                 "state_kind": "rwkv7", "supported_codecs": list(SUPPORTED_CODECS), "requires_ggml_bin": False,
                 "token_generation": True, "logits_probe": True, "state_transfer": True,
@@ -264,23 +296,72 @@ class CudaB200Backend(_PackBase):
             raise RuntimeError("cuda_b200: call prepare_provider() before generating")
         return self._engine
 
-    def _snapshot(self, last: int) -> RecurrentState:
+    # Two forms of RecurrentState.  The *live* form (what prefill and decode
+    # return) holds the state after every consumed token in rwkv7_state and,
+    # in external_state, the next token's logits ("pending_logits") plus the
+    # state before the last token ("pre_state").  The *portable* form (what
+    # get_recurrent_state returns and snapshot files hold) is the reference's:
+    # rwkv7_state = the state before last_token_id, nothing else; resuming
+    # consumes last_token_id first (rwkv7_forward.py:941-990).
+    def _snapshot(self, last: int, pre: list[torch.Tensor]) -> RecurrentState:
         eng = self._engine
         return RecurrentState(last_token_id=int(last), rwkv7_state=eng.get_state(),
-                              external_state={"pending_logits": eng.logits.clone()})
+                              external_state={"pending_logits": eng.logits.clone(), "pre_state": pre})
 
-    def _restore(self, state: RecurrentState) -> None:
+    def _restore(self, state: RecurrentState) -> list[torch.Tensor]:
+        """Load ``state`` into the engine (consuming ``last_token_id`` for the
+        portable form); returns the state before the last token."""
         eng = self._engine
         if state.rwkv7_state is None:
             raise ValueError("cuda_b200 state has no rwkv7_state")
-        eng.set_state(state.rwkv7_state)
         ext = state.external_state if isinstance(state.external_state, dict) else {}
         pl = ext.get("pending_logits")
         if pl is not None:
+            eng.set_state(state.rwkv7_state)
             eng.logits.copy_(pl.to(eng.device, torch.float32))
+            pre = ext.get("pre_state")
+            return [t.clone() for t in pre] if pre is not None else eng.get_state()
+        eng.set_state(state.rwkv7_state)
+        pre = eng.get_state()
+        eng.forward([int(state.last_token_id)])
+        return pre
 
     def get_recurrent_state(self) -> RecurrentState | None:
-        return self._last_state.clone() if self._last_state is not None else None
+        """The portable form of the current state (single representation, as
+        the reference's snapshot writer requires)."""
+        st = self._last_state
+        if st is None:
+            return None
+        ext = st.external_state if isinstance(st.external_state, dict) else {}
+        pre = ext.get("pre_state")
+        if pre is None:
+            return st.clone()
+        return RecurrentState(last_token_id=int(st.last_token_id), rwkv7_state=[t.clone() for t in pre])
+
+    def save_snapshot(self, path, *, prompt: str = "", state: RecurrentState | None = None):
+        """Write the current (or the given) state as a reference-format snapshot
+        file (``rwkv_b200.snapshot``); the reference engine's load_snapshot
+        reads it, and load_snapshot here reads the reference's."""
+        from . import snapshot
+
+        st = state if state is not None else self.get_recurrent_state()
+        if st is None:
+            raise RuntimeError("cuda_b200 has no recurrent state to snapshot")
+        ext = st.external_state if isinstance(st.external_state, dict) else {}
+        pre = ext.get("pre_state") if ext.get("pending_logits") is not None else None
+        tensors = pre if pre is not None else st.rwkv7_state
+        meta = snapshot.SnapshotMeta(prompt=prompt, last_token_id=int(st.last_token_id))
+        return snapshot.save_snapshot(path, tensors, meta)
+
+    def load_snapshot(self, path) -> RecurrentState:
+        """Read a snapshot file (this backend's or the reference engine's) and
+        make it the current state (portable form)."""
+        from . import snapshot
+
+        tensors, meta = snapshot.load_snapshot(path)
+        st = RecurrentState(last_token_id=int(meta.last_token_id), rwkv7_state=tensors)
+        self.set_recurrent_state(st)
+        return st.clone()
 
     def set_recurrent_state(self, state: RecurrentState) -> None:
         if state.rwkv7_state is None or len(state.rwkv7_state) != 3 * self.num_layers:
@@ -313,8 +394,8 @@ class CudaB200Backend(_PackBase):
             else:
                 eng.reset()
             ids = [int(t) for t in token_ids] or [0]
-            done = self._chunked_prefill(ids, ctl)
-            rest = ids[done:]
+            done = self._chunked_prefill(ids[:-1], ctl)
+            rest = ids[done:-1]
             if ctl is None:
                 if rest:
                     eng.forward(rest)
@@ -322,7 +403,11 @@ class CudaB200Backend(_PackBase):
                 for t in rest:
                     ctl.check()
                     eng.forward([t])
-            state = self._snapshot(ids[-1])
+            pre = eng.get_state()  # the state before the last prompt token (portable form)
+            if ctl is not None:
+                ctl.check()
+            eng.forward([ids[-1]])
+            state = self._snapshot(ids[-1], pre)
         torch.cuda.synchronize(eng.device)
         if metrics is not None and hasattr(metrics, "prefill_wall_s"):
             metrics.prefill_wall_s = time.perf_counter() - t0
@@ -389,16 +474,17 @@ class CudaB200Backend(_PackBase):
         ctl = _control(token_callback, cancel_event, deadline)
         out: list[int] = []
         with self._lock:
-            self._restore(state)
-            if isinstance(state.external_state, dict) and state.external_state.get("pending_logits") is None:
-                eng.forward([state.last_token_id])
+            pre = self._restore(state)
             t0 = time.perf_counter()
             if n and float(temperature) <= 0.0 and (ctl is None or eng.persistent_active):
                 first = int(torch.argmax(eng.logits).item())
                 if ctl is None:
-                    # step i consumes emitted token i; the n-th step leaves the
-                    # logits after the last emitted token pending
-                    out = [first] + eng.decode_greedy(first, n)[: n - 1]
+                    # step i consumes emitted token i: n - 1 steps on the
+                    # device, the state before the last emitted token is kept
+                    # (portable form), then the last token is consumed
+                    out = [first] + (eng.decode_greedy(first, n - 1) if n > 1 else [])
+                    pre = eng.get_state()
+                    eng.forward([out[-1]])
                     lat = (time.perf_counter() - t0) * 1e3 / n
                     self._record(metrics, [lat] * n)
                 else:
@@ -415,8 +501,7 @@ class CudaB200Backend(_PackBase):
                     emit(first)
 
                     def on_token(i: int, tok: int) -> None:
-                        if i < n - 1:
-                            emit(tok)
+                        emit(tok)
 
                     def should_stop() -> bool:
                         try:
@@ -425,11 +510,15 @@ class CudaB200Backend(_PackBase):
                             return True
                         return False
 
-                    eng.decode_stream(first, n, on_token=on_token, should_stop=should_stop)
-                    self._record(metrics, lats)
+                    if n > 1:
+                        eng.decode_stream(first, n - 1, on_token=on_token, should_stop=should_stop)
                     if len(out) < n:  # stopped at a token boundary by the cancel word
+                        self._record(metrics, lats)
                         ctl.check()
                         raise GenerationCancelled("generation cancelled")
+                    pre = eng.get_state()
+                    eng.forward([out[-1]])
+                    self._record(metrics, lats)
             else:
                 lats = []
                 for _ in range(n):
@@ -438,12 +527,13 @@ class CudaB200Backend(_PackBase):
                     s0 = time.perf_counter()
                     tok = self._sample(eng.logits, float(temperature))
                     out.append(tok)
+                    pre = eng.get_state()
                     eng.forward([tok])
                     if ctl is not None:
                         ctl.emit(tok)
                     lats.append((time.perf_counter() - s0) * 1e3)
                 self._record(metrics, lats)
-            self._last_state = self._snapshot(out[-1] if out else state.last_token_id)
+            self._last_state = self._snapshot(out[-1] if out else state.last_token_id, pre)
         return out
 
     @staticmethod

@@ -23,7 +23,7 @@ import numpy as np
 import torch
 
 from . import native
-from .residency import VectorArena, WeightArena
+from .residency import LayerStaging, VectorArena, WeightArena, _place, layer_of, plan_residency
 from .synth import RWKV7Shape
 
 _MATS = ("att.receptance.weight", "att.key.weight", "att.value.weight", "att.output.weight",
@@ -61,10 +61,17 @@ def infer_shape(pack) -> RWKV7Shape:
 
 
 class ModelUpload:
-    """A packed model resident in HBM plus its ``rwkvb_model_desc`` (weights in one
-    ``WeightArena``, fp32 vectors in one ``VectorArena``)."""
+    """A packed model in HBM plus its ``rwkvb_model_desc`` (weights in one
+    ``WeightArena``, fp32 vectors in one ``VectorArena``).
 
-    def __init__(self, pack, device: torch.device):
+    Residency tiers: with ``hbm_budget`` (bytes of packed weights) below the
+    model's size, or an explicit ``resident_layers`` list, the layers that do
+    not fit stay in pinned host memory and ``stage`` (a ``LayerStaging``)
+    streams them through ``stage_slots`` device slots on every token step; the
+    embedding, the head and the kept ("hot") layers are resident."""
+
+    def __init__(self, pack, device: torch.device, *, hbm_budget: int | None = None, stage_slots: int = 2,
+                 resident_layers: list[int] | None = None):
         s = infer_shape(pack)
         self.shape = s
         self.device = device
@@ -78,7 +85,17 @@ class ModelUpload:
             else:
                 vecs[name] = np.asarray(e.payload, dtype=np.float32).reshape(-1) \
                     if not isinstance(e.payload, torch.Tensor) else e.payload
-        self.weights = WeightArena(mats, device)
+        # per-layer matrices (r_k is decoded into a vector at load: always resident)
+        by_layer: dict[int, list] = {li: [] for li in range(s.n_layer)}
+        globals_ = []
+        for it in mats:
+            li = layer_of(it[0])
+            (by_layer[li] if li >= 0 and not it[0].endswith(".att.r_k") else globals_).append(it)
+        streamed = plan_residency({li: _place(v)[2] for li, v in by_layer.items()}, _place(globals_)[2], s.n_layer,
+                                  hbm_budget=hbm_budget, n_slots=stage_slots, resident_layers=resident_layers)
+        resident = globals_ + [it for li in range(s.n_layer) if li not in set(streamed) for it in by_layer[li]]
+        self.stage = LayerStaging(by_layer, streamed, s.n_layer, stage_slots, device) if streamed else None
+        self.weights = WeightArena(resident, device)
         self.vectors = VectorArena(vecs, device)
         for i in range(s.n_layer):
             nm = f"blocks.{i}.att.r_k"
@@ -92,6 +109,8 @@ class ModelUpload:
                 name = f"blocks.{i}.{suffix}"
                 if name in self.weights:
                     setattr(d, _DESC_FIELD[suffix], self.weights[name].desc)
+                elif self.stage is not None and name in self.stage.descs:
+                    setattr(d, _DESC_FIELD[suffix], self.stage.descs[name].desc)
             for suffix, field in _VEC_FIELD.items():
                 name = f"blocks.{i}.{suffix}"
                 if name in self.vectors.offs or name in self.vectors.extra:
@@ -138,8 +157,13 @@ class B200Engine:
             if ring_slots is not None:
                 flags |= (int(ring_slots) & 0xF) << native.FLAG_RING_SLOTS_SHIFT
             h = ctypes.c_void_p()
-            native.check(self.lib.rwkvb_engine_create(ctypes.byref(md), flags, ctypes.byref(h)),
-                         "rwkvb_engine_create")
+            if self._model.stage is not None:
+                # streamed layers: the multi-kernel step with the staging copies in it
+                native.check(self.lib.rwkvb_engine_create_staged(ctypes.byref(md), ctypes.byref(self._model.stage.desc),
+                                                                 flags, ctypes.byref(h)), "rwkvb_engine_create_staged")
+            else:
+                native.check(self.lib.rwkvb_engine_create(ctypes.byref(md), flags, ctypes.byref(h)),
+                             "rwkvb_engine_create")
             self._h = h
             att, wkv, ffn, logits = (ctypes.c_void_p() for _ in range(4))
             native.check(self.lib.rwkvb_engine_buffers(h, ctypes.byref(att), ctypes.byref(wkv), ctypes.byref(ffn),
@@ -338,6 +362,8 @@ class B200BatchEngine:
         self.batch = int(batch)
         with torch.cuda.device(self.device):
             self._model = pack if isinstance(pack, ModelUpload) else ModelUpload(pack, self.device)
+            if self._model.stage is not None:
+                raise ValueError("B200BatchEngine needs every layer resident (the model has streamed layers)")
             self.shape = s = self._model.shape
             flags = 0 if use_graph else native.FLAG_NO_GRAPH
             if not pdl:

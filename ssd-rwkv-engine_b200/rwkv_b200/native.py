@@ -92,6 +92,12 @@ class TPDesc(ctypes.Structure):
                 ("peer", ctypes.POINTER(ctypes.c_void_p))]
 
 
+class StageDesc(ctypes.Structure):
+    _fields_ = [("n_slots", ctypes.c_int32), ("slot_of_layer", ctypes.POINTER(ctypes.c_int32)),
+                ("host_src", ctypes.POINTER(ctypes.c_void_p)), ("slot_dev", ctypes.POINTER(ctypes.c_void_p)),
+                ("layer_bytes", ctypes.c_uint64)]
+
+
 def native_lib_path() -> Path | None:
     return _build.LIB if _build.LIB.is_file() else None
 
@@ -122,6 +128,7 @@ def _declare(h: ctypes.CDLL) -> None:
                                           ctypes.c_int, ctypes.c_int, vp]),
         "rwkvb_engine_create": (ctypes.c_int, [P(ModelDesc), u32, P(vp)]),
         "rwkvb_engine_destroy": (ctypes.c_int, [vp]),
+        "rwkvb_engine_create_staged": (ctypes.c_int, [P(ModelDesc), P(StageDesc), u32, P(vp)]),
         "rwkvb_engine_buffers": (ctypes.c_int, [vp, P(vp), P(vp), P(vp), P(vp)]),
         "rwkvb_engine_reset": (ctypes.c_int, [vp, vp]),
         "rwkvb_engine_forward": (ctypes.c_int, [vp, P(i32), i32, vp]),

@@ -155,3 +155,19 @@ def test_prefix_state_reuse_matches_full_prefill(model):
     st_b = b.prefill_text(pre + suf, prov, metrics=None)
     c = b.decode_greedy(st_b, prov, 6, metrics=None)
     assert a == c == oracle.greedy(list((pre + suf).encode()), 6)[0]
+
+
+def test_snapshot_file_resumes_the_generation(model, tmp_path):
+    """State export to a reference-format snapshot file and back: the portable
+    state (before the last token) resumes exactly where the live state does."""
+    shape, pack, oracle, b, prov = model
+    st = b.prefill_text("snap", prov, metrics=None)
+    first = b.decode_greedy(st, prov, 5, metrics=None)
+    live = b._last_state.clone()
+    path = b.save_snapshot(tmp_path / "s.rws", prompt="snap")
+    direct = b.decode_greedy(live, prov, 6, metrics=None)
+    restored = b.load_snapshot(path)
+    assert restored.external_state is None and restored.last_token_id == first[-1]
+    resumed = b.decode_greedy(b.get_recurrent_state(), prov, 6, metrics=None)
+    assert resumed == direct
+    assert first + direct == oracle.greedy(list(b"snap"), 11)[0]
