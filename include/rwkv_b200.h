@@ -20,6 +20,7 @@
  *    uploaded to device memory unchanged:
  *      SG8\x01 : u32 group | f32[groups][2] (min,max) | u8[numel]      (pack_codec.py:13-68)
  *      TR2\x03..\x07 : u32 group | records[groups] | 2-bit codes       (trinity_codec.py:52-58)
+ *      TR2\x01 : f32 codebook[4] | 2-bit codes (one codebook per tensor)  (trinity_codec.py:612-625)
  *    The fast GEMV paths need the code payload 16-byte aligned; other
  *    placements use the general (slower) path with identical results.
  *  - All arithmetic is fp32.  Dequantised weights are bit-identical to the
@@ -54,6 +55,10 @@ extern "C" {
 #define RWKVB_KIND_LUT2_RES 5u     /* TR2\x05: fp16 centroids + 2 residuals, 16-byte records */
 #define RWKVB_KIND_LUT2_IN_F16 6u  /* TR2\x06: as \x04, tensor stored input-major */
 #define RWKVB_KIND_LUT2_IN_RES 7u  /* TR2\x07: as \x05, tensor stored input-major */
+/* TR2\x01, the legacy per-tensor LUT2 (trinity_codec.py:51, :612-625): one fp32
+ * codebook of 4 values at byte 4, then the 2-bit codes of the flattened tensor
+ * (LSB first) at byte 20.  Its fourth magic byte equals SG8's, hence its own id. */
+#define RWKVB_KIND_LUT2_TENSOR 33u
 
 /* One packed matrix of checkpoint shape [rows, cols] resident in device memory. */
 typedef struct rwkvb_packed {
@@ -65,6 +70,7 @@ typedef struct rwkvb_packed {
   int32_t cols;
 } rwkvb_packed;
 
+/* Bytes of one per-group record (the codebook for RWKVB_KIND_LUT2_TENSOR). */
 static inline uint32_t rwkvb_lut2_record_bytes(uint32_t kind) {
   return (kind == RWKVB_KIND_LUT2_F16 || kind == RWKVB_KIND_LUT2_IN_F16) ? 8u : 16u;
 }
@@ -90,8 +96,39 @@ int rwkvb_dequant_f32(float* out, const rwkvb_packed* w, void* stream);
 
 /* y[rows] = W @ x[cols].  SG8 replaces scale_u8_grouped_gemv_f32_export
  * (lut2_gather.c:491-496); LUT2 kinds replace trinity_grouped_lut2_gemv_f32_export
- * (lut2_gather.c:328-333); the dispatch mirrors lut2_gemv (lut_gemm_fused.py:1095-1192). */
+ * (lut2_gather.c:328-333); the per-tensor LUT2 replaces lut2_gemv_f32_export
+ * (lut2_gather.c:179-211, :253-262), including its row walk (row r reads the
+ * codes from byte (r*cols)/4 on, low bits first, which differs from the
+ * flattened order when cols % 4 != 0); the dispatch mirrors lut2_gemv
+ * (lut_gemm_fused.py:1095-1192). */
 int rwkvb_gemv_f32(float* y, const rwkvb_packed* w, const float* x, void* stream);
+
+/* n_mats (1..4) GEMVs with distinct inputs in one launch: y_out[m][rows] =
+ * W_m @ x_m, every W_m of one shape [rows, cols] and any supported kind
+ * (HOST arrays of descriptors / device input pointers).  Replaces the four-
+ * and three-map batches scale_u8_grouped_tmix_gemv_f32_export (lut2_gather.c:
+ * 1427-1437) and lut2_tmix_gemv_f32_export / lut2_tmix_qkv_gemv_f32_export
+ * (lut2_gather.c:1517-1595, flattened code order), behind
+ * lut2_tmix_gemv_batched (lut_gemm_fused.py:1724-1769). */
+int rwkvb_tmix_gemv_f32(float* y_out, const rwkvb_packed* const* w, const float* const* x, int32_t n_mats,
+                        void* stream);
+
+/* Opt-in activation-INT8 SG8 GEMV: per input group of the weight's group size,
+ * x is quantised to int8 with scale max|x| / 127 (1 when max|x| <= 1e-12),
+ * rounding half away from zero, clamped to +-127; the exact fp32 sum of the
+ * group is kept for the minimum term:
+ *   y[row] = sum_g min_g * sum(x_g) + (max_g - min_g) / 255 * scale_g * sum(q * x_i8)
+ * with an exact integer dot.  Changes rounding against the float path, like
+ * the reference, which keeps it behind RWKV_LUT_ACTIVATION_INT8.  cols not a
+ * multiple of the group: the float GEMV (as the reference falls back).  The
+ * int8 activations live in a stream-ordered allocation made by the call.
+ * Replaces scale_u8_grouped_i8_gemv_f32_export (lut2_gather.c:612-796). */
+int rwkvb_gemv_sg8_i8_f32(float* y, const rwkvb_packed* w, const float* x, void* stream);
+
+/* The activation-INT8 form of rwkvb_tmix_qkv_gemv_f32 (three SG8 maps of one
+ * group size, each input quantised on its own).  Replaces
+ * scale_u8_grouped_tmix_qkv_i8_gemv_f32_export (lut2_gather.c:1451-1515). */
+int rwkvb_tmix_qkv_i8_gemv_f32(float* y_out, const rwkvb_packed* const* w3, const float* const* x3, void* stream);
 
 /* y[cols] = x[rows] @ W for a row-major SG8 W (compact TMix adapters).
  * Replaces scale_u8_grouped_transposed_gemv_f32_export (lut2_gather.c:939-944). */

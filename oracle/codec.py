@@ -217,19 +217,21 @@ def encode_lut2_grouped(
     """Restates ``encode_trinity_lut2`` for the k-means grouped kinds.
 
     ``kind`` ``TR2\\x04`` (``groupwise_kmeans_fp16``), ``TR2\\x06``
-    (``groupwise_input_fp16``: the 2-D tensor is transposed first) and
-    ``TR2\\x03`` (``groupwise_kmeans``, fp32 records); see
-    ``trinity_codec.py:494-623``.  The residual kinds 5 / 7 are decoded and
-    multiplied here but their encoder is not restated (their fixtures come
-    from the reference encoder).
+    (``groupwise_input_fp16``: the 2-D tensor is transposed first),
+    ``TR2\\x03`` (``groupwise_kmeans``, fp32 records) and the residual kinds
+    ``TR2\\x05`` / ``TR2\\x07`` (``groupwise_kmeans_residual`` /
+    ``groupwise_input_residual``: 16-byte records of the fp16 codebook, the
+    two in-group positions of largest |residual| and their fp16 residuals,
+    ``_residual_metadata``, ``trinity_codec.py:162-217``); see
+    ``trinity_codec.py:494-623``.
     """
     t = np.asarray(tensor, dtype=np.float32)
-    if kind == LUT2_INPUT_FP16 and t.ndim == 2:
+    if kind in (LUT2_INPUT_FP16, LUT2_INPUT_RESIDUAL) and t.ndim == 2:
         flat = np.ascontiguousarray(t.T).reshape(-1)
-    elif kind in (LUT2_GROUPED_FP16, LUT2_GROUPED, LUT2_INPUT_FP16):
+    elif kind in LUT2_GROUPED_KINDS:
         flat = t.reshape(-1)
     else:
-        raise ValueError(f"encoder not restated for kind {kind!r}")
+        raise ValueError(f"not a grouped LUT2 kind: {kind!r}")
     cb = kmeans_codebooks(flat, group_size)
     if kind != LUT2_GROUPED:
         cb = cb.astype(np.float16).astype(np.float32)
@@ -237,7 +239,37 @@ def encode_lut2_grouped(
     head = kind + struct.pack("<I", group_size)
     if kind == LUT2_GROUPED:
         return head + cb.astype(np.float32).tobytes() + pack_2bit(idx)
+    if kind in (LUT2_GROUPED_RESIDUAL, LUT2_INPUT_RESIDUAL):
+        return head + _residual_records(flat, cb.astype(np.float16), idx, group_size) + pack_2bit(idx)
     return head + cb.astype(np.float16).tobytes() + pack_2bit(idx)
+
+
+def _residual_records(flat: np.ndarray, cb16: np.ndarray, idx: np.ndarray, g: int) -> bytes:
+    """16-byte residual records: fp16 codebook[4], u8 positions[2] of the two
+    largest |value - codebook value| in the group, their fp16 residuals, two
+    reserved bytes."""
+    groups = cb16.shape[0]
+    rec = np.zeros(groups, dtype=np.dtype([("cb", "<f2", (4,)), ("pos", "u1", (2,)), ("dlt", "<f2", (2,)),
+                                           ("pad", "u1", (2,))]))
+    rec["cb"] = cb16
+    padded = np.zeros(groups * g, dtype=np.float32)
+    gid = np.arange(flat.size) // g
+    padded[:flat.size] = flat - cb16.astype(np.float32)[gid, idx]
+    res = padded.reshape(groups, g)
+    pos = np.argpartition(np.abs(res), -2, axis=1)[:, -2:] if g > 1 else np.zeros((groups, 2), np.intp)
+    rec["pos"] = pos.astype(np.uint8)
+    rec["dlt"] = np.take_along_axis(res, pos, axis=1).astype(np.float16)
+    return rec.tobytes()
+
+
+def encode_lut2_tensor(tensor: np.ndarray, iters: int = 12) -> bytes:
+    """A per-tensor LUT2 blob (``TR2\\x01``): one fp32 codebook of four k-means
+    centroids for the whole tensor and its flattened 2-bit codes
+    (``trinity_codec.py:612-625``)."""
+    flat = np.asarray(tensor, dtype=np.float32).reshape(-1)
+    cb = kmeans_codebooks(flat, flat.size, iters)
+    idx = lut2_assign(flat, cb, flat.size)
+    return b"TR2\x01" + cb.reshape(-1).astype(np.float32).tobytes() + pack_2bit(idx)
 
 
 def lut2_record_bytes(kind: bytes) -> int:
@@ -290,3 +322,14 @@ def decode_lut2_grouped(blob: bytes | memoryview, shape: tuple[int, ...]) -> np.
     if kind in (LUT2_INPUT_FP16, LUT2_INPUT_RESIDUAL) and len(shape) == 2:
         return np.ascontiguousarray(flat.reshape(shape[1], shape[0]).T)
     return flat.reshape(shape)
+
+
+def decode_lut2_tensor(blob: bytes | memoryview, numel: int) -> np.ndarray:
+    """Restates the per-tensor LUT2 (``TR2\\x01``) decode: ``lut2_gather_packed``
+    (``lut2_gather.c:81-105``) over the flattened codes after the fp32
+    codebook (``trinity_codec.py:306-323``)."""
+    buf = bytes(blob)
+    if buf[:4] != b"TR2\x01" or len(buf) < 20 + (numel + 3) // 4:
+        raise ValueError("not a per-tensor LUT2 blob")
+    cb = np.frombuffer(buf, dtype=np.float32, offset=4, count=4)
+    return cb[unpack_2bit(memoryview(buf)[20:], numel)].astype(np.float32)

@@ -191,3 +191,89 @@ int oracle_sg8_cmix(float* y, const uint8_t* key_blob, const uint8_t* value_blob
     free(h);
     return rc;
 }
+
+/* Per-tensor LUT2 (TR2\x01: magic, fp32 codebook[4], 2-bit codes LSB first):
+   y = W @ x with the row walk of lut2_gemv_f32 (lut2_gather.c:179-211) -- row r
+   reads its codes from byte (r * in) / 4 on, four per byte; per byte the four
+   products are summed, then added to the row total. */
+int oracle_lut2_tensor_gemv(float* y, const uint8_t* blob, const float* x, int out_f, int in_f) {
+    if (out_f <= 0 || in_f <= 0 || memcmp(blob, "TR2\x01", 4) != 0) return 1;
+    float cb[4];
+    for (int k = 0; k < 4; ++k) cb[k] = rd_f32(blob + 4 + 4 * k);
+    const uint8_t* packed = blob + 20;
+#pragma omp parallel for schedule(static)
+    for (int row = 0; row < out_f; ++row) {
+        const uint8_t* prow = packed + (((size_t)row * (size_t)in_f) >> 2);
+        float acc = 0.0f;
+        int col = 0;
+        for (; col + 4 <= in_f; col += 4) {
+            const uint8_t b = *prow++;
+            acc += cb[b & 3u] * x[col] + cb[(b >> 2) & 3u] * x[col + 1] + cb[(b >> 4) & 3u] * x[col + 2] +
+                   cb[(b >> 6) & 3u] * x[col + 3];
+        }
+        if (col < in_f) {
+            const uint8_t b = *prow;
+            for (int shift = 0; col < in_f; ++col, shift += 2) acc += cb[(b >> shift) & 3u] * x[col];
+        }
+        y[row] = acc;
+    }
+    return 0;
+}
+
+/* Activation-INT8 SG8 GEMV (lut2_gather.c:612-796): per input group, scale =
+   max|x| / 127 (1 when max|x| <= 1e-12), q = x * (1 / scale) rounded half away
+   from zero, clamped to +-127, sum(x) in column order; per row and group
+   min * sum(x) + (max - min) / 255 * scale * sum(q_w * q_x) with an exact
+   integer dot.  A row width that is not a multiple of the group falls back
+   to the float GEMV, as the reference does. */
+int oracle_sg8_i8_gemv(float* y, const uint8_t* blob, const float* x, int out_f, int in_f) {
+    if (memcmp(blob, "SG8\x01", 4) != 0 || out_f <= 0 || in_f <= 0) return 1;
+    const uint32_t g = rd_u32(blob + 4);
+    if (g == 0u || (in_f % (int)g) != 0) return oracle_sg8_gemv(y, blob, x, out_f, in_f);
+    const int groups = in_f / (int)g;
+    int8_t* q = (int8_t*)malloc((size_t)in_f);
+    float* scale = (float*)malloc((size_t)groups * sizeof(float));
+    float* sum_x = (float*)malloc((size_t)groups * sizeof(float));
+    if (!q || !scale || !sum_x) { free(q); free(scale); free(sum_x); return 2; }
+    for (int gi = 0; gi < groups; ++gi) {
+        const int b0 = gi * (int)g, b1 = b0 + (int)g;
+        float m = 0.0f, s = 0.0f;
+        for (int c = b0; c < b1; ++c) {
+            const float a = x[c] < 0.0f ? -x[c] : x[c];
+            if (a > m) m = a;
+            s += x[c];
+        }
+        const float sc = m > 1.0e-12f ? m / 127.0f : 1.0f;
+        const float inv = 1.0f / sc;
+        scale[gi] = sc;
+        sum_x[gi] = s;
+        for (int c = b0; c < b1; ++c) {
+            const float v = x[c] * inv;
+            int qi = v >= 0.0f ? (int)(v + 0.5f) : (int)(v - 0.5f);
+            qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+            q[c] = (int8_t)qi;
+        }
+    }
+    const size_t n = (size_t)out_f * (size_t)in_f;
+    const size_t ngroups = (n + g - 1u) / g;
+    const uint8_t* scales = blob + 8;
+    const uint8_t* quant = scales + ngroups * 8u;
+#pragma omp parallel for schedule(static)
+    for (int row = 0; row < out_f; ++row) {
+        const size_t rg = (size_t)row * (size_t)groups;
+        float acc = 0.0f;
+        for (int gi = 0; gi < groups; ++gi) {
+            const uint8_t* wq = quant + (rg + (size_t)gi) * g;
+            int32_t dot = 0;
+            for (uint32_t c = 0; c < g; ++c) dot += (int32_t)wq[c] * (int32_t)q[(size_t)gi * g + c];
+            const float mn = rd_f32(scales + (rg + (size_t)gi) * 8u);
+            const float mx = rd_f32(scales + (rg + (size_t)gi) * 8u + 4u);
+            acc += mn * sum_x[gi] + (mx - mn) * (1.0f / 255.0f) * scale[gi] * (float)dot;
+        }
+        y[row] = acc;
+    }
+    free(q);
+    free(scale);
+    free(sum_x);
+    return 0;
+}

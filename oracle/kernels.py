@@ -134,6 +134,8 @@ def packed_gemv(blob, x, out_f: int, in_f: int, impl: str = "oracle") -> np.ndar
         return sg8_gemv(blob, x, out_f, in_f, impl)
     if magic[:3] == b"TR2" and magic[3] in (3, 4, 5, 6, 7):
         return lut2_gemv(blob, x, out_f, in_f, impl)
+    if magic == b"TR2\x01":
+        return lut2_tensor_gemv(blob, x, out_f, in_f, impl)
     raise ValueError(f"unsupported packed blob magic {magic!r}")
 
 
@@ -188,4 +190,27 @@ def sg8_tmix_qkv(blobs, xs, out_f: int, in_f: int, impl: str = "oracle") -> np.n
         lib().oracle_sg8_tmix_qkv(_fp(y), bp, xp, int(out_f), int(in_f), 3)
     else:
         lib(impl).scale_u8_grouped_tmix_qkv_gemv_f32_export(_fp(y), bp, xp, int(out_f), int(in_f))
+    return y
+
+
+def lut2_tensor_gemv(blob, x, out_f: int, in_f: int, impl: str = "oracle") -> np.ndarray:
+    """``y = W @ x`` for a per-tensor LUT2 blob (``TR2\\x01``), the row walk of
+    ``lut2_gemv_f32`` (K3)."""
+    b, xv = _blob(blob), _f32(x)
+    y = np.empty(out_f, dtype=np.float32)
+    if impl == "oracle":
+        lib().oracle_lut2_tensor_gemv(_fp(y), _bp(b), _fp(xv), int(out_f), int(in_f))
+    else:
+        cb = np.frombuffer(b.tobytes(), dtype=np.float32, offset=4, count=4).copy()
+        pk = np.ascontiguousarray(b[20:])
+        lib(impl).lut2_gemv_f32_export(_fp(y), _fp(cb), _bp(pk), _fp(xv), int(out_f), int(in_f))
+    return y
+
+
+def sg8_i8_gemv(blob, x, out_f: int, in_f: int, impl: str = "oracle") -> np.ndarray:
+    """Activation-INT8 SG8 GEMV (K7)."""
+    b, xv = _blob(blob), _f32(x)
+    y = np.empty(out_f, dtype=np.float32)
+    fn = lib().oracle_sg8_i8_gemv if impl == "oracle" else lib(impl).scale_u8_grouped_i8_gemv_f32_export
+    fn(_fp(y), _bp(b), _fp(xv), int(out_f), int(in_f))
     return y

@@ -25,7 +25,8 @@ struct PackedView {
 
 __host__ inline PackedView make_view(const rwkvb_packed& p) {
   PackedView v;
-  v.meta = p.data + 8;
+  // the per-tensor LUT2's codebook (its one "group record") starts at byte 4
+  v.meta = p.data + (p.kind == RWKVB_KIND_LUT2_TENSOR ? 4 : 8);
   v.kind = p.kind;
   v.group = p.group_size;
   uint64_t numel = (uint64_t)p.rows * (uint64_t)p.cols;
@@ -122,7 +123,7 @@ __device__ __forceinline__ float lut2_elem(const PackedView& w, uint64_t e) {
   uint32_t code = (__ldg(w.payload + (e >> 2)) >> ((e & 3u) * 2u)) & 3u;
   const uint8_t* r = w.meta + g * w.rec;
   float v;
-  if (w.kind == RWKVB_KIND_LUT2_F32) {
+  if (w.kind == RWKVB_KIND_LUT2_F32 || w.kind == RWKVB_KIND_LUT2_TENSOR) {
     v = __ldg(reinterpret_cast<const float*>(r) + code);
   } else {
     v = half_bits_to_f(__ldg(reinterpret_cast<const unsigned short*>(r) + code));

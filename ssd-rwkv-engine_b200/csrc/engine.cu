@@ -673,7 +673,7 @@ LayerDev make_layer(const rwkvb_layer_desc& s) {
 
 bool desc_ok(const rwkvb_packed& p, int rows, int cols) {
   return p.data && p.rows == rows && p.cols == cols && p.group_size > 0 &&
-         (p.kind == RWKVB_KIND_SG8 || (p.kind >= 3 && p.kind <= 7));
+         (p.kind == RWKVB_KIND_SG8 || (p.kind >= 3 && p.kind <= 7) || p.kind == RWKVB_KIND_LUT2_TENSOR);
 }
 
 void pf_add(Prefetch& pf, const rwkvb_packed& p) {

@@ -34,11 +34,11 @@ __global__ void dequant_kernel(PackedView w, float* out, uint64_t numel) {
 // y[row] = W[row, :] @ x for rows [blockIdx.x * rpc, ...).  blockIdx.y selects
 // one of up to 3 (W, x, y) triples (batched QKV).
 struct GemvArgs {
-  PackedView w[3];
-  const float* x[3];
-  float* y[3];
-  int mode[3];
-  int lg[3];
+  PackedView w[4];
+  const float* x[4];
+  float* y[4];
+  int mode[4];
+  int lg[4];
   int rpc;   // rows per CTA
   int epi;   // 0 store, 1 relu^2
 };
@@ -99,6 +99,100 @@ int launch_gemv(const PackedView* w, const float* const* x, float* const* y, int
   dim3 grid((max_rows + rpc - 1) / rpc, n);
   gemv_kernel<<<grid, 256, sm, s>>>(a);
   return cuda_status(cudaGetLastError());
+}
+
+// ------------------------------------------- per-tensor LUT2 (TR2\x01) W @ x
+// One warp per row, the reference's row walk (lut2_gather.c:186-210): row r
+// reads its codes from byte (r * cols) / 4 on, four per byte, low bits first.
+__global__ void __launch_bounds__(256) lut2_tensor_gemv_kernel(PackedView w, const float* x, float* y) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= w.rows) return;
+  const int K = w.cols;
+  const float* cb = reinterpret_cast<const float*>(w.meta);
+  const float c0 = __ldg(cb), c1 = __ldg(cb + 1), c2 = __ldg(cb + 2), c3 = __ldg(cb + 3);
+  const uint8_t* prow = w.payload + (((uint64_t)row * (uint64_t)K) >> 2);
+  float acc = 0.f;
+  for (int j = lane; 4 * j < K; j += 32) {
+    const uint32_t b = __ldg(prow + j);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int col = 4 * j + u;
+      if (col < K) {
+        const uint32_t code = (b >> (2 * u)) & 3u;
+        const float v = code == 0 ? c0 : (code == 1 ? c1 : (code == 2 ? c2 : c3));
+        acc = fmaf(v, __ldg(x + col), acc);
+      }
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) y[row] = acc;
+}
+
+// ------------------------------------------------- activation-INT8 SG8 GEMV
+// Per input group (one warp each): int8 codes q, scale and the fp32 group sum,
+// following the reference's quantiser (lut2_gather.c:636-689): scale =
+// max|x| / 127 (1 when max|x| <= 1e-12), q = x * (1 / scale) rounded half away
+// from zero by truncating +-0.5, clamped to +-127; the sum in column order.
+__global__ void i8_quant_kernel(const float* __restrict__ x, int g, int groups, int8_t* __restrict__ q,
+                                float* __restrict__ scale, float* __restrict__ sum_x) {
+  const int grp = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (grp >= groups) return;
+  const float* xg = x + (size_t)grp * g;
+  float m = 0.f;
+  for (int i = lane; i < g; i += 32) m = fmaxf(m, fabsf(__ldg(xg + i)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float sc = m > 1.0e-12f ? __fdiv_rn(m, 127.0f) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, sc);
+  for (int i = lane; i < g; i += 32) {
+    const float v = __fmul_rn(__ldg(xg + i), inv);
+    int qi = v >= 0.f ? __float2int_rz(__fadd_rn(v, 0.5f)) : __float2int_rz(__fsub_rn(v, 0.5f));
+    qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+    q[(size_t)grp * g + i] = (int8_t)qi;
+  }
+  if (lane == 0) {
+    float sx = 0.f;
+    for (int i = 0; i < g; ++i) sx = __fadd_rn(sx, __ldg(xg + i));
+    scale[grp] = sc;
+    sum_x[grp] = sx;
+  }
+}
+
+__device__ __forceinline__ int dp4a_u8s8(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+struct I8Args {
+  PackedView w[3];
+  const int8_t* q[3];
+  const float* scale[3];
+  const float* sum_x[3];
+  float* y[3];
+};
+
+// One warp per row (blockIdx.y selects the map): lane l takes groups l, l + 32,
+// ...; per group the exact integer dot of the u8 codes and int8 activations,
+// then min * sum(x) + (max - min) / 255 * scale * dot.
+__global__ void __launch_bounds__(256) i8_gemv_kernel(I8Args a, int g) {
+  const int m = blockIdx.y;
+  const PackedView& w = a.w[m];
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= w.rows) return;
+  const int K = w.cols, groups = K / g;
+  const size_t rg = (size_t)row * (size_t)groups;  // first weight group of the row
+  float acc = 0.f;
+  for (int gi = lane; gi < groups; gi += 32) {
+    const uint32_t* wq = reinterpret_cast<const uint32_t*>(w.payload + (rg + gi) * (size_t)g);
+    const uint32_t* xq = reinterpret_cast<const uint32_t*>(a.q[m] + (size_t)gi * g);
+    int dot = 0;
+    for (int i = 0; i < (g >> 2); ++i) dot = dp4a_u8s8(__ldg(wq + i), __ldg(xq + i), dot);
+    const float2 p = ldg_f2(w.meta + (rg + gi) * 8);
+    acc += p.x * __ldg(a.sum_x[m] + gi) + (p.y - p.x) * kInv255 * __ldg(a.scale[m] + gi) * (float)dot;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) a.y[m][row] = acc;
 }
 
 // ----------------------------------------------------- transposed (x @ W)
@@ -181,9 +275,10 @@ extern "C" int rwkvb_packed_init(rwkvb_packed* out, const uint8_t* header, uint6
   if (!out || !header || rows <= 0 || cols <= 0 || blob_bytes < 8) return RWKVB_EARG;
   uint32_t group;
   memcpy(&group, header + 4, 4);
-  if (group == 0) return RWKVB_EARG;
+  const bool per_tensor = header[0] == 'T' && header[1] == 'R' && header[2] == '2' && header[3] == 1;
+  if (group == 0 && !per_tensor) return RWKVB_EARG;
   uint64_t numel = (uint64_t)rows * (uint64_t)cols;
-  uint64_t groups = (numel + group - 1) / group;
+  uint64_t groups = per_tensor ? 1 : (numel + group - 1) / group;
   uint32_t kind;
   if (header[0] == 'S' && header[1] == 'G' && header[2] == '8' && header[3] == 1) {
     kind = RWKVB_KIND_SG8;
@@ -191,6 +286,13 @@ extern "C" int rwkvb_packed_init(rwkvb_packed* out, const uint8_t* header, uint6
   } else if (header[0] == 'T' && header[1] == 'R' && header[2] == '2' && header[3] >= 3 && header[3] <= 7) {
     kind = header[3];
     if (blob_bytes < 8 + groups * rwkvb_lut2_record_bytes(kind) + (numel + 3) / 4) return RWKVB_EARG;
+  } else if (header[0] == 'T' && header[1] == 'R' && header[2] == '2' && header[3] == 1) {
+    // per-tensor LUT2: the whole tensor is the one "group" of its codebook
+    // (bytes 4..8 are codebook[0], not a group size); _lut2_inner_view checks
+    // the 20-byte header (trinity_codec.py:306-323)
+    kind = RWKVB_KIND_LUT2_TENSOR;
+    if (numel > 0xffffffffull || blob_bytes < 20 + (numel + 3) / 4) return RWKVB_EARG;
+    group = (uint32_t)numel;
   } else {
     return RWKVB_EARG;
   }
@@ -205,7 +307,7 @@ extern "C" int rwkvb_packed_init(rwkvb_packed* out, const uint8_t* header, uint6
 
 static bool packed_ok(const rwkvb_packed* w) {
   return w && w->data && w->rows > 0 && w->cols > 0 && w->group_size > 0 &&
-         (w->kind == RWKVB_KIND_SG8 || (w->kind >= 3 && w->kind <= 7));
+         (w->kind == RWKVB_KIND_SG8 || (w->kind >= 3 && w->kind <= 7) || w->kind == RWKVB_KIND_LUT2_TENSOR);
 }
 
 extern "C" int rwkvb_dequant_f32(float* out, const rwkvb_packed* w, void* stream) {
@@ -221,7 +323,84 @@ extern "C" int rwkvb_dequant_f32(float* out, const rwkvb_packed* w, void* stream
 extern "C" int rwkvb_gemv_f32(float* y, const rwkvb_packed* w, const float* x, void* stream) {
   if (!y || !x || !packed_ok(w)) return RWKVB_EARG;
   PackedView v = make_view(*w);
+  if (v.kind == RWKVB_KIND_LUT2_TENSOR) {
+    lut2_tensor_gemv_kernel<<<(v.rows + 7) / 8, 256, 0, (cudaStream_t)stream>>>(v, x, y);
+    return cuda_status(cudaGetLastError());
+  }
   return launch_gemv(&v, &x, &y, 1, 0, (cudaStream_t)stream);
+}
+
+extern "C" int rwkvb_tmix_gemv_f32(float* y_out, const rwkvb_packed* const* w, const float* const* x, int32_t n,
+                                   void* stream) {
+  if (!y_out || !w || !x || n < 1 || n > 4) return RWKVB_EARG;
+  PackedView v[4];
+  float* ys[4];
+  for (int m = 0; m < n; ++m) {
+    if (!packed_ok(w[m]) || !x[m]) return RWKVB_EARG;
+    if (w[m]->rows != w[0]->rows || w[m]->cols != w[0]->cols) return RWKVB_EARG;
+    v[m] = make_view(*w[m]);
+    ys[m] = y_out + (size_t)m * w[0]->rows;
+  }
+  return launch_gemv(v, x, ys, n, 0, (cudaStream_t)stream);
+}
+
+// Activation-INT8 SG8 maps (1 or 3): quantise every input, then the integer
+// GEMV; scratch [K] int8 + [2 * groups] fp32 per map, stream-ordered.
+static int i8_maps(const rwkvb_packed* const* w, const float* const* x, float* const* y, int n, cudaStream_t s) {
+  const int K = w[0]->cols, g = (int)w[0]->group_size, groups = K / g;
+  const size_t per = ((size_t)K + 255) / 256 * 256 + (size_t)groups * 8;
+  uint8_t* scratch = nullptr;
+  if (cudaMallocAsync((void**)&scratch, per * n, s) != cudaSuccess) {
+    cudaGetLastError();
+    return RWKVB_EALLOC;
+  }
+  I8Args a;
+  memset(&a, 0, sizeof(a));
+  int st = RWKVB_OK;
+  for (int m = 0; m < n && st == RWKVB_OK; ++m) {
+    uint8_t* base = scratch + per * m;
+    int8_t* q = reinterpret_cast<int8_t*>(base);
+    float* sc = reinterpret_cast<float*>(base + ((size_t)K + 255) / 256 * 256);
+    float* sx = sc + groups;
+    i8_quant_kernel<<<(groups + 7) / 8, 256, 0, s>>>(x[m], g, groups, q, sc, sx);
+    st = cuda_status(cudaGetLastError());
+    a.w[m] = make_view(*w[m]);
+    a.q[m] = q;
+    a.scale[m] = sc;
+    a.sum_x[m] = sx;
+    a.y[m] = y[m];
+  }
+  if (st == RWKVB_OK) {
+    i8_gemv_kernel<<<dim3((w[0]->rows + 7) / 8, n), 256, 0, s>>>(a, g);
+    st = cuda_status(cudaGetLastError());
+  }
+  cudaFreeAsync(scratch, s);
+  return st;
+}
+
+static bool i8_ok(const rwkvb_packed* w) {
+  return packed_ok(w) && w->kind == RWKVB_KIND_SG8 && w->cols % (int)w->group_size == 0 && w->group_size % 4 == 0;
+}
+
+extern "C" int rwkvb_gemv_sg8_i8_f32(float* y, const rwkvb_packed* w, const float* x, void* stream) {
+  if (!y || !x || !packed_ok(w) || w->kind != RWKVB_KIND_SG8) return RWKVB_EARG;
+  if (!i8_ok(w) || ((uintptr_t)make_view(*w).payload & 3u)) return rwkvb_gemv_f32(y, w, x, stream);  // float path
+  return i8_maps(&w, &x, &y, 1, (cudaStream_t)stream);
+}
+
+extern "C" int rwkvb_tmix_qkv_i8_gemv_f32(float* y_out, const rwkvb_packed* const* w3, const float* const* x3,
+                                          void* stream) {
+  if (!y_out || !w3 || !x3) return RWKVB_EARG;
+  bool fast = true;
+  for (int m = 0; m < 3; ++m) {
+    if (!packed_ok(w3[m]) || !x3[m] || w3[m]->kind != RWKVB_KIND_SG8) return RWKVB_EARG;
+    if (w3[m]->rows != w3[0]->rows || w3[m]->cols != w3[0]->cols) return RWKVB_EARG;
+    fast = fast && i8_ok(w3[m]) && w3[m]->group_size == w3[0]->group_size &&
+           !((uintptr_t)make_view(*w3[m]).payload & 3u);
+  }
+  if (!fast) return rwkvb_tmix_qkv_gemv_f32(y_out, w3, x3, stream);  // the reference's float fallback
+  float* ys[3] = {y_out, y_out + w3[0]->rows, y_out + 2 * (size_t)w3[0]->rows};
+  return i8_maps(w3, x3, ys, 3, (cudaStream_t)stream);
 }
 
 extern "C" int rwkvb_tmix_qkv_gemv_f32(float* y_out, const rwkvb_packed* const* w3, const float* const* x3,

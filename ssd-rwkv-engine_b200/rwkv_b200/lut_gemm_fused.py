@@ -7,8 +7,12 @@ the sm_100a library through its C ABI on CUDA tensors:
 =====================================  ===========================================  =========================
 function                               reference                                    C ABI
 =====================================  ===========================================  =========================
-``lut2_gemv``                          ``lut_gemm_fused.py:1095-1192``              ``rwkvb_gemv_f32``
-``lut2_tmix_qkv_gemv_batched``         ``lut_gemm_fused.py:1771-1817``              ``rwkvb_tmix_qkv_gemv_f32``
+``lut2_gemv``                          ``lut_gemm_fused.py:1095-1192``              ``rwkvb_gemv_f32``,
+                                                                                    ``rwkvb_gemv_sg8_i8_f32``
+``lut2_tmix_gemv_batched``             ``lut_gemm_fused.py:1724-1769``              ``rwkvb_tmix_gemv_f32``
+``lut2_tmix_qkv_gemv_batched``         ``lut_gemm_fused.py:1771-1817``              ``rwkvb_tmix_qkv_gemv_f32``,
+                                                                                    ``rwkvb_tmix_qkv_i8_gemv_f32``
+``lut2_layer_gather``                  ``lut2_gather.c:135-171``                    ``rwkvb_dequant_f32``
 ``grouped_u8_transposed_gemv``         ``lut_gemm_fused.py:1195-1233``              ``rwkvb_transposed_gemv_f32``
 ``grouped_u8_transposed_tmix_fused``   ``lut_gemm_fused.py:704-724``                ``rwkvb_tmix_adapters_f32``
 ``grouped_u8_cmix_gemv``               ``lut_gemm_fused.py:1431-1495``              ``rwkvb_cmix_gemv_f32``
@@ -26,6 +30,7 @@ dtype/device; callers here live on the GPU).  There is no CPU fallback.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -68,19 +73,55 @@ def _magic(blob) -> bytes:
     return bytes(blob[:4])
 
 
+def activation_int8_enabled(*, head: bool = False) -> bool:
+    """Whether the opt-in activation-INT8 SG8 GEMV is on: the reference's
+    switches ``RWKV_LUT_ACTIVATION_INT8`` / ``..._HEAD`` (lut_gemm_fused.py:54-66)."""
+    name = "RWKV_LUT_ACTIVATION_INT8_HEAD" if head else "RWKV_LUT_ACTIVATION_INT8"
+    return os.environ.get(name, "0").strip().lower() in ("1", "true", "yes", "on")
+
+
 def lut2_gemv(weight_blob, x: torch.Tensor, *, out_features: int, in_features: int,
               activation_int8: bool | None = None) -> torch.Tensor:
-    """``y = W @ x`` for an SG8 or grouped-LUT2 ``W [out_features, in_features]``."""
-    if activation_int8:
-        raise NotImplementedError("the opt-in INT8 activation GEMV is not provided by this backend")
+    """``y = W @ x`` for an SG8, grouped-LUT2 or per-tensor LUT2 (``TR2\\x01``)
+    ``W [out_features, in_features]``; SG8 with ``activation_int8`` (default:
+    ``activation_int8_enabled()``) quantises x per group to int8 first."""
+    if activation_int8 is None:
+        activation_int8 = activation_int8_enabled()
     keep: list = []
     w = _resident(weight_blob, out_features, in_features, keep)
     xv = _vec(x, in_features)
     y = torch.empty(out_features, dtype=torch.float32, device=_dev())
-    native.check(native.lib().rwkvb_gemv_f32(y.data_ptr(), ctypes.byref(w.desc), xv.data_ptr(), _stream()),
-                 "rwkvb_gemv_f32")
+    if activation_int8 and w.codec == "sg8":
+        native.check(native.lib().rwkvb_gemv_sg8_i8_f32(y.data_ptr(), ctypes.byref(w.desc), xv.data_ptr(),
+                                                        _stream()), "rwkvb_gemv_sg8_i8_f32")
+    else:
+        native.check(native.lib().rwkvb_gemv_f32(y.data_ptr(), ctypes.byref(w.desc), xv.data_ptr(), _stream()),
+                     "rwkvb_gemv_f32")
     torch.cuda.current_stream().synchronize() if keep else None
     return y
+
+
+def lut2_tmix_gemv_batched(blobs, xs, *, out_features: int, in_features: int):
+    """Four attention maps (r, k, v, o) with distinct inputs in one launch, any
+    packed kind (SG8, grouped or per-tensor LUT2)."""
+    if isinstance(xs, torch.Tensor):
+        xs = (xs, xs, xs, xs)
+    keep: list = []
+    ws = [_resident(b, out_features, in_features, keep) for b in blobs[:4]]
+    xv = [_vec(x, in_features) for x in xs]
+    y = torch.empty((4, out_features), dtype=torch.float32, device=_dev())
+    wp = (ctypes.POINTER(native.Packed) * 4)(*[ctypes.pointer(w.desc) for w in ws])
+    xp = (ctypes.c_void_p * 4)(*[x.data_ptr() for x in xv])
+    native.check(native.lib().rwkvb_tmix_gemv_f32(y.data_ptr(), wp, xp, 4, _stream()), "rwkvb_tmix_gemv_f32")
+    if keep:
+        torch.cuda.current_stream().synchronize()
+    return y[0], y[1], y[2], y[3]
+
+
+def lut2_layer_gather(blobs, shapes) -> list[torch.Tensor]:
+    """Decode several packed tensors (``lut2_layer_gather_export``,
+    lut2_gather.c:135-171): one bit-exact fp32 tensor per blob."""
+    return [decode_packed(b, int(s[0]), int(s[1])) for b, s in zip(blobs, shapes)]
 
 
 def lut2_linear_forward(weight_blob, x: torch.Tensor, shape: tuple[int, ...]) -> torch.Tensor:
@@ -121,13 +162,18 @@ def lut2_tmix_qkv_gemv_batched(blobs, xs, *, out_features: int, in_features: int
     keep: list = []
     ws = [_resident(b, out_features, in_features, keep) for b in blobs[:3]]
     xv = [_vec(x, in_features) for x in xs]
-    if not all(_magic(b) == SG8_MAGIC for b in blobs[:3]):
-        # grouped LUT2 attention maps: one GEMV each (lut_gemm_fused.py:1807-1817)
-        return tuple(lut2_gemv(w, x, out_features=out_features, in_features=in_features) for w, x in zip(ws, xv))
     y = torch.empty((3, out_features), dtype=torch.float32, device=_dev())
     wp = (ctypes.POINTER(native.Packed) * 3)(*[ctypes.pointer(w.desc) for w in ws])
     xp = (ctypes.c_void_p * 3)(*[x.data_ptr() for x in xv])
-    native.check(native.lib().rwkvb_tmix_qkv_gemv_f32(y.data_ptr(), wp, xp, _stream()), "rwkvb_tmix_qkv_gemv_f32")
+    if not all(_magic(b) == SG8_MAGIC for b in blobs[:3]):
+        # LUT2 attention maps (grouped or per-tensor): one batched launch
+        native.check(native.lib().rwkvb_tmix_gemv_f32(y.data_ptr(), wp, xp, 3, _stream()), "rwkvb_tmix_gemv_f32")
+    elif activation_int8_enabled():
+        native.check(native.lib().rwkvb_tmix_qkv_i8_gemv_f32(y.data_ptr(), wp, xp, _stream()),
+                     "rwkvb_tmix_qkv_i8_gemv_f32")
+    else:
+        native.check(native.lib().rwkvb_tmix_qkv_gemv_f32(y.data_ptr(), wp, xp, _stream()),
+                     "rwkvb_tmix_qkv_gemv_f32")
     if keep:
         torch.cuda.current_stream().synchronize()
     return y[0], y[1], y[2]

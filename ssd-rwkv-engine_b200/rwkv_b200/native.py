@@ -31,6 +31,7 @@ RWKVB_ESCRATCH = 6
 CMIX_NOALLOC_MAX_FFN = 16384
 
 KIND_SG8 = 1
+KIND_LUT2_TENSOR = 33  # TR2\x01 (per-tensor LUT2)
 LUT2_KINDS = (3, 4, 5, 6, 7)
 
 # Engine flags (rwkvb_engine_create)
@@ -120,6 +121,9 @@ def _declare(h: ctypes.CDLL) -> None:
         "rwkvb_gemv_f32": (ctypes.c_int, [vp, P(Packed), vp, vp]),
         "rwkvb_transposed_gemv_f32": (ctypes.c_int, [vp, P(Packed), vp, vp]),
         "rwkvb_tmix_qkv_gemv_f32": (ctypes.c_int, [vp, P(P(Packed)), P(vp), vp]),
+        "rwkvb_tmix_gemv_f32": (ctypes.c_int, [vp, P(P(Packed)), P(vp), i32, vp]),
+        "rwkvb_gemv_sg8_i8_f32": (ctypes.c_int, [vp, P(Packed), vp, vp]),
+        "rwkvb_tmix_qkv_i8_gemv_f32": (ctypes.c_int, [vp, P(P(Packed)), P(vp), vp]),
         "rwkvb_tmix_adapters_f32": (ctypes.c_int, [vp, vp, vp, vp, P(P(Packed)), P(vp), vp, ctypes.c_int, vp]),
         "rwkvb_cmix_gemv_f32": (ctypes.c_int, [vp, P(Packed), P(Packed), vp, vp]),
         "rwkvb_cmix_gemv_f32_noalloc": (ctypes.c_int, [vp, P(Packed), P(Packed), vp, vp]),

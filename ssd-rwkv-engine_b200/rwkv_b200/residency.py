@@ -45,6 +45,8 @@ def _blob_len(payload) -> int:
 
 def _meta_bytes(header: bytes, rows: int, cols: int) -> int:
     """Header + per-group records: the offset of the code payload in the blob."""
+    if header[:4] == b"TR2\x01":  # per-tensor LUT2: magic + fp32 codebook[4]
+        return 20
     (g,) = struct.unpack("<I", header[4:8])
     if g == 0:
         raise ValueError("packed blob with zero group size")

@@ -10,6 +10,8 @@ The reference package is copied to a temporary directory, its
 * ``codec_lut2.npz``   — ``encode_trinity_lut2`` blobs (kinds 3..7) + decoded values
 * ``gemv.npz``         — outputs of the reference C kernels (SG8 / LUT2 / transposed /
                          fused adapters / fused CMix / batched QKV)
+* ``gemv_extra.npz``   — legacy per-tensor LUT2 (``TR2\\x01``) decode / GEMV / batched maps,
+                         four-map SG8 batch, activation-INT8 SG8 GEMV and QKV maps
 * ``forward_tiny_sg8.npz`` / ``forward_tiny_lut2.npz`` — the reference packed RWKV-7 forward
   (``forward_block_packed`` + packed head + argmax) on the seeded 4-layer, d_model 256 model:
   8 prompt tokens then 16 greedy tokens; per-pass logits, ids and final recurrent state,
@@ -18,7 +20,7 @@ The reference package is copied to a temporary directory, its
 The committed ``.npz`` files are what the tests read; nothing at test time
 touches the reference tree.  Re-run with::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [codec] [gemv] [extra] [forward]   # default: all
 """
 
 from __future__ import annotations
@@ -204,6 +206,80 @@ def gemv_fixtures() -> None:
     np.savez_compressed(HERE / "gemv.npz", **out)
 
 
+def extra_fixtures() -> None:
+    """``gemv_extra.npz``: legacy per-tensor LUT2 ``TR2\\x01`` (decode K1, W @ x
+    K3, four- and three-map batches K15), the four-map SG8 batch (K13) and the
+    activation-INT8 SG8 kernels (K7, K14), all from the reference's own
+    encoders and C kernels."""
+    os.environ["RWKV_LUT_KERNEL"] = "c"
+    from rwkv_ssd.runtime import lut_gemm_fused as lg
+    from rwkv_ssd.runtime.pack_codec import encode_scale_u8_grouped
+    from rwkv_ssd.runtime.trinity_codec import decode_trinity_lut2_to_tensor, encode_trinity_lut2
+
+    gen = torch.Generator().manual_seed(SEED + 2)
+    out: dict[str, np.ndarray] = {}
+
+    def rnd(*s, scale=0.02):
+        return torch.randn(s, generator=gen) * scale
+
+    # TR2\x01: one fp32 codebook per tensor; "odd" has rows that do not start on
+    # a code byte (the K3 row walk reads them from the row's first whole byte)
+    for tag, (o, i), algo in (("sq", (64, 256), "kmeans"), ("lin", (48, 128), "linspace"),
+                              ("odd", (9, 13), "kmeans")):
+        w, x = rnd(o, i), rnd(i, scale=1.0)
+        blob = encode_trinity_lut2(w, codebook=algo)
+        assert bytes(blob[:4]) == b"TR2\x01"
+        dec = decode_trinity_lut2_to_tensor(blob, _entry(tag, (o, i), len(blob), "trinity_lut2"),
+                                            torch.device("cpu"))
+        y = lg.lut2_gemv(blob, x, out_features=o, in_features=i)
+        key = f"tensor_{tag}"
+        out[f"{key}/blob"] = np.frombuffer(blob, np.uint8).copy()
+        out[f"{key}/x"] = x.numpy()
+        out[f"{key}/y"] = y.numpy()
+        out[f"{key}/decoded"] = dec.float().numpy()
+        out[f"{key}/shape"] = np.array([o, i])
+    C = 128
+    blobs = tuple(encode_trinity_lut2(rnd(C, C), codebook="kmeans") for _ in range(4))
+    xs = tuple(rnd(C, scale=1.0) for _ in range(4))
+    ys = lg.lut2_tmix_gemv_batched(blobs, xs, out_features=C, in_features=C)
+    ys3 = lg.lut2_tmix_qkv_gemv_batched(blobs[:3], xs[:3], out_features=C, in_features=C)
+    for j in range(4):
+        out[f"tensor_maps/blob{j}"] = np.frombuffer(blobs[j], np.uint8).copy()
+        out[f"tensor_maps/x{j}"] = xs[j].numpy()
+    out["tensor_maps/y4"] = torch.stack(list(ys)).numpy()
+    out["tensor_maps/y3"] = torch.stack(list(ys3)).numpy()
+    # SG8 four maps (K13)
+    blobs = tuple(encode_scale_u8_grouped(rnd(C, 2 * C), group_size=128) for _ in range(4))
+    xs = tuple(rnd(2 * C, scale=1.0) for _ in range(4))
+    ys = lg.lut2_tmix_gemv_batched(blobs, xs, out_features=C, in_features=2 * C)
+    for j in range(4):
+        out[f"sg8_maps/blob{j}"] = np.frombuffer(blobs[j], np.uint8).copy()
+        out[f"sg8_maps/x{j}"] = xs[j].numpy()
+    out["sg8_maps/y4"] = torch.stack(list(ys)).numpy()
+    # activation INT8 (K7): one group of x all zero (scale 1 rule), one with a large outlier
+    for tag, (o, i), g in (("sq", (256, 256), 128), ("g64", (96, 192), 64)):
+        w, x = rnd(o, i), rnd(i, scale=1.0)
+        x[:g] = 0.0
+        x[g + 3] = 40.0
+        blob = encode_scale_u8_grouped(w, group_size=g)
+        y = lg.lut2_gemv(blob, x, out_features=o, in_features=i, activation_int8=True)
+        out[f"i8_{tag}/blob"] = np.frombuffer(blob, np.uint8).copy()
+        out[f"i8_{tag}/x"] = x.numpy()
+        out[f"i8_{tag}/y"] = y.numpy()
+        out[f"i8_{tag}/shape"] = np.array([o, i])
+    # activation INT8 three maps (K14)
+    os.environ["RWKV_LUT_ACTIVATION_INT8"] = "1"
+    blobs = tuple(encode_scale_u8_grouped(rnd(C, 2 * C), group_size=128) for _ in range(3))
+    xs = tuple(rnd(2 * C, scale=1.0) for _ in range(3))
+    ys = lg.lut2_tmix_qkv_gemv_batched(blobs, xs, out_features=C, in_features=2 * C)
+    os.environ["RWKV_LUT_ACTIVATION_INT8"] = "0"
+    for j in range(3):
+        out[f"i8_qkv/blob{j}"] = np.frombuffer(blobs[j], np.uint8).copy()
+        out[f"i8_qkv/x{j}"] = xs[j].numpy()
+    out["i8_qkv/y"] = torch.stack(list(ys)).numpy()
+    np.savez_compressed(HERE / "gemv_extra.npz", **out)
+
+
 class _StubProvider:
     """Duck-typed provider exposing the fused-blob protocol
     (``weight_provider.py:660-667``)."""
@@ -308,10 +384,16 @@ def main() -> None:
     torch.set_num_threads(1)
     tmp = _prepare_reference()
     try:
-        codec_fixtures()
-        gemv_fixtures()
-        forward_fixture("sg8")
-        forward_fixture("lut2")
+        which = set(sys.argv[1:]) or {"codec", "gemv", "extra", "forward"}
+        if "codec" in which:
+            codec_fixtures()
+        if "gemv" in which:
+            gemv_fixtures()
+        if "extra" in which:
+            extra_fixtures()
+        if "forward" in which:
+            forward_fixture("sg8")
+            forward_fixture("lut2")
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
     for p in sorted(HERE.glob("*.npz")):

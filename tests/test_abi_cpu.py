@@ -77,7 +77,13 @@ def test_packed_init_rejects_malformed_blobs_like_the_reference_decoder():
     assert _init(b"SG8\x02" + good[4:], n, rows, cols)[0] == native.RWKVB_EARG  # bad magic
     assert _init(b"SG8\x01" + struct.pack("<I", 0), n, rows, cols)[0] == native.RWKVB_EARG  # zero group
     assert _init(good, n, 0, cols)[0] == native.RWKVB_EARG
-    assert _init(b"TR2\x01" + good[4:], n, rows, cols)[0] == native.RWKVB_EARG  # per-tensor LUT2 not grouped
+    # per-tensor LUT2 (TR2\x01): magic + fp32 codebook[4] + codes; its own kind id
+    tensor = b"TR2\x01" + struct.pack("<f", 0.0)  # codebook[0] = 0.0 is not a zero group size
+    need = 20 + (rows * cols + 3) // 4
+    st, d = _init(tensor, need, rows, cols)
+    assert st == native.RWKVB_OK and d.kind == native.KIND_LUT2_TENSOR and d.group_size == rows * cols
+    assert _init(tensor, need - 1, rows, cols)[0] == native.RWKVB_EARG
+    assert _init(b"TR2\x02" + good[4:], need, rows, cols)[0] == native.RWKVB_EARG  # FLUTE rows: not a device kind
     short = 8 + (rows * cols // 64) * 8 + rows * cols // 4 - 1
     assert _init(b"TR2\x04" + struct.pack("<I", 64), short, rows, cols)[0] == native.RWKVB_EARG
 

@@ -245,3 +245,82 @@ def test_engine_0p1b_shape_matches_oracle_first_tokens(persistent):
             np.testing.assert_allclose(_np(st[j]).reshape(-1), state_ref[j].reshape(-1), rtol=0, atol=LOGIT_TOL)
     finally:
         eng.close()
+
+
+def test_per_tensor_lut2_int8_activation_and_four_maps_match_reference_kernels():
+    """``gemv_extra.npz`` (reference encoders and C kernels): per-tensor LUT2
+    decode bit-exact (K1), its row-walk GEMV (K3), the four/three-map batches
+    (K15, K13), the activation-INT8 SG8 GEMV (K7) and its QKV maps (K14)."""
+    E = load_golden("gemv_extra.npz")
+    for t in ("sq", "lin", "odd"):
+        o, i = (int(v) for v in E[f"tensor_{t}/shape"])
+        blob = E[f"tensor_{t}/blob"].tobytes()
+        got = _np(lg.decode_packed(blob, o, i)).reshape(-1)
+        assert np.array_equal(_bits(got), _bits(E[f"tensor_{t}/decoded"].reshape(-1))), t
+        y = lg.lut2_gemv(blob, torch.from_numpy(E[f"tensor_{t}/x"]), out_features=o, in_features=i)
+        np.testing.assert_allclose(_np(y), E[f"tensor_{t}/y"], **TOL, err_msg=t)
+    C = 128
+    blobs = [E[f"tensor_maps/blob{j}"].tobytes() for j in range(4)]
+    xs = [torch.from_numpy(E[f"tensor_maps/x{j}"]) for j in range(4)]
+    ys = lg.lut2_tmix_gemv_batched(blobs, xs, out_features=C, in_features=C)
+    np.testing.assert_allclose(np.stack([_np(y) for y in ys]), E["tensor_maps/y4"], **TOL)
+    ys = lg.lut2_tmix_qkv_gemv_batched(blobs[:3], xs[:3], out_features=C, in_features=C)
+    np.testing.assert_allclose(np.stack([_np(y) for y in ys]), E["tensor_maps/y3"], **TOL)
+    blobs = [E[f"sg8_maps/blob{j}"].tobytes() for j in range(4)]
+    xs = [torch.from_numpy(E[f"sg8_maps/x{j}"]) for j in range(4)]
+    ys = lg.lut2_tmix_gemv_batched(blobs, xs, out_features=C, in_features=2 * C)
+    np.testing.assert_allclose(np.stack([_np(y) for y in ys]), E["sg8_maps/y4"], **TOL)
+    for t in ("sq", "g64"):
+        o, i = (int(v) for v in E[f"i8_{t}/shape"])
+        y = lg.lut2_gemv(E[f"i8_{t}/blob"].tobytes(), torch.from_numpy(E[f"i8_{t}/x"]), out_features=o,
+                         in_features=i, activation_int8=True)
+        np.testing.assert_allclose(_np(y), E[f"i8_{t}/y"], **TOL, err_msg=t)
+    import os
+
+    os.environ["RWKV_LUT_ACTIVATION_INT8"] = "1"
+    try:
+        blobs = [E[f"i8_qkv/blob{j}"].tobytes() for j in range(3)]
+        xs = [torch.from_numpy(E[f"i8_qkv/x{j}"]) for j in range(3)]
+        ys = lg.lut2_tmix_qkv_gemv_batched(blobs, xs, out_features=C, in_features=2 * C)
+    finally:
+        os.environ["RWKV_LUT_ACTIVATION_INT8"] = "0"
+    np.testing.assert_allclose(np.stack([_np(y) for y in ys]), E["i8_qkv/y"], **TOL)
+
+
+def _kind_pack(kind: bytes, seed: int):
+    """The tiny model with its projections and head in one LUT2 wire kind
+    (``TR2\\x01`` per-tensor, or a grouped kind 3..7), adapters / embedding SG8."""
+    shape = synth.PRESETS["tiny"]
+    sd = synth.generate_state_dict(shape, seed, "cpu")
+    pack = {}
+    for name, t in sd.items():
+        arr = t.numpy()
+        codec = synth.codec_for(name, tuple(t.shape), "lut2")
+        if codec == "none":
+            pack[name] = synth.PackedTensor(name, tuple(t.shape), "none", arr.reshape(-1).copy())
+        elif codec == "sg8":
+            pack[name] = synth.PackedTensor(name, tuple(t.shape), "sg8", oc.encode_sg8(arr, 128))
+        else:
+            blob = oc.encode_lut2_tensor(arr) if kind == b"TR2\x01" else oc.encode_lut2_grouped(arr, 64, kind=kind)
+            pack[name] = synth.PackedTensor(name, tuple(t.shape), "lut2", blob)
+    return shape, pack
+
+
+@pytest.mark.parametrize("kind", [b"TR2\x01", oc.LUT2_GROUPED, oc.LUT2_GROUPED_RESIDUAL, oc.LUT2_INPUT_FP16,
+                                  oc.LUT2_INPUT_RESIDUAL])
+def test_engine_decodes_every_lut2_wire_kind_like_the_oracle(kind):
+    """The batch-1 engine on packs whose projections and head use each LUT2
+    wire kind (the multi-kernel step) against the oracle forward."""
+    shape, pack = _kind_pack(kind, 17 + kind[3])
+    model = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size)
+    prompt = synth.seeded_prompt(4, shape.vocab, 17)
+    ids_ref, logits_ref, state_ref = model.greedy(prompt, 6)
+    eng = B200Engine(pack)
+    try:
+        ids, logits = eng.greedy(prompt, 6, keep_logits=True)
+        assert ids == ids_ref
+        np.testing.assert_allclose(_np(logits), logits_ref, rtol=0, atol=LOGIT_TOL)
+        for j, s in enumerate(eng.get_state()):
+            np.testing.assert_allclose(_np(s).reshape(-1), state_ref[j].reshape(-1), rtol=0, atol=LOGIT_TOL)
+    finally:
+        eng.close()

@@ -143,3 +143,39 @@ def test_oracle_forward_matches_reference_forward(policy):
     np.testing.assert_allclose(logits, gold["logits"], rtol=0, atol=1e-4)
     for j, s in enumerate(state):
         np.testing.assert_allclose(s, gold[f"state/{j}"], rtol=0, atol=1e-4)
+
+
+EXTRA = load_golden("gemv_extra.npz")
+
+
+@pytest.mark.parametrize("impl", ["oracle", "reference"])
+def test_per_tensor_lut2_and_int8_activation_match_reference_kernels(impl):
+    """Legacy per-tensor LUT2 (``TR2\\x01``: decode K1, row-walk GEMV K3) and the
+    activation-INT8 SG8 GEMV (K7) against the reference's own outputs."""
+    if impl == "reference" and not ok.ref_available():
+        pytest.skip("reference C kernels not built")
+    for t in ("sq", "lin", "odd"):
+        o, i = (int(v) for v in EXTRA[f"tensor_{t}/shape"])
+        blob = EXTRA[f"tensor_{t}/blob"]
+        y = ok.lut2_tensor_gemv(blob, EXTRA[f"tensor_{t}/x"], o, i, impl)
+        np.testing.assert_allclose(y, EXTRA[f"tensor_{t}/y"], rtol=1e-5, atol=1e-6, err_msg=t)
+        dec = oc.decode_lut2_tensor(blob.tobytes(), o * i)
+        assert np.array_equal(dec.view(np.uint32), EXTRA[f"tensor_{t}/decoded"].reshape(-1).view(np.uint32)), t
+    for t in ("sq", "g64"):
+        o, i = (int(v) for v in EXTRA[f"i8_{t}/shape"])
+        y = ok.sg8_i8_gemv(EXTRA[f"i8_{t}/blob"], EXTRA[f"i8_{t}/x"], o, i, impl)
+        np.testing.assert_allclose(y, EXTRA[f"i8_{t}/y"], rtol=1e-5, atol=1e-6, err_msg=t)
+
+
+def test_residual_and_per_tensor_encoders_round_trip():
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((32, 128)) * 0.02).astype(np.float32)
+    errs = {}
+    for kind in oc.LUT2_GROUPED_KINDS:
+        d = oc.decode_lut2_grouped(oc.encode_lut2_grouped(w, 64, kind=kind), w.shape)
+        errs[kind] = float(np.abs(d - w).max())
+    # two exact-ish residuals per group only lower the error
+    assert errs[oc.LUT2_GROUPED_RESIDUAL] < errs[oc.LUT2_GROUPED_FP16]
+    assert errs[oc.LUT2_INPUT_RESIDUAL] < errs[oc.LUT2_INPUT_FP16]
+    d = oc.decode_lut2_tensor(oc.encode_lut2_tensor(w), w.size)
+    assert float(np.abs(d.reshape(w.shape) - w).max()) < 0.1
