@@ -335,6 +335,65 @@ def run_prefill(eng, args, shape, bpt: int, dev, stream, world: int, rank: int) 
                     "d2h_bytes_per_step": 0, "how": "B200BatchEngine.prefill(host prompts): tokens copied per chunk"}}
 
 
+def run_lut2(args, shape, dev, stream, world: int, rank: int) -> dict:
+    """The LUT2 legs (the 2.9B LUT2 configuration: 2-bit codes into a 4-entry
+    fp16 codebook per 64-column group): the same seeded model encoded as
+    ``TR2\x04``, greedy decode at batch 1 (``args.lut2_steps`` tokens, one
+    launch) and the batched step at ``args.lut2_sessions`` sessions."""
+    import argparse
+
+    import torch.distributed as dist
+    from rwkv_b200 import synth
+    from rwkv_b200.engine import B200BatchEngine, B200Engine, ModelUpload
+
+    largs = argparse.Namespace(**vars(args))
+    largs.policy = "lut2"
+    pack = synth.make_pack_streaming(shape, SEED + rank, dev, policy="lut2")
+    bpt = bytes_per_token(pack, shape)
+    model = ModelUpload(pack, dev)
+    del pack
+    torch.cuda.empty_cache()
+    eng = B200Engine(model, device=dev.index)
+    out = {}
+    try:
+        prompt = synth.seeded_prompt(PROMPT, shape.vocab, SEED + rank)
+        eng.forward(prompt)
+        first = int(torch.argmax(eng.logits).item())
+        ids = torch.empty(max(args.lut2_steps, args.warmup) + 8, dtype=torch.int32, device=dev)
+        eng.decode_greedy_async(first, args.warmup, ids)
+        torch.cuda.synchronize(dev)
+        nxt = int(ids[args.warmup - 1].item())
+        if world > 1:
+            dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        eng.decode_greedy_async(nxt, args.lut2_steps, ids)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = replicas.max_over_ranks(t0.elapsed_time(t1))
+        ms_step = ms / args.lut2_steps
+        peak, peak_kind = _peaks()
+        achieved = bpt / (ms_step / 1e3) / 1e9
+        out["bs1"] = {"metric": metric_name(largs), "value": args.lut2_steps * world / (ms / 1e3), "unit": "tok/s",
+                      "steps": args.lut2_steps, "ms_per_step": ms_step,
+                      "path": "persistent kernel" if eng.persistent_active else "multi-kernel CUDA graph",
+                      "gpu_launches": (eng.launches_per_step * args.lut2_steps) if eng.launches_per_step else 1,
+                      "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                   "frac": achieved / peak, "traffic": None, "algorithmic_bytes_per_step": bpt,
+                                   "what": f"bs1 decode: algorithmic bytes/token {bpt} (TR2x04 projections and head, "
+                                           f"SG8 adapters and embedding row, state) / device time per token; peak: "
+                                           f"{peak_kind} HBM copy bandwidth"}}
+    finally:
+        eng.close()
+    if args.lut2_sessions > 0:
+        beng = B200BatchEngine(model, args.lut2_sessions, device=dev.index)
+        out["batched"] = run_batched(beng, largs, shape, bpt, dev, stream, world, rank)
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_tp(args, dev, stream, world: int, rank: int) -> dict:
     """Tensor-parallel leg: ``args.tp_sessions`` sessions of the ``args.tp_config``
     model decoded with the model split over all ranks (heads, FFN rows and
@@ -476,6 +535,8 @@ def main() -> None:
     ap.add_argument("--batch-steps", type=int, default=64)
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill leg: tokens per session (0: skip)")
     ap.add_argument("--prefill-sessions", type=int, default=8)
+    ap.add_argument("--lut2-steps", type=int, default=64, help="LUT2 leg: bs1 decode tokens (0: skip the leg)")
+    ap.add_argument("--lut2-sessions", type=int, default=64, help="LUT2 leg: batched sessions (0: bs1 only)")
     ap.add_argument("--tp-config", default="7.2b", choices=["tiny", "7.2b", "7.2b-l4", "2.9b"],
                     help="tensor-parallel leg: model split over all ranks")
     ap.add_argument("--tp-sessions", type=int, default=8, help="tensor-parallel leg sessions (0: skip the leg)")
@@ -589,6 +650,14 @@ def main() -> None:
 
     batched = run_batched(batch_eng, args, shape, bpt, dev, stream, world, rank) if batch_eng is not None else None
     prefill = run_prefill(prefill_eng, args, shape, bpt, dev, stream, world, rank) if prefill_eng is not None else None
+    lut2 = None
+    if args.lut2_steps > 0 and args.policy == "sg8" and args.config in ("2.9b", "2.9b-l4", "0.1b", "tiny"):
+        # the LUT2 configuration of the same shape; a failure is reported in the line
+        try:
+            lut2 = run_lut2(args, shape, dev, stream, world, rank)
+        except Exception as exc:  # noqa: BLE001
+            lut2 = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            torch.cuda.synchronize(dev)
     tpres = None
     if args.tp_sessions > 0:
         # the tensor-parallel leg must not take the line's other results with it:
@@ -643,6 +712,8 @@ def main() -> None:
             res["prefill"] = prefill
         if tpres is not None:
             res["tp"] = tpres
+        if lut2 is not None:
+            res["lut2"] = lut2
         if cpu_pack is not None:
             backend.close()
             cb = cpu_baseline(cpu_pack, shape, args, gpu_ids)

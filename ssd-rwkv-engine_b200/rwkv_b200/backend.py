@@ -197,6 +197,7 @@ class CudaB200Backend(_PackBase):
         self._batch_engines: dict[int, Any] = {}
         self._last_state: RecurrentState | None = None
         self._lock = threading.Lock()
+        self._epoch = 0  # moved by every change of the engine's state (see _snapshot)
 
     # -------------------------------------------------------- RecurrentBackend
     def load(self, model_path: str, strategy: str, device: str) -> None:
@@ -224,6 +225,7 @@ class CudaB200Backend(_PackBase):
             self._model = ModelUpload(pack, self._device, hbm_budget=budget, resident_layers=resident,
                                       stage_slots=slots)
         self._engine = B200Engine(self._model, device=self._device, use_graph=self.use_graph)
+        self._epoch += 1
 
     @staticmethod
     def _residency(config, pack) -> tuple[int | None, list[int] | None, int]:
@@ -303,10 +305,17 @@ class CudaB200Backend(_PackBase):
     # get_recurrent_state returns and snapshot files hold) is the reference's:
     # rwkv7_state = the state before last_token_id, nothing else; resuming
     # consumes last_token_id first (rwkv7_forward.py:941-990).
+    #
+    # A live state also carries ("engine_epoch") the backend and the epoch at
+    # which it was taken.  Every operation that changes the engine's state
+    # moves the epoch first, so a state whose mark equals the current epoch is
+    # exactly what the engine holds and resuming it copies nothing.
     def _snapshot(self, last: int, pre: list[torch.Tensor]) -> RecurrentState:
         eng = self._engine
+        self._epoch += 1
         return RecurrentState(last_token_id=int(last), rwkv7_state=eng.get_state(),
-                              external_state={"pending_logits": eng.logits.clone(), "pre_state": pre})
+                              external_state={"pending_logits": eng.logits.clone(), "pre_state": pre,
+                                              "engine_epoch": (id(self), self._epoch)})
 
     def _restore(self, state: RecurrentState) -> list[torch.Tensor]:
         """Load ``state`` into the engine (consuming ``last_token_id`` for the
@@ -316,6 +325,10 @@ class CudaB200Backend(_PackBase):
             raise ValueError("cuda_b200 state has no rwkv7_state")
         ext = state.external_state if isinstance(state.external_state, dict) else {}
         pl = ext.get("pending_logits")
+        if pl is not None and ext.get("engine_epoch") == (id(self), self._epoch):
+            pre = ext.get("pre_state")
+            return list(pre) if pre is not None else eng.get_state()
+        self._epoch += 1
         if pl is not None:
             eng.set_state(state.rwkv7_state)
             eng.logits.copy_(pl.to(eng.device, torch.float32))
@@ -391,7 +404,8 @@ class CudaB200Backend(_PackBase):
         with self._lock:
             if initial_state is not None:
                 self._restore(initial_state)
-            else:
+            self._epoch += 1
+            if initial_state is None:
                 eng.reset()
             ids = [int(t) for t in token_ids] or [0]
             done = self._chunked_prefill(ids[:-1], ctl)
@@ -475,6 +489,7 @@ class CudaB200Backend(_PackBase):
         out: list[int] = []
         with self._lock:
             pre = self._restore(state)
+            self._epoch += 1
             t0 = time.perf_counter()
             if n and float(temperature) <= 0.0 and (ctl is None or eng.persistent_active):
                 first = int(torch.argmax(eng.logits).item())
@@ -622,6 +637,7 @@ class CudaB200Backend(_PackBase):
         if self._engine is not None:
             self._engine.close()
             self._engine = None
+            self._epoch += 1
         self._model = None
 
 

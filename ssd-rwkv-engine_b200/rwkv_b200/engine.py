@@ -221,19 +221,25 @@ class B200Engine:
         native.check(self.lib.rwkvb_engine_reset(self._h, self._stream(stream)), "rwkvb_engine_reset")
 
     def get_state(self) -> list[torch.Tensor]:
-        """Clone of the state as ``RecurrentState.rwkv7_state`` (3 tensors per layer)."""
+        """Clone of the state as ``RecurrentState.rwkv7_state`` (3 tensors per
+        layer): three device copies, returned as per-layer views of them."""
+        att, wkv, ffn = self.att_x.clone(), self.wkv.clone(), self.ffn_x.clone()
         out = []
         for i in range(self.shape.n_layer):
-            out += [self.att_x[i].clone(), self.wkv[i].clone(), self.ffn_x[i].clone()]
+            out += [att[i], wkv[i], ffn[i]]
         return out
 
     def set_state(self, state: list[torch.Tensor]) -> None:
         if len(state) != 3 * self.shape.n_layer:
             raise ValueError(f"expected {3 * self.shape.n_layer} state tensors, got {len(state)}")
-        for i in range(self.shape.n_layer):
-            self.att_x[i].copy_(state[3 * i].reshape(-1).to(self.device, torch.float32))
-            self.wkv[i].copy_(state[3 * i + 1].reshape(self.wkv[i].shape).to(self.device, torch.float32))
-            self.ffn_x[i].copy_(state[3 * i + 2].reshape(-1).to(self.device, torch.float32))
+        for j, dst in enumerate((self.att_x, self.wkv, self.ffn_x)):
+            parts = state[j::3]
+            for i, t in enumerate(parts):
+                if t.numel() != dst[i].numel():
+                    raise ValueError(f"state tensor {3 * i + j} has {t.numel()} elements, expected {dst[i].numel()}")
+            # one gather on the source device, one copy into the engine
+            src = torch.stack([t.reshape(dst.shape[1:]) for t in parts])
+            dst.copy_(src.to(self.device, torch.float32))
 
     # ------------------------------------------------------------- stepping
     def forward(self, tokens, stream=None) -> torch.Tensor:

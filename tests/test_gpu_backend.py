@@ -171,3 +171,29 @@ def test_snapshot_file_resumes_the_generation(model, tmp_path):
     resumed = b.decode_greedy(b.get_recurrent_state(), prov, 6, metrics=None)
     assert resumed == direct
     assert first + direct == oracle.greedy(list(b"snap"), 11)[0]
+
+
+def test_live_state_resumes_without_a_copy_and_stale_states_are_restored(model):
+    """A state the engine still holds resumes as is; a state taken before a
+    later change of the engine is copied back in full: both continue exactly
+    like the oracle."""
+    shape, pack, oracle, b, prov = model
+    text = "live"
+    ref, _, _ = oracle.greedy(list(text.encode()), 7)
+    st0 = b.prefill_text(text, prov, metrics=None)
+    keep = st0.clone()
+    calls = []
+    orig = b._engine.set_state
+    b._engine.set_state = lambda s: (calls.append(1), orig(s))[1]
+    try:
+        a = b.decode_greedy(st0, prov, 3, metrics=None)  # the engine holds st0: no copy
+        assert calls == []
+        st1 = b._last_state
+        c = b.decode_greedy(st1, prov, 4, metrics=None)  # live again
+        assert calls == []
+        assert a + c == ref
+        again = b.decode_greedy(keep, prov, 7, metrics=None)  # stale: restored in full
+        assert calls == [1]
+        assert again == ref
+    finally:
+        b._engine.set_state = orig
