@@ -249,7 +249,10 @@ typedef struct rwkvb_engine rwkvb_engine;
  *               state and activations re-read every layer stay in L2);
  *        bits 12..15 = ring slots of weight tiles in flight per SM in the
  *               persistent kernel, 3..8 (0: the default, 3 -- deeper rings
- *               delay the kernel's own small loads behind the weight stream). 
+ *               delay the kernel's own small loads behind the weight stream);
+ *        bit16 = persistent kernel: the FFN value projection as its own phase
+ *               behind a grid barrier (default: fused -- each SM computes whole
+ *               key rows and multiplies its column slice of the value matrix). 
  * When every projection is SG8 with one power-of-two group size and the
  * 16-byte layout that rwkvb upload placement gives, decode runs as ONE
  * cooperative persistent launch per call (all tokens, all layers); otherwise

@@ -28,6 +28,14 @@
 //   C  output projection                      (att_x[l] <- ln1 slice)
 //   D  x += att; ln2 + mix; ffn key rows
 //   E  relu^2; ffn value rows                 (ffn_x[l] <- ln2 slice)
+// Fused FFN (the default): in D every CTA computes whole key rows [r0, r1)
+// (both column chunks of its 16-row tiles), so relu^2 of its rows is final in
+// its own shared memory; E is then this CTA's column slice W_v[:, r0:r1] times
+// those values (unit images built for the slice, one bulk copy each), every
+// output row accumulated in 2^-32 fixed point with 64-bit integer adds (exact,
+// so the sum of the CTAs' partials does not depend on their order).  No grid
+// barrier separates D and E, and no CTA builds the digits of the whole
+// FFN-wide vector; ffn_x[l] is stored after the next barrier.
 // then the head (ln_out, logits) and a two-barrier first-maximum argmax.
 //
 // Every wait is bounded (slot barriers, grid barrier).  A timeout sets the
@@ -76,6 +84,11 @@ __device__ __forceinline__ int d_ld_relaxed_sys(const int* p) {
 
 __device__ __forceinline__ void d_st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Fire-and-forget 64-bit integer add (the fixed-point accumulators).
+__device__ __forceinline__ void red_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned d_ld_acquire(const unsigned* p) {
@@ -145,6 +158,11 @@ struct DArgs {
   // dedicated shared memory at the start of the layer instead of ring slots
   int pre;
   uint32_t o_adp, o_item, adp_b0, adp_b1;
+  // fused FFN (efuse != 0): the value projection as per-CTA column slices,
+  // layer l's images at ebase + l * eimg_b, units of eru rows
+  int efuse, eru;
+  uint32_t eimg_b;
+  const uint8_t* ebase;
 };
 
 struct DTable {
@@ -154,6 +172,10 @@ struct DTable {
   int npc[2];     // adapter second-stage pieces: layer 0 (no v2), other layers; 0 unless a head CTA
   int pm[kDMaxPieces], pr0[kDMaxPieces];
   int zc0, zc1, zf0, zf1, z3c0, z3c1, zv0, zv1, zr0, zr1;  // zeroing slices (C, F, 3C, V, rtot)
+  // fused FFN: key rows [er0, er0 + ew) of this CTA, flush segments, image row
+  // bytes (codes + (min, max) pairs), units, offset of this CTA's images
+  int er0, ew, enseg, erowb, enunits;
+  uint32_t eoff;
 };
 
 // [a, b) = part i of [0, n) split into `parts` (n * parts < 2^32).
@@ -162,10 +184,10 @@ __device__ __noinline__ void d_split(int n, int parts, int i, int* a, int* b) {
   *b = (int)((unsigned)n * (unsigned)(i + 1) / (unsigned)parts);
 }
 
-__device__ __forceinline__ void d_range(int tiles, int nch, int G, int b, DRange& R) {
+__device__ __forceinline__ void d_range(int tiles, int nch, int G, int b, DRange& R, bool whole = false) {
   const int U = tiles * nch;
   R.nch = nch;
-  if (U / G >= nch - 1) {  // every range spans >= nch - 1 units: a tile meets at most two CTAs
+  if (!whole && U / G >= nch - 1) {  // every range spans >= nch - 1 units: a tile meets at most two CTAs
     d_split(U, G, b, &R.u0, &R.u1);
   } else {  // whole tiles
     int t0, t1;
@@ -173,6 +195,35 @@ __device__ __forceinline__ void d_range(int tiles, int nch, int G, int b, DRange
     R.u0 = t0 * nch;
     R.u1 = t1 * nch;
   }
+}
+
+// Fused FFN: the key rows of CTA b (whole 16-row tiles of the F rows, split
+// as d_split does), its flush segments (the slice's parts of 2^lg-column
+// weight groups) and the bytes of one row of its value-projection images.
+struct ESlice {
+  int r0, w, nseg, rowb;
+};
+__host__ __device__ __forceinline__ ESlice e_slice(int F, int G, int b, int lg) {
+  const int tiles = F / 16;
+  const int t0 = (int)((unsigned)tiles * (unsigned)b / (unsigned)G);
+  const int t1 = (int)((unsigned)tiles * (unsigned)(b + 1) / (unsigned)G);
+  ESlice e;
+  e.r0 = 16 * t0;
+  e.w = 16 * (t1 - t0);
+  e.nseg = e.w ? ((e.r0 + e.w - 1) >> lg) - (e.r0 >> lg) + 1 : 0;
+  e.rowb = e.w + 8 * e.nseg;
+  return e;
+}
+
+// 16-byte chunk position of logical chunk j in row r of a slice image whose
+// rows hold nch chunks: a permutation inside the row chosen so that the eight
+// rows one mma fragment load touches fall on distinct shared-memory banks for
+// any row stride.
+__host__ __device__ __forceinline__ int e_swz(int r, int j, int nch) {
+  if (nch & 1) return j;
+  if (nch & 2) return j ^ ((r >> 2) & 1);
+  if (nch & 4) return j ^ ((r >> 1) & 3);
+  return j ^ (r & 7);
 }
 
 __device__ __forceinline__ int d_rank(const Dims& d, int m) {
@@ -195,7 +246,7 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
   const int nc = C / a.kc, nf = F / a.kc;
   d_range(3 * C / 16, nc, G, bx, T.r[0]);
   d_range(C / 16, nc, G, bx, T.r[1]);
-  d_range(F / 16, nc, G, bx, T.r[2]);
+  d_range(F / 16, nc, G, bx, T.r[2], a.efuse != 0);
   d_range(C / 16, nf, G, bx, T.r[3]);
   d_range((a.d.V + 15) / 16, nc, G, bx, T.r[4]);
   const int items3 = a.d.abase[3], items4 = a.d.abase[4];
@@ -223,6 +274,17 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
   d_split(3 * C, G, bx, &T.z3c0, &T.z3c1);
   d_split(a.d.V, G, bx, &T.zv0, &T.zv1);
   d_split(a.d.rtot, G, bx, &T.zr0, &T.zr1);
+  T.er0 = T.ew = T.enseg = T.erowb = T.enunits = 0;
+  T.eoff = 0;
+  if (a.efuse) {
+    for (int b = 0; b < bx; ++b) T.eoff += (uint32_t)C * (uint32_t)e_slice(F, G, b, a.lg).rowb;
+    const ESlice e = e_slice(F, G, bx, a.lg);
+    T.er0 = e.r0;
+    T.ew = e.w;
+    T.enseg = e.nseg;
+    T.erowb = e.rowb;
+    T.enunits = e.w ? (C + a.eru - 1) / a.eru : 0;
+  }
 }
 
 // ------------------------------------------------------------- producer
@@ -330,6 +392,51 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
         ++mi;
       }
     }
+  }
+  seq_io = seq;
+  return ok;
+}
+
+// Producer, fused FFN: this CTA's value-projection slice images of layer l,
+// one bulk copy per unit of eru rows (the last unit may be shorter).
+__device__ __noinline__ bool d_issue_eunits(const DArgs& a, const DTable& T, int l, uint8_t* ring, uint64_t* full,
+                                            uint64_t* empty, volatile int* abort_flag, int& seq_io) {
+  const int nst = a.nst, eru = a.eru, C = a.d.C, n = T.enunits, rowb = T.erowb;
+  const uint32_t slot_b = a.slot;
+  const uint8_t* base = a.ebase + (size_t)l * a.eimg_b + T.eoff;
+  unsigned long long* tr = (a.trace && blockIdx.x == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
+  const int tr_n = 2 * a.trace_cap;
+  const bool hint = a.l2_first != 0;
+  const uint64_t pol = l2_evict_first();
+  int seq = seq_io;
+  bool ok = true;
+#pragma unroll 1
+  for (int j = 0; j < n; ++j) {
+    const int slot = seq % nst;
+    if (seq >= nst) {
+      const uint32_t par = (uint32_t)((seq / nst - 1) & 1);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait_hint(&empty[slot], par, 20000u)) {
+        if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
+          if (!*abort_flag) {
+            atomicOr(a.b.err, kErrTimeout);
+            *abort_flag = 1;
+          }
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) break;
+    }
+    const int rows = min(eru, C - j * eru);
+    const uint32_t bytes = (uint32_t)rows * (uint32_t)rowb;
+    uint8_t* dst = ring + (size_t)slot * slot_b;
+    const uint8_t* src = base + (size_t)j * eru * rowb;
+    mbar_expect_tx(&full[slot], bytes);
+    if (hint) bulk_g2s_hint(dst, src, bytes, &full[slot], pol);
+    else bulk_g2s(dst, src, bytes, &full[slot]);
+    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq] = global_ns();
+    ++seq;
   }
   seq_io = seq;
   return ok;
@@ -481,7 +588,11 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
         }
         if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0, M.su[1]);
         if (ok) ok = units(T.r[2], M.q + 4, M.p + 4, 0, M.su[2]);
-        if (ok) ok = units(T.r[3], M.q + 5, M.p + 5, 0, M.su[3]);
+        if (a.efuse) {
+          if (ok && T.enunits > 0) ok = d_issue_eunits(a, T, l, ring, full, empty, abort_flag, seq);
+        } else if (ok) {
+          ok = units(T.r[3], M.q + 5, M.p + 5, 0, M.su[3]);
+        }
       }
       if (ok && head) {
         d_prefetch_map(a.head_maps);
@@ -662,6 +773,16 @@ __device__ __forceinline__ void ldcg8(float (&v)[8], const float* p) {
   const float4 a = ldcg4(p), b = ldcg4(p + 4);
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
+// Eight 2^-32 fixed-point values (one rounding each to fp32).
+__device__ __forceinline__ float unfix(unsigned long long v) { return __ll2float_rn((long long)v) * kUnfix; }
+__device__ __forceinline__ void ldcg8_fix(float (&v)[8], const unsigned long long* p) {
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const ulonglong2 w = __ldcg(reinterpret_cast<const ulonglong2*>(p) + h);
+    v[2 * h] = unfix(w.x);
+    v[2 * h + 1] = unfix(w.y);
+  }
+}
 __device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
   reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
@@ -671,6 +792,7 @@ __device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
 struct DLnMix {
   const float* xs;   // shared input vector
   const float* add;  // global vector added to it (nullptr: none)
+  const unsigned long long* add64;  // or a 2^-32 fixed-point vector added to it (nullptr: none)
   float* xo;         // shared copy of the sum (nullptr: not kept)
   const float *w, *b;  // LayerNorm weight, bias (global)
   const float* prev;   // previous-token vector (global; nullptr: mixes are the LayerNorm output itself)
@@ -694,6 +816,12 @@ __device__ __noinline__ void d_ln_mix(const DArgs& a, DCons& c, const DLnMix& q,
   if (q.add) {
     float ad[8];
     ldcg8(ad, q.add + i0);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) x[u] += ad[u];
+  }
+  if (q.add64) {
+    float ad[8];
+    ldcg8_fix(ad, q.add64 + i0);
 #pragma unroll
     for (int u = 0; u < 8; ++u) x[u] += ad[u];
   }
@@ -771,7 +899,7 @@ __device__ __forceinline__ void d_slot_release(const DArgs& a, DCons& c) {
 // be repeated each iteration).
 template <int LFK>
 __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, uint8_t* dig, uint32_t stride, int K,
-                                     int per_set, float* out, int rows_total) {
+                                     int per_set, float* out, int rows_total, float* lout = nullptr, int lrow0 = 0) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const ImmaLane L = imma_lane();
   const int nst = a.nst, nb = a.nb, pr = a.pr, lg = a.lg, kch = a.kc >> 5, u0 = R.u0, u1 = R.u1, nch = R.nch;
@@ -844,7 +972,9 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
           float v = 0.f;
           for (int w = 0; w < nb; ++w) v += q[w * 16];
           const int row = (ftile + (i >> 4)) * 16 + (i & 15);
-          if (row < rows_total && !dead) atomicAdd(out + row, v);
+          if (lout) {
+            if (row < rows_total) lout[row - lrow0] = v;  // whole tiles of this CTA: the row is complete
+          } else if (row < rows_total && !dead) atomicAdd(out + row, v);
         }
         d_csync();  // the buffer is rewritten next
         nt = 0;
@@ -854,6 +984,195 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
     if (++chunk == nch) {
       chunk = 0;
       ++tile;
+    }
+  }
+  c.seq = seq;
+  c.dead = dead;
+}
+
+// Fused FFN, shared-memory layout inside `misc` (E phase only): the CTA's
+// key rows, then the digit words of its slice (k16-step s, digit n, quarter t
+// at [s * 12 + n * 4 + t]: digit n of x[16 s + 4 t .. + 4)), then per flush
+// segment c_s = 2^e_s / 127 and sum_x, then the segments' first k16-steps.
+constexpr int kEMaxW = 512;  // key rows per CTA
+constexpr int kEKeys = 0, kEXd = kEMaxW, kESc = kEXd + (kEMaxW / 16) * 12, kESks = kESc + 16;
+static_assert(kESks + 16 <= kDMisc, "fused-FFN slice data lives in misc");
+
+// Fused FFN: relu^2 of this CTA's key rows (final in shared memory) and the
+// three-digit form of each flush segment (the slice's part of one weight
+// group: its own exponent and sum).  Warp 0 does it (W <= 512 values); ends
+// with the consumer barrier.
+__device__ __noinline__ void d_eprep(const DArgs& a, const DTable& T, float* misc) {
+  const int t = threadIdx.x, lane = t & 31;
+  const int W = T.ew, r0 = T.er0, lg = a.lg, nseg = T.enseg, g0 = r0 >> lg;
+  const float* keys = misc + kEKeys;
+  uint32_t* xd = reinterpret_cast<uint32_t*>(misc + kEXd);
+  float* sc = misc + kESc;
+  int* sks = reinterpret_cast<int*>(misc + kESks);
+  if (t < 32) {
+    float m[4] = {0.f, 0.f, 0.f, 0.f}, sm[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+    for (int base = 0; base < W; base += 128) {
+      const int k = base + 4 * lane;
+      if (k < W) {
+        const int sg = ((r0 + k) >> lg) - g0;
+        float mx = 0.f, su = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float v = keys[k + u] > 0.f ? keys[k + u] * keys[k + u] : 0.f;
+          mx = fmaxf(mx, v);
+          su += v;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (q == sg) {
+            m[q] = fmaxf(m[q], mx);
+            sm[q] += su;
+          }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      for (int o = 16; o > 0; o >>= 1) {
+        m[q] = fmaxf(m[q], __shfl_xor_sync(0xffffffffu, m[q], o));
+        sm[q] += __shfl_xor_sync(0xffffffffu, sm[q], o);
+      }
+    }
+    // per segment: exponent of the largest value (values are >= 0), 127 * 2^-e, 2^e / 127
+    float inv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      int e = 0;
+      if (m[q] > 0.f) {
+        const uint32_t be = __float_as_uint(m[q]) >> 23;
+        if (be != 0u) e = (int)be - 126;
+        else frexpf(m[q], &e);
+      }
+      inv[q] = (e > -122 && e < 127) ? 127.0f * __uint_as_float((uint32_t)(127 - e) << 23) : ldexpf(127.0f, -e);
+      if (lane == 0 && q < nseg) {
+        sc[q] = (e > -127 && e < 128) ? __uint_as_float((uint32_t)(127 + e) << 23) * (1.0f / 127.0f)
+                                      : ldexpf(1.0f, e) / 127.0f;
+        sc[4 + q] = sm[q];
+        const int c0 = max(r0, (g0 + q) << lg);
+        sks[q] = (c0 - r0) >> 4;
+      }
+    }
+    if (lane == 0) sks[nseg] = W >> 4;
+    constexpr float kShift = 12582912.0f;  // rounding by the 1.5 * 2^23 shift, as emit_digits
+#pragma unroll 1
+    for (int base = 0; base < W; base += 128) {
+      const int k = base + 4 * lane;
+      if (k < W) {
+        const int sg = ((r0 + k) >> lg) - g0;
+        const float iv = sg == 0 ? inv[0] : (sg == 1 ? inv[1] : (sg == 2 ? inv[2] : inv[3]));
+        uint32_t w0 = 0u, w1 = 0u, w2 = 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float v = keys[k + u] > 0.f ? keys[k + u] * keys[k + u] : 0.f;
+          const float y0 = v * iv;
+          const float s0 = __fadd_rn(y0, kShift);
+          const float x0 = __fsub_rn(s0, kShift);
+          const float y1 = (y0 - x0) * 254.0f;
+          const float s1 = __fadd_rn(y1, kShift);
+          const float x1 = __fsub_rn(s1, kShift);
+          const float s2 = __fadd_rn((y1 - x1) * 254.0f, kShift);
+          w0 |= (__float_as_uint(s0) & 0xffu) << (8 * u);
+          w1 |= (__float_as_uint(s1) & 0xffu) << (8 * u);
+          w2 |= (__float_as_uint(s2) & 0xffu) << (8 * u);
+        }
+        const int ks = k >> 4, tq = (k >> 2) & 3;
+        xd[ks * 12 + tq] = w0;
+        xd[ks * 12 + 4 + tq] = w1;
+        xd[ks * 12 + 8 + tq] = w2;
+      }
+    }
+  }
+  d_csync();
+}
+
+// Fused FFN: the value projection's column slice of this CTA.  Unit j (rows
+// [j eru, j eru + rows)) is one ring slot: codes [rows][W] (chunks permuted by
+// e_swz), then (min, max) [rows][nseg].  Warp w takes rows [16 w, 16 w + 16)
+// of the unit; per flush segment the three digit sums come from
+// mma.m16n8k16 (u8 x s8), then the group algebra of imma_block; the row's
+// partial goes to the 2^-32 fixed-point accumulator with one 64-bit add.
+__device__ __noinline__ void d_eunits(const DArgs& a, DCons& c, const DTable& T, const float* misc) {
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, g = lane >> 2, tq = lane & 3;
+  const int nst = a.nst, eru = a.eru, C = a.d.C, n = T.enunits, W = T.ew, nch = W >> 4, nseg = T.enseg;
+  const uint32_t slot_b = a.slot;
+  uint8_t* const sm = c.sm;
+  uint64_t* const full = c.full;
+  uint64_t* const empty = c.empty;
+  const uint32_t* xd = reinterpret_cast<const uint32_t*>(misc + kEXd);
+  const float* sc = misc + kESc;
+  const int* sks = reinterpret_cast<const int*>(misc + kESks);
+  unsigned long long* fo = a.b.fo64;
+  unsigned long long* tr = (a.trace && blockIdx.x == 0 && t == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
+  const int tr_n = 2 * a.trace_cap;
+  int seq = c.seq;
+  int slot = seq % nst;
+  uint32_t ph = (uint32_t)((seq / nst) & 1);
+  bool dead = c.dead;
+  const int ra = 16 * warp + g, rb = ra + 8;
+#pragma unroll 1
+  for (int j = 0; j < n; ++j) {
+    const int rows = min(eru, C - j * eru);
+    if (!dead) {
+      bool got = mbar_try_wait(&full[slot], ph);
+      if (!got) got = mbar_wait_suspend(&full[slot], ph);
+      if (!__all_sync(0xffffffffu, got)) {
+        dead = true;
+        if (lane == 0) {
+          atomicOr(a.b.err, kErrTimeout);
+          *c.abort = 1;
+        }
+      }
+    }
+    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 1] = global_ns();
+    if (!dead && 16 * warp < rows) {
+      const uint8_t* sl = sm + (size_t)slot * slot_b;
+      const uint8_t* qa = sl + ra * W + 4 * tq;
+      const uint8_t* qb = sl + rb * W + 4 * tq;
+      const float2* rec = reinterpret_cast<const float2*>(sl + rows * W);
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+      for (int sg = 0; sg < nseg; ++sg) {
+        int d[4] = {0, 0, 0, 0};
+#pragma unroll 1
+        for (int ks = sks[sg]; ks < sks[sg + 1]; ++ks) {
+          const uint32_t a0 = *reinterpret_cast<const uint32_t*>(qa + (e_swz(ra, ks, nch) << 4));
+          const uint32_t a1 = *reinterpret_cast<const uint32_t*>(qb + (e_swz(rb, ks, nch) << 4));
+          const uint32_t b0 = lane < 12 ? xd[ks * 12 + lane] : 0u;
+          imma_16816(d, a0, a1, b0);
+        }
+        if (tq < 2) {
+          const float cs = sc[sg];
+          const float2 p0 = rec[ra * nseg + sg], p1 = rec[rb * nseg + sg];
+          const float da = (p0.y - p0.x) * kInv255 * cs, db = (p1.y - p1.x) * kInv255 * cs;
+          if (tq == 0) {
+            const float xs = sc[4 + sg];
+            acc0 = fmaf(da, fmaf((float)d[1], kInv254, (float)d[0]), fmaf(p0.x, xs, acc0));
+            acc1 = fmaf(db, fmaf((float)d[3], kInv254, (float)d[2]), fmaf(p1.x, xs, acc1));
+          } else {
+            acc0 = fmaf(da * kInv254sq, (float)d[0], acc0);
+            acc1 = fmaf(db * kInv254sq, (float)d[2], acc1);
+          }
+        }
+      }
+      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+      if (tq == 0) {
+        red_add_u64(fo + j * eru + ra, (unsigned long long)__float2ll_rn(acc0 * kFix));
+        red_add_u64(fo + j * eru + rb, (unsigned long long)__float2ll_rn(acc1 * kFix));
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 2] = global_ns();
+    ++seq;
+    if (++slot == nst) {
+      slot = 0;
+      ph ^= 1u;
     }
   }
   c.seq = seq;
@@ -1285,6 +1604,13 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   d_zero(logits, T.zv0, T.zv1);
   #pragma unroll 1
   for (int i = T.zr0 + t; i < T.zr1; i += kDT) a.b.adp64[i] = 0ull;
+  const bool efuse = a.efuse != 0;
+  unsigned long long* fo64 = a.b.fo64;
+  #pragma unroll 1
+  for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
+  // fused FFN: this thread's element of the CTA's ln2 slice, kept from phase D
+  // to the next grid barrier (ffn_x[l] is read by every CTA in phase D)
+  float ffn_keep = 0.f;
   int tok = a.mode == 0 ? (a.first_tok >= 0 ? a.first_tok : __ldcg(a.b.tok)) : __ldg(a.forced);
   bool alive = d_gsync(a, c);
   for (int step = 0; step < a.ntok && alive; ++step) {
@@ -1304,11 +1630,13 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         break;
       }
       d_mark(a, c);  // A start
+      if (efuse && l > 0 && T.zc0 + t < T.zc1) a.b.ffn_x[(size_t)(l - 1) * C + T.zc0 + t] = ffn_keep;
       // ================= A: ln1, mixes, r/k/v rows, adapter first stages
       if (fused) {
         DLnMix q{};
         q.xs = l > 0 ? XB : X;
-        q.add = l > 0 ? acc_fo : nullptr;
+        q.add = l > 0 && !efuse ? acc_fo : nullptr;
+        q.add64 = l > 0 && efuse ? fo64 : nullptr;
         q.xo = X;
         q.w = Ly.ln1_w;
         q.b = Ly.ln1_b;
@@ -1324,7 +1652,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       } else {
         if (l > 0) {
 #pragma unroll 1
-          for (int i = t; i < C; i += kDT) X[i] = XB[i] + __ldcg(acc_fo + i);
+          for (int i = t; i < C; i += kDT) X[i] = XB[i] + (efuse ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
           d_csync();
         }
         d_layer_norm(TV, X, Ly.ln1_w, Ly.ln1_b, C, s_stat, red);
@@ -1355,6 +1683,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       }
       d_mark(a, c);  // B barrier
       d_zero(acc_hk, T.zf0, T.zf1);
+      if (efuse) d_zero(acc_ao, T.zc0, T.zc1);  // read by every CTA in the previous layer's D
       if (l == 0) d_zero(logits, T.zv0, T.zv1);
       if (is_head) d_head_wkv(a, c, T, l, S, misc);
       d_mark(a, c);  // B done
@@ -1364,7 +1693,12 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       }
       d_mark(a, c);  // C barrier
       // ================= C: output projection; att_x[l] <- ln1 slice
-      d_zero(acc_fo, T.zc0, T.zc1);
+      if (efuse) {
+        #pragma unroll 1
+        for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
+      } else {
+        d_zero(acc_fo, T.zc0, T.zc1);
+      }
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
         a.b.att_x[(size_t)l * C + i] = TV[i];  // ln1 output of phase A, still in shared memory
@@ -1405,6 +1739,19 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         d_build<LFK>(DSrc{0, TV, PV, Ly.ffn_x_k}, C, dig);
       }
       d_mark(a, c);  // D prep done
+      if (efuse) {
+        // whole key rows of this CTA into shared memory, then its value-projection slice
+        if (T.zc0 + t < T.zc1) ffn_keep = TV[T.zc0 + t];
+        d_units<LFK>(a, c, T.r[2], dig, 0, C, 0, nullptr, F, misc + kEKeys, T.er0);
+        d_mark(a, c);  // D done
+        d_mark(a, c);  // E barrier (none: the slice needs only this CTA's rows)
+        d_mark(a, c);  // E slices stored (after the next barrier)
+        d_eprep(a, T, misc);
+        d_mark(a, c);  // E prep done
+        d_eunits(a, c, T, misc);
+        d_mark(a, c);  // E done
+        continue;
+      }
       d_units<LFK>(a, c, T.r[2], dig, 0, C, 0, acc_hk, F);
       d_mark(a, c);  // D done
       if (!d_gsync(a, c)) {
@@ -1424,7 +1771,19 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_mark(a, c);  // E done
     }
     if (!alive) break;
-    if (!head) continue;
+    if (!head) {
+      if (efuse) {
+        // without the head's barriers: every CTA has finished the last layer's
+        // D phase (its zeroing and its reads of ffn_x) before the next token's
+        // A phase writes accumulators, and ffn_x[L - 1] is stored after it
+        if (!d_gsync(a, c)) {
+          alive = false;
+          break;
+        }
+        if (T.zc0 + t < T.zc1) a.b.ffn_x[(size_t)(a.d.L - 1) * C + T.zc0 + t] = ffn_keep;
+      }
+      continue;
+    }
     // ================= head: ln_out, logits, argmax (first maximum)
     if (!d_gsync(a, c)) {
       alive = false;
@@ -1437,10 +1796,12 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     int cancel_seen = 0;
     if (a.ring_cancel && bx == 0 && t == 0) cancel_seen = d_ld_relaxed_sys(a.ring_cancel);
     d_zero(acc_hk, T.zf0, T.zf1);
-        if (fused) {
+    if (efuse && T.zc0 + t < T.zc1) a.b.ffn_x[(size_t)(a.d.L - 1) * C + T.zc0 + t] = ffn_keep;
+    if (fused) {
       DLnMix q{};
       q.xs = XB;
-      q.add = acc_fo;
+      q.add = efuse ? nullptr : acc_fo;
+      q.add64 = efuse ? fo64 : nullptr;
       q.w = a.lnout_w;
       q.b = a.lnout_b;
       q.nmix = 1;
@@ -1448,7 +1809,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_ln_mix<LFK>(a, c, q, dig, 0);
     } else {
 #pragma unroll 1
-      for (int i = t; i < C; i += kDT) PV[i] = XB[i] + __ldcg(acc_fo + i);
+      for (int i = t; i < C; i += kDT) PV[i] = XB[i] + (efuse ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
       d_csync();
       d_layer_norm(TV, PV, a.lnout_w, a.lnout_b, C, nullptr, red);
       d_build<LFK>(DSrc{1, TV, nullptr, nullptr}, C, dig);
@@ -1460,7 +1821,12 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       alive = false;
       break;
     }
-    d_zero(acc_fo, T.zc0, T.zc1);
+    if (efuse) {
+      #pragma unroll 1
+      for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
+    } else {
+      d_zero(acc_fo, T.zc0, T.zc1);
+    }
     d_argmax_part(a, T, s_bv, s_bi);
     if (a.ring_cancel && bx == 0 && t == 0) *a.b.stop = cancel_seen;
     if (!d_gsync(a, c)) {

@@ -36,6 +36,15 @@ __device__ __forceinline__ void imma_16832(int (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// m16n8k16 form (A 16 x 16 u8: a0 row g, a1 row g + 8, k 4t..4t+3 each; B
+// 16 x 8 s8: b0 = k 4t..4t+3 of column g; D as in m16n8k32).
+__device__ __forceinline__ void imma_16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+
 // Named barrier over the `n` consumer threads (barrier 0 is __syncthreads).
 __device__ __forceinline__ void bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");

@@ -181,6 +181,23 @@ def test_engine_decode_matches_reference_forward(policy, path):
         eng.close()
 
 
+def test_engine_separate_ffn_phase_matches_reference_forward():
+    """The persistent kernel with the FFN value projection as its own phase
+    (the default fuses it into per-SM column slices): same ids, logits and
+    state as the reference forward."""
+    gold, shape, pack = _reference_pack("sg8")
+    eng = B200Engine(pack, fused_ffn=False)
+    try:
+        assert eng.persistent_active
+        ids, logits = eng.greedy([int(t) for t in gold["prompt"]], len(gold["ids"]), keep_logits=True)
+        assert ids == [int(t) for t in gold["ids"]]
+        np.testing.assert_allclose(_np(logits), gold["logits"], rtol=0, atol=LOGIT_TOL)
+        for j, st in enumerate(eng.get_state()):
+            np.testing.assert_allclose(_np(st).reshape(-1), gold[f"state/{j}"].reshape(-1), rtol=0, atol=LOGIT_TOL)
+    finally:
+        eng.close()
+
+
 @pytest.mark.parametrize("prefetch", [0, 1, 2])
 def test_engine_prefetch_distance_does_not_change_results(prefetch):
     gold, shape, pack = _reference_pack("sg8")
