@@ -250,9 +250,10 @@ typedef struct rwkvb_engine rwkvb_engine;
  *        bits 12..15 = ring slots of weight tiles in flight per SM in the
  *               persistent kernel, 3..8 (0: the default, 3 -- deeper rings
  *               delay the kernel's own small loads behind the weight stream);
- *        bit16 = persistent kernel: the FFN value projection as its own phase
- *               behind a grid barrier (default: fused -- each SM computes whole
- *               key rows and multiplies its column slice of the value matrix). 
+ *        bit16 = persistent kernel: FFN value-projection units in row order
+ *               with fp32 accumulation (default: column-chunk order, so each
+ *               SM builds the activation digits of only its one or two chunks,
+ *               and 2^-32 fixed-point accumulation). 
  * When every projection is SG8 with one power-of-two group size and the
  * 16-byte layout that rwkvb upload placement gives, decode runs as ONE
  * cooperative persistent launch per call (all tokens, all layers); otherwise

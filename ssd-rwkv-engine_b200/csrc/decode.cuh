@@ -28,14 +28,11 @@
 //   C  output projection                      (att_x[l] <- ln1 slice)
 //   D  x += att; ln2 + mix; ffn key rows
 //   E  relu^2; ffn value rows                 (ffn_x[l] <- ln2 slice)
-// Fused FFN (the default): in D every CTA computes whole key rows [r0, r1)
-// (both column chunks of its 16-row tiles), so relu^2 of its rows is final in
-// its own shared memory; E is then this CTA's column slice W_v[:, r0:r1] times
-// those values (unit images built for the slice, one bulk copy each), every
-// output row accumulated in 2^-32 fixed point with 64-bit integer adds (exact,
-// so the sum of the CTAs' partials does not depend on their order).  No grid
-// barrier separates D and E, and no CTA builds the digits of the whole
-// FFN-wide vector; ffn_x[l] is stored after the next barrier.
+// FFN value rows in column-chunk order (the default): E's units are numbered
+// chunk by chunk, so each CTA's range covers one or two KC-column chunks and
+// it builds the digits of only those chunks of relu^2(k) instead of the whole
+// FFN-wide vector; a row then receives one partial per chunk, accumulated in
+// 2^-32 fixed point with 64-bit integer adds (exact: independent of order).
 // then the head (ln_out, logits) and a two-barrier first-maximum argmax.
 //
 // Every wait is bounded (slot barriers, grid barrier).  A timeout sets the
@@ -62,6 +59,7 @@ constexpr int kDRingDefault = 3;       // ring slots unless the engine flags ask
 constexpr int kDBar = 1;               // named barrier of the consumers
 constexpr int kDMaxItems = 8;          // adapter first-stage items per CTA
 constexpr int kDPartTiles = 8;         // GEMV tiles whose per-warp partial sums are buffered per CTA reduction
+constexpr uint32_t kDPartBytes = kDPartTiles * kDW * 16 * 4 + 128;  // the partial sums, then their tile indices
 constexpr int kDMaxPieces = 8;         // adapter second-stage tile pieces per layer
 constexpr int kDMisc = 2560;           // misc shared floats
 static_assert((kDW / 2) * 4 * 64 <= kDMisc, "phase-B adapter partials [warps / 2][4][64] live in misc");
@@ -158,11 +156,9 @@ struct DArgs {
   // dedicated shared memory at the start of the layer instead of ring slots
   int pre;
   uint32_t o_adp, o_item, adp_b0, adp_b1;
-  // fused FFN (efuse != 0): the value projection as per-CTA column slices,
-  // layer l's images at ebase + l * eimg_b, units of eru rows
-  int efuse, eru;
-  uint32_t eimg_b;
-  const uint8_t* ebase;
+  // FFN value rows in column-chunk order with fixed-point accumulation (0:
+  // row order, fp32 atomics)
+  int ecm;
 };
 
 struct DTable {
@@ -172,10 +168,7 @@ struct DTable {
   int npc[2];     // adapter second-stage pieces: layer 0 (no v2), other layers; 0 unless a head CTA
   int pm[kDMaxPieces], pr0[kDMaxPieces];
   int zc0, zc1, zf0, zf1, z3c0, z3c1, zv0, zv1, zr0, zr1;  // zeroing slices (C, F, 3C, V, rtot)
-  // fused FFN: key rows [er0, er0 + ew) of this CTA, flush segments, image row
-  // bytes (codes + (min, max) pairs), units, offset of this CTA's images
-  int er0, ew, enseg, erowb, enunits;
-  uint32_t eoff;
+  int ech0, ech1;  // chunk-ordered E: first and last column chunk of this CTA's units
 };
 
 // [a, b) = part i of [0, n) split into `parts` (n * parts < 2^32).
@@ -195,35 +188,6 @@ __device__ __forceinline__ void d_range(int tiles, int nch, int G, int b, DRange
     R.u0 = t0 * nch;
     R.u1 = t1 * nch;
   }
-}
-
-// Fused FFN: the key rows of CTA b (whole 16-row tiles of the F rows, split
-// as d_split does), its flush segments (the slice's parts of 2^lg-column
-// weight groups) and the bytes of one row of its value-projection images.
-struct ESlice {
-  int r0, w, nseg, rowb;
-};
-__host__ __device__ __forceinline__ ESlice e_slice(int F, int G, int b, int lg) {
-  const int tiles = F / 16;
-  const int t0 = (int)((unsigned)tiles * (unsigned)b / (unsigned)G);
-  const int t1 = (int)((unsigned)tiles * (unsigned)(b + 1) / (unsigned)G);
-  ESlice e;
-  e.r0 = 16 * t0;
-  e.w = 16 * (t1 - t0);
-  e.nseg = e.w ? ((e.r0 + e.w - 1) >> lg) - (e.r0 >> lg) + 1 : 0;
-  e.rowb = e.w + 8 * e.nseg;
-  return e;
-}
-
-// 16-byte chunk position of logical chunk j in row r of a slice image whose
-// rows hold nch chunks: a permutation inside the row chosen so that the eight
-// rows one mma fragment load touches fall on distinct shared-memory banks for
-// any row stride.
-__host__ __device__ __forceinline__ int e_swz(int r, int j, int nch) {
-  if (nch & 1) return j;
-  if (nch & 2) return j ^ ((r >> 2) & 1);
-  if (nch & 4) return j ^ ((r >> 1) & 3);
-  return j ^ (r & 7);
 }
 
 __device__ __forceinline__ int d_rank(const Dims& d, int m) {
@@ -246,8 +210,17 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
   const int nc = C / a.kc, nf = F / a.kc;
   d_range(3 * C / 16, nc, G, bx, T.r[0]);
   d_range(C / 16, nc, G, bx, T.r[1]);
-  d_range(F / 16, nc, G, bx, T.r[2], a.efuse != 0);
-  d_range(C / 16, nf, G, bx, T.r[3]);
+  d_range(F / 16, nc, G, bx, T.r[2]);
+  if (a.ecm) {  // chunk order: equal contiguous shares of the chunk-major unit numbering
+    T.r[3].nch = nf;
+    d_split(C / 16 * nf, G, bx, &T.r[3].u0, &T.r[3].u1);
+    T.ech0 = T.r[3].u0 / (C / 16);
+    T.ech1 = T.r[3].u1 > T.r[3].u0 ? (T.r[3].u1 - 1) / (C / 16) : T.ech0;
+  } else {
+    d_range(C / 16, nf, G, bx, T.r[3]);
+    T.ech0 = 0;
+    T.ech1 = nf - 1;
+  }
   d_range((a.d.V + 15) / 16, nc, G, bx, T.r[4]);
   const int items3 = a.d.abase[3], items4 = a.d.abase[4];
   T.nitem[0] = T.nitem[1] = 0;
@@ -274,17 +247,6 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
   d_split(3 * C, G, bx, &T.z3c0, &T.z3c1);
   d_split(a.d.V, G, bx, &T.zv0, &T.zv1);
   d_split(a.d.rtot, G, bx, &T.zr0, &T.zr1);
-  T.er0 = T.ew = T.enseg = T.erowb = T.enunits = 0;
-  T.eoff = 0;
-  if (a.efuse) {
-    for (int b = 0; b < bx; ++b) T.eoff += (uint32_t)C * (uint32_t)e_slice(F, G, b, a.lg).rowb;
-    const ESlice e = e_slice(F, G, bx, a.lg);
-    T.er0 = e.r0;
-    T.ew = e.w;
-    T.enseg = e.nseg;
-    T.erowb = e.rowb;
-    T.enunits = e.w ? (C + a.eru - 1) / a.eru : 0;
-  }
 }
 
 // ------------------------------------------------------------- producer
@@ -340,7 +302,7 @@ __device__ __forceinline__ void d_issued(const DArgs& a, int& seq) {
 // copy (a single TMA operation per unit instead of a code box and a pair box).
 __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, const CUtensorMap* q, const CUtensorMap* p,
                                            int per_map, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                                           volatile int* abort_flag, int& seq_io, const uint8_t* su) {
+                                           volatile int* abort_flag, int& seq_io, const uint8_t* su, int tiles_cm) {
   const int nst = a.nst, nb = a.nb, pr8 = a.pr * 8, u0 = R.u0, u1 = R.u1, nch = R.nch;
   const uint32_t slot_b = a.slot, code_b = a.code_b, bytes = a.code_b + a.pair_b;
   unsigned long long* tr = (a.trace && blockIdx.x == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
@@ -348,7 +310,8 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
   int seq = seq_io;
   const bool hint = a.l2_first != 0;
   const uint64_t pol = l2_evict_first();
-  int tile = u0 / nch, chunk = u0 - tile * nch;
+  // unit u: (tile, chunk) = (u / nch, u % nch), or chunk-major (u % tiles_cm, u / tiles_cm)
+  int tile = tiles_cm ? u0 % tiles_cm : u0 / nch, chunk = tiles_cm ? u0 / tiles_cm : u0 - tile * nch;
   int mi = per_map ? tile / per_map : 0, row0 = (tile - mi * per_map) * 16;
   bool ok = true;
 #pragma unroll 1
@@ -372,7 +335,7 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     uint8_t* dst = ring + (size_t)slot * slot_b;
     mbar_expect_tx(&full[slot], bytes);
     if (su) {
-      const uint8_t* src = su + (size_t)u * bytes;
+      const uint8_t* src = su + (size_t)(tile * nch + chunk) * bytes;  // images are stored tile by tile
       if (hint) bulk_g2s_hint(dst, src, bytes, &full[slot], pol);
       else bulk_g2s(dst, src, bytes, &full[slot]);
     } else if (hint) {
@@ -384,59 +347,22 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     }
     if (tr && 3 * seq + 2 < tr_n) tr[3 * seq] = global_ns();
     ++seq;
-    if (++chunk == nch) {
+    if (tiles_cm) {
+      row0 += 16;
+      if (++tile == tiles_cm) {
+        tile = 0;
+        row0 = 0;
+        ++chunk;
+      }
+    } else if (++chunk == nch) {
       chunk = 0;
+      ++tile;
       row0 += 16;
       if (per_map && row0 == per_map * 16) {
         row0 = 0;
         ++mi;
       }
     }
-  }
-  seq_io = seq;
-  return ok;
-}
-
-// Producer, fused FFN: this CTA's value-projection slice images of layer l,
-// one bulk copy per unit of eru rows (the last unit may be shorter).
-__device__ __noinline__ bool d_issue_eunits(const DArgs& a, const DTable& T, int l, uint8_t* ring, uint64_t* full,
-                                            uint64_t* empty, volatile int* abort_flag, int& seq_io) {
-  const int nst = a.nst, eru = a.eru, C = a.d.C, n = T.enunits, rowb = T.erowb;
-  const uint32_t slot_b = a.slot;
-  const uint8_t* base = a.ebase + (size_t)l * a.eimg_b + T.eoff;
-  unsigned long long* tr = (a.trace && blockIdx.x == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
-  const int tr_n = 2 * a.trace_cap;
-  const bool hint = a.l2_first != 0;
-  const uint64_t pol = l2_evict_first();
-  int seq = seq_io;
-  bool ok = true;
-#pragma unroll 1
-  for (int j = 0; j < n; ++j) {
-    const int slot = seq % nst;
-    if (seq >= nst) {
-      const uint32_t par = (uint32_t)((seq / nst - 1) & 1);
-      const uint64_t t0 = globaltimer_ns();
-      while (!mbar_try_wait_hint(&empty[slot], par, 20000u)) {
-        if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
-          if (!*abort_flag) {
-            atomicOr(a.b.err, kErrTimeout);
-            *abort_flag = 1;
-          }
-          ok = false;
-          break;
-        }
-      }
-      if (!ok) break;
-    }
-    const int rows = min(eru, C - j * eru);
-    const uint32_t bytes = (uint32_t)rows * (uint32_t)rowb;
-    uint8_t* dst = ring + (size_t)slot * slot_b;
-    const uint8_t* src = base + (size_t)j * eru * rowb;
-    mbar_expect_tx(&full[slot], bytes);
-    if (hint) bulk_g2s_hint(dst, src, bytes, &full[slot], pol);
-    else bulk_g2s(dst, src, bytes, &full[slot]);
-    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq] = global_ns();
-    ++seq;
   }
   seq_io = seq;
   return ok;
@@ -513,8 +439,8 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
     const int C = a.d.C, ct = C / 16, bx = blockIdx.x;
     bool ok = true;
     auto units = [&](const DRange& R, const CUtensorMap* q, const CUtensorMap* p, int per_map,
-                     const uint8_t* su) -> bool {
-      return d_issue_units(a, R, q, p, per_map, ring, full, empty, abort_flag, seq, su);
+                     const uint8_t* su, int tiles_cm = 0) -> bool {
+      return d_issue_units(a, R, q, p, per_map, ring, full, empty, abort_flag, seq, su, tiles_cm);
     };
     for (int tok = 0; tok < a.ntok && ok; ++tok) {
       const bool head = a.mode == 0 || tok == a.ntok - 1;
@@ -588,11 +514,7 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
         }
         if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0, M.su[1]);
         if (ok) ok = units(T.r[2], M.q + 4, M.p + 4, 0, M.su[2]);
-        if (a.efuse) {
-          if (ok && T.enunits > 0) ok = d_issue_eunits(a, T, l, ring, full, empty, abort_flag, seq);
-        } else if (ok) {
-          ok = units(T.r[3], M.q + 5, M.p + 5, 0, M.su[3]);
-        }
+        if (ok) ok = units(T.r[3], M.q + 5, M.p + 5, 0, M.su[3], a.ecm ? C / 16 : 0);
       }
       if (ok && head) {
         d_prefetch_map(a.head_maps);
@@ -898,8 +820,12 @@ __device__ __forceinline__ void d_slot_release(const DArgs& a, DCons& c) {
 // for the loop (it stores to shared memory, so reads through `a` or `c` would
 // be repeated each iteration).
 template <int LFK>
+// tiles_cm > 0: units in chunk-major order (tiles_cm tiles per chunk; every
+// unit ends a tile), the digits built for chunks [ch0, ..] only, row sums
+// added to the 2^-32 fixed-point `out64` instead of `out`.
 __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, uint8_t* dig, uint32_t stride, int K,
-                                     int per_set, float* out, int rows_total, float* lout = nullptr, int lrow0 = 0) {
+                                     int per_set, float* out, int rows_total, int tiles_cm = 0, int ch0 = 0,
+                                     unsigned long long* out64 = nullptr) {
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const ImmaLane L = imma_lane();
   const int nst = a.nst, nb = a.nb, pr = a.pr, lg = a.lg, kch = a.kc >> 5, u0 = R.u0, u1 = R.u1, nch = R.nch;
@@ -918,8 +844,9 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
   float acc0 = 0.f, acc1 = 0.f;
   int cur_set = -1;
   XDigits X{};
-  int tile = u0 / nch, chunk = u0 - tile * nch;
-  int nt = 0, ftile = tile;  // tiles buffered in `part`, the first of them
+  int tile = tiles_cm ? u0 % tiles_cm : u0 / nch, chunk = tiles_cm ? u0 / tiles_cm : u0 - tile * nch;
+  int nt = 0;  // tiles buffered in `part`
+  int* ptile = reinterpret_cast<int*>(part + kDPartTiles * kDW * 16);  // their tile indices
 #pragma unroll 1
   for (int u = u0; u < u1; ++u) {
     const int set = per_set ? tile / per_set : 0;
@@ -942,7 +869,7 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
     if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 1] = global_ns();
     if (!dead && warp < nb) {
       const float2* pp = reinterpret_cast<const float2*>(sl + code_b) + pofs;
-      imma_block<LFK>(sl + warp * 2048, pp, pp + 8 * pr, chunk * kch + warp * 4, X, L, acc0, acc1);
+      imma_block<LFK>(sl + warp * 2048, pp, pp + 8 * pr, (chunk - ch0) * kch + warp * 4, X, L, acc0, acc1);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
@@ -952,7 +879,7 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
       slot = 0;
       ph ^= 1u;
     }
-    if (chunk == nch - 1 || u == u1 - 1) {
+    if (tiles_cm || chunk == nch - 1 || u == u1 - 1) {
       // tile end: this warp's partial sums of the tile's 16 rows go to the
       // buffer; the CTA sums them over warps (in warp order) and adds each row
       // to `out` once per kDPartTiles tiles instead of meeting at every tile
@@ -963,6 +890,7 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
         pt[warp * 16 + L.ra] = acc0;
         pt[warp * 16 + L.ra + 8] = acc1;
       }
+      if (t == 0) ptile[nt] = tile;
       acc0 = acc1 = 0.f;
       if (++nt == kDPartTiles || u == u1 - 1) {
         d_csync();
@@ -971,208 +899,24 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
           const float* q = part + (i >> 4) * (kDW * 16) + (i & 15);
           float v = 0.f;
           for (int w = 0; w < nb; ++w) v += q[w * 16];
-          const int row = (ftile + (i >> 4)) * 16 + (i & 15);
-          if (lout) {
-            if (row < rows_total) lout[row - lrow0] = v;  // whole tiles of this CTA: the row is complete
-          } else if (row < rows_total && !dead) atomicAdd(out + row, v);
+          const int row = ptile[i >> 4] * 16 + (i & 15);
+          if (row < rows_total && !dead) {
+            if (out64) red_add_u64(out64 + row, (unsigned long long)__float2ll_rn(v * kFix));
+            else atomicAdd(out + row, v);
+          }
         }
         d_csync();  // the buffer is rewritten next
         nt = 0;
-        ftile = tile + 1;
       }
     }
-    if (++chunk == nch) {
+    if (tiles_cm) {
+      if (++tile == tiles_cm) {
+        tile = 0;
+        ++chunk;
+      }
+    } else if (++chunk == nch) {
       chunk = 0;
       ++tile;
-    }
-  }
-  c.seq = seq;
-  c.dead = dead;
-}
-
-// Fused FFN, shared-memory layout inside `misc` (E phase only): the CTA's
-// key rows, then the digit words of its slice (k16-step s, digit n, quarter t
-// at [s * 12 + n * 4 + t]: digit n of x[16 s + 4 t .. + 4)), then per flush
-// segment c_s = 2^e_s / 127 and sum_x, then the segments' first k16-steps.
-constexpr int kEMaxW = 512;  // key rows per CTA
-constexpr int kEKeys = 0, kEXd = kEMaxW, kESc = kEXd + (kEMaxW / 16) * 12, kESks = kESc + 16;
-static_assert(kESks + 16 <= kDMisc, "fused-FFN slice data lives in misc");
-
-// Fused FFN: relu^2 of this CTA's key rows (final in shared memory) and the
-// three-digit form of each flush segment (the slice's part of one weight
-// group: its own exponent and sum).  Warp 0 does it (W <= 512 values); ends
-// with the consumer barrier.
-__device__ __noinline__ void d_eprep(const DArgs& a, const DTable& T, float* misc) {
-  const int t = threadIdx.x, lane = t & 31;
-  const int W = T.ew, r0 = T.er0, lg = a.lg, nseg = T.enseg, g0 = r0 >> lg;
-  const float* keys = misc + kEKeys;
-  uint32_t* xd = reinterpret_cast<uint32_t*>(misc + kEXd);
-  float* sc = misc + kESc;
-  int* sks = reinterpret_cast<int*>(misc + kESks);
-  if (t < 32) {
-    float m[4] = {0.f, 0.f, 0.f, 0.f}, sm[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-    for (int base = 0; base < W; base += 128) {
-      const int k = base + 4 * lane;
-      if (k < W) {
-        const int sg = ((r0 + k) >> lg) - g0;
-        float mx = 0.f, su = 0.f;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float v = keys[k + u] > 0.f ? keys[k + u] * keys[k + u] : 0.f;
-          mx = fmaxf(mx, v);
-          su += v;
-        }
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (q == sg) {
-            m[q] = fmaxf(m[q], mx);
-            sm[q] += su;
-          }
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      for (int o = 16; o > 0; o >>= 1) {
-        m[q] = fmaxf(m[q], __shfl_xor_sync(0xffffffffu, m[q], o));
-        sm[q] += __shfl_xor_sync(0xffffffffu, sm[q], o);
-      }
-    }
-    // per segment: exponent of the largest value (values are >= 0), 127 * 2^-e, 2^e / 127
-    float inv[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      int e = 0;
-      if (m[q] > 0.f) {
-        const uint32_t be = __float_as_uint(m[q]) >> 23;
-        if (be != 0u) e = (int)be - 126;
-        else frexpf(m[q], &e);
-      }
-      inv[q] = (e > -122 && e < 127) ? 127.0f * __uint_as_float((uint32_t)(127 - e) << 23) : ldexpf(127.0f, -e);
-      if (lane == 0 && q < nseg) {
-        sc[q] = (e > -127 && e < 128) ? __uint_as_float((uint32_t)(127 + e) << 23) * (1.0f / 127.0f)
-                                      : ldexpf(1.0f, e) / 127.0f;
-        sc[4 + q] = sm[q];
-        const int c0 = max(r0, (g0 + q) << lg);
-        sks[q] = (c0 - r0) >> 4;
-      }
-    }
-    if (lane == 0) sks[nseg] = W >> 4;
-    constexpr float kShift = 12582912.0f;  // rounding by the 1.5 * 2^23 shift, as emit_digits
-#pragma unroll 1
-    for (int base = 0; base < W; base += 128) {
-      const int k = base + 4 * lane;
-      if (k < W) {
-        const int sg = ((r0 + k) >> lg) - g0;
-        const float iv = sg == 0 ? inv[0] : (sg == 1 ? inv[1] : (sg == 2 ? inv[2] : inv[3]));
-        uint32_t w0 = 0u, w1 = 0u, w2 = 0u;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float v = keys[k + u] > 0.f ? keys[k + u] * keys[k + u] : 0.f;
-          const float y0 = v * iv;
-          const float s0 = __fadd_rn(y0, kShift);
-          const float x0 = __fsub_rn(s0, kShift);
-          const float y1 = (y0 - x0) * 254.0f;
-          const float s1 = __fadd_rn(y1, kShift);
-          const float x1 = __fsub_rn(s1, kShift);
-          const float s2 = __fadd_rn((y1 - x1) * 254.0f, kShift);
-          w0 |= (__float_as_uint(s0) & 0xffu) << (8 * u);
-          w1 |= (__float_as_uint(s1) & 0xffu) << (8 * u);
-          w2 |= (__float_as_uint(s2) & 0xffu) << (8 * u);
-        }
-        const int ks = k >> 4, tq = (k >> 2) & 3;
-        xd[ks * 12 + tq] = w0;
-        xd[ks * 12 + 4 + tq] = w1;
-        xd[ks * 12 + 8 + tq] = w2;
-      }
-    }
-  }
-  d_csync();
-}
-
-// Fused FFN: the value projection's column slice of this CTA.  Unit j (rows
-// [j eru, j eru + rows)) is one ring slot: codes [rows][W] (chunks permuted by
-// e_swz), then (min, max) [rows][nseg].  Warp w takes rows [16 w, 16 w + 16)
-// of the unit; per flush segment the three digit sums come from
-// mma.m16n8k16 (u8 x s8), then the group algebra of imma_block; the row's
-// partial goes to the 2^-32 fixed-point accumulator with one 64-bit add.
-__device__ __noinline__ void d_eunits(const DArgs& a, DCons& c, const DTable& T, const float* misc) {
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, g = lane >> 2, tq = lane & 3;
-  const int nst = a.nst, eru = a.eru, C = a.d.C, n = T.enunits, W = T.ew, nch = W >> 4, nseg = T.enseg;
-  const uint32_t slot_b = a.slot;
-  uint8_t* const sm = c.sm;
-  uint64_t* const full = c.full;
-  uint64_t* const empty = c.empty;
-  const uint32_t* xd = reinterpret_cast<const uint32_t*>(misc + kEXd);
-  const float* sc = misc + kESc;
-  const int* sks = reinterpret_cast<const int*>(misc + kESks);
-  unsigned long long* fo = a.b.fo64;
-  unsigned long long* tr = (a.trace && blockIdx.x == 0 && t == 0) ? a.trace + 2 * (size_t)a.trace_cap : nullptr;
-  const int tr_n = 2 * a.trace_cap;
-  int seq = c.seq;
-  int slot = seq % nst;
-  uint32_t ph = (uint32_t)((seq / nst) & 1);
-  bool dead = c.dead;
-  const int ra = 16 * warp + g, rb = ra + 8;
-#pragma unroll 1
-  for (int j = 0; j < n; ++j) {
-    const int rows = min(eru, C - j * eru);
-    if (!dead) {
-      bool got = mbar_try_wait(&full[slot], ph);
-      if (!got) got = mbar_wait_suspend(&full[slot], ph);
-      if (!__all_sync(0xffffffffu, got)) {
-        dead = true;
-        if (lane == 0) {
-          atomicOr(a.b.err, kErrTimeout);
-          *c.abort = 1;
-        }
-      }
-    }
-    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 1] = global_ns();
-    if (!dead && 16 * warp < rows) {
-      const uint8_t* sl = sm + (size_t)slot * slot_b;
-      const uint8_t* qa = sl + ra * W + 4 * tq;
-      const uint8_t* qb = sl + rb * W + 4 * tq;
-      const float2* rec = reinterpret_cast<const float2*>(sl + rows * W);
-      float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll 1
-      for (int sg = 0; sg < nseg; ++sg) {
-        int d[4] = {0, 0, 0, 0};
-#pragma unroll 1
-        for (int ks = sks[sg]; ks < sks[sg + 1]; ++ks) {
-          const uint32_t a0 = *reinterpret_cast<const uint32_t*>(qa + (e_swz(ra, ks, nch) << 4));
-          const uint32_t a1 = *reinterpret_cast<const uint32_t*>(qb + (e_swz(rb, ks, nch) << 4));
-          const uint32_t b0 = lane < 12 ? xd[ks * 12 + lane] : 0u;
-          imma_16816(d, a0, a1, b0);
-        }
-        if (tq < 2) {
-          const float cs = sc[sg];
-          const float2 p0 = rec[ra * nseg + sg], p1 = rec[rb * nseg + sg];
-          const float da = (p0.y - p0.x) * kInv255 * cs, db = (p1.y - p1.x) * kInv255 * cs;
-          if (tq == 0) {
-            const float xs = sc[4 + sg];
-            acc0 = fmaf(da, fmaf((float)d[1], kInv254, (float)d[0]), fmaf(p0.x, xs, acc0));
-            acc1 = fmaf(db, fmaf((float)d[3], kInv254, (float)d[2]), fmaf(p1.x, xs, acc1));
-          } else {
-            acc0 = fmaf(da * kInv254sq, (float)d[0], acc0);
-            acc1 = fmaf(db * kInv254sq, (float)d[2], acc1);
-          }
-        }
-      }
-      acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
-      acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
-      if (tq == 0) {
-        red_add_u64(fo + j * eru + ra, (unsigned long long)__float2ll_rn(acc0 * kFix));
-        red_add_u64(fo + j * eru + rb, (unsigned long long)__float2ll_rn(acc1 * kFix));
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
-    if (tr && 3 * seq + 2 < tr_n) tr[3 * seq + 2] = global_ns();
-    ++seq;
-    if (++slot == nst) {
-      slot = 0;
-      ph ^= 1u;
     }
   }
   c.seq = seq;
@@ -1604,13 +1348,10 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   d_zero(logits, T.zv0, T.zv1);
   #pragma unroll 1
   for (int i = T.zr0 + t; i < T.zr1; i += kDT) a.b.adp64[i] = 0ull;
-  const bool efuse = a.efuse != 0;
+  const bool ecm = a.ecm != 0;  // FFN value rows in chunk order, output in fixed point
   unsigned long long* fo64 = a.b.fo64;
   #pragma unroll 1
   for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
-  // fused FFN: this thread's element of the CTA's ln2 slice, kept from phase D
-  // to the next grid barrier (ffn_x[l] is read by every CTA in phase D)
-  float ffn_keep = 0.f;
   int tok = a.mode == 0 ? (a.first_tok >= 0 ? a.first_tok : __ldcg(a.b.tok)) : __ldg(a.forced);
   bool alive = d_gsync(a, c);
   for (int step = 0; step < a.ntok && alive; ++step) {
@@ -1630,13 +1371,12 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         break;
       }
       d_mark(a, c);  // A start
-      if (efuse && l > 0 && T.zc0 + t < T.zc1) a.b.ffn_x[(size_t)(l - 1) * C + T.zc0 + t] = ffn_keep;
       // ================= A: ln1, mixes, r/k/v rows, adapter first stages
       if (fused) {
         DLnMix q{};
         q.xs = l > 0 ? XB : X;
-        q.add = l > 0 && !efuse ? acc_fo : nullptr;
-        q.add64 = l > 0 && efuse ? fo64 : nullptr;
+        q.add = l > 0 && !ecm ? acc_fo : nullptr;
+        q.add64 = l > 0 && ecm ? fo64 : nullptr;
         q.xo = X;
         q.w = Ly.ln1_w;
         q.b = Ly.ln1_b;
@@ -1652,7 +1392,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       } else {
         if (l > 0) {
 #pragma unroll 1
-          for (int i = t; i < C; i += kDT) X[i] = XB[i] + (efuse ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
+          for (int i = t; i < C; i += kDT) X[i] = XB[i] + (ecm ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
           d_csync();
         }
         d_layer_norm(TV, X, Ly.ln1_w, Ly.ln1_b, C, s_stat, red);
@@ -1683,7 +1423,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       }
       d_mark(a, c);  // B barrier
       d_zero(acc_hk, T.zf0, T.zf1);
-      if (efuse) d_zero(acc_ao, T.zc0, T.zc1);  // read by every CTA in the previous layer's D
       if (l == 0) d_zero(logits, T.zv0, T.zv1);
       if (is_head) d_head_wkv(a, c, T, l, S, misc);
       d_mark(a, c);  // B done
@@ -1693,7 +1432,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       }
       d_mark(a, c);  // C barrier
       // ================= C: output projection; att_x[l] <- ln1 slice
-      if (efuse) {
+      if (ecm) {
         #pragma unroll 1
         for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
       } else {
@@ -1739,19 +1478,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         d_build<LFK>(DSrc{0, TV, PV, Ly.ffn_x_k}, C, dig);
       }
       d_mark(a, c);  // D prep done
-      if (efuse) {
-        // whole key rows of this CTA into shared memory, then its value-projection slice
-        if (T.zc0 + t < T.zc1) ffn_keep = TV[T.zc0 + t];
-        d_units<LFK>(a, c, T.r[2], dig, 0, C, 0, nullptr, F, misc + kEKeys, T.er0);
-        d_mark(a, c);  // D done
-        d_mark(a, c);  // E barrier (none: the slice needs only this CTA's rows)
-        d_mark(a, c);  // E slices stored (after the next barrier)
-        d_eprep(a, T, misc);
-        d_mark(a, c);  // E prep done
-        d_eunits(a, c, T, misc);
-        d_mark(a, c);  // E done
-        continue;
-      }
       d_units<LFK>(a, c, T.r[2], dig, 0, C, 0, acc_hk, F);
       d_mark(a, c);  // D done
       if (!d_gsync(a, c)) {
@@ -1765,25 +1491,21 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
         a.b.ffn_x[(size_t)l * C + i] = TV[i];  // ln2 output of phase D, still in shared memory
       d_mark(a, c);  // E slices stored
-      d_build<LFK>(DSrc{3, nullptr, nullptr, acc_hk}, F, dig);
-      d_mark(a, c);  // E prep done
-      d_units<LFK>(a, c, T.r[3], dig, 0, F, 0, acc_fo, C);
+      if (ecm) {
+        // only the chunks of this CTA's units: [ech0, ech1] of kc columns each
+        const int k0 = T.ech0 * a.kc, kl = (T.ech1 - T.ech0 + 1) * a.kc;
+        d_build<LFK>(DSrc{3, nullptr, nullptr, acc_hk + k0}, kl, dig);
+        d_mark(a, c);  // E prep done
+        d_units<LFK>(a, c, T.r[3], dig, 0, kl, 0, nullptr, C, C / 16, T.ech0, fo64);
+      } else {
+        d_build<LFK>(DSrc{3, nullptr, nullptr, acc_hk}, F, dig);
+        d_mark(a, c);  // E prep done
+        d_units<LFK>(a, c, T.r[3], dig, 0, F, 0, acc_fo, C);
+      }
       d_mark(a, c);  // E done
     }
     if (!alive) break;
-    if (!head) {
-      if (efuse) {
-        // without the head's barriers: every CTA has finished the last layer's
-        // D phase (its zeroing and its reads of ffn_x) before the next token's
-        // A phase writes accumulators, and ffn_x[L - 1] is stored after it
-        if (!d_gsync(a, c)) {
-          alive = false;
-          break;
-        }
-        if (T.zc0 + t < T.zc1) a.b.ffn_x[(size_t)(a.d.L - 1) * C + T.zc0 + t] = ffn_keep;
-      }
-      continue;
-    }
+    if (!head) continue;
     // ================= head: ln_out, logits, argmax (first maximum)
     if (!d_gsync(a, c)) {
       alive = false;
@@ -1796,12 +1518,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     int cancel_seen = 0;
     if (a.ring_cancel && bx == 0 && t == 0) cancel_seen = d_ld_relaxed_sys(a.ring_cancel);
     d_zero(acc_hk, T.zf0, T.zf1);
-    if (efuse && T.zc0 + t < T.zc1) a.b.ffn_x[(size_t)(a.d.L - 1) * C + T.zc0 + t] = ffn_keep;
     if (fused) {
       DLnMix q{};
       q.xs = XB;
-      q.add = efuse ? nullptr : acc_fo;
-      q.add64 = efuse ? fo64 : nullptr;
+      q.add = ecm ? nullptr : acc_fo;
+      q.add64 = ecm ? fo64 : nullptr;
       q.w = a.lnout_w;
       q.b = a.lnout_b;
       q.nmix = 1;
@@ -1809,7 +1530,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_ln_mix<LFK>(a, c, q, dig, 0);
     } else {
 #pragma unroll 1
-      for (int i = t; i < C; i += kDT) PV[i] = XB[i] + (efuse ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
+      for (int i = t; i < C; i += kDT) PV[i] = XB[i] + (ecm ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
       d_csync();
       d_layer_norm(TV, PV, a.lnout_w, a.lnout_b, C, nullptr, red);
       d_build<LFK>(DSrc{1, TV, nullptr, nullptr}, C, dig);
@@ -1821,7 +1542,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       alive = false;
       break;
     }
-    if (efuse) {
+    if (ecm) {
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
     } else {

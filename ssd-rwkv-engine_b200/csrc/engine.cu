@@ -67,7 +67,7 @@ struct Bufs {
   float *logits;               // [V]
   float *ao, *fo;              // [C] attention / ffn output accumulators (persistent kernel)
   unsigned long long* adp64;   // [Rtot] first-adapter accumulators, 2^-32 fixed point (persistent kernel)
-  unsigned long long* fo64;    // [C] ffn output accumulator, 2^-32 fixed point (persistent kernel, fused FFN)
+  unsigned long long* fo64;    // [C] ffn output accumulator, 2^-32 fixed point (persistent kernel, chunk-ordered E)
   float *amax_v;               // [grid] per-CTA argmax value
   int *amax_i;                 // [grid] per-CTA argmax index
   unsigned *ticket;            // last-CTA election for the argmax
@@ -641,7 +641,6 @@ struct rwkvb_engine {
   uint8_t* hring = nullptr;
   uint8_t* hring_dev = nullptr;  // the same memory as the device addresses it
   uint8_t* dstream = nullptr;    // streaming copy of the big matrices (persistent kernel)
-  uint8_t* deimg = nullptr;      // fused FFN: per-CTA column-slice images of every layer's value projection
   // staged layers (rwkvb_engine_create_staged): layer li is streamed when
   // stage_slot[li] >= 0; its image (stage_bytes) is copied from pinned host
   // memory into device slot stage_slot[li] on the copy stream before the
@@ -944,75 +943,6 @@ __global__ void adp_image_kernel(uint8_t* dst, PackedView w, uint32_t img_b, uin
         *reinterpret_cast<const uint4*>(w.meta + ((size_t)r * gpr + px) * 8);
 }
 
-// Fused FFN: the value projection W_v [C][F] as per-CTA column slices.  CTA
-// b (one block each) owns key rows = W_v columns [r0, r0 + w) (e_slice); its
-// images start at off_b = sum over b' < b of C * rowb(b') and hold units of
-// `eru` rows (the last may be shorter): codes [rows][w] with chunk j of unit
-// row r stored at chunk e_swz(r, j, w / 16), then the rows' (min, max) pairs of
-// the slice's nseg weight groups, [rows][nseg] float2.
-__global__ void e_image_kernel(uint8_t* dst, PackedView wv, int G, int eru) {
-  const int b = blockIdx.x, C = wv.rows, F = wv.cols, lg = wv.lg;
-  size_t off = 0;
-  for (int c = 0; c < b; ++c) off += (size_t)C * (size_t)e_slice(F, G, c, lg).rowb;
-  const ESlice e = e_slice(F, G, b, lg);
-  if (!e.w) return;
-  const int nch = e.w >> 4, gpr = F >> lg, g0 = e.r0 >> lg;
-  for (int i = threadIdx.x; i < C * nch; i += blockDim.x) {
-    const int r = i / nch, j = i - r * nch, u = r / eru, rr = r - u * eru;
-    const int rows = min(eru, C - u * eru);
-    uint8_t* ub = dst + off + (size_t)u * eru * e.rowb;
-    *reinterpret_cast<uint4*>(ub + (size_t)rr * e.w + (e_swz(rr, j, nch) << 4)) =
-        *reinterpret_cast<const uint4*>(wv.payload + (size_t)r * F + e.r0 + j * 16);
-    if (j == 0) {
-      float2* rec = reinterpret_cast<float2*>(ub + (size_t)rows * e.w) + (size_t)rr * e.nseg;
-      for (int q = 0; q < e.nseg; ++q) rec[q] = reinterpret_cast<const float2*>(wv.meta)[(size_t)r * gpr + g0 + q];
-    }
-  }
-}
-
-// Plan and build the fused FFN (bit 16 of the engine flags keeps the separate
-// E phase): whole 16-row key tiles per CTA, the value projection's slice
-// images in units that fit a ring slot.  False leaves the separate phase.
-bool plan_efuse(rwkvb_engine* e, int G) {
-  DArgs& a = e->da;
-  a.efuse = 0;
-  if (e->flags & 0x10000u) return false;
-  const int C = e->d.C, F = e->d.F, lg = a.lg;
-  int wmax = 0, rbmax = 0, nsmax = 0;
-  uint64_t img = 0;
-  for (int b = 0; b < G; ++b) {
-    const ESlice s = e_slice(F, G, b, lg);
-    wmax = s.w > wmax ? s.w : wmax;
-    rbmax = s.rowb > rbmax ? s.rowb : rbmax;
-    nsmax = s.nseg > nsmax ? s.nseg : nsmax;
-    img += (uint64_t)C * (uint64_t)s.rowb;
-  }
-  // d_eprep keeps up to four flush segments per slice
-  if (wmax == 0 || wmax > kEMaxW || nsmax > 4 || img >= (1ull << 32)) return false;
-  int eru = (int)(a.slot / (uint32_t)rbmax) / 16 * 16;
-  eru = eru < 16 * kDW ? eru : 16 * kDW;
-  if (eru < 16 || C % 16 != 0) return false;
-  for (const LayerDev& l : e->layers)
-    if (l.fv.kind != RWKVB_KIND_SG8 || l.fv.lg != lg || l.fv.rows != C || l.fv.cols != F) return false;
-  if (cudaMalloc((void**)&e->deimg, img * (uint64_t)e->d.L) != cudaSuccess) {
-    cudaGetLastError();
-    e->deimg = nullptr;
-    return false;
-  }
-  for (int i = 0; i < e->d.L; ++i) e_image_kernel<<<G, 256>>>(e->deimg + (size_t)i * img, e->layers[i].fv, G, eru);
-  if (cudaDeviceSynchronize() != cudaSuccess) {
-    cudaGetLastError();
-    cudaFree(e->deimg);
-    e->deimg = nullptr;
-    return false;
-  }
-  a.efuse = 1;
-  a.eru = eru;
-  a.eimg_b = (uint32_t)img;
-  a.ebase = e->deimg;
-  return true;
-}
-
 uint64_t stream_units(const PackedView& w, int kc) { return (uint64_t)((w.rows + 15) / 16) * (uint64_t)(w.cols / kc); }
 
 // Build the streaming copy of every big matrix (bit 10 of the engine flags
@@ -1177,7 +1107,7 @@ bool plan_decode(rwkvb_engine* e) {
   dig = dig > wkv ? dig : wkv;
   dig = (dig + 127u) & ~127u;
   const uint32_t vec = ((uint32_t)d.C * 4u + 127u) & ~127u;
-  const uint32_t rest = dig + 4u * vec + (uint32_t)kDPartTiles * kDW * 16u * 4u + (uint32_t)kDMisc * 4u;
+  const uint32_t rest = dig + 4u * vec + kDPartBytes + (uint32_t)kDMisc * 4u;
   const uint32_t budget = 227u * 1024u - 1024u - 3u * 1024u;  // dynamic-smem alignment slack, static shared
   // Ring depth: the consumers' own small loads (accumulators, vectors) queue
   // behind the weight tiles in flight on their SM, so a deeper ring than the
@@ -1195,7 +1125,7 @@ bool plan_decode(rwkvb_engine* e) {
   a.o_xb = off;   off += vec;
   a.o_t = off;    off += vec;
   a.o_p = off;    off += vec;
-  a.o_part = off; off += (uint32_t)kDPartTiles * kDW * 16u * 4u;
+  a.o_part = off; off += kDPartBytes;
   a.o_misc = off; off += (uint32_t)kDMisc * 4u;
   // Preload mode: the phase-B adapter image of a head CTA (80 B per adapter
   // rank row) and the CTA's adapter first-stage item get dedicated shared
@@ -1227,7 +1157,6 @@ bool plan_decode(rwkvb_engine* e) {
   if (encode_big(e->head, a, &hh[0], &hh[1]) != RWKVB_OK) return false;
   plan_stream_copy(e, hm, want_pre);
   if (!a.pre) a.smem_total = a.o_misc + (uint32_t)kDMisc * 4u;  // no dedicated buffers
-  plan_efuse(e, e->sms);
   if (e->dstream && cudaDeviceSynchronize() != cudaSuccess) return false;
   if (cudaMalloc((void**)&e->dmaps, sizeof(DLayerMaps) * (size_t)d.L) != cudaSuccess ||
       cudaMalloc((void**)&e->dhead, sizeof(CUtensorMap) * 2) != cudaSuccess) {
@@ -1248,6 +1177,7 @@ bool plan_decode(rwkvb_engine* e) {
   a.d = d;
   a.spin_limit = 1u << 22;
   a.l2_first = (e->flags & 0x200u) ? 0 : 1;  // bit 9: plain weight-stream loads (no L2 policy)
+  a.ecm = (e->flags & 0x10000u) ? 0 : 1;     // bit 16: FFN value rows in row order, fp32 accumulation
   const PackedView& E = e->emb;
   a.emb_fast = E.kind == RWKVB_KIND_SG8 && E.lg >= 4 && d.C % (int)E.group == 0 && ((d.C >> E.lg) % 2) == 0 &&
                aligned16(E.payload) && aligned16(E.meta);
@@ -1493,7 +1423,6 @@ extern "C" int rwkvb_engine_destroy(rwkvb_engine* e) {
   if (e->dtrace) cudaFree(e->dtrace);
   if (e->hring) cudaFreeHost(e->hring);
   if (e->dstream) cudaFree(e->dstream);
-  if (e->deimg) cudaFree(e->deimg);
   for (cudaEvent_t ev : e->ev_loaded) cudaEventDestroy(ev);
   for (cudaEvent_t ev : e->ev_done) cudaEventDestroy(ev);
   if (e->ev_fork) cudaEventDestroy(e->ev_fork);

@@ -136,7 +136,7 @@ class B200Engine:
 
     def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
                  prefetch_distance: int | None = None, persistent: bool = True, trace: bool = False,
-                 l2_policy: bool = True, ring_slots: int | None = None, fused_ffn: bool = True):
+                 l2_policy: bool = True, ring_slots: int | None = None, ffn_chunk_order: bool = True):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
@@ -156,8 +156,8 @@ class B200Engine:
                 flags |= native.FLAG_EXPLICIT_PREFETCH | ((int(prefetch_distance) & 0xF) << 4)
             if ring_slots is not None:
                 flags |= (int(ring_slots) & 0xF) << native.FLAG_RING_SLOTS_SHIFT
-            if not fused_ffn:
-                flags |= native.FLAG_SEPARATE_FFN
+            if not ffn_chunk_order:
+                flags |= native.FLAG_FFN_ROW_ORDER
             h = ctypes.c_void_p()
             if self._model.stage is not None:
                 # streamed layers: the multi-kernel step with the staging copies in it

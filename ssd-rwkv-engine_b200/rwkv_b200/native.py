@@ -43,7 +43,7 @@ FLAG_TRACE = 0x8
 FLAG_EXPLICIT_PREFETCH = 0x100
 FLAG_NO_L2_POLICY = 0x200
 FLAG_RING_SLOTS_SHIFT = 12  # bits 12..15: persistent-kernel ring slots, 3..8 (0: default 3)
-FLAG_SEPARATE_FFN = 0x10000  # persistent kernel: FFN value rows as a separate phase (no fused slices)
+FLAG_FFN_ROW_ORDER = 0x10000  # persistent kernel: FFN value units in row order, fp32 accumulation
 
 
 class RwkvbError(RuntimeError):

@@ -70,15 +70,15 @@ def lut2_l4():
     return shape, up, oracle
 
 
-@pytest.mark.parametrize("ring,fused", [(None, True), (6, True), (None, False)])
-def test_persistent_2p9b_width_matches_oracle(sg8_l4, ring, fused):
+@pytest.mark.parametrize("ring,chunk_order", [(None, True), (6, True), (None, False)])
+def test_persistent_2p9b_width_matches_oracle(sg8_l4, ring, chunk_order):
     """The persistent kernel at the width it is tuned for, with the default
-    ring depth and a deeper one, with the fused FFN (key rows and value slices
-    per SM) and with the value projection as its own phase."""
+    ring depth and a deeper one, with the FFN value units in column-chunk
+    order (fixed-point sums, the default) and in row order."""
     shape, up, oracle = sg8_l4
     prompt = synth.seeded_prompt(4, shape.vocab, 29)
     ids_ref, logits_ref, state_ref = oracle.greedy(prompt, 4)
-    eng = B200Engine(up, ring_slots=ring, fused_ffn=fused)
+    eng = B200Engine(up, ring_slots=ring, ffn_chunk_order=chunk_order)
     try:
         assert eng.persistent_active
         ids, logits = eng.greedy(prompt, 4, keep_logits=True)

@@ -181,12 +181,12 @@ def test_engine_decode_matches_reference_forward(policy, path):
         eng.close()
 
 
-def test_engine_separate_ffn_phase_matches_reference_forward():
-    """The persistent kernel with the FFN value projection as its own phase
-    (the default fuses it into per-SM column slices): same ids, logits and
-    state as the reference forward."""
+def test_engine_ffn_row_order_matches_reference_forward():
+    """The persistent kernel with the FFN value units in row order and fp32
+    accumulation (the default orders them by column chunk and sums in fixed
+    point): same ids, logits and state as the reference forward."""
     gold, shape, pack = _reference_pack("sg8")
-    eng = B200Engine(pack, fused_ffn=False)
+    eng = B200Engine(pack, ffn_chunk_order=False)
     try:
         assert eng.persistent_active
         ids, logits = eng.greedy([int(t) for t in gold["prompt"]], len(gold["ids"]), keep_logits=True)
