@@ -61,10 +61,16 @@ constexpr int kDMaxItems = 8;          // adapter first-stage items per CTA
 constexpr int kDPartTiles = 8;         // GEMV tiles whose per-warp partial sums are buffered per CTA reduction
 constexpr uint32_t kDPartBytes = kDPartTiles * kDW * 16 * 4 + 128;  // the partial sums, then their tile indices
 constexpr int kDMaxPieces = 8;         // adapter second-stage tile pieces per layer
+constexpr int kDPieceSteps = 2;        // preload mode: 32-row k-steps per phase-B tensor-core task
+constexpr int kDMaxChunks = 16;        // preload mode: k-step chunks over the four adapters
 constexpr int kDMisc = 2560;           // misc shared floats
 static_assert((kDW / 2) * 4 * 64 <= kDMisc, "phase-B adapter partials [warps / 2][4][64] live in misc");
 static_assert(256 + 4 * kDT <= kDMisc, "adapter item inputs and row-group partials live in misc");
 constexpr int kMidPer = (2048 + kDT - 1) / kDT;  // first-adapter sums per consumer thread (rtot <= 2048)
+// Preload-mode phase B keeps in misc: x' and the min terms (rt floats each),
+// the digit blocks of the four adapters (3.25 bytes per row), the task
+// partials [4 nchunk][16], the adapter biases [4].
+__host__ __device__ constexpr int d_pieces_misc_floats(int rt, int nchunk) { return 2 * rt + rt * 13 / 16 + 64 * nchunk + 4; }
 constexpr float kFix = 4294967296.0f;  // 2^32 fixed-point scale of adapter partials
 constexpr float kUnfix = 1.0f / 4294967296.0f;
 
@@ -156,6 +162,11 @@ struct DArgs {
   // dedicated shared memory at the start of the layer instead of ring slots
   int pre;
   uint32_t o_adp, o_item, adp_b0, adp_b1;
+  // preload images of the adapter second stages, per adapter m (w, a, g, v):
+  // codes transposed, [64 columns][aps[m] bytes] (row = one output column,
+  // its apr[m] = rank rounded up to 32 codes, zero-padded), then the rows'
+  // (min, max) pair of pairs [apr[m]][16 B]
+  int aps[4], apr[4];
   // FFN value rows in column-chunk order with fixed-point accumulation (0:
   // row order, fp32 atomics)
   int ecm;
@@ -167,6 +178,9 @@ struct DTable {
   int item[kDMaxItems];
   int npc[2];     // adapter second-stage pieces: layer 0 (no v2), other layers; 0 unless a head CTA
   int pm[kDMaxPieces], pr0[kDMaxPieces];
+  // preload mode: phase B's k-step chunks (adapter, first k-step), v last
+  int nck[2];     // layer 0 (no v2), other layers
+  int ckm[kDMaxChunks], cks[kDMaxChunks];
   int zc0, zc1, zf0, zf1, z3c0, z3c1, zv0, zv1, zr0, zr1;  // zeroing slices (C, F, 3C, V, rtot)
   int ech0, ech1;  // chunk-ordered E: first and last column chunk of this CTA's units
 };
@@ -241,6 +255,19 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
       }
     }
     T.npc[1] = n;
+  }
+  {
+    int n = 0;
+    T.nck[0] = 0;
+    for (int m = 0; m < 4; ++m) {
+      if (m == 3) T.nck[0] = n;
+      for (int s0 = 0; s0 < a.apr[m] / 32 && n < kDMaxChunks; s0 += kDPieceSteps) {
+        T.ckm[n] = m;
+        T.cks[n] = s0;
+        ++n;
+      }
+    }
+    T.nck[1] = n;
   }
   d_split(C, G, bx, &T.zc0, &T.zc1);
   d_split(F, G, bx, &T.zf0, &T.zf1);
@@ -995,6 +1022,133 @@ __device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, 
   }
 }
 
+// Phase B, preload mode: the four adapter second stages of head h on the
+// integer tensor cores.  Output column c of adapter m is
+//     sum_r mid_r (q[r][c] d_r + min_r) = sum_r x'_r q[r][c] + sum_r mid_r min_r,
+// x'_r = mid_r d_r (d, min of row r's weight group, which holds all 64 columns
+// of the head): a GEMV whose activation x' is split into three digits per
+// 32-row flush group (emit_digits) and whose A operand is the transposed code
+// image ([64 columns][rank]).  Tasks (chunk of kDPieceSteps k-steps, 16-column
+// tile) go round-robin to the warps; partials are summed in chunk order.
+// Writes vec[m * 64 + c] for the layer's adapters; ends with the consumer
+// barrier.
+__device__ __noinline__ void d_pieces_mma(const DArgs& a, DCons& c, const DTable& T, int l, const float* mid,
+                                          float* misc, float* vec) {
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5, g = lane >> 2, tq = lane & 3, h = blockIdx.x;
+  const int nm = l == 0 ? 3 : 4, nck = T.nck[l == 0 ? 0 : 1];
+  d_pre_wait(a, c, &c.pbar[0], c.nadp);
+  const uint8_t* img = c.sm + a.o_adp;
+  uint32_t boff[4];
+  int roff[5];
+  {
+    uint32_t o = 0;
+    int r = 0;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      boff[m] = o;
+      roff[m] = r;
+      o += 64u * (uint32_t)a.aps[m] + 16u * (uint32_t)a.apr[m];
+      r += a.apr[m];
+    }
+    roff[4] = r;
+  }
+  const int rt = roff[4];
+  float* xp = misc;                                            // [rt] x'
+  float* bt = misc + rt;                                       // [rt] mid * min
+  uint8_t* dgb = reinterpret_cast<uint8_t*>(misc + 2 * rt);    // digit blocks, 3.25 bytes per row
+  float* part = misc + 2 * rt + rt * 13 / 16;                  // [4 nck][16]
+  float* bias = part + 64 * nck;                               // [4]
+  auto adapter_of = [&](int j) { return j >= roff[3] ? 3 : (j >= roff[2] ? 2 : (j >= roff[1] ? 1 : 0)); };
+  auto digits_of = [&](int m) {
+    XDigits X;
+    uint8_t* b = dgb + (size_t)roff[m] * 13 / 4;
+    X.xd = reinterpret_cast<uint2*>(b);
+    X.xc = reinterpret_cast<float*>(b + 3 * a.apr[m]);
+    X.xsum = X.xc + a.apr[m] / 32;
+    return X;
+  };
+  if (!c.dead) {
+#pragma unroll 1
+    for (int j = t; j < rt; j += kDT) {
+      const int m = adapter_of(j), r = j - roff[m];
+      float xv = 0.f, bv = 0.f;
+      if (m < nm && r < d_rank(a.d, m)) {
+        const int sel = ((h * 64) >> a.alg[m]) & 1;
+        const float2 pq = reinterpret_cast<const float2*>(img + boff[m] + 64u * (uint32_t)a.aps[m])[r * 2 + sel];
+        const float md = mid[d_rank_off(a.d, m) + r];
+        xv = md * __fmul_rn(__fsub_rn(pq.y, pq.x), kInv255);
+        bv = md * pq.x;
+      }
+      xp[j] = xv;
+      bt[j] = bv;
+    }
+  }
+  d_csync();
+  // digits of x' (8 rows per item, 32-row flush groups) and the min-term sums
+  const int nit = rt >> 3;
+  if (w * 32 < nit) {
+    const int it = w * 32 + lane;
+    const bool act = it < nit;
+    const int m = act ? adapter_of(it * 8) : 0;
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = act ? xp[it * 8 + u] : 0.f;
+    emit_digits(v, act ? it - roff[m] / 8 : 0, act, 0, digits_of(m));
+  }
+  if (w < nm) {
+    float sb = 0.f;
+    for (int j = roff[w] + lane; j < roff[w + 1]; j += 32) sb += bt[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    if (lane == 0) bias[w] = sb;
+  }
+  d_csync();
+#pragma unroll 1
+  for (int tau = w; !c.dead && tau < 4 * nck; tau += kDW) {
+    const int k = tau >> 2, tile = tau & 3, m = T.ckm[k], s0 = T.cks[k];
+    const int s1 = min(s0 + kDPieceSteps, a.apr[m] / 32);
+    const XDigits X = digits_of(m);
+    const uint8_t* rowa = img + boff[m] + (uint32_t)(tile * 16 + g) * (uint32_t)a.aps[m] + 8 * tq;
+    const uint8_t* rowb = rowa + 8 * a.aps[m];
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+    for (int ks = s0; ks < s1; ++ks) {
+      const uint2 w0 = *reinterpret_cast<const uint2*>(rowa + ks * 32);
+      const uint2 w1 = *reinterpret_cast<const uint2*>(rowb + ks * 32);
+      const uint2 bb = lane < 12 ? X.xd[ks * 12 + lane] : make_uint2(0u, 0u);
+      int d[4] = {0, 0, 0, 0};
+      imma_16832(d, w0.x, w1.x, w0.y, w1.y, bb.x, bb.y);
+      if (tq < 2) {
+        const float cs = X.xc[ks];
+        if (tq == 0) {
+          acc0 = fmaf(cs, fmaf((float)d[1], kInv254, (float)d[0]), acc0);
+          acc1 = fmaf(cs, fmaf((float)d[3], kInv254, (float)d[2]), acc1);
+        } else {
+          acc0 = fmaf(cs * kInv254sq, (float)d[0], acc0);
+          acc1 = fmaf(cs * kInv254sq, (float)d[2], acc1);
+        }
+      }
+    }
+    acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
+    acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
+    if (tq == 0) {
+      part[tau * 16 + g] = acc0;
+      part[tau * 16 + g + 8] = acc1;
+    }
+  }
+  d_csync();
+  if (t < 256) {
+    const int m = t >> 6, cc = t & 63, tile = cc >> 4, r = cc & 15;
+    if (m < nm) {
+      float sacc = bias[m];
+      for (int k = 0; k < nck; ++k)
+        if (T.ckm[k] == m) sacc += part[(k * 4 + tile) * 16 + r];
+      vec[m * 64 + cc] = sacc;
+    }
+  }
+  d_csync();
+}
+
 // Phase B for head h = blockIdx.x: adapter second stages, kk-normalize, decay,
 // WKV7 update of S (already in shared memory), GroupNorm, bonus, gate.
 __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& T, int l, float* S, float* misc) {
@@ -1053,7 +1207,11 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
   float* vp = misc;  // [kDW / 2 warp pairs][4 matrices][64 columns] partials
   cp_async_wait_all();
   d_csync();
-  {
+  if (a.pre) {
+    d_pieces_mma(a, c, T, l, mid, misc, vec);
+    if (t == 0) mbar_arrive(&c.pbar[1]);  // the head image buffer may be refilled
+    ++c.nadp;
+  } else {
     // 16 lanes per tile row, 4 columns each (one 32-bit code word); the two
     // half-warps take alternate rows: row phase rp of 20.  Per row the scale
     // is folded into the input: mid * (q * d + mn) = (mid * d) * q + mid * mn.
@@ -1063,20 +1221,12 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
     for (int mm = 0; mm < 4; ++mm)
 #pragma unroll
       for (int u = 0; u < 5; ++u) acc4[mm][u] = 0.f;
-    if (a.pre) d_pre_wait(a, c, &c.pbar[0], c.nadp);
-    uint32_t img_off = 0;  // preload mode: offset of adapter m's block in the head's image
-    const int npc = a.pre ? nm : T.npc[l == 0 ? 0 : 1];
+    const int npc = T.npc[l == 0 ? 0 : 1];
     for (int pc = 0; pc < npc; ++pc) {
-      const uint8_t* sl;
-      if (a.pre) {
-        sl = c.sm + a.o_adp + img_off;
-        img_off += 80u * (uint32_t)d_rank(a.d, pc);
-      } else {
-        sl = d_slot_wait(a, c);
-      }
+      const uint8_t* sl = d_slot_wait(a, c);
       if (!c.dead) {
-        const int m = a.pre ? pc : T.pm[pc];
-        const int br = a.pre ? d_rank(a.d, m) : a.abr[m], r0 = a.pre ? 0 : T.pr0[pc];
+        const int m = T.pm[pc];
+        const int br = a.abr[m], r0 = T.pr0[pc];
         const int nr = min(br, d_rank(a.d, m) - r0);
         const float2* pairs = reinterpret_cast<const float2*>(sl + br * 64);
         const int sel = ((h * 64) >> a.alg[m]) & 1;
@@ -1111,7 +1261,7 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
             acc4[mm][4] += bs;
           }
       }
-      if (!a.pre) d_slot_release(a, c);
+      d_slot_release(a, c);
     }
     // fixed-order fold of the warps' partials: warp w + kDW/2 stores, warp w adds
     // its own, then the sum over the kDW/2 pairs (below) in pair order
@@ -1134,20 +1284,16 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
         v4.w += acc4[mm][3] + acc4[mm][4];
         *dst = v4;
       }
+    d_csync();
+    if (t < 256) {
+      const int m = t >> 6, cc = t & 63;
+      float s = 0.f;
+      if (m < nm)
+        for (int q = 0; q < kDW / 2; ++q) s += vp[(q * 4 + m) * 64 + cc];
+      vec[m * 64 + cc] = s;
+    }
+    d_csync();
   }
-  d_csync();
-  if (a.pre) {
-    if (t == 0) mbar_arrive(&c.pbar[1]);  // the head image buffer may be refilled
-    ++c.nadp;
-  }
-  if (t < 256) {
-    const int m = t >> 6, cc = t & 63;
-    float s = 0.f;
-    if (m < nm)
-      for (int q = 0; q < kDW / 2; ++q) s += vp[(q * 4 + m) * 64 + cc];
-    vec[m * 64 + cc] = s;
-  }
-  d_csync();
   const float kkv = t < 64 ? k * kk_w : 0.f;
   const float nrm = sqrtf(d_csum(kkv * kkv, c.red));
   if (t < 64) {

@@ -926,21 +926,22 @@ __global__ void stream_layout_kernel(uint8_t* dst, PackedView w, int nb, int pr,
 
 // Phase-B adapter images of one adapter second stage W2 [R][C] (SG8, group
 // 2^lg >= 64): for every head h (one block each) the block at
-// dst + h * img_b + off holds the R rows of columns [64 h, 64 h + 64), then per
-// row the two (min, max) pairs of the even-aligned group pair around them
-// ([R][64] codes, [R][16 B] pairs).
-__global__ void adp_image_kernel(uint8_t* dst, PackedView w, uint32_t img_b, uint32_t off) {
+// dst + h * img_b + off holds the head's columns [64 h, 64 h + 64) transposed,
+// [64][stride] codes (column c's R codes, zero up to stride), then per row r <
+// rpad the two (min, max) pairs of the even-aligned group pair around the
+// columns ([rpad][16 B], zero past R).  Transposed so that the column is the
+// row of an integer-mma A operand and the rank the k dimension.
+__global__ void adp_image_kernel(uint8_t* dst, PackedView w, uint32_t img_b, uint32_t off, int stride, int rpad) {
   const int h = blockIdx.x, R = w.rows, C = w.cols;
   uint8_t* out = dst + (size_t)h * img_b + off;
-  for (int i = threadIdx.x; i < R * 4; i += blockDim.x) {
-    const int r = i >> 2, q = i & 3;
-    *reinterpret_cast<uint4*>(out + r * 64 + q * 16) =
-        *reinterpret_cast<const uint4*>(w.payload + (size_t)r * C + h * 64 + q * 16);
+  for (int i = threadIdx.x; i < 64 * stride; i += blockDim.x) {
+    const int c = i / stride, r = i - c * stride;
+    out[i] = r < R ? w.payload[(size_t)r * C + h * 64 + c] : (uint8_t)0;
   }
   const int gpr = C >> w.lg, px = ((h * 64) >> w.lg) & ~1;
-  for (int r = threadIdx.x; r < R; r += blockDim.x)
-    *reinterpret_cast<uint4*>(out + (size_t)R * 64 + r * 16) =
-        *reinterpret_cast<const uint4*>(w.meta + ((size_t)r * gpr + px) * 8);
+  uint4* pd = reinterpret_cast<uint4*>(out + (size_t)64 * stride);
+  for (int r = threadIdx.x; r < rpad; r += blockDim.x)
+    pd[r] = r < R ? *reinterpret_cast<const uint4*>(w.meta + ((size_t)r * gpr + px) * 8) : make_uint4(0u, 0u, 0u, 0u);
 }
 
 uint64_t stream_units(const PackedView& w, int kc) { return (uint64_t)((w.rows + 15) / 16) * (uint64_t)(w.cols / kc); }
@@ -990,8 +991,8 @@ void plan_stream_copy(rwkvb_engine* e, std::vector<DLayerMaps>& hm, bool pre) {
       const PackedView* w2[4] = {&l.w2, &l.a2, &l.g2, &l.v2};
       uint32_t off = 0;
       for (int m = 0; m < (i == 0 ? 3 : 4); ++m) {
-        adp_image_kernel<<<e->d.H, 256>>>(cur, *w2[m], ib, off);
-        off += 80u * (uint32_t)w2[m]->rows;
+        adp_image_kernel<<<e->d.H, 256>>>(cur, *w2[m], ib, off, a.aps[m], a.apr[m]);
+        off += 64u * (uint32_t)a.aps[m] + 16u * (uint32_t)a.apr[m];
       }
       hm[i].ai = cur;
       cur += (size_t)e->d.H * ib;
@@ -1102,7 +1103,21 @@ bool plan_decode(rwkvb_engine* e) {
   auto set_bytes = [&](int K) { return ((uint32_t)K * 3u + 2u * (uint32_t)(K / a.fg) * 4u + 15u) & ~15u; };
   a.dig_set = set_bytes(d.C);
   uint32_t dig = 3u * a.dig_set;
-  dig = dig > set_bytes(d.F) ? dig : set_bytes(d.F);
+  // phase E's digits: the whole FFN width in row order; in chunk order only
+  // the widest chunk span of one CTA's units
+  a.ecm = (e->flags & 0x10000u) ? 0 : 1;  // bit 16: FFN value rows in row order, fp32 accumulation
+  int kl = d.F;
+  if (a.ecm) {
+    const int tiles = d.C / 16, U = tiles * (d.F / a.kc);
+    kl = 0;
+    for (int b = 0; b < e->sms; ++b) {
+      const int u0 = (int)((unsigned)U * (unsigned)b / (unsigned)e->sms);
+      const int u1 = (int)((unsigned)U * (unsigned)(b + 1) / (unsigned)e->sms);
+      const int span = u1 > u0 ? ((u1 - 1) / tiles - u0 / tiles + 1) * a.kc : 0;
+      kl = span > kl ? span : kl;
+    }
+  }
+  dig = dig > set_bytes(kl) ? dig : set_bytes(kl);
   const uint32_t wkv = (uint32_t)(4096 + ((d.rtot + 3) & ~3) + 256 + 7 * 64) * 4u;
   dig = dig > wkv ? dig : wkv;
   dig = (dig + 127u) & ~127u;
@@ -1131,11 +1146,24 @@ bool plan_decode(rwkvb_engine* e) {
   // rank row) and the CTA's adapter first-stage item get dedicated shared
   // memory, loaded at the start of each layer, when both fit beside the ring
   // and no CTA has more than one item (bit 11 of the flags turns it off).
-  a.adp_b0 = 80u * (uint32_t)(d.rw + d.ra + d.rg);
-  a.adp_b1 = 80u * (uint32_t)(d.L > 1 ? d.rtot : d.rw + d.ra + d.rg);
+  // transposed images: rank padded to whole 32-code k-steps, column stride
+  // = 32 mod 64 bytes (the eight columns of one fragment load on distinct banks)
+  uint32_t blk[4];
+  int rt = 0, nchunk = 0;
+  for (int m = 0; m < 4; ++m) {
+    a.apr[m] = (ranks[m] + 31) / 32 * 32;
+    a.aps[m] = a.apr[m] + ((32 - a.apr[m] % 64) + 64) % 64;
+    blk[m] = 64u * (uint32_t)a.aps[m] + 16u * (uint32_t)a.apr[m];
+    rt += a.apr[m];
+    nchunk += (a.apr[m] / 32 + kDPieceSteps - 1) / kDPieceSteps;
+  }
+  a.adp_b0 = blk[0] + blk[1] + blk[2];
+  a.adp_b1 = d.L > 1 ? a.adp_b0 + blk[3] : a.adp_b0;
   const uint32_t adp_buf = ((a.adp_b1 > a.adp_b0 ? a.adp_b1 : a.adp_b0) + 127u) & ~127u;
+  // phase B's tensor-core pieces keep x', its digits and the piece partials in misc
+  const bool pieces_fit = nchunk <= kDMaxChunks && d_pieces_misc_floats(rt, nchunk) <= kDMisc;
   const bool want_pre = !(e->flags & 0x400u) && !(e->flags & 0x800u) && e->d.abase[4] <= e->sms &&
-                        off + adp_buf + a.slot <= budget;
+                        pieces_fit && off + adp_buf + a.slot <= budget;
   if (want_pre) {
     a.o_adp = off;  off += adp_buf;
     a.o_item = off; off += a.slot;
@@ -1177,7 +1205,6 @@ bool plan_decode(rwkvb_engine* e) {
   a.d = d;
   a.spin_limit = 1u << 22;
   a.l2_first = (e->flags & 0x200u) ? 0 : 1;  // bit 9: plain weight-stream loads (no L2 policy)
-  a.ecm = (e->flags & 0x10000u) ? 0 : 1;     // bit 16: FFN value rows in row order, fp32 accumulation
   const PackedView& E = e->emb;
   a.emb_fast = E.kind == RWKVB_KIND_SG8 && E.lg >= 4 && d.C % (int)E.group == 0 && ((d.C >> E.lg) % 2) == 0 &&
                aligned16(E.payload) && aligned16(E.meta);
