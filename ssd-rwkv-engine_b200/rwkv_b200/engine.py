@@ -136,7 +136,8 @@ class B200Engine:
 
     def __init__(self, pack, *, device: int | torch.device = 0, use_graph: bool = True,
                  prefetch_distance: int | None = None, persistent: bool = True, trace: bool = False,
-                 l2_policy: bool = True, ring_slots: int | None = None, ffn_chunk_order: bool = True):
+                 l2_policy: bool = True, ring_slots: int | None = None, ffn_chunk_order: bool = True,
+                 extra_flags: int = 0):
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("B200Engine needs a CUDA device; there is no CPU path")
@@ -158,6 +159,7 @@ class B200Engine:
                 flags |= (int(ring_slots) & 0xF) << native.FLAG_RING_SLOTS_SHIFT
             if not ffn_chunk_order:
                 flags |= native.FLAG_FFN_ROW_ORDER
+            flags |= int(extra_flags)  # further rwkvb_engine_create flag bits (include/rwkv_b200.h)
             h = ctypes.c_void_p()
             if self._model.stage is not None:
                 # streamed layers: the multi-kernel step with the staging copies in it
