@@ -152,7 +152,7 @@ __device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, const Bg
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
+__global__ void __maxnreg__(112) bgemm_kernel(const __grid_constant__ BgArgs a) {
   extern __shared__ __align__(1024) uint8_t bg_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bg_smem_raw) + 1023) & ~uintptr_t(1023));
   const int stage_bytes = kBgTileBytes + a.nrows * 128;
@@ -322,12 +322,14 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
       uint64_t acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0ull;
-      // (min, max) of this row's flush groups, loaded one group ahead
+      // (min, max) of this row's flush groups, loaded two groups ahead
       const int g_end = sg.s1 * nfl;
       float2 pr_a = __ldg(prow + sg.s0 * nfl);
+      float2 pr_b = sg.s0 * nfl + 1 < g_end ? __ldg(prow + sg.s0 * nfl + 1) : make_float2(0.f, 0.f);
       for (int g = sg.s0 * nfl; g < g_end; ++g, ++fl) {
         const float2 pr = pr_a;
-        if (g + 1 < g_end) pr_a = __ldg(prow + g + 1);
+        pr_a = pr_b;
+        if (g + 2 < g_end) pr_b = __ldg(prow + g + 2);
         const uint32_t tb = fl & 1;
         if (!bg_wait(&tfull[tb], (fl >> 1) & 1, a, &s_abort)) goto epi_done;
         tc_fence_after();
@@ -347,18 +349,22 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
             const uint32_t co = (uint32_t)(ch * 16 + hf * 8);
             uint32_t d0[8], d1[8], d2[8];
             tmem_ld8x3_sync(ta + co, ta + a.bp + co, ta + 2 * a.bp + co, d0, d1, d2);
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-              const int sp = hf * 4 + s;  // session pair
-              const uint64_t c2 = *reinterpret_cast<const uint64_t*>(cg + 2 * sp);
-              const uint64_t x2 = *reinterpret_cast<const uint64_t*>(cg + a.bp + 2 * sp);
-              const uint64_t f0 = fadd2(fx2(__int_as_float(d0[2 * s]), __int_as_float(d0[2 * s + 1])), nk2);
-              const uint64_t f1 = fadd2(fx2(__int_as_float(d1[2 * s]), __int_as_float(d1[2 * s + 1])), nk2);
-              const uint64_t f2 = fadd2(fx2(__int_as_float(d2[2 * s]), __int_as_float(d2[2 * s + 1])), nk2);
-              const uint64_t t = ffma2(ffma2(f2, inv254, f1), inv254, f0);
-              acc[sp] = ffma2(fmul2(dg2, c2), t, ffma2(mn2, x2, acc[sp]));
-            }
             tmem_fill8x3(ta + co, ta + a.bp + co, ta + 2 * a.bp + co, kBgArm);  // re-arm for the next group
+#pragma unroll
+            for (int s2 = 0; s2 < 2; ++s2) {  // four sessions per 16-byte load of c_f and of sum_x
+              const ulonglong2 c4 = __ldg(reinterpret_cast<const ulonglong2*>(cg + hf * 8 + s2 * 4));
+              const ulonglong2 x4 = __ldg(reinterpret_cast<const ulonglong2*>(cg + a.bp + hf * 8 + s2 * 4));
+#pragma unroll
+              for (int s1 = 0; s1 < 2; ++s1) {
+                const int s = s2 * 2 + s1, sp = hf * 4 + s;  // session pair
+                const uint64_t c2 = s1 ? c4.y : c4.x, x2 = s1 ? x4.y : x4.x;
+                const uint64_t f0 = fadd2(fx2(__int_as_float(d0[2 * s]), __int_as_float(d0[2 * s + 1])), nk2);
+                const uint64_t f1 = fadd2(fx2(__int_as_float(d1[2 * s]), __int_as_float(d1[2 * s + 1])), nk2);
+                const uint64_t f2 = fadd2(fx2(__int_as_float(d2[2 * s]), __int_as_float(d2[2 * s + 1])), nk2);
+                const uint64_t t = ffma2(ffma2(f2, inv254, f1), inv254, f0);
+                acc[sp] = ffma2(fmul2(dg2, c2), t, ffma2(mn2, x2, acc[sp]));
+              }
+            }
           }
           tmem_wait_st();
         }
