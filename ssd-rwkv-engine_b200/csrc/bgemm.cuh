@@ -16,12 +16,8 @@
 //     min * sum_x + d * c_f * (D0 + D1/254 + D2/254^2),   d = (max - min) / 255
 // which is the per-group algebra of the reference's SG8 row dot
 // (rwkv_ssd/native/lut2_gather.c:344-381) for every session at once.
-// The digit accumulators start every flush group at the bit pattern of 2^23
-// (the epilogue stores it back after reading them) and the MMA always
-// accumulates, so a column holds the bits of the float 2^23 + D'_i exactly
-// (D'_i < 2^23); with Q from the ones row (kept as a running total, read as
-// the difference from the group before) one packed float subtract of
-// 2^23 + 127 Q gives D_i, exactly (|D_i| < 2^22).
+// |D_i| <= 128 * 255 * 127 < 2^22, so a D_i becomes a float exactly through
+// the 1.5 * 2^23 bias (one integer add and one float subtract).
 //
 // Work split: the (tile, 128-column stage) pairs of all matrices of a launch
 // are numbered in order and every CTA takes a contiguous, equal share, so
@@ -79,7 +75,8 @@ constexpr int kBgTileBytes = 128 * 128;  // A stage: 128 rows x 128 codes
 constexpr int kBgTmemCols = 512;
 constexpr int kBgAccStride = 256;        // TMEM columns between the two accumulators
 constexpr int kBgMaxStages = 6;
-constexpr uint32_t kBgArm = 0x4B000000u;  // bits of 2^23: the digit accumulators' start value
+constexpr int kBgBias = 0x4B400000;      // bits of 1.5 * 2^23
+constexpr float kBgBiasF = 12582912.0f;  // 1.5 * 2^23
 
 struct BgMat {
   const float2* pairs;  // (min, max) per (row, group): [rows][k / group]
@@ -152,7 +149,7 @@ __device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, const Bg
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__global__ void __maxnreg__(112) bgemm_kernel(const __grid_constant__ BgArgs a) {
+__global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
   extern __shared__ __align__(1024) uint8_t bg_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(bg_smem_raw) + 1023) & ~uintptr_t(1023));
   const int stage_bytes = kBgTileBytes + a.nrows * 128;
@@ -185,26 +182,6 @@ __global__ void __maxnreg__(112) bgemm_kernel(const __grid_constant__ BgArgs a) 
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = s_tbase;
-  if (warp >= 2) {
-    // arm both accumulators: digit columns at 2^23, the ones-row column (Q, a
-    // running total per accumulator) at 0
-    const int q4 = warp & 3, ch = (warp - 2) >> 2;
-    if (ch < (a.bp >> 4)) {
-      const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16);
-      for (int tb = 0; tb < 2; ++tb) {
-        const uint32_t ta = tl + tb * kBgAccStride;
-        for (int hf = 0; hf < 2; ++hf) {
-          const uint32_t co = (uint32_t)(ch * 16 + hf * 8);
-          tmem_fill8x3(ta + co, ta + a.bp + co, ta + 2 * a.bp + co, kBgArm);
-        }
-        if (ch == 0) tmem_fill1(ta + 3 * a.bp, 0u);
-      }
-      tmem_wait_st();
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -281,7 +258,7 @@ __global__ void __maxnreg__(112) bgemm_kernel(const __grid_constant__ BgArgs a) 
             const uint32_t dt = tbase + tb * kBgAccStride;
             for (int j = 0; j < kpf; ++j) {
               const uint32_t ko = (uint32_t)((f * kpf + j) * 32);
-              umma_u8(dt, sdesc_k128(sa + ko), sdesc_k128(sb + ko), a.idesc, 1u);  // onto the armed values
+              umma_u8(dt, sdesc_k128(sa + ko), sdesc_k128(sb + ko), a.idesc, j > 0 ? 1u : 0u);
             }
             umma_commit(&tfull[tb]);
           }
@@ -308,8 +285,7 @@ __global__ void __maxnreg__(112) bgemm_kernel(const __grid_constant__ BgArgs a) 
     const int q4 = warp & 3, ch = (warp - 2) >> 2;
     const bool active = ch < (a.bp >> 4);
     const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16);
-    const uint64_t inv254 = fx2(kInv254, kInv254);
-    int qp0 = 0, qp1 = 0;  // running totals of the ones-row column per accumulator
+    const uint64_t neg_bias = fx2(-kBgBiasF, -kBgBiasF), inv254 = fx2(kInv254, kInv254);
     uint32_t fl = 0;
     for (int x = lo; x < hi;) {
       const BgSeg sg = bg_segment(a, x, hi);
@@ -335,12 +311,8 @@ __global__ void __maxnreg__(112) bgemm_kernel(const __grid_constant__ BgArgs a) 
         tc_fence_after();
         if (active) {
           const uint32_t ta = tl + tb * kBgAccStride;
-          const int qt = (int)tmem_ld1_sync(ta + 3 * a.bp);
-          const int q = qt - (tb ? qp1 : qp0);
-          if (tb) qp1 = qt;
-          else qp0 = qt;
-          const float kq = __int_as_float((int)kBgArm + 127 * q);  // 2^23 + 127 Q, exact
-          const uint64_t nk2 = fx2(-kq, -kq);
+          const int q = (int)tmem_ld1_sync(ta + 3 * a.bp);
+          const int kq = kBgBias - 127 * q;
           const float dg = (pr.y - pr.x) * kInv255;
           const uint64_t dg2 = fx2(dg, dg), mn2 = fx2(pr.x, pr.x);
           const float* cg = csm + (size_t)g * 2 * a.bp;  // c_f of the chunk's sessions; sum_x at + bp
@@ -349,24 +321,21 @@ __global__ void __maxnreg__(112) bgemm_kernel(const __grid_constant__ BgArgs a) 
             const uint32_t co = (uint32_t)(ch * 16 + hf * 8);
             uint32_t d0[8], d1[8], d2[8];
             tmem_ld8x3_sync(ta + co, ta + a.bp + co, ta + 2 * a.bp + co, d0, d1, d2);
-            tmem_fill8x3(ta + co, ta + a.bp + co, ta + 2 * a.bp + co, kBgArm);  // re-arm for the next group
 #pragma unroll
-            for (int s2 = 0; s2 < 2; ++s2) {  // four sessions per 16-byte load of c_f and of sum_x
-              const ulonglong2 c4 = __ldg(reinterpret_cast<const ulonglong2*>(cg + hf * 8 + s2 * 4));
-              const ulonglong2 x4 = __ldg(reinterpret_cast<const ulonglong2*>(cg + a.bp + hf * 8 + s2 * 4));
-#pragma unroll
-              for (int s1 = 0; s1 < 2; ++s1) {
-                const int s = s2 * 2 + s1, sp = hf * 4 + s;  // session pair
-                const uint64_t c2 = s1 ? c4.y : c4.x, x2 = s1 ? x4.y : x4.x;
-                const uint64_t f0 = fadd2(fx2(__int_as_float(d0[2 * s]), __int_as_float(d0[2 * s + 1])), nk2);
-                const uint64_t f1 = fadd2(fx2(__int_as_float(d1[2 * s]), __int_as_float(d1[2 * s + 1])), nk2);
-                const uint64_t f2 = fadd2(fx2(__int_as_float(d2[2 * s]), __int_as_float(d2[2 * s + 1])), nk2);
-                const uint64_t t = ffma2(ffma2(f2, inv254, f1), inv254, f0);
-                acc[sp] = ffma2(fmul2(dg2, c2), t, ffma2(mn2, x2, acc[sp]));
-              }
+            for (int s = 0; s < 4; ++s) {
+              const int sp = hf * 4 + s;  // session pair
+              const uint64_t c2 = *reinterpret_cast<const uint64_t*>(cg + 2 * sp);
+              const uint64_t x2 = *reinterpret_cast<const uint64_t*>(cg + a.bp + 2 * sp);
+              const uint64_t f0 = fadd2(
+                  fx2(__int_as_float((int)d0[2 * s] + kq), __int_as_float((int)d0[2 * s + 1] + kq)), neg_bias);
+              const uint64_t f1 = fadd2(
+                  fx2(__int_as_float((int)d1[2 * s] + kq), __int_as_float((int)d1[2 * s + 1] + kq)), neg_bias);
+              const uint64_t f2 = fadd2(
+                  fx2(__int_as_float((int)d2[2 * s] + kq), __int_as_float((int)d2[2 * s + 1] + kq)), neg_bias);
+              const uint64_t t = ffma2(ffma2(f2, inv254, f1), inv254, f0);
+              acc[sp] = ffma2(fmul2(dg2, c2), t, ffma2(mn2, x2, acc[sp]));
             }
           }
-          tmem_wait_st();
         }
         tc_fence_before();
         __syncwarp();

@@ -105,21 +105,6 @@ __device__ __forceinline__ void tmem_ld8x3_sync(uint32_t t0, uint32_t t1, uint32
       : "memory");
 }
 
-// TMEM stores of one 32-bit value into every lane of 8 columns at t0, t1 and t2
-// (and one column), then the stores' completion wait.
-__device__ __forceinline__ void tmem_fill8x3(uint32_t t0, uint32_t t1, uint32_t t2, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%3,%3,%3,%3,%3,%3,%3,%3};\n"
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%1], {%3,%3,%3,%3,%3,%3,%3,%3};\n"
-      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%2], {%3,%3,%3,%3,%3,%3,%3,%3};\n" ::"r"(t0),
-      "r"(t1), "r"(t2), "r"(v)
-      : "memory");
-}
-__device__ __forceinline__ void tmem_fill1(uint32_t t, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};\n" ::"r"(t), "r"(v) : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 // Three 16-column loads (columns t0.., t1.., t2..) and one wait.
 __device__ __forceinline__ void tmem_ld16x3_sync(uint32_t t0, uint32_t t1, uint32_t t2, uint32_t (&a)[16],
                                                  uint32_t (&b)[16], uint32_t (&c)[16]) {
