@@ -183,8 +183,6 @@ struct DTable {
   int ckm[kDMaxChunks], cks[kDMaxChunks];
   int zc0, zc1, zf0, zf1, z3c0, z3c1, zv0, zv1, zr0, zr1;  // zeroing slices (C, F, 3C, V, rtot)
   int ech0, ech1;  // chunk-ordered E: first and last column chunk of this CTA's units
-  int cch0, cch1;  // chunk-ordered C: the same for the output projection
-  uint32_t aneed;  // chunk-ordered A: bit (m * chunks + c) = this CTA has units of matrix m (r, k, v) in chunk c
 };
 
 // [a, b) = part i of [0, n) split into `parts` (n * parts < 2^32).
@@ -224,22 +222,8 @@ __device__ __forceinline__ int d_rank_off(const Dims& d, int m) {
 __device__ void d_build_table(const DArgs& a, DTable& T) {
   const int G = gridDim.x, bx = blockIdx.x, C = a.d.C, F = a.d.F;
   const int nc = C / a.kc, nf = F / a.kc;
-  const int ct = C / 16;
-  T.aneed = 0xffffffffu;
-  T.cch0 = 0;
-  T.cch1 = nc - 1;
-  if (a.ecm) {  // chunk order for r/k/v and the output projection too
-    T.r[0].nch = T.r[1].nch = nc;
-    d_split(3 * ct * nc, G, bx, &T.r[0].u0, &T.r[0].u1);
-    T.aneed = 0u;
-    for (int u = T.r[0].u0; u < T.r[0].u1; ++u) T.aneed |= 1u << (u / ct);  // u / ct = m * nc + chunk
-    d_split(ct * nc, G, bx, &T.r[1].u0, &T.r[1].u1);
-    T.cch0 = T.r[1].u0 / ct;
-    T.cch1 = T.r[1].u1 > T.r[1].u0 ? (T.r[1].u1 - 1) / ct : T.cch0;
-  } else {
-    d_range(3 * ct, nc, G, bx, T.r[0]);
-    d_range(ct, nc, G, bx, T.r[1]);
-  }
+  d_range(3 * C / 16, nc, G, bx, T.r[0]);
+  d_range(C / 16, nc, G, bx, T.r[1]);
   d_range(F / 16, nc, G, bx, T.r[2]);
   if (a.ecm) {  // chunk order: equal contiguous shares of the chunk-major unit numbering
     T.r[3].nch = nf;
@@ -353,22 +337,9 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
   int seq = seq_io;
   const bool hint = a.l2_first != 0;
   const uint64_t pol = l2_evict_first();
-  // unit u: (tile, chunk) = (u / nch, u % nch), or in chunk order (tiles_cm
-  // tiles per matrix): matrix u / (nch tiles_cm), then chunk, then tile
-  int tile, chunk, mi, row0;
-  if (tiles_cm) {
-    mi = u0 / (nch * tiles_cm);
-    const int rem = u0 - mi * nch * tiles_cm;
-    chunk = rem / tiles_cm;
-    row0 = (rem - chunk * tiles_cm) * 16;
-    tile = mi * tiles_cm + row0 / 16;
-    if (!per_map) mi = 0;
-  } else {
-    tile = u0 / nch;
-    chunk = u0 - tile * nch;
-    mi = per_map ? tile / per_map : 0;
-    row0 = (tile - mi * per_map) * 16;
-  }
+  // unit u: (tile, chunk) = (u / nch, u % nch), or chunk-major (u % tiles_cm, u / tiles_cm)
+  int tile = tiles_cm ? u0 % tiles_cm : u0 / nch, chunk = tiles_cm ? u0 / tiles_cm : u0 - tile * nch;
+  int mi = per_map ? tile / per_map : 0, row0 = (tile - mi * per_map) * 16;
   bool ok = true;
 #pragma unroll 1
   for (int u = u0; u < u1; ++u) {
@@ -405,15 +376,10 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     ++seq;
     if (tiles_cm) {
       row0 += 16;
-      ++tile;
-      if (row0 == tiles_cm * 16) {  // next chunk of the same matrix, or the next matrix
+      if (++tile == tiles_cm) {
+        tile = 0;
         row0 = 0;
-        tile -= tiles_cm;
-        if (++chunk == nch) {
-          chunk = 0;
-          tile += tiles_cm;
-          if (per_map) ++mi;
-        }
+        ++chunk;
       }
     } else if (++chunk == nch) {
       chunk = 0;
@@ -529,7 +495,7 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
             }
           }
         }
-        if (ok) ok = units(T.r[0], M.q, M.p, ct, M.su[0], a.ecm ? ct : 0);
+        if (ok) ok = units(T.r[0], M.q, M.p, ct, M.su[0]);
         for (int k = 0; ok && !a.pre && k < T.nitem[l == 0 ? 0 : 1]; ++k) {
           const int item = T.item[k];
           const int m = d_item_mat(a.d, item);
@@ -573,7 +539,7 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
             issued();
           }
         }
-        if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0, M.su[1], a.ecm ? ct : 0);
+        if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0, M.su[1]);
         if (ok) ok = units(T.r[2], M.q + 4, M.p + 4, 0, M.su[2]);
         if (ok) ok = units(T.r[3], M.q + 5, M.p + 5, 0, M.su[3], a.ecm ? C / 16 : 0);
       }
@@ -782,8 +748,6 @@ struct DLnMix {
   float* pv;           // shared copy of prev (nullptr: not kept)
   const float* mix[3];  // token-shift mixes (global), one digit set each
   int nmix;
-  uint32_t need;  // bit (m * chunks + chunk): emit the digits of mix m in that column chunk
-  int kc;         // columns per chunk
   float* ln;     // shared LayerNorm output
   float* stat;   // mean, rstd (nullptr: not kept)
 };
@@ -839,15 +803,13 @@ __device__ __noinline__ void d_ln_mix(const DArgs& a, DCons& c, const DLnMix& q,
     q.stat[0] = mean;
     q.stat[1] = rstd;
   }
-  const int nck = C / q.kc, mych = i0 / q.kc;
 #pragma unroll
   for (int m = 0; m < 3; ++m) {
-    const bool mine = act && ((q.need >> (m * nck + mych)) & 1u);
-    if (m < q.nmix && __any_sync(0xffffffffu, mine)) {  // warp-uniform: the shuffles need the whole warp
+    if (m < q.nmix) {
       float v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) v[u] = q.prev ? y[u] + (pv[u] - y[u]) * mx[m][u] : y[u];
-      emit_digits(v, t, mine, LFK, d_digits_at(dig + (size_t)m * stride, C, LFK));
+      emit_digits(v, t, act, LFK, d_digits_at(dig + (size_t)m * stride, C, LFK));
     }
   }
   d_csync();
@@ -909,15 +871,7 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
   float acc0 = 0.f, acc1 = 0.f;
   int cur_set = -1;
   XDigits X{};
-  int tile, chunk;  // global tile (matrices back to back) and column chunk of unit u
-  if (tiles_cm) {
-    const int mat = u0 / (nch * tiles_cm), rem = u0 - mat * nch * tiles_cm;
-    chunk = rem / tiles_cm;
-    tile = mat * tiles_cm + rem - chunk * tiles_cm;
-  } else {
-    tile = u0 / nch;
-    chunk = u0 - tile * nch;
-  }
+  int tile = tiles_cm ? u0 % tiles_cm : u0 / nch, chunk = tiles_cm ? u0 / tiles_cm : u0 - tile * nch;
   int nt = 0;  // tiles buffered in `part`
   int* ptile = reinterpret_cast<int*>(part + kDPartTiles * kDW * 16);  // their tile indices
 #pragma unroll 1
@@ -983,12 +937,9 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
       }
     }
     if (tiles_cm) {
-      if (++tile % tiles_cm == 0) {  // end of a chunk of this matrix
-        tile -= tiles_cm;
-        if (++chunk == nch) {
-          chunk = 0;
-          tile += tiles_cm;
-        }
+      if (++tile == tiles_cm) {
+        tile = 0;
+        ++chunk;
       }
     } else if (++chunk == nch) {
       chunk = 0;
@@ -1581,8 +1532,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.mix[1] = Ly.x_k;
         q.mix[2] = Ly.x_v;
         q.nmix = 3;
-        q.need = T.aneed;  // chunk order: only the (matrix, chunk) pairs of this CTA's units
-        q.kc = a.kc;
         q.ln = TV;
         q.stat = s_stat;
         d_ln_mix<LFK>(a, c, q, dig, a.dig_set);
@@ -1601,7 +1550,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         d_build<LFK>(DSrc{0, TV, PV, Ly.x_v}, C, dig + 2 * a.dig_set);
       }
       d_mark(a, c);  // A prep done
-      d_units<LFK>(a, c, T.r[0], dig, a.dig_set, C, C / 16, acc_rkv, 3 * C, ecm ? C / 16 : 0);
+      d_units<LFK>(a, c, T.r[0], dig, a.dig_set, C, C / 16, acc_rkv, 3 * C);
       d_mark(a, c);  // A units done
       d_items(a, c, T, l, TV, PV, misc);
       d_mark(a, c);  // A done
@@ -1638,13 +1587,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
         a.b.att_x[(size_t)l * C + i] = TV[i];  // ln1 output of phase A, still in shared memory
-      {
-        // chunk order: the digits of this CTA's chunks [cch0, cch1] only
-        const int k0 = T.cch0 * a.kc, kl = (T.cch1 - T.cch0 + 1) * a.kc;
-        d_build<LFK>(DSrc{2, nullptr, nullptr, a.b.att_y + k0}, kl, dig);
-        d_mark(a, c);  // C prep done
-        d_units<LFK>(a, c, T.r[1], dig, 0, kl, 0, acc_ao, C, ecm ? C / 16 : 0, T.cch0);
-      }
+      d_build<LFK>(DSrc{2, nullptr, nullptr, a.b.att_y}, C, dig);
+      d_mark(a, c);  // C prep done
+      d_units<LFK>(a, c, T.r[1], dig, 0, C, 0, acc_ao, C);
       d_mark(a, c);  // C done
       if (!d_gsync(a, c)) {
         alive = false;
@@ -1665,8 +1610,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.prev = a.b.ffn_x + (size_t)l * C;
         q.mix[0] = Ly.ffn_x_k;
         q.nmix = 1;
-        q.need = 0xffffffffu;
-        q.kc = a.kc;
         q.ln = TV;
         q.stat = s_stat + 2;
         d_ln_mix<LFK>(a, c, q, dig, 0);
@@ -1729,8 +1672,6 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       q.w = a.lnout_w;
       q.b = a.lnout_b;
       q.nmix = 1;
-      q.need = 0xffffffffu;
-      q.kc = a.kc;
       q.ln = TV;
       d_ln_mix<LFK>(a, c, q, dig, 0);
     } else {
