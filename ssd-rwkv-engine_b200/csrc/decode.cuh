@@ -183,6 +183,7 @@ struct DTable {
   int ckm[kDMaxChunks], cks[kDMaxChunks];
   int zc0, zc1, zf0, zf1, z3c0, z3c1, zv0, zv1, zr0, zr1;  // zeroing slices (C, F, 3C, V, rtot)
   int ech0, ech1;  // chunk-ordered E: first and last column chunk of this CTA's units
+  uint32_t aneed;  // bit m: this CTA has r/k/v units of matrix m (r, k, v), so phase A builds its digits
 };
 
 // [a, b) = part i of [0, n) split into `parts` (n * parts < 2^32).
@@ -224,6 +225,8 @@ __device__ void d_build_table(const DArgs& a, DTable& T) {
   const int nc = C / a.kc, nf = F / a.kc;
   d_range(3 * C / 16, nc, G, bx, T.r[0]);
   d_range(C / 16, nc, G, bx, T.r[1]);
+  T.aneed = 0u;
+  for (int u = T.r[0].u0; u < T.r[0].u1; ++u) T.aneed |= 1u << (u / nc / (C / 16));
   d_range(F / 16, nc, G, bx, T.r[2]);
   if (a.ecm) {  // chunk order: equal contiguous shares of the chunk-major unit numbering
     T.r[3].nch = nf;
@@ -748,6 +751,7 @@ struct DLnMix {
   float* pv;           // shared copy of prev (nullptr: not kept)
   const float* mix[3];  // token-shift mixes (global), one digit set each
   int nmix;
+  uint32_t need;  // bit m: emit the digits of mix m (the others are not used by this CTA)
   float* ln;     // shared LayerNorm output
   float* stat;   // mean, rstd (nullptr: not kept)
 };
@@ -805,7 +809,7 @@ __device__ __noinline__ void d_ln_mix(const DArgs& a, DCons& c, const DLnMix& q,
   }
 #pragma unroll
   for (int m = 0; m < 3; ++m) {
-    if (m < q.nmix) {
+    if (m < q.nmix && ((q.need >> m) & 1u)) {  // CTA-uniform
       float v[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) v[u] = q.prev ? y[u] + (pv[u] - y[u]) * mx[m][u] : y[u];
@@ -1532,6 +1536,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.mix[1] = Ly.x_k;
         q.mix[2] = Ly.x_v;
         q.nmix = 3;
+        q.need = T.aneed;  // only the r/k/v digit sets this CTA's units read
         q.ln = TV;
         q.stat = s_stat;
         d_ln_mix<LFK>(a, c, q, dig, a.dig_set);
@@ -1545,9 +1550,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
 #pragma unroll 1
         for (int i = t; i < C; i += kDT) PV[i] = __ldcg(a.b.att_x + (size_t)l * C + i);
         d_csync();
-        d_build<LFK>(DSrc{0, TV, PV, Ly.x_r}, C, dig);
-        d_build<LFK>(DSrc{0, TV, PV, Ly.x_k}, C, dig + a.dig_set);
-        d_build<LFK>(DSrc{0, TV, PV, Ly.x_v}, C, dig + 2 * a.dig_set);
+        if (T.aneed & 1u) d_build<LFK>(DSrc{0, TV, PV, Ly.x_r}, C, dig);
+        if (T.aneed & 2u) d_build<LFK>(DSrc{0, TV, PV, Ly.x_k}, C, dig + a.dig_set);
+        if (T.aneed & 4u) d_build<LFK>(DSrc{0, TV, PV, Ly.x_v}, C, dig + 2 * a.dig_set);
       }
       d_mark(a, c);  // A prep done
       d_units<LFK>(a, c, T.r[0], dig, a.dig_set, C, C / 16, acc_rkv, 3 * C);
@@ -1610,6 +1615,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.prev = a.b.ffn_x + (size_t)l * C;
         q.mix[0] = Ly.ffn_x_k;
         q.nmix = 1;
+        q.need = 1u;
         q.ln = TV;
         q.stat = s_stat + 2;
         d_ln_mix<LFK>(a, c, q, dig, 0);
@@ -1672,6 +1678,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       q.w = a.lnout_w;
       q.b = a.lnout_b;
       q.nmix = 1;
+      q.need = 1u;
       q.ln = TV;
       d_ln_mix<LFK>(a, c, q, dig, 0);
     } else {
