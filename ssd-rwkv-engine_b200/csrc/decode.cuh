@@ -615,6 +615,27 @@ __device__ __noinline__ float d_csum(float v, float* red) {
   return r;
 }
 
+// Sums over the 64 threads of warps 0 and 1 only (a head's channels): warp
+// shuffles, one 64-thread named barrier; `red` gets two (or four) fresh
+// floats per call so that successive calls do not race.
+constexpr int kDBar64 = 3;  // named barrier of warps 0-1
+__device__ __forceinline__ float d_sum64(float v, float* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  bar_sync(kDBar64, 64);
+  return red[0] + red[1];
+}
+__device__ __forceinline__ float2 d_sum64x2(float v, float w, float* red) {
+  v = warp_sum(v);
+  w = warp_sum(w);
+  if ((threadIdx.x & 31) == 0) {
+    red[threadIdx.x >> 5] = v;
+    red[2 + (threadIdx.x >> 5)] = w;
+  }
+  bar_sync(kDBar64, 64);
+  return make_float2(red[0] + red[1], red[2] + red[3]);
+}
+
 // Grid barrier of the consumers; false (CTA-uniform) when it gave up or an
 // earlier wait of this CTA failed.
 __device__ __noinline__ bool d_gsync(const DArgs& a, DCons& c) {
@@ -1298,10 +1319,11 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
     }
     d_csync();
   }
-  const float kkv = t < 64 ? k * kk_w : 0.f;
-  const float nrm = sqrtf(d_csum(kkv * kkv, c.red));
+  // the head's 64 channels live in warps 0-1: their sums use a 64-thread barrier
   if (t < 64) {
     const int ch = h * 64 + t;
+    const float kkv = k * kk_w;
+    const float nrm = sqrtf(d_sum64(kkv * kkv, c.red));
     const float aa = sigmoidf_(a0 + vec[64 + t]);
     const float kk = kkv / fmaxf(nrm, 1e-12f);
     const float kn = k * (1.0f + (aa - 1.0f) * ka);
@@ -1315,21 +1337,20 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
     ska[t] = kk * aa;
   }
   d_csync();
-  if (t < 256) wkv7_head64(S, sr, sd, sk, sv, skk, ska, sy);
-  d_csync();
-  #pragma unroll 1
-  for (int u = t; u < 1024; u += kDT) reinterpret_cast<float4*>(Sg)[u] = reinterpret_cast<const float4*>(S)[u];
-  const float yv = t < 64 ? sy[t] : 0.f;
-  const float mean = d_csum(yv, c.red) / 64.f;
-  const float dv = t < 64 ? yv - mean : 0.f;
-  const float var = d_csum(dv * dv, c.red) / 64.f;
-  const float bon = t < 64 ? sr[t] * sk[t] * rk : 0.f;
-  const float bonus = d_csum(bon, c.red);
-  if (t < 64) {
-    const int ch = h * 64 + t;
-    float o = dv * rsqrtf(var + 64e-5f) * lw + lb;
-    o = o + bonus * sv[t];
-    a.b.att_y[ch] = o * vec[128 + t];
+  if (t < 256) {
+    wkv7_head64(S, sr, sd, sk, sv, skk, ska, sy, Sg);  // the new state straight to global memory
+    bar_sync(kDBar64 - 1, 256);                       // y of every channel visible to warps 0-1
+    if (t < 64) {
+      const int ch = h * 64 + t;
+      const float yv = sy[t];
+      const float2 mb = d_sum64x2(yv, sr[t] * sk[t] * rk, c.red + 2);
+      const float mean = mb.x / 64.f;
+      const float dv = yv - mean;
+      const float var = d_sum64(dv * dv, c.red + 6) / 64.f;
+      float o = dv * rsqrtf(var + 64e-5f) * lw + lb;
+      o = o + mb.y * sv[t];
+      a.b.att_y[ch] = o * vec[128 + t];
+    }
   }
 }
 

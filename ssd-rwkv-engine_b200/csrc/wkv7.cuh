@@ -12,9 +12,10 @@ namespace rwkvb {
 //   y[i] = sum_j S[i][j] * r[j]
 // Vectors live in shared memory.  Thread t owns row t/4, columns (t%4)*16..+16:
 // the state is read and written exactly once, with 64-byte vector accesses.
+// out != nullptr: the new state goes to `out` (global, same layout) instead of S.
 __device__ __forceinline__ void wkv7_head64(float* __restrict__ S, const float* r, const float* d,
                                             const float* k, const float* v, const float* kk, const float* ka,
-                                            float* y) {
+                                            float* y, float* out = nullptr) {
   const int t = threadIdx.x;
   const int i = t >> 2, q = (t & 3) << 4;
   float4* row = reinterpret_cast<float4*>(S + i * 64 + q);
@@ -39,8 +40,9 @@ __device__ __forceinline__ void wkv7_head64(float* __restrict__ S, const float* 
   }
   yy += __shfl_xor_sync(0xffffffffu, yy, 1);
   yy += __shfl_xor_sync(0xffffffffu, yy, 2);
+  float4* dst = out ? reinterpret_cast<float4*>(out + i * 64 + q) : row;
 #pragma unroll
-  for (int u = 0; u < 4; ++u) row[u] = make_float4(s[4 * u], s[4 * u + 1], s[4 * u + 2], s[4 * u + 3]);
+  for (int u = 0; u < 4; ++u) dst[u] = make_float4(s[4 * u], s[4 * u + 1], s[4 * u + 2], s[4 * u + 3]);
   if ((t & 3) == 0) y[i] = yy;
 }
 
