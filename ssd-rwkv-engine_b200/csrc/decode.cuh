@@ -67,10 +67,10 @@ constexpr int kDMisc = 2560;           // misc shared floats
 static_assert((kDW / 2) * 4 * 64 <= kDMisc, "phase-B adapter partials [warps / 2][4][64] live in misc");
 static_assert(256 + 4 * kDT <= kDMisc, "adapter item inputs and row-group partials live in misc");
 constexpr int kMidPer = (2048 + kDT - 1) / kDT;  // first-adapter sums per consumer thread (rtot <= 2048)
-// Preload-mode phase B keeps in misc: x' and the min terms (rt floats each),
-// the digit blocks of the four adapters (3.25 bytes per row), the task
-// partials [4 nchunk][16], the adapter biases [4].
-__host__ __device__ constexpr int d_pieces_misc_floats(int rt, int nchunk) { return 2 * rt + rt * 13 / 16 + 64 * nchunk + 4; }
+// Preload-mode phase B keeps in misc: the min-term partials of the 8-row
+// items (rt / 8 floats), the digit blocks of the four adapters (3.25 bytes per
+// row), the task partials [4 nchunk][16], the adapter biases [4].
+__host__ __device__ constexpr int d_pieces_misc_floats(int rt, int nchunk) { return rt / 8 + rt * 13 / 16 + 64 * nchunk + 4; }
 constexpr float kFix = 4294967296.0f;  // 2^32 fixed-point scale of adapter partials
 constexpr float kUnfix = 1.0f / 4294967296.0f;
 
@@ -1077,11 +1077,10 @@ __device__ __noinline__ void d_pieces_mma(const DArgs& a, DCons& c, const DTable
     }
     roff[4] = r;
   }
-  const int rt = roff[4];
-  float* xp = misc;                                            // [rt] x'
-  float* bt = misc + rt;                                       // [rt] mid * min
-  uint8_t* dgb = reinterpret_cast<uint8_t*>(misc + 2 * rt);    // digit blocks, 3.25 bytes per row
-  float* part = misc + 2 * rt + rt * 13 / 16;                  // [4 nck][16]
+  const int rt = roff[4], nit = rt >> 3;
+  float* bpart = misc;                                         // [nit] sum over an item's rows of mid * min
+  uint8_t* dgb = reinterpret_cast<uint8_t*>(misc + nit);       // digit blocks, 3.25 bytes per row
+  float* part = misc + nit + rt * 13 / 16;                     // [4 nck][16]
   float* bias = part + 64 * nck;                               // [4]
   auto adapter_of = [&](int j) { return j >= roff[3] ? 3 : (j >= roff[2] ? 2 : (j >= roff[1] ? 1 : 0)); };
   auto digits_of = [&](int m) {
@@ -1092,42 +1091,36 @@ __device__ __noinline__ void d_pieces_mma(const DArgs& a, DCons& c, const DTable
     X.xsum = X.xc + a.apr[m] / 32;
     return X;
   };
-  if (!c.dead) {
-#pragma unroll 1
-    for (int j = t; j < rt; j += kDT) {
-      const int m = adapter_of(j), r = j - roff[m];
-      float xv = 0.f, bv = 0.f;
-      if (m < nm && r < d_rank(a.d, m)) {
-        const int sel = ((h * 64) >> a.alg[m]) & 1;
-        const float2 pq = reinterpret_cast<const float2*>(img + boff[m] + 64u * (uint32_t)a.aps[m])[r * 2 + sel];
-        const float md = mid[d_rank_off(a.d, m) + r];
-        xv = md * __fmul_rn(__fsub_rn(pq.y, pq.x), kInv255);
-        bv = md * pq.x;
-      }
-      xp[j] = xv;
-      bt[j] = bv;
-    }
-  }
-  d_csync();
-  // digits of x' (8 rows per item, 32-row flush groups) and the min-term sums
-  const int nit = rt >> 3;
+  // one 8-row item per lane: x'_r = mid_r d_r of its rows, their digits (32-row
+  // flush groups: four adjacent lanes), and the item's sum of mid_r min_r
   if (w * 32 < nit) {
     const int it = w * 32 + lane;
-    const bool act = it < nit;
-    const int m = act ? adapter_of(it * 8) : 0;
-    float v[8];
+    const bool act = it < nit && !c.dead;
+    const int m = it < nit ? adapter_of(it * 8) : 0;
+    const int R = d_rank(a.d, m), sel = ((h * 64) >> a.alg[m]) & 1;
+    const float2* pairs = reinterpret_cast<const float2*>(img + boff[m] + 64u * (uint32_t)a.aps[m]);
+    const float* md = mid + d_rank_off(a.d, m);
+    float v[8], bs = 0.f;
 #pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = act ? xp[it * 8 + u] : 0.f;
+    for (int u = 0; u < 8; ++u) {
+      const int r = it * 8 + u - roff[m];
+      v[u] = 0.f;
+      if (act && m < nm && r < R) {
+        const float2 pq = pairs[r * 2 + sel];
+        v[u] = md[r] * __fmul_rn(__fsub_rn(pq.y, pq.x), kInv255);
+        bs = fmaf(md[r], pq.x, bs);
+      }
+    }
+    if (act) bpart[it] = bs;
     emit_digits(v, act ? it - roff[m] / 8 : 0, act, 0, digits_of(m));
   }
-  if (w < nm) {
+  d_csync();
+  if (w < nm) {  // the adapter's min term, its items in order
     float sb = 0.f;
-    for (int j = roff[w] + lane; j < roff[w + 1]; j += 32) sb += bt[j];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sb += __shfl_xor_sync(0xffffffffu, sb, o);
+    for (int i = roff[w] / 8 + lane; i < roff[w + 1] / 8; i += 32) sb += bpart[i];
+    sb = warp_sum(sb);
     if (lane == 0) bias[w] = sb;
   }
-  d_csync();
 #pragma unroll 1
   for (int tau = w; !c.dead && tau < 4 * nck; tau += kDW) {
     const int k = tau >> 2, tile = tau & 3, m = T.ckm[k], s0 = T.cks[k];
