@@ -321,13 +321,17 @@ int rwkvb_engine_decode_greedy_async(rwkvb_engine* e, int32_t first_token, int32
  * per token.
  *
  * rwkvb_engine_host_ring: the engine's ring (allocated at the first call):
- *   ids[cap]  each step's greedy id, written as soon as the step ends;
- *   *count    ids written so far, stored after the ids (system-scope release);
- *   *cancel   read by the device once per token: non-zero stops the decode at
- *             the next token boundary.
+ *   ids[cap]  each step's greedy id: rwkvb_engine_decode_stream sets ids[0..n)
+ *             to -1 and the device replaces slot i with step i's id (one 32-bit
+ *             store) as soon as the step ends, so a reader polls the slot it
+ *             waits for;
+ *   *count    ids written so far (exact once the launch has ended);
+ *   *cancel   read by the device once per token and acted on at the following
+ *             token: non-zero stops the decode at a token boundary.
  * rwkvb_engine_decode_stream: greedy decode of n <= cap steps from first_token
  * (step 0 consumes it, step i > 0 consumes step i-1's id), streamed into the
- * ring; resets *count and *cancel, launches and returns without synchronising.
+ * ring; resets ids[0..n), *count and *cancel, launches and returns without
+ * synchronising.  No step waits on the host or the bus.
  * The previous streamed decode of the engine must have finished (its stream
  * synchronised) before the next call.  When cancelled, *count gives the steps
  * that ran; the state is that after those steps.  out_tokens_dev (device, may be

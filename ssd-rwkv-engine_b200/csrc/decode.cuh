@@ -86,8 +86,8 @@ __device__ __forceinline__ int d_ld_relaxed_sys(const int* p) {
   return v;
 }
 
-__device__ __forceinline__ void d_st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void d_st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 // Fire-and-forget 64-bit integer add (the fixed-point accumulators).
@@ -1517,6 +1517,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   #pragma unroll 1
   for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
   int tok = a.mode == 0 ? (a.first_tok >= 0 ? a.first_tok : __ldcg(a.b.tok)) : __ldg(a.forced);
+  // streamed decode: the host's cancel word as CTA 0 read it during the
+  // previous token's head (loaded a token ahead, so no step waits on the bus)
+  int cancel_next = 0;
   bool alive = d_gsync(a, c);
   for (int step = 0; step < a.ntok && alive; ++step) {
     const bool head = a.mode == 0 || step == a.ntok - 1;
@@ -1678,11 +1681,15 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       break;
     }
     d_mark(a, c);  // head barrier
-    // the host's cancel word crosses the bus once per token, read here so that
-    // its latency overlaps the head; published to every CTA before the last
-    // barrier of the token
+    // the host's cancel word crosses the bus once per token: the value read
+    // during the previous token's head is acted on now (published to every CTA
+    // before the last barrier of the token) and the next read is issued, to be
+    // used one token later, so its latency never stalls a step
     int cancel_seen = 0;
-    if (a.ring_cancel && bx == 0 && t == 0) cancel_seen = d_ld_relaxed_sys(a.ring_cancel);
+    if (a.ring_cancel && bx == 0 && t == 0) {
+      cancel_seen = cancel_next;
+      cancel_next = d_ld_relaxed_sys(a.ring_cancel);
+    }
     d_zero(acc_hk, T.zf0, T.zf1);
     if (fused) {
       DLnMix q{};
@@ -1726,9 +1733,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       a.b.hist[step % a.d.hist_cap] = tok;
       *a.b.tok = tok;
       if (a.ring_ids) {
-        a.ring_ids[step] = tok;
-        __threadfence_system();  // the id is visible to the host before the count that announces it
-        d_st_release_sys(a.ring_count, (unsigned)(step + 1));
+        // one 32-bit store replaces the -1 the host left in the slot (the host
+        // polls the slot itself, so no fence orders it with anything); the
+        // count is exact once the launch has ended
+        d_st_relaxed_sys(reinterpret_cast<unsigned*>(a.ring_ids + step), (unsigned)tok);
+        d_st_relaxed_sys(a.ring_count, (unsigned)(step + 1));
       }
     }
     if (a.ring_cancel && __ldcg(a.b.stop)) {

@@ -1611,6 +1611,8 @@ extern "C" int rwkvb_engine_decode_stream(rwkvb_engine* e, int32_t first, int32_
   // precondition), so nothing on the device writes the ring now
   *reinterpret_cast<volatile uint32_t*>(e->hring) = 0u;
   *reinterpret_cast<volatile int32_t*>(e->hring + 64) = 0;
+  volatile int32_t* ids = reinterpret_cast<volatile int32_t*>(e->hring + 128);
+  for (int i = 0; i < n; ++i) ids[i] = -1;  // a step's id replaces -1 when the step ends
   std::atomic_thread_fence(std::memory_order_seq_cst);
   if (n == 0) return RWKVB_OK;
   cudaStream_t s = (cudaStream_t)stream;

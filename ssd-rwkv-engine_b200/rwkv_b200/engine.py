@@ -287,8 +287,10 @@ class B200Engine:
         ``on_token(i, id)`` runs on this thread for every id in order;
         ``should_stop()`` is polled meanwhile.  When it returns true, or
         ``on_token`` raises, the device cancel word is set and the decode stops
-        at the next token boundary; the exception (if any) is re-raised after
-        the launch has ended.  Returns the ids the device produced."""
+        at a token boundary (the device acts on the word one token after it
+        reads it, so no step waits on the bus); later ids are not passed to
+        ``on_token``; the exception (if any) is re-raised after the launch has
+        ended.  Returns the ids the device produced."""
         if not self.persistent_active:
             raise native.RwkvbError(native.RWKVB_EUNSUPPORTED, "decode_stream (persistent engines only)")
         ids_view, count, cancel, cap = self._host_ring()
@@ -303,9 +305,10 @@ class B200Engine:
         err: BaseException | None = None
         stopping = False
         while True:
-            c = count.value
-            while len(out) < c:
+            while len(out) < n:  # a slot holds -1 until its step's id replaces it
                 tok = int(ids_view[len(out)])
+                if tok < 0:
+                    break
                 out.append(tok)
                 if on_token is not None and err is None and not stopping:
                     try:
@@ -319,7 +322,7 @@ class B200Engine:
             if len(out) >= n:
                 break
             if done.query():
-                if count.value <= len(out):
+                if min(int(count.value), n) <= len(out):
                     break
                 continue
             time.sleep(poll_s)
