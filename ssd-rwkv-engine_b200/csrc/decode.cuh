@@ -409,7 +409,12 @@ __device__ __noinline__ void d_issue_item(const DArgs& a, const LayerDev& Ly, in
   const uint32_t g0 = (uint32_t)(((uint64_t)i0 * R) >> W.lg) & ~1u;
   const uint32_t g1 = ((uint32_t)((((uint64_t)i1 * R - 1) >> W.lg) + 1) + 1u) & ~1u;
   const uint32_t sb = (g1 - g0) * 8u;
-  mbar_expect_tx(bar, qb + sb);
+  // the item's slice of its token-shift mix vector follows the pairs, so the
+  // consumers mix the item's inputs from shared memory only
+  const float* mix = m == 0 ? Ly.x_w : (m == 1 ? Ly.x_a : (m == 2 ? Ly.x_g : Ly.x_v));
+  const uint32_t xb = (uint32_t)(i1 - i0) * 4u;
+  const uint32_t xo = ((qb + 15u) & ~15u) + sb;
+  mbar_expect_tx(bar, qb + sb + xb);
   if (a.l2_first) {
     const uint64_t pol = l2_evict_first();
     bulk_g2s_hint(dst, W.payload + (size_t)i0 * R, qb, bar, pol);
@@ -418,6 +423,7 @@ __device__ __noinline__ void d_issue_item(const DArgs& a, const LayerDev& Ly, in
     bulk_g2s(dst, W.payload + (size_t)i0 * R, qb, bar);
     bulk_g2s(dst + ((qb + 15u) & ~15u), W.meta + (size_t)g0 * 8, sb, bar);
   }
+  bulk_g2s(dst + xo, mix + i0, xb, bar);  // re-read every token: default L2 policy
 }
 
 // Producer: wait until the consumers released load n - 1 of a dedicated
@@ -990,14 +996,21 @@ __device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, 
     const int i0 = (item - a.d.abase[m]) * a.d.arow[m], i1 = min(C, i0 + a.d.arow[m]), nr = i1 - i0;
     float* xm = misc;          // [arow[m] <= 256]
     float* pacc = misc + 256;  // [nrg][R]
-    #pragma unroll 1
-    for (int i = t; i < nr; i += kDT) xm[i] = TV[i0 + i] + (PV[i0 + i] - TV[i0 + i]) * __ldg(mix + i0 + i);
-    d_csync();
     const uint8_t* sl;
-    if (a.pre) {
+    if (a.pre) {  // the mix slice came with the item (d_issue_item)
       d_pre_wait(a, c, &c.pbar[2], c.nitm);
       sl = c.sm + a.o_item;
+      const uint32_t qb0 = (uint32_t)(nr * R);
+      const uint32_t g00 = (uint32_t)(((uint64_t)i0 * R) >> wlg) & ~1u;
+      const uint32_t g10 = ((uint32_t)((((uint64_t)i1 * R - 1) >> wlg) + 1) + 1u) & ~1u;
+      const float* mx = reinterpret_cast<const float*>(sl + ((qb0 + 15u) & ~15u) + (g10 - g00) * 8u);
+      #pragma unroll 1
+      for (int i = t; i < nr; i += kDT) xm[i] = TV[i0 + i] + (PV[i0 + i] - TV[i0 + i]) * mx[i];
+      d_csync();
     } else {
+      #pragma unroll 1
+      for (int i = t; i < nr; i += kDT) xm[i] = TV[i0 + i] + (PV[i0 + i] - TV[i0 + i]) * __ldg(mix + i0 + i);
+      d_csync();
       sl = d_slot_wait(a, c);
     }
     // four columns per thread (one 32-bit code word; a group holds whole

@@ -1083,19 +1083,23 @@ bool plan_decode(rwkvb_engine* e) {
     const PackedView* w1s[4] = {&l.w1, &l.a1, &l.g1, &l.v1};
     for (int m = 0; m < (i > 0 ? 4 : 3); ++m) alg = w1s[m]->lg < alg ? w1s[m]->lg : alg;
   }
-  auto item_bytes = [&](uint32_t nel) { return (nel + 15u) / 16u * 16u + ((nel >> alg) + 4u) * 8u; };
+  // codes, (min, max) pairs, then the item rows' slice of the mix vector (fp32)
+  auto item_bytes = [&](uint32_t rows, uint32_t rank) {
+    const uint32_t nel = rows * rank;
+    return (nel + 15u) / 16u * 16u + ((nel >> alg) + 4u) * 8u + 4u * rows;
+  };
   const uint32_t unit_b = a.code_b + a.pair_b;
   e->d.abase[0] = 0;
   for (int m = 0; m < 4; ++m) {
     int r = 256;
-    while (r > 16 && (d.C % r != 0 || item_bytes((uint32_t)(r * ranks[m])) > unit_b)) r /= 2;
+    while (r > 16 && (d.C % r != 0 || item_bytes((uint32_t)r, (uint32_t)ranks[m]) > unit_b)) r /= 2;
     e->d.arow[m] = r;
     e->d.abase[m + 1] = e->d.abase[m] + (ranks[m] > 0 ? (d.C + r - 1) / r : 0);
   }
   // slot: one GEMV unit, one adapter first-stage item, one adapter second-stage piece
   uint32_t slot = unit_b;
   for (int m = 0; m < 4; ++m) {
-    const uint32_t item = item_bytes((uint32_t)(d.arow[m] * ranks[m]));
+    const uint32_t item = item_bytes((uint32_t)d.arow[m], (uint32_t)ranks[m]);
     slot = slot > item ? slot : item;
   }
   for (int m = 0; m < 4; ++m) slot = slot > (uint32_t)a.abr[m] * 80u ? slot : (uint32_t)a.abr[m] * 80u;
