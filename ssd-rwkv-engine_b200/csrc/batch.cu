@@ -2812,9 +2812,6 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
     if (st == RWKVB_OK)
       st = cuda_status(cudaFuncSetAttribute(bt_in_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)(sizeof(float) * 5 * C)));
-    if (st == RWKVB_OK)  // three 16 KB state stages (beyond the 48 KB default with the static vectors)
-      st = cuda_status(cudaFuncSetAttribute(bt_wkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)(3 * 1024 * sizeof(float4))));
   }
   if (st != RWKVB_OK) {
     cudaFree(e->arena);
