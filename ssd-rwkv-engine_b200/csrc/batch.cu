@@ -807,10 +807,9 @@ __device__ __forceinline__ float2 bt_chan_sum2(float x, float y, float2* red2) {
 
 // Persistent over (head, session) pairs taken head-major (q = h * nb + b) in a
 // contiguous block per CTA, 256 threads per CTA, kBtWkvCtasPerSm CTAs per SM.
-//   - the next two pairs' states (16 KB each) are copied into the other two
-//     shared-memory stages with cp.async while this pair is computed, and
-//     threads 0..63 load the next pair's channel inputs into registers: ~128 KB
-//     of state reads per SM in flight;
+//   - the next pair's state (16 KB) is copied into the other shared-memory
+//     stage with cp.async while this pair is computed, and threads 0..63 load
+//     its channel inputs into registers: ~128 KB of state reads per SM in flight;
 //   - the head's eight per-channel vectors are loaded when the head changes;
 //   - thread t works on float4 f = t + 256 u (u < 4) of the state: rows
 //     (t >> 4) + 16 u, columns 4 (t & 15) .. + 3; a row's dot products are
@@ -821,7 +820,7 @@ __device__ __forceinline__ float2 bt_chan_sum2(float x, float y, float2* red2) {
 __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtWkvArgs a) {
   pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   pdl_launch_dependents();
-  extern __shared__ __align__(16) float4 bt_stage[];  // [3][1024]: this pair and the next two
+  extern __shared__ __align__(16) float4 bt_stage[];  // [2][1024]
   __shared__ float2 red2[2];
   __shared__ __align__(16) float vd[64], vkk[64], vka[64], vk[64], vr[64], vv[64], sy[64];
   const int t = threadIdx.x, i = t & 63;
@@ -834,13 +833,10 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
   auto state_of = [&](int q) -> float4* {
     return reinterpret_cast<float4*>(a.wkv + ((size_t)(q % a.nb) * a.H + q / a.nb) * 4096);
   };
-  // the first two pairs' states in flight before the loop (one group each)
-  for (int k = 0; k < 2; ++k) {
-    if (q0 + k < q1) {
-      const float4* src = state_of(q0 + k);
+  {
+    const float4* src = state_of(q0);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[k * 1024 + t + 256 * u], &src[t + 256 * u]);
-    }
+    for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[t + 256 * u], &src[t + 256 * u]);
     cp_async_commit();
   }
   BtWkvChan cur{};
@@ -848,14 +844,14 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
   int vh = -1;  // head whose vectors are in registers
   float kkw = 0.f, a0v = 0.f, v0v = 0.f, w0v = 0.f, kav = 0.f, rkv = 0.f, lw = 0.f, lb = 0.f;
   for (int q = q0, it = 0; q < q1; ++q, ++it) {
-    const int st = it % 3, nx = q + 1;
+    const int st = it & 1, nx = q + 1;
     const int b = q % a.nb, h = q / a.nb, ch = h * 64 + i;
-    if (q + 2 < q1) {  // two pairs ahead, into the stage the previous pair used
-      const float4* src = state_of(q + 2);
+    if (nx < q1) {
+      const float4* src = state_of(nx);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[((it + 2) % 3) * 1024 + t + 256 * u], &src[t + 256 * u]);
+      for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[(st ^ 1) * 1024 + t + 256 * u], &src[t + 256 * u]);
     }
-    cp_async_commit();  // an empty group when there is no such pair
+    cp_async_commit();  // an empty group when there is no next pair
     BtWkvChan nxt{};
     float kn = 0.f, v = 0.f;
     if (chan) {
@@ -881,7 +877,7 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
       vr[i] = cur.r;
       vv[i] = v;
     }
-    cp_async_wait_group<2>();  // this pair's stage (two groups were issued after it)
+    cp_async_wait_group<1>();  // this pair's stage (the group before the prefetch just issued)
     __syncthreads();
     // rows:  sa = S (-kk);  S = S diag(d) + sa (kk a)^T + v_row k^T;  y_row = S r
     {
@@ -2089,7 +2085,7 @@ int bt_record_step(rwkvb_batch* e, cudaStream_t s) {
       a.lnx_w = ly.lnx_w, a.lnx_b = ly.lnx_b;
       a.C = Ca, a.H = e->H, a.nb = nb, a.layer0 = l0 ? 1 : 0;
       const int pairs = nb * e->H, grid = std::min(pairs, e->sms * kBtWkvCtasPerSm);
-      bt_go(e->pdl, bt_wkv_kernel, dim3(grid), dim3(kBtThreads), 3 * 1024 * sizeof(float4), s, a);
+      bt_go(e->pdl, bt_wkv_kernel, dim3(grid), dim3(kBtThreads), 2 * 1024 * sizeof(float4), s, a);
       BT_CHECK();
     }
     if (bg_digits(e->dig_y, e->cs_y, e->att_y, Ca, Ca, nb, e->group, s, e->pdl) != RWKVB_OK) return RWKVB_ECUDA;
