@@ -351,6 +351,40 @@ __device__ __forceinline__ float bt_fold(const float* part, const BtPieces& p, i
   return s;
 }
 
+// bt_fold for the four elements n..n+3 (n % 4 == 0: one 128-row tile, so one
+// piece count): 16-byte loads, all issued together.
+__device__ __forceinline__ float4 bt_fold4(const float* part, const BtPieces& p, int nb, int rows, int b, int n) {
+  const int np = bt_npieces(p, n);
+  const float* q = part + (size_t)b * rows + n;
+  const size_t st = (size_t)nb * rows;
+  float4 v[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) v[u] = u < np ? ldcg4(q + u * st) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 s = v[0];
+#pragma unroll
+  for (int u = 1; u < 8; ++u)
+    if (u < np) s = make_float4(s.x + v[u].x, s.y + v[u].y, s.z + v[u].z, s.w + v[u].w);
+  for (int u = 8; u < np; ++u) {
+    const float4 w = ldcg4(q + u * st);
+    s = make_float4(s.x + w.x, s.y + w.y, s.z + w.z, s.w + w.w);
+  }
+  return s;
+}
+
+__device__ __forceinline__ float4 f4_add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+__device__ __forceinline__ float4 f4_lerp(float4 z, float4 p, float4 m) {  // z + (p - z) * m
+  return make_float4(z.x + (p.x - z.x) * m.x, z.y + (p.y - z.y) * m.y, z.z + (p.z - z.z) * m.z, z.w + (p.w - z.w) * m.w);
+}
+
+// LayerNorm of a row held as one float4 per thread (threads t < C / 4): two
+// block sums (mean, then centred squares), eps 1e-5.
+__device__ __forceinline__ float4 bt_ln4(float4 x, bool act, float4 w, float4 bb, int C, float* red) {
+  const float mean = block_sum(act ? x.x + x.y + x.z + x.w : 0.f, red) / (float)C;
+  const float4 d = make_float4(x.x - mean, x.y - mean, x.z - mean, x.w - mean);
+  const float rstd = rsqrtf(block_sum(act ? d.x * d.x + d.y * d.y + d.z * d.z + d.w * d.w : 0.f, red) / (float)C + 1e-5f);
+  return make_float4(d.x * rstd * w.x + bb.x, d.y * rstd * w.y + bb.y, d.z * rstd * w.z + bb.z, d.w * rstd * w.w + bb.w);
+}
+
 // Digit rows of the block's shared-memory vector src[0..K) for session b.
 __device__ __forceinline__ void bt_digits_block(const float* src, int K, int lfk, uint8_t* dig, float2* cs, int b,
                                                 int bp) {
@@ -429,51 +463,63 @@ struct BtInArgs {
 
 constexpr int kBtRowThreads = 1024;  // per-session row kernels (one CTA per session)
 
+// One float4 of the row per thread (C / 4 <= kBtRowThreads): the LayerNorm
+// weights are fetched before the dependency wait, every load of the input is
+// issued in one round, and the mixes are fetched while the LayerNorm sums run.
 __global__ void __launch_bounds__(kBtRowThreads) bt_in_kernel(BtInArgs a) {
-  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
-  pdl_launch_dependents();
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
-  const int b = blockIdx.x, C = a.C;
-  float* xl = bt_sm;       // ln output
-  float* prev = xl + C;    // previous ln output (token shift)
-  float* mixed = prev + C; // r, k, v inputs [3][C]
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    float v;
-    if (a.part) {
-      v = a.xm[(size_t)b * C + i] + bt_fold(a.part, a.pp, a.nb, C, b, i);
-      a.x[(size_t)b * C + i] = v;
-    } else if (a.add) {
-      v = a.xm[(size_t)b * C + i] + a.add[(size_t)b * C + i];
-      a.x[(size_t)b * C + i] = v;
-    } else {
-      v = a.x[(size_t)b * C + i];
-    }
-    xl[i] = v;
+  const int b = blockIdx.x, C = a.C, t = threadIdx.x, i = 4 * t;
+  const bool act = i < C;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 w4 = z4, b4 = z4, m4[6];
+#pragma unroll
+  for (int j = 0; j < 6; ++j) m4[j] = z4;
+  if (act) {
+    w4 = ldg4(a.ln_w + i);
+    b4 = ldg4(a.ln_b + i);
   }
-  __syncthreads();
-  bt_layer_norm(xl, a.ln_w, a.ln_b, C, red);
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
+  float* xl = bt_sm;       // ln output
+  float* mixed = xl + C;   // r, k, v inputs [3][C]
+  float4 x4 = z4, p4 = z4;
+  if (act) {
+    const size_t o = (size_t)b * C + i;
+    if (a.state) p4 = ldcg4(a.state + o);
+    if (a.part) {
+      x4 = f4_add(ldcg4(a.xm + o), bt_fold4(a.part, a.pp, a.nb, C, b, i));
+      *reinterpret_cast<float4*>(a.x + o) = x4;
+    } else if (a.add) {
+      x4 = f4_add(ldcg4(a.xm + o), ldcg4(a.add + o));
+      *reinterpret_cast<float4*>(a.x + o) = x4;
+    } else {
+      x4 = ldcg4(a.x + o);
+    }
+    if (a.state)  // the mixes (weights) land while the LayerNorm sums run
+#pragma unroll
+      for (int j = 0; j < 6; ++j) m4[j] = ldg4(a.mix[j] + i);
+  }
+  const float4 y4 = bt_ln4(x4, act, w4, b4, C, red);
   if (!a.state) {  // head input: ln_out only
+    if (act) *reinterpret_cast<float4*>(xl + i) = y4;
+    __syncthreads();
     bt_digits_block(xl, C, a.lfk, a.dig[0], a.cs[0], b, a.bp);
     return;
   }
-  float* st = a.state + (size_t)b * C;
-  const float *mr = a.mix[0], *mw = a.mix[1], *mk = a.mix[2], *mv = a.mix[3], *ma = a.mix[4], *mg = a.mix[5];
-  float* xw = a.xa4 + (size_t)b * C;
-  float* xa = xw + (size_t)a.nb * C;
-  float* xg = xa + (size_t)a.nb * C;
-  float* xv = xg + (size_t)a.nb * C;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const float z = xl[i], p = st[i], d = p - z;
-    st[i] = z;
-    mixed[i] = z + d * mr[i];
-    mixed[C + i] = z + d * mk[i];
-    const float vv = z + d * mv[i];
-    mixed[2 * C + i] = vv;
-    xw[i] = z + d * mw[i];
-    xa[i] = z + d * ma[i];
-    xg[i] = z + d * mg[i];
-    xv[i] = vv;
+  if (act) {
+    const size_t o = (size_t)b * C + i;
+    *reinterpret_cast<float4*>(a.state + o) = y4;
+    *reinterpret_cast<float4*>(mixed + i) = f4_lerp(y4, p4, m4[0]);          // r
+    *reinterpret_cast<float4*>(mixed + C + i) = f4_lerp(y4, p4, m4[2]);      // k
+    const float4 vv = f4_lerp(y4, p4, m4[3]);
+    *reinterpret_cast<float4*>(mixed + 2 * C + i) = vv;                     // v
+    float* xw = a.xa4 + o;
+    const size_t ps = (size_t)a.nb * C;
+    *reinterpret_cast<float4*>(xw) = f4_lerp(y4, p4, m4[1]);                // w
+    *reinterpret_cast<float4*>(xw + ps) = f4_lerp(y4, p4, m4[4]);           // a
+    *reinterpret_cast<float4*>(xw + 2 * ps) = f4_lerp(y4, p4, m4[5]);       // g
+    *reinterpret_cast<float4*>(xw + 3 * ps) = vv;                           // v
   }
   __syncthreads();
   // digit rows of r, k, v: one warp per (input, group)
@@ -944,25 +990,32 @@ struct BtFfnArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_ffn_kernel(BtFfnArgs a) {
-  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
-  pdl_launch_dependents();
   __shared__ float red[32];
   extern __shared__ __align__(16) float bt_sm[];
-  const int b = blockIdx.x, C = a.C;
-  float* xl = bt_sm;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const float o = a.add ? a.add[(size_t)b * C + i] : bt_fold(a.part, a.pp, a.nb, C, b, i);
-    const float v = a.x[(size_t)b * C + i] + o;
-    a.xm[(size_t)b * C + i] = v;
-    xl[i] = v;
+  const int b = blockIdx.x, C = a.C, t = threadIdx.x, i = 4 * t;
+  const bool act = i < C;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 w4 = z4, b4 = z4, m4 = z4;
+  if (act) {  // weights: before the dependency wait
+    w4 = ldg4(a.ln_w + i);
+    b4 = ldg4(a.ln_b + i);
+    m4 = ldg4(a.mix + i);
   }
-  __syncthreads();
-  bt_layer_norm(xl, a.ln_w, a.ln_b, C, red);
-  float* st = a.state + (size_t)b * C;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const float p = st[i], z = xl[i];
-    st[i] = z;
-    xl[i] = z + (p - z) * a.mix[i];
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
+  float* xl = bt_sm;
+  float4 x4 = z4, p4 = z4;
+  if (act) {
+    const size_t o = (size_t)b * C + i;
+    p4 = ldcg4(a.state + o);
+    const float4 att = a.add ? ldcg4(a.add + o) : bt_fold4(a.part, a.pp, a.nb, C, b, i);
+    x4 = f4_add(ldcg4(a.x + o), att);
+    *reinterpret_cast<float4*>(a.xm + o) = x4;
+  }
+  const float4 y4 = bt_ln4(x4, act, w4, b4, C, red);
+  if (act) {
+    *reinterpret_cast<float4*>(a.state + (size_t)b * C + i) = y4;
+    *reinterpret_cast<float4*>(xl + i) = f4_lerp(y4, p4, m4);
   }
   __syncthreads();
   bt_digits_block(xl, C, a.lfk, a.dig, a.cs, b, a.bp);
@@ -2478,6 +2531,7 @@ int bt_create(const rwkvb_model_desc* m, int32_t batch, uint32_t flags, const rw
   const int Ca = m->layers[0].att_r.rows;  // attention channels held here
   if (L <= 0 || C <= 0 || F <= 0 || V <= 0 || N != 64 || C % 128 || F % 128 || V % 128 || Ca <= 0 || Ca % 128)
     return RWKVB_EUNSUPPORTED;
+  if (C > 4 * kBtRowThreads) return RWKVB_EUNSUPPORTED;  // per-session row kernels: one float4 per thread
   if (!tp && (Ca != C || V != Vfull)) return RWKVB_EARG;
   if (tp && (tp->size < 2 || tp->rank < 0 || tp->rank >= tp->size || (!tp->collective && !tp->peer) ||
              tp->vocab_offset < 0 || tp->vocab_offset + V > Vfull || (tp->peer && tp->size > kBtMaxRanks)))
