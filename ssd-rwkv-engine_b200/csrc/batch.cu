@@ -1060,24 +1060,28 @@ struct BtLnRowsArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_lnrows_kernel(BtLnRowsArgs a) {
+  __shared__ float red[32];
+  const int row = blockIdx.x, C = a.C, i = 4 * threadIdx.x;
+  const bool act = i < C;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 w4 = z4, b4 = z4, x4 = z4;
+  if (act) {  // weights: before the dependency wait
+    w4 = ldg4(a.ln_w + i);
+    b4 = ldg4(a.ln_b + i);
+  }
   pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   pdl_launch_dependents();
-  __shared__ float red[32];
-  extern __shared__ __align__(16) float bt_sm[];
-  const int row = blockIdx.x, C = a.C;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    float v;
+  if (act) {
+    const size_t o = (size_t)row * C + i;
     if (a.part) {
-      v = a.xm[(size_t)row * C + i] + bt_fold(a.part, a.pp, a.rows, C, row, i);
-      a.x[(size_t)row * C + i] = v;
+      x4 = f4_add(ldcg4(a.xm + o), bt_fold4(a.part, a.pp, a.rows, C, row, i));
+      *reinterpret_cast<float4*>(a.x + o) = x4;
     } else {
-      v = a.x[(size_t)row * C + i];
+      x4 = ldcg4(a.x + o);
     }
-    bt_sm[i] = v;
   }
-  __syncthreads();
-  bt_layer_norm(bt_sm, a.ln_w, a.ln_b, C, red);
-  for (int i = threadIdx.x; i < C; i += blockDim.x) a.xln[(size_t)row * C + i] = bt_sm[i];
+  const float4 y4 = bt_ln4(x4, act, w4, b4, C, red);
+  if (act) *reinterpret_cast<float4*>(a.xln + (size_t)row * C + i) = y4;
 }
 
 // Token-shift mixes of every row.  mode 0 (time mix): six mixes; digit rows of
@@ -1095,44 +1099,40 @@ struct BtMixRowsArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_mixrows_kernel(BtMixRowsArgs a) {
+  extern __shared__ __align__(16) float bt_sm[];
+  const int row = blockIdx.x, C = a.C, s = row / a.P, j = row - s * a.P, i = 4 * threadIdx.x;
+  const bool act = i < C;
+  const int nd = a.mode == 0 ? 3 : 1;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 m4[6];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) m4[k] = z4;
+  if (act)  // the mixes (weights): before the dependency wait
+#pragma unroll
+    for (int k = 0; k < 6; ++k)
+      if (k < (a.mode == 0 ? 6 : 1)) m4[k] = ldg4(a.mix[k] + i);
   pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   pdl_launch_dependents();
-  extern __shared__ __align__(16) float bt_sm[];
-  const int row = blockIdx.x, C = a.C, s = row / a.P, j = row - s * a.P;
-  float* xl = bt_sm;
-  float* prev = xl + C;
-  float* mixed = prev + C;  // [3][C]
-  const float* own = a.xln + (size_t)row * C;
-  const float* pv = j > 0 ? a.xln + (size_t)(row - 1) * C : a.state + (size_t)s * C;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    xl[i] = own[i];
-    prev[i] = pv[i];
-  }
-  __syncthreads();
-  if (j == 0) {
-    const float* last = a.xln + (size_t)(row + a.P - 1) * C;
-    for (int i = threadIdx.x; i < C; i += blockDim.x) a.state[(size_t)s * C + i] = last[i];
-  }
-  const int nd = a.mode == 0 ? 3 : 1;
-  if (a.mode == 0) {
-    const float *mr = a.mix[0], *mw = a.mix[1], *mk = a.mix[2], *mv = a.mix[3], *ma = a.mix[4], *mg = a.mix[5];
-    float* xw = a.xa4 + (size_t)row * C;
-    float* xa = xw + (size_t)a.rows * C;
-    float* xg = xa + (size_t)a.rows * C;
-    float* xv = xg + (size_t)a.rows * C;
-    for (int i = threadIdx.x; i < C; i += blockDim.x) {
-      const float z = xl[i], d = prev[i] - z;
-      mixed[i] = z + d * mr[i];
-      mixed[C + i] = z + d * mk[i];
-      const float vv = z + d * mv[i];
-      mixed[2 * C + i] = vv;
-      xw[i] = z + d * mw[i];
-      xa[i] = z + d * ma[i];
-      xg[i] = z + d * mg[i];
-      xv[i] = vv;
+  float* mixed = bt_sm;  // [3][C]
+  if (act) {
+    const float4 z = ldcg4(a.xln + (size_t)row * C + i);
+    const float4 p = j > 0 ? ldcg4(a.xln + (size_t)(row - 1) * C + i) : ldcg4(a.state + (size_t)s * C + i);
+    if (j == 0)  // the chunk's last LayerNorm output becomes the session's state
+      *reinterpret_cast<float4*>(a.state + (size_t)s * C + i) = ldcg4(a.xln + (size_t)(row + a.P - 1) * C + i);
+    if (a.mode == 0) {
+      *reinterpret_cast<float4*>(mixed + i) = f4_lerp(z, p, m4[0]);          // r
+      *reinterpret_cast<float4*>(mixed + C + i) = f4_lerp(z, p, m4[2]);      // k
+      const float4 vv = f4_lerp(z, p, m4[3]);
+      *reinterpret_cast<float4*>(mixed + 2 * C + i) = vv;                   // v
+      float* xw = a.xa4 + (size_t)row * C + i;
+      const size_t ps = (size_t)a.rows * C;
+      *reinterpret_cast<float4*>(xw) = f4_lerp(z, p, m4[1]);                // w
+      *reinterpret_cast<float4*>(xw + ps) = f4_lerp(z, p, m4[4]);           // a
+      *reinterpret_cast<float4*>(xw + 2 * ps) = f4_lerp(z, p, m4[5]);       // g
+      *reinterpret_cast<float4*>(xw + 3 * ps) = vv;                         // v
+    } else {
+      *reinterpret_cast<float4*>(mixed + i) = f4_lerp(z, p, m4[0]);
     }
-  } else {
-    for (int i = threadIdx.x; i < C; i += blockDim.x) mixed[i] = xl[i] + (prev[i] - xl[i]) * a.mix[0][i];
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -1157,19 +1157,24 @@ struct BtFfnLnArgs {
 };
 
 __global__ void __launch_bounds__(kBtRowThreads) bt_ffnln_kernel(BtFfnLnArgs a) {
+  __shared__ float red[32];
+  const int row = blockIdx.x, C = a.C, i = 4 * threadIdx.x;
+  const bool act = i < C;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 w4 = z4, b4 = z4, x4 = z4;
+  if (act) {  // weights: before the dependency wait
+    w4 = ldg4(a.ln_w + i);
+    b4 = ldg4(a.ln_b + i);
+  }
   pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   pdl_launch_dependents();
-  __shared__ float red[32];
-  extern __shared__ __align__(16) float bt_sm[];
-  const int row = blockIdx.x, C = a.C;
-  for (int i = threadIdx.x; i < C; i += blockDim.x) {
-    const float v = a.x[(size_t)row * C + i] + bt_fold(a.part, a.pp, a.rows, C, row, i);
-    a.xm[(size_t)row * C + i] = v;
-    bt_sm[i] = v;
+  if (act) {
+    const size_t o = (size_t)row * C + i;
+    x4 = f4_add(ldcg4(a.x + o), bt_fold4(a.part, a.pp, a.rows, C, row, i));
+    *reinterpret_cast<float4*>(a.xm + o) = x4;
   }
-  __syncthreads();
-  bt_layer_norm(bt_sm, a.ln_w, a.ln_b, C, red);
-  for (int i = threadIdx.x; i < C; i += blockDim.x) a.xln[(size_t)row * C + i] = bt_sm[i];
+  const float4 y4 = bt_ln4(x4, act, w4, b4, C, red);
+  if (act) *reinterpret_cast<float4*>(a.xln + (size_t)row * C + i) = y4;
 }
 
 // WKV7 over the P positions of a chunk, in order, state rows in registers:
