@@ -549,8 +549,6 @@ struct BtAdp1Args {
 constexpr int kBtXsStride = 68;  // padded session stride of the staged inputs (bank spread, float4 aligned)
 
 __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
-  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
-  pdl_launch_dependents();
   extern __shared__ __align__(16) float bt_sm[];
   float* xs = bt_sm;                          // [kc][68]: inputs of 64 sessions
   float* ws = xs + kBtAdpKc * kBtXsStride;    // [kc][32]: dequantised weights
@@ -562,28 +560,7 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
   const int c0 = ((int)blockIdx.x - a.blk0[m]) * kBtAdpCols;
   const int k0 = blockIdx.y * kBtAdpKc;
   const float* xsrc = a.xa4 + (size_t)m * a.nb * a.C;
-  // inputs x[b][k0 .. k0 + 127] of the 64 session slots: 8 float4 loads per
-  // thread, all in flight before the first store; lanes take consecutive
-  // sessions, so the transposed stores xs[k][b] hit distinct banks
-  {
-    constexpr int kPer = kBtAdpKc * 64 / 4 / kBtThreads;
-    static_assert(kPer * 4 * kBtThreads == kBtAdpKc * 64, "x slice split");
-    float4 v[kPer];
-#pragma unroll
-    for (int r = 0; r < kPer; ++r) {
-      const int idx = t + r * kBtThreads, b = idx & 63, k4 = idx >> 6;
-      v[r] = b < a.nb ? *reinterpret_cast<const float4*>(xsrc + (size_t)b * a.C + k0 + 4 * k4)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll
-    for (int r = 0; r < kPer; ++r) {
-      const int idx = t + r * kBtThreads, b = idx & 63, k4 = idx >> 6;
-      xs[(4 * k4 + 0) * kBtXsStride + b] = v[r].x;
-      xs[(4 * k4 + 1) * kBtXsStride + b] = v[r].y;
-      xs[(4 * k4 + 2) * kBtXsStride + b] = v[r].z;
-      xs[(4 * k4 + 3) * kBtXsStride + b] = v[r].w;
-    }
-  }
+  // the weights do not depend on the previous kernel: dequantised before its wait
   if (a.fast[m]) {
     // one thread per (row, 16 codes): the row's 32 codes are contiguous
     for (int idx = t; idx < kBtAdpKc * 2; idx += blockDim.x) {
@@ -606,6 +583,30 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
     for (int idx = t; idx < kBtAdpKc * kBtAdpCols; idx += blockDim.x) {
       const int kk = idx / kBtAdpCols, j = idx - kk * kBtAdpCols;
       ws[idx] = c0 + j < R ? packed_at(W, k0 + kk, c0 + j) : 0.f;
+    }
+  }
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
+  // inputs x[b][k0 .. k0 + 127] of the 64 session slots: 8 float4 loads per
+  // thread, all in flight before the first store; lanes take consecutive
+  // sessions, so the transposed stores xs[k][b] hit distinct banks
+  {
+    constexpr int kPer = kBtAdpKc * 64 / 4 / kBtThreads;
+    static_assert(kPer * 4 * kBtThreads == kBtAdpKc * 64, "x slice split");
+    float4 v[kPer];
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int idx = t + r * kBtThreads, b = idx & 63, k4 = idx >> 6;
+      v[r] = b < a.nb ? *reinterpret_cast<const float4*>(xsrc + (size_t)b * a.C + k0 + 4 * k4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int idx = t + r * kBtThreads, b = idx & 63, k4 = idx >> 6;
+      xs[(4 * k4 + 0) * kBtXsStride + b] = v[r].x;
+      xs[(4 * k4 + 1) * kBtXsStride + b] = v[r].y;
+      xs[(4 * k4 + 2) * kBtXsStride + b] = v[r].z;
+      xs[(4 * k4 + 3) * kBtXsStride + b] = v[r].w;
     }
   }
   __syncthreads();
@@ -695,8 +696,6 @@ struct BtAdp2Args {
 constexpr int kBtAdp2Rc = 128;  // second-stage rows staged per round
 
 __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
-  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
-  pdl_launch_dependents();
   extern __shared__ __align__(16) float bt_sm[];
   const int ck = blockIdx.y, m = a.ck_m[ck], c0 = blockIdx.x * 64, t = threadIdx.x;
   const int R0 = a.ck_r0[ck], R1 = a.ck_r1[ck];
@@ -705,24 +704,8 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
   float* ws = ms + kBtAdp2Rc * 64;    // [rc][64 columns]
   const int bq = t & 15, cq = t >> 4;
   float acc[4][4] = {};
-  for (int r0 = R0; r0 < R1; r0 += kBtAdp2Rc) {
-    const int rc = min(kBtAdp2Rc, R1 - r0);
-    __syncthreads();
-    {
-      // rows r0 .. r0 + rc of mid (64 sessions each): up to 8 float4 per thread, loads issued together
-      const float4* src = reinterpret_cast<const float4*>(a.midT + (size_t)(a.off[m] + r0) * 64);
-      float4 v[kBtAdp2Rc * 16 / kBtThreads];
-#pragma unroll
-      for (int q = 0; q < kBtAdp2Rc * 16 / kBtThreads; ++q) {
-        const int idx = t + q * kBtThreads;
-        if (idx < rc * 16) v[q] = src[idx];
-      }
-#pragma unroll
-      for (int q = 0; q < kBtAdp2Rc * 16 / kBtThreads; ++q) {
-        const int idx = t + q * kBtThreads;
-        if (idx < rc * 16) reinterpret_cast<float4*>(ms)[idx] = v[q];
-      }
-    }
+  // rows r0 .. r0 + rc of W (64 columns) dequantised into ws
+  auto load_w = [&](int r0, int rc) {
     if (a.fast[m]) {
       for (int idx = t; idx < rc * 4; idx += blockDim.x) {
         const int r = idx >> 2, p = idx & 3;
@@ -738,6 +721,32 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
       for (int idx = t; idx < rc * 64; idx += blockDim.x) {
         const int r = idx >> 6, j = idx & 63;
         ws[idx] = packed_at(W, r0 + r, c0 + j);
+      }
+    }
+  };
+  // the first chunk's weights do not depend on the previous kernel: before its wait
+  load_w(R0, min(kBtAdp2Rc, R1 - R0));
+  pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
+  pdl_launch_dependents();
+  for (int r0 = R0; r0 < R1; r0 += kBtAdp2Rc) {
+    const int rc = min(kBtAdp2Rc, R1 - r0);
+    if (r0 != R0) {
+      __syncthreads();  // the previous chunk's ms / ws are no longer read
+      load_w(r0, rc);
+    }
+    {
+      // rows r0 .. r0 + rc of mid (64 sessions each): up to 8 float4 per thread, loads issued together
+      const float4* src = reinterpret_cast<const float4*>(a.midT + (size_t)(a.off[m] + r0) * 64);
+      float4 v[kBtAdp2Rc * 16 / kBtThreads];
+#pragma unroll
+      for (int q = 0; q < kBtAdp2Rc * 16 / kBtThreads; ++q) {
+        const int idx = t + q * kBtThreads;
+        if (idx < rc * 16) v[q] = src[idx];
+      }
+#pragma unroll
+      for (int q = 0; q < kBtAdp2Rc * 16 / kBtThreads; ++q) {
+        const int idx = t + q * kBtThreads;
+        if (idx < rc * 16) reinterpret_cast<float4*>(ms)[idx] = v[q];
       }
     }
     __syncthreads();
@@ -1033,9 +1042,17 @@ __global__ void __launch_bounds__(kBtThreads) bt_hdig_kernel(uint8_t* dig, float
   const int per = 1 << (lfk - 5);
   const int n0 = (g << lfk) + lane * per;
   float v[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int u = 0; u < per; ++u) {
-    const float y = bt_fold(part, pp, nb, F, b, n0 + u);
-    v[u] = y > 0.f ? y * y : 0.f;
+  if (per == 4) {  // one 16-byte load per piece for the lane's four values
+    const float4 y = bt_fold4(part, pp, nb, F, b, n0);
+    v[0] = y.x > 0.f ? y.x * y.x : 0.f;
+    v[1] = y.y > 0.f ? y.y * y.y : 0.f;
+    v[2] = y.z > 0.f ? y.z * y.z : 0.f;
+    v[3] = y.w > 0.f ? y.w * y.w : 0.f;
+  } else {
+    for (int u = 0; u < per; ++u) {
+      const float y = bt_fold(part, pp, nb, F, b, n0 + u);
+      v[u] = y > 0.f ? y * y : 0.f;
+    }
   }
   bg_emit_group(v, per, dig, cs, (size_t)F, (size_t)n0, b, bp, g);
 }
