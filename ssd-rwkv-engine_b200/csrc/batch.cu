@@ -860,6 +860,17 @@ __device__ __forceinline__ float2 bt_chan_sum2(float x, float y, float2* red2) {
   return r;
 }
 
+// The same over warps 2 and 3 (the GroupNorm threads): named barrier 2.
+__device__ __forceinline__ float2 bt_gn_sum2(float x, float y, float2* red2) {
+  x = warp_sum(x);
+  y = warp_sum(y);
+  if ((threadIdx.x & 31) == 0) red2[(threadIdx.x >> 5) - 2] = make_float2(x, y);
+  asm volatile("bar.sync 2, 64;" ::: "memory");
+  const float2 r = make_float2(red2[0].x + red2[1].x, red2[0].y + red2[1].y);
+  asm volatile("bar.sync 2, 64;" ::: "memory");
+  return r;
+}
+
 // Persistent over (head, session) pairs taken head-major (q = h * nb + b) in a
 // contiguous block per CTA, 256 threads per CTA, kBtWkvCtasPerSm CTAs per SM.
 //   - the next pair's state (16 KB) is copied into the other shared-memory
@@ -876,10 +887,12 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
   pdl_wait();  // programmatic dependent launch: the previous kernel's writes are visible
   pdl_launch_dependents();
   extern __shared__ __align__(16) float4 bt_stage[];  // [2][1024]
-  __shared__ float2 red2[2];
+  __shared__ float2 red2[2], gred2[2];
   __shared__ __align__(16) float vd[64], vkk[64], vka[64], vk[64], vr[64], vv[64], sy[64];
+  // GroupNorm inputs of the last updated pair (its bonus term and gate), double-buffered by pair parity
+  __shared__ float gbon[2][64], gv[2][64], ggate[2][64];
   const int t = threadIdx.x, i = t & 63;
-  const bool chan = t < 64;
+  const bool chan = t < 64, gnw = t >= 64 && t < 128;
   const int npairs = a.nb * a.H;
   const int q0 = (int)((long long)blockIdx.x * npairs / gridDim.x);
   const int q1 = (int)((long long)(blockIdx.x + 1) * npairs / gridDim.x);
@@ -887,6 +900,19 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
   // pair q = (head q / nb, session q % nb); its state is block (b, h) of [nb][H][64][64]
   auto state_of = [&](int q) -> float4* {
     return reinterpret_cast<float4*>(a.wkv + ((size_t)(q % a.nb) * a.H + q / a.nb) * 4096);
+  };
+  // GroupNorm over a head (eps 64e-5), bonus, gate of pair q, by warps 2-3
+  // while warps 0-1 prepare the next pair's channel vectors
+  auto group_norm = [&](int q, int par) {
+    const int b = q % a.nb, ch = (q / a.nb) * 64 + i;
+    const float y = sy[i];
+    const float2 mb = bt_gn_sum2(y, gbon[par][i], gred2);
+    const float mean = mb.x / 64.f;
+    const float dv = y - mean;
+    const float var = bt_gn_sum2(dv * dv, 0.f, gred2).x / 64.f;
+    float o = dv * rsqrtf(var + 64e-5f) * a.lnx_w[ch] + a.lnx_b[ch];
+    o = o + mb.y * gv[par][i];
+    a.att_y[(size_t)b * a.C + ch] = o * ggate[par][i];
   };
   {
     const float4* src = state_of(q0);
@@ -897,9 +923,9 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
   BtWkvChan cur{};
   if (chan) cur = bt_wkv_chan(a, q0 % a.nb, (q0 / a.nb) * 64 + i);
   int vh = -1;  // head whose vectors are in registers
-  float kkw = 0.f, a0v = 0.f, v0v = 0.f, w0v = 0.f, kav = 0.f, rkv = 0.f, lw = 0.f, lb = 0.f;
+  float kkw = 0.f, a0v = 0.f, v0v = 0.f, w0v = 0.f, kav = 0.f, rkv = 0.f;
   for (int q = q0, it = 0; q < q1; ++q, ++it) {
-    const int st = it & 1, nx = q + 1;
+    const int st = it & 1, nx = q + 1, par = it & 1;
     const int b = q % a.nb, h = q / a.nb, ch = h * 64 + i;
     if (nx < q1) {
       const float4* src = state_of(nx);
@@ -907,30 +933,34 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
       for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[(st ^ 1) * 1024 + t + 256 * u], &src[t + 256 * u]);
     }
     cp_async_commit();  // an empty group when there is no next pair
-    BtWkvChan nxt{};
-    float kn = 0.f, v = 0.f;
     if (chan) {
+      BtWkvChan nxt{};
       if (nx < q1) nxt = bt_wkv_chan(a, nx % a.nb, (nx / a.nb) * 64 + i);
       if (h != vh) {
         vh = h;
         kkw = a.k_k[ch], a0v = a.a0[ch], w0v = a.w0[ch], kav = a.k_a[ch], rkv = a.r_k[ch];
-        lw = a.lnx_w[ch], lb = a.lnx_b[ch];
         v0v = a.layer0 ? 0.f : a.v0[ch];
       }
-      v = cur.v;
+      float v = cur.v;
       const float kkv = cur.k * kkw;
       const float aa = sigmoidf_(a0v + cur.av);
       if (a.layer0) a.vfirst[(size_t)b * a.C + ch] = v;
       else v = v + (cur.vf - v) * sigmoidf_(v0v + cur.vg);
       const float nrm = sqrtf(bt_chan_sum2(kkv * kkv, 0.f, red2).x);
       const float kk = kkv / fmaxf(nrm, 1e-12f);
-      kn = cur.k * (1.0f + (aa - 1.0f) * kav);
+      const float kn = cur.k * (1.0f + (aa - 1.0f) * kav);
       vd[i] = expf(-0.606531f * sigmoidf_(w0v + cur.wv));
       vkk[i] = -kk;
       vka[i] = kk * aa;
       vk[i] = kn;
       vr[i] = cur.r;
       vv[i] = v;
+      gbon[par][i] = cur.r * kn * rkv;
+      gv[par][i] = v;
+      ggate[par][i] = cur.gv;
+      cur = nxt;
+    } else if (gnw && it > 0) {
+      group_norm(q - 1, par ^ 1);  // the previous pair (its sy is complete)
     }
     cp_async_wait_group<1>();  // this pair's stage (the group before the prefetch just issued)
     __syncthreads();
@@ -968,19 +998,8 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
       }
     }
     __syncthreads();  // sy complete; stage st and the vectors are free again
-    if (chan) {
-      // GroupNorm over the head (eps 64e-5), bonus, gate
-      const float y = sy[i];
-      const float2 mb = bt_chan_sum2(y, cur.r * kn * rkv, red2);
-      const float mean = mb.x / 64.f;
-      const float dv = y - mean;
-      const float var = bt_chan_sum2(dv * dv, 0.f, red2).x / 64.f;
-      float o = dv * rsqrtf(var + 64e-5f) * lw + lb;
-      o = o + mb.y * v;
-      a.att_y[(size_t)b * a.C + ch] = o * cur.gv;
-    }
-    cur = nxt;
   }
+  if (gnw) group_norm(q1 - 1, (q1 - 1 - q0) & 1);  // the last pair
   cp_async_wait_all();
 }
 
