@@ -139,7 +139,7 @@ __device__ __forceinline__ bool bg_wait(uint64_t* bar, uint32_t parity, const Bg
   int ok = 0;
   if ((threadIdx.x & 31) == 0) {
     if (!*abort_flag) {
-      ok = mbar_wait_suspend(bar, parity) ? 1 : 0;
+      ok = mbar_wait_spin(bar, parity, kWaitLimitNs) ? 1 : 0;  // one polling lane per warp: prompt hand-offs
       if (!ok) {
         atomicOr(a.err, kErrTimeout);
         *abort_flag = 1;
