@@ -170,9 +170,6 @@ struct DArgs {
   // FFN value rows in column-chunk order with fixed-point accumulation (0:
   // row order, fp32 atomics)
   int ecm;
-  // streaming copy: once this CTA's output-projection units are issued, pull
-  // its FFN key and value unit images into L2 (HBM is idle while phase B runs)
-  int l2_ahead;
 };
 
 struct DTable {
@@ -401,25 +398,6 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
   return ok;
 }
 
-// L2 prefetch of the unit images [R.u0, R.u1) of one streaming copy (same
-// unit order as d_issue_units).
-__device__ __noinline__ void d_prefetch_units(const DArgs& a, const DRange& R, const uint8_t* su, int tiles_cm) {
-  const uint32_t bytes = a.code_b + a.pair_b;
-  const int nch = R.nch;
-  for (int u = R.u0; u < R.u1; ++u) {
-    int tile, chunk;
-    if (tiles_cm) {
-      const int mat = u / (nch * tiles_cm), rem = u - mat * nch * tiles_cm;
-      chunk = rem / tiles_cm;
-      tile = mat * tiles_cm + rem - chunk * tiles_cm;
-    } else {
-      tile = u / nch;
-      chunk = u - tile * nch;
-    }
-    prefetch_l2_bulk(su + (size_t)(tile * nch + chunk) * bytes, bytes);
-  }
-}
-
 // One adapter first-stage item (rows [i0, i1) of W1 [C][R] and the (min, max)
 // pairs of the groups they touch) into `dst`, completing on `bar`.
 __device__ __noinline__ void d_issue_item(const DArgs& a, const LayerDev& Ly, int item, uint8_t* dst, uint64_t* bar) {
@@ -571,10 +549,6 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
           }
         }
         if (ok) ok = units(T.r[1], M.q + 3, M.p + 3, 0, M.su[1]);
-        if (ok && a.l2_ahead && M.su[2] && M.su[3]) {
-          d_prefetch_units(a, T.r[2], M.su[2], 0);
-          d_prefetch_units(a, T.r[3], M.su[3], a.ecm ? C / 16 : 0);
-        }
         if (ok) ok = units(T.r[2], M.q + 4, M.p + 4, 0, M.su[2]);
         if (ok) ok = units(T.r[3], M.q + 5, M.p + 5, 0, M.su[3], a.ecm ? C / 16 : 0);
       }

@@ -1209,7 +1209,6 @@ bool plan_decode(rwkvb_engine* e) {
   a.d = d;
   a.spin_limit = 1u << 22;
   a.l2_first = (e->flags & 0x200u) ? 0 : 1;  // bit 9: plain weight-stream loads (no L2 policy)
-  a.l2_ahead = (e->flags & 0x20000u) ? 1 : 0;  // bit 17: FFN unit images pulled into L2 during phase B
   const PackedView& E = e->emb;
   a.emb_fast = E.kind == RWKVB_KIND_SG8 && E.lg >= 4 && d.C % (int)E.group == 0 && ((d.C >> E.lg) % 2) == 0 &&
                aligned16(E.payload) && aligned16(E.meta);
