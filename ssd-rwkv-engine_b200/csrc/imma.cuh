@@ -237,22 +237,8 @@ __device__ __forceinline__ void imma_block(const uint8_t* blk, const float2* pa,
 #pragma unroll
   for (int f = 0; f < NF; ++f) {
     int d[4] = {0, 0, 0, 0};
-    if constexpr (KPF >= 4) {
-      // two independent accumulation chains (even and odd k-steps), summed
-      // exactly: half the dependent MMA latency per flush group
-      int e[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int j = f * KPF; j < (f + 1) * KPF; j += 2) {
-        imma_16832(d, w0[j].x, w1[j].x, w0[j].y, w1[j].y, bb[j].x, bb[j].y);
-        imma_16832(e, w0[j + 1].x, w1[j + 1].x, w0[j + 1].y, w1[j + 1].y, bb[j + 1].x, bb[j + 1].y);
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) d[i] += e[i];
-    } else {
-#pragma unroll
-      for (int j = f * KPF; j < (f + 1) * KPF; ++j)
-        imma_16832(d, w0[j].x, w1[j].x, w0[j].y, w1[j].y, bb[j].x, bb[j].y);
-    }
+    for (int j = f * KPF; j < (f + 1) * KPF; ++j) imma_16832(d, w0[j].x, w1[j].x, w0[j].y, w1[j].y, bb[j].x, bb[j].y);
     if (t < 2) {
       const int fg = (ks >> LFK) + f;
       const float c = X.xc[fg];
