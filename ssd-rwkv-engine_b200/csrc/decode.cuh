@@ -572,7 +572,10 @@ __device__ void d_producer(const DArgs& a, const DTable& T, uint8_t* ring, uint6
 // layer executes stays small enough to remain in the instruction caches while
 // the weight stream sweeps L2.
 
-// Consumer state shared by the subroutines.
+// Consumer state shared by the subroutines: one copy per consumer warp in
+// shared memory (the same values on every lane).  Kept in local memory it
+// would be re-read from L2 after every phase: the carve-out leaves the SM a
+// small L1, which the phase's vector loads sweep.
 struct DCons {
   uint8_t* sm;  // 1024-aligned dynamic shared memory (ring at offset 0)
   uint64_t* full;
@@ -585,6 +588,15 @@ struct DCons {
   uint64_t* pbar;  // preload mode: adp full/empty, item full/empty
   int nadp, nitm;  // dedicated-buffer loads consumed
 };
+
+// Warp-uniform update of a field of the warp's DCons: every lane reads the
+// old value (the argument) before lane 0 stores the new one.
+template <typename T>
+__device__ __forceinline__ void d_wset(T& f, T v) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) f = v;
+  __syncwarp();
+}
 
 // Consumers: wait for a dedicated-buffer load (all threads); a failed wait
 // marks this CTA dead like a ring wait.
@@ -605,7 +617,7 @@ __device__ __forceinline__ void d_csync() { bar_sync(kDBar, kDT); }
 __device__ __forceinline__ void d_mark(const DArgs& a, DCons& c) {
   if (a.trace && c.trow >= 0 && threadIdx.x == 0 && c.tr < a.trace_cap)
     a.trace[(size_t)c.trow * a.trace_cap + c.tr] = global_ns();
-  ++c.tr;
+  d_wset(c.tr, c.tr + 1);
 }
 
 // Sum over the consumer threads (all of them get the result).
@@ -646,7 +658,7 @@ __device__ __forceinline__ float2 d_sum64x2(float v, float w, float* red) {
 // earlier wait of this CTA failed.
 __device__ __noinline__ bool d_gsync(const DArgs& a, DCons& c) {
   d_csync();
-  c.target += gridDim.x;
+  d_wset(c.target, c.target + gridDim.x);
   if (threadIdx.x == 0) {
     bool ok = !*c.abort;
     if (ok) {
@@ -718,8 +730,8 @@ struct DSrc {
 };
 
 template <int LFK>
-__device__ __noinline__ void d_build(const DSrc& src, int K, uint8_t* base) {
-  const DSrc S = src;
+__device__ __noinline__ void d_build(int kind, const float* z, const float* p, const float* g, int K, uint8_t* base) {
+  const DSrc S{kind, z, p, g};
   auto get4 = [&](int i) -> float4 {
     if (S.kind == 0) {
       const float4 z = *reinterpret_cast<const float4*>(S.z + i), p = *reinterpret_cast<const float4*>(S.p + i);
@@ -782,6 +794,15 @@ struct DLnMix {
   float* ln;     // shared LayerNorm output
   float* stat;   // mean, rstd (nullptr: not kept)
 };
+
+// The warp's shared-memory copy of a prep's operands (stored by lane 0), so
+// the prep reads them from shared memory rather than from the stack.
+__device__ __forceinline__ const DLnMix& d_warp_copy(DLnMix& dst, const DLnMix& q) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) dst = q;
+  __syncwarp();
+  return dst;
+}
 
 // y = LayerNorm(xs + add); for each mix m: digits of y + (prev - y) * mix_m
 // into dig + m * stride.  One item of 8 columns per consumer thread (C <= 8 *
@@ -869,7 +890,7 @@ __device__ __forceinline__ void d_slot_release(const DArgs& a, DCons& c) {
   if ((threadIdx.x & 31) == 0) mbar_arrive(&c.empty[c.seq % a.nst]);
   if (a.trace && blockIdx.x == 0 && threadIdx.x == 0 && 3 * c.seq + 2 < 2 * a.trace_cap)
     a.trace[2 * (size_t)a.trace_cap + 3 * c.seq + 2] = global_ns();
-  ++c.seq;
+  d_wset(c.seq, c.seq + 1);
 }
 
 // GEMV units of one phase: out[row] += W[row, :] @ x for this CTA's units.
@@ -977,16 +998,19 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
       ++tile;
     }
   }
-  c.seq = seq;
-  c.dead = dead;
+  __syncwarp();
+  if (lane == 0) {
+    c.seq = seq;
+    c.dead = dead;
+  }
+  __syncwarp();
 }
 
 // Adapter first stages of this CTA (rows [i0, i1) of W1 [C][R] times the
 // mixed input), accumulated in 2^-32 fixed point.
-__device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, int l, const float* TV,
-                                     const float* PV, float* misc) {
+__device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, int l, const LayerDev& Ly,
+                                     const float* TV, const float* PV, float* misc) {
   const int t = threadIdx.x, C = a.d.C;
-  const LayerDev& Ly = a.layers[l];
   for (int k = 0; k < T.nitem[l == 0 ? 0 : 1]; ++k) {
     const int item = T.item[k];
     const int m = d_item_mat(a.d, item);
@@ -1045,7 +1069,7 @@ __device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, 
     d_csync();
     if (a.pre) {
       if (t == 0) mbar_arrive(&c.pbar[3]);  // the item buffer may be refilled
-      ++c.nitm;
+      d_wset(c.nitm, c.nitm + 1);
     }
     if (!c.dead) {
       const int off = d_rank_off(a.d, m);
@@ -1182,9 +1206,9 @@ __device__ __noinline__ void d_pieces_mma(const DArgs& a, DCons& c, const DTable
 
 // Phase B for head h = blockIdx.x: adapter second stages, kk-normalize, decay,
 // WKV7 update of S (already in shared memory), GroupNorm, bonus, gate.
-__device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& T, int l, float* S, float* misc) {
+__device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& T, int l, const LayerDev& Ly,
+                                        float* S, float* misc) {
   const int t = threadIdx.x, C = a.d.C, H = a.d.H, h = blockIdx.x;
-  const LayerDev& Ly = a.layers[l];
   float* mid = S + 4096;                     // [rtot]
   float* vec = mid + ((a.d.rtot + 3) & ~3);  // [4][64]
   float* sr = vec + 256;
@@ -1241,7 +1265,7 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
   if (a.pre) {
     d_pieces_mma(a, c, T, l, mid, misc, vec);
     if (t == 0) mbar_arrive(&c.pbar[1]);  // the head image buffer may be refilled
-    ++c.nadp;
+    d_wset(c.nadp, c.nadp + 1);
   } else {
     // 16 lanes per tile row, 4 columns each (one 32-bit code word); the two
     // half-warps take alternate rows: row phase rp of 20.  Per row the scale
@@ -1360,6 +1384,22 @@ __device__ __noinline__ void d_head_wkv(const DArgs& a, DCons& c, const DTable& 
   }
 }
 
+// Copy layer l's descriptor (weight views, vector pointers) into shared
+// memory with 4-byte cp.async copies (the caller commits and waits): read
+// from global memory it would cost a dependent L2 round trip at the start of
+// every phase that uses it.
+__device__ __forceinline__ void d_load_layer(const DArgs& a, LayerDev* dst, int l) {
+  static_assert(sizeof(LayerDev) % 4 == 0, "layer descriptor in 4-byte words");
+  constexpr int kWords = (int)(sizeof(LayerDev) / 4);
+  const int t = threadIdx.x;
+  if (t < kWords) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(a.layers + l) + t;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(reinterpret_cast<uint32_t*>(dst) + t)),
+                 "l"(src)
+                 : "memory");
+  }
+}
+
 // X = LayerNorm0(emb[tok]).
 __device__ __noinline__ void d_embed(const DArgs& a, DCons& c, int tok, float* X, float* TV, float* PV) {
   const int t = threadIdx.x, C = a.d.C;
@@ -1472,6 +1512,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   __shared__ float s_bv[kDW];
   __shared__ int s_bi[kDW];
   __shared__ float s_stat[4];  // mean / rstd of ln1 and ln2
+  __shared__ DCons s_cons[kDW];
+  __shared__ DLnMix s_q[kDW];
+  __shared__ __align__(16) LayerDev s_ly[2];  // descriptors of the current and the next layer
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   if (t == 0) {
@@ -1498,18 +1541,21 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   float* PV = reinterpret_cast<float*>(sm + a.o_p);   // previous-token vector
   float* misc = reinterpret_cast<float*>(sm + a.o_misc);
   uint8_t* dig = sm + a.o_dig;
-  DCons c;
-  c.sm = sm;
-  c.full = full;
-  c.empty = empty;
-  c.red = red;
-  c.abort = &s_abort;
-  c.flag = &s_flag;
-  c.seq = c.pbuf = c.dead = c.tr = 0;
-  c.pbar = pbar;
-  c.nadp = c.nitm = 0;
-  c.trow = bx == 0 ? 0 : (bx == G - 1 ? 1 : -1);
-  c.target = 0;
+  DCons& c = s_cons[warp];
+  if (lane == 0) {
+    c.sm = sm;
+    c.full = full;
+    c.empty = empty;
+    c.red = red;
+    c.abort = &s_abort;
+    c.flag = &s_flag;
+    c.seq = c.pbuf = c.dead = c.tr = 0;
+    c.pbar = pbar;
+    c.nadp = c.nitm = 0;
+    c.trow = bx == 0 ? 0 : (bx == G - 1 ? 1 : -1);
+    c.target = 0;
+  }
+  __syncwarp();
 
   float* acc_rkv = a.b.rkv;
   float* acc_ao = a.b.ao;
@@ -1533,7 +1579,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   // streamed decode: the host's cancel word as CTA 0 read it during the
   // previous token's head (loaded a token ahead, so no step waits on the bus)
   int cancel_next = 0;
+  d_load_layer(a, &s_ly[0], 0);
+  cp_async_commit();
+  cp_async_wait_all();  // published by the barrier below
   bool alive = d_gsync(a, c);
+  int gl = 0;  // layers run by this launch: s_ly[gl & 1] holds layer l's descriptor
   for (int step = 0; step < a.ntok && alive; ++step) {
     const bool head = a.mode == 0 || step == a.ntok - 1;
     if (a.mode == 1) tok = __ldg(a.forced + step);
@@ -1542,13 +1592,17 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       tok = 0;
     }
     d_mark(a, c);  // token start
+    cp_async_wait_all();  // layer 0's descriptor, published by the barriers of d_embed
     d_embed(a, c, tok, X, TV, PV);
 
-    for (int l = 0; l < a.d.L && alive; ++l) {
-      const LayerDev& Ly = a.layers[l];
-      if (l > 0 && !d_gsync(a, c)) {
-        alive = false;
-        break;
+    for (int l = 0; l < a.d.L && alive; ++l, ++gl) {
+      const LayerDev& Ly = s_ly[gl & 1];
+      if (l > 0) {
+        cp_async_wait_all();  // this layer's descriptor, published by the barrier
+        if (!d_gsync(a, c)) {
+          alive = false;
+          break;
+        }
       }
       d_mark(a, c);  // A start
       // ================= A: ln1, mixes, r/k/v rows, adapter first stages
@@ -1569,7 +1623,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.need = T.aneed;  // only the r/k/v digit sets this CTA's units read
         q.ln = TV;
         q.stat = s_stat;
-        d_ln_mix<LFK>(a, c, q, dig, a.dig_set);
+        d_ln_mix<LFK>(a, c, d_warp_copy(s_q[warp], q), dig, a.dig_set);
       } else {
         if (l > 0) {
 #pragma unroll 1
@@ -1580,24 +1634,27 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
 #pragma unroll 1
         for (int i = t; i < C; i += kDT) PV[i] = __ldcg(a.b.att_x + (size_t)l * C + i);
         d_csync();
-        if (T.aneed & 1u) d_build<LFK>(DSrc{0, TV, PV, Ly.x_r}, C, dig);
-        if (T.aneed & 2u) d_build<LFK>(DSrc{0, TV, PV, Ly.x_k}, C, dig + a.dig_set);
-        if (T.aneed & 4u) d_build<LFK>(DSrc{0, TV, PV, Ly.x_v}, C, dig + 2 * a.dig_set);
+        if (T.aneed & 1u) d_build<LFK>(0, TV, PV, Ly.x_r, C, dig);
+        if (T.aneed & 2u) d_build<LFK>(0, TV, PV, Ly.x_k, C, dig + a.dig_set);
+        if (T.aneed & 4u) d_build<LFK>(0, TV, PV, Ly.x_v, C, dig + 2 * a.dig_set);
       }
       d_mark(a, c);  // A prep done
       d_units<LFK>(a, c, T.r[0], dig, a.dig_set, C, C / 16, acc_rkv, 3 * C);
       d_mark(a, c);  // A units done
-      d_items(a, c, T, l, TV, PV, misc);
+      d_items(a, c, T, l, Ly, TV, PV, misc);
       d_mark(a, c);  // A done
       // ================= B: one CTA per head
       const bool is_head = bx < H;
       float* S = reinterpret_cast<float*>(dig);  // digit sets are dead in B
+      // the next layer's descriptor (the other buffer: the last reads of the
+      // previous layer's ended with its phase D)
+      d_load_layer(a, &s_ly[(gl + 1) & 1], l + 1 < a.d.L ? l + 1 : 0);
       if (is_head) {
         const float* Sg = a.b.wkv + ((size_t)l * H + bx) * 4096;
         #pragma unroll 1
         for (int u = t; u < 1024; u += kDT) cp_async16(S + u * 4, Sg + u * 4);
-        cp_async_commit();
       }
+      cp_async_commit();
       if (!d_gsync(a, c)) {
         alive = false;
         break;
@@ -1605,7 +1662,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_mark(a, c);  // B barrier
       d_zero(acc_hk, T.zf0, T.zf1);
       if (l == 0) d_zero(logits, T.zv0, T.zv1);
-      if (is_head) d_head_wkv(a, c, T, l, S, misc);
+      if (is_head) d_head_wkv(a, c, T, l, Ly, S, misc);
       d_mark(a, c);  // B done
       if (!d_gsync(a, c)) {
         alive = false;
@@ -1622,7 +1679,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
         a.b.att_x[(size_t)l * C + i] = TV[i];  // ln1 output of phase A, still in shared memory
-      d_build<LFK>(DSrc{2, nullptr, nullptr, a.b.att_y}, C, dig);
+      d_build<LFK>(2, nullptr, nullptr, a.b.att_y, C, dig);
       d_mark(a, c);  // C prep done
       d_units<LFK>(a, c, T.r[1], dig, 0, C, 0, acc_ao, C);
       d_mark(a, c);  // C done
@@ -1648,7 +1705,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.need = 1u;
         q.ln = TV;
         q.stat = s_stat + 2;
-        d_ln_mix<LFK>(a, c, q, dig, 0);
+        d_ln_mix<LFK>(a, c, d_warp_copy(s_q[warp], q), dig, 0);
       } else {
 #pragma unroll 1
         for (int i = t; i < C; i += kDT) {
@@ -1657,7 +1714,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         }
         d_csync();
         d_layer_norm(TV, XB, Ly.ln2_w, Ly.ln2_b, C, s_stat + 2, red);
-        d_build<LFK>(DSrc{0, TV, PV, Ly.ffn_x_k}, C, dig);
+        d_build<LFK>(0, TV, PV, Ly.ffn_x_k, C, dig);
       }
       d_mark(a, c);  // D prep done
       d_units<LFK>(a, c, T.r[2], dig, 0, C, 0, acc_hk, F);
@@ -1676,11 +1733,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       if (ecm) {
         // only the chunks of this CTA's units: [ech0, ech1] of kc columns each
         const int k0 = T.ech0 * a.kc, kl = (T.ech1 - T.ech0 + 1) * a.kc;
-        d_build<LFK>(DSrc{3, nullptr, nullptr, acc_hk + k0}, kl, dig);
+        d_build<LFK>(3, nullptr, nullptr, acc_hk + k0, kl, dig);
         d_mark(a, c);  // E prep done
         d_units<LFK>(a, c, T.r[3], dig, 0, kl, 0, nullptr, C, C / 16, T.ech0, fo64);
       } else {
-        d_build<LFK>(DSrc{3, nullptr, nullptr, acc_hk}, F, dig);
+        d_build<LFK>(3, nullptr, nullptr, acc_hk, F, dig);
         d_mark(a, c);  // E prep done
         d_units<LFK>(a, c, T.r[3], dig, 0, F, 0, acc_fo, C);
       }
@@ -1714,13 +1771,13 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       q.nmix = 1;
       q.need = 1u;
       q.ln = TV;
-      d_ln_mix<LFK>(a, c, q, dig, 0);
+      d_ln_mix<LFK>(a, c, d_warp_copy(s_q[warp], q), dig, 0);
     } else {
 #pragma unroll 1
       for (int i = t; i < C; i += kDT) PV[i] = XB[i] + (ecm ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
       d_csync();
       d_layer_norm(TV, PV, a.lnout_w, a.lnout_b, C, nullptr, red);
-      d_build<LFK>(DSrc{1, TV, nullptr, nullptr}, C, dig);
+      d_build<LFK>(1, TV, nullptr, nullptr, C, dig);
     }
     d_mark(a, c);  // head prep done
     d_units<LFK>(a, c, T.r[4], dig, 0, C, 0, logits, a.d.V);
