@@ -1585,11 +1585,12 @@ __device__ bool bt_x_handshake(const BtXPeers& P, size_t flags_off, int inst, in
   __threadfence_system();
   for (int r = 0; r < size; ++r)
     if (r != rank) bt_st_release_sys(bt_x_flag(P.base[r], flags_off, inst, rank, cta), ep);
-  const uint64_t t0 = globaltimer_ns();
+  uint64_t t0 = 0;  // the wall clock is read only once a flag was not there at the first poll
   for (int r = 0; r < size; ++r) {
     if (r == rank) continue;
     const uint32_t* f = bt_x_flag(P.base[rank], flags_off, inst, r, cta);
     while (bt_ld_acquire_sys(f) != ep) {
+      if (t0 == 0) t0 = globaltimer_ns();
       if (globaltimer_ns() - t0 > limit_ns) {
         atomicOr(err, kErrTimeout);
         return false;

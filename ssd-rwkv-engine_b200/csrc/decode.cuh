@@ -94,6 +94,14 @@ __device__ __forceinline__ void d_st_relaxed_sys(unsigned* p, unsigned v) {
 __device__ __forceinline__ void red_add_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+  asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+// Grid-barrier arrival: the release orders every write this CTA made before
+// its preceding CTA barrier ahead of the count.
+__device__ __forceinline__ void red_release_add_u32(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ unsigned d_ld_acquire(const unsigned* p) {
   unsigned v;
@@ -306,6 +314,7 @@ __device__ __noinline__ int d_acquire(const DArgs& a, uint64_t* empty, volatile 
   const int slot = seq % a.nst;
   if (seq >= a.nst) {
     const uint32_t par = (uint32_t)((seq / a.nst - 1) & 1);
+    if (mbar_try_wait_hint(&empty[slot], par, 20000u)) return slot;  // no wall-clock read on the common path
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait_hint(&empty[slot], par, 20000u)) {  // suspended, not spinning, while the ring is full
       if (*abort_flag) return -1;
@@ -349,8 +358,9 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     const int slot = seq % nst;
     if (seq >= nst) {
       const uint32_t par = (uint32_t)((seq / nst - 1) & 1);
-      const uint64_t t0 = globaltimer_ns();
+      uint64_t t0 = 0;  // the wall clock is read only once a wait has not ended at the first poll
       while (!mbar_try_wait_hint(&empty[slot], par, 20000u)) {
+        if (t0 == 0) t0 = globaltimer_ns();
         if (*abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
           if (!*abort_flag) {
             atomicOr(a.b.err, kErrTimeout);
@@ -432,6 +442,7 @@ __device__ __noinline__ void d_issue_item(const DArgs& a, const LayerDev& Ly, in
 __device__ __noinline__ bool d_pre_acquire(const DArgs& a, uint64_t* empty, int n, volatile int* abort_flag) {
   if (n == 0) return true;
   const uint32_t par = (uint32_t)((n - 1) & 1);
+  if (mbar_try_wait_hint(empty, par, 20000u)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (!mbar_try_wait_hint(empty, par, 20000u)) {
     if (*abort_flag) return false;
@@ -662,8 +673,7 @@ __device__ __noinline__ bool d_gsync(const DArgs& a, DCons& c) {
   if (threadIdx.x == 0) {
     bool ok = !*c.abort;
     if (ok) {
-      __threadfence();
-      atomicAdd(a.gbar, 1u);
+      red_release_add_u32(a.gbar, 1u);
       ok = false;
       for (uint32_t i = 0; i < a.spin_limit; ++i) {
         if (d_ld_acquire(a.gbar) >= c.target) {
@@ -981,7 +991,7 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
           const int row = ptile[i >> 4] * 16 + (i & 15);
           if (row < rows_total && !dead) {
             if (out64) red_add_u64(out64 + row, (unsigned long long)__float2ll_rn(v * kFix));
-            else atomicAdd(out + row, v);
+            else red_add_f32(out + row, v);
           }
         }
         d_csync();  // the buffer is rewritten next
@@ -1077,7 +1087,7 @@ __device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, 
       for (int j = t; j < R; j += kDT) {
         float v = 0.f;
         for (int rg = 0; rg < (q4 < kDT ? kDT / q4 : 1); ++rg) v += pacc[rg * R + j];
-        atomicAdd(a.b.adp64 + off + j, (unsigned long long)__float2ll_rn(v * kFix));
+        red_add_u64(a.b.adp64 + off + j, (unsigned long long)__float2ll_rn(v * kFix));
       }
     }
     d_csync();
@@ -1500,7 +1510,7 @@ __device__ __noinline__ int d_argmax_all(const DArgs& a, int* s_tok) {
 
 // --------------------------------------------------------------- kernel
 template <int LFK>
-__global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_constant__ DArgs a) {
+__global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_constant__ DArgs ga) {
   extern __shared__ __align__(1024) uint8_t d_smraw[];
   uint8_t* sm = d_smraw + ((1024u - (smem_u32(d_smraw) & 1023u)) & 1023u);
   __shared__ DTable T;
@@ -1515,11 +1525,21 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   __shared__ DCons s_cons[kDW];
   __shared__ DLnMix s_q[kDW];
   __shared__ __align__(16) LayerDev s_ly[2];  // descriptors of the current and the next layer
+  // the launch arguments in shared memory: indexed reads of the parameter
+  // space miss the SM's small constant cache and go out to memory
+  __shared__ __align__(16) DArgs s_args;
+  static_assert(sizeof(DArgs) % 4 == 0 && sizeof(DArgs) <= 1024, "launch arguments in shared memory");
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  for (int i = t; i < (int)(sizeof(DArgs) / 4); i += (int)blockDim.x)
+    reinterpret_cast<uint32_t*>(&s_args)[i] = reinterpret_cast<const uint32_t*>(&ga)[i];
+  __syncthreads();
+  // the subroutines read the shared copy; the code below reads fields of the
+  // parameter itself at fixed offsets (constant-bank operands)
+  const DArgs& a = s_args;
   if (t == 0) {
     d_build_table(a, T);
-    for (int i = 0; i < a.nst; ++i) {
+    for (int i = 0; i < ga.nst; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], kDW);
     }
@@ -1533,14 +1553,14 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     return;
   }
 
-  const int C = a.d.C, F = a.d.F, H = a.d.H, G = gridDim.x, bx = blockIdx.x;
+  const int C = ga.d.C, F = ga.d.F, H = ga.d.H, G = gridDim.x, bx = blockIdx.x;
   const bool fused = C <= 8 * kDT;  // one 8-column item per consumer thread: single-round preps
-  float* X = reinterpret_cast<float*>(sm + a.o_x);    // layer input (residual stream)
-  float* XB = reinterpret_cast<float*>(sm + a.o_xb);  // after attention
-  float* TV = reinterpret_cast<float*>(sm + a.o_t);   // normalised vector
-  float* PV = reinterpret_cast<float*>(sm + a.o_p);   // previous-token vector
-  float* misc = reinterpret_cast<float*>(sm + a.o_misc);
-  uint8_t* dig = sm + a.o_dig;
+  float* X = reinterpret_cast<float*>(sm + ga.o_x);    // layer input (residual stream)
+  float* XB = reinterpret_cast<float*>(sm + ga.o_xb);  // after attention
+  float* TV = reinterpret_cast<float*>(sm + ga.o_t);   // normalised vector
+  float* PV = reinterpret_cast<float*>(sm + ga.o_p);   // previous-token vector
+  float* misc = reinterpret_cast<float*>(sm + ga.o_misc);
+  uint8_t* dig = sm + ga.o_dig;
   DCons& c = s_cons[warp];
   if (lane == 0) {
     c.sm = sm;
@@ -1557,11 +1577,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   }
   __syncwarp();
 
-  float* acc_rkv = a.b.rkv;
-  float* acc_ao = a.b.ao;
-  float* acc_hk = a.b.h;
-  float* acc_fo = a.b.fo;
-  float* logits = a.b.logits;
+  float* acc_rkv = ga.b.rkv;
+  float* acc_ao = ga.b.ao;
+  float* acc_hk = ga.b.h;
+  float* acc_fo = ga.b.fo;
+  float* logits = ga.b.logits;
 
   // accumulators start from zero in every launch (a failed launch may leave partial sums)
   d_zero(acc_rkv, T.z3c0, T.z3c1);
@@ -1570,12 +1590,12 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   d_zero(acc_fo, T.zc0, T.zc1);
   d_zero(logits, T.zv0, T.zv1);
   #pragma unroll 1
-  for (int i = T.zr0 + t; i < T.zr1; i += kDT) a.b.adp64[i] = 0ull;
-  const bool ecm = a.ecm != 0;  // FFN value rows in chunk order, output in fixed point
-  unsigned long long* fo64 = a.b.fo64;
+  for (int i = T.zr0 + t; i < T.zr1; i += kDT) ga.b.adp64[i] = 0ull;
+  const bool ecm = ga.ecm != 0;  // FFN value rows in chunk order, output in fixed point
+  unsigned long long* fo64 = ga.b.fo64;
   #pragma unroll 1
   for (int i = T.zc0 + t; i < T.zc1; i += kDT) fo64[i] = 0ull;
-  int tok = a.mode == 0 ? (a.first_tok >= 0 ? a.first_tok : __ldcg(a.b.tok)) : __ldg(a.forced);
+  int tok = ga.mode == 0 ? (ga.first_tok >= 0 ? ga.first_tok : __ldcg(ga.b.tok)) : __ldg(ga.forced);
   // streamed decode: the host's cancel word as CTA 0 read it during the
   // previous token's head (loaded a token ahead, so no step waits on the bus)
   int cancel_next = 0;
@@ -1584,18 +1604,18 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   cp_async_wait_all();  // published by the barrier below
   bool alive = d_gsync(a, c);
   int gl = 0;  // layers run by this launch: s_ly[gl & 1] holds layer l's descriptor
-  for (int step = 0; step < a.ntok && alive; ++step) {
-    const bool head = a.mode == 0 || step == a.ntok - 1;
-    if (a.mode == 1) tok = __ldg(a.forced + step);
-    if (tok < 0 || tok >= a.d.V) {
-      if (t == 0) atomicOr(a.b.err, kErrToken);
+  for (int step = 0; step < ga.ntok && alive; ++step) {
+    const bool head = ga.mode == 0 || step == ga.ntok - 1;
+    if (ga.mode == 1) tok = __ldg(ga.forced + step);
+    if (tok < 0 || tok >= ga.d.V) {
+      if (t == 0) atomicOr(ga.b.err, kErrToken);
       tok = 0;
     }
     d_mark(a, c);  // token start
     cp_async_wait_all();  // layer 0's descriptor, published by the barriers of d_embed
     d_embed(a, c, tok, X, TV, PV);
 
-    for (int l = 0; l < a.d.L && alive; ++l, ++gl) {
+    for (int l = 0; l < ga.d.L && alive; ++l, ++gl) {
       const LayerDev& Ly = s_ly[gl & 1];
       if (l > 0) {
         cp_async_wait_all();  // this layer's descriptor, published by the barrier
@@ -1614,7 +1634,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.xo = X;
         q.w = Ly.ln1_w;
         q.b = Ly.ln1_b;
-        q.prev = a.b.att_x + (size_t)l * C;
+        q.prev = ga.b.att_x + (size_t)l * C;
         q.pv = PV;
         q.mix[0] = Ly.x_r;
         q.mix[1] = Ly.x_k;
@@ -1623,7 +1643,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.need = T.aneed;  // only the r/k/v digit sets this CTA's units read
         q.ln = TV;
         q.stat = s_stat;
-        d_ln_mix<LFK>(a, c, d_warp_copy(s_q[warp], q), dig, a.dig_set);
+        d_ln_mix<LFK>(a, c, d_warp_copy(s_q[warp], q), dig, ga.dig_set);
       } else {
         if (l > 0) {
 #pragma unroll 1
@@ -1632,14 +1652,14 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         }
         d_layer_norm(TV, X, Ly.ln1_w, Ly.ln1_b, C, s_stat, red);
 #pragma unroll 1
-        for (int i = t; i < C; i += kDT) PV[i] = __ldcg(a.b.att_x + (size_t)l * C + i);
+        for (int i = t; i < C; i += kDT) PV[i] = __ldcg(ga.b.att_x + (size_t)l * C + i);
         d_csync();
         if (T.aneed & 1u) d_build<LFK>(0, TV, PV, Ly.x_r, C, dig);
-        if (T.aneed & 2u) d_build<LFK>(0, TV, PV, Ly.x_k, C, dig + a.dig_set);
-        if (T.aneed & 4u) d_build<LFK>(0, TV, PV, Ly.x_v, C, dig + 2 * a.dig_set);
+        if (T.aneed & 2u) d_build<LFK>(0, TV, PV, Ly.x_k, C, dig + ga.dig_set);
+        if (T.aneed & 4u) d_build<LFK>(0, TV, PV, Ly.x_v, C, dig + 2 * ga.dig_set);
       }
       d_mark(a, c);  // A prep done
-      d_units<LFK>(a, c, T.r[0], dig, a.dig_set, C, C / 16, acc_rkv, 3 * C);
+      d_units<LFK>(a, c, T.r[0], dig, ga.dig_set, C, C / 16, acc_rkv, 3 * C);
       d_mark(a, c);  // A units done
       d_items(a, c, T, l, Ly, TV, PV, misc);
       d_mark(a, c);  // A done
@@ -1648,9 +1668,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       float* S = reinterpret_cast<float*>(dig);  // digit sets are dead in B
       // the next layer's descriptor (the other buffer: the last reads of the
       // previous layer's ended with its phase D)
-      d_load_layer(a, &s_ly[(gl + 1) & 1], l + 1 < a.d.L ? l + 1 : 0);
+      d_load_layer(a, &s_ly[(gl + 1) & 1], l + 1 < ga.d.L ? l + 1 : 0);
       if (is_head) {
-        const float* Sg = a.b.wkv + ((size_t)l * H + bx) * 4096;
+        const float* Sg = ga.b.wkv + ((size_t)l * H + bx) * 4096;
         #pragma unroll 1
         for (int u = t; u < 1024; u += kDT) cp_async16(S + u * 4, Sg + u * 4);
       }
@@ -1678,8 +1698,8 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       }
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
-        a.b.att_x[(size_t)l * C + i] = TV[i];  // ln1 output of phase A, still in shared memory
-      d_build<LFK>(2, nullptr, nullptr, a.b.att_y, C, dig);
+        ga.b.att_x[(size_t)l * C + i] = TV[i];  // ln1 output of phase A, still in shared memory
+      d_build<LFK>(2, nullptr, nullptr, ga.b.att_y, C, dig);
       d_mark(a, c);  // C prep done
       d_units<LFK>(a, c, T.r[1], dig, 0, C, 0, acc_ao, C);
       d_mark(a, c);  // C done
@@ -1691,7 +1711,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       // ================= D: x += att; ln2 + mix; ffn key rows
       d_zero(acc_rkv, T.z3c0, T.z3c1);
       #pragma unroll 1
-      for (int i = T.zr0 + t; i < T.zr1; i += kDT) a.b.adp64[i] = 0ull;
+      for (int i = T.zr0 + t; i < T.zr1; i += kDT) ga.b.adp64[i] = 0ull;
             if (fused) {
         DLnMix q{};
         q.xs = X;
@@ -1699,7 +1719,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
         q.xo = XB;
         q.w = Ly.ln2_w;
         q.b = Ly.ln2_b;
-        q.prev = a.b.ffn_x + (size_t)l * C;
+        q.prev = ga.b.ffn_x + (size_t)l * C;
         q.mix[0] = Ly.ffn_x_k;
         q.nmix = 1;
         q.need = 1u;
@@ -1710,7 +1730,7 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
 #pragma unroll 1
         for (int i = t; i < C; i += kDT) {
           XB[i] = X[i] + __ldcg(acc_ao + i);
-          PV[i] = __ldcg(a.b.ffn_x + (size_t)l * C + i);
+          PV[i] = __ldcg(ga.b.ffn_x + (size_t)l * C + i);
         }
         d_csync();
         d_layer_norm(TV, XB, Ly.ln2_w, Ly.ln2_b, C, s_stat + 2, red);
@@ -1728,11 +1748,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_zero(acc_ao, T.zc0, T.zc1);
       #pragma unroll 1
       for (int i = T.zc0 + t; i < T.zc1; i += kDT)
-        a.b.ffn_x[(size_t)l * C + i] = TV[i];  // ln2 output of phase D, still in shared memory
+        ga.b.ffn_x[(size_t)l * C + i] = TV[i];  // ln2 output of phase D, still in shared memory
       d_mark(a, c);  // E slices stored
       if (ecm) {
         // only the chunks of this CTA's units: [ech0, ech1] of kc columns each
-        const int k0 = T.ech0 * a.kc, kl = (T.ech1 - T.ech0 + 1) * a.kc;
+        const int k0 = T.ech0 * ga.kc, kl = (T.ech1 - T.ech0 + 1) * ga.kc;
         d_build<LFK>(3, nullptr, nullptr, acc_hk + k0, kl, dig);
         d_mark(a, c);  // E prep done
         d_units<LFK>(a, c, T.r[3], dig, 0, kl, 0, nullptr, C, C / 16, T.ech0, fo64);
@@ -1756,9 +1776,9 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
     // before the last barrier of the token) and the next read is issued, to be
     // used one token later, so its latency never stalls a step
     int cancel_seen = 0;
-    if (a.ring_cancel && bx == 0 && t == 0) {
+    if (ga.ring_cancel && bx == 0 && t == 0) {
       cancel_seen = cancel_next;
-      cancel_next = d_ld_relaxed_sys(a.ring_cancel);
+      cancel_next = d_ld_relaxed_sys(ga.ring_cancel);
     }
     d_zero(acc_hk, T.zf0, T.zf1);
     if (fused) {
@@ -1766,8 +1786,8 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       q.xs = XB;
       q.add = ecm ? nullptr : acc_fo;
       q.add64 = ecm ? fo64 : nullptr;
-      q.w = a.lnout_w;
-      q.b = a.lnout_b;
+      q.w = ga.lnout_w;
+      q.b = ga.lnout_b;
       q.nmix = 1;
       q.need = 1u;
       q.ln = TV;
@@ -1776,11 +1796,11 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
 #pragma unroll 1
       for (int i = t; i < C; i += kDT) PV[i] = XB[i] + (ecm ? unfix(__ldcg(fo64 + i)) : __ldcg(acc_fo + i));
       d_csync();
-      d_layer_norm(TV, PV, a.lnout_w, a.lnout_b, C, nullptr, red);
+      d_layer_norm(TV, PV, ga.lnout_w, ga.lnout_b, C, nullptr, red);
       d_build<LFK>(1, TV, nullptr, nullptr, C, dig);
     }
     d_mark(a, c);  // head prep done
-    d_units<LFK>(a, c, T.r[4], dig, 0, C, 0, logits, a.d.V);
+    d_units<LFK>(a, c, T.r[4], dig, 0, C, 0, logits, ga.d.V);
     d_mark(a, c);  // head done
     if (!d_gsync(a, c)) {
       alive = false;
@@ -1793,24 +1813,24 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
       d_zero(acc_fo, T.zc0, T.zc1);
     }
     d_argmax_part(a, T, s_bv, s_bi);
-    if (a.ring_cancel && bx == 0 && t == 0) *a.b.stop = cancel_seen;
+    if (ga.ring_cancel && bx == 0 && t == 0) *ga.b.stop = cancel_seen;
     if (!d_gsync(a, c)) {
       alive = false;
       break;
     }
     tok = d_argmax_all(a, &s_tok);
     if (bx == 0 && t == 0) {
-      a.b.hist[step % a.d.hist_cap] = tok;
-      *a.b.tok = tok;
-      if (a.ring_ids) {
+      ga.b.hist[step % ga.d.hist_cap] = tok;
+      *ga.b.tok = tok;
+      if (ga.ring_ids) {
         // one 32-bit store replaces the -1 the host left in the slot (the host
         // polls the slot itself, so no fence orders it with anything); the
         // count is exact once the launch has ended
-        d_st_relaxed_sys(reinterpret_cast<unsigned*>(a.ring_ids + step), (unsigned)tok);
-        d_st_relaxed_sys(a.ring_count, (unsigned)(step + 1));
+        d_st_relaxed_sys(reinterpret_cast<unsigned*>(ga.ring_ids + step), (unsigned)tok);
+        d_st_relaxed_sys(ga.ring_count, (unsigned)(step + 1));
       }
     }
-    if (a.ring_cancel && __ldcg(a.b.stop)) {
+    if (ga.ring_cancel && __ldcg(ga.b.stop)) {
       // cancelled by the host: every CTA stops after this token (the same
       // word, read after the same barrier); the producer sees the abort flag
       // in its slot waits, stops issuing and drains its copies in flight

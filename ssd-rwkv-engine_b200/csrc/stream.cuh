@@ -82,27 +82,6 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return false;
 }
 
-// Wait for phase `parity` of `bar` with the thread suspended in hardware
-// between polls (try_wait with a suspend-time hint: the thread resumes when
-// the phase completes, or after at most `hint_ns`), giving up after
-// `limit_ns` of wall time.  A waiting warp then takes no issue slots from
-// the warps doing the work, unlike a tight poll loop.
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
-__device__ __forceinline__ bool mbar_wait_suspend(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs,
-                                                  uint32_t hint_ns = 1000000u) {
-  const uint64_t t0 = globaltimer_ns();
-  for (;;) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-        : "memory");
-    if (ok) return true;
-    if (globaltimer_ns() - t0 > limit_ns) return false;
-  }
-}
-
 // One poll of phase `parity` of `bar` that may suspend the thread in hardware
 // for up to `hint_ns` (it resumes as soon as the phase completes).
 __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
@@ -113,6 +92,24 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
       : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` with the thread suspended in hardware
+// between polls (try_wait with a suspend-time hint: the thread resumes when
+// the phase completes, or after at most `hint_ns`), giving up after
+// `limit_ns` of wall time.  A waiting warp then takes no issue slots from
+// the warps doing the work, unlike a tight poll loop.  The wall clock is
+// read only once the first suspended poll has returned without the phase:
+// a %globaltimer read is slow next to a poll of shared memory.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+__device__ __forceinline__ bool mbar_wait_suspend(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs,
+                                                  uint32_t hint_ns = 1000000u) {
+  if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, hint_ns)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
 }
 
 // 1-D bulk copy global -> shared (this CTA), completion counted on `bar`.
