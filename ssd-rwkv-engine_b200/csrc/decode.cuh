@@ -353,11 +353,13 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
   int tile = tiles_cm ? u0 % tiles_cm : u0 / nch, chunk = tiles_cm ? u0 / tiles_cm : u0 - tile * nch;
   int mi = per_map ? tile / per_map : 0, row0 = (tile - mi * per_map) * 16;
   bool ok = true;
+  // ring position of stage seq, advanced incrementally: a division by the
+  // runtime depth per unit is a long dependent chain on the issue path
+  int slot = seq % nst;
+  uint32_t par = (uint32_t)((seq / nst - 1) & 1);  // parity of the release this stage waits for
 #pragma unroll 1
   for (int u = u0; u < u1; ++u) {
-    const int slot = seq % nst;
     if (seq >= nst) {
-      const uint32_t par = (uint32_t)((seq / nst - 1) & 1);
       uint64_t t0 = 0;  // the wall clock is read only once a wait has not ended at the first poll
       while (!mbar_try_wait_hint(&empty[slot], par, 20000u)) {
         if (t0 == 0) t0 = globaltimer_ns();
@@ -387,6 +389,10 @@ __device__ __noinline__ bool d_issue_units(const DArgs& a, const DRange& R, cons
     }
     if (tr && 3 * seq + 2 < tr_n) tr[3 * seq] = global_ns();
     ++seq;
+    if (++slot == nst) {
+      slot = 0;
+      par ^= 1u;
+    }
     if (tiles_cm) {
       row0 += 16;
       if (++tile == tiles_cm) {
@@ -936,9 +942,14 @@ __device__ __noinline__ void d_units(const DArgs& a, DCons& c, const DRange& R, 
   int tile = tiles_cm ? u0 % tiles_cm : u0 / nch, chunk = tiles_cm ? u0 / tiles_cm : u0 - tile * nch;
   int nt = 0;  // tiles buffered in `part`
   int* ptile = reinterpret_cast<int*>(part + kDPartTiles * kDW * 16);  // their tile indices
+  // digit set of the current tile (tile / per_set), advanced with the tile
+  int set = per_set ? tile / per_set : 0, set_end = per_set ? (set + 1) * per_set : 0x7fffffff;
 #pragma unroll 1
   for (int u = u0; u < u1; ++u) {
-    const int set = per_set ? tile / per_set : 0;
+    if (tile >= set_end) {
+      ++set;
+      set_end += per_set;
+    }
     if (set != cur_set) {
       X = d_digits_at(dig + (size_t)set * stride, K, LFK);
       cur_set = set;
@@ -1086,7 +1097,7 @@ __device__ __noinline__ void d_items(const DArgs& a, DCons& c, const DTable& T, 
       #pragma unroll 1
       for (int j = t; j < R; j += kDT) {
         float v = 0.f;
-        for (int rg = 0; rg < (q4 < kDT ? kDT / q4 : 1); ++rg) v += pacc[rg * R + j];
+        for (int rg = 0; rg < nrg; ++rg) v += pacc[rg * R + j];
         red_add_u64(a.b.adp64 + off + j, (unsigned long long)__float2ll_rn(v * kFix));
       }
     }
