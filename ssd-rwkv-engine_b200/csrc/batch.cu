@@ -113,6 +113,7 @@ int bg_setup(BgArgs* a, const BgJob* jobs, int njobs, const BgDigits* dg, int nd
   a->nmat = njobs;
   a->total = total;
   const int n = std::min(sms, total);
+  if ((long long)total * n >= (1ll << 31)) return RWKVB_EUNSUPPORTED;  // the kernel splits stages in 32-bit arithmetic
   const size_t stage_bytes = (size_t)kBgTileBytes + (size_t)a->nrows * 128;
   a->stages = (int)std::min<size_t>(kBgMaxStages, (kBgSmemBudget - 1024) / stage_bytes);
   if (a->stages < 2) return RWKVB_EUNSUPPORTED;
@@ -893,18 +894,26 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
   __shared__ float gbon[2][64], gv[2][64], ggate[2][64];
   const int t = threadIdx.x, i = t & 63;
   const bool chan = t < 64, gnw = t >= 64 && t < 128;
-  const int npairs = a.nb * a.H;
-  const int q0 = (int)((long long)blockIdx.x * npairs / gridDim.x);
-  const int q1 = (int)((long long)(blockIdx.x + 1) * npairs / gridDim.x);
+  const int npairs = a.nb * a.H;  // <= 64 * 64: the products below fit 32 bits
+  const int q0 = (int)((unsigned)blockIdx.x * (unsigned)npairs / gridDim.x);
+  const int q1 = (int)((unsigned)(blockIdx.x + 1) * (unsigned)npairs / gridDim.x);
   if (q0 >= q1) return;
-  // pair q = (head q / nb, session q % nb); its state is block (b, h) of [nb][H][64][64]
-  auto state_of = [&](int q) -> float4* {
-    return reinterpret_cast<float4*>(a.wkv + ((size_t)(q % a.nb) * a.H + q / a.nb) * 4096);
+  // pair q = (head q / nb, session q % nb); its state is block (b, h) of
+  // [nb][H][64][64].  (b, h) are advanced pair by pair: no division by the
+  // runtime session count in the loop
+  auto state_of = [&](int b, int h) -> float4* {
+    return reinterpret_cast<float4*>(a.wkv + ((size_t)b * a.H + h) * 4096);
   };
-  // GroupNorm over a head (eps 64e-5), bonus, gate of pair q, by warps 2-3
-  // while warps 0-1 prepare the next pair's channel vectors
-  auto group_norm = [&](int q, int par) {
-    const int b = q % a.nb, ch = (q / a.nb) * 64 + i;
+  auto advance = [&](int& b, int& h) {
+    if (++b == a.nb) {
+      b = 0;
+      ++h;
+    }
+  };
+  // GroupNorm over a head (eps 64e-5), bonus, gate of pair (b, h), by warps
+  // 2-3 while warps 0-1 prepare the next pair's channel vectors
+  auto group_norm = [&](int b, int h, int par) {
+    const int ch = h * 64 + i;
     const float y = sy[i];
     const float2 mb = bt_gn_sum2(y, gbon[par][i], gred2);
     const float mean = mb.x / 64.f;
@@ -914,28 +923,32 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
     o = o + mb.y * gv[par][i];
     a.att_y[(size_t)b * a.C + ch] = o * ggate[par][i];
   };
+  int b = q0 % a.nb, h = q0 / a.nb;  // pair q
+  int pb = b, ph = h;                 // pair q - 1
   {
-    const float4* src = state_of(q0);
+    const float4* src = state_of(b, h);
 #pragma unroll
     for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[t + 256 * u], &src[t + 256 * u]);
     cp_async_commit();
   }
   BtWkvChan cur{};
-  if (chan) cur = bt_wkv_chan(a, q0 % a.nb, (q0 / a.nb) * 64 + i);
+  if (chan) cur = bt_wkv_chan(a, b, h * 64 + i);
   int vh = -1;  // head whose vectors are in registers
   float kkw = 0.f, a0v = 0.f, v0v = 0.f, w0v = 0.f, kav = 0.f, rkv = 0.f;
   for (int q = q0, it = 0; q < q1; ++q, ++it) {
     const int st = it & 1, nx = q + 1, par = it & 1;
-    const int b = q % a.nb, h = q / a.nb, ch = h * 64 + i;
+    const int ch = h * 64 + i;
+    int bn = b, hn = h;  // pair nx
+    advance(bn, hn);
     if (nx < q1) {
-      const float4* src = state_of(nx);
+      const float4* src = state_of(bn, hn);
 #pragma unroll
       for (int u = 0; u < 4; ++u) cp_async16(&bt_stage[(st ^ 1) * 1024 + t + 256 * u], &src[t + 256 * u]);
     }
     cp_async_commit();  // an empty group when there is no next pair
     if (chan) {
       BtWkvChan nxt{};
-      if (nx < q1) nxt = bt_wkv_chan(a, nx % a.nb, (nx / a.nb) * 64 + i);
+      if (nx < q1) nxt = bt_wkv_chan(a, bn, hn * 64 + i);
       if (h != vh) {
         vh = h;
         kkw = a.k_k[ch], a0v = a.a0[ch], w0v = a.w0[ch], kav = a.k_a[ch], rkv = a.r_k[ch];
@@ -960,7 +973,7 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
       ggate[par][i] = cur.gv;
       cur = nxt;
     } else if (gnw && it > 0) {
-      group_norm(q - 1, par ^ 1);  // the previous pair (its sy is complete)
+      group_norm(pb, ph, par ^ 1);  // the previous pair (its sy is complete)
     }
     cp_async_wait_group<1>();  // this pair's stage (the group before the prefetch just issued)
     __syncthreads();
@@ -972,7 +985,7 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
       const float4 a4 = reinterpret_cast<const float4*>(vka)[cg];
       const float4 k4 = reinterpret_cast<const float4*>(vk)[cg];
       const float4 r4 = reinterpret_cast<const float4*>(vr)[cg];
-      float4* S = state_of(q);
+      float4* S = state_of(b, h);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int row = row0 + 16 * u;
@@ -998,8 +1011,12 @@ __global__ void __launch_bounds__(kBtThreads, kBtWkvCtasPerSm) bt_wkv_kernel(BtW
       }
     }
     __syncthreads();  // sy complete; stage st and the vectors are free again
+    pb = b;
+    ph = h;
+    b = bn;
+    h = hn;
   }
-  if (gnw) group_norm(q1 - 1, (q1 - 1 - q0) & 1);  // the last pair
+  if (gnw) group_norm(pb, ph, (q1 - 1 - q0) & 1);  // the last pair
   cp_async_wait_all();
 }
 
@@ -1952,6 +1969,7 @@ int lm_setup(LmArgs* a, const LmJob* jobs, int njobs, int nb, int sms, int pcap,
   a->idesc = idesc_f16f16_f32(128, 3 * a->bp);
   a->err = err_word;
   int n = std::min(sms, total);
+  if ((long long)total * n >= (1ll << 31)) return RWKVB_EUNSUPPORTED;  // the kernel splits stages in 32-bit arithmetic
   while (n > 1 && lm_pmax(*a, n) > pcap) --n;
   *grid = n;
   *smem = (size_t)kLmOps * a->op_bytes + (size_t)a->rstages * a->raw_bytes + 1024;

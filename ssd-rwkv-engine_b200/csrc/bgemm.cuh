@@ -109,6 +109,15 @@ __host__ __device__ __forceinline__ int bg_cta_of(long long x, int total, int n)
 __host__ __device__ __forceinline__ int bg_range_lo(int c, int total, int n) {
   return (int)(((long long)c * total) / n);
 }
+// The same in 32-bit unsigned arithmetic for the kernels (a 64-bit division is
+// a long software sequence at the start of every launch); exact while
+// total * n < 2^31, which the launch setup checks.
+__device__ __forceinline__ int bg_cta_of32(int x, int total, int n) {
+  return (int)(((unsigned)(x + 1) * (unsigned)n - 1u) / (unsigned)total);
+}
+__device__ __forceinline__ int bg_range_lo32(int c, int total, int n) {
+  return (int)(((unsigned)c * (unsigned)total) / (unsigned)n);
+}
 
 // One segment: stages [s0, s1) of tile t of matrix m, piece p.
 struct BgSeg {
@@ -129,8 +138,16 @@ __device__ __forceinline__ BgSeg bg_segment(const BgArgs& a, int x, int hi) {
   s.s0 = local - s.t * G;
   const int tile_hi = M.stage0 + (s.t + 1) * G;
   s.s1 = s.s0 + (min(hi, tile_hi) - x);
-  s.p = (int)blockIdx.x - bg_cta_of(M.stage0 + (long long)s.t * G, a.total, gridDim.x);
+  s.p = (int)blockIdx.x - bg_cta_of32(M.stage0 + s.t * G, a.total, gridDim.x);
   return s;
+}
+
+// Next ring slot; n counts the passes over the ring.
+__device__ __forceinline__ void bg_advance(uint32_t& slot, uint32_t& n, uint32_t nstages) {
+  if (++slot == nstages) {
+    slot = 0;
+    ++n;
+  }
 }
 
 // Bounded wait by lane 0 of the calling warp, result broadcast to the warp
@@ -158,8 +175,8 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int lo = bg_range_lo(blockIdx.x, a.total, gridDim.x);
-  const int hi = bg_range_lo(blockIdx.x + 1, a.total, gridDim.x);
+  const int lo = bg_range_lo32(blockIdx.x, a.total, gridDim.x);
+  const int hi = bg_range_lo32(blockIdx.x + 1, a.total, gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < a.stages; ++i) {
@@ -207,11 +224,14 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
     npre = __shfl_sync(0xffffffffu, npre, 0);
     pdl_wait();
     pdl_launch_dependents();
+    // ring slot and pass of stage `use`, advanced incrementally (no division
+    // by the runtime depth on the issue path)
+    uint32_t slot = 0, n = 0;
+    const uint32_t nstages = (uint32_t)a.stages;
     for (int x = lo; x < hi;) {
       const BgSeg sg = bg_segment(a, x, hi);
       const BgMat& M = a.mat[sg.m];
-      for (int st = sg.s0; st < sg.s1; ++st, ++use) {
-        const uint32_t slot = use % a.stages, n = use / a.stages;
+      for (int st = sg.s0; st < sg.s1; ++st, ++use, bg_advance(slot, n, nstages)) {
         if (use < npre) {  // weights already issued; ring slot fresh
           if (lane == 0) tma_load_2d(smem + slot * stage_bytes + kBgTileBytes, &a.bmap[M.digits], st * 128, 0,
                                      &full[slot]);
@@ -238,14 +258,14 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     pdl_launch_dependents();  // reads shared memory only (full barriers follow the producer's wait)
-    uint32_t use = 0, fl = 0;
+    uint32_t use = 0, fl = 0, slot = 0, n = 0;
+    const uint32_t nstages = (uint32_t)a.stages;
     for (int x = lo; x < hi;) {
       const BgSeg sg = bg_segment(a, x, hi);
       const BgMat& M = a.mat[sg.m];
       const int nfl = 128 >> M.lg;  // flush groups per stage (1 or 2)
       const int kpf = 4 / nfl;      // 32-column k-steps per flush group
-      for (int st = sg.s0; st < sg.s1; ++st, ++use) {
-        const uint32_t slot = use % a.stages, n = use / a.stages;
+      for (int st = sg.s0; st < sg.s1; ++st, ++use, bg_advance(slot, n, nstages)) {
         if (!bg_wait(&full[slot], n & 1, a, &s_abort)) goto mma_done;
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + slot * stage_bytes);

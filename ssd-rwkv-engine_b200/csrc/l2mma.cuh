@@ -128,7 +128,7 @@ __device__ __forceinline__ LmSeg lm_segment(const LmArgs& a, int x, int hi) {
   s.s0 = local - s.t * G;
   const int tile_hi = M.stage0 + (s.t + 1) * G;
   s.s1 = s.s0 + (min(hi, tile_hi) - x);
-  s.p = (int)blockIdx.x - bg_cta_of(M.stage0 + (long long)s.t * G, a.total, gridDim.x);
+  s.p = (int)blockIdx.x - bg_cta_of32(M.stage0 + s.t * G, a.total, gridDim.x);
   return s;
 }
 
@@ -181,8 +181,8 @@ __global__ void __launch_bounds__(kLmThreads, 1) l2mma_kernel(const __grid_const
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int lo = bg_range_lo(blockIdx.x, a.total, gridDim.x);
-  const int hi = bg_range_lo(blockIdx.x + 1, a.total, gridDim.x);
+  const int lo = bg_range_lo32(blockIdx.x, a.total, gridDim.x);
+  const int hi = bg_range_lo32(blockIdx.x + 1, a.total, gridDim.x);
   const uint32_t R = (uint32_t)a.rstages;
 
   if (threadIdx.x == 0) {
