@@ -846,8 +846,8 @@ __device__ __noinline__ void d_ln_mix(const DArgs& a, DCons& c, const DLnMix& q,
   ldg8(b, q.b + i0);
   if (q.prev) ldcg8(pv, q.prev + i0);
 #pragma unroll
-  for (int m = 0; m < 3; ++m)
-    if (m < q.nmix && q.mix[m]) ldg8(mx[m], q.mix[m] + i0);
+  for (int m = 0; m < 3; ++m)  // only the mixes whose digits this CTA emits (every CTA reads them: L2-bound)
+    if (m < q.nmix && q.mix[m] && ((q.need >> m) & 1u)) ldg8(mx[m], q.mix[m] + i0);
   float s = 0.f;
 #pragma unroll
   for (int u = 0; u < 8; ++u) s += act ? x[u] : 0.f;

@@ -239,20 +239,18 @@ __device__ __forceinline__ void imma_block(const uint8_t* blk, const float2* pa,
     int d[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int j = f * KPF; j < (f + 1) * KPF; ++j) imma_16832(d, w0[j].x, w1[j].x, w0[j].y, w1[j].y, bb[j].x, bb[j].y);
-    if (t < 2) {
-      const int fg = (ks >> LFK) + f;
-      const float c = X.xc[fg];
-      const float2 p0 = pa[f], p1 = pb[f];
-      const float da = (p0.y - p0.x) * kInv255 * c, db = (p1.y - p1.x) * kInv255 * c;
-      if (t == 0) {
-        const float xs = X.xsum[fg];
-        acc0 = fmaf(da, fmaf((float)d[1], kInv254, (float)d[0]), fmaf(p0.x, xs, acc0));
-        acc1 = fmaf(db, fmaf((float)d[3], kInv254, (float)d[2]), fmaf(p1.x, xs, acc1));
-      } else {
-        acc0 = fmaf(da * kInv254sq, (float)d[0], acc0);
-        acc1 = fmaf(db * kInv254sq, (float)d[2], acc1);
-      }
-    }
+    // without branches: lane t = 0 holds digits 0 and 1, t = 1 digit 2 and
+    // the zero column 3 (so d1 / d3 are 0 there), t >= 2 zero columns (their
+    // sums are never stored); each lane does exactly the operations of its
+    // case: t = 0  da (d0 + d1 / 254) + min x_sum,  t = 1  da / 254^2 d0
+    const int fg = (ks >> LFK) + f;
+    const float c = X.xc[fg], xs = X.xsum[fg];
+    const float2 p0 = pa[f], p1 = pb[f];
+    const float sc = t == 0 ? 1.0f : kInv254sq;
+    const float da = (p0.y - p0.x) * kInv255 * c, db = (p1.y - p1.x) * kInv255 * c;
+    const float m0 = t == 0 ? p0.x : 0.f, m1 = t == 0 ? p1.x : 0.f;
+    acc0 = fmaf(t == 0 ? da : da * sc, fmaf((float)d[1], kInv254, (float)d[0]), fmaf(m0, xs, acc0));
+    acc1 = fmaf(t == 0 ? db : db * sc, fmaf((float)d[3], kInv254, (float)d[2]), fmaf(m1, xs, acc1));
   }
 }
 
