@@ -58,7 +58,7 @@ constexpr int kDMaxSt = 8;             // ring slots (upper bound)
 constexpr int kDRingDefault = 3;       // ring slots unless the engine flags ask for more
 constexpr int kDBar = 1;               // named barrier of the consumers
 constexpr int kDMaxItems = 8;          // adapter first-stage items per CTA
-constexpr int kDPartTiles = 8;         // GEMV tiles whose per-warp partial sums are buffered per CTA reduction
+constexpr int kDPartTiles = 16;        // GEMV tiles whose per-warp partial sums are buffered per CTA reduction
 constexpr uint32_t kDPartBytes = kDPartTiles * kDW * 16 * 4 + 128;  // the partial sums, then their tile indices
 constexpr int kDMaxPieces = 8;         // adapter second-stage tile pieces per layer
 constexpr int kDPieceSteps = 2;        // preload mode: 32-row k-steps per phase-B tensor-core task

@@ -1127,7 +1127,7 @@ bool plan_decode(rwkvb_engine* e) {
   dig = (dig + 127u) & ~127u;
   const uint32_t vec = ((uint32_t)d.C * 4u + 127u) & ~127u;
   const uint32_t rest = dig + 4u * vec + kDPartBytes + (uint32_t)kDMisc * 4u;
-  const uint32_t budget = 227u * 1024u - 1024u - 6u * 1024u;  // dynamic-smem alignment slack, static shared
+  const uint32_t budget = 227u * 1024u - 1024u - 5u * 1024u;  // dynamic-smem alignment slack, static shared
   // Ring depth: the consumers' own small loads (accumulators, vectors) queue
   // behind the weight tiles in flight on their SM, so a deeper ring than the
   // HBM latency needs lengthens every step of the per-layer dependency chain
