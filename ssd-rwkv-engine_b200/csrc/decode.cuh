@@ -1194,16 +1194,12 @@ __device__ __noinline__ void d_pieces_mma(const DArgs& a, DCons& c, const DTable
       const uint2 bb = lane < 12 ? X.xd[ks * 12 + lane] : make_uint2(0u, 0u);
       int d[4] = {0, 0, 0, 0};
       imma_16832(d, w0.x, w1.x, w0.y, w1.y, bb.x, bb.y);
-      if (tq < 2) {
-        const float cs = X.xc[ks];
-        if (tq == 0) {
-          acc0 = fmaf(cs, fmaf((float)d[1], kInv254, (float)d[0]), acc0);
-          acc1 = fmaf(cs, fmaf((float)d[3], kInv254, (float)d[2]), acc1);
-        } else {
-          acc0 = fmaf(cs * kInv254sq, (float)d[0], acc0);
-          acc1 = fmaf(cs * kInv254sq, (float)d[2], acc1);
-        }
-      }
+      // lanes without branches (as in imma_block): tq = 1 holds digit 2 and
+      // the zero column 3, tq >= 2 zero columns whose sums are never stored
+      const float cs = X.xc[ks];
+      const float cq = tq == 0 ? cs : cs * kInv254sq;
+      acc0 = fmaf(cq, fmaf((float)d[1], kInv254, (float)d[0]), acc0);
+      acc1 = fmaf(cq, fmaf((float)d[3], kInv254, (float)d[2]), acc1);
     }
     acc0 += __shfl_xor_sync(0xffffffffu, acc0, 1);
     acc1 += __shfl_xor_sync(0xffffffffu, acc1, 1);
