@@ -233,7 +233,7 @@ int launch_transposed(const PackedView& w, const float* x, float* y, const float
 __global__ void __launch_bounds__(256) wkv7_kernel(float* state, float* y, const float* r, const float* w,
                                                    const float* k, const float* v, const float* kk,
                                                    const float* a, int n_head, int mode) {
-  __shared__ float sr[64], sd[64], sk[64], sv[64], skk[64], ska[64];
+  __shared__ __align__(16) float sr[64], sd[64], sk[64], sv[64], skk[64], ska[64];
   const int bh = blockIdx.x;  // batch * n_head + head
   const size_t off = (size_t)bh * 64;
   if (threadIdx.x < 64) {

@@ -25,18 +25,34 @@ __device__ __forceinline__ void wkv7_head64(float* __restrict__ S, const float* 
     float4 a = row[u];
     s[4 * u] = a.x; s[4 * u + 1] = a.y; s[4 * u + 2] = a.z; s[4 * u + 3] = a.w;
   }
+  // the 16 entries of each vector this thread uses, as four 16-byte loads
+  // (q is a multiple of 16; the vectors are 16-byte aligned)
+  auto ld16 = [&](const float* p, float (&o)[16]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float4 f = reinterpret_cast<const float4*>(p + q)[u];
+      o[4 * u] = f.x; o[4 * u + 1] = f.y; o[4 * u + 2] = f.z; o[4 * u + 3] = f.w;
+    }
+  };
+  float vkk[16];
+  ld16(kk, vkk);
   float sa = 0.f;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) sa = fmaf(s[j], -kk[q + j], sa);
+  for (int j = 0; j < 16; ++j) sa = fmaf(s[j], -vkk[j], sa);
   sa += __shfl_xor_sync(0xffffffffu, sa, 1);
   sa += __shfl_xor_sync(0xffffffffu, sa, 2);
   const float vi = v[i];
+  float vd[16], vka[16], vk[16], vr[16];
+  ld16(d, vd);
+  ld16(ka, vka);
+  ld16(k, vk);
+  ld16(r, vr);
   float yy = 0.f;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    float nv = s[j] * d[q + j] + sa * ka[q + j] + vi * k[q + j];
+    float nv = s[j] * vd[j] + sa * vka[j] + vi * vk[j];
     s[j] = nv;
-    yy = fmaf(nv, r[q + j], yy);
+    yy = fmaf(nv, vr[j], yy);
   }
   yy += __shfl_xor_sync(0xffffffffu, yy, 1);
   yy += __shfl_xor_sync(0xffffffffu, yy, 2);
