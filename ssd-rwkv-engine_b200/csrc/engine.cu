@@ -1026,6 +1026,8 @@ int encode_adp2(const PackedView& w, int box_rows, CUtensorMap* q, CUtensorMap* 
 // Decide whether the persistent decode kernel can run this model, fill its
 // arguments (everything except the per-launch token fields) and encode its
 // tensor maps.
+const void* decode_fn(int lfk);
+
 bool plan_decode(rwkvb_engine* e) {
   const Dims& d = e->d;
   const LayerDev& l0 = e->layers[0];
@@ -1127,7 +1129,18 @@ bool plan_decode(rwkvb_engine* e) {
   dig = (dig + 127u) & ~127u;
   const uint32_t vec = ((uint32_t)d.C * 4u + 127u) & ~127u;
   const uint32_t rest = dig + 4u * vec + kDPartBytes + (uint32_t)kDMisc * 4u;
-  const uint32_t budget = 227u * 1024u - 1024u - 5u * 1024u;  // dynamic-smem alignment slack, static shared
+  // per-block opt-in shared memory less the kernel's static shared memory and
+  // the dynamic area's 1 KB alignment slack
+  uint32_t budget = 227u * 1024u - 1024u - 5u * 1024u;
+  {
+    cudaFuncAttributes fa;
+    int dev = 0, optin = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess &&
+        cudaFuncGetAttributes(&fa, decode_fn(e->lfk)) == cudaSuccess && (size_t)optin > fa.sharedSizeBytes + 1024u)
+      budget = (uint32_t)((size_t)optin - fa.sharedSizeBytes - 1024u);
+    cudaGetLastError();
+  }
   // Ring depth: the consumers' own small loads (accumulators, vectors) queue
   // behind the weight tiles in flight on their SM, so a deeper ring than the
   // HBM latency needs lengthens every step of the per-layer dependency chain
