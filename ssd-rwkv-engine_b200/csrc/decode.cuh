@@ -1532,8 +1532,8 @@ __global__ void __launch_bounds__(kDThreads, 1) decode_kernel(const __grid_const
   __shared__ DCons s_cons[kDW];
   __shared__ DLnMix s_q[kDW];
   __shared__ __align__(16) LayerDev s_ly[2];  // descriptors of the current and the next layer
-  // the launch arguments in shared memory: indexed reads of the parameter
-  // space miss the SM's small constant cache and go out to memory
+  // the launch arguments in shared memory: the subroutines read them through
+  // a reference, and those reads measured slower from the parameter space
   __shared__ __align__(16) DArgs s_args;
   static_assert(sizeof(DArgs) % 4 == 0 && sizeof(DArgs) <= 1024, "launch arguments in shared memory");
 

@@ -99,8 +99,8 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
 // the phase completes, or after at most `hint_ns`), giving up after
 // `limit_ns` of wall time.  A waiting warp then takes no issue slots from
 // the warps doing the work, unlike a tight poll loop.  The wall clock is
-// read only once the first suspended poll has returned without the phase:
-// a %globaltimer read is slow next to a poll of shared memory.
+// read only once the first suspended poll has returned without the phase,
+// so the common case is a single poll.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 __device__ __forceinline__ bool mbar_wait_suspend(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs,
                                                   uint32_t hint_ns = 1000000u) {
