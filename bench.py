@@ -23,6 +23,13 @@ step = one token for every session.
 ``prefill`` is the sequence-prefill leg (``--prefill-sessions`` sessions x
 ``--prefill-tokens`` tokens through ``B200BatchEngine.prefill``).
 
+``tp`` is the 7.2B leg (``--tp-sessions`` sessions, tensor-parallel over the
+ranks; unsplit at one GPU), with, at one GPU, the 7.2B sequence prefill of
+``--tp-prefill-tokens`` tokens per session (``tp.prefill``, reported against
+HBM and against tensor throughput).  ``lut2`` holds the LUT2 (``TR2\x04``)
+legs of the same 2.9B shape, ``small`` the 0.1B-shaped bs1 leg (a
+``--small-prompt``-token prompt, then ``--small-steps`` greedy tokens).
+
 ``--impl reference`` times the reference's own C kernels (built from its
 sources into ``oracle/_ref``) driving the packed RWKV-7 forward on the host
 cores, on the same workload and metric (rank 0 only).
@@ -82,6 +89,17 @@ def _peaks() -> tuple[float, str]:
         except Exception:
             pass
     return 6650.0, "fallback"
+
+
+def _tflops_peak() -> tuple[float, str]:
+    """Sustained dense bf16 tensor throughput (the denominator of a flop roofline for a long step)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops_sustained"]), "measured sustained bf16"
+        except Exception:
+            pass
+    return 1400.0, "fallback sustained bf16"
 
 
 class ClockSampler:
@@ -459,6 +477,9 @@ def run_tp(args, dev, stream, world: int, rank: int) -> dict:
     peak, peak_kind = _peaks()
     achieved = step_bytes / (ms_step / 1e3) / 1e9
     launches = eng.launches_per_step
+    prefill = None
+    if world == 1 and args.tp_prefill_tokens > 0:
+        prefill = run_tp_prefill(eng, args, shape, nb, dev, stream)
     eng.close()
     return {"metric": f"RWKV-7 {args.tp_config} U8 decode tok/s (bs{nb}, tensor-parallel x{world})",
             "value": nb / (ms_step / 1e3), "unit": "tok/s", "n_gpus": world, "sessions": nb, "scaling": "strong",
@@ -475,7 +496,104 @@ def run_tp(args, dev, stream, world: int, rank: int) -> dict:
             "e2e": {"value": e_steps * nb / (e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 4 * nb, "steps": e_steps,
                     "how": "decode_greedy: ids of every step copied to the host"},
-            "ids_checksum": int(ids.astype("int64").sum()), "bytes_per_token_unsplit": bpt_local}
+            "ids_checksum": int(ids.astype("int64").sum()), "bytes_per_token_unsplit": bpt_local,
+            "prefill": prefill if world == 1 else {"skipped": "sequence prefill runs on the unsplit engine (N = 1)"}}
+
+
+def run_tp_prefill(eng, args, shape, nb: int, dev, stream) -> dict:
+    """Sequence prefill of the TP leg's model at one GPU: ``nb`` sessions x
+    ``args.tp_prefill_tokens`` seeded tokens through ``B200BatchEngine.prefill``
+    from a fresh state.  Reported against HBM (weights once per chunk) and
+    against tensor throughput (the model's matmul flops, two per weight and
+    token, over the measured sustained bf16 peak)."""
+    n = args.tp_prefill_tokens
+    prompts = [synth_prompt(n, shape.vocab, replicas.session_seed(SEED + 11, g)) for g in range(nb)]
+    eng.reset()
+    eng.prefill([p[:64] for p in prompts])  # builds the chunk plan and graph
+    eng.reset()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    _nvtx_push("timed_tp_prefill")
+    t0.record(stream)
+    eng.prefill(prompts)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    _nvtx_pop()
+    ms = t0.elapsed_time(t1)
+    tokens = nb * n
+    chunk = max(1, 64 // nb)
+    C, L, H = shape.n_embd, shape.n_layer, shape.n_head
+    state = L * (2 * C + H * 64 * 64) * 4
+    emb_row = C + (C // 128) * 8
+    head = shape.vocab * C + shape.vocab * (C // 128) * 8
+    weights = shape.weights_per_token() * 1.0625 - head  # projections and adapters, once per chunk
+    alg = (n // chunk) * (weights + nb * 2 * state + nb * chunk * emb_row) + head
+    peak, peak_kind = _peaks()
+    flops = 2.0 * (shape.weights_per_token() - shape.vocab * C) * tokens + 2.0 * shape.vocab * C * nb
+    tpk, tpk_kind = _tflops_peak()
+    return {"metric": f"RWKV-7 {args.tp_config} U8 prefill tok/s ({nb} sessions x {n} tokens)",
+            "value": tokens / (ms * 1e-3), "unit": "tok/s", "ms": ms, "sessions": nb, "tokens_per_session": n,
+            "chunk_positions": chunk,
+            "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None, "algorithmic_bytes": alg,
+                         "what": f"weights once per chunk of {chunk} positions x {nb} sessions, state per chunk and "
+                                 f"session, head once; peak: {peak_kind} HBM copy bandwidth"},
+            "roofline_flops": {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": tpk,
+                               "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / tpk,
+                               "algorithmic_flops": flops,
+                               "what": f"2 flops per projection weight per token (the head once per session); "
+                                       f"peak: {tpk_kind} (the GEMMs run as integer MMAs on 3 digit rows per input)"}}
+
+
+def run_small(args, dev, stream, world: int, rank: int) -> dict:
+    """The 0.1B-shaped configuration: a seeded ``args.small_prompt``-token
+    prompt, then ``args.small_steps`` greedy tokens at batch 1 on the
+    persistent kernel (each rank an independent replica)."""
+    from rwkv_b200 import synth
+    from rwkv_b200.engine import B200Engine, ModelUpload
+
+    shape = synth.PRESETS["0.1b"]
+    pack = synth.make_pack_streaming(shape, SEED + 13 + rank, dev, policy="sg8")
+    bpt = bytes_per_token(pack, shape)
+    model = ModelUpload(pack, dev)
+    del pack
+    eng = B200Engine(model, device=dev.index)
+    try:
+        prompt = synth_prompt(args.small_prompt, shape.vocab, SEED + 13 + rank)
+        eng.forward(prompt[:8])  # first launch of each path outside the timed regions
+        eng.reset()
+        torch.cuda.synchronize(dev)
+        p0 = torch.cuda.Event(enable_timing=True)
+        p1 = torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        eng.forward(prompt)
+        p1.record(stream)
+        torch.cuda.synchronize(dev)
+        pf_ms = replicas.max_over_ranks(p0.elapsed_time(p1))
+        first = int(torch.argmax(eng.logits).item())
+        ids = torch.empty(args.small_steps + 8, dtype=torch.int32, device=dev)
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        eng.decode_greedy_async(first, args.small_steps, ids)
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = replicas.max_over_ranks(t0.elapsed_time(t1))
+        persistent = eng.persistent_active
+    finally:
+        eng.close()
+    ms_step = ms / args.small_steps
+    peak, peak_kind = _peaks()
+    achieved = bpt / (ms_step / 1e3) / 1e9
+    return {"metric": "RWKV-7 0.1b U8 decode tok/s (bs1)", "value": args.small_steps * world / (ms / 1e3),
+            "unit": "tok/s", "steps": args.small_steps, "ms_per_step": ms_step,
+            "prompt_tokens": args.small_prompt, "prompt_tok_s": args.small_prompt * world / (pf_ms / 1e3),
+            "path": "persistent kernel" if persistent else "multi-kernel CUDA graph",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "algorithmic_bytes_per_step": bpt,
+                         "what": f"bs1 decode: algorithmic bytes/token {bpt} / device time per token; peak: "
+                                 f"{peak_kind} HBM copy bandwidth"}}
 
 
 def synth_prompt(n: int, vocab: int, seed: int) -> list[int]:
@@ -535,6 +653,10 @@ def main() -> None:
     ap.add_argument("--batch-steps", type=int, default=64)
     ap.add_argument("--prefill-tokens", type=int, default=512, help="prefill leg: tokens per session (0: skip)")
     ap.add_argument("--prefill-sessions", type=int, default=8)
+    ap.add_argument("--tp-prefill-tokens", type=int, default=4096,
+                    help="tp leg at one GPU: sequence prefill tokens per session (0: skip)")
+    ap.add_argument("--small-steps", type=int, default=256, help="0.1B leg: greedy tokens after the prompt (0: skip)")
+    ap.add_argument("--small-prompt", type=int, default=512, help="0.1B leg: prompt tokens")
     ap.add_argument("--lut2-steps", type=int, default=64, help="LUT2 leg: bs1 decode tokens (0: skip the leg)")
     ap.add_argument("--lut2-sessions", type=int, default=64, help="LUT2 leg: batched sessions (0: bs1 only)")
     ap.add_argument("--tp-config", default="7.2b", choices=["tiny", "7.2b", "7.2b-l4", "2.9b"],
@@ -658,6 +780,13 @@ def main() -> None:
         except Exception as exc:  # noqa: BLE001
             lut2 = {"error": f"{type(exc).__name__}: {exc}"[:300]}
             torch.cuda.synchronize(dev)
+    small = None
+    if args.small_steps > 0 and args.policy == "sg8":
+        try:
+            small = run_small(args, dev, stream, world, rank)
+        except Exception as exc:  # noqa: BLE001
+            small = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+            torch.cuda.synchronize(dev)
     tpres = None
     if args.tp_sessions > 0:
         # the tensor-parallel leg must not take the line's other results with it:
@@ -714,6 +843,8 @@ def main() -> None:
             res["tp"] = tpres
         if lut2 is not None:
             res["lut2"] = lut2
+        if small is not None:
+            res["small"] = small
         if cpu_pack is not None:
             backend.close()
             cb = cpu_baseline(cpu_pack, shape, args, gpu_ids)
