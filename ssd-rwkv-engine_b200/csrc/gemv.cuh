@@ -206,7 +206,7 @@ __device__ __forceinline__ void packed_rows(const PackedView& W, int mode, int l
   if (mode == 1) {
     sg8_rows<2>(W, lg, sx, sxc, r0, r1, epi);
   } else if (mode == 2) {
-    lut2_rows<2>(W, lg, sx, r0, r1, epi);
+    lut2_rows<3>(W, lg, sx, r0, r1, epi);
   } else {
     generic_rows(W, sx, r0, r1, epi);
   }
