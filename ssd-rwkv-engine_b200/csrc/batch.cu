@@ -1575,8 +1575,9 @@ inline BtXLayout bt_x_layout(int L, int nb, int C) {
   return x;
 }
 
-__device__ __forceinline__ void bt_st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void bt_fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void bt_st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t bt_ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
@@ -1595,13 +1596,16 @@ constexpr uint64_t kTpWaitLimitNs = 5000000000ull;  // 5 s
 // (bounded by `limit_ns` of wall time) for every peer's flag; false when a wait
 // gave up (error word set).  Once an exchange of the step has given up, the
 // later ones return at once instead of each waiting out the limit; the error
-// word stays set until the host reads and clears it.
+// word stays set until the host reads and clears it.  The release is one
+// system-scope acq_rel fence followed by relaxed flag stores (the PTX release
+// pattern): the CTA's data writes, ordered before the fence by the caller's
+// __syncthreads, are visible to every peer that observes a flag.
 __device__ bool bt_x_handshake(const BtXPeers& P, size_t flags_off, int inst, int cta, int rank, int size, uint32_t ep,
                                uint64_t limit_ns, int* err) {
   if (*reinterpret_cast<volatile int*>(err) & kErrTimeout) return false;
-  __threadfence_system();
+  bt_fence_acq_rel_sys();
   for (int r = 0; r < size; ++r)
-    if (r != rank) bt_st_release_sys(bt_x_flag(P.base[r], flags_off, inst, rank, cta), ep);
+    if (r != rank) bt_st_relaxed_sys(bt_x_flag(P.base[r], flags_off, inst, rank, cta), ep);
   uint64_t t0 = 0;  // the wall clock is read only once a flag was not there at the first poll
   for (int r = 0; r < size; ++r) {
     if (r == rank) continue;
@@ -1634,6 +1638,8 @@ __global__ void __launch_bounds__(kBtXThreads) bt_xreduce_kernel(BtXReduceArgs a
   __shared__ int s_ok;
   const int n = a.nb * a.C, c = blockIdx.x;
   const int e0 = (int)((long long)n * c / kBtXCtas), e1 = (int)((long long)n * (c + 1) / kBtXCtas);
+  pdl_wait();  // programmatic dependent launch: the GEMM pieces and the step's epoch are visible
+  pdl_launch_dependents();
   const uint32_t ep = (uint32_t)*a.epoch;
   float* mine = reinterpret_cast<float*>(a.peers.base[a.rank] + a.data_off) + (size_t)a.inst * n;
   for (int i = e0 + (int)threadIdx.x; i < e1; i += blockDim.x) {
@@ -1668,6 +1674,8 @@ struct BtXArgmaxArgs {
 // bt_argmax_kernel) merged first-maximum-wins in rank order.
 __global__ void __launch_bounds__(kBtXThreads) bt_xargmax_kernel(BtXArgmaxArgs a) {
   __shared__ int s_ok;
+  pdl_wait();  // programmatic dependent launch: this rank's bests and the step's epoch are visible
+  pdl_launch_dependents();
   const uint32_t ep = (uint32_t)*a.epoch;
   if (threadIdx.x == 0)
     s_ok = bt_x_handshake(a.peers, a.flags_off, a.inst, 0, a.rank, a.size, ep, a.limit_ns, a.err) ? 1 : 0;
@@ -2059,8 +2067,7 @@ int bt_record_head(rwkvb_batch* e, float* x, const float* xm, const float* part,
     x.flags_off = e->xl.flags, x.amax_off = e->xl.amax;
     x.nb = nb, x.rank = e->tp_rank, x.size = e->tp_size, x.inst = e->xl.ninst - 1, x.hist_cap = e->hist_cap;
     x.limit_ns = e->tp_wait_ns;
-    bt_xargmax_kernel<<<1, kBtXThreads, 0, s>>>(x);
-    return cuda_status(cudaGetLastError());
+    return bt_go(e->pdl, bt_xargmax_kernel, dim3(1), dim3(kBtXThreads), 0, s, x);
   }
   e->collective(1, e->amax_loc, e->amax_all, (int64_t)sizeof(float2) * nb, s, e->collective_user);
   bt_go(e->pdl, bt_argmax_merge_kernel, dim3((nb + 127) / 128), dim3(128), 0, s, e->amax_all, e->tp_size, nb, e->tok, e->hist, e->step,
@@ -2084,8 +2091,7 @@ int bt_reduce(rwkvb_batch* e, float* red, const float* part, const BtPieces& pp,
     x.flags_off = e->xl.flags, x.data_off = e->xl.data;
     x.nb = e->nb, x.C = e->C, x.rank = e->tp_rank, x.size = e->tp_size, x.inst = inst;
     x.limit_ns = e->tp_wait_ns;
-    bt_xreduce_kernel<<<kBtXCtas, kBtXThreads, 0, s>>>(x);
-    return cuda_status(cudaGetLastError());
+    return bt_go(e->pdl, bt_xreduce_kernel, dim3(kBtXCtas), dim3(kBtXThreads), 0, s, x);
   }
   const int n = e->nb * e->C;
   bg_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(red, part, e->nb, e->C, pp.stage0, pp.G, pp.total, pp.ncta);
