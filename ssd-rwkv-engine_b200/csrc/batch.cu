@@ -611,10 +611,17 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
     }
   }
   __syncthreads();
-  const int bq = t & 15, jq = t >> 4;
+  // threads: (k slice, column pair jq, session quad bq); 2^lp quads cover the
+  // sessions (16 at 64), and the 16 >> lp slices split the CTA's 128 inputs, so
+  // few sessions still keep every thread's FMAs useful
+  const int nq = (a.nb + 3) >> 2;
+  const int lp = nq > 8 ? 4 : nq > 4 ? 3 : nq > 2 ? 2 : nq > 1 ? 1 : 0;
+  const int U = 16 << lp;  // threads per slice
+  const int u = t & (U - 1), bq = u & ((1 << lp) - 1), jq = u >> lp;
+  const int kn = kBtAdpKc >> (4 - lp), kb = (t >> (4 + lp)) * kn;
   float acc[4][2] = {};
 #pragma unroll 4
-  for (int kk = 0; kk < kBtAdpKc; ++kk) {
+  for (int kk = kb; kk < kb + kn; ++kk) {
     const float4 xv = *reinterpret_cast<const float4*>(xs + kk * kBtXsStride + 4 * bq);
     const float2 wv = *reinterpret_cast<const float2*>(ws + kk * kBtAdpCols + 2 * jq);
     acc[0][0] = fmaf(xv.x, wv.x, acc[0][0]);
@@ -626,15 +633,32 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp1_kernel(BtAdp1Args a) {
     acc[3][0] = fmaf(xv.w, wv.x, acc[3][0]);
     acc[3][1] = fmaf(xv.w, wv.y, acc[3][1]);
   }
+  if (lp == 4) {  // one slice: the thread's sums are final
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int b = 4 * bq + u;
-    if (b >= a.nb) continue;
+    for (int q = 0; q < 4; ++q) {
+      const int b = 4 * bq + q;
+      if (b >= a.nb) continue;
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      const int c = c0 + 2 * jq + v;
-      if (c < R) a.out[((size_t)blockIdx.y * a.nb + b) * a.rtot + a.off[m] + c] = acc[u][v];
+      for (int v = 0; v < 2; ++v) {
+        const int c = c0 + 2 * jq + v;
+        if (c < R) a.out[((size_t)blockIdx.y * a.nb + b) * a.rtot + a.off[m] + c] = acc[q][v];
+      }
     }
+    return;
+  }
+  // slices' sums added in slice order (the staged inputs are dead: reused)
+  __syncthreads();
+  float* red = xs;  // [slice][U][8]: thread t's 8 sums at red[8 t]
+  *reinterpret_cast<float4*>(red + 8 * t) = make_float4(acc[0][0], acc[0][1], acc[1][0], acc[1][1]);
+  *reinterpret_cast<float4*>(red + 8 * t + 4) = make_float4(acc[2][0], acc[2][1], acc[3][0], acc[3][1]);
+  __syncthreads();
+  const int ks = 16 >> lp;
+  for (int o = t; o < 8 * U; o += blockDim.x) {
+    const int uu = o >> 3, e = o & 7;
+    const int b = 4 * (uu & ((1 << lp) - 1)) + (e >> 1), c = c0 + 2 * (uu >> lp) + (e & 1);
+    float v = 0.f;
+    for (int q = 0; q < ks; ++q) v += red[(q * U + uu) * 8 + e];
+    if (b < a.nb && c < R) a.out[((size_t)blockIdx.y * a.nb + b) * a.rtot + a.off[m] + c] = v;
   }
 }
 
@@ -648,7 +672,8 @@ __global__ void bt_adpr_kernel(float* midT, const float* part, int splits, int n
   if (i >= nb * used) return;
   const int b = i / used, j = i - b * used;
   float s = 0.f;
-  for (int q = 0; q < splits; ++q) s += part[((size_t)q * nb + b) * rtot + j];
+#pragma unroll 8
+  for (int q = 0; q < splits; ++q) s += part[((size_t)q * nb + b) * rtot + j];  // loads in flight together, adds in order
   if (j < rw) s = tanhf(s);
   else if (j >= rw + ra && j < rw + ra + rg) s = sigmoidf_(s);
   midT[(size_t)j * 64 + b] = s;
