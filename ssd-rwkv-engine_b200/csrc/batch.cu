@@ -728,7 +728,13 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
   const PackedView& W = a.w[m];
   float* ms = bt_sm;                  // [rc][64 sessions]
   float* ws = ms + kBtAdp2Rc * 64;    // [rc][64 columns]
-  const int bq = t & 15, cq = t >> 4;
+  // threads: (row slice, column quad cq, session quad bq); 2^lp quads cover the
+  // sessions (16 at 64), and the 16 >> lp slices take every (16 >> lp)-th row,
+  // so few sessions still keep every thread's FMAs useful
+  const int nq = (a.nb + 3) >> 2;
+  const int lp = nq > 8 ? 4 : nq > 4 ? 3 : nq > 2 ? 2 : nq > 1 ? 1 : 0;
+  const int U = 16 << lp, ks = 16 >> lp;  // threads per slice, slices
+  const int u = t & (U - 1), bq = u & ((1 << lp) - 1), cq = u >> lp, sl = t >> (4 + lp);
   float acc[4][4] = {};
   // rows r0 .. r0 + rc of W (64 columns) dequantised into ws
   auto load_w = [&](int r0, int rc) {
@@ -776,7 +782,7 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
       }
     }
     __syncthreads();
-    for (int r = 0; r < rc; ++r) {
+    for (int r = sl; r < rc; r += ks) {
       const float4 mv = *reinterpret_cast<const float4*>(ms + r * 64 + 4 * bq);
       const float4 wv = *reinterpret_cast<const float4*>(ws + r * 64 + 4 * cq);
       const float mm[4] = {mv.x, mv.y, mv.z, mv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
@@ -786,12 +792,30 @@ __global__ void __launch_bounds__(kBtThreads) bt_adp2_kernel(BtAdp2Args a) {
         for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(mm[u], ww[v], acc[u][v]);
     }
   }
+  if (lp == 4) {  // one slice: the thread's sums are final
 #pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    const int b = 4 * bq + u;
-    if (b >= a.nb) continue;
-    *reinterpret_cast<float4*>(a.out + ((size_t)a.ck_slot[ck] * a.nb + b) * a.C + c0 + 4 * cq) =
-        make_float4(acc[u][0], acc[u][1], acc[u][2], acc[u][3]);
+    for (int q = 0; q < 4; ++q) {
+      const int b = 4 * bq + q;
+      if (b >= a.nb) continue;
+      *reinterpret_cast<float4*>(a.out + ((size_t)a.ck_slot[ck] * a.nb + b) * a.C + c0 + 4 * cq) =
+          make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
+    }
+    return;
+  }
+  // slices' sums added in slice order (the staged mid rows are dead: reused)
+  __syncthreads();
+  float* red = ms;  // [slice][U][16]: thread t's 16 sums at red[16 t]
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<float4*>(red + 16 * t + 4 * q) = make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
+  __syncthreads();
+  for (int o = t; o < 4 * U; o += blockDim.x) {  // one float4 (session, column quad) per item
+    const int uu = o >> 2, q = o & 3;
+    const int b = 4 * (uu & ((1 << lp) - 1)) + q;
+    float4 v = *reinterpret_cast<const float4*>(red + uu * 16 + 4 * q);
+    for (int z = 1; z < ks; ++z) v = f4_add(v, *reinterpret_cast<const float4*>(red + (z * U + uu) * 16 + 4 * q));
+    if (b < a.nb)
+      *reinterpret_cast<float4*>(a.out + ((size_t)a.ck_slot[ck] * a.nb + b) * a.C + c0 + 4 * (uu >> lp)) = v;
   }
 }
 
