@@ -29,7 +29,8 @@
 // warp 1 allocates TMEM (two accumulators of up to 256 columns) and lane 0
 // issues the MMAs, one commit per flush group to the accumulator's "full"
 // barrier and one per stage to the slot's "empty" barrier; warps 2..17 are the
-// epilogue (TMEM lane quarter = warp % 4, 16 sessions per warp).
+// epilogue (TMEM lane quarter = warp % 4, 16 sessions per warp; 4 when the
+// sessions pad to 16).
 // Every wait is bounded: on a limit the CTA sets the error word, drains the
 // copies it issued and returns.
 #pragma once
@@ -302,8 +303,12 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
     pdl_launch_dependents();
     // warp w: TMEM lane quarter w % 4, sessions [16 ch, 16 ch + 16) with
     // ch = (w - 2) / 4; pairs of sessions go through packed f32x2 arithmetic.
+    // With 16 padded sessions (narrow) every warp takes four, [4 ch, 4 ch + 4),
+    // and one TMEM wait covers the ones column and the digits.
     const int q4 = warp & 3, ch = (warp - 2) >> 2;
-    const bool active = ch < (a.bp >> 4);
+    const bool narrow = a.bp == 16;
+    const int sb = narrow ? 4 * ch : 16 * ch;  // the warp's first session
+    const bool active = narrow || ch < (a.bp >> 4);
     const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16);
     const uint64_t neg_bias = fx2(-kBgBiasF, -kBgBiasF), inv254 = fx2(kInv254, kInv254);
     uint32_t fl = 0;
@@ -313,7 +318,7 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
       const int row = sg.t * 128 + q4 * 32 + lane;
       const int gpr = M.k >> M.lg;
       const float2* prow = M.pairs + (size_t)row * gpr;
-      const float* csm = a.cs[M.digits] + ch * 16;
+      const float* csm = a.cs[M.digits] + sb;
       const int nfl = 128 >> M.lg;
       uint64_t acc[8];
 #pragma unroll
@@ -329,7 +334,28 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
         const uint32_t tb = fl & 1;
         if (!bg_wait(&tfull[tb], (fl >> 1) & 1, a, &s_abort)) goto epi_done;
         tc_fence_after();
-        if (active) {
+        if (narrow) {
+          const uint32_t ta = tl + tb * kBgAccStride;
+          uint32_t d0[4], d1[4], d2[4];
+          const int q = (int)tmem_ld1_4x3_sync(ta + 3 * 16, ta + sb, ta + 16 + sb, ta + 2 * 16 + sb, d0, d1, d2);
+          const int kq = kBgBias - 127 * q;
+          const float dg = (pr.y - pr.x) * kInv255;
+          const uint64_t dg2 = fx2(dg, dg), mn2 = fx2(pr.x, pr.x);
+          const float* cg = csm + (size_t)g * 2 * 16;  // c_f of the warp's sessions; sum_x at + bp
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const uint64_t c2 = *reinterpret_cast<const uint64_t*>(cg + 2 * s);
+            const uint64_t x2 = *reinterpret_cast<const uint64_t*>(cg + 16 + 2 * s);
+            const uint64_t f0 = fadd2(
+                fx2(__int_as_float((int)d0[2 * s] + kq), __int_as_float((int)d0[2 * s + 1] + kq)), neg_bias);
+            const uint64_t f1 = fadd2(
+                fx2(__int_as_float((int)d1[2 * s] + kq), __int_as_float((int)d1[2 * s + 1] + kq)), neg_bias);
+            const uint64_t f2 = fadd2(
+                fx2(__int_as_float((int)d2[2 * s] + kq), __int_as_float((int)d2[2 * s + 1] + kq)), neg_bias);
+            const uint64_t t = ffma2(ffma2(f2, inv254, f1), inv254, f0);
+            acc[s] = ffma2(fmul2(dg2, c2), t, ffma2(mn2, x2, acc[s]));
+          }
+        } else if (active) {
           const uint32_t ta = tl + tb * kBgAccStride;
           const int q = (int)tmem_ld1_sync(ta + 3 * a.bp);
           const int kq = kBgBias - 127 * q;
@@ -338,7 +364,7 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
           const float* cg = csm + (size_t)g * 2 * a.bp;  // c_f of the chunk's sessions; sum_x at + bp
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {  // two rounds of 8 sessions (register budget)
-            const uint32_t co = (uint32_t)(ch * 16 + hf * 8);
+            const uint32_t co = (uint32_t)(sb + hf * 8);
             uint32_t d0[8], d1[8], d2[8];
             tmem_ld8x3_sync(ta + co, ta + a.bp + co, ta + 2 * a.bp + co, d0, d1, d2);
 #pragma unroll
@@ -365,9 +391,10 @@ __global__ void __maxnreg__(96) bgemm_kernel(const __grid_constant__ BgArgs a) {
         float* out = M.out + (size_t)sg.p * a.nb * M.rows + row;
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
+          if (narrow && s >= 2) break;
           float lo_v, hi_v;
           fx2_unpack(acc[s], lo_v, hi_v);
-          const int b = ch * 16 + 2 * s;
+          const int b = sb + 2 * s;
           if (b < a.nb) out[(size_t)b * M.rows] = lo_v;
           if (b + 1 < a.nb) out[(size_t)(b + 1) * M.rows] = hi_v;
         }

@@ -90,6 +90,23 @@ __device__ __forceinline__ uint32_t tmem_ld1_sync(uint32_t taddr) {
   return r;
 }
 
+// One column (tq) and three 4-column loads (columns t0.., t1.., t2..), one wait.
+__device__ __forceinline__ uint32_t tmem_ld1_4x3_sync(uint32_t tq, uint32_t t0, uint32_t t1, uint32_t t2,
+                                                     uint32_t (&a)[4], uint32_t (&b)[4], uint32_t (&c)[4]) {
+  uint32_t q;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%13];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%1,%2,%3,%4}, [%14];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%5,%6,%7,%8}, [%15];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x4.b32 {%9,%10,%11,%12}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(q), "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]),
+        "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(tq), "r"(t0), "r"(t1), "r"(t2)
+      : "memory");
+  return q;
+}
+
 // Three 8-column loads (columns t0.., t1.., t2..) and one wait.
 __device__ __forceinline__ void tmem_ld8x3_sync(uint32_t t0, uint32_t t1, uint32_t t2, uint32_t (&a)[8],
                                                 uint32_t (&b)[8], uint32_t (&c)[8]) {
