@@ -278,7 +278,7 @@ class CudaB200Backend(_PackBase):
             "name": "cuda_b200",
             "declared": {
                 "pack_streaming": True, "skeleton": False, "resident": True, "state_snapshot": True,
-                "batch": True, "prefix_cache": True, "tokenizer": self.tokenizer is not None,
+                "batch": True, "prefix_cache": False, "tokenizer": self.tokenizer is not None,
                 "state_kind": "rwkv7", "supported_codecs": list(SUPPORTED_CODECS), "requires_ggml_bin": False,
                 "token_generation": True, "logits_probe": True, "state_transfer": True,
                 "followup_generation": True, "sampling": True, "incremental_streaming": True,

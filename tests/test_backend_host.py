@@ -118,6 +118,8 @@ def test_capabilities_and_unloaded_errors():
     assert caps["name"] == "cuda_b200"
     assert "scale_u8_grouped" in caps["declared"]["supported_codecs"]
     assert b.supports_capability("logits_probe")
+    # no prefix cache is built: the backend must not claim one
+    assert not b.supports_capability("prefix_cache")
     assert b.get_recurrent_state() is None and b.probe_logits() is None
     with pytest.raises(RuntimeError):
         b._engine_or_raise()
