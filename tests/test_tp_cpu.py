@@ -86,9 +86,18 @@ def test_plans():
     assert [(p.v0, p.v1) for p in (tp.plan(odd, r, 2) for r in range(2))] == [(0, 1024), (1024, 1920)]
 
 
-def _tiny_pack(seed: int):
-    shape = synth.PRESETS["tiny"]
+# shapes of the rank tests: the tiny preset (4 heads: 2 ranks at most) and a
+# 2-layer model of 8 heads, so that 4 ranks hold 128 channels each
+SHAPES = {"tiny": synth.PRESETS["tiny"], "wide8h": synth.RWKV7Shape(2, 512, 64, 2048, 1024, 32, 32, 32, 64)}
+
+
+def _pack(key: str, seed: int):
+    shape = SHAPES[key]
     return shape, synth.make_pack(synth.generate_state_dict(shape, seed, "cpu"), policy="sg8")
+
+
+def _tiny_pack(seed: int):
+    return _pack("tiny", seed)
 
 
 def test_shards_reassemble_the_full_pack():
@@ -145,12 +154,12 @@ def _global_argmax(coll: tp.TPCollective, logits: np.ndarray, v0: int) -> int:
     return bi
 
 
-def _worker(rank: int, world: int, port: int, q) -> None:
+def _worker(rank: int, world: int, port: int, q, key: str = "tiny") -> None:
     sys.path[:0] = [p for p in os.environ.get("RWKVB_TEST_PATH", "").split(os.pathsep) if p]
     try:
         dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60))
-        shape, pack = _tiny_pack(5)
+        shape, pack = _pack(key, 5)
         local, plan = tp.shard_pack(pack, rank, world)
         coll = tp.TPCollective()
 
@@ -170,27 +179,29 @@ def _worker(rank: int, world: int, port: int, q) -> None:
         q.put(("error", rank, repr(e)))
 
 
-def test_two_rank_oracle_over_shards_matches_single_device():
+def _ranks_match_single_device(world: int, key: str) -> None:
+    """`world` gloo ranks run the oracle over their shards (all-reduce and
+    argmax hooks); ids, logits and state must equal the single-device oracle."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     os.environ["RWKVB_TEST_PATH"] = os.pathsep.join(sys.path)
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, key)) for r in range(world)]
     for p in procs:
         p.start()
-    out = [q.get(timeout=300) for _ in range(2)]
+    out = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
         if p.is_alive():  # pragma: no cover
             p.kill()
     assert not any(o[0] == "error" for o in out), out
     by_rank = {o[0]: o for o in out}
-    shape, pack = _tiny_pack(5)
+    shape, pack = _pack(key, 5)
     ref = OracleRWKV7(pack, n_layer=shape.n_layer, n_embd=shape.n_embd, head_size=shape.head_size)
     prompt = synth.seeded_prompt(6, shape.vocab, 5)
     ids_ref, logits_ref, state_ref = ref.greedy(prompt, 5)
-    logits = np.concatenate([by_rank[r][3] for r in range(2)], axis=1)
-    for r in range(2):
+    logits = np.concatenate([by_rank[r][3] for r in range(world)], axis=1)
+    for r in range(world):
         _, plan, ids, _, state, calls = by_rank[r]
         assert ids == ids_ref
         # per forward: 2 all-reduces per layer; per greedy pick: one all-gather
@@ -201,3 +212,11 @@ def test_two_rank_oracle_over_shards_matches_single_device():
                                        rtol=0, atol=1e-4)
             np.testing.assert_allclose(state[3 * layer + 2], state_ref[3 * layer + 2], rtol=0, atol=1e-4)
     np.testing.assert_allclose(logits, logits_ref, rtol=0, atol=1e-4)
+
+
+def test_two_rank_oracle_over_shards_matches_single_device():
+    _ranks_match_single_device(2, "tiny")
+
+
+def test_four_rank_oracle_over_shards_matches_single_device():
+    _ranks_match_single_device(4, "wide8h")
