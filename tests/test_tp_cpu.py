@@ -86,9 +86,10 @@ def test_plans():
     assert [(p.v0, p.v1) for p in (tp.plan(odd, r, 2) for r in range(2))] == [(0, 1024), (1024, 1920)]
 
 
-# shapes of the rank tests: the tiny preset (4 heads: 2 ranks at most) and a
-# 2-layer model of 8 heads, so that 4 ranks hold 128 channels each
-SHAPES = {"tiny": synth.PRESETS["tiny"], "wide8h": synth.RWKV7Shape(2, 512, 64, 2048, 1024, 32, 32, 32, 64)}
+# shapes of the rank tests: the tiny preset (4 heads: 2 ranks at most) and
+# 2-layer models of 8 and 16 heads, so that 4 and 8 ranks hold 128 channels each
+SHAPES = {"tiny": synth.PRESETS["tiny"], "wide8h": synth.RWKV7Shape(2, 512, 64, 2048, 1024, 32, 32, 32, 64),
+          "wide16h": synth.RWKV7Shape(2, 1024, 64, 4096, 1024, 32, 32, 32, 64)}
 
 
 def _pack(key: str, seed: int):
@@ -220,3 +221,7 @@ def test_two_rank_oracle_over_shards_matches_single_device():
 
 def test_four_rank_oracle_over_shards_matches_single_device():
     _ranks_match_single_device(4, "wide8h")
+
+
+def test_eight_rank_oracle_over_shards_matches_single_device():
+    _ranks_match_single_device(8, "wide16h")
