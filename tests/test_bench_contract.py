@@ -9,6 +9,7 @@ from __future__ import annotations
 import argparse
 import importlib.util
 import json
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -47,3 +48,30 @@ def test_reference_arm_line_matches_the_contract():
     # the GPU arm's metric string for the same configuration
     bench = _bench_module()
     assert d["metric"] == bench.metric_name(argparse.Namespace(config="tiny", policy="sg8"))
+
+
+def test_reference_arm_under_torchrun_prints_one_line_from_rank_zero():
+    """The driver launches the reference arm at N > 1 through torchrun as well:
+    rank 0 alone times the CPU implementation and prints the line (n_gpus = N,
+    all host threads), the other ranks exit 0 without work."""
+    out = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                          "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(REPO / "bench.py"),
+                          "--impl", "reference", "--gpus", "2", "--config", "tiny", "--steps", "2", "--warmup", "3"],
+                         cwd=REPO, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.strip().startswith("{")]
+    assert len(lines) == 1, out.stdout
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+    # torchrun exports OMP_NUM_THREADS=1 to every rank; the arm must still use the host's threads
+    assert d["cpu_baseline"]["cores"] >= 1
+    if len(os.sched_getaffinity(0)) > 1:
+        assert d["cpu_baseline"]["cores"] > 1
+
+
+def _free_port() -> int:
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
