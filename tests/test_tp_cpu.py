@@ -7,6 +7,7 @@ oracle."""
 
 from __future__ import annotations
 
+import ctypes
 import datetime
 import os
 import socket
@@ -225,3 +226,72 @@ def test_four_rank_oracle_over_shards_matches_single_device():
 
 def test_eight_rank_oracle_over_shards_matches_single_device():
     _ranks_match_single_device(8, "wide16h")
+
+
+# ------------------------------------------------ peer-exchange host side
+def _peer_worker(rank: int, world: int, port: int, q) -> None:
+    """PeerExchange over gloo with a fake of the C ABI's IPC calls: rank r's
+    "handle" is 64 bytes of (r + 1), its own buffer 0x10000 (r + 1), and opening
+    rank s's handle maps it at 0x7000000 + 0x10000 (s + 1)."""
+    sys.path[:0] = [p for p in os.environ.get("RWKVB_TEST_PATH", "").split(os.pathsep) if p]
+    try:
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        opened, closed, freed = [], [], []
+
+        class FakeIpc:
+            def rwkvb_ipc_alloc(self, nbytes, own_ref, handle):
+                own_ref._obj.value = 0x10000 * (rank + 1)
+                ctypes.memmove(handle, bytes([rank + 1]) * 64, 64)
+                return native.RWKVB_OK
+
+            def rwkvb_ipc_open(self, raw, ptr_ref):
+                src = raw[0] - 1
+                if raw != bytes([src + 1]) * 64 or src == rank:
+                    return native.RWKVB_EARG
+                ptr_ref._obj.value = 0x7000000 + 0x10000 * (src + 1)
+                opened.append(src)
+                return native.RWKVB_OK
+
+            def rwkvb_ipc_close(self, ptr):
+                closed.append(ptr.value)
+                return native.RWKVB_OK
+
+            def rwkvb_ipc_free(self, ptr):
+                freed.append(ptr.value)
+                return native.RWKVB_OK
+
+        native.lib = lambda: FakeIpc()
+        torch.cuda.synchronize = lambda *a, **k: None  # no device work to wait for on the CPU
+        ex = tp.PeerExchange(4096, device=torch.device("cpu"))
+        peers = [int(ex.peers[r]) for r in range(world)]
+        ex.close()
+        ex.close()  # a second close is a no-op
+        q.put((rank, peers, opened, closed, freed))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported through the queue
+        q.put(("error", rank, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange_maps_every_rank_in_rank_order(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    os.environ["RWKVB_TEST_PATH"] = os.pathsep.join(sys.path)
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():  # pragma: no cover
+            p.kill()
+    assert not any(o[0] == "error" for o in out), out
+    for rank, peers, opened, closed, freed in out:
+        want = [0x10000 * (r + 1) if r == rank else 0x7000000 + 0x10000 * (r + 1) for r in range(world)]
+        assert peers == want
+        assert opened == [r for r in range(world) if r != rank]
+        assert closed == [want[r] for r in range(world) if r != rank]
+        assert freed == [0x10000 * (rank + 1)]
