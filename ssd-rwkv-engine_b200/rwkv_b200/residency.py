@@ -83,6 +83,7 @@ def _place(items) -> tuple[list[int], list[bytes], int]:
         meta = _meta_bytes(head, shape[0], shape[1])
         cur = (cur + _ALIGN - 1) // _ALIGN * _ALIGN
         # payload (blob + meta) 16-byte aligned; blob start stays 8-byte aligned
+        # (4-byte for the 20-byte header of a per-tensor LUT2 blob)
         cur += (16 - meta % 16) % 16
         offs.append(cur)
         heads.append(head)

@@ -73,3 +73,28 @@ def test_explicit_resident_layers_win_over_the_budget():
     sizes = {i: 100 for i in range(4)}
     assert plan_residency(sizes, 50, 4, hbm_budget=None, resident_layers=[1, 2]) == [0, 3]
     assert plan_residency(sizes, 50, 4, hbm_budget=1, resident_layers=[0, 1, 2, 3]) == []
+
+
+def test_blob_placement_keeps_code_payloads_16_byte_aligned():
+    """Blobs packed back to back into one device image: each starts on a
+    256-byte boundary plus the padding that puts its code payload (after the
+    header and group records) on the 16-byte boundary the bulk copies need;
+    no two blobs overlap."""
+    from rwkv_b200 import synth
+    from rwkv_b200.residency import _meta_bytes, _place
+
+    shape = synth.PRESETS["tiny"]
+    sd = synth.generate_state_dict(shape, 4, "cpu")
+    for policy in ("sg8", "lut2"):
+        pack = synth.make_pack(sd, policy=policy)
+        items = [(n, e.payload, tuple(e.shape), e.codec) for n, e in pack.items() if e.codec != "none"]
+        assert {c for *_, c in items} >= ({"sg8"} if policy == "sg8" else {"sg8", "lut2"})
+        offs, heads, total = _place(items)
+        end = 0
+        for (name, payload, shp, _codec), off, head in zip(items, offs, heads):
+            meta = _meta_bytes(head, shp[0], shp[1])
+            assert (off + meta) % 16 == 0, name
+            assert off % 8 == 0 and off >= end, name
+            assert off - end < 256 + 16, name  # no more padding than the two alignments
+            end = off + len(payload)
+        assert total == end
